@@ -1,0 +1,249 @@
+/*
+ * tgb200.h -- C ABI of libtgb200.so, the sm_100a kernels behind tensorgrad_b200.
+ *
+ * The reference tensorgrad computes every op of the training step with NumPy/OpenBLAS inside
+ * its Python VJP closures; it has no FFI of its own. This header is the boundary that
+ * replaces those NumPy bodies: each entry point names the reference function (file:line in
+ * the tensorgrad 0.2.0 project) whose arithmetic it performs. Signatures use plain device
+ * pointers, element counts and a CUDA stream passed as `void*` (NULL = legacy default
+ * stream); no framework types cross the boundary. Every call is asynchronous on `stream`
+ * unless stated otherwise, and returns a status code (TG_OK = 0). tg_last_error() gives the
+ * detail of the last failure on the calling host thread.
+ *
+ * Layouts: all matrices are row-major. `dtype` is TG_F32 or TG_F64 (the float64 build mode);
+ * integer ids/targets are int64.
+ */
+#ifndef TGB200_H
+#define TGB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status and dtypes */
+enum tg_status {
+  TG_OK = 0,
+  TG_ERR_ARG = 1,         /* invalid argument (maps to ValueError in the host wrappers) */
+  TG_ERR_CUDA = 2,        /* a CUDA runtime/launch error */
+  TG_ERR_UNSUPPORTED = 3, /* shape/dtype combination not supported */
+  TG_ERR_INDEX = 4,       /* id/target out of range (maps to IndexError) */
+  TG_ERR_TIMEOUT = 5      /* a bounded device-side wait ran out */
+};
+enum tg_dtype { TG_F32 = 0, TG_F64 = 1, TG_I64 = 2 /* casts only */ };
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int tg_version(void);
+/* Static text for a status code. */
+const char* tg_status_string(int status);
+/* Copies the detail message of the calling thread's last failure into buf (NUL-terminated). */
+int tg_last_error(char* buf, size_t len);
+/* SM count and compute capability of `device`. */
+int tg_device_info(int device, int* sm_count, int* cc_major, int* cc_minor);
+
+/* ------------------------------------------------------------------ memory movement
+ * The reference keeps every array in host memory; these move tensor storage and inputs
+ * (token ids, targets, upstream gradients) between host and device. */
+int tg_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream);
+int tg_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream);
+int tg_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream);
+int tg_memset_zero(void* dst, size_t bytes, void* stream);
+int tg_stream_synchronize(void* stream);
+
+/* ------------------------------------------------------------------ GEMM
+ * C[m,n] = alpha * op(A)[m,k] @ op(B)[k,n] + beta * C (+ bias[n]); BLAS-like, row-major.
+ *   trans_a = 0: A is m x k (lda >= k);  trans_a = 1: A is stored k x m (lda >= m).
+ *   trans_b = 0: B is k x n (ldb >= n);  trans_b = 1: B is stored n x k (ldb >= k).
+ * beta = 0 never reads C. fp32 runs on the tcgen05 tensor cores with a 3xTF32 split
+ * (fp32-level accuracy) when strides are 16-byte aligned, otherwise on the SIMT path;
+ * fp64 runs on the SIMT path. Replaces the `@` products of ops/layers.py:34-49 and
+ * ops/linalg.py:16-63. */
+int tg_gemm(int dtype, int trans_a, int trans_b, int64_t m, int64_t n, int64_t k, double alpha,
+            const void* a, int64_t lda, const void* b, int64_t ldb, double beta, void* c,
+            int64_t ldc, const void* bias, void* stream);
+/* Same, forcing the SIMT (CUDA-core) kernel: the accuracy reference for tg_gemm. */
+int tg_gemm_simt(int dtype, int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
+                 double alpha, const void* a, int64_t lda, const void* b, int64_t ldb,
+                 double beta, void* c, int64_t ldc, const void* bias, void* stream);
+/* Live timing of the tensor-core GEMM (measurement support, no reference counterpart):
+ * tg_gemm_profile(1) brackets every following tensor-core launch with CUDA events on its
+ * stream; tg_gemm_profile_read() waits for them and returns the summed device time (ms),
+ * the launch count and the algorithmic FLOPs (2 m n k per launch), then clears the record. */
+int tg_gemm_profile(int enable);
+int tg_gemm_profile_read(double* total_ms, int64_t* launches, double* flops);
+/* Kernels launched by this library since load (every entry point counts its own). */
+uint64_t tg_launch_count(void);
+/* Reads (and with reset != 0 clears) the tensor-core GEMM's device status word: TG_OK, or
+ * TG_ERR_TIMEOUT when a bounded pipeline wait gave up. Synchronous. */
+int tg_gemm_tc_status(int reset);
+/* Strided-batched GEMM: `batch` products at element offsets i*stride_{a,b,c}. */
+int tg_gemm_batched(int dtype, int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
+                    double alpha, const void* a, int64_t lda, int64_t stride_a, const void* b,
+                    int64_t ldb, int64_t stride_b, double beta, void* c, int64_t ldc,
+                    int64_t stride_c, int64_t batch, void* stream);
+
+/* linear (ops/layers.py:22-62): y[rows,out] = x[rows,in] @ w[out,in]^T + bias. */
+int tg_linear_forward(int dtype, const void* x, const void* w, const void* bias, void* y,
+                      int64_t rows, int64_t in_features, int64_t out_features, void* stream);
+/* linear VJP (ops/layers.py:43-49): gx = g @ w, gw = g^T @ x (+ beta_gw * gw), gb = colsum(g).
+ * need bit 0 = gx, bit 1 = gw, bit 2 = gb (unset bits skip the launch). beta_gw = 1
+ * accumulates into an existing gw (tied weights). `scratch` holds at least
+ * tg_colsum_scratch_bytes(dtype, rows, out_features) bytes when bit 2 is set. */
+int tg_linear_backward(int dtype, const void* g, const void* x, const void* w, void* gx, void* gw,
+                       void* gb, int64_t rows, int64_t in_features, int64_t out_features,
+                       unsigned need, double beta_gw, void* scratch, void* stream);
+
+/* ------------------------------------------------------------------ reductions
+ * out[c] = (accumulate ? out[c] : 0) + sum_r x[r, c]: the bias-gradient / unbroadcast
+ * column sum (ops/_util.py:49-63, ops/layers.py:49). Deterministic two-pass reduction
+ * through `scratch` (tg_colsum_scratch_bytes bytes). */
+size_t tg_colsum_scratch_bytes(int dtype, int64_t rows, int64_t cols);
+int tg_colsum(int dtype, const void* x, void* out, int64_t rows, int64_t cols, int accumulate,
+              void* scratch, void* stream);
+/* General sum of a contiguous tensor of shape in_shape[ndim] down to keep-mask axes
+ * (keep[i] = 1 keeps axis i, 0 sums it); out is contiguous over the kept axes.
+ * The adjoint of broadcasting (ops/_util.py:49-63) and reduce.sum (ops/reduce.py). */
+int tg_reduce_sum(int dtype, int ndim, const int64_t* in_shape, const int* keep, const void* x,
+                  void* out, void* stream);
+/* out[0] = sum of all n elements (float64 accumulation; deterministic). reduce.sum / mean
+ * over all axes (ops/reduce.py). `scratch` holds tg_sum_all_scratch_bytes() bytes. */
+size_t tg_sum_all_scratch_bytes(void);
+int tg_sum_all(int dtype, const void* x, void* out, int64_t n, void* scratch, void* stream);
+
+/* ------------------------------------------------------------------ elementwise
+ * Broadcast binary op: out (contiguous, shape[ndim]) = a op b, with a/b read through element
+ * strides (0 on broadcast axes). ops/elementwise.py:43-121. op: */
+enum tg_binary_op { TG_ADD = 0, TG_SUB = 1, TG_MUL = 2, TG_DIV = 3, TG_POW = 4 };
+int tg_binary(int dtype, int op, int ndim, const int64_t* shape, const void* a,
+              const int64_t* a_strides, const void* b, const int64_t* b_strides, void* out,
+              void* stream);
+/* out = alpha * x + beta * y over n contiguous elements (y may be NULL when beta = 0). */
+int tg_axpby(int dtype, int64_t n, double alpha, const void* x, double beta, const void* y,
+             void* out, void* stream);
+/* out = alpha * x * (*scale_dev) (scale read on the device; used for upstream scalars). */
+int tg_scale_by_device_scalar(int dtype, int64_t n, const void* x, const void* scale_dev,
+                              double alpha, void* out, void* stream);
+/* Unary ops: out = f(x). ops/elementwise.py:133-268. */
+enum tg_unary_op {
+  TG_NEG = 0, TG_EXP = 1, TG_LOG = 2, TG_SQRT = 3, TG_TANH = 4, TG_SIGMOID = 5, TG_RELU = 6,
+  TG_SQUARE = 7, TG_FILL = 8 /* out = alpha */, TG_POWS = 9 /* out = x ** alpha */
+};
+int tg_unary(int dtype, int op, int64_t n, const void* x, double alpha, void* out, void* stream);
+/* dtype conversion of n elements (ops/elementwise.py:323-343 astype). */
+int tg_cast(int src_dtype, int dst_dtype, int64_t n, const void* src, void* dst, void* stream);
+/* dst[idx . dst_strides] = src[idx . src_strides] for every index of shape[ndim] (element
+ * strides, elem_bytes in {1, 4, 8}): permute/transpose, slicing, broadcast materialisation and
+ * the scatter of getitem's VJP (ops/shape.py:45-235). */
+int tg_strided_copy(int elem_bytes, int ndim, const int64_t* shape, const void* src,
+                    const int64_t* src_strides, void* dst, const int64_t* dst_strides,
+                    void* stream);
+/* GELU, tanh approximation (ops/elementwise.py:275-320). */
+int tg_gelu_forward(int dtype, int64_t n, const void* x, void* y, void* stream);
+int tg_gelu_backward(int dtype, int64_t n, const void* g, const void* x, void* gx, void* stream);
+/* ReLU VJP g * (x > 0) (ops/elementwise.py:261-262). */
+int tg_relu_backward(int dtype, int64_t n, const void* g, const void* x, void* gx, void* stream);
+/* Unary VJPs from the saved input x or output y: op = TG_EXP (g*y), TG_LOG (g/x),
+ * TG_SQRT (g/(2y)), TG_TANH (g(1-y^2)), TG_SIGMOID (g y (1-y)), TG_POWS (g a x^(a-1)). */
+int tg_unary_backward(int dtype, int op, int64_t n, const void* g, const void* x, const void* y,
+                      double alpha, void* gx, void* stream);
+
+/* ------------------------------------------------------------------ layer norm
+ * ops/layers.py:65-141. Per row of `cols`: mean, rstd = 1/sqrt(var + eps) (biased var),
+ * y = (x - mean) * rstd * w + b; w/b may be NULL. mean/rstd[rows] are saved for backward. */
+int tg_layer_norm_forward(int dtype, const void* x, const void* w, const void* b, void* y,
+                          void* mean, void* rstd, int64_t rows, int64_t cols, double eps,
+                          void* stream);
+/* gx = rstd (gh - mean(gh) - xhat mean(gh xhat)), gh = g w; gw = sum_rows g xhat;
+ * gb = sum_rows g. need bit 0 = gx, bit 1 = gw, bit 2 = gb. `scratch` holds
+ * tg_layer_norm_scratch_bytes bytes when gw or gb is needed. */
+size_t tg_layer_norm_scratch_bytes(int dtype, int64_t rows, int64_t cols);
+int tg_layer_norm_backward(int dtype, const void* g, const void* x, const void* w,
+                           const void* mean, const void* rstd, void* gx, void* gw, void* gb,
+                           int64_t rows, int64_t cols, unsigned need, void* scratch,
+                           void* stream);
+
+/* ------------------------------------------------------------------ embedding
+ * ops/layers.py:209-232. out[i, :] = w[ids[i], :]. Ids must be in [0, num) (checked on the
+ * host by the caller, as the reference does before indexing). */
+int tg_embedding_forward(int dtype, const int64_t* ids, const void* w, void* out, int64_t n,
+                         int64_t num, int64_t dim, void* stream);
+/* Scatter-add of gradient rows into gw[num, dim] in the reference's order
+ * (ops/layers.py:192-206: stable sort of ids, then a sum per run of equal ids):
+ * `order` is the stable argsort of ids, `seg_start[nseg + 1]` the run boundaries in it and
+ * `seg_id[nseg]` the id of each run. accumulate = 0 zero-fills gw first. */
+int tg_embedding_backward(int dtype, const void* g, const int64_t* order,
+                          const int64_t* seg_start, const int64_t* seg_id, int64_t nseg,
+                          void* gw, int64_t num, int64_t dim, int accumulate, void* stream);
+
+/* ------------------------------------------------------------------ cross entropy
+ * ops/loss.py:23-97 with ops/activation.py:48-52 (class axis last). Per row: lse = log sum
+ * exp(x), loss_row = lse - x[t] (0 where t == ignore_index). Targets are validated: a target
+ * outside [0, classes) that is not ignore_index sets *bad_target_dev (int32) to 1.
+ * Per-row losses go to row_loss[rows] (the result itself for reduction 2 = none);
+ * reduction 0 = mean over valid rows and 1 = sum write out[0], summed in float64 in row
+ * order. n_valid_dev (int64[1], may be NULL for none) receives the valid-row count. */
+int tg_cross_entropy_forward(int dtype, const void* logits, const int64_t* targets, void* lse,
+                             void* row_loss, void* out, int64_t rows, int64_t classes,
+                             int64_t ignore_index, int reduction, int64_t* n_valid_dev,
+                             int* bad_target_dev, void* stream);
+/* grad = (softmax(x) - onehot(t)) * valid * g_dev[0 or row] / (mean ? n_valid : 1). */
+int tg_cross_entropy_backward(int dtype, const void* logits, const int64_t* targets,
+                              const void* lse, const void* g_dev, const int64_t* n_valid_dev,
+                              void* grad, int64_t rows, int64_t classes, int64_t ignore_index,
+                              int reduction, void* stream);
+
+/* ------------------------------------------------------------------ attention
+ * Fused causal/non-causal softmax attention (ops/attention.py:71-116, 163-272) as a flash-
+ * style kernel: the forward stores O and the row log-sum-exp instead of P; the backward
+ * recomputes P. Tensors are (B, H, T, D) viewed through element strides
+ * (batch, head, token); the last axis is contiguous. For packed QKV, q/k/v point into one
+ * (B, T, 3*H*D) buffer at offsets 0, H*D, 2*H*D with token stride 3*H*D. Causal: key j is
+ * visible to query i iff j <= i + (tk - tq). lse is (B, H, tq) contiguous. */
+typedef struct tg_attn_shape {
+  int64_t batch, heads, tq, tk, head_dim;
+  int64_t q_sb, q_sh, q_st; /* strides of q (elements) */
+  int64_t k_sb, k_sh, k_st;
+  int64_t v_sb, v_sh, v_st;
+  int64_t o_sb, o_sh, o_st; /* strides of o / dO (same layout) */
+  int causal;
+} tg_attn_shape;
+int tg_attention_forward(int dtype, const tg_attn_shape* s, const void* q, const void* k,
+                         const void* v, void* o, void* lse, void* stream);
+/* dq/dk/dv use the strides of q/k/v. `scratch` holds tg_attention_scratch_bytes bytes. */
+size_t tg_attention_scratch_bytes(int dtype, const tg_attn_shape* s);
+int tg_attention_backward(int dtype, const tg_attn_shape* s, const void* q, const void* k,
+                          const void* v, const void* o, const void* lse, const void* dout,
+                          void* dq, void* dk, void* dv, void* scratch, void* stream);
+
+/* ------------------------------------------------------------------ optimiser
+ * optim/clip.py:15-31: total = sqrt(sum over tensors of sum(g^2)) accumulated in float64.
+ * ptrs/numels are HOST arrays of `count` device pointers / sizes. The result (float64) is
+ * written to total_dev[0]. `scratch` holds tg_sumsq_scratch_bytes(count) bytes. */
+size_t tg_sumsq_scratch_bytes(int count);
+int tg_sumsq_multi(int dtype, int count, void* const* ptrs, const int64_t* numels,
+                   double* total_dev, void* scratch, void* stream);
+/* If max_norm / (sqrt(total_sq... total_dev[0]) + eps) < 1, scale every tensor by that
+ * factor rounded to the tensor dtype (the reference casts the scale to g.dtype). */
+int tg_clip_scale_multi(int dtype, int count, void* const* ptrs, const int64_t* numels,
+                        const double* total_dev, double max_norm, double eps, void* scratch,
+                        void* stream);
+/* AdamW/Adam update of one flat range (optim/adam.py:59-94) in the reference's order:
+ * p *= 1 - lr*wd (decoupled); m = b1 m + (1-b1) g; v = b2 v + (1-b2) g^2;
+ * p -= (lr/bc1) m / (sqrt(v)/sqrt(bc2) + eps), with bc_i = 1 - b_i^step.
+ * decoupled = 0 gives Adam's L2 form (g += wd p). */
+int tg_adam_update(int dtype, int64_t n, void* p, const void* g, void* m, void* v, double lr,
+                   double beta1, double beta2, double eps, double weight_decay, int64_t step,
+                   int decoupled, void* stream);
+/* Multi-tensor variant: one launch over `count` ranges (HOST pointer/size/step arrays). */
+size_t tg_adam_multi_scratch_bytes(int count);
+int tg_adam_update_multi(int dtype, int count, void* const* p, void* const* g, void* const* m,
+                         void* const* v, const int64_t* numels, const int64_t* steps, double lr,
+                         double beta1, double beta2, double eps, double weight_decay,
+                         int decoupled, void* scratch, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TGB200_H */

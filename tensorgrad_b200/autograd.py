@@ -1,0 +1,352 @@
+"""The reverse-mode engine: graph nodes, grad mode, ``backward`` and ``grad``.
+
+Same contract as the reference engine (autograd.py:119-465 of tensorgrad 0.2.0): a
+:class:`Node` holds an op's parents and its VJP closure; the engine walks the tensors that
+require grad in reverse topological order (iterative post-order DFS), sums fan-out
+contributions, accumulates leaf gradients, and frees each node's saved state unless
+``retain_graph``. The walk runs on the host; the gradients it carries are device arrays and
+every sum is a device kernel. Error messages match the reference's, word for word.
+
+Differences, by design: ``create_graph=True`` (gradients that carry their own graph) is not
+available on the device path and raises ``NotImplementedError``; a hook lets data-parallel
+training start a gradient all-reduce the moment a leaf's gradient is final.
+"""
+
+from __future__ import annotations
+
+import functools
+import threading
+from collections.abc import Callable, Sequence
+from typing import TYPE_CHECKING, Any, TypeAlias, TypeVar
+
+import numpy as np
+
+from tensorgrad_b200 import profiler as _profiler
+
+if TYPE_CHECKING:
+    from tensorgrad_b200.device import DeviceArray
+    from tensorgrad_b200.tensor import Tensor
+
+__all__ = ["BackwardFn", "Node", "backward", "enable_grad", "grad", "is_grad_enabled", "no_grad"]
+
+#: VJP of one op on device arrays: given d(loss)/d(output) and, per input, whether its
+#: gradient is needed, return d(loss)/d(input_i) (``None`` where not needed).
+BackwardFn = Callable[["DeviceArray", tuple[bool, ...]], tuple["DeviceArray | None", ...]]
+GradOutputs: TypeAlias = "Tensor | np.ndarray | Sequence[Tensor | np.ndarray | None] | None"
+
+_R = TypeVar("_R")
+
+
+class _GradMode(threading.local):
+    enabled: bool = True
+
+
+_grad_mode = _GradMode()
+
+
+def is_grad_enabled() -> bool:
+    """Return ``True`` if ops currently record the graph needed for ``backward``."""
+    return _grad_mode.enabled
+
+
+class _GradModeContext:
+    _target: bool
+
+    def __init__(self) -> None:
+        self._previous: list[bool] = []
+
+    def __enter__(self) -> None:
+        self._previous.append(_grad_mode.enabled)
+        _grad_mode.enabled = self._target
+
+    def __exit__(self, *exc: object) -> None:
+        _grad_mode.enabled = self._previous.pop()
+
+    def __call__(self, fn: Callable[..., _R]) -> Callable[..., _R]:
+        @functools.wraps(fn)
+        def wrapper(*args: Any, **kwargs: Any) -> _R:
+            with type(self)():
+                return fn(*args, **kwargs)
+
+        return wrapper
+
+
+class no_grad(_GradModeContext):  # noqa: N801
+    """Disable graph recording (context manager or decorator)."""
+
+    _target = False
+
+
+class enable_grad(_GradModeContext):  # noqa: N801
+    """Re-enable graph recording inside a :class:`no_grad` region."""
+
+    _target = True
+
+
+class Node:
+    """A recorded op: its inputs and the VJP that maps the output gradient to theirs."""
+
+    __slots__ = ("_backward", "op", "parents")
+
+    def __init__(self, op: str, parents: tuple[Tensor, ...], backward: BackwardFn) -> None:
+        self.op = op
+        self.parents = parents
+        self._backward: BackwardFn | None = backward
+
+    @property
+    def released(self) -> bool:
+        """``True`` once a backward pass without ``retain_graph`` freed the saved state."""
+        return self._backward is None
+
+    def check_alive(self) -> None:
+        if self._backward is None:
+            raise self._freed_error()
+
+    def _freed_error(self) -> RuntimeError:
+        return RuntimeError(
+            f"Trying to backward through the graph a second time (op '{self.op}'); "
+            "the saved intermediate values were freed. Pass retain_graph=True to the "
+            "first backward() call if you need to backpropagate through it again."
+        )
+
+    def apply(self, grad: DeviceArray, need: tuple[bool, ...]) -> tuple[DeviceArray | None, ...]:
+        self.check_alive()
+        assert self._backward is not None
+        return self._backward(grad, need)
+
+    def release(self) -> None:
+        """Drop the closure (and the device buffers it saved) and the parent references."""
+        self._backward = None
+        self.parents = ()
+
+    def __repr__(self) -> str:
+        return f"<Node {self.op}>"
+
+
+# ---------------------------------------------------------------------------- engine
+def _topological_order(roots: Sequence[Tensor]) -> list[Tensor]:
+    """Every tensor the roots depend on (requiring grad), inputs before outputs."""
+    order: list[Tensor] = []
+    seen: set[int] = set()
+    stack: list[tuple[Tensor, bool]] = [(r, False) for r in roots]
+    while stack:
+        t, done = stack.pop()
+        if done:
+            order.append(t)
+            continue
+        if id(t) in seen:
+            continue
+        seen.add(id(t))
+        stack.append((t, True))
+        node = t._node
+        if node is not None:
+            for p in node.parents:
+                if p._requires_grad and id(p) not in seen:
+                    stack.append((p, False))
+    return order
+
+
+def _leads_to(order: list[Tensor], targets: set[int]) -> set[int]:
+    """Ids of tensors in ``order`` that are targets or have a target among their inputs."""
+    live: set[int] = set()
+    for t in order:
+        node = t._node
+        if id(t) in targets or (node is not None and any(id(p) in live for p in node.parents)):
+            live.add(id(t))
+    return live
+
+
+#: Called as ``hook(leaf)`` right after a leaf's gradient for this backward pass is final.
+_leaf_hooks: list[Callable[[Tensor], None]] = []
+
+
+def add_leaf_hook(hook: Callable[[Tensor], None]) -> Callable[[], None]:
+    """Register ``hook(leaf)`` (used by data-parallel gradient bucketing); returns a remover."""
+    _leaf_hooks.append(hook)
+    return lambda: _leaf_hooks.remove(hook)
+
+
+def _run_backward(
+    roots: Sequence[Tensor],
+    seeds: Sequence[DeviceArray],
+    *,
+    retain_graph: bool,
+    targets: Sequence[Tensor] | None,
+) -> dict[int, DeviceArray]:
+    prof = _profiler.active()
+    if prof is None:
+        return _backward_pass(roots, seeds, retain_graph, targets, None)
+    return prof.timed(_profiler.ENGINE, _backward_pass, roots, seeds, retain_graph, targets, prof)
+
+
+def _backward_pass(
+    roots: Sequence[Tensor],
+    seeds: Sequence[DeviceArray],
+    retain_graph: bool,
+    targets: Sequence[Tensor] | None,
+    prof: Any,
+) -> dict[int, DeviceArray]:
+    order = _topological_order(roots)
+    target_ids = None if targets is None else {id(t) for t in targets}
+    live = None if target_ids is None else _leads_to(order, target_ids)
+    pending: dict[int, DeviceArray] = {}
+    for root, seed in zip(roots, seeds, strict=True):
+        prev = pending.get(id(root))
+        pending[id(root)] = seed if prev is None else prev + seed
+    captured: dict[int, DeviceArray] = {}
+    hooks = _leaf_hooks
+    for t in reversed(order):
+        g = pending.pop(id(t), None)
+        if g is None:
+            continue
+        node = t._node
+        if target_ids is not None:
+            if id(t) in target_ids:
+                captured[id(t)] = g
+        elif node is None or t._retains_grad:
+            t._accumulate_grad(g)
+            if node is None and hooks:
+                for h in hooks:
+                    h(t)
+        if node is None:
+            continue
+        fn = node._backward
+        if fn is None:
+            raise node._freed_error()
+        parents = node.parents
+        if live is None:
+            need = tuple([p._requires_grad for p in parents])
+        else:
+            need = tuple([p._requires_grad and id(p) in live for p in parents])
+        if not any(need):
+            continue
+        if prof is None:
+            grads = fn(g, need)
+        else:
+            grads = prof.timed(node.op, fn, g, need)
+        if len(grads) != len(parents):
+            raise RuntimeError(
+                f"op '{node.op}' returned {len(grads)} gradients for {len(parents)} inputs"
+            )
+        for p, pg, wanted in zip(parents, grads, need, strict=True):
+            if pg is None or not wanted:
+                continue
+            if pg.shape != p.shape:
+                raise RuntimeError(
+                    f"op '{node.op}' produced a gradient of shape {pg.shape} "
+                    f"for an input of shape {p.shape}"
+                )
+            prev = pending.get(id(p))
+            pending[id(p)] = pg if prev is None else prev + pg
+        if not retain_graph:
+            node.release()
+    return captured
+
+
+# ---------------------------------------------------------------------------- public API
+def _as_tensors(value: Any, what: str) -> tuple[Tensor, ...]:
+    from tensorgrad_b200.tensor import Tensor
+
+    items = (value,) if isinstance(value, Tensor) else tuple(value)
+    if not items:
+        raise ValueError(f"{what} must contain at least one tensor")
+    for item in items:
+        if not isinstance(item, Tensor):
+            raise TypeError(f"{what} must be tensors, got {type(item).__name__}")
+    return items
+
+
+def _seeds(outputs: tuple[Tensor, ...], grad_outputs: GradOutputs) -> list[DeviceArray]:
+    from tensorgrad_b200 import device
+    from tensorgrad_b200.tensor import Tensor
+
+    if grad_outputs is None:
+        given: list[Any] = [None] * len(outputs)
+    elif isinstance(grad_outputs, Tensor | np.ndarray | device.DeviceArray):
+        given = [grad_outputs]
+    else:
+        given = list(grad_outputs)
+    if len(given) != len(outputs):
+        raise ValueError(f"got {len(given)} grad_outputs for {len(outputs)} outputs")
+    seeds: list[DeviceArray] = []
+    for out, g in zip(outputs, given, strict=True):
+        if g is None:
+            if out.size != 1:
+                raise RuntimeError(
+                    "grad can be implicitly created only for single-element outputs; "
+                    f"got shape {out.shape}"
+                )
+            seeds.append(device.from_numpy(np.ones(out.shape, dtype=out.dtype)))
+            continue
+        if isinstance(g, Tensor):
+            g = g.data
+        if isinstance(g, device.DeviceArray):
+            seed = g if g.dtype == out.dtype else g.astype(out.dtype)
+        else:
+            seed = device.from_numpy(np.asarray(g, dtype=out.dtype))
+        if seed.shape != out.shape:
+            raise ValueError(f"grad has shape {seed.shape}, expected {out.shape}")
+        seeds.append(seed)
+    return seeds
+
+
+def _no_create_graph(create_graph: bool) -> None:
+    if create_graph:
+        raise NotImplementedError(
+            "create_graph=True (differentiable gradients) is not available on the device "
+            "backward path"
+        )
+
+
+def backward(
+    tensors: Tensor | Sequence[Tensor],
+    grad_tensors: GradOutputs = None,
+    retain_graph: bool | None = None,
+    create_graph: bool = False,
+) -> None:
+    """Accumulate d(sum of ``tensors``)/d(leaf) into the ``.grad`` of every leaf."""
+    _no_create_graph(create_graph)
+    outputs = _as_tensors(tensors, "tensors")
+    for out in outputs:
+        if not out.requires_grad:
+            raise RuntimeError("backward() called on a tensor that does not require grad")
+    seeds = _seeds(outputs, grad_tensors)
+    _run_backward(outputs, seeds, retain_graph=bool(retain_graph), targets=None)
+
+
+def grad(
+    outputs: Tensor | Sequence[Tensor],
+    inputs: Tensor | Sequence[Tensor],
+    grad_outputs: GradOutputs = None,
+    retain_graph: bool | None = None,
+    create_graph: bool = False,
+    allow_unused: bool = False,
+) -> tuple[Tensor | None, ...]:
+    """Gradients of ``outputs`` with respect to ``inputs``, returned instead of accumulated."""
+    from tensorgrad_b200.tensor import Tensor
+
+    _no_create_graph(create_graph)
+    outs = _as_tensors(outputs, "outputs")
+    ins = _as_tensors(inputs, "inputs")
+    for i, out in enumerate(outs):
+        if not out.requires_grad:
+            raise RuntimeError(f"output {i} does not require grad and has no graph")
+    for i, inp in enumerate(ins):
+        if not inp.requires_grad:
+            raise RuntimeError(f"input {i} does not require grad")
+    seeds = _seeds(outs, grad_outputs)
+    captured = _run_backward(outs, seeds, retain_graph=bool(retain_graph), targets=ins)
+    result: list[Tensor | None] = []
+    for i, inp in enumerate(ins):
+        g = captured.get(id(inp))
+        if g is None:
+            if not allow_unused:
+                raise RuntimeError(
+                    f"input {i} was not used to compute the outputs; pass allow_unused=True "
+                    "to get None for it instead"
+                )
+            result.append(None)
+        else:
+            # A fresh array: the engine may hand back aliases of other gradients.
+            result.append(Tensor._wrap(g.astype(inp.dtype, copy=True)))
+    return tuple(result)

@@ -1,0 +1,197 @@
+// GEMM entry points and the linear layer's forward/VJP built on them.
+#include <stdlib.h>
+
+#include <vector>
+
+#include "common.cuh"
+#include "gemm.cuh"
+#include "reduce.cuh"
+
+namespace tg {
+namespace {
+
+template <typename T>
+GemmArgs<T> make_args(int ta, int tb, int64_t m, int64_t n, int64_t k, double alpha,
+                      const void* a, int64_t lda, int64_t sa, const void* b, int64_t ldb,
+                      int64_t sb, double beta, void* c, int64_t ldc, int64_t sc,
+                      const void* bias, int64_t batch) {
+  GemmArgs<T> p;
+  p.m = m; p.n = n; p.k = k;
+  p.a = (const T*)a; p.lda = lda; p.stride_a = sa;
+  p.b = (const T*)b; p.ldb = ldb; p.stride_b = sb;
+  p.c = (T*)c; p.ldc = ldc; p.stride_c = sc;
+  p.bias = (const T*)bias;
+  p.alpha = (T)alpha; p.beta = (T)beta;
+  p.trans_a = ta; p.trans_b = tb;
+  p.batch = batch;
+  return p;
+}
+
+int check_gemm(int ta, int tb, int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
+               int64_t ldc) {
+  TG_CHECK_ARG(m >= 0 && n >= 0 && k >= 0, "gemm: negative size");
+  TG_CHECK_ARG(lda >= (ta ? m : k) || m == 0 || k == 0, "gemm: lda too small");
+  TG_CHECK_ARG(ldb >= (tb ? k : n) || n == 0 || k == 0, "gemm: ldb too small");
+  TG_CHECK_ARG(ldc >= n || m == 0, "gemm: ldc too small");
+  return TG_OK;
+}
+
+// Forcing the SIMT path for fp32 (set TG_GEMM=simt) is a debugging switch for users.
+bool force_simt() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("TG_GEMM");
+    v = (e && e[0] == 's') ? 1 : 0;
+  }
+  return v == 1;
+}
+
+// Live timing of tensor-core GEMM launches: when enabled, each launch is bracketed by two
+// CUDA events on its own stream; tg_gemm_profile_read() sums the elapsed times.
+struct ProfileRec {
+  cudaEvent_t start, stop;
+  double flops;
+};
+std::vector<ProfileRec> g_prof;
+std::vector<cudaEvent_t> g_event_pool;
+bool g_prof_on = false;
+
+cudaEvent_t take_event() {
+  if (!g_event_pool.empty()) {
+    cudaEvent_t e = g_event_pool.back();
+    g_event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e;
+  cudaEventCreate(&e);
+  return e;
+}
+
+template <typename T>
+int gemm_dispatch(const GemmArgs<T>& p, bool allow_tc, cudaStream_t s) {
+  if (p.m == 0 || p.n == 0) return TG_OK;
+  if (p.k == 0) {
+    // C = beta * C (+ bias): run the SIMT kernel, whose k loop is empty.
+    return gemm_simt<T>(p, s);
+  }
+  if constexpr (sizeof(T) == 4) {
+    if (allow_tc && !force_simt()) {
+      ProfileRec rec{};
+      if (g_prof_on) {
+        rec = {take_event(), take_event(), 2.0 * (double)p.m * (double)p.n * (double)p.k};
+        cudaEventRecord(rec.start, s);
+      }
+      const int rc = gemm_tc_f32(p, s);
+      if (g_prof_on) {
+        if (rc == TG_OK) {
+          cudaEventRecord(rec.stop, s);
+          g_prof.push_back(rec);
+        } else {
+          g_event_pool.push_back(rec.start);
+          g_event_pool.push_back(rec.stop);
+        }
+      }
+      if (rc != TG_ERR_UNSUPPORTED) return rc;
+    }
+  }
+  return gemm_simt<T>(p, s);
+}
+
+}  // namespace
+}  // namespace tg
+
+using namespace tg;
+
+extern "C" {
+
+int tg_gemm(int dtype, int trans_a, int trans_b, int64_t m, int64_t n, int64_t k, double alpha,
+            const void* a, int64_t lda, const void* b, int64_t ldb, double beta, void* c,
+            int64_t ldc, const void* bias, void* stream) {
+  const int rc = check_gemm(trans_a, trans_b, m, n, k, lda, ldb, ldc);
+  if (rc) return rc;
+  return TG_DISPATCH_FLOAT(dtype, T, [&] {
+    auto p = make_args<T>(trans_a, trans_b, m, n, k, alpha, a, lda, 0, b, ldb, 0, beta, c, ldc,
+                          0, bias, 1);
+    return gemm_dispatch<T>(p, true, as_stream(stream));
+  });
+}
+
+int tg_gemm_simt(int dtype, int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
+                 double alpha, const void* a, int64_t lda, const void* b, int64_t ldb,
+                 double beta, void* c, int64_t ldc, const void* bias, void* stream) {
+  const int rc = check_gemm(trans_a, trans_b, m, n, k, lda, ldb, ldc);
+  if (rc) return rc;
+  return TG_DISPATCH_FLOAT(dtype, T, [&] {
+    auto p = make_args<T>(trans_a, trans_b, m, n, k, alpha, a, lda, 0, b, ldb, 0, beta, c, ldc,
+                          0, bias, 1);
+    return gemm_dispatch<T>(p, false, as_stream(stream));
+  });
+}
+
+int tg_gemm_batched(int dtype, int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
+                    double alpha, const void* a, int64_t lda, int64_t stride_a, const void* b,
+                    int64_t ldb, int64_t stride_b, double beta, void* c, int64_t ldc,
+                    int64_t stride_c, int64_t batch, void* stream) {
+  const int rc = check_gemm(trans_a, trans_b, m, n, k, lda, ldb, ldc);
+  if (rc) return rc;
+  TG_CHECK_ARG(batch >= 0 && batch <= 65535, "gemm_batched: batch %lld out of range",
+               (long long)batch);
+  if (batch == 0) return TG_OK;
+  return TG_DISPATCH_FLOAT(dtype, T, [&] {
+    auto p = make_args<T>(trans_a, trans_b, m, n, k, alpha, a, lda, stride_a, b, ldb, stride_b,
+                          beta, c, ldc, stride_c, nullptr, batch);
+    if (batch == 1) return gemm_dispatch<T>(p, true, as_stream(stream));
+    return gemm_simt<T>(p, as_stream(stream));
+  });
+}
+
+int tg_gemm_profile(int enable) {
+  g_prof_on = enable != 0;
+  return TG_OK;
+}
+
+int tg_gemm_profile_read(double* total_ms, int64_t* launches, double* flops) {
+  double ms = 0.0, fl = 0.0;
+  for (auto& r : g_prof) {
+    TG_CUDA_TRY(cudaEventSynchronize(r.stop));
+    float t = 0.f;
+    TG_CUDA_TRY(cudaEventElapsedTime(&t, r.start, r.stop));
+    ms += t;
+    fl += r.flops;
+    g_event_pool.push_back(r.start);
+    g_event_pool.push_back(r.stop);
+  }
+  if (total_ms) *total_ms = ms;
+  if (launches) *launches = (int64_t)g_prof.size();
+  if (flops) *flops = fl;
+  g_prof.clear();
+  return TG_OK;
+}
+
+int tg_linear_forward(int dtype, const void* x, const void* w, const void* bias, void* y,
+                      int64_t rows, int64_t in_features, int64_t out_features, void* stream) {
+  return tg_gemm(dtype, 0, 1, rows, out_features, in_features, 1.0, x, in_features, w,
+                 in_features, 0.0, y, out_features, bias, stream);
+}
+
+int tg_linear_backward(int dtype, const void* g, const void* x, const void* w, void* gx, void* gw,
+                       void* gb, int64_t rows, int64_t in_features, int64_t out_features,
+                       unsigned need, double beta_gw, void* scratch, void* stream) {
+  int rc = TG_OK;
+  if ((need & 1) && gx) {
+    // gx[rows, in] = g[rows, out] @ w[out, in]
+    rc = tg_gemm(dtype, 0, 0, rows, in_features, out_features, 1.0, g, out_features, w,
+                 in_features, 0.0, gx, in_features, nullptr, stream);
+    if (rc) return rc;
+  }
+  if ((need & 2) && gw) {
+    // gw[out, in] = g^T @ x: A = g stored rows x out (k x m), B = x stored rows x in (k x n)
+    rc = tg_gemm(dtype, 1, 0, out_features, in_features, rows, 1.0, g, out_features, x,
+                 in_features, beta_gw, gw, in_features, nullptr, stream);
+    if (rc) return rc;
+  }
+  if ((need & 4) && gb) rc = tg_colsum(dtype, g, gb, rows, out_features, 0, scratch, stream);
+  return rc;
+}
+
+}  // extern "C"

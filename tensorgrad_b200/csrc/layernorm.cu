@@ -1,0 +1,235 @@
+// Row-wise LayerNorm forward and VJP (ops/layers.py:65-141).
+//
+// One warp per row with the row held in registers (cols <= 1024): the mean is taken first
+// and the variance from the centred values, as the reference does, so nothing is re-read
+// from HBM. The weight/bias gradients are column sums over rows: each block reduces its rows
+// in shared memory and writes one partial row to `scratch`; a second pass sums the partials
+// in a fixed order (deterministic).
+#include "common.cuh"
+#include "reduce.cuh"
+
+namespace tg {
+namespace {
+
+constexpr int kWarps = 4;
+
+template <typename T, int V>
+__global__ void __launch_bounds__(kWarps * 32)
+ln_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ b,
+              T* __restrict__ y, T* __restrict__ mean_out, T* __restrict__ rstd_out,
+              int64_t rows, int cols, T eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const int64_t nwarps = (int64_t)gridDim.x * kWarps;
+  for (int64_t r = warp0; r < rows; r += nwarps) {
+    const T* xr = x + r * cols;
+    T v[V];
+    T s = T(0);
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      const int c = lane + 32 * j;
+      v[j] = c < cols ? xr[c] : T(0);
+      s += v[j];
+    }
+    const T mean = warp_sum(s) / T(cols);
+    T q = T(0);
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      const int c = lane + 32 * j;
+      v[j] = c < cols ? v[j] - mean : T(0);
+      q += v[j] * v[j];
+    }
+    const T rstd = T(1) / dev_sqrt<T>(warp_sum(q) / T(cols) + eps);
+    T* yr = y + r * cols;
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      const int c = lane + 32 * j;
+      if (c < cols) {
+        T o = v[j] * rstd;
+        if (w) o *= w[c];
+        if (b) o += b[c];
+        yr[c] = o;
+      }
+    }
+    if (lane == 0) {
+      mean_out[r] = mean;
+      rstd_out[r] = rstd;
+    }
+  }
+}
+
+template <typename T, int V>
+__global__ void __launch_bounds__(kWarps * 32)
+ln_bwd_kernel(const T* __restrict__ g, const T* __restrict__ x, const T* __restrict__ w,
+              const T* __restrict__ mean_in, const T* __restrict__ rstd_in, T* __restrict__ gx,
+              T* __restrict__ part_w, T* __restrict__ part_b, int64_t rows, int cols) {
+  extern __shared__ unsigned char smem_raw[];
+  T* sh = reinterpret_cast<T*>(smem_raw);  // [kWarps][2][cols]
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int64_t warp0 = (int64_t)blockIdx.x * kWarps + wid;
+  const int64_t nwarps = (int64_t)gridDim.x * kWarps;
+  const bool want_wb = part_w != nullptr;
+  T aw[V], ab[V];
+#pragma unroll
+  for (int j = 0; j < V; ++j) aw[j] = ab[j] = T(0);
+  for (int64_t r = warp0; r < rows; r += nwarps) {
+    const T* xr = x + r * cols;
+    const T* gr = g + r * cols;
+    const T mean = mean_in[r], rstd = rstd_in[r];
+    T xh[V], gh[V];
+    T s1 = T(0), s2 = T(0);
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      const int c = lane + 32 * j;
+      if (c < cols) {
+        xh[j] = (xr[c] - mean) * rstd;
+        const T gv = gr[c];
+        aw[j] += gv * xh[j];
+        ab[j] += gv;
+        gh[j] = w ? gv * w[c] : gv;
+      } else {
+        xh[j] = gh[j] = T(0);
+      }
+      s1 += gh[j];
+      s2 += gh[j] * xh[j];
+    }
+    if (gx) {
+      const T m1 = warp_sum(s1) / T(cols), m2 = warp_sum(s2) / T(cols);
+      T* gxr = gx + r * cols;
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        const int c = lane + 32 * j;
+        if (c < cols) gxr[c] = rstd * (gh[j] - m1 - xh[j] * m2);
+      }
+    }
+  }
+  if (!want_wb) return;
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int c = lane + 32 * j;
+    if (c < cols) {
+      sh[(wid * 2 + 0) * cols + c] = aw[j];
+      sh[(wid * 2 + 1) * cols + c] = ab[j];
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    T sw = T(0), sb = T(0);
+#pragma unroll
+    for (int i = 0; i < kWarps; ++i) {
+      sw += sh[(i * 2 + 0) * cols + c];
+      sb += sh[(i * 2 + 1) * cols + c];
+    }
+    part_w[(int64_t)blockIdx.x * cols + c] = sw;
+    part_b[(int64_t)blockIdx.x * cols + c] = sb;
+  }
+}
+
+template <typename T>
+__global__ void ln_final_kernel(const T* __restrict__ part_w, const T* __restrict__ part_b,
+                                T* __restrict__ gw, T* __restrict__ gb, int nparts, int cols) {
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < cols; c += gridDim.x * blockDim.x) {
+    T sw = T(0), sb = T(0);
+    for (int i = 0; i < nparts; ++i) {
+      sw += part_w[(int64_t)i * cols + c];
+      sb += part_b[(int64_t)i * cols + c];
+    }
+    if (gw) gw[c] = sw;
+    if (gb) gb[c] = sb;
+  }
+}
+
+int ln_blocks(int64_t rows) {
+  int64_t b = (rows + kWarps - 1) / kWarps;
+  if (b > 2 * 148) b = 2 * 148;
+  if (b < 1) b = 1;
+  return (int)b;
+}
+
+template <typename T, int V>
+int ln_forward_v(const T* x, const T* w, const T* b, T* y, T* mean, T* rstd, int64_t rows,
+                 int cols, T eps, cudaStream_t s) {
+  ln_fwd_kernel<T, V><<<ln_blocks(rows), kWarps * 32, 0, s>>>(x, w, b, y, mean, rstd, rows,
+                                                              cols, eps);
+  return check_launch("layer_norm_forward");
+}
+
+template <typename T, int V>
+int ln_backward_v(const T* g, const T* x, const T* w, const T* mean, const T* rstd, T* gx,
+                  T* gw, T* gb, int64_t rows, int cols, void* scratch, cudaStream_t s) {
+  const int nb = ln_blocks(rows);
+  T* part_w = nullptr;
+  T* part_b = nullptr;
+  if (gw || gb) {
+    part_w = reinterpret_cast<T*>(scratch);
+    part_b = part_w + (int64_t)nb * cols;
+  }
+  const size_t smem = (gw || gb) ? (size_t)kWarps * 2 * cols * sizeof(T) : 0;
+  if (smem > 48 * 1024)
+    TG_CUDA_TRY(cudaFuncSetAttribute(ln_bwd_kernel<T, V>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  ln_bwd_kernel<T, V><<<nb, kWarps * 32, smem, s>>>(g, x, w, mean, rstd, gx, part_w, part_b,
+                                                    rows, cols);
+  if (gw || gb)
+    ln_final_kernel<T><<<grid_for(cols, 256), 256, 0, s>>>(part_w, part_b, gw, gb, nb, cols);
+  return check_launch("layer_norm_backward", (gw || gb) ? 2 : 1);
+}
+
+}  // namespace
+}  // namespace tg
+
+using namespace tg;
+
+extern "C" {
+
+int tg_layer_norm_forward(int dtype, const void* x, const void* w, const void* b, void* y,
+                          void* mean, void* rstd, int64_t rows, int64_t cols, double eps,
+                          void* stream) {
+  TG_CHECK_ARG(cols > 0 && cols <= 1024, "layer_norm: %lld columns (supported: 1..1024)",
+               (long long)cols);
+  if (rows <= 0) return TG_OK;
+  cudaStream_t s = as_stream(stream);
+  return TG_DISPATCH_FLOAT(dtype, T, [&] {
+    const int c = (int)cols;
+    auto* X = (const T*)x; auto* W = (const T*)w; auto* B = (const T*)b;
+    auto* Y = (T*)y; auto* M = (T*)mean; auto* R = (T*)rstd;
+    if (c <= 128) return ln_forward_v<T, 4>(X, W, B, Y, M, R, rows, c, (T)eps, s);
+    if (c <= 256) return ln_forward_v<T, 8>(X, W, B, Y, M, R, rows, c, (T)eps, s);
+    if (c <= 512) return ln_forward_v<T, 16>(X, W, B, Y, M, R, rows, c, (T)eps, s);
+    return ln_forward_v<T, 32>(X, W, B, Y, M, R, rows, c, (T)eps, s);
+  });
+}
+
+size_t tg_layer_norm_scratch_bytes(int dtype, int64_t rows, int64_t cols) {
+  const size_t es = dtype == TG_F64 ? 8 : 4;
+  return (size_t)ln_blocks(rows) * 2 * (size_t)cols * es;
+}
+
+int tg_layer_norm_backward(int dtype, const void* g, const void* x, const void* w,
+                           const void* mean, const void* rstd, void* gx, void* gw, void* gb,
+                           int64_t rows, int64_t cols, unsigned need, void* scratch,
+                           void* stream) {
+  TG_CHECK_ARG(cols > 0 && cols <= 1024, "layer_norm: %lld columns (supported: 1..1024)",
+               (long long)cols);
+  if (!(need & 1)) gx = nullptr;
+  if (!(need & 2)) gw = nullptr;
+  if (!(need & 4)) gb = nullptr;
+  if (gw || gb) TG_CHECK_ARG(scratch != nullptr, "layer_norm_backward: scratch is NULL");
+  cudaStream_t s = as_stream(stream);
+  if (rows <= 0) {
+    if (gw) TG_CUDA_TRY(cudaMemsetAsync(gw, 0, cols * (dtype == TG_F64 ? 8 : 4), s));
+    if (gb) TG_CUDA_TRY(cudaMemsetAsync(gb, 0, cols * (dtype == TG_F64 ? 8 : 4), s));
+    return TG_OK;
+  }
+  return TG_DISPATCH_FLOAT(dtype, T, [&] {
+    const int c = (int)cols;
+    auto* G = (const T*)g; auto* X = (const T*)x; auto* W = (const T*)w;
+    auto* M = (const T*)mean; auto* R = (const T*)rstd;
+    if (c <= 128) return ln_backward_v<T, 4>(G, X, W, M, R, (T*)gx, (T*)gw, (T*)gb, rows, c, scratch, s);
+    if (c <= 256) return ln_backward_v<T, 8>(G, X, W, M, R, (T*)gx, (T*)gw, (T*)gb, rows, c, scratch, s);
+    if (c <= 512) return ln_backward_v<T, 16>(G, X, W, M, R, (T*)gx, (T*)gw, (T*)gb, rows, c, scratch, s);
+    return ln_backward_v<T, 32>(G, X, W, M, R, (T*)gx, (T*)gw, (T*)gb, rows, c, scratch, s);
+  });
+}
+
+}  // extern "C"

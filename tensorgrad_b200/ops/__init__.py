@@ -1,0 +1,22 @@
+"""Differentiable ops on device tensors; each records a node whose VJP runs device kernels."""
+
+from tensorgrad_b200 import tensor as _tensor  # noqa: F401  (binds Tensor before the ops)
+from tensorgrad_b200.ops.attention import packed_self_attention, scaled_dot_product_attention
+from tensorgrad_b200.ops.elementwise import (
+    add, astype, div, exp, gelu, log, mul, neg, pow, relu, sigmoid, sqrt, sub, tanh,
+)
+from tensorgrad_b200.ops.layers import batch_norm, dropout, embedding, layer_norm, linear
+from tensorgrad_b200.ops.linalg import matmul
+from tensorgrad_b200.ops.loss import cross_entropy, mse_loss
+from tensorgrad_b200.ops.reduce import max, mean, min, sum, var
+from tensorgrad_b200.ops.shape import (
+    broadcast_to, flatten, getitem, permute, reshape, squeeze, sum_to, transpose, unsqueeze,
+)
+
+__all__ = [
+    "add", "astype", "batch_norm", "broadcast_to", "cross_entropy", "div", "dropout",
+    "embedding", "exp", "flatten", "gelu", "getitem", "layer_norm", "linear", "log", "matmul",
+    "max", "mean", "min", "mse_loss", "mul", "neg", "packed_self_attention", "permute", "pow",
+    "relu", "reshape", "scaled_dot_product_attention", "sigmoid", "sqrt", "squeeze", "sub",
+    "sum", "sum_to", "tanh", "transpose", "unsqueeze", "var",
+]

@@ -1,0 +1,88 @@
+"""Helpers shared by the op implementations (the reference's ops/_util.py:12-92)."""
+
+from __future__ import annotations
+
+import math
+from typing import Any
+
+import numpy as np
+
+from tensorgrad_b200 import device
+from tensorgrad_b200._lib import check, int64_array, int_array, lib
+from tensorgrad_b200.autograd import BackwardFn, Node, is_grad_enabled
+from tensorgrad_b200.device import DeviceArray, dtype_code
+from tensorgrad_b200.tensor import Tensor
+
+Need = tuple[bool, ...]
+
+
+def as_tensor(x: Any, like: Tensor | None = None) -> Tensor:
+    """``x`` as a tensor; Python scalars adopt the floating dtype of ``like``."""
+    if isinstance(x, Tensor):
+        return x
+    if isinstance(x, int | float) and like is not None and np.issubdtype(like.dtype, np.floating):
+        return Tensor._wrap(device.from_numpy(np.asarray(x, dtype=like.dtype)))
+    return Tensor(x)
+
+
+def coerce_pair(a: Any, b: Any) -> tuple[Tensor, Tensor]:
+    ta = a if isinstance(a, Tensor) else None
+    tb = b if isinstance(b, Tensor) else None
+    return as_tensor(a, tb), as_tensor(b, ta)
+
+
+def make_result(data: DeviceArray, parents: tuple[Tensor, ...], backward: BackwardFn,
+                op: str) -> Tensor:
+    """Wrap an op's output, recording a graph node if any input requires grad
+    (ops/_util.py:28-46). ``backward`` is the VJP on device arrays."""
+    out = Tensor._wrap(data)
+    if is_grad_enabled() and any(p._requires_grad for p in parents):
+        out._requires_grad = True
+        out._node = Node(op, parents, backward)
+    return out
+
+
+def unbroadcast(grad: DeviceArray, shape: tuple[int, ...]) -> DeviceArray:
+    """Sum ``grad`` down to ``shape``: the adjoint of broadcasting (ops/_util.py:49-63).
+
+    Summing over leading axes only (bias and position-embedding gradients) is a column sum;
+    anything else goes through the keep-axis reduction.
+    """
+    if grad.shape == shape:
+        return grad
+    extra = grad.ndim - len(shape)
+    full = (1,) * extra + tuple(shape)
+    keep = [not (i < extra or (full[i] == 1 and grad.shape[i] != 1)) for i in range(grad.ndim)]
+    code = dtype_code(grad.dtype)
+    # Leading summed axes followed only by kept ones: a column sum over a 2-D view.
+    first_keep = keep.index(True) if True in keep else grad.ndim
+    if all(keep[first_keep:]):
+        rows = math.prod(grad.shape[:first_keep])
+        cols = math.prod(grad.shape[first_keep:])
+        out = device.empty(shape, grad.dtype)
+        scratch = device.scratch(lib.tg_colsum_scratch_bytes(code, rows, cols))
+        check(lib.tg_colsum(code, grad.ptr, out.ptr, rows, cols, 0, scratch.ptr,
+                            device.stream()), "unbroadcast")
+        return out
+    out = device.empty(shape, grad.dtype)
+    check(lib.tg_reduce_sum(code, grad.ndim, int64_array(grad.shape), int_array(keep),
+                            grad.ptr, out.ptr, device.stream()), "unbroadcast")
+    return out
+
+
+def normalize_axes(axis: Any, ndim: int) -> tuple[int, ...]:
+    if axis is None:
+        return tuple(range(ndim))
+    axes = (axis,) if isinstance(axis, int) else tuple(axis)
+    out = []
+    for ax in axes:
+        if not -ndim <= ax < max(ndim, 1):
+            raise np.exceptions.AxisError(ax, ndim)
+        out.append(ax % ndim if ndim else 0)
+    return tuple(sorted(set(out)))
+
+
+def normalize_axis(axis: int, ndim: int) -> int:
+    if not -ndim <= axis < ndim:
+        raise np.exceptions.AxisError(axis, ndim)
+    return axis % ndim

@@ -1,0 +1,159 @@
+"""Fused scaled-dot-product attention (the reference's ops/attention.py:40-272).
+
+``softmax(q k^T / sqrt(d) + causal mask) v`` as one graph node backed by the flash-style
+kernels of ``attention.cu``: the forward keeps the output and one log-sum-exp per query row
+instead of the ``(T_q, T_k)`` probabilities, and the VJP recomputes them.
+:func:`packed_self_attention` reads Q, K and V as strided views of the packed ``(B, T, 3D)``
+QKV projection and writes their gradients straight into one ``(B, T, 3D)`` buffer, as the
+reference does.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Any
+
+import numpy as np
+
+from tensorgrad_b200 import device
+from tensorgrad_b200._lib import AttnShape, check, lib
+from tensorgrad_b200.device import DeviceArray, dtype_code
+from tensorgrad_b200.ops._util import Need, as_tensor, make_result, unbroadcast
+from tensorgrad_b200.ops.elementwise import cast_array
+from tensorgrad_b200.profiler import profiled
+from tensorgrad_b200.tensor import Tensor
+
+__all__ = ["causal_mask", "packed_self_attention", "scaled_dot_product_attention"]
+
+
+def causal_mask(q_len: int, k_len: int) -> np.ndarray:
+    """Boolean mask, ``True`` where attention is forbidden (ops/attention.py:40-49)."""
+    return np.triu(np.ones((q_len, k_len), dtype=np.bool_), k=1 + k_len - q_len)
+
+
+def _shape(b: int, h: int, tq: int, tk: int, d: int, q: tuple[int, int, int],
+           k: tuple[int, int, int], v: tuple[int, int, int], o: tuple[int, int, int],
+           causal: bool) -> AttnShape:
+    return AttnShape(b, h, tq, tk, d, *q, *k, *v, *o, 1 if causal else 0)
+
+
+def _forward(shape: AttnShape, code: int, q: int, k: int, v: int, o: int, lse: int) -> None:
+    check(lib.tg_attention_forward(code, shape, q, k, v, o, lse, device.stream()), "attention")
+
+
+def _backward(shape: AttnShape, code: int, q: int, k: int, v: int, o: int, lse: int, do: int,
+              dq: int, dk: int, dv: int) -> None:
+    scratch = device.scratch(lib.tg_attention_scratch_bytes(code, shape))
+    check(lib.tg_attention_backward(code, shape, q, k, v, o, lse, do, dq, dk, dv, scratch.ptr,
+                                    device.stream()), "attention backward")
+
+
+def _as_bhtd(shape: tuple[int, ...]) -> tuple[int, int]:
+    """(B, H) of a ``(..., T, d)`` array: the batch axes collapse into B (and H = 1) unless
+    there are exactly two."""
+    lead = shape[:-2]
+    if len(lead) == 2:
+        return lead[0], lead[1]
+    return math.prod(lead), 1
+
+
+@profiled("attention")
+def scaled_dot_product_attention(
+    q: Any, k: Any, v: Any, *, causal: bool = False, mask: Any = None, dropout_p: float = 0.0,
+    training: bool = False, rng: np.random.Generator | None = None,
+) -> Tensor:
+    """``softmax(q k^T / sqrt(d)) v`` over the last two axes, fused (ops/attention.py:163-208).
+
+    ``q, k, v`` share their batch axes, or ``k``/``v`` broadcast over them (e.g. shared
+    across heads); their gradients are then summed back (ops/attention.py:211-213). An extra
+    boolean ``mask`` and attention dropout are not part of the fused device kernel.
+    """
+    if mask is not None:
+        raise NotImplementedError("scaled_dot_product_attention: only the causal mask is fused")
+    if training and dropout_p > 0.0:
+        raise NotImplementedError("attention dropout is not fused into the device kernel")
+    tq, tk, tv = as_tensor(q), as_tensor(k), as_tensor(v)
+    dt = np.result_type(tq.dtype, tk.dtype, tv.dtype)
+    qd, kd, vd = (t.data if t.dtype == dt else cast_array(t.data, dt) for t in (tq, tk, tv))
+    batch = tuple(np.broadcast_shapes(tq.shape[:-2], tk.shape[:-2], tv.shape[:-2]))
+    n_q, d = tq.shape[-2], tq.shape[-1]
+    n_k = tk.shape[-2]
+    if tk.shape[-1] != d or tv.shape[-1] != d or tv.shape[-2] != n_k:
+        raise ValueError(f"attention: incompatible q {tq.shape}, k {tk.shape}, v {tv.shape}")
+    full_shapes = [(*batch, n_q, d), (*batch, n_k, d), (*batch, n_k, d)]
+
+    def materialise(a: DeviceArray, full: tuple[int, ...]) -> DeviceArray:
+        if a.shape == full:
+            return a
+        from tensorgrad_b200.ops.shape import broadcast_array
+
+        return broadcast_array(a, full)
+
+    qf, kf, vf = (materialise(a, s) for a, s in zip((qd, kd, vd), full_shapes, strict=True))
+    b, h = _as_bhtd(full_shapes[0])
+    qs = (h * n_q * d, n_q * d, d)
+    ks = (h * n_k * d, n_k * d, d)
+    shp = _shape(b, h, n_q, n_k, d, qs, ks, ks, qs, causal)
+    code = dtype_code(dt)
+    out = device.empty(full_shapes[0], dt)
+    lse = device.empty((b * h * n_q,), dt)
+    _forward(shp, code, qf.ptr, kf.ptr, vf.ptr, out.ptr, lse.ptr)
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray | None, ...]:
+        if g.dtype != dt:
+            g = cast_array(g, dt)
+        dq = device.empty(full_shapes[0], dt)
+        dk = device.empty(full_shapes[1], dt)
+        dv = device.empty(full_shapes[2], dt)
+        _backward(shp, code, qf.ptr, kf.ptr, vf.ptr, out.ptr, lse.ptr, g.ptr, dq.ptr, dk.ptr,
+                  dv.ptr)
+        grads = []
+        for gr, t, wanted in zip((dq, dk, dv), (tq, tk, tv), need, strict=True):
+            if not wanted:
+                grads.append(None)
+                continue
+            gr = unbroadcast(gr, t.shape)
+            grads.append(gr if gr.dtype == t.dtype else cast_array(gr, t.dtype))
+        return tuple(grads)
+
+    return make_result(out, (tq, tk, tv), backward, "attention")
+
+
+@profiled("self_attention")
+def packed_self_attention(
+    qkv: Any, num_heads: int, *, causal: bool = True, dropout_p: float = 0.0,
+    training: bool = False, rng: np.random.Generator | None = None,
+) -> Tensor:
+    """Multi-head self-attention on a packed ``(B, T, 3 * D)`` QKV projection; returns merged
+    heads ``(B, T, D)`` (ops/attention.py:223-272)."""
+    tqkv = as_tensor(qkv)
+    if tqkv.ndim != 3 or tqkv.shape[-1] % (3 * num_heads):
+        raise ValueError(
+            f"expected (B, T, 3 * D) with D divisible by {num_heads}, got {tqkv.shape}"
+        )
+    if training and dropout_p > 0.0:
+        raise NotImplementedError("attention dropout is not fused into the device kernel")
+    b, t, d3 = tqkv.shape
+    d = d3 // 3
+    hd = d // num_heads
+    x = tqkv.data
+    code = dtype_code(x.dtype)
+    es = x.itemsize
+    src = (t * d3, hd, d3)           # strides of q, k, v inside the packed buffer
+    dst = (t * d, hd, d)             # strides of the merged-head output
+    shp = _shape(b, num_heads, t, t, hd, src, src, src, dst, causal)
+    out = device.empty((b, t, d), x.dtype)
+    lse = device.empty((b * num_heads * t,), x.dtype)
+    base = x.ptr
+    _forward(shp, code, base, base + d * es, base + 2 * d * es, out.ptr, lse.ptr)
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+        if g.dtype != x.dtype:
+            g = cast_array(g, x.dtype)
+        dqkv = device.empty((b, t, d3), x.dtype)
+        gb = dqkv.ptr
+        _backward(shp, code, base, base + d * es, base + 2 * d * es, out.ptr, lse.ptr, g.ptr,
+                  gb, gb + d * es, gb + 2 * d * es)
+        return (dqkv,)
+
+    return make_result(out, (tqkv,), backward, "self_attention")

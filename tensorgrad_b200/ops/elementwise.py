@@ -1,0 +1,260 @@
+"""Elementwise arithmetic and pointwise non-linearities (the reference's ops/elementwise.py).
+
+Forward values and VJPs follow ops/elementwise.py:43-343; each runs as one device kernel.
+"""
+
+from __future__ import annotations
+
+from typing import Any
+
+import numpy as np
+
+from tensorgrad_b200 import device
+from tensorgrad_b200._lib import (
+    ADD, DIV, EXP, F32, F64, LOG, MUL, NEG, POW, POWS, SIGMOID, SQRT, SUB, TANH, check, int64_array,
+    lib,
+)
+from tensorgrad_b200.device import DeviceArray, dtype_code
+from tensorgrad_b200.ops._util import Need, as_tensor, coerce_pair, make_result, unbroadcast
+from tensorgrad_b200.profiler import profiled
+from tensorgrad_b200.tensor import Tensor
+
+__all__ = ["add", "astype", "div", "exp", "gelu", "log", "mul", "neg", "pow", "relu", "sigmoid",
+           "sqrt", "sub", "tanh"]
+
+_CAST_CODES = {np.dtype(np.float32): F32, np.dtype(np.float64): F64, np.dtype(np.int64): 2}
+
+
+def cast_array(x: DeviceArray, dtype: np.dtype[Any]) -> DeviceArray:
+    out = device.empty(x.shape, dtype)
+    check(lib.tg_cast(_CAST_CODES[x.dtype], _CAST_CODES[np.dtype(dtype)], x.size, x.ptr, out.ptr,
+                      device.stream()), "astype")
+    return out
+
+
+def _promote(a: DeviceArray, b: DeviceArray) -> tuple[DeviceArray, DeviceArray, np.dtype[Any]]:
+    if a.dtype == b.dtype and a.dtype.kind == "f":
+        return a, b, a.dtype
+    dt = np.result_type(a.dtype, b.dtype)
+    if dt.kind != "f":
+        dt = np.dtype(np.float64)
+    return (a if a.dtype == dt else cast_array(a, dt)), (b if b.dtype == dt else cast_array(b, dt)), dt
+
+
+def _bcast_strides(shape: tuple[int, ...], out_shape: tuple[int, ...]) -> list[int]:
+    strides = device.contiguous_strides(shape)
+    pad = len(out_shape) - len(shape)
+    res = [0] * pad
+    for i, n in enumerate(shape):
+        res.append(0 if (n == 1 and out_shape[pad + i] != 1) else strides[i])
+    return res
+
+
+def binary_array(a: DeviceArray, b: DeviceArray, op: int, out: DeviceArray | None = None) -> DeviceArray:
+    """``a op b`` with NumPy broadcasting, into a new array (or ``out``)."""
+    a, b, dt = _promote(a, b)
+    shape = a.shape if a.shape == b.shape else tuple(np.broadcast_shapes(a.shape, b.shape))
+    if out is None:
+        out = device.empty(shape, dt)
+    sa = _bcast_strides(a.shape, shape) if a.shape != shape else device.contiguous_strides(shape)
+    sb = _bcast_strides(b.shape, shape) if b.shape != shape else device.contiguous_strides(shape)
+    check(lib.tg_binary(dtype_code(dt), op, len(shape), int64_array(shape), a.ptr,
+                        int64_array(sa), b.ptr, int64_array(sb), out.ptr, device.stream()),
+          "binary op")
+    return out
+
+
+def scale_array(x: DeviceArray, alpha: float) -> DeviceArray:
+    out = device.empty(x.shape, x.dtype)
+    check(lib.tg_axpby(dtype_code(x.dtype), x.size, alpha, x.ptr, 0.0, None, out.ptr,
+                       device.stream()), "scale")
+    return out
+
+
+def _unary(x: DeviceArray, op: int, alpha: float = 0.0) -> DeviceArray:
+    out = device.empty(x.shape, x.dtype)
+    check(lib.tg_unary(dtype_code(x.dtype), op, x.size, x.ptr, alpha, out.ptr, device.stream()),
+          "unary op")
+    return out
+
+
+def _unary_bwd(op: int, g: DeviceArray, x: DeviceArray | None, y: DeviceArray | None,
+               alpha: float = 0.0) -> DeviceArray:
+    out = device.empty(g.shape, g.dtype)
+    check(lib.tg_unary_backward(dtype_code(g.dtype), op, g.size, g.ptr,
+                                x.ptr if x is not None else None,
+                                y.ptr if y is not None else None, alpha, out.ptr,
+                                device.stream()), "unary backward")
+    return out
+
+
+def _float_input(t: Tensor) -> DeviceArray:
+    return t.data if t.dtype.kind == "f" else cast_array(t.data, np.dtype(np.float64))
+
+
+@profiled("add")
+def add(a: Any, b: Any) -> Tensor:
+    """``a + b`` with broadcasting (ops/elementwise.py:43-60)."""
+    ta, tb = coerce_pair(a, b)
+    sa, sb = ta.shape, tb.shape
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray | None, DeviceArray | None]:
+        return (unbroadcast(g, sa) if need[0] else None, unbroadcast(g, sb) if need[1] else None)
+
+    return make_result(binary_array(ta.data, tb.data, ADD), (ta, tb), backward, "add")
+
+
+@profiled("sub")
+def sub(a: Any, b: Any) -> Tensor:
+    """``a - b`` (ops/elementwise.py:63-80)."""
+    ta, tb = coerce_pair(a, b)
+    sa, sb = ta.shape, tb.shape
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray | None, DeviceArray | None]:
+        return (unbroadcast(g, sa) if need[0] else None,
+                unbroadcast(scale_array(g, -1.0), sb) if need[1] else None)
+
+    return make_result(binary_array(ta.data, tb.data, SUB), (ta, tb), backward, "sub")
+
+
+@profiled("mul")
+def mul(a: Any, b: Any) -> Tensor:
+    """``a * b`` (ops/elementwise.py:83-100)."""
+    ta, tb = coerce_pair(a, b)
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray | None, DeviceArray | None]:
+        return (unbroadcast(binary_array(g, tb.data, MUL), ta.shape) if need[0] else None,
+                unbroadcast(binary_array(g, ta.data, MUL), tb.shape) if need[1] else None)
+
+    return make_result(binary_array(ta.data, tb.data, MUL), (ta, tb), backward, "mul")
+
+
+@profiled("div")
+def div(a: Any, b: Any) -> Tensor:
+    """``a / b`` (ops/elementwise.py:103-121)."""
+    ta, tb = coerce_pair(a, b)
+    out = binary_array(ta.data, tb.data, DIV)
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray | None, DeviceArray | None]:
+        ga = unbroadcast(binary_array(g, tb.data, DIV), ta.shape) if need[0] else None
+        gb = None
+        if need[1]:
+            t = binary_array(binary_array(g, out, MUL), tb.data, DIV)
+            gb = unbroadcast(scale_array(t, -1.0), tb.shape)
+        return ga, gb
+
+    return make_result(out, (ta, tb), backward, "div")
+
+
+@profiled("neg")
+def neg(a: Any) -> Tensor:
+    """``-a`` (ops/elementwise.py:124-135)."""
+    ta = as_tensor(a)
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+        return (scale_array(g, -1.0),)
+
+    return make_result(scale_array(ta.data, -1.0), (ta,), backward, "neg")
+
+
+@profiled("pow")
+def pow(base: Any, exponent: Any) -> Tensor:  # noqa: A001
+    """``base ** exponent`` (ops/elementwise.py:138-167). A Python-number exponent runs as one
+    kernel; the gradient with respect to a tensor exponent is not on the device path."""
+    if isinstance(exponent, int | float) and isinstance(base, Tensor):
+        tb = base
+        e = float(exponent)
+        x = _float_input(tb)
+
+        def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+            return (_unary_bwd(POWS, g, x, None, e),)
+
+        return make_result(_unary(x, POWS, e), (tb,), backward, "pow")
+    tb, te = coerce_pair(base, exponent)
+    out = binary_array(tb.data, te.data, POW)
+
+    def backward2(g: DeviceArray, need: Need) -> tuple[DeviceArray | None, DeviceArray | None]:
+        if need[1]:
+            raise NotImplementedError("pow: gradient with respect to a tensor exponent")
+        em1 = binary_array(te.data, device.scalar_like(1.0, te.dtype), SUB)
+        d = binary_array(binary_array(g, te.data, MUL), binary_array(tb.data, em1, POW), MUL)
+        return unbroadcast(d, tb.shape), None
+
+    return make_result(out, (tb, te), backward2, "pow")
+
+
+def _unary_op(name: str, op: int, use_out: bool) -> Any:
+    @profiled(name)
+    def fn(a: Any) -> Tensor:
+        ta = as_tensor(a)
+        x = _float_input(ta)
+        out = _unary(x, op)
+
+        def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+            return (_unary_bwd(op, g, None if use_out else x, out if use_out else None),)
+
+        return make_result(out, (ta,), backward, name)
+
+    fn.__name__ = name
+    return fn
+
+
+exp = _unary_op("exp", EXP, True)        # ops/elementwise.py:170-181
+log = _unary_op("log", LOG, False)       # :184-195
+sqrt = _unary_op("sqrt", SQRT, True)     # :198-210
+tanh = _unary_op("tanh", TANH, True)     # :213-225
+sigmoid = _unary_op("sigmoid", SIGMOID, True)  # :240-252
+
+
+@profiled("relu")
+def relu(a: Any) -> Tensor:
+    """``max(a, 0)``; the VJP is ``g * (a > 0)`` (ops/elementwise.py:255-268)."""
+    ta = as_tensor(a)
+    x = ta.data
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+        out = device.empty(g.shape, g.dtype)
+        check(lib.tg_relu_backward(dtype_code(g.dtype), g.size, g.ptr, x.ptr, out.ptr,
+                                   device.stream()), "relu backward")
+        return (out,)
+
+    return make_result(_unary(x, 6), (ta,), backward, "relu")
+
+
+@profiled("gelu")
+def gelu(a: Any) -> Tensor:
+    """Tanh-approximate GELU; the VJP recomputes ``tanh`` from the saved input instead of
+    storing it (ops/elementwise.py:275-320)."""
+    ta = as_tensor(a)
+    x = _float_input(ta)
+    out = device.empty(x.shape, x.dtype)
+    check(lib.tg_gelu_forward(dtype_code(x.dtype), x.size, x.ptr, out.ptr, device.stream()),
+          "gelu")
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+        gx = device.empty(g.shape, g.dtype)
+        check(lib.tg_gelu_backward(dtype_code(g.dtype), g.size, g.ptr, x.ptr, gx.ptr,
+                                   device.stream()), "gelu backward")
+        return (gx,)
+
+    return make_result(out, (ta,), backward, "gelu")
+
+
+@profiled("astype")
+def astype(a: Any, dtype: Any) -> Tensor:
+    """Dtype conversion; integer results are constants (ops/elementwise.py:323-343)."""
+    ta = as_tensor(a)
+    source = ta.dtype
+    dt = np.dtype(dtype)
+    out = ta.data.copy() if dt == source else cast_array(ta.data, dt)
+    if dt.kind != "f":
+        return Tensor._wrap(out)
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+        return (g if g.dtype == source else cast_array(g, source),)
+
+    return make_result(out, (ta,), backward, "astype")
+
+
+# NEG kept for symmetry with the C enum (used by callers that negate in place).
+_ = NEG

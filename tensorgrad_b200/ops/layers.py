@@ -1,0 +1,230 @@
+"""Fused building blocks used by :mod:`tensorgrad_b200.nn` (the reference's ops/layers.py):
+linear, layer norm, batch norm, embedding and dropout."""
+
+from __future__ import annotations
+
+from typing import Any
+
+import numpy as np
+
+from tensorgrad_b200 import device
+from tensorgrad_b200._lib import MUL, check, lib
+from tensorgrad_b200._random import get_rng, keep_mask
+from tensorgrad_b200.autograd import no_grad
+from tensorgrad_b200.device import DeviceArray, dtype_code
+from tensorgrad_b200.ops import elementwise, reduce
+from tensorgrad_b200.ops._util import Need, as_tensor, make_result
+from tensorgrad_b200.ops.elementwise import binary_array, cast_array
+from tensorgrad_b200.profiler import profiled
+from tensorgrad_b200.tensor import Tensor
+
+__all__ = ["batch_norm", "dropout", "embedding", "layer_norm", "linear"]
+
+
+def _same_dtype(*arrays: DeviceArray | None) -> list[DeviceArray | None]:
+    dt = np.result_type(*[a.dtype for a in arrays if a is not None])
+    if dt.kind != "f":
+        dt = np.dtype(np.float64)
+    return [a if a is None or a.dtype == dt else cast_array(a, dt) for a in arrays]
+
+
+@profiled("linear")
+def linear(x: Any, weight: Any, bias: Any = None) -> Tensor:
+    """``x @ weight.T + bias`` over flattened leading axes, as one GEMM with the bias in its
+    epilogue (ops/layers.py:22-62). The VJP is two GEMMs and a column sum."""
+    tx, tw = as_tensor(x), as_tensor(weight)
+    tb = None if bias is None else as_tensor(bias)
+    if tw.ndim != 2 or tx.ndim == 0 or tx.shape[-1] != tw.shape[1]:
+        raise ValueError(f"linear: input {tx.shape} does not match weight {tw.shape}")
+    xd, wd, bd = _same_dtype(tx.data, tw.data, None if tb is None else tb.data)
+    assert xd is not None and wd is not None
+    out_f, in_f = tw.shape
+    rows = xd.size // in_f if in_f else 0
+    code = dtype_code(xd.dtype)
+    y = device.empty((*tx.shape[:-1], out_f), xd.dtype)
+    check(lib.tg_linear_forward(code, xd.ptr, wd.ptr, bd.ptr if bd is not None else None, y.ptr,
+                                rows, in_f, out_f, device.stream()), "linear")
+    has_bias = tb is not None
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray | None, ...]:
+        if g.dtype != xd.dtype:
+            g = cast_array(g, xd.dtype)
+        gx = device.empty(tx.shape, xd.dtype) if need[0] else None
+        gw = device.empty(tw.shape, xd.dtype) if need[1] else None
+        gb = device.empty((out_f,), xd.dtype) if has_bias and need[2] else None
+        mask = (1 if gx is not None else 0) | (2 if gw is not None else 0) | (4 if gb is not None else 0)
+        scratch = (device.scratch(lib.tg_colsum_scratch_bytes(code, rows, out_f))
+                   if gb is not None else None)
+        check(lib.tg_linear_backward(
+            code, g.ptr, xd.ptr, wd.ptr, gx.ptr if gx is not None else None,
+            gw.ptr if gw is not None else None, gb.ptr if gb is not None else None,
+            rows, in_f, out_f, mask, 0.0, scratch.ptr if scratch is not None else None,
+            device.stream()), "linear backward")
+        if gx is not None and gx.dtype != tx.dtype:
+            gx = cast_array(gx, tx.dtype)
+        return (gx, gw) if not has_bias else (gx, gw, gb)
+
+    parents = (tx, tw) if tb is None else (tx, tw, tb)
+    return make_result(y, parents, backward, "linear")
+
+
+@profiled("layer_norm")
+def layer_norm(x: Any, weight: Any = None, bias: Any = None, eps: float = 1e-5) -> Tensor:
+    """Normalise over the last axis, then scale and shift (ops/layers.py:65-141).
+
+    Forward saves the per-row mean and ``rstd``; the VJP recomputes ``xhat`` from them:
+    ``gx = rstd (gh - mean(gh) - xhat mean(gh xhat))`` with ``gh = g * weight``.
+    """
+    tx = as_tensor(x)
+    tw = None if weight is None else as_tensor(weight)
+    tb = None if bias is None else as_tensor(bias)
+    xd = tx.data if tx.dtype.kind == "f" else cast_array(tx.data, np.dtype(np.float64))
+    wd = None if tw is None else tw.data
+    bd = None if tb is None else tb.data
+    cols = tx.shape[-1]
+    rows = xd.size // cols if cols else 0
+    code = dtype_code(xd.dtype)
+    y = device.empty(tx.shape, xd.dtype)
+    mean = device.empty((rows,), xd.dtype)
+    rstd = device.empty((rows,), xd.dtype)
+    check(lib.tg_layer_norm_forward(code, xd.ptr, wd.ptr if wd is not None else None,
+                                    bd.ptr if bd is not None else None, y.ptr, mean.ptr,
+                                    rstd.ptr, rows, cols, eps, device.stream()), "layer_norm")
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray | None, ...]:
+        k = 1
+        need_w = need_b = False
+        if tw is not None:
+            need_w = need[k]
+            k += 1
+        if tb is not None:
+            need_b = need[k]
+        gx = device.empty(tx.shape, xd.dtype) if need[0] else None
+        gw = device.empty((cols,), xd.dtype) if need_w else None
+        gb = device.empty((cols,), xd.dtype) if need_b else None
+        mask = (1 if gx is not None else 0) | (2 if gw is not None else 0) | (4 if gb is not None else 0)
+        scratch = (device.scratch(lib.tg_layer_norm_scratch_bytes(code, rows, cols))
+                   if (gw is not None or gb is not None) else None)
+        check(lib.tg_layer_norm_backward(
+            code, g.ptr, xd.ptr, wd.ptr if wd is not None else None, mean.ptr, rstd.ptr,
+            gx.ptr if gx is not None else None, gw.ptr if gw is not None else None,
+            gb.ptr if gb is not None else None, rows, cols, mask,
+            scratch.ptr if scratch is not None else None, device.stream()), "layer_norm backward")
+        grads: list[DeviceArray | None] = [gx]
+        if tw is not None:
+            grads.append(gw)
+        if tb is not None:
+            grads.append(gb)
+        return tuple(grads)
+
+    parents = tuple(t for t in (tx, tw, tb) if t is not None)
+    return make_result(y, parents, backward, "layer_norm")
+
+
+@profiled("batch_norm")
+def batch_norm(
+    x: Tensor,
+    running_mean: DeviceArray | None,
+    running_var: DeviceArray | None,
+    weight: Tensor | None = None,
+    bias: Tensor | None = None,
+    *,
+    training: bool = True,
+    momentum: float = 0.1,
+    eps: float = 1e-5,
+) -> Tensor:
+    """Batch normalisation over ``(N, C, *spatial)`` with per-channel statistics, composed of
+    differentiable ops exactly as the reference composes it (ops/layers.py:144-189)."""
+    if x.ndim < 2:
+        raise ValueError(f"batch_norm expects (N, C, ...) input, got {x.shape}")
+    axes = (0, *range(2, x.ndim))
+    view = (1, -1, *([1] * (x.ndim - 2)))
+    if training:
+        mean = reduce.mean(x, axes, keepdims=True)
+        var = reduce.var(x, axes, keepdims=True, correction=0)
+        if running_mean is not None and running_var is not None:
+            n = x.size // x.shape[1]
+            with no_grad():
+                unbiased = var.data.reshape(-1) * (n / max(n - 1, 1))
+                running_mean *= 1 - momentum
+                running_mean += mean.data.reshape(-1) * momentum
+                running_var *= 1 - momentum
+                running_var += unbiased * momentum
+    else:
+        if running_mean is None or running_var is None:
+            raise ValueError("evaluation-mode batch_norm needs running statistics")
+        mean = Tensor._wrap(running_mean.astype(x.dtype, copy=False).reshape(view))
+        var = Tensor._wrap(running_var.astype(x.dtype, copy=False).reshape(view))
+    out = (x - mean) / elementwise.sqrt(var + eps)
+    if weight is not None:
+        out = out * weight.reshape(view)
+    if bias is not None:
+        out = out + bias.reshape(view)
+    return out
+
+
+def _segments(ids: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """Stable argsort of the ids and the runs of equal ids in it (ops/layers.py:192-206)."""
+    order = np.argsort(ids, kind="stable")
+    sorted_ids = ids[order]
+    starts = np.flatnonzero(np.concatenate(([True], sorted_ids[1:] != sorted_ids[:-1])))
+    seg_start = np.append(starts, ids.size).astype(np.int64)
+    return order.astype(np.int64), seg_start, sorted_ids[starts].astype(np.int64)
+
+
+@profiled("embedding")
+def embedding(indices: Any, weight: Any) -> Tensor:
+    """Row lookup; the VJP is a scatter-add in the reference's sorted order
+    (ops/layers.py:209-232). Ids are checked on the host before any device work."""
+    tw = as_tensor(weight)
+    if isinstance(indices, Tensor):
+        idx = indices.numpy()
+    elif isinstance(indices, DeviceArray):
+        idx = indices.numpy()
+    else:
+        idx = np.asarray(indices)
+    if not np.issubdtype(idx.dtype, np.integer):
+        raise TypeError(f"embedding indices must be integers, got {idx.dtype}")
+    num, dim = tw.shape
+    if idx.size and (idx.min() < 0 or idx.max() >= num):
+        raise IndexError(f"embedding ids must be in [0, {num}), got {idx.min()}..{idx.max()}")
+    flat = np.ascontiguousarray(idx.reshape(-1), dtype=np.int64)
+    ids_dev = device.from_numpy(flat)
+    wd = tw.data
+    code = dtype_code(wd.dtype)
+    out = device.empty((*idx.shape, dim), wd.dtype)
+    check(lib.tg_embedding_forward(code, ids_dev.ptr, wd.ptr, out.ptr, flat.size, num, dim,
+                                   device.stream()), "embedding")
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+        order, seg_start, seg_id = _segments(flat)
+        packed = device.from_numpy(np.concatenate([order, seg_start, seg_id]))
+        n, ns = order.size, seg_id.size
+        base = packed.ptr
+        gw = device.empty((num, dim), g.dtype)
+        check(lib.tg_embedding_backward(dtype_code(g.dtype), g.ptr, base, base + 8 * n,
+                                        base + 8 * (n + ns + 1), ns, gw.ptr, num, dim, 0,
+                                        device.stream()), "embedding backward")
+        return (gw,)
+
+    return make_result(out, (tw,), backward, "embedding")
+
+
+@profiled("dropout")
+def dropout(x: Any, p: float = 0.5, training: bool = True,
+            rng: np.random.Generator | None = None) -> Tensor:
+    """Inverted dropout with the reference's quantised keep-mask, drawn on the host from the
+    global generator and uploaded (ops/layers.py:235-259); the identity when ``p == 0`` or not
+    training."""
+    tx = as_tensor(x)
+    if not 0.0 <= p <= 1.0:
+        raise ValueError(f"dropout probability must be in [0, 1], got {p}")
+    if not training or p == 0.0:
+        return tx
+    keep, scale = keep_mask(tx.shape, p, rng or get_rng())
+    mask = device.from_numpy((keep * np.asarray(scale, dtype=tx.dtype)).astype(tx.dtype))
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+        return (binary_array(g, mask, MUL),)
+
+    return make_result(binary_array(tx.data, mask, MUL), (tx,), backward, "dropout")

@@ -1,0 +1,61 @@
+"""Matrix product (the reference's ops/linalg.py:16-63) on the GEMM kernels."""
+
+from __future__ import annotations
+
+import math
+from typing import Any
+
+import numpy as np
+
+from tensorgrad_b200 import device
+from tensorgrad_b200._lib import check, lib
+from tensorgrad_b200.device import DeviceArray, dtype_code
+from tensorgrad_b200.ops._util import Need, coerce_pair, make_result, unbroadcast
+from tensorgrad_b200.ops.elementwise import cast_array
+from tensorgrad_b200.ops.shape import broadcast_array
+from tensorgrad_b200.profiler import profiled
+from tensorgrad_b200.tensor import Tensor
+
+__all__ = ["matmul"]
+
+
+def _bmm(a: DeviceArray, b: DeviceArray, ta: int, tb: int, m: int, n: int, k: int,
+         batch: int) -> DeviceArray:
+    """``batch`` products op(a_i) @ op(b_i) of contiguous stacks."""
+    out = device.empty((batch, m, n), a.dtype)
+    lda = m if ta else k
+    ldb = k if tb else n
+    check(lib.tg_gemm_batched(dtype_code(a.dtype), ta, tb, m, n, k, 1.0, a.ptr, lda, m * k,
+                              b.ptr, ldb, k * n, 0.0, out.ptr, n, m * n, batch,
+                              device.stream()), "matmul")
+    return out
+
+
+@profiled("matmul")
+def matmul(a: Any, b: Any) -> Tensor:
+    """``a @ b`` for operands with at least two axes; leading axes broadcast."""
+    ta, tb = coerce_pair(a, b)
+    if ta.ndim < 2 or tb.ndim < 2:
+        raise NotImplementedError("matmul on device tensors needs operands with >= 2 axes")
+    dt = np.result_type(ta.dtype, tb.dtype)
+    ad = ta.data if ta.dtype == dt else cast_array(ta.data, dt)
+    bd = tb.data if tb.dtype == dt else cast_array(tb.data, dt)
+    m, k = ta.shape[-2:]
+    k2, n = tb.shape[-2:]
+    if k != k2:
+        raise ValueError(f"matmul: shapes {ta.shape} and {tb.shape} are not aligned")
+    batch = tuple(np.broadcast_shapes(ta.shape[:-2], tb.shape[:-2]))
+    nb = math.prod(batch)
+    af = broadcast_array(ad, (*batch, m, k))
+    bf = broadcast_array(bd, (*batch, k, n))
+    out = _bmm(af, bf, 0, 0, m, n, k, nb).reshape((*batch, m, n))
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray | None, DeviceArray | None]:
+        ga = gb = None
+        if need[0]:  # g @ b^T
+            ga = unbroadcast(_bmm(g, bf, 0, 1, m, k, n, nb).reshape((*batch, m, k)), ta.shape)
+        if need[1]:  # a^T @ g
+            gb = unbroadcast(_bmm(af, g, 1, 0, k, n, m, nb).reshape((*batch, k, n)), tb.shape)
+        return ga, gb
+
+    return make_result(out, (ta, tb), backward, "matmul")

@@ -1,0 +1,88 @@
+"""Loss functions (the reference's ops/loss.py)."""
+
+from __future__ import annotations
+
+from typing import Any, Literal
+
+import numpy as np
+
+from tensorgrad_b200 import device
+from tensorgrad_b200._lib import check, lib
+from tensorgrad_b200.device import DeviceArray, dtype_code
+from tensorgrad_b200.ops import reduce
+from tensorgrad_b200.ops._util import Need, as_tensor, coerce_pair, make_result
+from tensorgrad_b200.ops.elementwise import cast_array
+from tensorgrad_b200.profiler import profiled
+from tensorgrad_b200.tensor import Tensor
+
+__all__ = ["Reduction", "cross_entropy", "mse_loss"]
+
+Reduction = Literal["mean", "sum", "none"]
+_RED = {"mean": 0, "sum": 1, "none": 2}
+
+
+@profiled("cross_entropy")
+def cross_entropy(logits: Any, target: Any, *, ignore_index: int = -100,
+                  reduction: Reduction = "mean") -> Tensor:
+    """Softmax cross-entropy from unnormalised logits, class axis last (ops/loss.py:23-97).
+
+    One kernel pass per row computes the log-sum-exp (online max and sum) and the row loss;
+    the mean over non-ignored rows is a fixed-order float64 sum. The VJP is one pass writing
+    ``(softmax - onehot) * g / n_valid``. Targets are validated on the host, as the reference
+    does, before any device work.
+    """
+    tl = as_tensor(logits)
+    if isinstance(target, Tensor | DeviceArray):
+        t = target.numpy()
+    else:
+        t = np.asarray(target)
+    if not np.issubdtype(t.dtype, np.integer):
+        raise TypeError(f"cross_entropy targets must be integers, got {t.dtype}")
+    if tl.shape[:-1] != t.shape:
+        raise ValueError(f"logits {tl.shape} and targets {t.shape} are incompatible")
+    if reduction not in _RED:
+        raise ValueError(f"unknown reduction {reduction!r}")
+    classes = tl.shape[-1]
+    flat_t = np.ascontiguousarray(t.reshape(-1), dtype=np.int64)
+    valid = flat_t != ignore_index
+    safe = np.where(valid, flat_t, 0)
+    if np.any((safe < 0) | (safe >= classes)):
+        raise IndexError(f"target out of range for {classes} classes")
+    x = tl.data if tl.dtype.kind == "f" else cast_array(tl.data, np.dtype(np.float64))
+    rows = flat_t.size
+    code = dtype_code(x.dtype)
+    red = _RED[reduction]
+    tgt = device.from_numpy(flat_t)
+    lse = device.empty((rows,), x.dtype)
+    row_loss = device.empty((rows,), x.dtype)
+    n_valid = device.empty((1,), np.int64)
+    out = row_loss.reshape(t.shape) if red == 2 else device.empty((), x.dtype)
+    check(lib.tg_cross_entropy_forward(code, x.ptr, tgt.ptr, lse.ptr, row_loss.ptr, out.ptr,
+                                       rows, classes, ignore_index, red, n_valid.ptr, None,
+                                       device.stream()), "cross_entropy")
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+        if g.dtype != x.dtype:
+            g = cast_array(g, x.dtype)
+        grad = device.empty(tl.shape, x.dtype)
+        check(lib.tg_cross_entropy_backward(code, x.ptr, tgt.ptr, lse.ptr, g.ptr, n_valid.ptr,
+                                            grad.ptr, rows, classes, ignore_index, red,
+                                            device.stream()), "cross_entropy backward")
+        return (grad if grad.dtype == tl.dtype else cast_array(grad, tl.dtype),)
+
+    return make_result(out, (tl,), backward, "cross_entropy")
+
+
+@profiled("mse_loss")
+def mse_loss(prediction: Any, target: Any, *, reduction: Reduction = "mean") -> Tensor:
+    """``(prediction - target) ** 2`` reduced, composed as the reference composes it
+    (ops/loss.py:148-161)."""
+    tp, tt = coerce_pair(prediction, target)
+    sq = (tp - tt) ** 2
+    if reduction == "mean":
+        return reduce.mean(sq)
+    if reduction == "sum":
+        return reduce.sum(sq)
+    if reduction == "none":
+        return sq
+    raise ValueError(f"unknown reduction {reduction!r}")

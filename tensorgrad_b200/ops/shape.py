@@ -1,0 +1,171 @@
+"""Shape manipulation (the reference's ops/shape.py): views, permutes, broadcasts and basic
+indexing. Reshapes share storage; everything that moves elements is one strided-copy kernel."""
+
+from __future__ import annotations
+
+import math
+from typing import Any
+
+import numpy as np
+
+from tensorgrad_b200 import device
+from tensorgrad_b200._lib import check, int64_array, lib
+from tensorgrad_b200.device import DeviceArray
+from tensorgrad_b200.ops._util import Need, as_tensor, make_result, normalize_axis, unbroadcast
+from tensorgrad_b200.profiler import profiled
+from tensorgrad_b200.tensor import Tensor
+
+__all__ = ["broadcast_to", "flatten", "getitem", "permute", "reshape", "squeeze", "sum_to",
+           "transpose", "unsqueeze"]
+
+
+def strided_copy(src_ptr: int, src_strides: list[int], dst_ptr: int, dst_strides: list[int],
+                 shape: tuple[int, ...], itemsize: int) -> None:
+    check(lib.tg_strided_copy(itemsize, len(shape), int64_array(shape), src_ptr,
+                              int64_array(src_strides), dst_ptr, int64_array(dst_strides),
+                              device.stream()), "strided copy")
+
+
+def broadcast_array(a: DeviceArray, shape: tuple[int, ...]) -> DeviceArray:
+    """Materialise ``a`` broadcast to ``shape``."""
+    if a.shape == shape:
+        return a
+    out = device.empty(shape, a.dtype)
+    strides = device.contiguous_strides(a.shape)
+    pad = len(shape) - a.ndim
+    src = [0] * pad + [0 if (n == 1 and shape[pad + i] != 1) else strides[i]
+                       for i, n in enumerate(a.shape)]
+    strided_copy(a.ptr, src, out.ptr, device.contiguous_strides(shape), shape, a.itemsize)
+    return out
+
+
+def permute_array(a: DeviceArray, perm: tuple[int, ...]) -> DeviceArray:
+    shape = tuple(a.shape[p] for p in perm)
+    out = device.empty(shape, a.dtype)
+    strides = device.contiguous_strides(a.shape)
+    strided_copy(a.ptr, [strides[p] for p in perm], out.ptr, device.contiguous_strides(shape),
+                 shape, a.itemsize)
+    return out
+
+
+@profiled("reshape")
+def reshape(a: Any, shape: tuple[int, ...]) -> Tensor:
+    """A view with a new shape (one entry may be -1) (ops/shape.py:45)."""
+    ta = as_tensor(a)
+    out = ta.data.reshape(shape)
+    src_shape = ta.shape
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+        return (g.reshape(src_shape),)
+
+    return make_result(out, (ta,), backward, "reshape")
+
+
+def flatten(a: Any, start_axis: int = 0, end_axis: int = -1) -> Tensor:
+    ta = as_tensor(a)
+    if ta.ndim == 0:
+        return reshape(ta, (1,))
+    s = normalize_axis(start_axis, ta.ndim)
+    e = normalize_axis(end_axis, ta.ndim)
+    shape = ta.shape[:s] + (math.prod(ta.shape[s:e + 1]),) + ta.shape[e + 1:]
+    return reshape(ta, shape)
+
+
+@profiled("permute")
+def permute(a: Any, dims: tuple[int, ...]) -> Tensor:
+    ta = as_tensor(a)
+    perm = tuple(normalize_axis(d, ta.ndim) for d in dims)
+    if sorted(perm) != list(range(ta.ndim)):
+        raise ValueError(f"permute: {dims} is not a permutation of {ta.ndim} axes")
+    inv = tuple(np.argsort(perm))
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+        return (permute_array(g, inv),)
+
+    return make_result(permute_array(ta.data, perm), (ta,), backward, "permute")
+
+
+def transpose(a: Any, axis0: int, axis1: int) -> Tensor:
+    ta = as_tensor(a)
+    perm = list(range(ta.ndim))
+    i, j = normalize_axis(axis0, ta.ndim), normalize_axis(axis1, ta.ndim)
+    perm[i], perm[j] = perm[j], perm[i]
+    return permute(ta, tuple(perm))
+
+
+def unsqueeze(a: Any, axis: int) -> Tensor:
+    ta = as_tensor(a)
+    ax = normalize_axis(axis, ta.ndim + 1)
+    return reshape(ta, ta.shape[:ax] + (1,) + ta.shape[ax:])
+
+
+def squeeze(a: Any, axis: int | None = None) -> Tensor:
+    ta = as_tensor(a)
+    if axis is None:
+        return reshape(ta, tuple(n for n in ta.shape if n != 1))
+    ax = normalize_axis(axis, ta.ndim)
+    if ta.shape[ax] != 1:
+        return ta
+    return reshape(ta, ta.shape[:ax] + ta.shape[ax + 1:])
+
+
+@profiled("broadcast_to")
+def broadcast_to(a: Any, shape: tuple[int, ...]) -> Tensor:
+    ta = as_tensor(a)
+    shape = tuple(shape)
+    np.broadcast_shapes(ta.shape, shape)
+    src = ta.shape
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+        return (unbroadcast(g, src),)
+
+    return make_result(broadcast_array(ta.data, shape), (ta,), backward, "broadcast_to")
+
+
+def sum_to(a: Any, shape: tuple[int, ...]) -> Tensor:
+    ta = as_tensor(a)
+    shape = tuple(shape)
+    if ta.shape == shape:
+        return ta
+    target = ta.shape
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+        return (broadcast_array(g, target),)
+
+    return make_result(unbroadcast(ta.data, shape), (ta,), backward, "sum_to")
+
+
+def _basic_view(shape: tuple[int, ...], itemsize: int, index: Any) -> tuple[int, tuple[int, ...], list[int]]:
+    """Element offset, shape and element strides of ``x[index]`` for basic indexing."""
+    items = index if isinstance(index, tuple) else (index,)
+    for it in items:
+        if not (it is None or it is Ellipsis or isinstance(it, int | np.integer | slice)):
+            raise NotImplementedError("getitem on device tensors supports basic indexing only")
+    base = np.empty(0, dtype=np.dtype(f"V{itemsize}"))
+    strides = tuple(s * itemsize for s in device.contiguous_strides(shape))
+    fake = np.lib.stride_tricks.as_strided(base, shape=shape, strides=strides)
+    view = fake[index]
+    offset = view.__array_interface__["data"][0] - base.__array_interface__["data"][0]
+    return offset // itemsize, view.shape, [s // itemsize for s in view.strides]
+
+
+@profiled("getitem")
+def getitem(a: Any, index: Any) -> Tensor:
+    """``a[index]`` for ints, slices, ``...`` and ``None``; the VJP scatters the gradient into
+    zeros at the selected positions (ops/shape.py:182-235)."""
+    ta = as_tensor(a)
+    if isinstance(index, Tensor):
+        raise NotImplementedError("getitem on device tensors supports basic indexing only")
+    x = ta.data
+    offset, shape, strides = _basic_view(ta.shape, x.itemsize, index)
+    out = device.empty(shape, x.dtype)
+    strided_copy(x.ptr + offset * x.itemsize, strides, out.ptr, device.contiguous_strides(shape),
+                 shape, x.itemsize)
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+        gx = device.zeros(ta.shape, g.dtype)
+        strided_copy(g.ptr, device.contiguous_strides(shape), gx.ptr + offset * g.itemsize,
+                     strides, shape, g.itemsize)
+        return (gx,)
+
+    return make_result(out, (ta,), backward, "getitem")

@@ -1,0 +1,131 @@
+"""Adam and AdamW (the reference's optim/adam.py:38-94) as device kernels.
+
+At construction each parameter group is re-homed into a flat arena (parameters and gradient
+slots contiguous, 16-byte aligned), and the moments get buffers of the same layout. When
+every parameter of a group has its gradient in its slot and all share one step count, the
+whole group is ONE ``tg_adam_update`` launch over the flat buffers; otherwise the update is
+a multi-tensor launch over the parameters that have gradients, each with its own step count,
+exactly the reference's per-parameter semantics.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Iterable
+from dataclasses import dataclass
+from typing import Any
+
+from tensorgrad_b200 import device
+from tensorgrad_b200._lib import check, int64_array, lib, ptr_array
+from tensorgrad_b200.device import DeviceArray, dtype_code
+from tensorgrad_b200.optim.arena import Arena, arena_of, flatten_parameters
+from tensorgrad_b200.optim.optimizer import Optimizer, ParamGroup
+from tensorgrad_b200.tensor import Tensor
+
+__all__ = ["Adam", "AdamW"]
+
+
+@dataclass
+class _AdamState:
+    exp_avg: DeviceArray
+    exp_avg_sq: DeviceArray
+    step: int = 0
+
+
+class Adam(Optimizer[_AdamState]):
+    """Adam with bias correction; ``weight_decay`` is L2 added to the gradient."""
+
+    decoupled_weight_decay = False
+
+    def __init__(self, params: Iterable[Any], lr: float = 1e-3,
+                 betas: tuple[float, float] = (0.9, 0.999), eps: float = 1e-8,
+                 weight_decay: float = 0.0) -> None:
+        if not (0.0 <= betas[0] < 1.0 and 0.0 <= betas[1] < 1.0):
+            raise ValueError(f"invalid betas {betas}")
+        if eps < 0:
+            raise ValueError(f"invalid eps {eps}")
+        super().__init__(params, lr, weight_decay)
+        self.betas = betas
+        self.eps = eps
+        self._moments: dict[int, tuple[DeviceArray, DeviceArray]] = {}
+        for group in self.param_groups:
+            for arena in flatten_parameters(group.params):
+                if id(arena) not in self._moments:
+                    self._moments[id(arena)] = (device.zeros((arena.numel,), arena.dtype),
+                                                device.zeros((arena.numel,), arena.dtype))
+
+    def _state_for(self, p: Tensor) -> _AdamState:
+        st = self.state.get(id(p))
+        if st is None:
+            arena: Arena | None = getattr(p, "_arena", None)
+            if arena is not None and id(arena) in self._moments and arena.intact():
+                m_buf, v_buf = self._moments[id(arena)]
+                off = arena.offsets[arena.params.index(p)]
+                st = _AdamState(m_buf.flat_view(off, p.size, p.shape),
+                                v_buf.flat_view(off, p.size, p.shape))
+            else:
+                st = _AdamState(device.zeros(p.shape, p.dtype), device.zeros(p.shape, p.dtype))
+            self.state[id(p)] = st
+        return st
+
+    def _flat_ok(self, group: ParamGroup) -> Arena | None:
+        arena = arena_of(group.params)
+        if arena is None or id(arena) not in self._moments:
+            return None
+        if not (arena.intact() and arena.grads_in_slots()):
+            return None
+        steps = {self.state[id(p)].step if id(p) in self.state else 0 for p in group.params}
+        if len(steps) != 1:
+            return None
+        m_buf, _ = self._moments[id(arena)]
+        for p, off in zip(arena.params, arena.offsets, strict=True):
+            st = self.state.get(id(p))
+            if st is not None and st.exp_avg.ptr != m_buf.ptr + off * arena.dtype.itemsize:
+                return None
+        return arena
+
+    def step(self) -> None:
+        b1, b2 = self.betas
+        for group in self.param_groups:
+            wd = group.weight_decay
+            arena = self._flat_ok(group)
+            if arena is not None:
+                states = [self._state_for(p) for p in group.params]
+                for st in states:
+                    st.step += 1
+                m_buf, v_buf = self._moments[id(arena)]
+                check(lib.tg_adam_update(dtype_code(arena.dtype), arena.numel,
+                                         arena.param_buf.ptr, arena.grad_buf.ptr, m_buf.ptr,
+                                         v_buf.ptr, group.lr, b1, b2, self.eps, wd,
+                                         states[0].step, int(self.decoupled_weight_decay),
+                                         device.stream()), "adam step")
+                continue
+            by_dtype: dict[str, list[tuple[Tensor, DeviceArray, _AdamState]]] = {}
+            for p in group.params:
+                if p.grad is None:
+                    continue
+                st = self._state_for(p)
+                st.step += 1
+                g = p.grad.data if p.grad.dtype == p.dtype else p.grad.data.astype(p.dtype)
+                by_dtype.setdefault(str(p.dtype), []).append((p, g, st))
+            for items in by_dtype.values():
+                code = dtype_code(items[0][0].dtype)
+                n = len(items)
+                check(lib.tg_adam_update_multi(
+                    code, n, ptr_array(p.data.ptr for p, _, _ in items),
+                    ptr_array(g.ptr for _, g, _ in items),
+                    ptr_array(s.exp_avg.ptr for _, _, s in items),
+                    ptr_array(s.exp_avg_sq.ptr for _, _, s in items),
+                    int64_array(p.size for p, _, _ in items),
+                    int64_array(s.step for _, _, s in items), group.lr, b1, b2, self.eps, wd,
+                    int(self.decoupled_weight_decay), None, device.stream()), "adam step")
+
+
+class AdamW(Adam):
+    """Adam with decoupled weight decay: ``p *= 1 - lr * wd`` before the moment update."""
+
+    decoupled_weight_decay = True
+
+    def __init__(self, params: Iterable[Any], lr: float = 1e-3,
+                 betas: tuple[float, float] = (0.9, 0.999), eps: float = 1e-8,
+                 weight_decay: float = 1e-2) -> None:
+        super().__init__(params, lr, betas, eps, weight_decay)

@@ -1,0 +1,77 @@
+"""Gradient-norm clipping (the reference's optim/clip.py:15-31) on the device.
+
+The global L2 norm is accumulated in float64 over all gradients (one launch for a flat
+arena, or a multi-tensor launch), and the rescale ``g *= max_norm / (total + eps)`` (the
+factor rounded to the gradient dtype, as the reference casts it) runs only when that
+factor is below 1, decided on the device. Returning the norm as a Python float reads 8 bytes
+back, which synchronises the stream once per call.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Iterable
+
+import numpy as np
+
+from tensorgrad_b200 import device
+from tensorgrad_b200._lib import check, int64_array, lib, ptr_array
+from tensorgrad_b200.device import DeviceArray, dtype_code
+from tensorgrad_b200.optim.arena import arena_of
+from tensorgrad_b200.tensor import Tensor
+
+__all__ = ["clip_grad_norm_", "grad_norm_device"]
+
+
+def _segments(params: list[Tensor]) -> dict[str, list[DeviceArray]]:
+    """Gradient buffers to reduce, per dtype: the whole flat arena when it is exact."""
+    arena = arena_of(params)
+    if arena is not None and arena.grads_in_slots():
+        return {str(arena.dtype): [arena.grad_buf]}
+    out: dict[str, list[DeviceArray]] = {}
+    for p in params:
+        if p.grad is not None:
+            out.setdefault(str(p.grad.dtype), []).append(p.grad.data)
+    return out
+
+
+def grad_norm_device(params: Iterable[Tensor]) -> tuple[DeviceArray, dict[str, list[DeviceArray]]]:
+    """Total gradient norm as a float64 device scalar, and the buffers it covered."""
+    segs = _segments(list(params))
+    total = device.zeros((1,), np.float64)
+    parts: list[DeviceArray] = []
+    for bufs in segs.values():
+        code = dtype_code(bufs[0].dtype)
+        part = device.empty((1,), np.float64)
+        scratch = device.scratch(lib.tg_sumsq_scratch_bytes(len(bufs)))
+        check(lib.tg_sumsq_multi(code, len(bufs), ptr_array(b.ptr for b in bufs),
+                                 int64_array(b.size for b in bufs), part.ptr, scratch.ptr,
+                                 device.stream()), "grad norm")
+        parts.append(part)
+    if len(parts) == 1:
+        total = parts[0]
+    elif parts:
+        # sqrt(a^2 + b^2) across dtypes, on the device.
+        from tensorgrad_b200._lib import ADD, MUL, SQRT
+        from tensorgrad_b200.ops.elementwise import binary_array
+
+        acc = binary_array(parts[0], parts[0], MUL)
+        for p in parts[1:]:
+            acc = binary_array(acc, binary_array(p, p, MUL), ADD)
+        total = device.empty((1,), np.float64)
+        check(lib.tg_unary(1, SQRT, 1, acc.ptr, 0.0, total.ptr, device.stream()), "grad norm")
+    return total, segs
+
+
+def clip_grad_norm_(params: Iterable[Tensor], max_norm: float, eps: float = 1e-6) -> float:
+    """Rescale gradients in place so their global L2 norm is at most ``max_norm``.
+
+    Returns:
+        The total norm before clipping.
+    """
+    total, segs = grad_norm_device(params)
+    for bufs in segs.values():
+        code = dtype_code(bufs[0].dtype)
+        check(lib.tg_clip_scale_multi(code, len(bufs), ptr_array(b.ptr for b in bufs),
+                                      int64_array(b.size for b in bufs), total.ptr, max_norm,
+                                      eps, None, device.stream()), "clip")
+    return float(total.item())

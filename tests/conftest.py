@@ -1,0 +1,51 @@
+"""Shared pytest configuration: the ``gpu`` marker and common fixtures."""
+
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+
+
+def pytest_configure(config: pytest.Config) -> None:
+    config.addinivalue_line("markers", "gpu: needs a B200 (runs the CUDA kernels)")
+
+
+@pytest.fixture
+def rng() -> np.random.Generator:
+    """A seeded generator (seed 1234, as the reference's own test suite uses)."""
+    return np.random.default_rng(1234)
+
+
+def load_golden(name: str) -> dict[str, np.ndarray]:
+    with np.load(os.path.join(GOLDEN, name)) as f:
+        return {k: f[k] for k in f.files}
+
+
+def assert_parity(ours: np.ndarray, ref: np.ndarray, rel: float, what: str = "") -> None:
+    """The parity metric: ``max|d| <= rel * max|ref|`` and ``||d||_2 <= rel * ||ref||_2``.
+
+    Elementwise ``rtol`` is not used: any reordering of fp32 sums moves near-zero entries by
+    more than a relative 1e-4 of themselves, while the tensor as a whole agrees.
+    """
+    ours = np.asarray(ours, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    assert ours.shape == ref.shape, f"{what}: shape {ours.shape} != {ref.shape}"
+    assert np.all(np.isfinite(ours)), f"{what}: non-finite values"
+    d = ours - ref
+    max_ref = float(np.max(np.abs(ref))) if ref.size else 0.0
+    norm_ref = float(np.linalg.norm(ref))
+    max_err = float(np.max(np.abs(d))) if d.size else 0.0
+    norm_err = float(np.linalg.norm(d))
+    assert max_err <= rel * max_ref + 1e-30, f"{what}: max err {max_err:.3e} > {rel} * {max_ref:.3e}"
+    assert norm_err <= rel * norm_ref + 1e-30, (
+        f"{what}: norm err {norm_err:.3e} > {rel} * {norm_ref:.3e}"
+    )

@@ -1,0 +1,272 @@
+"""Per-op parity of the CUDA path (through the C ABI) against the float64 oracle."""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from oracle import ops as O
+from tests.conftest import assert_parity, load_golden
+from tests.golden.specs import ATTN_CASES, attention_inputs
+
+pytestmark = pytest.mark.gpu
+
+REL32 = 1e-4   # fp32 kernels vs the float64 reference
+REL64 = 1e-10  # float64 build mode
+
+
+@pytest.fixture(params=[np.float32, np.float64], ids=["fp32", "fp64"])
+def dtype(request):
+    import tensorgrad_b200 as tg
+
+    tg.set_default_dtype(request.param)
+    yield request.param
+    tg.set_default_dtype(np.float32)
+
+
+def rel(dtype) -> float:
+    return REL32 if dtype == np.float32 else REL64
+
+
+def tensor(a, dtype, requires_grad=True):
+    import tensorgrad_b200 as tg
+
+    return tg.Tensor(np.asarray(a, dtype=dtype), requires_grad=requires_grad)
+
+
+# ------------------------------------------------------------------------------- GEMM
+GEMM_SHAPES = [(1, 1, 1), (7, 5, 3), (128, 128, 32), (130, 257, 100), (300, 64, 768),
+               (64, 300, 36), (1000, 333, 68), (8192 // 16, 3072 // 4, 768)]
+
+
+@pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+def test_gemm_tensor_core_matches_float64(m, n, k, ta, tb):
+    from tensorgrad_b200 import device
+    from tensorgrad_b200._lib import F32, check, lib
+
+    rng = np.random.default_rng(m * 7 + n * 3 + k + 10 * ta + tb)
+    a = rng.standard_normal((k, m) if ta else (m, k))
+    b = rng.standard_normal((n, k) if tb else (k, n))
+    c0 = rng.standard_normal((m, n))
+    bias = rng.standard_normal(n)
+    ref = 0.5 * ((a.T if ta else a) @ (b.T if tb else b)) + 0.25 * c0 + bias
+    da = device.from_numpy(a.astype(np.float32))
+    db = device.from_numpy(b.astype(np.float32))
+    dc = device.from_numpy(c0.astype(np.float32))
+    dbias = device.from_numpy(bias.astype(np.float32))
+    lda, ldb = a.shape[1], b.shape[1]
+    check(lib.tg_gemm(F32, ta, tb, m, n, k, 0.5, da.ptr, lda, db.ptr, ldb, 0.25, dc.ptr, n,
+                      dbias.ptr, device.stream()))
+    out = dc.numpy()
+    assert lib.tg_gemm_tc_status(1) == 0
+    # 3xTF32 reaches fp32-level accuracy: far inside the parity tolerance.
+    assert_parity(out, ref, 2e-6, f"gemm {m}x{n}x{k} ta={ta} tb={tb}")
+
+
+def test_gemm_simt_fp64():
+    from tensorgrad_b200 import device
+    from tensorgrad_b200._lib import F64, check, lib
+
+    rng = np.random.default_rng(0)
+    a, b = rng.standard_normal((77, 45)), rng.standard_normal((45, 93))
+    da, db = device.from_numpy(a), device.from_numpy(b)
+    dc = device.empty((77, 93), np.float64)
+    check(lib.tg_gemm(F64, 0, 0, 77, 93, 45, 1.0, da.ptr, 45, db.ptr, 93, 0.0, dc.ptr, 93, None,
+                      device.stream()))
+    assert_parity(dc.numpy(), a @ b, 1e-13, "gemm fp64")
+
+
+# ------------------------------------------------------------------------------- layers
+def test_linear(dtype):
+    import tensorgrad_b200 as tg
+
+    rng = np.random.default_rng(1)
+    x, w, b, g = (rng.standard_normal(s) for s in ((4, 9, 24), (40, 24), (40,), (4, 9, 40)))
+    tx, tw, tb = tensor(x, dtype), tensor(w, dtype), tensor(b, dtype)
+    y = tg.linear(tx, tw, tb)
+    y.backward(g.astype(dtype))
+    assert_parity(y.numpy(), O.linear_forward(x, w, b), rel(dtype), "y")
+    gx, gw, gb = O.linear_backward(g, x, w, True)
+    assert_parity(tx.grad.numpy(), gx, rel(dtype), "gx")
+    assert_parity(tw.grad.numpy(), gw, rel(dtype), "gw")
+    assert_parity(tb.grad.numpy(), gb, rel(dtype), "gb")
+
+
+@pytest.mark.parametrize("cols", [16, 128, 768, 1000])
+def test_layer_norm(dtype, cols):
+    import tensorgrad_b200 as tg
+
+    rng = np.random.default_rng(cols)
+    x = rng.standard_normal((3, 37, cols)) * 3 + 1
+    w, b = 1 + 0.1 * rng.standard_normal(cols), 0.1 * rng.standard_normal(cols)
+    g = rng.standard_normal(x.shape)
+    tx, tw, tb = tensor(x, dtype), tensor(w, dtype), tensor(b, dtype)
+    y = tg.layer_norm(tx, tw, tb)
+    y.backward(g.astype(dtype))
+    ref, xhat, rstd = O.layer_norm_forward(x, w, b)
+    gx, gw, gb = O.layer_norm_backward(g, xhat, rstd, w)
+    assert_parity(y.numpy(), ref, rel(dtype), "y")
+    assert_parity(tx.grad.numpy(), gx, rel(dtype), "gx")
+    assert_parity(tw.grad.numpy(), gw, rel(dtype), "gw")
+    assert_parity(tb.grad.numpy(), gb, rel(dtype), "gb")
+
+
+def test_gelu_and_relu(dtype):
+    import tensorgrad_b200 as tg
+
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((5, 203)) * 3
+    g = rng.standard_normal(x.shape)
+    tx = tensor(x, dtype)
+    y = tg.gelu(tx)
+    y.backward(g.astype(dtype))
+    ref, t = O.gelu_forward(x)
+    assert_parity(y.numpy(), ref, rel(dtype), "gelu")
+    assert_parity(tx.grad.numpy(), O.gelu_backward(g, x, t), rel(dtype), "gelu grad")
+    assert float(tg.gelu(tg.Tensor(np.array(1.0))).item()) == pytest.approx(0.841192, abs=1e-6)
+    tr = tensor(x, dtype)
+    yr = tg.relu(tr)
+    yr.backward(g.astype(dtype))
+    assert_parity(yr.numpy(), O.relu_forward(x), rel(dtype), "relu")
+    assert_parity(tr.grad.numpy(), O.relu_backward(g, x), rel(dtype), "relu grad")
+
+
+@pytest.mark.parametrize("vocab", [1, 5, 300])
+def test_embedding_scatter_add(dtype, vocab):
+    import tensorgrad_b200 as tg
+
+    rng = np.random.default_rng(vocab)
+    ids = rng.integers(0, vocab, size=(7, 11))
+    w = rng.standard_normal((vocab, 3))
+    g = rng.standard_normal((7, 11, 3))
+    tw = tensor(w, dtype)
+    out = tg.embedding(ids, tw)
+    out.backward(g.astype(dtype))
+    assert_parity(out.numpy(), w[ids], rel(dtype), "gather")
+    assert_parity(tw.grad.numpy(), O.embedding_backward(ids, g, vocab), rel(dtype), "scatter")
+
+
+def test_embedding_rejects_bad_ids():
+    import tensorgrad_b200 as tg
+
+    w = tg.Tensor(np.arange(12.0).reshape(4, 3))
+    for bad in (-1, 4):
+        with pytest.raises(IndexError, match="embedding ids"):
+            tg.embedding(np.array([bad]), w)
+    with pytest.raises(TypeError, match="integers"):
+        tg.embedding(np.array([0.5]), w)
+
+
+@pytest.mark.parametrize("classes", [4, 65, 50304])
+def test_cross_entropy(dtype, classes):
+    import tensorgrad_b200 as tg
+
+    rng = np.random.default_rng(classes)
+    rows = 37 if classes > 1000 else 300
+    logits = rng.standard_normal((rows, classes)) * 2
+    target = rng.integers(0, classes, size=rows)
+    target[::7] = -100
+    tl = tensor(logits, dtype)
+    loss = tg.cross_entropy(tl, target)
+    loss.backward()
+    ref, logp = O.cross_entropy_forward(logits, target)
+    assert float(loss.item()) == pytest.approx(float(ref), rel=rel(dtype))
+    assert_parity(tl.grad.numpy(), O.cross_entropy_backward(1.0, logp, target, logits.shape),
+                  rel(dtype), "ce grad")
+    for red in ("sum", "none"):
+        out = tg.cross_entropy(tensor(logits, dtype, False), target, reduction=red)
+        refr, _ = O.cross_entropy_forward(logits, target, reduction=red)
+        assert_parity(out.numpy(), refr, rel(dtype), f"ce {red}")
+
+
+def test_cross_entropy_all_ignored_and_bad_target():
+    import tensorgrad_b200 as tg
+
+    out = tg.cross_entropy(tg.Tensor(np.zeros((2, 3))), np.array([7, 7]), ignore_index=7)
+    assert out.item() == 0.0
+    with pytest.raises(IndexError, match="target out of range"):
+        tg.cross_entropy(tg.Tensor(np.zeros((2, 3))), np.array([0, 3]))
+
+
+# ------------------------------------------------------------------------------- attention
+@pytest.mark.parametrize("shape,causal,seed", ATTN_CASES)
+def test_attention_matches_reference_fixture(dtype, shape, causal, seed):
+    import tensorgrad_b200 as tg
+
+    gold = load_golden("attention.npz")
+    key = "x".join(map(str, shape)) + ("_causal" if causal else "")
+    q, k, v, do = attention_inputs(shape, seed)
+    tq, tk, tv = (tensor(a, dtype) for a in (q, k, v))
+    o = tg.nn.functional.scaled_dot_product_attention(tq, tk, tv, causal=causal)
+    dq, dk, dv = tg.autograd.grad(o, [tq, tk, tv], grad_outputs=do.astype(dtype))
+    for name, ours in (("out", o), ("dq", dq), ("dk", dk), ("dv", dv)):
+        assert_parity(ours.numpy(), gold[f"{key}/{name}"], rel(dtype), f"{key} {name}")
+
+
+@pytest.mark.parametrize("b,t,h,hd", [(2, 64, 4, 32), (1, 129, 2, 64), (2, 40, 3, 16),
+                                      (1, 70, 1, 128)])
+def test_packed_self_attention(dtype, b, t, h, hd):
+    import tensorgrad_b200 as tg
+
+    rng = np.random.default_rng(t + h)
+    qkv = rng.standard_normal((b, t, 3 * h * hd))
+    g = rng.standard_normal((b, t, h * hd))
+    tq = tensor(qkv, dtype)
+    y = tg.nn.functional.packed_self_attention(tq, h)
+    y.backward(g.astype(dtype))
+    ref, p = O.packed_self_attention_forward(qkv, h)
+    assert_parity(y.numpy(), ref, rel(dtype), "y")
+    assert_parity(tq.grad.numpy(), O.packed_self_attention_backward(g, qkv, p, h), rel(dtype),
+                  "dqkv")
+
+
+# ------------------------------------------------------------------------------- optimiser
+def test_clip_and_adamw_match_reference(dtype):
+    import tensorgrad_b200 as tg
+
+    rng = np.random.default_rng(3)
+    shapes = [(17, 5), (64,), (3, 3, 3), (1000,)]
+    ps = [rng.standard_normal(s) for s in shapes]
+    gs = [rng.standard_normal(s) * 0.3 for s in shapes]
+    params = [tg.nn.Parameter(p.astype(dtype)) for p in ps]
+    opt = tg.optim.AdamW(params, lr=1e-2, weight_decay=0.1)
+    ref_p, ref_m, ref_v = list(ps), [np.zeros_like(p) for p in ps], [np.zeros_like(p) for p in ps]
+    for step in (1, 2, 3):
+        for p, g in zip(params, gs, strict=True):
+            p.grad = g.astype(dtype) * step
+        total = tg.optim.clip_grad_norm_(params, 1.5)
+        ref_total, clipped = O.clip_grad_norm([g * step for g in gs], 1.5)
+        assert total == pytest.approx(ref_total, rel=rel(dtype))
+        for p, c in zip(params, clipped, strict=True):
+            assert_parity(p.grad.numpy(), c, rel(dtype), "clipped grad")
+        opt.step()
+        for i in range(len(ps)):
+            ref_p[i], ref_m[i], ref_v[i] = O.adamw_update(ref_p[i], clipped[i], ref_m[i],
+                                                          ref_v[i], step, 1e-2, (0.9, 0.999),
+                                                          1e-8, 0.1)
+        for p, r in zip(params, ref_p, strict=True):
+            assert_parity(p.numpy(), r, rel(dtype), f"param step {step}")
+
+
+def test_adam_state_is_per_parameter():
+    import tensorgrad_b200 as tg
+
+    a, b = tg.nn.Parameter(np.ones(1)), tg.nn.Parameter(np.ones(1))
+    opt = tg.optim.Adam([a, b], lr=0.1)
+    a.grad = np.array([1.0], dtype=np.float32)
+    opt.step()
+    assert b.numpy()[0] == 1.0
+    assert len(opt.state) == 1
+    np.testing.assert_allclose(a.numpy(), [0.9], rtol=1e-6)
+
+
+def test_library_status_codes_raise_reference_exceptions():
+    from tensorgrad_b200._lib import check, lib
+
+    buf = ctypes.create_string_buffer(64)
+    assert lib.tg_last_error(buf, 64) == 0
+    with pytest.raises(ValueError):
+        check(lib.tg_layer_norm_forward(0, None, None, None, None, None, None, 4, 0, 1e-5, None))
