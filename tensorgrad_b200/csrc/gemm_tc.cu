@@ -159,15 +159,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// UMMA shared-memory descriptor, 128-byte swizzle, sm_100 version bits.
-//   start: byte address; lbo/sbo: leading/stride byte offsets.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t start, uint32_t lbo, uint32_t sbo) {
+// UMMA shared-memory descriptor with sm_100 version bits.
+//   start: byte address; lbo/sbo: leading/stride byte offsets; layout: 2 = SWIZZLE_128B
+//   (16-byte atoms, 8-row period), 1 = SWIZZLE_128B_BASE32B (32-byte atoms, 4-row period).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t start, uint32_t lbo, uint32_t sbo,
+                                              uint32_t layout) {
   uint64_t d = 0;
   d |= (uint64_t)((start >> 4) & 0x3FFF);
   d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
   d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
   d |= (uint64_t)1 << 46;  // descriptor version (Blackwell)
-  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+  d |= (uint64_t)layout << 61;
   return d;
 }
 
@@ -193,12 +195,17 @@ struct Layout {
   static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
 };
 
-// Byte offset, inside a 128 x BK (K-major) or BK x 128 (MN-major, 32-wide chunks) tile, of the
-// start of k-step kk (8 tf32 along K), and the descriptor offsets for that major-ness.
+// Descriptor of k-step kk (8 tf32 along K) of a stage tile.
+//  K-major: rows of 32 K values (128 B), 128-byte swizzle; the step starts 32 B into each
+//           row; the next 8-row group is 1024 B on.
+//  MN-major: the tile is 32-wide MN chunks of BK K-rows (128 B each, 4 KB per chunk). TF32
+//           MN-major operands use the 128-byte swizzle with 32-byte atoms (4-row period):
+//           the step starts 8 rows (1024 B) on, the next 4-row group is 512 B on (SBO) and the
+//           next 32-wide MN chunk 4 KB on (LBO).
 template <bool MN>
 __device__ __forceinline__ uint64_t tile_desc(uint32_t tile_base, int kk) {
-  if (MN) return smem_desc(tile_base + kk * 1024, /*lbo: next 32 MN*/ 32 * BK * 4, /*sbo*/ 1024);
-  return smem_desc(tile_base + kk * 32, /*lbo (unused)*/ 16, /*sbo: next 8 rows*/ 1024);
+  if (MN) return smem_desc(tile_base + kk * 1024, /*lbo*/ 32 * BK * 4, /*sbo*/ 512, 1);
+  return smem_desc(tile_base + kk * 32, /*lbo (unused)*/ 16, /*sbo*/ 1024, 2);
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN>
@@ -381,7 +388,7 @@ static EncodeFn get_encode() {
 
 // 2-D fp32 map over a row-major matrix of `rows` x `inner` with row stride `ld` elements.
 static int make_map(CUtensorMap* map, const float* ptr, int64_t inner, int64_t rows, int64_t ld,
-                    uint32_t box_inner, uint32_t box_rows) {
+                    uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
   EncodeFn enc = get_encode();
   if (!enc) return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
@@ -389,7 +396,7 @@ static int make_map(CUtensorMap* map, const float* ptr, int64_t inner, int64_t r
   cuuint32_t box[2] = {box_inner, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims,
-                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: tensor map encode failed (%d)", (int)r);
   return TG_OK;
@@ -401,11 +408,13 @@ static int launch(const GemmArgs<float>& p, cudaStream_t stream) {
   CUtensorMap ta, tb;
   int rc;
   // A: K-major = m rows of k; MN-major = k rows of m.
-  if (A_MN) rc = make_map(&ta, p.a, p.m, p.k, p.lda, 32, BK);
-  else rc = make_map(&ta, p.a, p.k, p.m, p.lda, BK, BM);
+  constexpr CUtensorMapSwizzle kSwK = CU_TENSOR_MAP_SWIZZLE_128B;
+  constexpr CUtensorMapSwizzle kSwMN = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+  if (A_MN) rc = make_map(&ta, p.a, p.m, p.k, p.lda, 32, BK, kSwMN);
+  else rc = make_map(&ta, p.a, p.k, p.m, p.lda, BK, BM, kSwK);
   if (rc != TG_OK) return rc;
-  if (B_MN) rc = make_map(&tb, p.b, p.n, p.k, p.ldb, 32, BK);
-  else rc = make_map(&tb, p.b, p.k, p.n, p.ldb, BK, BN);
+  if (B_MN) rc = make_map(&tb, p.b, p.n, p.k, p.ldb, 32, BK, kSwMN);
+  else rc = make_map(&tb, p.b, p.k, p.n, p.ldb, BK, BN, kSwK);
   if (rc != TG_OK) return rc;
   const size_t smem = STAGES * L::STAGE + 1024 + 256;
   static bool configured = false;

@@ -59,7 +59,7 @@ class Adam(Optimizer[_AdamState]):
             arena: Arena | None = getattr(p, "_arena", None)
             if arena is not None and id(arena) in self._moments and arena.intact():
                 m_buf, v_buf = self._moments[id(arena)]
-                off = arena.offsets[arena.params.index(p)]
+                off = arena.offsets[arena.index[id(p)]]
                 st = _AdamState(m_buf.flat_view(off, p.size, p.shape),
                                 v_buf.flat_view(off, p.size, p.shape))
             else:

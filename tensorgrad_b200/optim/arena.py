@@ -33,6 +33,7 @@ class Arena:
         self.dtype: np.dtype[Any] = params[0].dtype
         align = max(_ALIGN_BYTES // self.dtype.itemsize, 1)
         self.params = list(params)
+        self.index = {id(p): i for i, p in enumerate(self.params)}  # by identity, never ==
         self.offsets: list[int] = []
         total = 0
         for p in self.params:

