@@ -164,6 +164,21 @@ int tg_layer_norm_backward(int dtype, const void* g, const void* x, const void* 
                            int64_t rows, int64_t cols, unsigned need, void* scratch,
                            void* stream);
 
+/* Same as tg_layer_norm_backward, but allocation-free: for callers that cannot allocate
+ * device memory (a C or FFI host without a CUDA allocator of its own, or a latency-critical
+ * path where a cudaMalloc, which may synchronise the device, is not acceptable). No
+ * counterpart in the reference, which allocates its NumPy temporaries freely. The weight/
+ * bias partial sums use a file-scope device array of 4 MiB per device instead of `scratch`;
+ * a call whose partials need more (tg_layer_norm_scratch_bytes(dtype, rows, cols) > 4 MiB)
+ * returns TG_ERR_ARG. The array's device address is looked up on a device's first call,
+ * which should therefore come before any stream capture. All calls on a device share its
+ * array, so calls that overlap on that GPU (e.g. on two streams) race; each call overwrites
+ * every partial it reads, so no clearing is needed between calls. */
+int tg_layer_norm_backward_noalloc(int dtype, const void* g, const void* x, const void* w,
+                                   const void* mean, const void* rstd, void* gx, void* gw,
+                                   void* gb, int64_t rows, int64_t cols, unsigned need,
+                                   void* stream);
+
 /* ------------------------------------------------------------------ embedding
  * ops/layers.py:209-232. out[i, :] = w[ids[i], :]. Ids must be in [0, num) (checked on the
  * host by the caller, as the reference does before indexing). */

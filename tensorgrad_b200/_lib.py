@@ -84,6 +84,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tg_layer_norm_scratch_bytes": (sz, [c_int, i64, i64]),
     "tg_layer_norm_backward": (c_int, [c_int, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, u32, vp,
                                        vp]),
+    "tg_layer_norm_backward_noalloc": (c_int, [c_int, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64,
+                                               u32, vp]),
     "tg_embedding_forward": (c_int, [c_int, vp, vp, vp, i64, i64, i64, vp]),
     "tg_embedding_backward": (c_int, [c_int, vp, vp, vp, vp, i64, vp, i64, i64, c_int, vp]),
     "tg_cross_entropy_forward": (c_int, [c_int, vp, vp, vp, vp, vp, i64, i64, i64, c_int, vp, vp,

@@ -233,3 +233,65 @@ int tg_layer_norm_backward(int dtype, const void* g, const void* x, const void* 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- allocation-free variant
+// Some callers cannot allocate device memory for the VJP's scratch: a C or FFI host that
+// binds this library without any CUDA allocator of its own, or a latency-critical path
+// where cudaMalloc (which may synchronise the whole device) is not acceptable. For them
+// the weight/bias partial sums live in one file-scope device array of a fixed size, shared
+// by every call on a device.
+#include <mutex>
+
+namespace tg {
+namespace {
+
+constexpr size_t kLnStaticScratchBytes = size_t(4) << 20;  // 4 MiB per device
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_ln_static_scratch[kLnStaticScratchBytes];
+
+void* g_ln_static_ptr[kMaxDevices] = {};
+std::mutex g_ln_static_mutex;
+
+// Device address of the array on the current device (host code only sees a stand-in
+// symbol, so the address is looked up once per device, with that device current).
+int ln_static_scratch(void** out) {
+  int dev = 0;
+  TG_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return set_error(TG_ERR_UNSUPPORTED, "device %d", dev);
+  std::lock_guard<std::mutex> lock(g_ln_static_mutex);
+  if (!g_ln_static_ptr[dev]) {
+    void* p = nullptr;
+    TG_CUDA_TRY(cudaGetSymbolAddress(&p, g_ln_static_scratch));
+    g_ln_static_ptr[dev] = p;
+  }
+  *out = g_ln_static_ptr[dev];
+  return TG_OK;
+}
+
+}  // namespace
+}  // namespace tg
+
+extern "C" int tg_layer_norm_backward_noalloc(int dtype, const void* g, const void* x,
+                                              const void* w, const void* mean, const void* rstd,
+                                              void* gx, void* gw, void* gb, int64_t rows,
+                                              int64_t cols, unsigned need, void* stream) {
+  TG_CHECK_ARG(cols > 0 && cols <= 1024, "layer_norm: %lld columns (supported: 1..1024)",
+               (long long)cols);
+  const bool partials = (need & 2) || (need & 4);
+  const size_t bytes = partials ? tg_layer_norm_scratch_bytes(dtype, rows, cols) : 0;
+  if (bytes > tg::kLnStaticScratchBytes)
+    return tg::set_error(TG_ERR_ARG,
+                         "layer_norm_backward_noalloc: %zu bytes of partial sums exceed the "
+                         "%zu-byte static scratch (rows %lld, cols %lld)",
+                         bytes, tg::kLnStaticScratchBytes, (long long)rows, (long long)cols);
+  void* scratch = nullptr;
+  if (partials) {
+    const int rc = tg::ln_static_scratch(&scratch);
+    if (rc != TG_OK) return rc;
+  }
+  // Every partial the second pass reads is written by the first pass of the same call, so
+  // the array's previous contents never matter and nothing needs clearing.
+  return tg_layer_norm_backward(dtype, g, x, w, mean, rstd, gx, gw, gb, rows, cols, need,
+                                scratch, stream);
+}
