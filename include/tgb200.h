@@ -224,10 +224,17 @@ typedef struct tg_attn_shape {
   int64_t o_sb, o_sh, o_st; /* strides of o / dO (same layout) */
   int causal;
 } tg_attn_shape;
+/* fp32 with head_dim % 4 == 0 (and, when causal, tq == tk) runs on the tensor cores: batched
+ * 3xTF32 tcgen05 GEMMs for the score and value products, causal tiles above the diagonal
+ * skipped, softmax in warp-per-row kernels; the scores live in `scratch` for the call only.
+ * Other shapes and float64 use flash-style CUDA-core kernels (O and lse only, no scores).
+ * `scratch` holds tg_attention_forward_scratch_bytes bytes. */
+size_t tg_attention_forward_scratch_bytes(int dtype, const tg_attn_shape* s);
 int tg_attention_forward(int dtype, const tg_attn_shape* s, const void* q, const void* k,
-                         const void* v, void* o, void* lse, void* stream);
-/* dq/dk/dv use the strides of q/k/v. `scratch` holds tg_attention_scratch_bytes bytes. */
-size_t tg_attention_scratch_bytes(int dtype, const tg_attn_shape* s);
+                         const void* v, void* o, void* lse, void* scratch, void* stream);
+/* dq/dk/dv use the strides of q/k/v; P is recomputed from lse.
+ * `scratch` holds tg_attention_backward_scratch_bytes bytes. */
+size_t tg_attention_backward_scratch_bytes(int dtype, const tg_attn_shape* s);
 int tg_attention_backward(int dtype, const tg_attn_shape* s, const void* q, const void* k,
                           const void* v, const void* o, const void* lse, const void* dout,
                           void* dq, void* dk, void* dv, void* scratch, void* stream);

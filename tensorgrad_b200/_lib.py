@@ -92,8 +92,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                          vp]),
     "tg_cross_entropy_backward": (c_int, [c_int, vp, vp, vp, vp, vp, vp, i64, i64, i64, c_int,
                                           vp]),
-    "tg_attention_forward": (c_int, [c_int, POINTER(AttnShape), vp, vp, vp, vp, vp, vp]),
-    "tg_attention_scratch_bytes": (sz, [c_int, POINTER(AttnShape)]),
+    "tg_attention_forward_scratch_bytes": (sz, [c_int, POINTER(AttnShape)]),
+    "tg_attention_forward": (c_int, [c_int, POINTER(AttnShape), vp, vp, vp, vp, vp, vp, vp]),
+    "tg_attention_backward_scratch_bytes": (sz, [c_int, POINTER(AttnShape)]),
     "tg_attention_backward": (c_int, [c_int, POINTER(AttnShape), vp, vp, vp, vp, vp, vp, vp, vp,
                                       vp, vp, vp]),
     "tg_sumsq_scratch_bytes": (sz, [c_int]),

@@ -1,4 +1,5 @@
-// Fused softmax attention, flash style (ops/attention.py:71-116, 163-272).
+// Fused softmax attention, flash style (ops/attention.py:71-116, 163-272): the CUDA-core path
+// (float64, and fp32 shapes the tensor-core path of attention_tc.cu does not take).
 //
 // Forward: per (batch, head, block of query rows), keys/values stream through shared memory
 // in tiles; each query row keeps a running max, running sum and output accumulator, so P is
@@ -10,6 +11,8 @@
 //
 // Each query (or key) row is handled by TPR consecutive lanes that own DPT = D / TPR of its
 // dimensions; dot products are finished with xor-shuffles inside the lane group.
+#include <stdlib.h>
+
 #include "common.cuh"
 
 namespace tg {
@@ -343,25 +346,59 @@ int attn_backward_any(const AttnDims& p, const T* q, const T* k, const T* v, con
 }  // namespace
 }  // namespace tg
 
+namespace tg {
+// Tensor-core path (attention_tc.cu).
+bool attention_tc_supported(int dtype, const tg_attn_shape* s);
+size_t attention_tc_forward_scratch(const tg_attn_shape* s);
+size_t attention_tc_backward_scratch(const tg_attn_shape* s);
+int attention_tc_forward(const tg_attn_shape* s, const float* q, const float* k, const float* v,
+                         float* o, float* lse, void* scratch, cudaStream_t st);
+int attention_tc_backward(const tg_attn_shape* s, const float* q, const float* k, const float* v,
+                          const float* o, const float* lse, const float* dout, float* dq,
+                          float* dk, float* dv, void* scratch, cudaStream_t st);
+}  // namespace tg
+
 using namespace tg;
+
+namespace {
+// TG_ATTENTION=simt forces the CUDA-core kernels (a debugging switch for users).
+bool use_tc(int dtype, const tg_attn_shape* s) {
+  static int forced = -1;
+  if (forced < 0) {
+    const char* e = getenv("TG_ATTENTION");
+    forced = (e && e[0] == 's') ? 1 : 0;
+  }
+  return !forced && attention_tc_supported(dtype, s);
+}
+}  // namespace
 
 extern "C" {
 
+size_t tg_attention_forward_scratch_bytes(int dtype, const tg_attn_shape* s) {
+  return use_tc(dtype, s) ? attention_tc_forward_scratch(s) : 16;
+}
+
 int tg_attention_forward(int dtype, const tg_attn_shape* s, const void* q, const void* k,
-                         const void* v, void* o, void* lse, void* stream) {
+                         const void* v, void* o, void* lse, void* scratch, void* stream) {
   TG_CHECK_ARG(s && s->batch >= 0 && s->heads >= 0 && s->tq >= 0 && s->tk >= 0,
                "attention: bad shape");
   if (s->batch * s->heads * s->tq == 0) return TG_OK;
-  const AttnDims p = make_dims(s);
   cudaStream_t st = as_stream(stream);
+  if (use_tc(dtype, s)) {
+    TG_CHECK_ARG(scratch, "attention_forward: NULL scratch");
+    return attention_tc_forward(s, (const float*)q, (const float*)k, (const float*)v, (float*)o,
+                                (float*)lse, scratch, st);
+  }
+  const AttnDims p = make_dims(s);
   return TG_DISPATCH_FLOAT(dtype, T, [&] {
     return attn_forward_any<T>(p, (const T*)q, (const T*)k, (const T*)v, (T*)o, (T*)lse, st);
   });
 }
 
-size_t tg_attention_scratch_bytes(int dtype, const tg_attn_shape* s) {
+size_t tg_attention_backward_scratch_bytes(int dtype, const tg_attn_shape* s) {
+  if (use_tc(dtype, s)) return attention_tc_backward_scratch(s);
   const size_t es = dtype == TG_F64 ? 8 : 4;
-  return (size_t)(s->batch * s->heads * s->tq) * es;
+  return (size_t)(s->batch * s->heads * s->tq) * es + 16;
 }
 
 int tg_attention_backward(int dtype, const tg_attn_shape* s, const void* q, const void* k,
@@ -369,8 +406,12 @@ int tg_attention_backward(int dtype, const tg_attn_shape* s, const void* q, cons
                           void* dq, void* dk, void* dv, void* scratch, void* stream) {
   TG_CHECK_ARG(s && scratch, "attention_backward: NULL shape or scratch");
   if (s->batch * s->heads * (s->tq + s->tk) == 0) return TG_OK;
-  const AttnDims p = make_dims(s);
   cudaStream_t st = as_stream(stream);
+  if (use_tc(dtype, s))
+    return attention_tc_backward(s, (const float*)q, (const float*)k, (const float*)v,
+                                 (const float*)o, (const float*)lse, (const float*)dout,
+                                 (float*)dq, (float*)dk, (float*)dv, scratch, st);
+  const AttnDims p = make_dims(s);
   return TG_DISPATCH_FLOAT(dtype, T, [&] {
     return attn_backward_any<T>(p, (const T*)q, (const T*)k, (const T*)v, (const T*)o,
                                 (const T*)lse, (const T*)dout, (T*)dq, (T*)dk, (T*)dv,

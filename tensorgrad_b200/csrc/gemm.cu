@@ -140,8 +140,7 @@ int tg_gemm_batched(int dtype, int trans_a, int trans_b, int64_t m, int64_t n, i
   return TG_DISPATCH_FLOAT(dtype, T, [&] {
     auto p = make_args<T>(trans_a, trans_b, m, n, k, alpha, a, lda, stride_a, b, ldb, stride_b,
                           beta, c, ldc, stride_c, nullptr, batch);
-    if (batch == 1) return gemm_dispatch<T>(p, true, as_stream(stream));
-    return gemm_simt<T>(p, as_stream(stream));
+    return gemm_dispatch<T>(p, true, as_stream(stream));
   });
 }
 

@@ -4,6 +4,14 @@
 
 namespace tg {
 
+// Per-output-tile reduction ranges for the causal attention products (tensor-core path; the
+// tile is 128 output rows starting at m0):
+//   GEMM_K_UP_TO_ROW  -- reduce over k < m0 + 128 (operand zero beyond the diagonal tile)
+//   GEMM_K_FROM_ROW   -- reduce over k >= m0 rounded down to 32 (operand zero before it)
+//   GEMM_K_SKIP_UPPER -- full reduction, but tiles whose first column n0 > m0 + 127 are
+//                        skipped (never written)
+enum GemmKMode { GEMM_K_FULL = 0, GEMM_K_UP_TO_ROW = 1, GEMM_K_FROM_ROW = 2, GEMM_K_SKIP_UPPER = 3 };
+
 template <typename T>
 struct GemmArgs {
   int64_t m, n, k;
@@ -17,6 +25,7 @@ struct GemmArgs {
   T alpha, beta;
   int trans_a, trans_b;
   int64_t batch;
+  int kmode = GEMM_K_FULL;
 };
 
 template <typename T>

@@ -9,12 +9,13 @@
 // as hi*hi + hi*lo + lo*hi in fp32 in TMEM. The dropped lo*lo term and the TF32 truncation
 // of lo are ~2^-20 relative, close to fp32 rounding.
 //
-// Pipeline (one 128 x BN output tile per CTA, 256 threads):
+// Pipeline (one 128 x BN output tile per CTA, BN = 64 or 128, 256 threads; batched products
+// index the third tensor-map dimension with blockIdx.z):
 //   warp 0, lane 0 : TMA producer -- 128B-swizzled A/B tiles (BK = 32 fp32 = one swizzle
 //                    row) into a STAGES-deep ring, completion on full[s].
-//   warps 4..7     : split the stage into hi (in place) and lo (its own buffer), fence the
-//                    generic-proxy writes for the async proxy, arrive on split[s]; later the
-//                    epilogue (TMEM lanes 32*(warp-4) .. +31 via tcgen05.ld).
+//   warps 2..7     : split the stage into hi (in place) and lo (its own buffer), fence the
+//                    generic-proxy writes for the async proxy, arrive on split[s]; warps 4..7
+//                    then run the epilogue (TMEM lanes 32*(warp-4) .. +31 via tcgen05.ld).
 //   warp 1, lane 0 : MMA issuer -- 3 x (BK/8) tcgen05.mma per stage, tcgen05.commit frees
 //                    the stage (empty[s]); a final commit signals the accumulator.
 // Operands may be K-major (rows hold K) or MN-major (rows hold M or N); both are native
@@ -98,12 +99,13 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
-                                            int x, int y) {
+// 3-D tiled load (x innermost, z = batch); no multicast.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int x, int y, int z) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
 
@@ -182,10 +184,14 @@ __host__ __device__ constexpr uint32_t instr_desc(int m, int n, bool a_mn, bool 
 struct TcArgs {
   int64_t m, n, k;
   float* c;
-  int64_t ldc;
+  int64_t ldc, stride_c;  // row stride and batch stride of C (elements)
   const float* bias;
   float alpha, beta;
+  int kmode;              // GemmKMode: reduction range / tile skipping per output tile
 };
+
+// Split threads: warps 2..7.
+constexpr int kSplitThreads = 192;
 
 template <int BN>
 struct Layout {
@@ -213,6 +219,22 @@ __global__ void __launch_bounds__(256, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                TcArgs args) {
   using L = Layout<BN>;
+  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
+  const int bz = (int)blockIdx.z;
+  // Causal attention products: a tile strictly above the diagonal is skipped outright
+  // (kSkipUpper), and reductions over a triangular operand stop at (kUpToRow) or start
+  // from (kFromRow) the tile's first output row. Uniform per CTA, so before any sync.
+  if (args.kmode == GEMM_K_SKIP_UPPER && n0 > m0 + BM - 1) return;
+  const int nk_all = (int)((args.k + BK - 1) / BK);
+  int kb0 = 0, kb1 = nk_all;
+  if (args.kmode == GEMM_K_UP_TO_ROW) {
+    const int64_t kend = m0 + BM < args.k ? m0 + BM : args.k;
+    kb1 = (int)((kend + BK - 1) / BK);
+  } else if (args.kmode == GEMM_K_FROM_ROW) {
+    kb0 = (int)(m0 / BK);
+  }
+  const int nk = kb1 > kb0 ? kb1 - kb0 : 0;
+
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -225,13 +247,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
-  const int nk = (int)((args.k + BK - 1) / BK);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&split[s], 128);
+      mbar_init(&split[s], kSplitThreads);
       mbar_init(&empty[s], 1);
     }
     mbar_init(accum, 1);
@@ -247,33 +267,33 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
   if (warp == 0) {
     if (lane == 0) {
-      int kb = 0;
-      for (; kb < nk; ++kb) {
-        const int s = kb % STAGES, round = kb / STAGES;
+      int it = 0;
+      for (; it < nk; ++it) {
+        const int s = it % STAGES, round = it / STAGES;
         if (round > 0 && !wait_bar(&empty[s], (round - 1) & 1, abort_flag)) break;
         uint8_t* st = smem + s * L::STAGE;
         uint8_t* a_hi = st;
         uint8_t* b_hi = st + 2 * L::A_BYTES;
         mbar_arrive_expect_tx(&full[s], L::A_BYTES + L::B_BYTES);
-        const int k0 = kb * BK;
+        const int k0 = (kb0 + it) * BK;
         if (A_MN) {
 #pragma unroll
           for (int c = 0; c < BM / 32; ++c)
-            tma_load_2d(a_hi + c * 32 * BK * 4, &tmA, &full[s], (int)m0 + 32 * c, k0);
+            tma_load_3d(a_hi + c * 32 * BK * 4, &tmA, &full[s], (int)m0 + 32 * c, k0, bz);
         } else {
-          tma_load_2d(a_hi, &tmA, &full[s], k0, (int)m0);
+          tma_load_3d(a_hi, &tmA, &full[s], k0, (int)m0, bz);
         }
         if (B_MN) {
 #pragma unroll
           for (int c = 0; c < BN / 32; ++c)
-            tma_load_2d(b_hi + c * 32 * BK * 4, &tmB, &full[s], (int)n0 + 32 * c, k0);
+            tma_load_3d(b_hi + c * 32 * BK * 4, &tmB, &full[s], (int)n0 + 32 * c, k0, bz);
         } else {
-          tma_load_2d(b_hi, &tmB, &full[s], k0, (int)n0);
+          tma_load_3d(b_hi, &tmB, &full[s], k0, (int)n0, bz);
         }
       }
       if (*abort_flag) {
         // Let the copies already issued land before the CTA's shared memory goes away.
-        for (int j = kb - STAGES; j < kb; ++j) {
+        for (int j = it - STAGES; j < it; ++j) {
           if (j < 0) continue;
           wait_bar(&full[j % STAGES], (j / STAGES) & 1, abort_flag, false);
         }
@@ -283,8 +303,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (lane == 0) {
       constexpr uint32_t idesc = instr_desc(BM, BN, A_MN, B_MN);
       bool ok = true;
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % STAGES, round = kb / STAGES;
+      for (int it = 0; it < nk; ++it) {
+        const int s = it % STAGES, round = it / STAGES;
         if (!wait_bar(&split[s], round & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t st = smem_u32(smem + s * L::STAGE);
@@ -294,23 +314,24 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         for (int kk = 0; kk < BK / 8; ++kk) {
           const uint64_t ah = tile_desc<A_MN>(a_hi, kk), al = tile_desc<A_MN>(a_lo, kk);
           const uint64_t bh = tile_desc<B_MN>(b_hi, kk), bl = tile_desc<B_MN>(b_lo, kk);
-          mma_tf32(tmem, al, bh, idesc, (kb | kk) != 0);
+          mma_tf32(tmem, al, bh, idesc, (it | kk) != 0);
           mma_tf32(tmem, ah, bl, idesc, 1);
           mma_tf32(tmem, ah, bh, idesc, 1);
         }
         mma_commit(&empty[s]);
       }
       if (ok) {
-        mma_commit(accum);
+        mma_commit(accum);  // with nk == 0 this fires at once; the epilogue then uses 0
       } else {
         mma_commit(drain);
         wait_bar(drain, 0, abort_flag, false);  // MMAs already issued finish before dealloc
       }
     }
-  } else if (warp >= 4) {
-    const int t = threadIdx.x - 128;
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % STAGES, round = kb / STAGES;
+  }
+  if (warp >= 2) {
+    const int t = threadIdx.x - 64;
+    for (int it = 0; it < nk; ++it) {
+      const int s = it % STAGES, round = it / STAGES;
       if (!wait_bar(&full[s], round & 1, abort_flag)) break;
       uint8_t* st = smem + s * L::STAGE;
       float4* a_hi = reinterpret_cast<float4*>(st);
@@ -328,12 +349,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         lo[i] = l;
       };
 #pragma unroll 4
-      for (int i = t; i < (int)(L::A_BYTES / 16); i += 128) split4(a_hi, a_lo, i);
+      for (int i = t; i < (int)(L::A_BYTES / 16); i += kSplitThreads) split4(a_hi, a_lo, i);
 #pragma unroll 4
-      for (int i = t; i < (int)(L::B_BYTES / 16); i += 128) split4(b_hi, b_lo, i);
+      for (int i = t; i < (int)(L::B_BYTES / 16); i += kSplitThreads) split4(b_hi, b_lo, i);
       fence_proxy_async_smem();
       mbar_arrive(&split[s]);
     }
+  }
+  if (warp >= 4) {
     // Epilogue: TMEM lane r = 32 * (warp - 4) + lane holds output row m0 + r.
     // tcgen05.ld is warp-collective: decide per warp.
     const bool have = __all_sync(0xffffffffu, wait_bar(accum, 0, abort_flag));
@@ -341,7 +364,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (have) {
       const int ew = warp - 4;
       const int64_t row = m0 + 32 * ew + lane;
-      float* crow = args.c + row * args.ldc;
+      float* crow = args.c + (int64_t)bz * args.stride_c + row * args.ldc;
 #pragma unroll 1
       for (int cc = 0; cc < BN / 32; ++cc) {
         uint32_t r[32];
@@ -351,7 +374,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           for (int j = 0; j < 32; ++j) {
             const int64_t col = n0 + cc * 32 + j;
             if (col < args.n) {
-              float v = args.alpha * __uint_as_float(r[j]);
+              float v = nk ? args.alpha * __uint_as_float(r[j]) : 0.f;
               if (args.beta != 0.f) v += args.beta * crow[col];
               if (args.bias) v += args.bias[col];
               crow[col] = v;
@@ -386,19 +409,22 @@ static EncodeFn get_encode() {
   return fn;
 }
 
-// 2-D fp32 map over a row-major matrix of `rows` x `inner` with row stride `ld` elements.
+// 3-D fp32 map: `batch` row-major matrices of `rows` x `inner` (row stride `ld`, batch
+// stride `bstride` elements); boxes of box_inner x box_rows x 1.
 static int make_map(CUtensorMap* map, const float* ptr, int64_t inner, int64_t rows, int64_t ld,
-                    uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
+                    int64_t batch, int64_t bstride, uint32_t box_inner, uint32_t box_rows,
+                    CUtensorMapSwizzle swizzle) {
   EncodeFn enc = get_encode();
   if (!enc) return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-  cuuint32_t box[2] = {box_inner, box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims,
+  cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)(batch > 1 ? bstride : rows * ld) * 4};
+  cuuint32_t box[3] = {box_inner, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(ptr), dims,
                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: tensor map encode failed (%d)", (int)r);
+  if (r != CUDA_SUCCESS)
+    return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: tensor map encode failed (%d)", (int)r);
   return TG_OK;
 }
 
@@ -407,14 +433,14 @@ static int launch(const GemmArgs<float>& p, cudaStream_t stream) {
   using L = Layout<BN>;
   CUtensorMap ta, tb;
   int rc;
-  // A: K-major = m rows of k; MN-major = k rows of m.
+  // A: K-major = m rows of k; MN-major = k rows of m. Likewise B with n.
   constexpr CUtensorMapSwizzle kSwK = CU_TENSOR_MAP_SWIZZLE_128B;
   constexpr CUtensorMapSwizzle kSwMN = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
-  if (A_MN) rc = make_map(&ta, p.a, p.m, p.k, p.lda, 32, BK, kSwMN);
-  else rc = make_map(&ta, p.a, p.k, p.m, p.lda, BK, BM, kSwK);
+  if (A_MN) rc = make_map(&ta, p.a, p.m, p.k, p.lda, p.batch, p.stride_a, 32, BK, kSwMN);
+  else rc = make_map(&ta, p.a, p.k, p.m, p.lda, p.batch, p.stride_a, BK, BM, kSwK);
   if (rc != TG_OK) return rc;
-  if (B_MN) rc = make_map(&tb, p.b, p.n, p.k, p.ldb, 32, BK, kSwMN);
-  else rc = make_map(&tb, p.b, p.k, p.n, p.ldb, BK, BN, kSwK);
+  if (B_MN) rc = make_map(&tb, p.b, p.n, p.k, p.ldb, p.batch, p.stride_b, 32, BK, kSwMN);
+  else rc = make_map(&tb, p.b, p.k, p.n, p.ldb, p.batch, p.stride_b, BK, BN, kSwK);
   if (rc != TG_OK) return rc;
   const size_t smem = STAGES * L::STAGE + 1024 + 256;
   static bool configured = false;
@@ -423,10 +449,18 @@ static int launch(const GemmArgs<float>& p, cudaStream_t stream) {
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     configured = true;
   }
-  TcArgs a{p.m, p.n, p.k, p.c, p.ldc, p.bias, p.alpha, p.beta};
-  dim3 grid((unsigned)((p.n + BN - 1) / BN), (unsigned)((p.m + BM - 1) / BM));
+  TcArgs a{p.m, p.n, p.k, p.c, p.ldc, p.stride_c, p.bias, p.alpha, p.beta, p.kmode};
+  dim3 grid((unsigned)((p.n + BN - 1) / BN), (unsigned)((p.m + BM - 1) / BM), (unsigned)p.batch);
   gemm_tc_kernel<BN, STAGES, A_MN, B_MN><<<grid, 256, smem, stream>>>(ta, tb, a);
   return check_launch("gemm_tc");
+}
+
+template <int BN, int ST>
+static int launch_any(const GemmArgs<float>& p, bool a_mn, bool b_mn, cudaStream_t stream) {
+  if (!a_mn && !b_mn) return launch<BN, ST, false, false>(p, stream);
+  if (!a_mn && b_mn) return launch<BN, ST, false, true>(p, stream);
+  if (a_mn && !b_mn) return launch<BN, ST, true, false>(p, stream);
+  return launch<BN, ST, true, true>(p, stream);
 }
 
 }  // namespace tc
@@ -434,19 +468,18 @@ static int launch(const GemmArgs<float>& p, cudaStream_t stream) {
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 int gemm_tc_f32(const GemmArgs<float>& p, cudaStream_t stream) {
-  if (p.batch != 1 || p.m <= 0 || p.n <= 0 || p.k <= 0)
+  if (p.batch < 1 || p.batch > 65535 || p.m <= 0 || p.n <= 0 || p.k <= 0)
     return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: batch/empty shape");
   if (!aligned16(p.a) || !aligned16(p.b) || (p.lda % 4) || (p.ldb % 4))
     return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: operands not 16-byte aligned");
+  if (p.batch > 1 && ((p.stride_a % 4) || (p.stride_b % 4)))
+    return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: batch strides not 16-byte aligned");
   if (p.m > INT32_MAX || p.n > INT32_MAX || p.k > INT32_MAX)
     return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: dimension beyond int32");
   const bool a_mn = p.trans_a != 0;   // A stored k x m
   const bool b_mn = p.trans_b == 0;   // B stored k x n
-  constexpr int BN = 128, ST = 3;
-  if (!a_mn && !b_mn) return tc::launch<BN, ST, false, false>(p, stream);
-  if (!a_mn && b_mn) return tc::launch<BN, ST, false, true>(p, stream);
-  if (a_mn && !b_mn) return tc::launch<BN, ST, true, false>(p, stream);
-  return tc::launch<BN, ST, true, true>(p, stream);
+  if (p.n <= 64) return tc::launch_any<64, 4>(p, a_mn, b_mn, stream);
+  return tc::launch_any<128, 3>(p, a_mn, b_mn, stream);
 }
 
 }  // namespace tg

@@ -38,12 +38,14 @@ def _shape(b: int, h: int, tq: int, tk: int, d: int, q: tuple[int, int, int],
 
 
 def _forward(shape: AttnShape, code: int, q: int, k: int, v: int, o: int, lse: int) -> None:
-    check(lib.tg_attention_forward(code, shape, q, k, v, o, lse, device.stream()), "attention")
+    scratch = device.scratch(lib.tg_attention_forward_scratch_bytes(code, shape))
+    check(lib.tg_attention_forward(code, shape, q, k, v, o, lse, scratch.ptr, device.stream()),
+          "attention")
 
 
 def _backward(shape: AttnShape, code: int, q: int, k: int, v: int, o: int, lse: int, do: int,
               dq: int, dk: int, dv: int) -> None:
-    scratch = device.scratch(lib.tg_attention_scratch_bytes(code, shape))
+    scratch = device.scratch(lib.tg_attention_backward_scratch_bytes(code, shape))
     check(lib.tg_attention_backward(code, shape, q, k, v, o, lse, do, dq, dk, dv, scratch.ptr,
                                     device.stream()), "attention backward")
 

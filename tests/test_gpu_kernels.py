@@ -206,8 +206,24 @@ def test_attention_matches_reference_fixture(dtype, shape, causal, seed):
         assert_parity(ours.numpy(), gold[f"{key}/{name}"], rel(dtype), f"{key} {name}")
 
 
+def test_attention_causal_with_longer_keys(dtype):
+    # Causal with tk > tq (query i sees keys j <= i + tk - tq): the CUDA-core path.
+    import tensorgrad_b200 as tg
+
+    rng = np.random.default_rng(9)
+    q, k, v = (rng.standard_normal(s) for s in ((1, 2, 5, 16), (1, 2, 9, 16), (1, 2, 9, 16)))
+    do = rng.standard_normal((1, 2, 5, 16))
+    tq, tk, tv = (tensor(a, dtype) for a in (q, k, v))
+    o = tg.nn.functional.scaled_dot_product_attention(tq, tk, tv, causal=True)
+    dq, dk, dv = tg.autograd.grad(o, [tq, tk, tv], grad_outputs=do.astype(dtype))
+    ref_o, p = O.attention_forward(q, k, v, True)
+    for ours, ref, name in zip((o, dq, dk, dv), (ref_o, *O.attention_backward(do, q, k, v, p)),
+                               ("out", "dq", "dk", "dv"), strict=True):
+        assert_parity(ours.numpy(), ref, rel(dtype), name)
+
+
 @pytest.mark.parametrize("b,t,h,hd", [(2, 64, 4, 32), (1, 129, 2, 64), (2, 40, 3, 16),
-                                      (1, 70, 1, 128)])
+                                      (1, 70, 1, 128), (2, 300, 2, 64)])
 def test_packed_self_attention(dtype, b, t, h, hd):
     import tensorgrad_b200 as tg
 
