@@ -63,6 +63,10 @@ int tg_stream_synchronize(void* stream);
 int tg_gemm(int dtype, int trans_a, int trans_b, int64_t m, int64_t n, int64_t k, double alpha,
             const void* a, int64_t lda, const void* b, int64_t ldb, double beta, void* c,
             int64_t ldc, const void* bias, void* stream);
+/* Precision of the fp32 tensor-core GEMMs issued through tg_gemm / tg_linear_*: 0 (default)
+ * = fp32-accurate 3xTF32; 1 = plain TF32 (one MMA per product, ~2^-11 relative error; fast,
+ * outside the 1e-4 parity bar). Process-wide; no reference counterpart. */
+int tg_set_matmul_precision(int precision);
 /* Same, forcing the SIMT (CUDA-core) kernel: the accuracy reference for tg_gemm. */
 int tg_gemm_simt(int dtype, int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
                  double alpha, const void* a, int64_t lda, const void* b, int64_t ldb,

@@ -67,9 +67,13 @@ cudaEvent_t take_event() {
   return e;
 }
 
+// Process-wide matmul precision of the fp32 tensor-core path (tg_set_matmul_precision).
+int g_precision = 0;
+
 template <typename T>
-int gemm_dispatch(const GemmArgs<T>& p, bool allow_tc, cudaStream_t s) {
+int gemm_dispatch(GemmArgs<T> p, bool allow_tc, cudaStream_t s) {
   if (p.m == 0 || p.n == 0) return TG_OK;
+  p.precision = g_precision;
   if (p.k == 0) {
     // C = beta * C (+ bias): run the SIMT kernel, whose k loop is empty.
     return gemm_simt<T>(p, s);
@@ -142,6 +146,13 @@ int tg_gemm_batched(int dtype, int trans_a, int trans_b, int64_t m, int64_t n, i
                           beta, c, ldc, stride_c, nullptr, batch);
     return gemm_dispatch<T>(p, true, as_stream(stream));
   });
+}
+
+int tg_set_matmul_precision(int precision) {
+  TG_CHECK_ARG(precision == 0 || precision == 1, "matmul precision %d (0 = fp32, 1 = tf32)",
+               precision);
+  g_precision = precision;
+  return TG_OK;
 }
 
 int tg_gemm_profile(int enable) {

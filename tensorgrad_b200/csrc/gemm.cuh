@@ -26,6 +26,7 @@ struct GemmArgs {
   int trans_a, trans_b;
   int64_t batch;
   int kmode = GEMM_K_FULL;
+  int precision = 0;  // 0: fp32-accurate (3xTF32 on the tensor cores); 1: plain TF32
 };
 
 template <typename T>

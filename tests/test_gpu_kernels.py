@@ -286,3 +286,39 @@ def test_library_status_codes_raise_reference_exceptions():
     assert lib.tg_last_error(buf, 64) == 0
     with pytest.raises(ValueError):
         check(lib.tg_layer_norm_forward(0, None, None, None, None, None, None, 4, 0, 1e-5, None))
+
+
+def test_tensor_core_tf32_input_conversion_and_plain_tf32_mode():
+    """Plain TF32 mode (tg_set_matmul_precision(1)) and how the tensor core converts fp32
+    inputs to TF32. The default 3xTF32 split clears hi's low 13 bits itself, so it does not
+    depend on the conversion; this records it."""
+    from tensorgrad_b200 import device
+    from tensorgrad_b200._lib import F32, check, lib
+
+    ulp = 2.0**-10
+    xs = np.array([1 + 0.75 * ulp, 1 + 0.5 * ulp, 1 + 1.5 * ulp, -(1 + 0.75 * ulp)] * 32)
+    m, k, n = xs.size, 4, 128
+    a = np.zeros((m, k), np.float32)
+    a[:, 0] = xs
+    b = np.zeros((k, n), np.float32)
+    b[0, :] = 1.0
+    da, db, dc = device.from_numpy(a), device.from_numpy(b), device.empty((m, n), np.float32)
+    check(lib.tg_set_matmul_precision(1))
+    try:
+        check(lib.tg_gemm(F32, 0, 0, m, n, k, 1.0, da.ptr, k, db.ptr, n, 0.0, dc.ptr, n, None,
+                          device.stream()))
+        got = dc.numpy()[:, 0].astype(np.float64)
+    finally:
+        check(lib.tg_set_matmul_precision(0))
+    x32 = xs.astype(np.float32)
+    trunc = (x32.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32).astype(np.float64)
+    rne = np.array([np.float64(np.float32(v)) for v in xs])  # placeholder, replaced below
+    q = np.abs(xs) / ulp
+    rne = np.sign(xs) * ulp * np.where(np.abs(q - np.floor(q) - 0.5) < 1e-12,
+                                       np.where(np.floor(q) % 2 == 0, np.floor(q), np.ceil(q)),
+                                       np.round(q))
+    rna = np.sign(xs) * ulp * np.floor(q + 0.5)
+    modes = {"truncate": trunc, "nearest-even": rne, "nearest-away": rna}
+    matched = [name for name, v in modes.items() if np.array_equal(got, v)]
+    print("tensor-core fp32->tf32 conversion:", matched)
+    assert matched, f"TF32 conversion matches no known rounding: {got[:4]}"
