@@ -243,6 +243,95 @@ int tg_attention_backward(int dtype, const tg_attn_shape* s, const void* q, cons
                           const void* v, const void* o, const void* lse, const void* dout,
                           void* dq, void* dk, void* dv, void* scratch, void* stream);
 
+/* ------------------------------------------------------------------ convolution / pooling
+ * conv2d (ops/conv.py:128-177): cross-correlation of x (n, c, h, w) with w (c_out, c, kh, kw)
+ * by an im2col patch matrix `cols` of (n*oh*ow) rows x cols_ld columns (row = image*oh*ow +
+ * pixel, column = channel*kh*kw + i*kw + j, zero beyond c*kh*kw; cols_ld =
+ * tg_conv2d_cols_ld(s), a multiple of 4 so the rows suit the TMA), then one GEMM per
+ * direction: y = cols W^T (+ b) written straight to NCHW by the GEMM epilogue; dW = G^T cols
+ * with the reduction running over images and pixels of the NCHW gradient; dcols = G W per
+ * image, folded back onto dx by col2im (a gather, deterministic). `cols` is written by the
+ * forward call and read by the backward call (the reference keeps it for the weight
+ * gradient too, ops/conv.py:91-98, 114-116). Zero padding (ph, pw), strides (sh, sw). */
+typedef struct tg_conv_shape {
+  int64_t n, c, h, w;      /* input */
+  int64_t c_out, kh, kw;   /* filters */
+  int64_t sh, sw, ph, pw;  /* stride, zero padding */
+  int64_t oh, ow;          /* output: (h + 2 ph - kh) / sh + 1, likewise ow */
+} tg_conv_shape;
+int64_t tg_conv2d_cols_ld(const tg_conv_shape* s);
+size_t tg_conv2d_forward_scratch_bytes(int dtype, const tg_conv_shape* s);
+int tg_conv2d_forward(int dtype, const tg_conv_shape* s, const void* x, const void* w,
+                      const void* b, void* y, void* cols, void* scratch, void* stream);
+/* g: (n, c_out, oh, ow). gx / gw / gb may be NULL (not needed). */
+size_t tg_conv2d_backward_scratch_bytes(int dtype, const tg_conv_shape* s, int need_gx);
+int tg_conv2d_backward(int dtype, const tg_conv_shape* s, const void* g, const void* cols,
+                       const void* w, void* gx, void* gw, void* gb, void* scratch, void* stream);
+
+/* Training-mode batch norm over (n, c, hw) (ops/layers.py:144-189; BatchNorm1d/2d): per
+ * channel the biased batch mean/variance, y = (x - mean) * rstd * w + b with rstd =
+ * 1/sqrt(var + eps); mean and rstd (c) are saved for the VJP; running_mean / running_var (c,
+ * may be NULL) become (1 - momentum) r + momentum * stat with the unbiased variance
+ * var * m / (m - 1), m = n*hw. w / b may be NULL (no affine). Statistics accumulate in
+ * float64. `scratch`: tg_batch_norm_scratch_bytes. */
+size_t tg_batch_norm_scratch_bytes(int dtype, int64_t n, int64_t c, int64_t hw);
+int tg_batch_norm_forward(int dtype, int64_t n, int64_t c, int64_t hw, const void* x,
+                          const void* w, const void* b, void* y, void* mean, void* rstd,
+                          void* running_mean, void* running_var, double momentum, double eps,
+                          void* scratch, void* stream);
+/* The VJP of the composite the reference records: with xhat = (x - mean) rstd,
+ * gb = sum g, gw = sum g xhat, gx = rstd w (g - gb/m - xhat gw/m). Any of gx/gw/gb NULL. */
+int tg_batch_norm_backward(int dtype, int64_t n, int64_t c, int64_t hw, const void* g,
+                           const void* x, const void* w, const void* mean, const void* rstd,
+                           void* gx, void* gw, void* gb, void* scratch, void* stream);
+
+/* max_pool2d (ops/conv.py:300-357): -inf padding (ph <= kh/2, pw <= kw/2), first maximum of
+ * each window in row-major order wins, a NaN counts as the maximum. The winning cell's
+ * window offset (i*kw + j, kh*kw <= 256) is stored in `argmax` (n, c, oh, ow bytes) for the
+ * VJP, which sums g into every input cell over the windows that chose it. The struct's
+ * c_out is ignored. */
+int tg_max_pool2d_forward(int dtype, const tg_conv_shape* s, const void* x, void* y,
+                          uint8_t* argmax, void* stream);
+int tg_max_pool2d_backward(int dtype, const tg_conv_shape* s, const void* g,
+                           const uint8_t* argmax, void* gx, void* stream);
+
+/* ------------------------------------------------------------------ recurrent layers
+ * ops/recurrent.py:223-437: a whole time-major sequence x (T, B, I) per call; gate order and
+ * formulas are the reference's (PyTorch's). W_ih (G*H, I), W_hh (G*H, H), biases (G*H) may
+ * both be NULL (not one). Forward: one GEMM projects every step, then per step one
+ * recurrent GEMM and one gate kernel. Backward (BPTT): per step in reverse one gate-VJP
+ * kernel and one GEMM dh = dz W_hh, then one GEMM per weight and column sums for the biases.
+ *
+ * LSTM (G = 4, gates i, f, g, o): out (T, B, 2, H) holds h_t and c_t of every step; acts
+ * (T, B, 4H) receives the activated gates and tanh_c (T, B, H) tanh(c_t), both kept for the
+ * VJP. g is the gradient of out (T, B, 2, H). dx, dh0, dc0, dw_ih, dw_hh, db_ih, db_hh may be
+ * NULL (not needed). */
+size_t tg_lstm_forward_scratch_bytes(int dtype, int64_t T, int64_t B, int64_t I, int64_t H);
+int tg_lstm_forward(int dtype, int64_t T, int64_t B, int64_t I, int64_t H, const void* x,
+                    const void* h0, const void* c0, const void* w_ih, const void* w_hh,
+                    const void* b_ih, const void* b_hh, void* acts, void* out, void* tanh_c,
+                    void* scratch, void* stream);
+size_t tg_lstm_backward_scratch_bytes(int dtype, int64_t T, int64_t B, int64_t I, int64_t H);
+int tg_lstm_backward(int dtype, int64_t T, int64_t B, int64_t I, int64_t H, const void* g,
+                     const void* x, const void* h0, const void* c0, const void* w_ih,
+                     const void* w_hh, const void* acts, const void* out, const void* tanh_c,
+                     void* dx, void* dh0, void* dc0, void* dw_ih, void* dw_hh, void* db_ih,
+                     void* db_hh, void* scratch, void* stream);
+/* GRU (G = 3, gates r, u, n; n = tanh(a_n + r (h W_hn^T + b_hn)), h_t = (h - n) u + n):
+ * out (T, B, H); acts (T, B, 3H) receives (r, u, n) and hn (T, B, H) the h W_hn^T + b_hn
+ * term. g is the gradient of out. */
+size_t tg_gru_forward_scratch_bytes(int dtype, int64_t T, int64_t B, int64_t I, int64_t H);
+int tg_gru_forward(int dtype, int64_t T, int64_t B, int64_t I, int64_t H, const void* x,
+                   const void* h0, const void* w_ih, const void* w_hh, const void* b_ih,
+                   const void* b_hh, void* acts, void* hn, void* out, void* scratch,
+                   void* stream);
+size_t tg_gru_backward_scratch_bytes(int dtype, int64_t T, int64_t B, int64_t I, int64_t H);
+int tg_gru_backward(int dtype, int64_t T, int64_t B, int64_t I, int64_t H, const void* g,
+                    const void* x, const void* h0, const void* w_ih, const void* w_hh,
+                    const void* acts, const void* hn, const void* out, void* dx, void* dh0,
+                    void* dw_ih, void* dw_hh, void* db_ih, void* db_hh, void* scratch,
+                    void* stream);
+
 /* ------------------------------------------------------------------ optimiser
  * optim/clip.py:15-31: total = sqrt(sum over tensors of sum(g^2)) accumulated in float64.
  * ptrs/numels are HOST arrays of `count` device pointers / sizes. The result (float64) is

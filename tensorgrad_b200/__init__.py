@@ -11,9 +11,9 @@ from tensorgrad_b200._random import get_rng, manual_seed
 from tensorgrad_b200.autograd import enable_grad, is_grad_enabled, no_grad
 from tensorgrad_b200.device import DeviceArray, set_device, synchronize
 from tensorgrad_b200.ops import (
-    add, broadcast_to, cross_entropy, div, dropout, embedding, exp, flatten, gelu, layer_norm,
-    linear, log, matmul, max, mean, min, mse_loss, mul, neg, permute, pow, relu, reshape,
-    sigmoid, sqrt, squeeze, sub, sum, tanh, transpose, unsqueeze, var,
+    add, broadcast_to, conv2d, cross_entropy, div, dropout, embedding, exp, flatten, gelu, layer_norm,
+    linear, log, matmul, max, max_pool2d, mean, min, mse_loss, mul, neg, permute, pow, relu, reshape,
+    sigmoid, sqrt, squeeze, stack, sub, sum, tanh, transpose, unsqueeze, var,
 )
 from tensorgrad_b200.tensor import (
     Tensor, arange, full, get_default_dtype, ones, ones_like, rand, randn, set_default_dtype,
@@ -32,11 +32,12 @@ def _lib_launches() -> int:
     return int(lib.tg_launch_count())
 
 __all__ = [
-    "DeviceArray", "Tensor", "add", "arange", "autograd", "broadcast_to", "cross_entropy", "div",
+    "DeviceArray", "Tensor", "add", "arange", "autograd", "broadcast_to", "conv2d",
+    "cross_entropy", "div",
     "dropout", "embedding", "enable_grad", "exp", "flatten", "full", "gelu", "get_default_dtype",
-    "get_rng", "is_grad_enabled", "layer_norm", "linear", "log", "manual_seed", "matmul", "max",
+    "get_rng", "is_grad_enabled", "layer_norm", "linear", "log", "manual_seed", "matmul", "max", "max_pool2d",
     "mean", "min", "mse_loss", "mul", "neg", "nn", "no_grad", "ones", "ones_like", "optim",
     "permute", "pow", "profiler", "rand", "randn", "relu", "reshape", "set_default_dtype",
-    "set_device", "sigmoid", "sqrt", "squeeze", "sub", "sum", "synchronize", "tanh", "tensor",
+    "set_device", "sigmoid", "sqrt", "squeeze", "stack", "sub", "sum", "synchronize", "tanh", "tensor",
     "transpose", "unsqueeze", "var", "zeros", "zeros_like",
 ]

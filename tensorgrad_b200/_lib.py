@@ -36,6 +36,15 @@ class AttnShape(ctypes.Structure):
     )] + [("causal", c_int)]
 
 
+class ConvShape(ctypes.Structure):
+    """``tg_conv_shape``: input (n, c, h, w), filters (c_out, kh, kw), stride, padding and
+    the output size (oh, ow)."""
+
+    _fields_ = [(name, c_int64) for name in (
+        "n", "c", "h", "w", "c_out", "kh", "kw", "sh", "sw", "ph", "pw", "oh", "ow",
+    )]
+
+
 vp, i64, dbl, u32, sz = c_void_p, c_int64, c_double, c_uint, c_size_t
 pi64 = POINTER(c_int64)
 pint = POINTER(c_int)
@@ -98,6 +107,26 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tg_attention_backward_scratch_bytes": (sz, [c_int, POINTER(AttnShape)]),
     "tg_attention_backward": (c_int, [c_int, POINTER(AttnShape), vp, vp, vp, vp, vp, vp, vp, vp,
                                       vp, vp, vp]),
+    "tg_conv2d_cols_ld": (i64, [POINTER(ConvShape)]),
+    "tg_conv2d_forward_scratch_bytes": (sz, [c_int, POINTER(ConvShape)]),
+    "tg_conv2d_forward": (c_int, [c_int, POINTER(ConvShape), vp, vp, vp, vp, vp, vp, vp]),
+    "tg_conv2d_backward_scratch_bytes": (sz, [c_int, POINTER(ConvShape), c_int]),
+    "tg_conv2d_backward": (c_int, [c_int, POINTER(ConvShape), vp, vp, vp, vp, vp, vp, vp, vp]),
+    "tg_batch_norm_scratch_bytes": (sz, [c_int, i64, i64, i64]),
+    "tg_batch_norm_forward": (c_int, [c_int, i64, i64, i64, vp, vp, vp, vp, vp, vp, vp, vp, dbl,
+                                      dbl, vp, vp]),
+    "tg_batch_norm_backward": (c_int, [c_int, i64, i64, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp,
+                                       vp]),
+    "tg_max_pool2d_forward": (c_int, [c_int, POINTER(ConvShape), vp, vp, vp, vp]),
+    "tg_max_pool2d_backward": (c_int, [c_int, POINTER(ConvShape), vp, vp, vp, vp]),
+    "tg_lstm_forward_scratch_bytes": (sz, [c_int, i64, i64, i64, i64]),
+    "tg_lstm_forward": (c_int, [c_int, i64, i64, i64, i64] + [vp] * 12),
+    "tg_lstm_backward_scratch_bytes": (sz, [c_int, i64, i64, i64, i64]),
+    "tg_lstm_backward": (c_int, [c_int, i64, i64, i64, i64] + [vp] * 18),
+    "tg_gru_forward_scratch_bytes": (sz, [c_int, i64, i64, i64, i64]),
+    "tg_gru_forward": (c_int, [c_int, i64, i64, i64, i64] + [vp] * 11),
+    "tg_gru_backward_scratch_bytes": (sz, [c_int, i64, i64, i64, i64]),
+    "tg_gru_backward": (c_int, [c_int, i64, i64, i64, i64] + [vp] * 16),
     "tg_sumsq_scratch_bytes": (sz, [c_int]),
     "tg_sumsq_multi": (c_int, [c_int, c_int, pvp, pi64, vp, vp, vp]),
     "tg_clip_scale_multi": (c_int, [c_int, c_int, pvp, pi64, vp, dbl, dbl, vp, vp]),

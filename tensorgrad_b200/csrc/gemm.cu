@@ -102,6 +102,14 @@ int gemm_dispatch(GemmArgs<T> p, bool allow_tc, cudaStream_t s) {
 }
 
 }  // namespace
+
+template <typename T>
+int gemm_run(const GemmArgs<T>& p, cudaStream_t stream) {
+  return gemm_dispatch<T>(p, true, stream);
+}
+template int gemm_run<float>(const GemmArgs<float>&, cudaStream_t);
+template int gemm_run<double>(const GemmArgs<double>&, cudaStream_t);
+
 }  // namespace tg
 
 using namespace tg;

@@ -27,10 +27,36 @@ struct GemmArgs {
   int64_t batch;
   int kmode = GEMM_K_FULL;
   int precision = 0;  // 0: fp32-accurate (3xTF32 on the tensor cores); 1: plain TF32
+  // Convolution addressing (0 = plain row-major operands):
+  //   a_fold > 0: the reduction index of a K-major A (trans_a == 0) folds as
+  //               k = q * a_fold + r -> element (m, k) at a + q * stride_a + m * lda + r,
+  //               so k may run over images of an NCHW tensor (A itself is then not batched).
+  //   c_hw > 0  : C(m, n) at c + (m / c_hw) * stride_c + n * ldc + (m % c_hw): the GEMM row
+  //               is image * hw + pixel and the column a channel, written as NCHW (batch 1).
+  int64_t a_fold = 0;
+  int64_t c_hw = 0;
+  // Split-K partials (tensor-core path, batch 1): with a workspace of workspace_bytes the
+  // reduction may be split over more CTAs, each writing an fp32 partial, summed in split
+  // order by a second kernel (deterministic). nullptr: no split.
+  float* workspace = nullptr;
+  size_t workspace_bytes = 0;
 };
+
+// Address of C(m, n) of batch entry bz under the layouts above.
+template <typename T>
+__host__ __device__ __forceinline__ int64_t gemm_c_offset(const GemmArgs<T>& p, int64_t bz,
+                                                          int64_t m, int64_t n) {
+  if (p.c_hw > 0) return (m / p.c_hw) * p.stride_c + n * p.ldc + (m % p.c_hw);
+  return bz * p.stride_c + m * p.ldc + n;
+}
 
 template <typename T>
 int gemm_simt(const GemmArgs<T>& p, cudaStream_t stream);
+
+// The library's GEMM: the tensor-core kernel for fp32 where the TMA can address the
+// operands, the SIMT kernel otherwise (and for fp64); live-profiled like tg_gemm.
+template <typename T>
+int gemm_run(const GemmArgs<T>& p, cudaStream_t stream);
 
 // tcgen05 3xTF32 path. Returns TG_ERR_UNSUPPORTED (without launching) when the operands'
 // strides or base addresses do not meet the TMA's 16-byte rules, so the caller can fall back.

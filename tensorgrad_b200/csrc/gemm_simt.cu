@@ -16,9 +16,9 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(GemmArgs<T> p) {
   __shared__ T As[BK][BM + 4];
   __shared__ T Bs[BK][BN + 4];
   const int64_t bz = blockIdx.z;
-  const T* __restrict__ A = p.a + bz * p.stride_a;
+  const T* __restrict__ A = p.a + (p.a_fold > 0 ? 0 : bz * p.stride_a);
   const T* __restrict__ B = p.b + bz * p.stride_b;
-  T* __restrict__ C = p.c + bz * p.stride_c;
+  T* __restrict__ C = p.c;
   const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
   const int tid = threadIdx.x;
   const int tx = tid % (BN / TN), ty = tid / (BN / TN);
@@ -38,7 +38,10 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(GemmArgs<T> p) {
       if (p.trans_a) { kk = e / BM; r = e % BM; } else { r = e / BK; kk = e % BK; }
       const int64_t gi = m0 + r, gk = k0 + kk;
       T v = T(0);
-      if (gi < p.m && gk < p.k) v = p.trans_a ? A[gk * p.lda + gi] : A[gi * p.lda + gk];
+      if (gi < p.m && gk < p.k) {
+        if (p.a_fold > 0) v = A[(gk / p.a_fold) * p.stride_a + gi * p.lda + gk % p.a_fold];
+        else v = p.trans_a ? A[gk * p.lda + gi] : A[gi * p.lda + gk];
+      }
       As[kk][r] = v;
     }
 #pragma unroll
@@ -74,10 +77,11 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(GemmArgs<T> p) {
     for (int j = 0; j < TN; ++j) {
       const int64_t gj = n0 + tx * TN + j;
       if (gj >= p.n) continue;
+      const int64_t off = gemm_c_offset(p, bz, gi, gj);
       T v = p.alpha * acc[i][j];
-      if (p.beta != T(0)) v += p.beta * C[gi * p.ldc + gj];
+      if (p.beta != T(0)) v += p.beta * C[off];
       if (p.bias) v += p.bias[gj];
-      C[gi * p.ldc + gj] = v;
+      C[off] = v;
     }
   }
 }

@@ -193,6 +193,11 @@ struct TcArgs {
   int kmode;              // GemmKMode: reduction range / tile skipping per output tile
   int raw;                // 1: plain TF32 (no split; the tensor core truncates the fp32 bits)
   int m_tiles, n_tiles, batch;
+  int a_fold;             // > 0: A's k index folds over its third map dimension
+  int a_bcast, b_bcast;   // 1: the operand is shared by every batch entry (map depth 1)
+  int64_t c_hw;           // > 0: NCHW output (see GemmArgs::c_hw)
+  int splits, kb_per_split;
+  float* ws;              // splits > 1: partial sums, [splits][m][n]
 };
 
 constexpr int kThreads = 512;
@@ -227,16 +232,18 @@ __device__ __forceinline__ uint64_t tile_desc(uint32_t tile_base, int kk) {
 // Which output tile, batch entry and k-block range the t-th tile of the product is.
 struct TileInfo {
   int64_t m0, n0;
-  int bz, kb0, nk;
+  int bz, split, kb0, nk;
   bool skip;
 };
 
 __device__ __forceinline__ TileInfo tile_info(const TcArgs& a, int t, int bn) {
   TileInfo ti;
   const int mt = t % a.m_tiles;
-  const int rest = t / a.m_tiles;
+  int rest = t / a.m_tiles;
   const int nt = rest % a.n_tiles;
-  ti.bz = rest / a.n_tiles;
+  rest /= a.n_tiles;
+  ti.bz = rest % a.batch;
+  ti.split = rest / a.batch;
   ti.m0 = (int64_t)mt * BM;
   ti.n0 = (int64_t)nt * bn;
   // Causal attention products: a tile strictly above the diagonal is skipped outright, and
@@ -244,7 +251,10 @@ __device__ __forceinline__ TileInfo tile_info(const TcArgs& a, int t, int bn) {
   ti.skip = a.kmode == GEMM_K_SKIP_UPPER && ti.n0 > ti.m0 + BM - 1;
   const int nk_all = (int)((a.k + BK - 1) / BK);
   int kb0 = 0, kb1 = nk_all;
-  if (a.kmode == GEMM_K_UP_TO_ROW) {
+  if (a.splits > 1) {
+    kb0 = ti.split * a.kb_per_split;
+    kb1 = kb0 + a.kb_per_split < nk_all ? kb0 + a.kb_per_split : nk_all;
+  } else if (a.kmode == GEMM_K_UP_TO_ROW) {
     const int64_t kend = ti.m0 + BM < a.k ? ti.m0 + BM : a.k;
     kb1 = (int)((kend + BK - 1) / BK);
   } else if (a.kmode == GEMM_K_FROM_ROW) {
@@ -273,7 +283,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int total = args.m_tiles * args.n_tiles * args.batch;
+  const int total = args.m_tiles * args.n_tiles * args.batch * args.splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -309,19 +319,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           uint8_t* b_raw = st + 2 * L::A_BYTES;
           mbar_arrive_expect_tx(&full[s], L::A_BYTES + L::B_BYTES);
           const int k0 = (ti.kb0 + j) * BK;
+          const int za = args.a_bcast ? 0 : ti.bz, zb = args.b_bcast ? 0 : ti.bz;
           if (A_MN) {
 #pragma unroll
             for (int c = 0; c < BM / 32; ++c)
-              tma_load_3d(a_raw + c * 32 * BK * 4, &tmA, &full[s], (int)ti.m0 + 32 * c, k0, ti.bz);
+              tma_load_3d(a_raw + c * 32 * BK * 4, &tmA, &full[s], (int)ti.m0 + 32 * c, k0, za);
+          } else if (args.a_fold > 0) {
+            tma_load_3d(a_raw, &tmA, &full[s], k0 % args.a_fold, (int)ti.m0, k0 / args.a_fold);
           } else {
-            tma_load_3d(a_raw, &tmA, &full[s], k0, (int)ti.m0, ti.bz);
+            tma_load_3d(a_raw, &tmA, &full[s], k0, (int)ti.m0, za);
           }
           if (B_MN) {
 #pragma unroll
             for (int c = 0; c < BN / 32; ++c)
-              tma_load_3d(b_raw + c * 32 * BK * 4, &tmB, &full[s], (int)ti.n0 + 32 * c, k0, ti.bz);
+              tma_load_3d(b_raw + c * 32 * BK * 4, &tmB, &full[s], (int)ti.n0 + 32 * c, k0, zb);
           } else {
-            tma_load_3d(b_raw, &tmB, &full[s], k0, (int)ti.n0, ti.bz);
+            tma_load_3d(b_raw, &tmB, &full[s], k0, (int)ti.n0, zb);
           }
         }
       }
@@ -411,7 +424,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   } else if (warp >= kEpiWarp0) {
     const int ew = warp - kEpiWarp0;  // == warp % 4: TMEM lanes 32*ew .. +31
     int tc = 0;
-    const bool vec = (args.ldc % 4 == 0) && (args.stride_c % 4 == 0) &&
+    const bool vec = args.c_hw == 0 && (args.ldc % 4 == 0) && (args.stride_c % 4 == 0) &&
                      ((reinterpret_cast<uintptr_t>(args.c) & 15) == 0) &&
                      (!args.bias || (reinterpret_cast<uintptr_t>(args.bias) & 15) == 0);
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
@@ -423,7 +436,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       if (!have) break;
       tc_fence_after();
       const int64_t row = ti.m0 + 32 * ew + lane;
-      float* crow = args.c + (int64_t)ti.bz * args.stride_c + row * args.ldc;
+      // Partial sums of a split reduction go to the workspace unscaled (the reduce kernel
+      // applies alpha, beta and the bias). NCHW output: lanes are consecutive pixels, so the
+      // 32 stores of one column are one coalesced line.
+      const bool part = args.splits > 1;
+      float* crow;
+      int64_t cstep = 1;
+      if (part) {
+        crow = args.ws + ((int64_t)ti.split * args.m + row) * args.n;
+      } else if (args.c_hw > 0) {
+        crow = args.c + (row / args.c_hw) * args.stride_c + row % args.c_hw;
+        cstep = args.ldc;
+      } else {
+        crow = args.c + (int64_t)ti.bz * args.stride_c + row * args.ldc;
+      }
+      const float alpha = part ? 1.f : args.alpha, beta = part ? 0.f : args.beta;
+      const float* bias = part ? nullptr : args.bias;
+      const bool vrow = part ? (args.n % 4 == 0) : vec;
       const uint32_t acc = tmem + (uint32_t)(buf * BN) + ((uint32_t)(32 * ew) << 16);
 #pragma unroll 1
       for (int cc = 0; cc < BN / 32; ++cc) {
@@ -431,22 +460,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         tmem_ld32(acc + (uint32_t)(cc * 32), r);
         const int64_t c0 = ti.n0 + cc * 32;
         if (row < args.m && c0 < args.n) {
-          if (vec && c0 + 32 <= args.n) {
+          if (vrow && c0 + 32 <= args.n) {
 #pragma unroll
             for (int j = 0; j < 32; j += 4) {
               float4 v;
-              v.x = ti.nk ? args.alpha * __uint_as_float(r[j + 0]) : 0.f;
-              v.y = ti.nk ? args.alpha * __uint_as_float(r[j + 1]) : 0.f;
-              v.z = ti.nk ? args.alpha * __uint_as_float(r[j + 2]) : 0.f;
-              v.w = ti.nk ? args.alpha * __uint_as_float(r[j + 3]) : 0.f;
+              v.x = ti.nk ? alpha * __uint_as_float(r[j + 0]) : 0.f;
+              v.y = ti.nk ? alpha * __uint_as_float(r[j + 1]) : 0.f;
+              v.z = ti.nk ? alpha * __uint_as_float(r[j + 2]) : 0.f;
+              v.w = ti.nk ? alpha * __uint_as_float(r[j + 3]) : 0.f;
               float4* dst = reinterpret_cast<float4*>(crow + c0 + j);
-              if (args.beta != 0.f) {
+              if (beta != 0.f) {
                 const float4 o = *dst;
-                v.x += args.beta * o.x; v.y += args.beta * o.y;
-                v.z += args.beta * o.z; v.w += args.beta * o.w;
+                v.x += beta * o.x; v.y += beta * o.y;
+                v.z += beta * o.z; v.w += beta * o.w;
               }
-              if (args.bias) {
-                const float4 bb = *reinterpret_cast<const float4*>(args.bias + c0 + j);
+              if (bias) {
+                const float4 bb = *reinterpret_cast<const float4*>(bias + c0 + j);
                 v.x += bb.x; v.y += bb.y; v.z += bb.z; v.w += bb.w;
               }
               *dst = v;
@@ -456,10 +485,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             for (int j = 0; j < 32; ++j) {
               const int64_t col = c0 + j;
               if (col < args.n) {
-                float v = ti.nk ? args.alpha * __uint_as_float(r[j]) : 0.f;
-                if (args.beta != 0.f) v += args.beta * crow[col];
-                if (args.bias) v += args.bias[col];
-                crow[col] = v;
+                float* d = crow + col * cstep;
+                float v = ti.nk ? alpha * __uint_as_float(r[j]) : 0.f;
+                if (beta != 0.f) v += beta * *d;
+                if (bias) v += bias[col];
+                *d = v;
               }
             }
           }
@@ -526,20 +556,42 @@ static int sm_count() {
   return n;
 }
 
+// Sum of the split partials in split order, then alpha / beta / bias into C's layout.
+__global__ void __launch_bounds__(256)
+splitk_reduce_kernel(const float* __restrict__ ws, int splits, GemmArgs<float> p) {
+  const int64_t mn = p.m * p.n;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < mn;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int sp = 0; sp < splits; ++sp) s += ws[sp * mn + i];
+    const int64_t row = i / p.n, col = i % p.n;
+    const int64_t off = gemm_c_offset(p, 0, row, col);
+    float v = p.alpha * s;
+    if (p.beta != 0.f) v += p.beta * p.c[off];
+    if (p.bias) v += p.bias[col];
+    p.c[off] = v;
+  }
+}
+
 template <int BN, bool A_MN, bool B_MN>
-static int launch(const GemmArgs<float>& p, cudaStream_t stream) {
+static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
   using L = Layout<BN>;
   constexpr int STAGES = stages_for<BN>();
   CUtensorMap ta, tb;
   int rc;
-  // A: K-major = m rows of k; MN-major = k rows of m. Likewise B with n.
+  // A: K-major = m rows of k; MN-major = k rows of m. Likewise B with n. An operand shared
+  // by every batch entry (stride 0) gets a map of depth 1; a folded A has depth k / a_fold.
   constexpr CUtensorMapSwizzle kSwK = CU_TENSOR_MAP_SWIZZLE_64B;
   constexpr CUtensorMapSwizzle kSwMN = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
-  if (A_MN) rc = make_map(&ta, p.a, p.m, p.k, p.lda, p.batch, p.stride_a, 32, BK, kSwMN);
-  else rc = make_map(&ta, p.a, p.k, p.m, p.lda, p.batch, p.stride_a, BK, BM, kSwK);
+  const bool a_bcast = p.batch > 1 && p.stride_a == 0, b_bcast = p.batch > 1 && p.stride_b == 0;
+  const int64_t a_depth = a_bcast ? 1 : p.batch, b_depth = b_bcast ? 1 : p.batch;
+  if (A_MN) rc = make_map(&ta, p.a, p.m, p.k, p.lda, a_depth, p.stride_a, 32, BK, kSwMN);
+  else if (p.a_fold > 0)
+    rc = make_map(&ta, p.a, p.a_fold, p.m, p.lda, p.k / p.a_fold, p.stride_a, BK, BM, kSwK);
+  else rc = make_map(&ta, p.a, p.k, p.m, p.lda, a_depth, p.stride_a, BK, BM, kSwK);
   if (rc != TG_OK) return rc;
-  if (B_MN) rc = make_map(&tb, p.b, p.n, p.k, p.ldb, p.batch, p.stride_b, 32, BK, kSwMN);
-  else rc = make_map(&tb, p.b, p.k, p.n, p.ldb, p.batch, p.stride_b, BK, BN, kSwK);
+  if (B_MN) rc = make_map(&tb, p.b, p.n, p.k, p.ldb, b_depth, p.stride_b, 32, BK, kSwMN);
+  else rc = make_map(&tb, p.b, p.k, p.n, p.ldb, b_depth, p.stride_b, BK, BN, kSwK);
   if (rc != TG_OK) return rc;
   const size_t smem = STAGES * L::STAGE + 1024 + 256;
   static bool configured = false;
@@ -548,20 +600,44 @@ static int launch(const GemmArgs<float>& p, cudaStream_t stream) {
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     configured = true;
   }
-  TcArgs a{p.m, p.n, p.k, p.c, p.ldc, p.stride_c, p.bias, p.alpha, p.beta, p.kmode,
-           p.precision, (int)((p.m + BM - 1) / BM), (int)((p.n + BN - 1) / BN), (int)p.batch};
-  const int64_t tiles = (int64_t)a.m_tiles * a.n_tiles * a.batch;
+  TcArgs a{};
+  a.m = p.m; a.n = p.n; a.k = p.k;
+  a.c = p.c; a.ldc = p.ldc; a.stride_c = p.stride_c; a.bias = p.bias;
+  a.alpha = p.alpha; a.beta = p.beta;
+  a.kmode = p.kmode; a.raw = p.precision;
+  a.m_tiles = (int)((p.m + BM - 1) / BM);
+  a.n_tiles = (int)((p.n + BN - 1) / BN);
+  a.batch = (int)p.batch;
+  a.a_fold = (int)p.a_fold;
+  a.a_bcast = a_bcast; a.b_bcast = b_bcast;
+  a.c_hw = p.c_hw;
+  const int nk_all = (int)((p.k + BK - 1) / BK);
+  a.splits = 1;
+  a.kb_per_split = nk_all;
+  if (splits > 1) {
+    a.kb_per_split = (nk_all + splits - 1) / splits;
+    a.splits = (nk_all + a.kb_per_split - 1) / a.kb_per_split;  // every split non-empty
+    a.ws = p.workspace;
+  }
+  const int64_t tiles = (int64_t)a.m_tiles * a.n_tiles * a.batch * a.splits;
   const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
   gemm_tc_kernel<BN, STAGES, A_MN, B_MN><<<grid, kThreads, smem, stream>>>(ta, tb, a);
+  if (a.splits > 1) {
+    const int64_t mn = p.m * p.n;
+    const int blocks = (int)((mn + 255) / 256 < 4 * sm_count() ? (mn + 255) / 256 : 4 * sm_count());
+    splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(p.workspace, a.splits, p);
+    return check_launch("gemm_tc(split-k)", 2);
+  }
   return check_launch("gemm_tc");
 }
 
 template <int BN>
-static int launch_any(const GemmArgs<float>& p, bool a_mn, bool b_mn, cudaStream_t stream) {
-  if (!a_mn && !b_mn) return launch<BN, false, false>(p, stream);
-  if (!a_mn && b_mn) return launch<BN, false, true>(p, stream);
-  if (a_mn && !b_mn) return launch<BN, true, false>(p, stream);
-  return launch<BN, true, true>(p, stream);
+static int launch_any(const GemmArgs<float>& p, bool a_mn, bool b_mn, int splits,
+                      cudaStream_t stream) {
+  if (!a_mn && !b_mn) return launch<BN, false, false>(p, splits, stream);
+  if (!a_mn && b_mn) return launch<BN, false, true>(p, splits, stream);
+  if (a_mn && !b_mn) return launch<BN, true, false>(p, splits, stream);
+  return launch<BN, true, true>(p, splits, stream);
 }
 
 }  // namespace tc
@@ -577,6 +653,11 @@ int gemm_tc_f32(const GemmArgs<float>& p, cudaStream_t stream) {
     return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: batch strides not 16-byte aligned");
   if (p.m > INT32_MAX / 2 || p.n > INT32_MAX / 2 || p.k > INT32_MAX / 2)
     return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: dimension beyond int32");
+  if (p.a_fold > 0 && (p.trans_a || p.batch != 1 || p.a_fold % tc::BK || p.k % p.a_fold ||
+                       (p.stride_a % 4) || p.k / p.a_fold > INT32_MAX))
+    return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: folded A needs K-major, fold %% 16 == 0");
+  if (p.c_hw > 0 && p.batch != 1)
+    return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: NCHW output is not batched");
   const bool a_mn = p.trans_a != 0;   // A stored k x m
   const bool b_mn = p.trans_b == 0;   // B stored k x n
   // Tile width by estimated makespan: each persistent CTA runs ceil(tiles / SMs) tiles. A tile
@@ -595,9 +676,23 @@ int gemm_tc_f32(const GemmArgs<float>& p, cudaStream_t stream) {
       best = bn;
     }
   }
-  if (best == 64) return tc::launch_any<64>(p, a_mn, b_mn, stream);
-  if (best == 128) return tc::launch_any<128>(p, a_mn, b_mn, stream);
-  return tc::launch_any<256>(p, a_mn, b_mn, stream);
+  // Split-K when the output has too few tiles to occupy half the SMs and each split keeps at
+  // least 8 k-blocks (the pipeline's fill and the epilogue amortise over them).
+  int splits = 1;
+  if (p.workspace && p.batch == 1 && p.kmode == GEMM_K_FULL) {
+    const int64_t tiles = mt * ((p.n + best - 1) / best);
+    const int64_t nk = (p.k + tc::BK - 1) / tc::BK;
+    if (2 * tiles <= sms && nk >= 16) {
+      int64_t s = sms / tiles;
+      if (s > nk / 8) s = nk / 8;
+      const int64_t fit = (int64_t)(p.workspace_bytes / (sizeof(float) * (size_t)(p.m * p.n)));
+      if (s > fit) s = fit;
+      if (s >= 2) splits = (int)s;
+    }
+  }
+  if (best == 64) return tc::launch_any<64>(p, a_mn, b_mn, splits, stream);
+  if (best == 128) return tc::launch_any<128>(p, a_mn, b_mn, splits, stream);
+  return tc::launch_any<256>(p, a_mn, b_mn, splits, stream);
 }
 
 }  // namespace tg

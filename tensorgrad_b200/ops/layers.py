@@ -133,12 +133,23 @@ def batch_norm(
     momentum: float = 0.1,
     eps: float = 1e-5,
 ) -> Tensor:
-    """Batch normalisation over ``(N, C, *spatial)`` with per-channel statistics, composed of
-    differentiable ops exactly as the reference composes it (ops/layers.py:144-189)."""
+    """Batch normalisation over ``(N, C, *spatial)`` with per-channel statistics
+    (ops/layers.py:144-189).
+
+    Training mode runs fused kernels: one pass for the float64 per-channel statistics (and
+    the running-statistics update), one for the normalisation; the VJP is one reduction pass
+    and one elementwise pass, the closed form of the composite the reference records
+    (``mean``, ``var``, ``sub``, ``div``, ``sqrt``, ``mul``, ``add``). Evaluation mode is that
+    composite, as in the reference.
+    """
     if x.ndim < 2:
         raise ValueError(f"batch_norm expects (N, C, ...) input, got {x.shape}")
     axes = (0, *range(2, x.ndim))
     view = (1, -1, *([1] * (x.ndim - 2)))
+    stats_ok = running_mean is None or running_var is None or (
+        running_mean.dtype == x.dtype and running_var.dtype == x.dtype)
+    if training and x.dtype.kind == "f" and stats_ok and x.size:
+        return _batch_norm_train(x, running_mean, running_var, weight, bias, momentum, eps)
     if training:
         mean = reduce.mean(x, axes, keepdims=True)
         var = reduce.var(x, axes, keepdims=True, correction=0)
@@ -161,6 +172,59 @@ def batch_norm(
     if bias is not None:
         out = out + bias.reshape(view)
     return out
+
+
+def _batch_norm_train(x: Tensor, running_mean: DeviceArray | None,
+                      running_var: DeviceArray | None, weight: Tensor | None,
+                      bias: Tensor | None, momentum: float, eps: float) -> Tensor:
+    n, c = x.shape[0], x.shape[1]
+    hw = x.size // (n * c)
+    xd = x.data
+    wd = None if weight is None else (weight.data if weight.dtype == xd.dtype
+                                      else cast_array(weight.data, xd.dtype))
+    bd = None if bias is None else (bias.data if bias.dtype == xd.dtype
+                                    else cast_array(bias.data, xd.dtype))
+    if wd is not None and wd.size != c or bd is not None and bd.size != c:
+        raise ValueError(f"batch_norm: weight/bias must have {c} elements")
+    code = dtype_code(xd.dtype)
+    y = device.empty(x.shape, xd.dtype)
+    mean = device.empty((c,), xd.dtype)
+    rstd = device.empty((c,), xd.dtype)
+    track = running_mean is not None and running_var is not None
+    scratch = device.scratch(lib.tg_batch_norm_scratch_bytes(code, n, c, hw))
+    check(lib.tg_batch_norm_forward(
+        code, n, c, hw, xd.ptr, wd.ptr if wd is not None else None,
+        bd.ptr if bd is not None else None, y.ptr, mean.ptr, rstd.ptr,
+        running_mean.ptr if track else None, running_var.ptr if track else None,
+        momentum, eps, scratch.ptr, device.stream()), "batch_norm")
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray | None, ...]:
+        if g.dtype != xd.dtype:
+            g = cast_array(g, xd.dtype)
+        k = 1
+        need_w = need_b = False
+        if weight is not None:
+            need_w = need[k]
+            k += 1
+        if bias is not None:
+            need_b = need[k]
+        gx = device.empty(x.shape, xd.dtype) if need[0] else None
+        gw = device.empty((c,), xd.dtype) if need_w else None
+        gb = device.empty((c,), xd.dtype) if need_b else None
+        scr = device.scratch(lib.tg_batch_norm_scratch_bytes(code, n, c, hw))
+        check(lib.tg_batch_norm_backward(
+            code, n, c, hw, g.ptr, xd.ptr, wd.ptr if wd is not None else None, mean.ptr,
+            rstd.ptr, gx.ptr if gx is not None else None, gw.ptr if gw is not None else None,
+            gb.ptr if gb is not None else None, scr.ptr, device.stream()), "batch_norm backward")
+        grads: list[DeviceArray | None] = [gx]
+        if weight is not None:
+            grads.append(None if gw is None else gw.reshape(weight.shape))
+        if bias is not None:
+            grads.append(None if gb is None else gb.reshape(bias.shape))
+        return tuple(grads)
+
+    parents = tuple(t for t in (x, weight, bias) if t is not None)
+    return make_result(y, parents, backward, "batch_norm")
 
 
 def _segments(ids: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.ndarray]:

@@ -15,7 +15,7 @@ from tensorgrad_b200.ops._util import Need, as_tensor, make_result, normalize_ax
 from tensorgrad_b200.profiler import profiled
 from tensorgrad_b200.tensor import Tensor
 
-__all__ = ["broadcast_to", "flatten", "getitem", "permute", "reshape", "squeeze", "sum_to",
+__all__ = ["broadcast_to", "flatten", "getitem", "permute", "reshape", "squeeze", "stack", "sum_to",
            "transpose", "unsqueeze"]
 
 
@@ -169,3 +169,39 @@ def getitem(a: Any, index: Any) -> Tensor:
         return (gx,)
 
     return make_result(out, (ta,), backward, "getitem")
+
+
+@profiled("stack")
+def stack(tensors: Any, axis: int = 0) -> Tensor:
+    """Join equally shaped tensors along a new axis (ops/shape.py:265-281); the VJP hands
+    each input its slice of the gradient."""
+    ts = [as_tensor(t) for t in tensors]
+    if not ts:
+        raise ValueError("stack needs at least one tensor")
+    shape0 = ts[0].shape
+    if any(t.shape != shape0 for t in ts):
+        raise ValueError(f"stack: shapes differ: {[t.shape for t in ts]}")
+    ax = normalize_axis(axis, len(shape0) + 1)
+    dt = np.result_type(*[t.dtype for t in ts])
+    out_shape = (*shape0[:ax], len(ts), *shape0[ax:])
+    out = device.empty(out_shape, dt)
+    ostr = device.contiguous_strides(out_shape)
+    slot_strides = ostr[:ax] + ostr[ax + 1:]
+    for k, t in enumerate(ts):
+        src = t.data if t.dtype == dt else t.data.astype(dt)
+        strided_copy(src.ptr, device.contiguous_strides(shape0), out.ptr + k * ostr[ax] * out.itemsize,
+                     slot_strides, shape0, out.itemsize)
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray | None, ...]:
+        grads: list[DeviceArray | None] = []
+        for k in range(len(ts)):
+            if not need[k]:
+                grads.append(None)
+                continue
+            gk = device.empty(shape0, g.dtype)
+            strided_copy(g.ptr + k * ostr[ax] * g.itemsize, slot_strides, gk.ptr,
+                         device.contiguous_strides(shape0), shape0, g.itemsize)
+            grads.append(gk)
+        return tuple(grads)
+
+    return make_result(out, tuple(ts), backward, "stack")

@@ -86,3 +86,14 @@ def assert_update_parity(ours: np.ndarray, ref: np.ndarray, ill: np.ndarray, rel
         f"{what}: max err {err:.3e} over well-conditioned entries > {rel} * "
         f"{np.abs(ref).max():.3e}"
     )
+
+
+def assert_zero_gradient(ours: np.ndarray, scale: float, rel: float, what: str = "") -> None:
+    """A gradient that is exactly zero in exact arithmetic: the bias of a convolution that
+    feeds a batch norm (the norm removes any per-channel shift). Both the reference and this
+    build hold rounding noise there, so the check is absolute: every entry within
+    ``rel * scale``, ``scale`` the largest entry of the same layer's weight gradient."""
+    ours = np.asarray(ours, dtype=np.float64)
+    assert np.all(np.isfinite(ours)), f"{what}: non-finite values"
+    err = float(np.abs(ours).max()) if ours.size else 0.0
+    assert err <= rel * scale, f"{what}: |g| {err:.3e} > {rel} * {scale:.3e}"

@@ -7,10 +7,15 @@ import math
 import numpy as np
 import pytest
 
+from oracle import cnn as ocnn
 from oracle import gpt as ogpt
 from oracle import ops
-from tests.conftest import assert_parity, load_golden
-from tests.golden.specs import ATTN_CASES, GPT_SMALL, attention_inputs
+from oracle import rnn as ornn
+from tests.conftest import assert_parity, assert_zero_gradient, load_golden
+from tests.golden.specs import (
+    ATTN_CASES, CNN_SMALL, CNN_ZERO_GRAD, CONV_CASES, GPT_SMALL, POOL_CASES, RNN_CASES, RNN_SMALL,
+    attention_inputs, conv_inputs, pool_input, rnn_inputs,
+)
 
 REL64 = 1e-10  # float64 restatement vs float64 reference
 
@@ -103,3 +108,147 @@ def test_embedding_backward_is_add_at() -> None:
     np.testing.assert_allclose(ops.embedding_backward(ids, g, 5), expected, rtol=1e-12)
     with pytest.raises(IndexError):
         ops.embedding_forward(np.array([-1]), np.zeros((4, 3)))
+
+
+# ---------------------------------------------------------------------------- CNN path
+def test_cnn_two_steps_match_reference_fixture() -> None:
+    gold = load_golden("cnn_small.npz")
+    cfg = CNN_SMALL["cfg"]
+    params, buffers, state = ocnn.init_params(cfg, CNN_SMALL["seed"]), ocnn.init_buffers(cfg), None
+    for step in range(1, CNN_SMALL["steps"] + 1):
+        x, labels = ocnn.synthetic_batch(cfg, CNN_SMALL["batch"], CNN_SMALL["seed"] + step)
+        out = ocnn.train_step(params, buffers, x, labels, state)
+        assert out["loss"] == pytest.approx(float(gold[f"step{step}/loss"]), rel=REL64)
+        for name, g in out["grads"].items():
+            ref = gold[f"step{step}/grad/{name}"]
+            if name in CNN_ZERO_GRAD:
+                scale = float(np.abs(gold[f"step{step}/grad/{CNN_ZERO_GRAD[name]}"]).max())
+                assert_zero_gradient(g, scale, REL64, f"step{step} grad {name}")
+                assert_zero_gradient(ref, scale, REL64, f"reference step{step} grad {name}")
+            else:
+                assert_parity(g, ref, REL64, f"step{step} grad {name}")
+        for name, p in out["params"].items():
+            assert_parity(p, gold[f"step{step}/param/{name}"], REL64, f"step{step} param {name}")
+        for name, b in out["buffers"].items():
+            assert_parity(b, gold[f"step{step}/buffer/{name}"], REL64, f"step{step} {name}")
+        params, state = out["params"], out["state"]
+
+
+@pytest.mark.parametrize("case", range(len(CONV_CASES)))
+def test_conv2d_matches_reference_fixture(case) -> None:
+    gold = load_golden("conv_pool.npz")
+    x_shape, wspec, stride, padding, seed = CONV_CASES[case]
+    x, w, b, rng = conv_inputs(x_shape, wspec, seed)
+    y, cols = ocnn.conv2d_forward(x, w, b, stride, padding)
+    g = rng.standard_normal(y.shape)
+    gx, gw, gb = ocnn.conv2d_backward(g, x.shape, w, cols, stride, padding)
+    for name, ours in (("y", y), ("gx", gx), ("gw", gw), ("gb", gb)):
+        assert_parity(ours, gold[f"conv{case}/{name}"], REL64, f"conv{case} {name}")
+
+
+@pytest.mark.parametrize("case", range(len(POOL_CASES)))
+def test_max_pool2d_matches_reference_fixture(case) -> None:
+    gold = load_golden("conv_pool.npz")
+    x_shape, kernel, stride, padding, seed = POOL_CASES[case]
+    x, rng = pool_input(x_shape, seed)
+    y, winner = ocnn.max_pool2d_forward(x, kernel, stride, padding)
+    g = rng.standard_normal(y.shape)
+    gx = ocnn.max_pool2d_backward(g, winner, x.shape, kernel, stride, padding)
+    np.testing.assert_array_equal(y, gold[f"pool{case}/y"])
+    np.testing.assert_array_equal(gx, gold[f"pool{case}/gx"])
+
+
+def naive_conv2d(x, w, b, stride, pad):
+    """Direct loops over output positions (the reference's tests/test_ops_values.py:14-27)."""
+    xp = np.pad(x, ((0, 0), (0, 0), (pad, pad), (pad, pad)))
+    n, _, h, wd = xp.shape
+    c_out, _, k, _ = w.shape
+    oh, ow = (h - k) // stride + 1, (wd - k) // stride + 1
+    out = np.zeros((n, c_out, oh, ow))
+    for i in range(oh):
+        for j in range(ow):
+            patch = xp[:, :, i * stride:i * stride + k, j * stride:j * stride + k]
+            out[:, :, i, j] = np.tensordot(patch, w, axes=([1, 2, 3], [1, 2, 3])) + b
+    return out
+
+
+@pytest.mark.parametrize(("stride", "pad"), [(1, 0), (1, 1), (2, 1), (3, 0)])
+def test_conv2d_matches_naive_loops(rng, stride, pad) -> None:
+    x = rng.standard_normal((2, 3, 7, 6))
+    w = rng.standard_normal((4, 3, 3, 3))
+    b = rng.standard_normal(4)
+    y, _ = ocnn.conv2d_forward(x, w, b, (stride, stride), (pad, pad))
+    np.testing.assert_allclose(y, naive_conv2d(x, w, b, stride, pad), atol=1e-12)
+
+
+def argmax_pool(x, g, k, stride, pad):
+    """Output and input gradient where each window's gradient goes to the cell numpy.argmax
+    picks (the first maximum, or the first NaN): the rule of tests/test_ops_values.py:56-74."""
+    xp = np.pad(x, ((0, 0), (0, 0), (pad, pad), (pad, pad)), constant_values=-np.inf)
+    n, c, hp, wp = xp.shape
+    oh, ow = (hp - k) // stride + 1, (wp - k) // stride + 1
+    out = np.empty((n, c, oh, ow))
+    dxp = np.zeros_like(xp)
+    for bi, ch, i, j in np.ndindex(n, c, oh, ow):
+        window = xp[bi, ch, i * stride:i * stride + k, j * stride:j * stride + k]
+        r, q = divmod(int(np.argmax(window)), k)
+        out[bi, ch, i, j] = window[r, q]
+        dxp[bi, ch, i * stride + r, j * stride + q] += g[bi, ch, i, j]
+    return out, dxp[:, :, pad:pad + x.shape[2], pad:pad + x.shape[3]]
+
+
+@pytest.mark.parametrize(("k", "stride", "pad"), [(2, 2, 0), (3, 1, 1), (3, 2, 1), (2, 1, 0)])
+def test_max_pool2d_ties_and_nans_follow_argmax(k, stride, pad) -> None:
+    rng = np.random.default_rng(k * 10 + stride)
+    x = np.round(rng.standard_normal((2, 3, 7, 6)))
+    x.reshape(-1)[::13] = np.nan
+    y, winner = ocnn.max_pool2d_forward(x, (k, k), (stride, stride), (pad, pad))
+    g = rng.standard_normal(y.shape)
+    gx = ocnn.max_pool2d_backward(g, winner, x.shape, (k, k), (stride, stride), (pad, pad))
+    ey, egx = argmax_pool(x, g, k, stride, pad)
+    np.testing.assert_array_equal(y, ey)
+    np.testing.assert_allclose(gx, egx)
+
+
+# ---------------------------------------------------------------------------- LSTM / GRU
+def rnn_oracle(cell, x, h0, c0, w_ih, w_hh, b_ih, b_hh, g):
+    """Output and gradients of one recurrent op in the fixture's order."""
+    if cell == "lstm":
+        out, cache = ornn.lstm_forward(x, h0, c0, w_ih, w_hh, b_ih, b_hh)
+        grads = ornn.lstm_backward(g, x, h0, c0, w_ih, w_hh, True, out, cache)
+        names = ["dx", "dh0", "dc0", "dw_ih", "dw_hh", "db_ih", "db_hh"]
+    else:
+        out, cache = ornn.gru_forward(x, h0, w_ih, w_hh, b_ih, b_hh)
+        grads = ornn.gru_backward(g, x, h0, w_ih, w_hh, True, out, cache)
+        names = ["dx", "dh0", "dw_ih", "dw_hh", "db_ih", "db_hh"]
+    return out, dict(zip(names, grads, strict=True))
+
+
+@pytest.mark.parametrize("case", range(len(RNN_CASES)))
+def test_recurrent_ops_match_reference_fixture(case) -> None:
+    gold = load_golden("rnn_ops.npz")
+    cell, steps, batch, inputs, hidden, seed = RNN_CASES[case]
+    x, h0, c0, w_ih, w_hh, b_ih, b_hh, rng = rnn_inputs(cell, steps, batch, inputs, hidden, seed)
+    shape = (steps, batch, 2, hidden) if cell == "lstm" else (steps, batch, hidden)
+    g = rng.standard_normal(shape)
+    out, grads = rnn_oracle(cell, x, h0, c0, w_ih, w_hh, b_ih, b_hh, g)
+    assert_parity(out, gold[f"{cell}{case}/out"], REL64, f"{cell}{case} out")
+    for name, ours in grads.items():
+        assert_parity(ours, gold[f"{cell}{case}/{name}"], REL64, f"{cell}{case} {name}")
+
+
+@pytest.mark.parametrize("cell", ["lstm", "gru"])
+def test_recurrent_regressor_two_steps_match_reference_fixture(cell) -> None:
+    gold = load_golden("rnn_small.npz")
+    s = RNN_SMALL
+    cfg = ornn.Config(cell=cell, hidden=s["hidden"], seq=s["seq"])
+    params, state = ornn.init_params(cfg, s["seed"]), None
+    for step in range(1, s["steps"] + 1):
+        x, y = ornn.synthetic_batch(cfg, s["batch"], s["seed"] + step)
+        out = ornn.train_step(params, cfg, x, y, state)
+        assert out["loss"] == pytest.approx(float(gold[f"{cell}/step{step}/loss"]), rel=REL64)
+        for name, g in out["grads"].items():
+            assert_parity(g, gold[f"{cell}/step{step}/grad/{name}"], REL64, f"step{step} {name}")
+        for name, p in out["params"].items():
+            assert_parity(p, gold[f"{cell}/step{step}/param/{name}"], REL64, f"step{step} {name}")
+        params, state = out["params"], out["state"]
