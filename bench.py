@@ -1,19 +1,28 @@
-"""Throughput of the GPT training step (forward, backward, clip_grad_norm_, AdamW) on B200s.
+"""Throughput of the tensorgrad training step (forward, backward, AdamW) on B200s.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload gpt2|char_gpt|mha|cnn|lstm|gru]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N
 
-Workload: the GPT-2-small-shape configuration (12 layers, d_model 768, 12 heads, block 1024,
-vocab 50304, tied head), micro-batch 8 sequences of 1024 tokens per GPU, AdamW (lr 3e-4,
-wd 1e-4) with gradient clipping at 1.0, fp32 parameters; token ids uniform from a seed
-(synthetic, no dataset). Data parallel over N GPUs (one process per GPU, NCCL all-reduce of
-the gradient buffer), weak scaling: each GPU processes its own 8 x 1024 tokens.
+Workloads (synthetic seeded inputs of each configuration's shapes; no dataset):
 
-Prints one JSON line (rank 0). ``value`` is tokens/s of the whole job with the token ids
-already in device memory; ``e2e`` is the same step through the public API from pinned host
-arrays (uploads and the loss read-back inside the timed region). ``roofline`` is the
-tensor-core GEMM (the dominant kernel), timed live with CUDA events around every launch in
-the timed region. ``cpu_baseline`` is the float32 NumPy restatement of the reference's step
+* ``gpt2`` (default): GPT-2-small shape (12 layers, d_model 768, 12 heads, block 1024, vocab
+  50304, tied head), micro-batch 8 x 1024 tokens per GPU, AdamW (lr 3e-4, wd 1e-4), clip 1.0.
+  Data parallel over N GPUs (one process per GPU, NCCL all-reduce of the gradient arena),
+  weak scaling.
+* ``char_gpt``: 4 layers, d_model 128, 4 heads, block 128, vocab 65, batch 32; AdamW, clip 1.0.
+* ``mha``: the fused causal attention op alone, forward + backward, Q/K/V/dO (16, 8, 512, 64).
+* ``cnn``: Conv(3->32)-BN-ReLU-Pool, Conv(32->64)-BN-ReLU-Pool, Linear(16384->4) on 256
+  images of 3x64x64; cross entropy; AdamW.
+* ``lstm`` / ``gru``: the adding problem, T = 100, batch 512, hidden 512, Linear(512->1) on
+  the last state, MSE; BPTT; AdamW.
+
+Prints one JSON line (rank 0). ``value`` is the workload's throughput for the whole job with
+the inputs already in device memory; ``e2e`` is the same step through the public API from
+pinned host arrays (uploads and the read-back of the step's result inside the timed region).
+``roofline`` is the tensor-core GEMM (the dominant kernel), timed live with CUDA events
+around each of its launches in the timed region; its FLOPs are algorithmic (causal products
+counted at half). ``cpu_baseline`` is the float32 NumPy restatement of the reference's step
 (the oracle) on a bounded sample, timed on this host's cores.
 
 ``--impl reference`` times that CPU implementation alone (rank 0; other ranks exit 0).
@@ -29,17 +38,13 @@ import subprocess
 import sys
 import tempfile
 import time
+from dataclasses import dataclass, field
+from typing import Any
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-GPT2 = dict(vocab_size=50304, block_size=1024, n_layer=12, n_head=12, n_embd=768)
-MICRO_BATCH = 8
-SEQ = 1024
-METRIC = "GPT fwd+bwd+AdamW tokens/s"
-WORKLOAD = ("GPT-2-small-shape train step: 12 layers, d_model 768, 12 heads, block 1024, "
-            "vocab 50304, tied head; micro-batch 8 x 1024 tokens per GPU; AdamW lr 3e-4 wd 1e-4, "
-            "clip 1.0")
+ADAMW = dict(lr=3e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=1e-4)
 
 
 def parse() -> argparse.Namespace:
@@ -48,6 +53,7 @@ def parse() -> argparse.Namespace:
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=sorted(WORKLOADS), default="gpt2")
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     return p.parse_args()
 
@@ -61,30 +67,289 @@ def peaks() -> dict:
                 "source": "fallback"}
 
 
-# ----------------------------------------------------------------------------- CPU leg
-def cpu_reference_step_fn(threads: int):
-    """A callable running one oracle step (float32 NumPy, the reference's algorithm) on one
-    1024-token sequence of the workload, and a description of that sample."""
+# ----------------------------------------------------------------------------- workloads
+@dataclass
+class Built:
+    """A workload instantiated on the device."""
+
+    step: Any                     # step(inputs) -> result (a Tensor or tuple of them)
+    dev_inputs: tuple             # inputs already in device memory
+    pinned_inputs: tuple          # the same inputs in page-locked host memory
+    h2d_bytes: int
+    d2h_bytes: int
+    readback: Any                 # readback(result) -> host value (the e2e read of the result)
+    params: list = field(default_factory=list)
+
+
+@dataclass
+class Workload:
+    name: str
+    metric: str
+    unit: str
+    units_per_step: int           # tokens / samples / calls one GPU processes per step
+    description: str
+    config: dict
+
+    def flops(self) -> float:
+        return 0.0
+
+
+def _train_step(tg, model_fn, params, loss_fn, reducer, clip: float | None):
+    opt = tg.optim.AdamW(params, **ADAMW)
+
+    def step(*inputs):
+        loss = loss_fn(model_fn(inputs[0]), inputs[1])
+        opt.zero_grad()
+        loss.backward()
+        if reducer is not None:
+            reducer.reduce()
+        if clip is not None:
+            tg.optim.clip_grad_norm_(params, clip)
+        opt.step()
+        return loss
+
+    return step
+
+
+def _pinned(device, arrays):
     import numpy as np
-    from threadpoolctl import threadpool_limits
 
-    from oracle import gpt as ogpt
-
-    cfg = ogpt.Config(**GPT2)
-    params = {k: v.astype(np.float32) for k, v in ogpt.init_params(cfg, 1234).items()}
-    state = {"params": params, "state": None}
-    ids, targets = ogpt.synthetic_batch(cfg, 1, SEQ, 99)
-    limiter = threadpool_limits(threads)
-
-    def step() -> None:
-        out = ogpt.train_step(state["params"], ids, targets, cfg, state["state"])
-        state["params"], state["state"] = out["params"], out["state"]
-
-    sample = (f"1 sequence x {SEQ} tokens of the workload (full 12-layer GPT-2-small model, "
-              f"float32 NumPy restatement of the reference step), {threads} BLAS threads")
-    return step, sample, limiter
+    out = []
+    for a in arrays:
+        p = device.pinned_empty(a.shape, a.dtype if a.dtype != np.float64 else np.float32)
+        p[...] = a
+        out.append(p)
+    return tuple(out)
 
 
+class GPTWorkload(Workload):
+    def __init__(self, name, cfg: dict, batch: int, seq: int, description: str) -> None:
+        super().__init__(name, "GPT fwd+bwd+AdamW tokens/s", "tokens/s", batch * seq,
+                         description, {"global_batch": batch, "seq_len": seq})
+        self.cfg, self.batch, self.seq = cfg, batch, seq
+
+    def flops(self) -> float:
+        from oracle import gpt as ogpt
+
+        return ogpt.step_flops(ogpt.Config(**self.cfg), self.batch, self.seq)
+
+    def build(self, tg, device, rank, reducer_cls) -> Built:
+        import numpy as np
+
+        tg.manual_seed(1234)
+        model = tg.nn.GPT(tg.nn.GPTConfig(**self.cfg, dropout=0.0))
+        params = list(model.parameters())
+        reducer = reducer_cls(params) if reducer_cls else None
+        step = _train_step(tg, model, params, tg.cross_entropy, reducer, 1.0)
+        rng = np.random.default_rng(1000 + rank)
+        v = self.cfg["vocab_size"]
+        ids = rng.integers(0, v, size=(self.batch, self.seq), dtype=np.int64)
+        tgt = rng.integers(0, v, size=(self.batch, self.seq), dtype=np.int64)
+        return Built(step, (tg.Tensor(ids), tg.Tensor(tgt)), _pinned(device, (ids, tgt)),
+                     ids.nbytes + tgt.nbytes, 4, lambda loss: loss.item(), params)
+
+    def cpu_step(self, threads: int):
+        import numpy as np
+
+        from oracle import gpt as ogpt
+
+        cfg = ogpt.Config(**self.cfg)
+        batch = 1 if self.seq >= 1024 else self.batch
+        params = {k: v.astype(np.float32) for k, v in ogpt.init_params(cfg, 1234).items()}
+        state = {"params": params, "state": None}
+        ids, targets = ogpt.synthetic_batch(cfg, batch, self.seq, 99)
+
+        def step() -> None:
+            out = ogpt.train_step(state["params"], ids, targets, cfg, state["state"])
+            state["params"], state["state"] = out["params"], out["state"]
+
+        return step, batch * self.seq, (
+            f"{batch} x {self.seq} tokens of the workload (full model), float32 NumPy "
+            f"restatement of the reference step, {threads} BLAS threads")
+
+
+class MHAWorkload(Workload):
+    SHAPE = (16, 8, 512, 64)
+
+    def __init__(self) -> None:
+        super().__init__("mha", "causal MHA fwd+bwd calls/s", "calls/s", 1,
+                         "fused causal multi-head attention forward + backward alone: Q, K, V, "
+                         "dO (16, 8, 512, 64) ~ N(0, 1); outputs dQ, dK, dV",
+                         {"shape": list(self.SHAPE), "causal": True})
+
+    def flops(self) -> float:
+        b, h, t, d = self.SHAPE
+        return 14.0 * b * h * t * t * d / 2  # fwd 4 + bwd 10 (incl. recompute), causal half
+
+    def build(self, tg, device, rank, reducer_cls) -> Built:
+        import numpy as np
+
+        rng = np.random.default_rng(77 + rank)
+        arrays = [rng.standard_normal(self.SHAPE).astype(np.float32) for _ in range(4)]
+
+        def step(q, k, v, do):
+            q, k, v = (tg.Tensor(a, requires_grad=True) if not isinstance(a, tg.Tensor) or
+                       not a.requires_grad else a for a in (q, k, v))
+            o = tg.nn.functional.scaled_dot_product_attention(q, k, v, causal=True)
+            return tg.autograd.grad(o, [q, k, v], grad_outputs=do)
+
+        dev = tuple(tg.Tensor(a, requires_grad=i < 3) for i, a in enumerate(arrays))
+        nbytes = arrays[0].nbytes
+        return Built(step, dev, _pinned(device, arrays), 4 * nbytes, 3 * nbytes,
+                     lambda grads: [g.numpy() for g in grads])
+
+    def cpu_step(self, threads: int):
+        import numpy as np
+
+        from oracle import ops as O
+
+        b, h, t, d = self.SHAPE
+        rng = np.random.default_rng(5)
+        q, k, v, do = (rng.standard_normal((1, h, t, d)).astype(np.float32) for _ in range(4))
+
+        def step() -> None:
+            o, p = O.attention_forward(q, k, v, True)
+            O.attention_backward(do, q, k, v, p)
+
+        return step, 1.0 / b, (f"1 of the 16 batch entries (8 heads x 512 x 64), float32 NumPy "
+                               f"restatement of the reference's attention VJP, {threads} BLAS "
+                               "threads; calls/s scaled by 1/16")
+
+
+class CNNWorkload(Workload):
+    def __init__(self) -> None:
+        super().__init__("cnn", "CNN fwd+bwd+AdamW samples/s", "samples/s", 256,
+                         "CNN train step: Conv2d 3->32 3x3 pad 1 + BatchNorm2d + ReLU + "
+                         "MaxPool2d 2, Conv2d 32->64 same, Flatten, Linear 16384->4; 256 images "
+                         "3x64x64 ~ N(0,1), 4 classes; cross entropy; AdamW",
+                         {"global_batch": 256, "image": [3, 64, 64]})
+
+    def flops(self) -> float:
+        from oracle import cnn as ocnn
+
+        return ocnn.step_flops(ocnn.Config(), 256)
+
+    def build(self, tg, device, rank, reducer_cls) -> Built:
+        import numpy as np
+
+        from oracle import cnn as ocnn
+
+        cfg = ocnn.Config()
+        nn = tg.nn
+        model = nn.Sequential(
+            nn.Conv2d(3, 32, 3, padding=1), nn.BatchNorm2d(32), nn.ReLU(), nn.MaxPool2d(2),
+            nn.Conv2d(32, 64, 3, padding=1), nn.BatchNorm2d(64), nn.ReLU(), nn.MaxPool2d(2),
+            nn.Flatten(), nn.Linear(64 * 16 * 16, 4))
+        model.load_state_dict(ocnn.init_params(cfg, 3) | ocnn.init_buffers(cfg))
+        params = list(model.parameters())
+        reducer = reducer_cls(params) if reducer_cls else None
+        step = _train_step(tg, model, params, tg.cross_entropy, reducer, None)
+        x, labels = ocnn.synthetic_batch(cfg, 256, 100 + rank)
+        x = x.astype(np.float32)
+        return Built(step, (tg.Tensor(x), tg.Tensor(labels)), _pinned(device, (x, labels)),
+                     x.nbytes + labels.nbytes, 4, lambda loss: loss.item(), params)
+
+    def cpu_step(self, threads: int):
+        import numpy as np
+
+        from oracle import cnn as ocnn
+
+        cfg = ocnn.Config()
+        batch = 16
+        params = {k: v.astype(np.float32) for k, v in ocnn.init_params(cfg, 3).items()}
+        bufs = {k: v.astype(np.float32) for k, v in ocnn.init_buffers(cfg).items()}
+        x, labels = ocnn.synthetic_batch(cfg, batch, 7)
+        x = x.astype(np.float32)
+        state = {"params": params, "state": None}
+
+        def step() -> None:
+            out = ocnn.train_step(state["params"], bufs, x, labels, state["state"])
+            state["params"], state["state"] = out["params"], out["state"]
+
+        return step, batch, (f"{batch} of the 256 images, float32 NumPy restatement of the "
+                             f"reference step, {threads} BLAS threads")
+
+
+class RNNWorkload(Workload):
+    def __init__(self, cell: str) -> None:
+        super().__init__(cell, f"{cell.upper()} BPTT fwd+bwd+AdamW samples/s", "samples/s",
+                         512, f"{cell.upper()} adding-problem train step: T 100, batch 512, "
+                         "input 2 (values U[0,1], markers {0,1}), hidden 512, Linear 512->1 on "
+                         "the last state, MSE, full BPTT, AdamW",
+                         {"global_batch": 512, "seq_len": 100, "hidden": 512})
+        self.cell = cell
+
+    def flops(self) -> float:
+        from oracle import rnn as ornn
+
+        return ornn.step_flops(ornn.Config(cell=self.cell), 512)
+
+    def build(self, tg, device, rank, reducer_cls) -> Built:
+        import numpy as np
+
+        from oracle import rnn as ornn
+
+        cfg = ornn.Config(cell=self.cell)
+        cell_cls = tg.nn.LSTM if self.cell == "lstm" else tg.nn.GRU
+
+        class Regressor(tg.nn.Module):
+            def __init__(self) -> None:
+                super().__init__()
+                self.rnn = cell_cls(2, 512)
+                self.head = tg.nn.Linear(512, 1)
+
+            def forward(self, x):
+                output, _ = self.rnn(x)
+                return self.head(output[-1])
+
+        model = Regressor()
+        model.load_state_dict(ornn.init_params(cfg, 9))
+        params = list(model.parameters())
+        reducer = reducer_cls(params) if reducer_cls else None
+        step = _train_step(tg, model, params, tg.mse_loss, reducer, None)
+        x, y = ornn.synthetic_batch(cfg, 512, 200 + rank)
+        x, y = x.astype(np.float32), y.astype(np.float32)
+        return Built(step, (tg.Tensor(x), tg.Tensor(y)), _pinned(device, (x, y)),
+                     x.nbytes + y.nbytes, 4, lambda loss: loss.item(), params)
+
+    def cpu_step(self, threads: int):
+        import numpy as np
+
+        from oracle import rnn as ornn
+
+        cfg = ornn.Config(cell=self.cell)
+        batch = 32
+        params = {k: v.astype(np.float32) for k, v in ornn.init_params(cfg, 9).items()}
+        x, y = ornn.synthetic_batch(cfg, batch, 3)
+        x, y = x.astype(np.float32), y.astype(np.float32)
+        state = {"params": params, "state": None}
+
+        def step() -> None:
+            out = ornn.train_step(state["params"], cfg, x, y, state["state"])
+            state["params"], state["state"] = out["params"], out["state"]
+
+        return step, batch, (f"{batch} of the 512 sequences (T 100, hidden 512), float32 NumPy "
+                             f"restatement of the reference step, {threads} BLAS threads")
+
+
+WORKLOADS: dict[str, Workload] = {
+    "gpt2": GPTWorkload(
+        "gpt2", dict(vocab_size=50304, block_size=1024, n_layer=12, n_head=12, n_embd=768), 8,
+        1024, "GPT-2-small-shape train step: 12 layers, d_model 768, 12 heads, block 1024, "
+              "vocab 50304, tied head; micro-batch 8 x 1024 tokens per GPU; AdamW lr 3e-4 wd "
+              "1e-4, clip 1.0"),
+    "char_gpt": GPTWorkload(
+        "char_gpt", dict(vocab_size=65, block_size=128, n_layer=4, n_head=4, n_embd=128), 32,
+        128, "char-level GPT train step: 4 pre-LN layers, d_model 128, 4 heads, block 128, "
+             "vocab 65, batch 32; AdamW lr 3e-4 wd 1e-4, clip 1.0"),
+    "mha": MHAWorkload(),
+    "cnn": CNNWorkload(),
+    "lstm": RNNWorkload("lstm"),
+    "gru": RNNWorkload("gru"),
+}
+
+
+# ----------------------------------------------------------------------------- CPU legs
 def time_cpu(step, steps: int, budget_s: float) -> tuple[float, int]:
     """Median seconds per step over up to ``steps`` timed steps within ``budget_s``."""
     times: list[float] = []
@@ -98,37 +363,39 @@ def time_cpu(step, steps: int, budget_s: float) -> tuple[float, int]:
     return statistics.median(times), len(times)
 
 
-def cpu_baseline(budget_s: float = 30.0) -> dict:
+def cpu_measure(wl: Workload, steps: int, warmup: int, budget_s: float) -> tuple[float, int, str, int]:
+    from threadpoolctl import threadpool_limits
+
     threads = os.cpu_count() or 1
-    step, sample, _lim = cpu_reference_step_fn(threads)
-    step()  # allocator and BLAS warm-up
-    sec, n = time_cpu(step, 3, budget_s)
-    return {"value": SEQ / sec, "unit": "tokens/s", "cores": threads, "kind": "port",
+    with threadpool_limits(threads):
+        step, units, sample = wl.cpu_step(threads)
+        for _ in range(max(warmup, 1)):
+            step()  # allocator and BLAS warm-up
+        sec, n = time_cpu(step, steps, budget_s)
+    return units / sec, n, sample, threads
+
+
+def cpu_baseline(wl: Workload, budget_s: float = 30.0) -> dict:
+    value, n, sample, threads = cpu_measure(wl, 3, 1, budget_s)
+    return {"value": value, "unit": wl.unit, "cores": threads, "kind": "port",
             "sample": f"{sample}; median of {n} steps after 1 warm-up"}
 
 
-def run_reference(args: argparse.Namespace) -> None:
+def run_reference(args: argparse.Namespace, wl: Workload) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    threads = os.cpu_count() or 1
-    step, sample, _lim = cpu_reference_step_fn(threads)
-    t_warm = time.perf_counter()
-    for _ in range(max(min(args.warmup, 1), 0)):
-        step()
-    warm = time.perf_counter() - t_warm
-    sec, n = time_cpu(step, args.steps, budget_s=max(150.0 - warm, 10.0))
-    value = SEQ / sec
+    value, n, sample, threads = cpu_measure(wl, args.steps, min(args.warmup, 1), 150.0)
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "impl": "reference", "metric": wl.metric, "value": value, "unit": wl.unit,
         "n_gpus": args.gpus, "steps": n, "warmup": min(args.warmup, 1),
-        "ms_per_step": 1e3 * sec, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": SEQ,
-                   "parallelism": "host cores", "sample": sample},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+        "ms_per_step": 1e3 * wl.units_per_step / value, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": wl.description, **wl.config, "parallelism": "host cores",
+                   "sample": sample},
+        "cpu_baseline": {"value": value, "unit": wl.unit, "cores": threads, "kind": "port",
                          "sample": f"{sample}; median of {n} steps"},
-        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+        "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -168,8 +435,9 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- our arm
-def run_ours(args: argparse.Namespace) -> None:
-    import numpy as np
+def run_ours(args: argparse.Namespace, wl: Workload) -> None:
+    import ctypes
+
     import torch
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -190,30 +458,10 @@ def run_ours(args: argparse.Namespace) -> None:
     from tensorgrad_b200.distributed import GradientAllReduce, barrier, max_over_ranks
 
     tg.set_device(local)
-    tg.manual_seed(1234)
-    model = tg.nn.GPT(tg.nn.GPTConfig(**GPT2, dropout=0.0))
-    params = list(model.parameters())
-    opt = tg.optim.AdamW(params, lr=3e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=1e-4)
-    reducer = GradientAllReduce(params) if world > 1 else None
-
-    rng = np.random.default_rng(1000 + rank)
-    ids_np = rng.integers(0, GPT2["vocab_size"], size=(MICRO_BATCH, SEQ), dtype=np.int64)
-    tgt_np = rng.integers(0, GPT2["vocab_size"], size=(MICRO_BATCH, SEQ), dtype=np.int64)
-    ids_dev, tgt_dev = tg.Tensor(ids_np), tg.Tensor(tgt_np)
-    ids_pin = device.pinned_empty(ids_np.shape, np.int64)
-    tgt_pin = device.pinned_empty(tgt_np.shape, np.int64)
-    ids_pin[...] = ids_np
-    tgt_pin[...] = tgt_np
-
-    def step(ids, targets):
-        loss = tg.cross_entropy(model(ids), targets)
-        opt.zero_grad()
-        loss.backward()
-        if reducer is not None:
-            reducer.reduce()
-        tg.optim.clip_grad_norm_(params, 1.0)
-        opt.step()
-        return loss
+    # The attention op alone has no parameters: N GPUs run N replicas.
+    reducer_cls = GradientAllReduce if world > 1 and wl.name != "mha" else None
+    built = wl.build(tg, device, rank, reducer_cls)
+    results: list = []
 
     def timed(k: int, fn) -> float:
         barrier()
@@ -229,39 +477,36 @@ def run_ours(args: argparse.Namespace) -> None:
 
     # Device-resident inputs: the value line.
     for _ in range(args.warmup):
-        step(ids_dev, tgt_dev)
+        built.step(*built.dev_inputs)
     phys = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
     gpu_index = int(phys[local]) if len(phys) > local and phys[local].strip().isdigit() else local
     clocks = ClockSampler(gpu_index)
     launches0 = int(lib.tg_launch_count())
     lib.tg_gemm_profile(1)
-    sec = timed(args.steps, lambda: step(ids_dev, tgt_dev))
+    sec = timed(args.steps, lambda: built.step(*built.dev_inputs))
     lib.tg_gemm_profile(0)
     launches = int(lib.tg_launch_count()) - launches0
     clock = clocks.stop()
-    import ctypes
-
     gms, gl, gfl = ctypes.c_double(), ctypes.c_int64(), ctypes.c_double()
     lib.tg_gemm_profile_read(ctypes.byref(gms), ctypes.byref(gl), ctypes.byref(gfl))
 
-    # End to end: pinned host ids/targets uploaded inside the step, loss read back.
-    losses = []
-
+    # End to end: pinned host inputs uploaded inside the step, the result read back.
     def e2e_step():
-        losses.append(step(ids_pin, tgt_pin).item())
+        results.append(built.readback(built.step(*built.pinned_inputs)))
 
     for _ in range(args.warmup):
         e2e_step()
     sec_e2e = timed(args.steps, e2e_step)
 
-    tokens = MICRO_BATCH * SEQ * world
+    units = wl.units_per_step * world
     pk = peaks()
     achieved = gfl.value / (gms.value / 1e3) / 1e12 if gms.value > 0 else 0.0
     peak = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")))
+    last = results[-1] if results and not isinstance(results[-1], list) else None
     out = {
-        "metric": METRIC,
-        "value": tokens * args.steps / sec,
-        "unit": "tokens/s",
+        "metric": wl.metric,
+        "value": units * args.steps / sec,
+        "unit": wl.unit,
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
@@ -270,11 +515,14 @@ def run_ours(args: argparse.Namespace) -> None:
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "f32",
-        "data": "synthetic token ids (uniform, seeded); GPT-2 init from the seeded host RNG",
-        "config": {"workload": WORKLOAD, "global_batch": MICRO_BATCH * world, "seq_len": SEQ,
-                   "parallelism": f"dp{world}",
+        "data": "synthetic seeded inputs of the configuration's shapes; seeded weights",
+        "config": {"workload": wl.description, **wl.config,
+                   "parallelism": (f"dp{world}" if reducer_cls or world == 1 else
+                                   f"{world} replicas"),
                    "matmul": "tcgen05 kind::tf32 with a 3xTF32 split (fp32-level accuracy)",
-                   "l2": "no flush: every step streams several GB of activations, >> 126 MB L2"},
+                   "l2": "no flush: every step streams its activations and parameters; the "
+                         "GEMM operands of the timed steps exceed the 126 MB L2 except for the "
+                         "small configurations, whose timings include L2 reuse"},
         "roofline": {
             "kernel": "tensor-core GEMM (gemm_tc_kernel, 3xTF32)",
             "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
@@ -283,18 +531,17 @@ def run_ours(args: argparse.Namespace) -> None:
             "launches": gl.value, "device_ms_per_step": gms.value / args.steps,
             "tf32_ceiling_frac": achieved / (peak / 2) if peak else None,
             "tf32x3_ceiling_frac": achieved / (peak / 6) if peak else None,
+            "step_tflops": wl.flops() * world / (sec / args.steps) / 1e12,
         },
         "clocks": clock,
-        "e2e": {"value": tokens * args.steps / sec_e2e, "unit": "tokens/s",
-                "h2d_bytes_per_step": int(ids_np.nbytes + tgt_np.nbytes),
-                "d2h_bytes_per_step": 4 + 8},
+        "e2e": {"value": units * args.steps / sec_e2e, "unit": wl.unit,
+                "h2d_bytes_per_step": int(built.h2d_bytes),
+                "d2h_bytes_per_step": int(built.d2h_bytes)},
         "gpu_launches": launches,
-        "final_loss": losses[-1] if losses else None,
+        "final_loss": last,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_baseline()
-    if reducer is not None:
-        reducer.close()
+        out["cpu_baseline"] = cpu_baseline(wl)
     if rank == 0:
         print(json.dumps(out), flush=True)
     if world > 1:
@@ -305,10 +552,11 @@ def run_ours(args: argparse.Namespace) -> None:
 
 def main() -> None:
     args = parse()
+    wl = WORKLOADS[args.workload]
     if args.impl == "reference":
-        run_reference(args)
+        run_reference(args, wl)
     else:
-        run_ours(args)
+        run_ours(args, wl)
 
 
 if __name__ == "__main__":

@@ -159,7 +159,7 @@ int bgemm(int ta, int tb, int64_t m, int64_t n, int64_t k, float alpha, const fl
   p.trans_a = ta; p.trans_b = tb; p.batch = batch; p.kmode = kmode;
   // attention_tc_supported() guarantees the tensor-core path's alignment rules; the causal
   // k-ranges are only meaningful there, so a refusal is an error, not a fallback.
-  return gemm_tc_f32(p, s);
+  return gemm_tc_profiled(p, s);
 }
 
 }  // namespace

@@ -70,6 +70,45 @@ cudaEvent_t take_event() {
 // Process-wide matmul precision of the fp32 tensor-core path (tg_set_matmul_precision).
 int g_precision = 0;
 
+// sum_{i < m} min(cap, i + 1): the entries of a causal (lower-triangular) band.
+double tri_count(double m, double cap) {
+  if (m <= cap) return m * (m + 1) / 2;
+  return cap * (cap + 1) / 2 + (m - cap) * cap;
+}
+
+// Algorithmic FLOPs of one product: 2mnk per batch entry, counting only the causal half
+// of the attention products (scores i >= j; reductions over k <= i or k >= i).
+template <typename T>
+double algorithmic_flops(const GemmArgs<T>& p) {
+  const double m = (double)p.m, n = (double)p.n, k = (double)p.k, b = (double)p.batch;
+  switch (p.kmode) {
+    case GEMM_K_SKIP_UPPER: return 2.0 * b * k * tri_count(m, n);
+    case GEMM_K_UP_TO_ROW: return 2.0 * b * n * tri_count(m, k);
+    case GEMM_K_FROM_ROW: return 2.0 * b * n * (m * k - tri_count(m, k) + (m < k ? m : k));
+    default: return 2.0 * b * m * n * k;
+  }
+}
+
+// The tensor-core kernel, bracketed by profiling events when profiling is on.
+int tc_timed(const GemmArgs<float>& p, cudaStream_t s) {
+  ProfileRec rec{};
+  if (g_prof_on) {
+    rec = {take_event(), take_event(), algorithmic_flops(p)};
+    cudaEventRecord(rec.start, s);
+  }
+  const int rc = gemm_tc_f32(p, s);
+  if (g_prof_on) {
+    if (rc == TG_OK) {
+      cudaEventRecord(rec.stop, s);
+      g_prof.push_back(rec);
+    } else {
+      g_event_pool.push_back(rec.start);
+      g_event_pool.push_back(rec.stop);
+    }
+  }
+  return rc;
+}
+
 template <typename T>
 int gemm_dispatch(GemmArgs<T> p, bool allow_tc, cudaStream_t s) {
   if (p.m == 0 || p.n == 0) return TG_OK;
@@ -80,21 +119,7 @@ int gemm_dispatch(GemmArgs<T> p, bool allow_tc, cudaStream_t s) {
   }
   if constexpr (sizeof(T) == 4) {
     if (allow_tc && !force_simt()) {
-      ProfileRec rec{};
-      if (g_prof_on) {
-        rec = {take_event(), take_event(), 2.0 * (double)p.m * (double)p.n * (double)p.k};
-        cudaEventRecord(rec.start, s);
-      }
-      const int rc = gemm_tc_f32(p, s);
-      if (g_prof_on) {
-        if (rc == TG_OK) {
-          cudaEventRecord(rec.stop, s);
-          g_prof.push_back(rec);
-        } else {
-          g_event_pool.push_back(rec.start);
-          g_event_pool.push_back(rec.stop);
-        }
-      }
+      const int rc = tc_timed(p, s);
       if (rc != TG_ERR_UNSUPPORTED) return rc;
     }
   }
@@ -102,6 +127,10 @@ int gemm_dispatch(GemmArgs<T> p, bool allow_tc, cudaStream_t s) {
 }
 
 }  // namespace
+
+int gemm_tc_profiled(const GemmArgs<float>& p, cudaStream_t stream) {
+  return tc_timed(p, stream);
+}
 
 template <typename T>
 int gemm_run(const GemmArgs<T>& p, cudaStream_t stream) {

@@ -58,6 +58,9 @@ int gemm_simt(const GemmArgs<T>& p, cudaStream_t stream);
 template <typename T>
 int gemm_run(const GemmArgs<T>& p, cudaStream_t stream);
 
+// The tensor-core kernel alone (no SIMT fallback), live-profiled like gemm_run.
+int gemm_tc_profiled(const GemmArgs<float>& p, cudaStream_t stream);
+
 // tcgen05 3xTF32 path. Returns TG_ERR_UNSUPPORTED (without launching) when the operands'
 // strides or base addresses do not meet the TMA's 16-byte rules, so the caller can fall back.
 int gemm_tc_f32(const GemmArgs<float>& p, cudaStream_t stream);
