@@ -13,6 +13,8 @@
 // dimensions; dot products are finished with xor-shuffles inside the lane group.
 #include <stdlib.h>
 
+#include <initializer_list>
+
 #include "common.cuh"
 
 namespace tg {
@@ -370,6 +372,13 @@ bool use_tc(int dtype, const tg_attn_shape* s) {
   }
   return !forced && attention_tc_supported(dtype, s);
 }
+
+// The tensor maps also need 16-byte aligned base addresses (known only at the call).
+bool aligned(std::initializer_list<const void*> ptrs) {
+  for (const void* p : ptrs)
+    if (reinterpret_cast<uintptr_t>(p) & 15) return false;
+  return true;
+}
 }  // namespace
 
 extern "C" {
@@ -384,7 +393,7 @@ int tg_attention_forward(int dtype, const tg_attn_shape* s, const void* q, const
                "attention: bad shape");
   if (s->batch * s->heads * s->tq == 0) return TG_OK;
   cudaStream_t st = as_stream(stream);
-  if (use_tc(dtype, s)) {
+  if (use_tc(dtype, s) && aligned({q, k, v, o})) {
     TG_CHECK_ARG(scratch, "attention_forward: NULL scratch");
     return attention_tc_forward(s, (const float*)q, (const float*)k, (const float*)v, (float*)o,
                                 (float*)lse, scratch, st);
@@ -407,7 +416,7 @@ int tg_attention_backward(int dtype, const tg_attn_shape* s, const void* q, cons
   TG_CHECK_ARG(s && scratch, "attention_backward: NULL shape or scratch");
   if (s->batch * s->heads * (s->tq + s->tk) == 0) return TG_OK;
   cudaStream_t st = as_stream(stream);
-  if (use_tc(dtype, s))
+  if (use_tc(dtype, s) && aligned({q, k, v, o, dout, dq, dk, dv}))
     return attention_tc_backward(s, (const float*)q, (const float*)k, (const float*)v,
                                  (const float*)o, (const float*)lse, (const float*)dout,
                                  (float*)dq, (float*)dk, (float*)dv, scratch, st);

@@ -11,6 +11,7 @@ namespace tg {
 //   GEMM_K_SKIP_UPPER -- full reduction, but tiles whose first column n0 > m0 + 127 are
 //                        skipped (never written)
 enum GemmKMode { GEMM_K_FULL = 0, GEMM_K_UP_TO_ROW = 1, GEMM_K_FROM_ROW = 2, GEMM_K_SKIP_UPPER = 3 };
+enum GemmEpilogue { GEMM_EPI_STORE = 0, GEMM_EPI_SOFTMAX_DS = 1 };
 
 template <typename T>
 struct GemmArgs {
@@ -35,6 +36,19 @@ struct GemmArgs {
   //               is image * hw + pixel and the column a channel, written as NCHW (batch 1).
   int64_t a_fold = 0;
   int64_t c_hw = 0;
+  // Batch entries split as (outer, head) with bz = outer * heads + head; each operand is
+  // addressed at outer * stride_x + head * stride_xh (attention over (B, H, T, D) views with
+  // arbitrary strides, e.g. the packed QKV projection). heads == 1: plain batch strides.
+  int64_t heads = 1;
+  int64_t stride_ah = 0, stride_bh = 0, stride_ch = 0;
+  // Epilogue (tensor-core path): GEMM_EPI_STORE, or GEMM_EPI_SOFTMAX_DS for the attention
+  // backward: with the product dP, the scores S in `aux` (same layout as C), rv0 = lse and
+  // rv1 = delta per output row (index bz * m + row), it writes P = exp(S - lse) (zero above
+  // the diagonal when kmode is GEMM_K_SKIP_UPPER) over S and dS = P (dP - delta) alpha to C.
+  int epi = 0;
+  const T* rv0 = nullptr;
+  const T* rv1 = nullptr;
+  T* aux = nullptr;
   // Split-K partials (tensor-core path, batch 1): with a workspace of workspace_bytes the
   // reduction may be split over more CTAs, each writing an fp32 partial, summed in split
   // order by a second kernel (deterministic). nullptr: no split.
@@ -47,7 +61,7 @@ template <typename T>
 __host__ __device__ __forceinline__ int64_t gemm_c_offset(const GemmArgs<T>& p, int64_t bz,
                                                           int64_t m, int64_t n) {
   if (p.c_hw > 0) return (m / p.c_hw) * p.stride_c + n * p.ldc + (m % p.c_hw);
-  return bz * p.stride_c + m * p.ldc + n;
+  return (bz / p.heads) * p.stride_c + (bz % p.heads) * p.stride_ch + m * p.ldc + n;
 }
 
 template <typename T>

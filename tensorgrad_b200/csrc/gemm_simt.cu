@@ -16,8 +16,9 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(GemmArgs<T> p) {
   __shared__ T As[BK][BM + 4];
   __shared__ T Bs[BK][BN + 4];
   const int64_t bz = blockIdx.z;
-  const T* __restrict__ A = p.a + (p.a_fold > 0 ? 0 : bz * p.stride_a);
-  const T* __restrict__ B = p.b + bz * p.stride_b;
+  const int64_t bo = bz / p.heads, bh = bz % p.heads;
+  const T* __restrict__ A = p.a + (p.a_fold > 0 ? 0 : bo * p.stride_a + bh * p.stride_ah);
+  const T* __restrict__ B = p.b + bo * p.stride_b + bh * p.stride_bh;
   T* __restrict__ C = p.c;
   const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
   const int tid = threadIdx.x;

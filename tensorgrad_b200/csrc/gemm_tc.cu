@@ -102,13 +102,13 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// 3-D tiled load (x innermost, z = batch); no multicast.
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
-                                            int x, int y, int z) {
+// 4-D tiled load (x innermost, y rows, h head, b outer batch); no multicast.
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int x, int y, int h, int b) {
   asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(h), "r"(b)
       : "memory");
 }
 
@@ -198,6 +198,12 @@ struct TcArgs {
   int64_t c_hw;           // > 0: NCHW output (see GemmArgs::c_hw)
   int splits, kb_per_split;
   float* ws;              // splits > 1: partial sums, [splits][m][n]
+  int heads;              // batch entry bz = outer * heads + head
+  int64_t stride_ch;      // head stride of C
+  int epi;                // GemmEpilogue
+  const float* rv0;       // GEMM_EPI_SOFTMAX_DS: lse, delta per row; aux = scores in, P out
+  const float* rv1;
+  float* aux;
 };
 
 constexpr int kThreads = 512;
@@ -319,22 +325,27 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           uint8_t* b_raw = st + 2 * L::A_BYTES;
           mbar_arrive_expect_tx(&full[s], L::A_BYTES + L::B_BYTES);
           const int k0 = (ti.kb0 + j) * BK;
-          const int za = args.a_bcast ? 0 : ti.bz, zb = args.b_bcast ? 0 : ti.bz;
+          const int hh = ti.bz % args.heads, bo = ti.bz / args.heads;
+          const int ha = args.a_bcast ? 0 : hh, ba = args.a_bcast ? 0 : bo;
+          const int hb = args.b_bcast ? 0 : hh, bb = args.b_bcast ? 0 : bo;
           if (A_MN) {
 #pragma unroll
             for (int c = 0; c < BM / 32; ++c)
-              tma_load_3d(a_raw + c * 32 * BK * 4, &tmA, &full[s], (int)ti.m0 + 32 * c, k0, za);
+              tma_load_4d(a_raw + c * 32 * BK * 4, &tmA, &full[s], (int)ti.m0 + 32 * c, k0, ha,
+                          ba);
           } else if (args.a_fold > 0) {
-            tma_load_3d(a_raw, &tmA, &full[s], k0 % args.a_fold, (int)ti.m0, k0 / args.a_fold);
+            tma_load_4d(a_raw, &tmA, &full[s], k0 % args.a_fold, (int)ti.m0, 0,
+                        k0 / args.a_fold);
           } else {
-            tma_load_3d(a_raw, &tmA, &full[s], k0, (int)ti.m0, za);
+            tma_load_4d(a_raw, &tmA, &full[s], k0, (int)ti.m0, ha, ba);
           }
           if (B_MN) {
 #pragma unroll
             for (int c = 0; c < BN / 32; ++c)
-              tma_load_3d(b_raw + c * 32 * BK * 4, &tmB, &full[s], (int)ti.n0 + 32 * c, k0, zb);
+              tma_load_4d(b_raw + c * 32 * BK * 4, &tmB, &full[s], (int)ti.n0 + 32 * c, k0, hb,
+                          bb);
           } else {
-            tma_load_3d(b_raw, &tmB, &full[s], k0, (int)ti.n0, zb);
+            tma_load_4d(b_raw, &tmB, &full[s], k0, (int)ti.n0, hb, bb);
           }
         }
       }
@@ -425,6 +436,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int ew = warp - kEpiWarp0;  // == warp % 4: TMEM lanes 32*ew .. +31
     int tc = 0;
     const bool vec = args.c_hw == 0 && (args.ldc % 4 == 0) && (args.stride_c % 4 == 0) &&
+                     (args.stride_ch % 4 == 0) &&
                      ((reinterpret_cast<uintptr_t>(args.c) & 15) == 0) &&
                      (!args.bias || (reinterpret_cast<uintptr_t>(args.bias) & 15) == 0);
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
@@ -448,19 +460,74 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         crow = args.c + (row / args.c_hw) * args.stride_c + row % args.c_hw;
         cstep = args.ldc;
       } else {
-        crow = args.c + (int64_t)ti.bz * args.stride_c + row * args.ldc;
+        crow = args.c + (int64_t)(ti.bz / args.heads) * args.stride_c +
+               (int64_t)(ti.bz % args.heads) * args.stride_ch + row * args.ldc;
       }
       const float alpha = part ? 1.f : args.alpha, beta = part ? 0.f : args.beta;
       const float* bias = part ? nullptr : args.bias;
       const bool vrow = part ? (args.n % 4 == 0) : vec;
       const uint32_t acc = tmem + (uint32_t)(buf * BN) + ((uint32_t)(32 * ew) << 16);
+      // Attention backward: P = exp(S - lse) over S (in aux), dS = P (dP - delta) alpha to C.
+      const bool ds = args.epi == GEMM_EPI_SOFTMAX_DS && !part;
+      const bool causal = args.kmode == GEMM_K_SKIP_UPPER;
+      float* arow = ds ? args.aux + (crow - args.c) : nullptr;
+      float lse_r = 0.f, delta_r = 0.f;
+      if (ds && row < args.m) {
+        lse_r = args.rv0[(int64_t)ti.bz * args.m + row];
+        delta_r = args.rv1[(int64_t)ti.bz * args.m + row];
+      }
 #pragma unroll 1
       for (int cc = 0; cc < BN / 32; ++cc) {
         uint32_t r[32];
         tmem_ld32(acc + (uint32_t)(cc * 32), r);
         const int64_t c0 = ti.n0 + cc * 32;
-        if (row < args.m && c0 < args.n) {
+        if (ds && row < args.m && c0 < args.n) {
+          // All loads of the chunk first: the stores below may alias them for the compiler,
+          // which would otherwise serialise every load behind the previous store.
+          float sv[32];
+          const bool full = vrow && c0 + 32 <= args.n;
+          if (full) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              const float4 t = *reinterpret_cast<const float4*>(arow + c0 + j);
+              sv[j] = t.x; sv[j + 1] = t.y; sv[j + 2] = t.z; sv[j + 3] = t.w;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) sv[j] = c0 + j < args.n ? arow[c0 + j] : 0.f;
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float p = (causal && c0 + j > row) ? 0.f : expf(sv[j] - lse_r);
+            sv[j] = p;
+            r[j] = __float_as_uint(p * (__uint_as_float(r[j]) - delta_r) * alpha);
+          }
+          if (full) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              *reinterpret_cast<float4*>(arow + c0 + j) =
+                  make_float4(sv[j], sv[j + 1], sv[j + 2], sv[j + 3]);
+              *reinterpret_cast<float4*>(crow + c0 + j) =
+                  make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                              __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (c0 + j < args.n) {
+                arow[c0 + j] = sv[j];
+                crow[c0 + j] = __uint_as_float(r[j]);
+              }
+            }
+          }
+        } else if (row < args.m && c0 < args.n) {
           if (vrow && c0 + 32 <= args.n) {
+            float4 old[8];
+            if (beta != 0.f) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                old[j / 4] = *reinterpret_cast<const float4*>(crow + c0 + j);
+            }
 #pragma unroll
             for (int j = 0; j < 32; j += 4) {
               float4 v;
@@ -470,7 +537,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               v.w = ti.nk ? alpha * __uint_as_float(r[j + 3]) : 0.f;
               float4* dst = reinterpret_cast<float4*>(crow + c0 + j);
               if (beta != 0.f) {
-                const float4 o = *dst;
+                const float4 o = old[j / 4];
                 v.x += beta * o.x; v.y += beta * o.y;
                 v.z += beta * o.z; v.w += beta * o.w;
               }
@@ -526,18 +593,24 @@ static EncodeFn get_encode() {
   return fn;
 }
 
-// 3-D fp32 map: `batch` row-major matrices of `rows` x `inner` (row stride `ld`, batch
-// stride `bstride` elements); boxes of box_inner x box_rows x 1.
+// 4-D fp32 map: `nb` outer entries of `heads` row-major matrices of `rows` x `inner` (row
+// stride `ld`, head stride `hstride`, outer stride `bstride` elements); boxes of
+// box_inner x box_rows. Dimensions of extent 1 get a harmless stride (the encoder still
+// wants a multiple of 16 bytes).
 static int make_map(CUtensorMap* map, const float* ptr, int64_t inner, int64_t rows, int64_t ld,
-                    int64_t batch, int64_t bstride, uint32_t box_inner, uint32_t box_rows,
-                    CUtensorMapSwizzle swizzle) {
+                    int64_t heads, int64_t hstride, int64_t nb, int64_t bstride,
+                    uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
   EncodeFn enc = get_encode();
   if (!enc) return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)rows, (cuuint64_t)batch};
-  cuuint64_t strides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)(batch > 1 ? bstride : rows * ld) * 4};
-  cuuint32_t box[3] = {box_inner, box_rows, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(ptr), dims,
+  const int64_t hs = heads > 1 ? hstride : rows * ld;
+  const int64_t bs = nb > 1 ? bstride : (heads > 1 ? heads * hstride : rows * ld);
+  if (hs <= 0 || bs <= 0 || (hs % 4) || (bs % 4))
+    return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: head/batch strides not 16-byte multiples");
+  cuuint64_t dims[4] = {(cuuint64_t)inner, (cuuint64_t)rows, (cuuint64_t)heads, (cuuint64_t)nb};
+  cuuint64_t strides[3] = {(cuuint64_t)ld * 4, (cuuint64_t)hs * 4, (cuuint64_t)bs * 4};
+  cuuint32_t box[4] = {box_inner, box_rows, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(ptr), dims,
                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
@@ -583,15 +656,21 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
   // by every batch entry (stride 0) gets a map of depth 1; a folded A has depth k / a_fold.
   constexpr CUtensorMapSwizzle kSwK = CU_TENSOR_MAP_SWIZZLE_64B;
   constexpr CUtensorMapSwizzle kSwMN = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
-  const bool a_bcast = p.batch > 1 && p.stride_a == 0, b_bcast = p.batch > 1 && p.stride_b == 0;
-  const int64_t a_depth = a_bcast ? 1 : p.batch, b_depth = b_bcast ? 1 : p.batch;
-  if (A_MN) rc = make_map(&ta, p.a, p.m, p.k, p.lda, a_depth, p.stride_a, 32, BK, kSwMN);
+  const bool a_bcast = p.batch > 1 && p.stride_a == 0 && p.stride_ah == 0;
+  const bool b_bcast = p.batch > 1 && p.stride_b == 0 && p.stride_bh == 0;
+  const int64_t nb = p.batch / p.heads;
+  const int64_t ah = a_bcast ? 1 : p.heads, an = a_bcast ? 1 : nb;
+  const int64_t bh = b_bcast ? 1 : p.heads, bn = b_bcast ? 1 : nb;
+  if (A_MN)
+    rc = make_map(&ta, p.a, p.m, p.k, p.lda, ah, p.stride_ah, an, p.stride_a, 32, BK, kSwMN);
   else if (p.a_fold > 0)
-    rc = make_map(&ta, p.a, p.a_fold, p.m, p.lda, p.k / p.a_fold, p.stride_a, BK, BM, kSwK);
-  else rc = make_map(&ta, p.a, p.k, p.m, p.lda, a_depth, p.stride_a, BK, BM, kSwK);
+    rc = make_map(&ta, p.a, p.a_fold, p.m, p.lda, 1, 0, p.k / p.a_fold, p.stride_a, BK, BM,
+                  kSwK);
+  else rc = make_map(&ta, p.a, p.k, p.m, p.lda, ah, p.stride_ah, an, p.stride_a, BK, BM, kSwK);
   if (rc != TG_OK) return rc;
-  if (B_MN) rc = make_map(&tb, p.b, p.n, p.k, p.ldb, b_depth, p.stride_b, 32, BK, kSwMN);
-  else rc = make_map(&tb, p.b, p.k, p.n, p.ldb, b_depth, p.stride_b, BK, BN, kSwK);
+  if (B_MN)
+    rc = make_map(&tb, p.b, p.n, p.k, p.ldb, bh, p.stride_bh, bn, p.stride_b, 32, BK, kSwMN);
+  else rc = make_map(&tb, p.b, p.k, p.n, p.ldb, bh, p.stride_bh, bn, p.stride_b, BK, BN, kSwK);
   if (rc != TG_OK) return rc;
   const size_t smem = STAGES * L::STAGE + 1024 + 256;
   static bool configured = false;
@@ -611,6 +690,12 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
   a.a_fold = (int)p.a_fold;
   a.a_bcast = a_bcast; a.b_bcast = b_bcast;
   a.c_hw = p.c_hw;
+  a.heads = (int)p.heads;
+  a.stride_ch = p.stride_ch;
+  a.epi = p.epi;
+  a.rv0 = p.rv0;
+  a.rv1 = p.rv1;
+  a.aux = p.aux;
   const int nk_all = (int)((p.k + BK - 1) / BK);
   a.splits = 1;
   a.kb_per_split = nk_all;
@@ -649,8 +734,12 @@ int gemm_tc_f32(const GemmArgs<float>& p, cudaStream_t stream) {
     return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: batch/empty shape");
   if (!aligned16(p.a) || !aligned16(p.b) || (p.lda % 4) || (p.ldb % 4))
     return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: operands not 16-byte aligned");
-  if (p.batch > 1 && ((p.stride_a % 4) || (p.stride_b % 4)))
+  if (p.batch > 1 && ((p.stride_a % 4) || (p.stride_b % 4) || (p.stride_ah % 4) ||
+                      (p.stride_bh % 4)))
     return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: batch strides not 16-byte aligned");
+  if (p.heads < 1 || p.batch % p.heads)
+    return set_error(TG_ERR_ARG, "gemm_tc: batch %lld is not a multiple of heads %lld",
+                     (long long)p.batch, (long long)p.heads);
   if (p.m > INT32_MAX / 2 || p.n > INT32_MAX / 2 || p.k > INT32_MAX / 2)
     return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: dimension beyond int32");
   if (p.a_fold > 0 && (p.trans_a || p.batch != 1 || p.a_fold % tc::BK || p.k % p.a_fold ||
