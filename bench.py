@@ -55,7 +55,42 @@ def parse() -> argparse.Namespace:
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="gpt2")
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
+    p.add_argument("--gemm", metavar="M,N,K,TA,TB",
+                   help="time one fp32 tg_gemm of this shape instead of a training step "
+                        "(a kernel probe: C = op(A) op(B), TA/TB = 1 for transposed storage)")
     return p.parse_args()
+
+
+def run_gemm(args: argparse.Namespace) -> None:
+    """Time ``tg_gemm`` alone on one shape (device-resident N(0,1) operands, CUDA events)."""
+    import numpy as np
+    import torch
+
+    from tensorgrad_b200 import device
+    from tensorgrad_b200._lib import check, lib
+
+    m, n, k, ta, tb = (int(v) for v in args.gemm.split(","))
+    rng = np.random.default_rng(0)
+    a = device.from_numpy(rng.standard_normal((k, m) if ta else (m, k)).astype(np.float32))
+    b = device.from_numpy(rng.standard_normal((n, k) if tb else (k, n)).astype(np.float32))
+    c = device.empty((m, n), np.float32)
+
+    def call() -> None:
+        check(lib.tg_gemm(0, ta, tb, m, n, k, 1.0, a.ptr, m if ta else k, b.ptr,
+                          k if tb else n, 0.0, c.ptr, n, None, device.stream()), "gemm")
+
+    for _ in range(args.warmup):
+        call()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        call()
+    stop.record()
+    stop.synchronize()
+    ms = start.elapsed_time(stop) / max(args.steps, 1)
+    print(json.dumps({"metric": "fp32 GEMM TFLOP/s (3xTF32)", "value": 2.0 * m * n * k / ms / 1e9,
+                      "unit": "TFLOP/s", "ms_per_call": ms, "shape": [m, n, k, ta, tb],
+                      "steps": args.steps, "warmup": args.warmup}), flush=True)
 
 
 def peaks() -> dict:
@@ -552,6 +587,9 @@ def run_ours(args: argparse.Namespace, wl: Workload) -> None:
 
 def main() -> None:
     args = parse()
+    if args.gemm:
+        run_gemm(args)
+        return
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
         run_reference(args, wl)
