@@ -30,6 +30,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <stdlib.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -102,6 +104,66 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// ---- CTA-pair (cluster of 2) helpers for the cta_group::2 variant
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+
+// The same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
+  return out;
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+// Arrival on a barrier of another CTA of the cluster with the default semantics (release
+// at CTA scope): enough for hand-offs that tcgen05 fences order, e.g. an accumulator
+// released after tcgen05.ld.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait with cluster-scope acquire (for barriers that the peer CTA arrives on).
+__device__ __forceinline__ bool wait_bar_cluster(uint64_t* bar, uint32_t parity,
+                                                 volatile int* abort_flag,
+                                                 bool respect_abort = true) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (respect_abort && *abort_flag) return false;
+    if (clock64() - t0 > kTimeoutCycles) {
+      *abort_flag = 1;
+      atomicExch(&g_status, (int)TG_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // 4-D tiled load (x innermost, y rows, h head, b outer batch); no multicast.
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int x, int y, int h, int b) {
@@ -122,6 +184,50 @@ __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
 
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// Pair allocation: the same warp of both CTAs of the pair executes it.
+__device__ __forceinline__ void tmem_alloc2(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(slot)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// 256-row MMA across the CTA pair: A rows 0..127 and B columns 0..N/2-1 come from the
+// issuing (even) CTA's shared memory, A rows 128..255 and B columns N/2..N-1 from the same
+// offsets in the odd CTA; each CTA's TMEM receives its 128 rows.
+__device__ __forceinline__ void mma_tf32_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on the barrier at this offset in both CTAs of the pair once the pair's MMAs issued
+// so far have completed.
+__device__ __forceinline__ void mma_commit_pair_both(uint64_t* bar) {
+  const uint16_t mask = 0x3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(mask)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit_pair_local(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
                : "memory");
 }
 
@@ -210,17 +316,20 @@ constexpr int kThreads = 512;
 constexpr int kSplitWarp0 = 4, kSplitThreads = 256;  // warps 4..11
 constexpr int kEpiWarp0 = 12;                        // warps 12..15
 
-template <int BN>
+// PAIR: a CTA of a cta_group::2 pair holds its 128 rows of A and half of the BN columns of B.
+template <int BN, bool PAIR = false>
 struct Layout {
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
   static constexpr uint32_t A_BYTES = BM * BK * 4;  // 8 KB
-  static constexpr uint32_t B_BYTES = BN * BK * 4;
+  static constexpr uint32_t B_BYTES = B_ROWS * BK * 4;
   static constexpr uint32_t STAGE = 2 * A_BYTES + 2 * B_BYTES;  // raw + lo of A and B
   static constexpr uint32_t TMEM_COLS = 2 * BN;                 // two accumulators
 };
 
-template <int BN>
+template <int BN, bool PAIR = false>
 constexpr int stages_for() {
-  return (200 * 1024) / Layout<BN>::STAGE > 8 ? 8 : (200 * 1024) / Layout<BN>::STAGE;
+  constexpr uint32_t s = Layout<BN, PAIR>::STAGE;
+  return (200 * 1024) / s > 8 ? 8 : (200 * 1024) / s;
 }
 
 // Descriptor of k-step kk (8 tf32 along K) of a stage tile.
@@ -242,7 +351,7 @@ struct TileInfo {
   bool skip;
 };
 
-__device__ __forceinline__ TileInfo tile_info(const TcArgs& a, int t, int bn) {
+__device__ __forceinline__ TileInfo tile_info(const TcArgs& a, int t, int bn, int bm = BM) {
   TileInfo ti;
   const int mt = t % a.m_tiles;
   int rest = t / a.m_tiles;
@@ -250,7 +359,7 @@ __device__ __forceinline__ TileInfo tile_info(const TcArgs& a, int t, int bn) {
   rest /= a.n_tiles;
   ti.bz = rest % a.batch;
   ti.split = rest / a.batch;
-  ti.m0 = (int64_t)mt * BM;
+  ti.m0 = (int64_t)mt * bm;
   ti.n0 = (int64_t)nt * bn;
   // Causal attention products: a tile strictly above the diagonal is skipped outright, and
   // reductions over a triangular operand stop at / start from the tile's first output row.
@@ -271,11 +380,17 @@ __device__ __forceinline__ TileInfo tile_info(const TcArgs& a, int t, int bn) {
   return ti;
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN>
+// PAIR = true: launched in clusters of two CTAs; each pair computes 256 x BN tiles with
+// cta_group::2 MMAs issued by the even CTA (see mma_tf32_pair). Every role runs in both
+// CTAs on its own 128 rows and half of B, except the MMA issuer (even CTA only). The split
+// warps and the epilogue of the odd CTA arrive on the even CTA's barriers; the MMA commits
+// arrive on both CTAs' barriers.
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                TcArgs args) {
-  using L = Layout<BN>;
+  using L = Layout<BN, PAIR>;
+  constexpr int TILE_M = PAIR ? 2 * BM : BM;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -290,24 +405,34 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total = args.m_tiles * args.n_tiles * args.batch * args.splits;
+  // Work unit: a CTA, or a CTA pair (tile t goes to unit t % units).
+  const uint32_t rank = PAIR ? cluster_rank() : 0;
+  const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int64_t row_off = (int64_t)rank * BM;  // this CTA's rows within a pair tile
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&split[s], kSplitThreads);
+      // PAIR: one arrival per local split warp, plus (even CTA) the odd CTA's relay.
+      mbar_init(&split[s], PAIR ? (kSplitThreads / 32) + (rank == 0 ? 1 : 0) : kSplitThreads);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+      mbar_init(&acc_empty[b], PAIR ? 8 : 4);  // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, L::TMEM_COLS);
+  if (warp == 1) {
+    if (PAIR) tmem_alloc2(tmem_slot, L::TMEM_COLS);
+    else tmem_alloc(tmem_slot, L::TMEM_COLS);
+  }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrive
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -315,8 +440,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (lane == 0) {
       int it = 0;
       bool stop = false;
-      for (int t = blockIdx.x; t < total && !stop; t += gridDim.x) {
-        const TileInfo ti = tile_info(args, t, BN);
+      for (int t = unit; t < total && !stop; t += units) {
+        const TileInfo ti = tile_info(args, t, BN, TILE_M);
         for (int j = 0; j < ti.nk; ++j, ++it) {
           const int s = it % STAGES, round = it / STAGES;
           if (round > 0 && !wait_bar(&empty[s], (round - 1) & 1, abort_flag)) { stop = true; break; }
@@ -328,24 +453,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           const int hh = ti.bz % args.heads, bo = ti.bz / args.heads;
           const int ha = args.a_bcast ? 0 : hh, ba = args.a_bcast ? 0 : bo;
           const int hb = args.b_bcast ? 0 : hh, bb = args.b_bcast ? 0 : bo;
+          const int am0 = (int)(ti.m0 + row_off);
+          const int bn0 = (int)ti.n0 + (int)rank * L::B_ROWS;
           if (A_MN) {
 #pragma unroll
             for (int c = 0; c < BM / 32; ++c)
-              tma_load_4d(a_raw + c * 32 * BK * 4, &tmA, &full[s], (int)ti.m0 + 32 * c, k0, ha,
-                          ba);
+              tma_load_4d(a_raw + c * 32 * BK * 4, &tmA, &full[s], am0 + 32 * c, k0, ha, ba);
           } else if (args.a_fold > 0) {
-            tma_load_4d(a_raw, &tmA, &full[s], k0 % args.a_fold, (int)ti.m0, 0,
-                        k0 / args.a_fold);
+            tma_load_4d(a_raw, &tmA, &full[s], k0 % args.a_fold, am0, 0, k0 / args.a_fold);
           } else {
-            tma_load_4d(a_raw, &tmA, &full[s], k0, (int)ti.m0, ha, ba);
+            tma_load_4d(a_raw, &tmA, &full[s], k0, am0, ha, ba);
           }
           if (B_MN) {
 #pragma unroll
-            for (int c = 0; c < BN / 32; ++c)
-              tma_load_4d(b_raw + c * 32 * BK * 4, &tmB, &full[s], (int)ti.n0 + 32 * c, k0, hb,
-                          bb);
+            for (int c = 0; c < L::B_ROWS / 32; ++c)
+              tma_load_4d(b_raw + c * 32 * BK * 4, &tmB, &full[s], bn0 + 32 * c, k0, hb, bb);
           } else {
-            tma_load_4d(b_raw, &tmB, &full[s], k0, (int)ti.n0, hb, bb);
+            tma_load_4d(b_raw, &tmB, &full[s], k0, bn0, hb, bb);
           }
         }
       }
@@ -355,23 +479,49 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           if (j < 0) continue;
           wait_bar(&full[j % STAGES], (j / STAGES) & 1, abort_flag, false);
         }
+      } else {
+        // Tail: the MMA's last stage releases (tcgen05.commit arrivals on this CTA's empty
+        // barriers) land before the CTA may exit.
+        for (int j = it - STAGES; j < it; ++j) {
+          if (j < 0) continue;
+          wait_bar(&empty[j % STAGES], (j / STAGES) & 1, abort_flag);
+        }
+      }
+    }
+  } else if (PAIR && warp == 2) {
+    if (lane == 0 && rank == 1) {
+      // Relay: once this CTA's split warps finished stage s (local barrier), one
+      // cluster-scope release arrival tells the even CTA's MMA issuer.
+      int it = 0;
+      bool ok = true;
+      for (int t = unit; t < total && ok; t += units) {
+        const TileInfo ti = tile_info(args, t, BN, TILE_M);
+        for (int j = 0; j < ti.nk; ++j, ++it) {
+          const int s = it % STAGES, round = it / STAGES;
+          if (!wait_bar(&split[s], round & 1, abort_flag)) { ok = false; break; }
+          mbar_arrive_cluster(map_to_rank(&split[s], 0));
+        }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = instr_desc(BM, BN, A_MN, B_MN);
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = instr_desc(TILE_M, BN, A_MN, B_MN);
       int it = 0, tc = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        const TileInfo ti = tile_info(args, t, BN);
+      for (int t = unit; t < total && ok; t += units) {
+        const TileInfo ti = tile_info(args, t, BN, TILE_M);
         if (ti.skip) continue;
         const int buf = tc & 1;
-        if (tc >= 2 && !wait_bar(&acc_empty[buf], ((tc >> 1) - 1) & 1, abort_flag)) { ok = false; break; }
+        if (tc >= 2) {
+          const uint32_t par = ((tc >> 1) - 1) & 1;
+          if (!wait_bar(&acc_empty[buf], par, abort_flag)) { ok = false; break; }
+        }
         tc_fence_after();
         const uint32_t acc = tmem + (uint32_t)(buf * BN);
         for (int j = 0; j < ti.nk; ++j, ++it) {
           const int s = it % STAGES, round = it / STAGES;
-          if (!wait_bar(&split[s], round & 1, abort_flag)) { ok = false; break; }
+          if (!(PAIR ? wait_bar_cluster(&split[s], round & 1, abort_flag)
+                     : wait_bar(&split[s], round & 1, abort_flag))) { ok = false; break; }
           tc_fence_after();
           const uint32_t st = smem_u32(smem + s * L::STAGE);
           const uint32_t a_raw = st, a_lo = st + L::A_BYTES;
@@ -380,7 +530,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           for (int kk = 0; kk < BK / 8; ++kk) {
             const uint64_t ah = tile_desc<A_MN>(a_raw, kk), al = tile_desc<A_MN>(a_lo, kk);
             const uint64_t bh = tile_desc<B_MN>(b_raw, kk), bl = tile_desc<B_MN>(b_lo, kk);
-            if (args.raw) {
+            if (PAIR) {
+              if (args.raw) {
+                mma_tf32_pair(acc, ah, bh, idesc, (j | kk) != 0);
+              } else {
+                mma_tf32_pair(acc, al, bh, idesc, (j | kk) != 0);
+                mma_tf32_pair(acc, ah, bl, idesc, 1);
+                mma_tf32_pair(acc, ah, bh, idesc, 1);
+              }
+            } else if (args.raw) {
               mma_tf32(acc, ah, bh, idesc, (j | kk) != 0);
             } else {
               mma_tf32(acc, al, bh, idesc, (j | kk) != 0);
@@ -388,14 +546,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               mma_tf32(acc, ah, bh, idesc, 1);
             }
           }
-          mma_commit(&empty[s]);
+          if (PAIR) mma_commit_pair_both(&empty[s]);
+          else mma_commit(&empty[s]);
         }
         if (!ok) break;
-        mma_commit(&acc_full[buf]);  // with nk == 0 this fires at once; the epilogue uses 0
+        // with nk == 0 this fires at once; the epilogue uses 0
+        if (PAIR) mma_commit_pair_both(&acc_full[buf]);
+        else mma_commit(&acc_full[buf]);
         ++tc;
       }
       if (!ok) {
-        mma_commit(drain);
+        if (PAIR) mma_commit_pair_local(drain);
+        else mma_commit(drain);
         wait_bar(drain, 0, abort_flag, false);  // MMAs already issued finish before dealloc
       }
     }
@@ -403,11 +565,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int t0 = threadIdx.x - kSplitWarp0 * 32;
     int it = 0;
     bool stop = false;
-    for (int t = blockIdx.x; t < total && !stop; t += gridDim.x) {
-      const TileInfo ti = tile_info(args, t, BN);
+    for (int t = unit; t < total && !stop; t += units) {
+      const TileInfo ti = tile_info(args, t, BN, TILE_M);
       for (int j = 0; j < ti.nk; ++j, ++it) {
         const int s = it % STAGES, round = it / STAGES;
-        if (!wait_bar(&full[s], round & 1, abort_flag)) { stop = true; break; }
+        // Warp-uniform decision: the warp stays converged for the arrival below.
+        const bool landed = wait_bar(&full[s], round & 1, abort_flag);
+        if (!__all_sync(0xffffffffu, landed)) { stop = true; break; }
         if (!args.raw) {
           uint8_t* st = smem + s * L::STAGE;
           const float4* a_raw = reinterpret_cast<const float4*>(st);
@@ -429,7 +593,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           for (int i = t0; i < (int)(L::B_BYTES / 16); i += kSplitThreads) lo4(b_raw, b_lo, i);
         }
         fence_proxy_async_smem();
-        mbar_arrive(&split[s]);
+        if (PAIR) {
+          // One local arrival per warp after all lanes fenced; the odd CTA's relay thread
+          // forwards its stage to the even CTA.
+          __syncwarp();
+          if ((threadIdx.x & 31) == 0) mbar_arrive(&split[s]);
+        } else {
+          mbar_arrive(&split[s]);
+        }
       }
     }
   } else if (warp >= kEpiWarp0) {
@@ -439,15 +610,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                      (args.stride_ch % 4 == 0) &&
                      ((reinterpret_cast<uintptr_t>(args.c) & 15) == 0) &&
                      (!args.bias || (reinterpret_cast<uintptr_t>(args.bias) & 15) == 0);
-    for (int t = blockIdx.x; t < total; t += gridDim.x) {
-      const TileInfo ti = tile_info(args, t, BN);
+    for (int t = unit; t < total; t += units) {
+      const TileInfo ti = tile_info(args, t, BN, TILE_M);
       if (ti.skip) continue;
       const int buf = tc & 1;
       // tcgen05.ld is warp-collective: decide per warp.
       const bool have = __all_sync(0xffffffffu, wait_bar(&acc_full[buf], (tc >> 1) & 1, abort_flag));
       if (!have) break;
       tc_fence_after();
-      const int64_t row = ti.m0 + 32 * ew + lane;
+      const int64_t row = ti.m0 + row_off + 32 * ew + lane;
       // Partial sums of a split reduction go to the workspace unscaled (the reduce kernel
       // applies alpha, beta and the bias). NCHW output: lanes are consecutive pixels, so the
       // 32 stores of one column are one coalesced line.
@@ -482,70 +653,76 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         tmem_ld32(acc + (uint32_t)(cc * 32), r);
         const int64_t c0 = ti.n0 + cc * 32;
         if (ds && row < args.m && c0 < args.n) {
-          // All loads of the chunk first: the stores below may alias them for the compiler,
-          // which would otherwise serialise every load behind the previous store.
-          float sv[32];
+          // Loads of each 16-column half first: the stores below may alias them for the
+          // compiler, which would otherwise serialise every load behind the previous store.
           const bool full = vrow && c0 + 32 <= args.n;
-          if (full) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              const float4 t = *reinterpret_cast<const float4*>(arow + c0 + j);
-              sv[j] = t.x; sv[j + 1] = t.y; sv[j + 2] = t.z; sv[j + 3] = t.w;
+          for (int h = 0; h < 32; h += 16) {
+            float sv[16];
+            if (full) {
+#pragma unroll
+              for (int j = 0; j < 16; j += 4) {
+                const float4 t = *reinterpret_cast<const float4*>(arow + c0 + h + j);
+                sv[j] = t.x; sv[j + 1] = t.y; sv[j + 2] = t.z; sv[j + 3] = t.w;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) sv[j] = c0 + h + j < args.n ? arow[c0 + h + j] : 0.f;
             }
-          } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) sv[j] = c0 + j < args.n ? arow[c0 + j] : 0.f;
-          }
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float p = (causal && c0 + j > row) ? 0.f : expf(sv[j] - lse_r);
-            sv[j] = p;
-            r[j] = __float_as_uint(p * (__uint_as_float(r[j]) - delta_r) * alpha);
-          }
-          if (full) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              *reinterpret_cast<float4*>(arow + c0 + j) =
-                  make_float4(sv[j], sv[j + 1], sv[j + 2], sv[j + 3]);
-              *reinterpret_cast<float4*>(crow + c0 + j) =
-                  make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                              __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+            for (int j = 0; j < 16; ++j) {
+              const float p = (causal && c0 + h + j > row) ? 0.f : expf(sv[j] - lse_r);
+              sv[j] = p;
+              r[h + j] = __float_as_uint(p * (__uint_as_float(r[h + j]) - delta_r) * alpha);
             }
-          } else {
+            if (full) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (c0 + j < args.n) {
-                arow[c0 + j] = sv[j];
-                crow[c0 + j] = __uint_as_float(r[j]);
+              for (int j = 0; j < 16; j += 4) {
+                *reinterpret_cast<float4*>(arow + c0 + h + j) =
+                    make_float4(sv[j], sv[j + 1], sv[j + 2], sv[j + 3]);
+                *reinterpret_cast<float4*>(crow + c0 + h + j) =
+                    make_float4(__uint_as_float(r[h + j]), __uint_as_float(r[h + j + 1]),
+                                __uint_as_float(r[h + j + 2]), __uint_as_float(r[h + j + 3]));
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                if (c0 + h + j < args.n) {
+                  arow[c0 + h + j] = sv[j];
+                  crow[c0 + h + j] = __uint_as_float(r[h + j]);
+                }
               }
             }
           }
         } else if (row < args.m && c0 < args.n) {
           if (vrow && c0 + 32 <= args.n) {
-            float4 old[8];
-            if (beta != 0.f) {
 #pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                old[j / 4] = *reinterpret_cast<const float4*>(crow + c0 + j);
-            }
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              float4 v;
-              v.x = ti.nk ? alpha * __uint_as_float(r[j + 0]) : 0.f;
-              v.y = ti.nk ? alpha * __uint_as_float(r[j + 1]) : 0.f;
-              v.z = ti.nk ? alpha * __uint_as_float(r[j + 2]) : 0.f;
-              v.w = ti.nk ? alpha * __uint_as_float(r[j + 3]) : 0.f;
-              float4* dst = reinterpret_cast<float4*>(crow + c0 + j);
+            for (int h = 0; h < 32; h += 16) {
+              float4 old[4];
               if (beta != 0.f) {
-                const float4 o = old[j / 4];
-                v.x += beta * o.x; v.y += beta * o.y;
-                v.z += beta * o.z; v.w += beta * o.w;
+#pragma unroll
+                for (int j = 0; j < 16; j += 4)
+                  old[j / 4] = *reinterpret_cast<const float4*>(crow + c0 + h + j);
               }
-              if (bias) {
-                const float4 bb = *reinterpret_cast<const float4*>(bias + c0 + j);
-                v.x += bb.x; v.y += bb.y; v.z += bb.z; v.w += bb.w;
+#pragma unroll
+              for (int j = 0; j < 16; j += 4) {
+                float4 v;
+                v.x = ti.nk ? alpha * __uint_as_float(r[h + j + 0]) : 0.f;
+                v.y = ti.nk ? alpha * __uint_as_float(r[h + j + 1]) : 0.f;
+                v.z = ti.nk ? alpha * __uint_as_float(r[h + j + 2]) : 0.f;
+                v.w = ti.nk ? alpha * __uint_as_float(r[h + j + 3]) : 0.f;
+                float4* dst = reinterpret_cast<float4*>(crow + c0 + h + j);
+                if (beta != 0.f) {
+                  const float4 o = old[j / 4];
+                  v.x += beta * o.x; v.y += beta * o.y;
+                  v.z += beta * o.z; v.w += beta * o.w;
+                }
+                if (bias) {
+                  const float4 bb = *reinterpret_cast<const float4*>(bias + c0 + h + j);
+                  v.x += bb.x; v.y += bb.y; v.z += bb.z; v.w += bb.w;
+                }
+                *dst = v;
               }
-              *dst = v;
             }
           } else {
 #pragma unroll
@@ -564,15 +741,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      if (lane == 0) {
+        if (PAIR) mbar_arrive_remote(map_to_rank(&acc_empty[buf], 0));
+        else mbar_arrive(&acc_empty[buf]);
+      }
       ++tc;
     }
   }
   tc_fence_before();
   __syncthreads();
+  // PAIR: neither CTA leaves (or frees TMEM) while the pair's MMAs may still read its shared
+  // memory or write its TMEM.
+  if (PAIR) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, L::TMEM_COLS);
+    if (PAIR) tmem_dealloc2(tmem, L::TMEM_COLS);
+    else tmem_dealloc(tmem, L::TMEM_COLS);
   }
 }
 
@@ -646,10 +830,12 @@ splitk_reduce_kernel(const float* __restrict__ ws, int splits, GemmArgs<float> p
   }
 }
 
-template <int BN, bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN, bool PAIR>
 static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
-  using L = Layout<BN>;
-  constexpr int STAGES = stages_for<BN>();
+  using L = Layout<BN, PAIR>;
+  constexpr int STAGES = stages_for<BN, PAIR>();
+  constexpr int TILE_M = PAIR ? 2 * BM : BM;
+  auto kernel = gemm_tc_kernel<BN, STAGES, A_MN, B_MN, PAIR>;
   CUtensorMap ta, tb;
   int rc;
   // A: K-major = m rows of k; MN-major = k rows of m. Likewise B with n. An operand shared
@@ -670,13 +856,35 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
   if (rc != TG_OK) return rc;
   if (B_MN)
     rc = make_map(&tb, p.b, p.n, p.k, p.ldb, bh, p.stride_bh, bn, p.stride_b, 32, BK, kSwMN);
-  else rc = make_map(&tb, p.b, p.k, p.n, p.ldb, bh, p.stride_bh, bn, p.stride_b, BK, BN, kSwK);
+  else
+    rc = make_map(&tb, p.b, p.k, p.n, p.ldb, bh, p.stride_bh, bn, p.stride_b, BK, L::B_ROWS,
+                  kSwK);
   if (rc != TG_OK) return rc;
   const size_t smem = STAGES * L::STAGE + 1024 + 256;
   static bool configured = false;
+  static int max_pairs = 0;
   if (!configured) {
-    TG_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES, A_MN, B_MN>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    TG_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem));
+    if (PAIR) {
+      cudaLaunchConfig_t q = {};
+      q.gridDim = dim3(2 * (sm_count() / 2));
+      q.blockDim = dim3(kThreads);
+      q.dynamicSmemBytes = smem;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = 2;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      q.attrs = at;
+      q.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kernel, &q) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = sm_count() / 2;
+      }
+      max_pairs = n;
+    }
     configured = true;
   }
   TcArgs a{};
@@ -684,7 +892,7 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
   a.c = p.c; a.ldc = p.ldc; a.stride_c = p.stride_c; a.bias = p.bias;
   a.alpha = p.alpha; a.beta = p.beta;
   a.kmode = p.kmode; a.raw = p.precision;
-  a.m_tiles = (int)((p.m + BM - 1) / BM);
+  a.m_tiles = (int)((p.m + TILE_M - 1) / TILE_M);
   a.n_tiles = (int)((p.n + BN - 1) / BN);
   a.batch = (int)p.batch;
   a.a_fold = (int)p.a_fold;
@@ -705,24 +913,54 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
     a.ws = p.workspace;
   }
   const int64_t tiles = (int64_t)a.m_tiles * a.n_tiles * a.batch * a.splits;
-  const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
-  gemm_tc_kernel<BN, STAGES, A_MN, B_MN><<<grid, kThreads, smem, stream>>>(ta, tb, a);
+  if (PAIR) {
+    const int pairs = (int)(tiles < max_pairs ? tiles : max_pairs);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    TG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, ta, tb, a));
+  } else {
+    const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
+    kernel<<<grid, kThreads, smem, stream>>>(ta, tb, a);
+  }
   if (a.splits > 1) {
     const int64_t mn = p.m * p.n;
     const int blocks = (int)((mn + 255) / 256 < 4 * sm_count() ? (mn + 255) / 256 : 4 * sm_count());
     splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(p.workspace, a.splits, p);
     return check_launch("gemm_tc(split-k)", 2);
   }
-  return check_launch("gemm_tc");
+  return check_launch(PAIR ? "gemm_tc(pair)" : "gemm_tc");
 }
 
-template <int BN>
+template <int BN, bool PAIR>
 static int launch_any(const GemmArgs<float>& p, bool a_mn, bool b_mn, int splits,
                       cudaStream_t stream) {
-  if (!a_mn && !b_mn) return launch<BN, false, false>(p, splits, stream);
-  if (!a_mn && b_mn) return launch<BN, false, true>(p, splits, stream);
-  if (a_mn && !b_mn) return launch<BN, true, false>(p, splits, stream);
-  return launch<BN, true, true>(p, splits, stream);
+  if (!a_mn && !b_mn) return launch<BN, false, false, PAIR>(p, splits, stream);
+  if (!a_mn && b_mn) return launch<BN, false, true, PAIR>(p, splits, stream);
+  if (a_mn && !b_mn) return launch<BN, true, false, PAIR>(p, splits, stream);
+  return launch<BN, true, true, PAIR>(p, splits, stream);
+}
+
+// CTA pairs are opt-in (TG_GEMM_PAIR=1). Measured on B200 they run at about 0.9x of the
+// single-CTA kernel: the in-kernel lo split makes every stage of the pair wait for a
+// cross-SM hand-off (split warps -> relay -> cluster-scope acquire by the MMA issuer), which
+// costs more than the halved B-operand traffic saves.
+static bool pair_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("TG_GEMM_PAIR");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
 }
 
 }  // namespace tc
@@ -779,9 +1017,24 @@ int gemm_tc_f32(const GemmArgs<float>& p, cudaStream_t stream) {
       if (s >= 2) splits = (int)s;
     }
   }
-  if (best == 64) return tc::launch_any<64>(p, a_mn, b_mn, splits, stream);
-  if (best == 128) return tc::launch_any<128>(p, a_mn, b_mn, splits, stream);
-  return tc::launch_any<256>(p, a_mn, b_mn, splits, stream);
+  // CTA pairs (256-row tiles, cta_group::2) for plain single products when their makespan
+  // wins. A pair tile is two single tiles' work on two SMs; with the B-operand traffic per SM
+  // halved it is modelled at 3/4 of a single tile's time.
+  if (splits == 1 && p.batch == 1 && p.kmode == GEMM_K_FULL && p.epi == GEMM_EPI_STORE &&
+      p.a_fold == 0 && p.m > tc::BM && best >= 128 && tc::pair_enabled()) {
+    const int64_t pairs = sms / 2;
+    const int64_t mt2 = (p.m + 2 * tc::BM - 1) / (2 * tc::BM);
+    const int64_t tiles2 = mt2 * ((p.n + best - 1) / best);
+    const int64_t single_tile = best == 256 ? 10 : 8;
+    const int64_t pair_cost = (tiles2 + pairs - 1) / pairs * single_tile * 3 / 4;
+    if (pair_cost < best_cost) {
+      if (best == 128) return tc::launch_any<128, true>(p, a_mn, b_mn, 1, stream);
+      return tc::launch_any<256, true>(p, a_mn, b_mn, 1, stream);
+    }
+  }
+  if (best == 64) return tc::launch_any<64, false>(p, a_mn, b_mn, splits, stream);
+  if (best == 128) return tc::launch_any<128, false>(p, a_mn, b_mn, splits, stream);
+  return tc::launch_any<256, false>(p, a_mn, b_mn, splits, stream);
 }
 
 }  // namespace tg

@@ -37,8 +37,12 @@ def tensor(a, dtype, requires_grad=True):
 
 
 # ------------------------------------------------------------------------------- GEMM
+# The last two are large enough for CTA pairs (256-row tiles, cta_group::2) when those are
+# enabled: 128- and 256-wide tiles with ragged rows (the odd CTA of the last pair has none)
+# and ragged columns (see test_gemm_cta_pairs_match_float64).
 GEMM_SHAPES = [(1, 1, 1), (7, 5, 3), (128, 128, 32), (130, 257, 100), (300, 64, 768),
-               (64, 300, 36), (1000, 333, 68), (8192 // 16, 3072 // 4, 768)]
+               (64, 300, 36), (1000, 333, 68), (8192 // 16, 3072 // 4, 768), (2100, 1000, 100),
+               (4096, 2000, 300)]
 
 
 @pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
@@ -64,6 +68,23 @@ def test_gemm_tensor_core_matches_float64(m, n, k, ta, tb):
     assert lib.tg_gemm_tc_status(1) == 0
     # 3xTF32 reaches near-fp32 accuracy (~1e-5 of max|C|): far inside the 1e-4 tolerance.
     assert_parity(out, ref, 2e-5, f"gemm {m}x{n}x{k} ta={ta} tb={tb}")
+
+
+def test_gemm_cta_pairs_match_float64():
+    # The opt-in CTA-pair kernel (TG_GEMM_PAIR=1 is read once per process): the GEMM tests
+    # above, on the pair-sized shapes, in a child process with pairs enabled.
+    import os
+    import subprocess
+    import sys
+
+    env = dict(os.environ, TG_GEMM_PAIR="1")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    res = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-p", "no:cacheprovider",
+                          os.path.join(root, "tests", "test_gpu_kernels.py"), "-k",
+                          "gemm_tensor_core and (2100-1000-100 or 4096-2000-300)"],
+                         env=env, cwd=root, capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-2000:]
+    assert "8 passed" in res.stdout, res.stdout[-2000:]
 
 
 def test_gemm_simt_fp64():
