@@ -2,17 +2,23 @@
 //
 // One warp per row with the row held in registers (cols <= 1024): the mean is taken first
 // and the variance from the centred values, as the reference does, so nothing is re-read
-// from HBM. The weight/bias gradients are column sums over rows: each block reduces its rows
-// in shared memory and writes one partial row to `scratch`; a second pass sums the partials
-// in a fixed order (deterministic).
+// from HBM. fp32 rows whose length is a multiple of 4 move as 16-byte vectors; other shapes
+// and float64 use the scalar kernels. The weight/bias gradients are column sums over rows:
+// each block reduces its warps' per-lane sums in shared memory and writes one partial row to
+// `scratch`; a second kernel sums the partial rows in a fixed order (deterministic), 32
+// columns x 8 row groups per block.
+#include <initializer_list>
+
 #include "common.cuh"
 #include "reduce.cuh"
 
 namespace tg {
 namespace {
 
-constexpr int kWarps = 4;
+constexpr int kWarps = 8;
+constexpr int kMaxPartials = 2 * 148;  // blocks of the backward pass (partial rows)
 
+// ---------------------------------------------------------------- scalar kernels
 template <typename T, int V>
 __global__ void __launch_bounds__(kWarps * 32)
 ln_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ b,
@@ -55,6 +61,23 @@ ln_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restr
       mean_out[r] = mean;
       rstd_out[r] = rstd;
     }
+  }
+}
+
+// Block-level reduction of per-lane column sums (sh: [kWarps][2][cols]) into one partial row.
+template <typename T>
+__device__ __forceinline__ void ln_block_partials(T* sh, T* __restrict__ part_w,
+                                                  T* __restrict__ part_b, int cols) {
+  __syncthreads();
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    T sw = T(0), sb = T(0);
+#pragma unroll
+    for (int i = 0; i < kWarps; ++i) {
+      sw += sh[(i * 2 + 0) * cols + c];
+      sb += sh[(i * 2 + 1) * cols + c];
+    }
+    part_w[(int64_t)blockIdx.x * cols + c] = sw;
+    part_b[(int64_t)blockIdx.x * cols + c] = sb;
   }
 }
 
@@ -112,39 +135,175 @@ ln_bwd_kernel(const T* __restrict__ g, const T* __restrict__ x, const T* __restr
       sh[(wid * 2 + 1) * cols + c] = ab[j];
     }
   }
-  __syncthreads();
-  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
-    T sw = T(0), sb = T(0);
+  ln_block_partials<T>(sh, part_w, part_b, cols);
+}
+
+// ---------------------------------------------------------------- fp32 16-byte kernels
+// Lane `lane` holds the float4 vectors lane, lane + 32, ... of its row (NV of them).
+__device__ __forceinline__ float sum4(float4 v) { return (v.x + v.y) + (v.z + v.w); }
+
+template <int NV>
+__global__ void __launch_bounds__(kWarps * 32)
+ln_fwd_vec4(const float* __restrict__ x, const float* __restrict__ w,
+            const float* __restrict__ b, float* __restrict__ y, float* __restrict__ mean_out,
+            float* __restrict__ rstd_out, int64_t rows, int cols, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int nv = cols >> 2;
+  const float4* xr = reinterpret_cast<const float4*>(x + r * cols);
+  float4 v[NV];
+  float s = 0.f;
 #pragma unroll
-    for (int i = 0; i < kWarps; ++i) {
-      sw += sh[(i * 2 + 0) * cols + c];
-      sb += sh[(i * 2 + 1) * cols + c];
+  for (int j = 0; j < NV; ++j) {
+    const int i = lane + 32 * j;
+    v[j] = i < nv ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    s += sum4(v[j]);
+  }
+  const float mean = warp_sum(s) / (float)cols;
+  float q = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = lane + 32 * j;
+    if (i < nv) {
+      v[j].x -= mean; v[j].y -= mean; v[j].z -= mean; v[j].w -= mean;
+      q += (v[j].x * v[j].x + v[j].y * v[j].y) + (v[j].z * v[j].z + v[j].w * v[j].w);
     }
-    part_w[(int64_t)blockIdx.x * cols + c] = sw;
-    part_b[(int64_t)blockIdx.x * cols + c] = sb;
+  }
+  const float rstd = 1.f / sqrtf(warp_sum(q) / (float)cols + eps);
+  float4* yr = reinterpret_cast<float4*>(y + r * cols);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  const float4* b4 = reinterpret_cast<const float4*>(b);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = lane + 32 * j;
+    if (i < nv) {
+      float4 o = make_float4(v[j].x * rstd, v[j].y * rstd, v[j].z * rstd, v[j].w * rstd);
+      if (w) {
+        const float4 ww = w4[i];
+        o.x *= ww.x; o.y *= ww.y; o.z *= ww.z; o.w *= ww.w;
+      }
+      if (b) {
+        const float4 bb = b4[i];
+        o.x += bb.x; o.y += bb.y; o.z += bb.z; o.w += bb.w;
+      }
+      yr[i] = o;
+    }
+  }
+  if (lane == 0) {
+    mean_out[r] = mean;
+    rstd_out[r] = rstd;
   }
 }
 
+template <int NV>
+__global__ void __launch_bounds__(kWarps * 32)
+ln_bwd_vec4(const float* __restrict__ g, const float* __restrict__ x,
+            const float* __restrict__ w, const float* __restrict__ mean_in,
+            const float* __restrict__ rstd_in, float* __restrict__ gx,
+            float* __restrict__ part_w, float* __restrict__ part_b, int64_t rows, int cols) {
+  extern __shared__ unsigned char smem_raw[];
+  float* sh = reinterpret_cast<float*>(smem_raw);  // [kWarps][2][cols]
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int64_t warp0 = (int64_t)blockIdx.x * kWarps + wid;
+  const int64_t nwarps = (int64_t)gridDim.x * kWarps;
+  const int nv = cols >> 2;
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  float4 aw[NV], ab[NV];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) aw[j] = ab[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int64_t r = warp0; r < rows; r += nwarps) {
+    const float4* xr = reinterpret_cast<const float4*>(x + r * cols);
+    const float4* gr = reinterpret_cast<const float4*>(g + r * cols);
+    const float mean = mean_in[r], rstd = rstd_in[r];
+    float4 xh[NV], gh[NV];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int i = lane + 32 * j;
+      if (i < nv) {
+        const float4 xv = xr[i], gv = gr[i];
+        xh[j] = make_float4((xv.x - mean) * rstd, (xv.y - mean) * rstd, (xv.z - mean) * rstd,
+                            (xv.w - mean) * rstd);
+        aw[j].x += gv.x * xh[j].x; aw[j].y += gv.y * xh[j].y;
+        aw[j].z += gv.z * xh[j].z; aw[j].w += gv.w * xh[j].w;
+        ab[j].x += gv.x; ab[j].y += gv.y; ab[j].z += gv.z; ab[j].w += gv.w;
+        if (w) {
+          const float4 ww = w4[i];
+          gh[j] = make_float4(gv.x * ww.x, gv.y * ww.y, gv.z * ww.z, gv.w * ww.w);
+        } else {
+          gh[j] = gv;
+        }
+      } else {
+        xh[j] = gh[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      s1 += sum4(gh[j]);
+      s2 += (gh[j].x * xh[j].x + gh[j].y * xh[j].y) + (gh[j].z * xh[j].z + gh[j].w * xh[j].w);
+    }
+    if (gx) {
+      const float m1 = warp_sum(s1) / (float)cols, m2 = warp_sum(s2) / (float)cols;
+      float4* gxr = reinterpret_cast<float4*>(gx + r * cols);
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        const int i = lane + 32 * j;
+        if (i < nv)
+          gxr[i] = make_float4(rstd * (gh[j].x - m1 - xh[j].x * m2),
+                               rstd * (gh[j].y - m1 - xh[j].y * m2),
+                               rstd * (gh[j].z - m1 - xh[j].z * m2),
+                               rstd * (gh[j].w - m1 - xh[j].w * m2));
+      }
+    }
+  }
+  if (!part_w) return;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = lane + 32 * j;
+    if (i < nv) {
+      reinterpret_cast<float4*>(sh + (wid * 2 + 0) * cols)[i] = aw[j];
+      reinterpret_cast<float4*>(sh + (wid * 2 + 1) * cols)[i] = ab[j];
+    }
+  }
+  ln_block_partials<float>(sh, part_w, part_b, cols);
+}
+
+// Sum of the partial rows: block (32 columns x 8 row groups), then the 8 group sums in order.
 template <typename T>
-__global__ void ln_final_kernel(const T* __restrict__ part_w, const T* __restrict__ part_b,
-                                T* __restrict__ gw, T* __restrict__ gb, int nparts, int cols) {
-  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < cols; c += gridDim.x * blockDim.x) {
-    T sw = T(0), sb = T(0);
-    for (int i = 0; i < nparts; ++i) {
+__global__ void __launch_bounds__(256)
+ln_final_kernel(const T* __restrict__ part_w, const T* __restrict__ part_b, T* __restrict__ gw,
+                T* __restrict__ gb, int nparts, int cols) {
+  __shared__ T sw_sh[8][32], sb_sh[8][32];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + tx;
+  T sw = T(0), sb = T(0);
+  if (c < cols) {
+    for (int i = ty; i < nparts; i += 8) {
       sw += part_w[(int64_t)i * cols + c];
       sb += part_b[(int64_t)i * cols + c];
     }
-    if (gw) gw[c] = sw;
-    if (gb) gb[c] = sb;
+  }
+  sw_sh[ty][tx] = sw;
+  sb_sh[ty][tx] = sb;
+  __syncthreads();
+  if (ty == 0 && c < cols) {
+    T tw = T(0), tb = T(0);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      tw += sw_sh[k][tx];
+      tb += sb_sh[k][tx];
+    }
+    if (gw) gw[c] = tw;
+    if (gb) gb[c] = tb;
   }
 }
 
 int ln_blocks(int64_t rows) {
   int64_t b = (rows + kWarps - 1) / kWarps;
-  if (b > 2 * 148) b = 2 * 148;
+  if (b > kMaxPartials) b = kMaxPartials;
   if (b < 1) b = 1;
   return (int)b;
 }
+
+bool aligned16(const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 template <typename T, int V>
 int ln_forward_v(const T* x, const T* w, const T* b, T* y, T* mean, T* rstd, int64_t rows,
@@ -152,6 +311,22 @@ int ln_forward_v(const T* x, const T* w, const T* b, T* y, T* mean, T* rstd, int
   ln_fwd_kernel<T, V><<<ln_blocks(rows), kWarps * 32, 0, s>>>(x, w, b, y, mean, rstd, rows,
                                                               cols, eps);
   return check_launch("layer_norm_forward");
+}
+
+template <int NV>
+int ln_forward_vec(const float* x, const float* w, const float* b, float* y, float* mean,
+                   float* rstd, int64_t rows, int cols, float eps, cudaStream_t s) {
+  const unsigned grid = (unsigned)((rows + kWarps - 1) / kWarps);
+  ln_fwd_vec4<NV><<<grid, kWarps * 32, 0, s>>>(x, w, b, y, mean, rstd, rows, cols, eps);
+  return check_launch("layer_norm_forward");
+}
+
+template <typename K>
+int set_smem(K kernel, size_t smem) {
+  if (smem > 48 * 1024)
+    TG_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem));
+  return TG_OK;
 }
 
 template <typename T, int V>
@@ -165,14 +340,42 @@ int ln_backward_v(const T* g, const T* x, const T* w, const T* mean, const T* rs
     part_b = part_w + (int64_t)nb * cols;
   }
   const size_t smem = (gw || gb) ? (size_t)kWarps * 2 * cols * sizeof(T) : 0;
-  if (smem > 48 * 1024)
-    TG_CUDA_TRY(cudaFuncSetAttribute(ln_bwd_kernel<T, V>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int rc = set_smem(ln_bwd_kernel<T, V>, smem);
+  if (rc) return rc;
   ln_bwd_kernel<T, V><<<nb, kWarps * 32, smem, s>>>(g, x, w, mean, rstd, gx, part_w, part_b,
                                                     rows, cols);
   if (gw || gb)
-    ln_final_kernel<T><<<grid_for(cols, 256), 256, 0, s>>>(part_w, part_b, gw, gb, nb, cols);
+    ln_final_kernel<T><<<(cols + 31) / 32, 256, 0, s>>>(part_w, part_b, gw, gb, nb, cols);
   return check_launch("layer_norm_backward", (gw || gb) ? 2 : 1);
+}
+
+template <int NV>
+int ln_backward_vec(const float* g, const float* x, const float* w, const float* mean,
+                    const float* rstd, float* gx, float* gw, float* gb, int64_t rows, int cols,
+                    void* scratch, cudaStream_t s) {
+  const int nb = ln_blocks(rows);
+  float* part_w = nullptr;
+  float* part_b = nullptr;
+  if (gw || gb) {
+    part_w = reinterpret_cast<float*>(scratch);
+    part_b = part_w + (int64_t)nb * cols;
+  }
+  const size_t smem = (gw || gb) ? (size_t)kWarps * 2 * cols * sizeof(float) : 0;
+  int rc = set_smem(ln_bwd_vec4<NV>, smem);
+  if (rc) return rc;
+  ln_bwd_vec4<NV><<<nb, kWarps * 32, smem, s>>>(g, x, w, mean, rstd, gx, part_w, part_b, rows,
+                                                cols);
+  if (gw || gb)
+    ln_final_kernel<float><<<(cols + 31) / 32, 256, 0, s>>>(part_w, part_b, gw, gb, nb, cols);
+  return check_launch("layer_norm_backward", (gw || gb) ? 2 : 1);
+}
+
+// fp32 rows of a multiple of 4 columns with 16-byte aligned buffers take the vector kernels.
+bool use_vec4(int cols, std::initializer_list<const void*> ptrs) {
+  if (cols % 4) return false;
+  for (const void* p : ptrs)
+    if (!aligned16(p)) return false;
+  return true;
 }
 
 }  // namespace
@@ -189,6 +392,17 @@ int tg_layer_norm_forward(int dtype, const void* x, const void* w, const void* b
                (long long)cols);
   if (rows <= 0) return TG_OK;
   cudaStream_t s = as_stream(stream);
+  if (dtype == TG_F32 && use_vec4((int)cols, {x, w, b, y})) {
+    const int c = (int)cols, nv = (c / 4 + 31) / 32;
+    auto* X = (const float*)x; auto* W = (const float*)w; auto* B = (const float*)b;
+    auto* Y = (float*)y; auto* M = (float*)mean; auto* R = (float*)rstd;
+    const float e = (float)eps;
+    if (nv <= 1) return ln_forward_vec<1>(X, W, B, Y, M, R, rows, c, e, s);
+    if (nv <= 2) return ln_forward_vec<2>(X, W, B, Y, M, R, rows, c, e, s);
+    if (nv <= 4) return ln_forward_vec<4>(X, W, B, Y, M, R, rows, c, e, s);
+    if (nv <= 6) return ln_forward_vec<6>(X, W, B, Y, M, R, rows, c, e, s);
+    return ln_forward_vec<8>(X, W, B, Y, M, R, rows, c, e, s);
+  }
   return TG_DISPATCH_FLOAT(dtype, T, [&] {
     const int c = (int)cols;
     auto* X = (const T*)x; auto* W = (const T*)w; auto* B = (const T*)b;
@@ -220,6 +434,17 @@ int tg_layer_norm_backward(int dtype, const void* g, const void* x, const void* 
     if (gw) TG_CUDA_TRY(cudaMemsetAsync(gw, 0, cols * (dtype == TG_F64 ? 8 : 4), s));
     if (gb) TG_CUDA_TRY(cudaMemsetAsync(gb, 0, cols * (dtype == TG_F64 ? 8 : 4), s));
     return TG_OK;
+  }
+  if (dtype == TG_F32 && use_vec4((int)cols, {g, x, w, gx})) {
+    const int c = (int)cols, nv = (c / 4 + 31) / 32;
+    auto* G = (const float*)g; auto* X = (const float*)x; auto* W = (const float*)w;
+    auto* M = (const float*)mean; auto* R = (const float*)rstd;
+    auto* GX = (float*)gx; auto* GW = (float*)gw; auto* GB = (float*)gb;
+    if (nv <= 1) return ln_backward_vec<1>(G, X, W, M, R, GX, GW, GB, rows, c, scratch, s);
+    if (nv <= 2) return ln_backward_vec<2>(G, X, W, M, R, GX, GW, GB, rows, c, scratch, s);
+    if (nv <= 4) return ln_backward_vec<4>(G, X, W, M, R, GX, GW, GB, rows, c, scratch, s);
+    if (nv <= 6) return ln_backward_vec<6>(G, X, W, M, R, GX, GW, GB, rows, c, scratch, s);
+    return ln_backward_vec<8>(G, X, W, M, R, GX, GW, GB, rows, c, scratch, s);
   }
   return TG_DISPATCH_FLOAT(dtype, T, [&] {
     const int c = (int)cols;

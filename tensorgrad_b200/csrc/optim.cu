@@ -10,7 +10,7 @@ namespace tg {
 namespace {
 
 constexpr int kMaxTensors = 64;
-constexpr int kNormBlocks = 296;
+constexpr int kNormBlocks = 148 * 8;
 
 struct TensorList {
   int count;
@@ -29,18 +29,36 @@ struct AdamList {
   double bc2_sqrt[kMaxTensors];   // sqrt(1 - beta2^step)
 };
 
+// Sum of squares in float64. fp32 tensors with 16-byte aligned storage are read as float4
+// with four independent accumulators (the scalar tail after them); other tensors element by
+// element. The element-to-thread map and the reduction order are fixed (deterministic).
 template <typename T>
 __global__ void __launch_bounds__(256) sumsq_kernel(TensorList L, double* __restrict__ partial) {
   __shared__ double sh[32];
-  double acc = 0.0;
+  double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int t = 0; t < L.count; ++t) {
     const T* x = reinterpret_cast<const T*>(L.ptr[t]);
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < L.numel[t]; i += stride) {
+    int64_t done = 0;
+    if (sizeof(T) == 4 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+      const int64_t n4 = L.numel[t] >> 2;
+      const float4* x4 = reinterpret_cast<const float4*>(x);
+      for (int64_t i = tid; i < n4; i += stride) {
+        const float4 v = x4[i];
+        a0 += (double)v.x * (double)v.x;
+        a1 += (double)v.y * (double)v.y;
+        a2 += (double)v.z * (double)v.z;
+        a3 += (double)v.w * (double)v.w;
+      }
+      done = n4 << 2;
+    }
+    for (int64_t i = done + tid; i < L.numel[t]; i += stride) {
       const double v = (double)x[i];
-      acc += v * v;
+      a0 += v * v;
     }
   }
+  double acc = (a0 + a1) + (a2 + a3);
   acc = block_sum(acc, sh);
   if (threadIdx.x == 0) partial[blockIdx.x] = acc;
 }

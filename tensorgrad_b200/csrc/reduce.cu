@@ -9,6 +9,49 @@ namespace {
 constexpr int kColTile = 32;   // columns per block (one warp wide)
 constexpr int kRowLanes = 8;   // row groups per block
 
+// Pass 1 (fp32, 16-byte vectors): block (cx, chunk) sums rows [chunk*rpc, ...) of 128
+// columns (a float4 per lane) into partial[chunk][c]; each row group keeps 4 rows in flight.
+constexpr int kVecCols = 4 * kColTile;
+
+__global__ void __launch_bounds__(kColTile * kRowLanes)
+colsum_partial_vec4(const float* __restrict__ x, float* __restrict__ partial, int64_t rows,
+                    int64_t cols, int64_t rows_per_chunk) {
+  __shared__ float4 sh[kRowLanes][kColTile];
+  const int64_t c4 = (int64_t)blockIdx.x * kColTile + threadIdx.x;  // float4 column index
+  const int64_t n4 = cols >> 2;
+  const int64_t r0 = (int64_t)blockIdx.y * rows_per_chunk;
+  int64_t r1 = r0 + rows_per_chunk;
+  if (r1 > rows) r1 = rows;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (c4 < n4) {
+    const float4* xc = reinterpret_cast<const float4*>(x) + c4;
+    int64_t r = r0 + threadIdx.y;
+    for (; r + 3 * kRowLanes < r1; r += 4 * kRowLanes) {
+      const float4 a = xc[r * n4], b = xc[(r + kRowLanes) * n4];
+      const float4 c = xc[(r + 2 * kRowLanes) * n4], d = xc[(r + 3 * kRowLanes) * n4];
+      acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
+      acc.x += b.x; acc.y += b.y; acc.z += b.z; acc.w += b.w;
+      acc.x += c.x; acc.y += c.y; acc.z += c.z; acc.w += c.w;
+      acc.x += d.x; acc.y += d.y; acc.z += d.z; acc.w += d.w;
+    }
+    for (; r < r1; r += kRowLanes) {
+      const float4 a = xc[r * n4];
+      acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
+    }
+  }
+  sh[threadIdx.y][threadIdx.x] = acc;
+  __syncthreads();
+  if (threadIdx.y == 0 && c4 < n4) {
+    float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < kRowLanes; ++i) {
+      const float4 v = sh[i][threadIdx.x];
+      t.x += v.x; t.y += v.y; t.z += v.z; t.w += v.w;
+    }
+    reinterpret_cast<float4*>(partial + (int64_t)blockIdx.y * cols)[c4] = t;
+  }
+}
+
 // Pass 1: block (cx, chunk) sums rows [chunk*rpc, ...) of 32 columns into partial[chunk][c].
 template <typename T>
 __global__ void __launch_bounds__(kColTile * kRowLanes)
@@ -92,9 +135,10 @@ __global__ void sum_final_kernel(const double* __restrict__ partial, int nparts,
 }  // namespace
 
 int64_t colsum_chunks(int64_t rows, int64_t cols) {
-  const int64_t col_blocks = (cols + kColTile - 1) / kColTile;
-  int64_t chunks = (2 * 148 + col_blocks - 1) / col_blocks;
-  const int64_t max_chunks = (rows + 63) / 64;  // at least 64 rows per chunk
+  // Enough blocks for about four per SM; at least 32 rows per chunk.
+  const int64_t col_blocks = (cols + kVecCols - 1) / kVecCols;
+  int64_t chunks = (4 * 148 + col_blocks - 1) / col_blocks;
+  const int64_t max_chunks = (rows + 31) / 32;
   if (chunks > max_chunks) chunks = max_chunks;
   if (chunks < 1) chunks = 1;
   return chunks;
@@ -111,9 +155,16 @@ int colsum(const T* x, T* out, int64_t rows, int64_t cols, int accumulate, void*
   const int64_t chunks = colsum_chunks(rows, cols);
   const int64_t rpc = (rows + chunks - 1) / chunks;
   T* partial = reinterpret_cast<T*>(scratch);
-  dim3 grid((unsigned)((cols + kColTile - 1) / kColTile), (unsigned)chunks);
-  colsum_partial_kernel<T><<<grid, dim3(kColTile, kRowLanes), 0, stream>>>(x, partial, rows,
-                                                                          cols, rpc);
+  if (sizeof(T) == 4 && cols % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(scratch) & 15) == 0) {
+    dim3 grid((unsigned)((cols + kVecCols - 1) / kVecCols), (unsigned)chunks);
+    colsum_partial_vec4<<<grid, dim3(kColTile, kRowLanes), 0, stream>>>(
+        reinterpret_cast<const float*>(x), reinterpret_cast<float*>(partial), rows, cols, rpc);
+  } else {
+    dim3 grid((unsigned)((cols + kColTile - 1) / kColTile), (unsigned)chunks);
+    colsum_partial_kernel<T><<<grid, dim3(kColTile, kRowLanes), 0, stream>>>(x, partial, rows,
+                                                                            cols, rpc);
+  }
   colsum_final_kernel<T><<<grid_for(cols, 256), 256, 0, stream>>>(partial, out, cols, chunks,
                                                                   accumulate);
   return check_launch("colsum", 2);
