@@ -93,8 +93,13 @@ int tg_linear_forward(int dtype, const void* x, const void* w, const void* bias,
                       int64_t rows, int64_t in_features, int64_t out_features, void* stream);
 /* linear VJP (ops/layers.py:43-49): gx = g @ w, gw = g^T @ x (+ beta_gw * gw), gb = colsum(g).
  * need bit 0 = gx, bit 1 = gw, bit 2 = gb (unset bits skip the launch). beta_gw = 1
- * accumulates into an existing gw (tied weights). `scratch` holds at least
- * tg_colsum_scratch_bytes(dtype, rows, out_features) bytes when bit 2 is set. */
+ * accumulates into an existing gw (tied weights). `scratch` holds
+ * tg_linear_backward_scratch_bytes(dtype, rows, in, out, need) bytes: the column-sum partials
+ * and a workspace that lets the fp32 products split their reduction over more CTAs (e.g. the
+ * vocabulary-wide head, whose 192 output tiles would leave the second wave of 148 SMs mostly
+ * idle). It may be NULL when bit 2 is clear; the products then run unsplit. */
+size_t tg_linear_backward_scratch_bytes(int dtype, int64_t rows, int64_t in_features,
+                                        int64_t out_features, unsigned need);
 int tg_linear_backward(int dtype, const void* g, const void* x, const void* w, void* gx, void* gw,
                        void* gb, int64_t rows, int64_t in_features, int64_t out_features,
                        unsigned need, double beta_gw, void* scratch, void* stream);

@@ -73,6 +73,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tg_gemm_batched": (c_int, [c_int, c_int, c_int, i64, i64, i64, dbl, vp, i64, i64, vp, i64,
                                 i64, dbl, vp, i64, i64, i64, vp]),
     "tg_linear_forward": (c_int, [c_int, vp, vp, vp, vp, i64, i64, i64, vp]),
+    "tg_linear_backward_scratch_bytes": (sz, [c_int, i64, i64, i64, u32]),
     "tg_linear_backward": (c_int, [c_int, vp, vp, vp, vp, vp, vp, i64, i64, i64, u32, dbl, vp,
                                    vp]),
     "tg_colsum_scratch_bytes": (sz, [c_int, i64, i64]),

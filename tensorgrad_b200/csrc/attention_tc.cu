@@ -82,6 +82,52 @@ __global__ void softmax_rows_kernel(float* __restrict__ S, int64_t ldS, float* _
   }
 }
 
+// The same softmax with the row in registers (rows of up to 128 * NV keys): one 16-byte read
+// and one 16-byte write per element, the maximum and the sum from registers.
+template <int NV>
+__global__ void __launch_bounds__(256)
+softmax_rows_vec4(float* __restrict__ S, int64_t ldS, float* __restrict__ lse, int64_t Tq,
+                  int64_t Tk, int causal, int64_t rows) {
+  const int lane = threadIdx.x & 31;
+  for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows;
+       r += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    float4* s4 = reinterpret_cast<float4*>(S + r * ldS);
+    const int64_t i = r % Tq;
+    const int64_t valid = row_valid(i, Tk, causal), written = row_written(i, Tk, causal);
+    const int64_t nv = (valid + 3) >> 2, nw = (written + 3) >> 2;
+    float4 v[NV];
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int64_t q = lane + 32 * j;
+      v[j] = q < nv ? s4[q] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      const int64_t c = 4 * q;
+      if (c + 0 >= valid) v[j].x = -INFINITY;
+      if (c + 1 >= valid) v[j].y = -INFINITY;
+      if (c + 2 >= valid) v[j].z = -INFINITY;
+      if (c + 3 >= valid) v[j].w = -INFINITY;
+      m = fmaxf(m, fmaxf(fmaxf(v[j].x, v[j].y), fmaxf(v[j].z, v[j].w)));
+    }
+    m = warp_max(m);
+    float l = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      v[j].x = expf(v[j].x - m); v[j].y = expf(v[j].y - m);
+      v[j].z = expf(v[j].z - m); v[j].w = expf(v[j].w - m);
+      l += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+    }
+    l = warp_sum(l);
+    const float inv = 1.f / l;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int64_t q = lane + 32 * j;
+      if (q < nw)
+        s4[q] = make_float4(v[j].x * inv, v[j].y * inv, v[j].z * inv, v[j].w * inv);
+    }
+    if (lane == 0) lse[r] = m + logf(l);
+  }
+}
+
 // delta[(b*H + h)*T + t] = dO[b, h, t, :] . O[b, h, t, :], one warp per row.
 __global__ void row_dot_kernel(View a, View b, float* __restrict__ out, int64_t H, int64_t T,
                                int64_t D, int64_t rows) {
@@ -165,8 +211,13 @@ int attention_tc_forward(const tg_attn_shape* s, const float* q, const float* k,
                              causal ? GEMM_K_SKIP_UPPER : GEMM_K_FULL), st)))
     return rc;
   const int64_t rows = p.BH * p.Tq;
-  softmax_rows_kernel<<<grid_for(rows * 32, 256), 256, 0, st>>>(S, p.ldS, lse, p.Tq, p.Tk, causal,
-                                                                rows);
+  const unsigned grid = grid_for(rows * 32, 256, 148 * 64);
+  const int64_t nv = (p.Tk + 127) / 128;  // float4 per lane for a whole row
+  if (nv <= 1) softmax_rows_vec4<1><<<grid, 256, 0, st>>>(S, p.ldS, lse, p.Tq, p.Tk, causal, rows);
+  else if (nv <= 2) softmax_rows_vec4<2><<<grid, 256, 0, st>>>(S, p.ldS, lse, p.Tq, p.Tk, causal, rows);
+  else if (nv <= 4) softmax_rows_vec4<4><<<grid, 256, 0, st>>>(S, p.ldS, lse, p.Tq, p.Tk, causal, rows);
+  else if (nv <= 8) softmax_rows_vec4<8><<<grid, 256, 0, st>>>(S, p.ldS, lse, p.Tq, p.Tk, causal, rows);
+  else softmax_rows_kernel<<<grid, 256, 0, st>>>(S, p.ldS, lse, p.Tq, p.Tk, causal, rows);
   if ((rc = check_launch("attention softmax"))) return rc;
   // O = P V  (V stored Tk x D: the "k x n" operand)
   return bgemm(bgemm_args(0, 0, p.Tq, p.D, p.Tk, 1.f, Sv, V, O, p,

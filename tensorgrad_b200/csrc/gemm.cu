@@ -67,6 +67,9 @@ cudaEvent_t take_event() {
   return e;
 }
 
+// Largest split-K workspace the linear VJP asks its caller for.
+constexpr size_t kLinearWorkspaceCap = size_t(128) << 20;
+
 // Process-wide matmul precision of the fp32 tensor-core path (tg_set_matmul_precision).
 int g_precision = 0;
 
@@ -221,22 +224,60 @@ int tg_linear_forward(int dtype, const void* x, const void* w, const void* bias,
                  in_features, 0.0, y, out_features, bias, stream);
 }
 
+size_t tg_linear_backward_scratch_bytes(int dtype, int64_t rows, int64_t in_features,
+                                        int64_t out_features, unsigned need) {
+  const size_t es = dtype == TG_F64 ? 8 : 4;
+  size_t bytes = (need & 4) ? (tg_colsum_scratch_bytes(dtype, rows, out_features) + 255) / 256 * 256
+                            : 0;
+  if (dtype == TG_F32) {
+    int64_t mn = 0;
+    if (need & 1) mn = rows * in_features;
+    if ((need & 2) && out_features * in_features > mn) mn = out_features * in_features;
+    size_t ws = (size_t)mn * es * 4;  // room for four split-K partials
+    if (ws > kLinearWorkspaceCap) ws = kLinearWorkspaceCap;
+    bytes += ws;
+  }
+  return bytes ? bytes : 16;
+}
+
 int tg_linear_backward(int dtype, const void* g, const void* x, const void* w, void* gx, void* gw,
                        void* gb, int64_t rows, int64_t in_features, int64_t out_features,
                        unsigned need, double beta_gw, void* scratch, void* stream) {
-  int rc = TG_OK;
-  if ((need & 1) && gx) {
-    // gx[rows, in] = g[rows, out] @ w[out, in]
-    rc = tg_gemm(dtype, 0, 0, rows, in_features, out_features, 1.0, g, out_features, w,
-                 in_features, 0.0, gx, in_features, nullptr, stream);
-    if (rc) return rc;
-  }
-  if ((need & 2) && gw) {
-    // gw[out, in] = g^T @ x: A = g stored rows x out (k x m), B = x stored rows x in (k x n)
-    rc = tg_gemm(dtype, 1, 0, out_features, in_features, rows, 1.0, g, out_features, x,
-                 in_features, beta_gw, gw, in_features, nullptr, stream);
-    if (rc) return rc;
-  }
+  int rc = check_gemm(0, 0, rows, in_features, out_features, out_features, in_features,
+                      in_features);
+  if (rc) return rc;
+  TG_CHECK_ARG(!((need & 4) && gb) || scratch, "linear_backward: scratch is NULL");
+  // Split-K partials (tensor-core products) live after the column-sum partials.
+  const size_t cs = (need & 4) ? (tg_colsum_scratch_bytes(dtype, rows, out_features) + 255) / 256 * 256
+                               : 0;
+  const size_t total = scratch ? tg_linear_backward_scratch_bytes(dtype, rows, in_features,
+                                                                  out_features, need) : 0;
+  float* ws = (scratch && total > cs + 16) ? reinterpret_cast<float*>((uint8_t*)scratch + cs)
+                                           : nullptr;
+  const size_t ws_bytes = ws ? total - cs : 0;
+  cudaStream_t s = as_stream(stream);
+  rc = TG_DISPATCH_FLOAT(dtype, T, [&] {
+    if ((need & 1) && gx) {
+      // gx[rows, in] = g[rows, out] @ w[out, in]
+      auto p = make_args<T>(0, 0, rows, in_features, out_features, 1.0, g, out_features, 0, w,
+                            in_features, 0, 0.0, gx, in_features, 0, nullptr, 1);
+      p.workspace = ws;
+      p.workspace_bytes = ws_bytes;
+      const int r = gemm_dispatch<T>(p, true, s);
+      if (r) return r;
+    }
+    if ((need & 2) && gw) {
+      // gw[out, in] = g^T @ x: A = g stored rows x out (k x m), B = x stored rows x in (k x n)
+      auto p = make_args<T>(1, 0, out_features, in_features, rows, 1.0, g, out_features, 0, x,
+                            in_features, 0, beta_gw, gw, in_features, 0, nullptr, 1);
+      p.workspace = ws;
+      p.workspace_bytes = ws_bytes;
+      const int r = gemm_dispatch<T>(p, true, s);
+      if (r) return r;
+    }
+    return (int)TG_OK;
+  });
+  if (rc) return rc;
   if ((need & 4) && gb) rc = tg_colsum(dtype, g, gb, rows, out_features, 0, scratch, stream);
   return rc;
 }

@@ -1003,18 +1003,31 @@ int gemm_tc_f32(const GemmArgs<float>& p, cudaStream_t stream) {
       best = bn;
     }
   }
-  // Split-K when the output has too few tiles to occupy half the SMs and each split keeps at
-  // least 8 k-blocks (the pipeline's fill and the epilogue amortise over them).
+  // Split-K (when the caller supplied a workspace): the number of splits s minimising the
+  // modelled makespan ceil(tiles * s / SMs) * (nk / s + 2) + s / 2, in k-block units (each
+  // tile also pays about two k-blocks of pipeline fill and epilogue; the partial sums cost
+  // about half a k-block per split). It fills the SMs when the output has few tiles and
+  // evens out the last wave when it has a few more tiles than SMs; every split keeps at
+  // least 8 k-blocks.
   int splits = 1;
   if (p.workspace && p.batch == 1 && p.kmode == GEMM_K_FULL) {
     const int64_t tiles = mt * ((p.n + best - 1) / best);
     const int64_t nk = (p.k + tc::BK - 1) / tc::BK;
-    if (2 * tiles <= sms && nk >= 16) {
-      int64_t s = sms / tiles;
-      if (s > nk / 8) s = nk / 8;
-      const int64_t fit = (int64_t)(p.workspace_bytes / (sizeof(float) * (size_t)(p.m * p.n)));
-      if (s > fit) s = fit;
-      if (s >= 2) splits = (int)s;
+    const int64_t fit = (int64_t)(p.workspace_bytes / (sizeof(float) * (size_t)(p.m * p.n)));
+    int64_t smax = nk / 8;
+    if (smax > fit) smax = fit;
+    if (smax > sms) smax = sms;
+    auto cost = [&](int64_t s) {
+      return (double)((tiles * s + sms - 1) / sms) * ((double)nk / (double)s + 2.0) +
+             (s > 1 ? 0.5 * (double)s : 0.0);
+    };
+    double best_t = cost(1);
+    for (int64_t s = 2; s <= smax; ++s) {
+      const double t = cost(s);
+      if (t < best_t - 1e-9) {
+        best_t = t;
+        splits = (int)s;
+      }
     }
   }
   // CTA pairs (256-row tiles, cta_group::2) for plain single products when their makespan

@@ -53,12 +53,12 @@ def linear(x: Any, weight: Any, bias: Any = None) -> Tensor:
         gw = device.empty(tw.shape, xd.dtype) if need[1] else None
         gb = device.empty((out_f,), xd.dtype) if has_bias and need[2] else None
         mask = (1 if gx is not None else 0) | (2 if gw is not None else 0) | (4 if gb is not None else 0)
-        scratch = (device.scratch(lib.tg_colsum_scratch_bytes(code, rows, out_f))
-                   if gb is not None else None)
+        scratch = device.scratch(lib.tg_linear_backward_scratch_bytes(code, rows, in_f, out_f,
+                                                                      mask))
         check(lib.tg_linear_backward(
             code, g.ptr, xd.ptr, wd.ptr, gx.ptr if gx is not None else None,
             gw.ptr if gw is not None else None, gb.ptr if gb is not None else None,
-            rows, in_f, out_f, mask, 0.0, scratch.ptr if scratch is not None else None,
+            rows, in_f, out_f, mask, 0.0, scratch.ptr,
             device.stream()), "linear backward")
         if gx is not None and gx.dtype != tx.dtype:
             gx = cast_array(gx, tx.dtype)
