@@ -143,7 +143,35 @@ def _topological_order(roots: Sequence[Tensor]) -> list[Tensor]:
             for p in node.parents:
                 if p._requires_grad and id(p) not in seen:
                     stack.append((p, False))
-    return order
+    return _leaves_before_first_use(order)
+
+
+def _leaves_before_first_use(order: list[Tensor]) -> list[Tensor]:
+    """The same order with every leaf moved to just before its first consumer.
+
+    The backward walk visits ``order`` reversed, so a leaf is then finalised right after the
+    last op that contributes to its gradient, not wherever the depth-first search happened
+    to reach it (the last parameters a backward pass sees, e.g. the earliest blocks' weights,
+    are otherwise reached first and processed last). The ops' order, and therefore every
+    sum, is unchanged; only the moment a leaf's ``.grad`` is written (and the leaf hooks of
+    data-parallel bucketing fire) moves earlier.
+    """
+    placed: set[int] = set()
+    out: list[Tensor] = []
+    for t in order:
+        node = t._node
+        if node is None:
+            continue
+        for p in node.parents:
+            if p._node is None and p._requires_grad and id(p) not in placed:
+                placed.add(id(p))
+                out.append(p)
+        out.append(t)
+    # Leaves nobody consumes (e.g. a root that is a leaf) keep their place at the end.
+    for t in order:
+        if t._node is None and id(t) not in placed:
+            out.append(t)
+    return out
 
 
 def _leads_to(order: list[Tensor], targets: set[int]) -> set[int]:

@@ -133,3 +133,31 @@ def test_leaf_hook_fires_once_per_leaf_when_final():
     finally:
         remove()
     assert sorted(fired) == sorted([(id(a), 1.0), (id(w), 2.0)])
+
+
+def test_leaf_is_finalised_right_after_its_last_consumer():
+    # y = f(h, w2), h = g(x, w1): w2's gradient is final once f's VJP ran, so its leaf hook
+    # (data-parallel bucketing) fires before g's VJP, not at the end of the walk.
+    from tensorgrad_b200 import autograd
+
+    x, w1, w2 = leaf([1.0]), leaf([2.0]), leaf([3.0])
+    events = []
+
+    def g_vjp(g, need):
+        events.append("vjp g")
+        return (g, g)
+
+    def f_vjp(g, need):
+        events.append("vjp f")
+        return (g, g)
+
+    h = op([x, w1], [1.0], g_vjp, "g")
+    y = op([h, w2], [1.0], f_vjp, "f")
+    names = {id(x): "x", id(w1): "w1", id(w2): "w2"}
+    remove = autograd.add_leaf_hook(lambda t: events.append("leaf " + names[id(t)]))
+    try:
+        autograd._run_backward((y,), (np.ones(1),), retain_graph=False, targets=None)
+    finally:
+        remove()
+    assert events.index("leaf w2") < events.index("vjp g")
+    assert sorted(e for e in events if e.startswith("leaf")) == ["leaf w1", "leaf w2", "leaf x"]
