@@ -830,6 +830,42 @@ splitk_reduce_kernel(const float* __restrict__ ws, int splits, GemmArgs<float> p
   }
 }
 
+// The same for a plain row-major C whose rows are whole float4s: 16-byte accesses, the
+// splits' loads of one vector issued together.
+__global__ void __launch_bounds__(256)
+splitk_reduce_vec4(const float4* __restrict__ ws, int splits, GemmArgs<float> p) {
+  const int64_t mn4 = p.m * p.n / 4, n4 = p.n / 4;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < mn4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    int sp = 0;
+    for (; sp + 4 <= splits; sp += 4) {
+      const float4 a = ws[sp * mn4 + i], b = ws[(sp + 1) * mn4 + i];
+      const float4 c = ws[(sp + 2) * mn4 + i], d = ws[(sp + 3) * mn4 + i];
+      s.x += a.x; s.y += a.y; s.z += a.z; s.w += a.w;
+      s.x += b.x; s.y += b.y; s.z += b.z; s.w += b.w;
+      s.x += c.x; s.y += c.y; s.z += c.z; s.w += c.w;
+      s.x += d.x; s.y += d.y; s.z += d.z; s.w += d.w;
+    }
+    for (; sp < splits; ++sp) {
+      const float4 a = ws[sp * mn4 + i];
+      s.x += a.x; s.y += a.y; s.z += a.z; s.w += a.w;
+    }
+    const int64_t row = i / n4, c4 = i % n4;
+    float4* dst = reinterpret_cast<float4*>(p.c + row * p.ldc) + c4;
+    float4 v = make_float4(p.alpha * s.x, p.alpha * s.y, p.alpha * s.z, p.alpha * s.w);
+    if (p.beta != 0.f) {
+      const float4 o = *dst;
+      v.x += p.beta * o.x; v.y += p.beta * o.y; v.z += p.beta * o.z; v.w += p.beta * o.w;
+    }
+    if (p.bias) {
+      const float4 bb = reinterpret_cast<const float4*>(p.bias)[c4];
+      v.x += bb.x; v.y += bb.y; v.z += bb.z; v.w += bb.w;
+    }
+    *dst = v;
+  }
+}
+
 template <int BN, bool A_MN, bool B_MN, bool PAIR>
 static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
   using L = Layout<BN, PAIR>;
@@ -934,8 +970,17 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
   }
   if (a.splits > 1) {
     const int64_t mn = p.m * p.n;
-    const int blocks = (int)((mn + 255) / 256 < 4 * sm_count() ? (mn + 255) / 256 : 4 * sm_count());
-    splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(p.workspace, a.splits, p);
+    const bool v4 = p.c_hw == 0 && p.n % 4 == 0 && p.ldc % 4 == 0 &&
+                    (reinterpret_cast<uintptr_t>(p.c) & 15) == 0 &&
+                    (!p.bias || (reinterpret_cast<uintptr_t>(p.bias) & 15) == 0);
+    const int64_t work = v4 ? mn / 4 : mn;
+    const int blocks = (int)((work + 255) / 256 < 8 * sm_count() ? (work + 255) / 256
+                                                                    : 8 * sm_count());
+    if (v4)
+      splitk_reduce_vec4<<<blocks, 256, 0, stream>>>(reinterpret_cast<const float4*>(p.workspace),
+                                                     a.splits, p);
+    else
+      splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(p.workspace, a.splits, p);
     return check_launch("gemm_tc(split-k)", 2);
   }
   return check_launch(PAIR ? "gemm_tc(pair)" : "gemm_tc");
@@ -1004,11 +1049,12 @@ int gemm_tc_f32(const GemmArgs<float>& p, cudaStream_t stream) {
     }
   }
   // Split-K (when the caller supplied a workspace): the number of splits s minimising the
-  // modelled makespan ceil(tiles * s / SMs) * (nk / s + 2) + s / 2, in k-block units (each
-  // tile also pays about two k-blocks of pipeline fill and epilogue; the partial sums cost
-  // about half a k-block per split). It fills the SMs when the output has few tiles and
-  // evens out the last wave when it has a few more tiles than SMs; every split keeps at
-  // least 8 k-blocks.
+  // modelled makespan ceil(tiles * s / SMs) * (nk / s + 2 + 12 [s > 1]), in k-block units:
+  // every tile also pays about two k-blocks of pipeline fill and epilogue, and a split tile
+  // about twelve more for writing its fp32 partial and reading it back in the reduction
+  // (a 128 x 256 partial is 128 KB each way at an SM's share of HBM bandwidth). It fills the
+  // SMs when the output has few tiles and evens out the last wave of long reductions; every
+  // split keeps at least 8 k-blocks.
   int splits = 1;
   if (p.workspace && p.batch == 1 && p.kmode == GEMM_K_FULL) {
     const int64_t tiles = mt * ((p.n + best - 1) / best);
@@ -1018,8 +1064,8 @@ int gemm_tc_f32(const GemmArgs<float>& p, cudaStream_t stream) {
     if (smax > fit) smax = fit;
     if (smax > sms) smax = sms;
     auto cost = [&](int64_t s) {
-      return (double)((tiles * s + sms - 1) / sms) * ((double)nk / (double)s + 2.0) +
-             (s > 1 ? 0.5 * (double)s : 0.0);
+      return (double)((tiles * s + sms - 1) / sms) *
+             ((double)nk / (double)s + 2.0 + (s > 1 ? 12.0 : 0.0));
     };
     double best_t = cost(1);
     for (int64_t s = 2; s <= smax; ++s) {
