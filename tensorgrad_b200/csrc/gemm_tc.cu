@@ -32,7 +32,9 @@
 
 #include <stdlib.h>
 
+#include <functional>
 #include <mutex>
+#include <unordered_map>
 
 #include "common.cuh"
 #include "gemm.cuh"
@@ -781,9 +783,67 @@ static EncodeFn get_encode() {
 // stride `ld`, head stride `hstride`, outer stride `bstride` elements); boxes of
 // box_inner x box_rows. Dimensions of extent 1 get a harmless stride (the encoder still
 // wants a multiple of 16 bytes).
+struct MapKey {
+  const void* ptr;
+  int64_t v[8];
+  int dev;
+  bool operator==(const MapKey& o) const {
+    if (ptr != o.ptr || dev != o.dev) return false;
+    for (int i = 0; i < 8; ++i)
+      if (v[i] != o.v[i]) return false;
+    return true;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    size_t h = std::hash<const void*>()(k.ptr) ^ (size_t)k.dev * 0x9E3779B97F4A7C15ull;
+    for (int i = 0; i < 8; ++i) h = (h ^ (size_t)k.v[i]) * 0x100000001B3ull;
+    return h;
+  }
+};
+
+// Encoded maps by value (a map holds only an address, extents, strides and the box, so a
+// cached entry is valid whenever the same values recur, e.g. the recurrent products of every
+// time step of every training step). Host-side cost of an encode is then paid once.
+static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_map_cache;
+static std::mutex g_map_mutex;
+constexpr size_t kMapCacheCap = 1 << 14;
+
+static int make_map_uncached(CUtensorMap* map, const float* ptr, int64_t inner, int64_t rows,
+                             int64_t ld, int64_t heads, int64_t hstride, int64_t nb,
+                             int64_t bstride, uint32_t box_inner, uint32_t box_rows,
+                             CUtensorMapSwizzle swizzle);
+
 static int make_map(CUtensorMap* map, const float* ptr, int64_t inner, int64_t rows, int64_t ld,
                     int64_t heads, int64_t hstride, int64_t nb, int64_t bstride,
                     uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  MapKey key{ptr, {inner, rows, ld, heads, hstride, nb, bstride,
+                   ((int64_t)box_inner << 32) | ((int64_t)box_rows << 8) | (int64_t)swizzle},
+             dev};
+  {
+    std::lock_guard<std::mutex> lock(g_map_mutex);
+    auto it = g_map_cache.find(key);
+    if (it != g_map_cache.end()) {
+      *map = it->second;
+      return TG_OK;
+    }
+  }
+  const int rc = make_map_uncached(map, ptr, inner, rows, ld, heads, hstride, nb, bstride,
+                                   box_inner, box_rows, swizzle);
+  if (rc == TG_OK) {
+    std::lock_guard<std::mutex> lock(g_map_mutex);
+    if (g_map_cache.size() >= kMapCacheCap) g_map_cache.clear();
+    g_map_cache.emplace(key, *map);
+  }
+  return rc;
+}
+
+static int make_map_uncached(CUtensorMap* map, const float* ptr, int64_t inner, int64_t rows,
+                             int64_t ld, int64_t heads, int64_t hstride, int64_t nb,
+                             int64_t bstride, uint32_t box_inner, uint32_t box_rows,
+                             CUtensorMapSwizzle swizzle) {
   EncodeFn enc = get_encode();
   if (!enc) return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: cuTensorMapEncodeTiled unavailable");
   const int64_t hs = heads > 1 ? hstride : rows * ld;
