@@ -34,9 +34,7 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 from dataclasses import dataclass, field
 from typing import Any
@@ -436,37 +434,94 @@ def run_reference(args: argparse.Namespace, wl: Workload) -> None:
 
 
 # ----------------------------------------------------------------------------- clocks
-class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+CLOCK_REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+                 ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+                 ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+                 ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
-    def __init__(self, gpu_index: int) -> None:
-        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+def sample_clocks(uuid: str, out_path: str, period: float = 0.005) -> None:
+    """Clock sampler process: every ``period`` s append ``monotonic time, SM MHz, max SM MHz,
+    clock-event reason bits`` of the GPU ``uuid`` to ``out_path`` (NVML, the fields of
+    ``nvidia-smi --query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.*``) until killed.
+    Reading them changes no setting of the GPU."""
+    import pynvml as nv
+
+    nv.nvmlInit()
+    h = nv.nvmlDeviceGetHandleByUUID(uuid)
+    mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+    with open(out_path, "w") as f:
+        while True:
+            sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+            bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+            f.write(f"{time.monotonic()},{sm},{mx},{bits}\n")
+            f.flush()
+            time.sleep(period)
+
+
+class ClockSampler:
+    """Runs ``sample_clocks`` in a child process (no contention with the launching thread)
+    and summarises the samples taken between ``begin()`` and ``end()``."""
+
+    def __init__(self, local_index: int) -> None:
+        import tempfile
+
+        self.proc = None
+        self.error = None
+        self.t0 = self.t1 = 0.0
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(gpu_index)], stdout=self.file,
-                stderr=subprocess.DEVNULL)
-        except OSError:
-            self.proc = None
+            import torch
+
+            uuid = f"GPU-{torch.cuda.get_device_properties(local_index).uuid}"
+        except Exception as exc:  # noqa: BLE001 - no UUID: no sampling, said in the line
+            self.error = f"no GPU UUID: {type(exc).__name__}"
+            return
+        fd, self.path = tempfile.mkstemp(suffix=".clocks")
+        os.close(fd)
+        import subprocess
+
+        self.proc = subprocess.Popen(
+            [sys.executable, os.path.abspath(__file__), "--sample-clocks", uuid, self.path],
+            stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        deadline = time.monotonic() + 20.0
+        while time.monotonic() < deadline and self.proc.poll() is None:
+            if os.path.getsize(self.path) > 0:
+                break
+            time.sleep(0.01)
+        if self.proc.poll() is not None:
+            self.error = "nvml sampler exited"
+
+    def begin(self) -> None:
+        self.t0 = time.monotonic()
+
+    def end(self) -> None:
+        self.t1 = time.monotonic()
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        if self.proc is None or self.error:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.error], "samples": 0}
+        time.sleep(0.02)
         self.proc.terminate()
         self.proc.wait(timeout=10)
-        self.file.seek(0)
-        rows = [r.split(", ") for r in self.file.read().strip().splitlines() if r.strip()]
-        os.unlink(self.file.name)
-        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows if len(r) >= 9 for i in range(4)
-                          if r[5 + i].strip() == "Active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(sm)}
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = line.strip().split(",")
+                if len(parts) == 4:
+                    rows.append((float(parts[0]), float(parts[1]), float(parts[2]),
+                                 int(parts[3])))
+        os.unlink(self.path)
+        inside = [r for r in rows if self.t0 <= r[0] <= self.t1]
+        if not inside:  # a timed region shorter than one period: the nearest sample after it
+            inside = [r for r in rows if r[0] >= self.t1][:1]
+        import pynvml as nv
+
+        reasons = sorted({name for *_, bits in inside for name, const in CLOCK_REASONS
+                          if bits & int(getattr(nv, const))})
+        return {"sm_mhz": statistics.median(r[1] for r in inside) if inside else None,
+                "sm_max_mhz": max(r[2] for r in inside) if inside else None,
+                "reasons": reasons, "samples": len(inside),
+                "source": "nvml every 5 ms during the timed steps"}
 
 
 # ----------------------------------------------------------------------------- our arm
@@ -498,26 +553,28 @@ def run_ours(args: argparse.Namespace, wl: Workload) -> None:
     built = wl.build(tg, device, rank, reducer_cls)
     results: list = []
 
-    def timed(k: int, fn) -> float:
+    def timed(k: int, fn, sampler: ClockSampler | None = None) -> float:
         barrier()
         tg.synchronize()
         start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if sampler is not None:
+            sampler.begin()
         start.record()
         for _ in range(k):
             fn()
         stop.record()
         stop.synchronize()
+        if sampler is not None:
+            sampler.end()
         barrier()
         return max_over_ranks(start.elapsed_time(stop) / 1e3)
 
     # Device-resident inputs: the value line.
+    clocks = ClockSampler(local)
     for _ in range(args.warmup):
         built.step(*built.dev_inputs)
-    phys = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
-    gpu_index = int(phys[local]) if len(phys) > local and phys[local].strip().isdigit() else local
-    clocks = ClockSampler(gpu_index)
     launches0 = int(lib.tg_launch_count())
-    sec = timed(args.steps, lambda: built.step(*built.dev_inputs))
+    sec = timed(args.steps, lambda: built.step(*built.dev_inputs), clocks)
     launches = int(lib.tg_launch_count()) - launches0
     clock = clocks.stop()
     # The roofline pass: the same steps again with every tensor-core GEMM bracketed by CUDA
@@ -589,6 +646,9 @@ def run_ours(args: argparse.Namespace, wl: Workload) -> None:
 
 
 def main() -> None:
+    if len(sys.argv) == 4 and sys.argv[1] == "--sample-clocks":
+        sample_clocks(sys.argv[2], sys.argv[3])
+        return
     args = parse()
     if args.gemm:
         run_gemm(args)

@@ -88,9 +88,14 @@ int tg_gemm_batched(int dtype, int trans_a, int trans_b, int64_t m, int64_t n, i
                     int64_t ldb, int64_t stride_b, double beta, void* c, int64_t ldc,
                     int64_t stride_c, int64_t batch, void* stream);
 
-/* linear (ops/layers.py:22-62): y[rows,out] = x[rows,in] @ w[out,in]^T + bias. */
+/* linear (ops/layers.py:22-62): y[rows,out] = x[rows,in] @ w[out,in]^T + bias. `scratch`
+ * (tg_linear_forward_scratch_bytes, may be NULL) holds split-K partials for outputs with few
+ * tiles and a long reduction; the partials are summed in a fixed order (deterministic). */
+size_t tg_linear_forward_scratch_bytes(int dtype, int64_t rows, int64_t in_features,
+                                       int64_t out_features);
 int tg_linear_forward(int dtype, const void* x, const void* w, const void* bias, void* y,
-                      int64_t rows, int64_t in_features, int64_t out_features, void* stream);
+                      int64_t rows, int64_t in_features, int64_t out_features, void* scratch,
+                      void* stream);
 /* linear VJP (ops/layers.py:43-49): gx = g @ w, gw = g^T @ x (+ beta_gw * gw), gb = colsum(g).
  * need bit 0 = gx, bit 1 = gw, bit 2 = gb (unset bits skip the launch). beta_gw = 1
  * accumulates into an existing gw (tied weights). `scratch` holds
@@ -250,21 +255,22 @@ int tg_attention_backward(int dtype, const tg_attn_shape* s, const void* q, cons
 
 /* ------------------------------------------------------------------ convolution / pooling
  * conv2d (ops/conv.py:128-177): cross-correlation of x (n, c, h, w) with w (c_out, c, kh, kw)
- * by an im2col patch matrix `cols` of (n*oh*ow) rows x cols_ld columns (row = image*oh*ow +
- * pixel, column = channel*kh*kw + i*kw + j, zero beyond c*kh*kw; cols_ld =
- * tg_conv2d_cols_ld(s), a multiple of 4 so the rows suit the TMA), then one GEMM per
- * direction: y = cols W^T (+ b) written straight to NCHW by the GEMM epilogue; dW = G^T cols
- * with the reduction running over images and pixels of the NCHW gradient; dcols = G W per
- * image, folded back onto dx by col2im (a gather, deterministic). `cols` is written by the
- * forward call and read by the backward call (the reference keeps it for the weight
- * gradient too, ops/conv.py:91-98, 114-116). Zero padding (ph, pw), strides (sh, sw). */
+ * by an im2col patch matrix `cols` stored patch-major: `rows` x `ld` from
+ * tg_conv2d_cols_shape (row kk = channel*kh*kw + i*kw + j, zero rows beyond c*kh*kw; column
+ * m = image*oh*ow + pixel; ld >= n*oh*ow, both multiples of 4 so the rows suit the TMA). Then
+ * one GEMM per direction: y = cols^T W^T (+ b) written straight to NCHW by the GEMM
+ * epilogue; dW = G cols^T with the reduction running over images and pixels of the NCHW
+ * gradient; dcols = W^T G per image, folded back onto dx by col2im (a gather,
+ * deterministic). `cols` is written by the forward call and read by the backward call (the
+ * reference keeps its patch matrix for the weight gradient too, ops/conv.py:91-98,
+ * 114-116). Zero padding (ph, pw), strides (sh, sw). */
 typedef struct tg_conv_shape {
   int64_t n, c, h, w;      /* input */
   int64_t c_out, kh, kw;   /* filters */
   int64_t sh, sw, ph, pw;  /* stride, zero padding */
   int64_t oh, ow;          /* output: (h + 2 ph - kh) / sh + 1, likewise ow */
 } tg_conv_shape;
-int64_t tg_conv2d_cols_ld(const tg_conv_shape* s);
+int tg_conv2d_cols_shape(const tg_conv_shape* s, int64_t* rows, int64_t* ld);
 size_t tg_conv2d_forward_scratch_bytes(int dtype, const tg_conv_shape* s);
 int tg_conv2d_forward(int dtype, const tg_conv_shape* s, const void* x, const void* w,
                       const void* b, void* y, void* cols, void* scratch, void* stream);

@@ -72,7 +72,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tg_launch_count": (ctypes.c_uint64, []),
     "tg_gemm_batched": (c_int, [c_int, c_int, c_int, i64, i64, i64, dbl, vp, i64, i64, vp, i64,
                                 i64, dbl, vp, i64, i64, i64, vp]),
-    "tg_linear_forward": (c_int, [c_int, vp, vp, vp, vp, i64, i64, i64, vp]),
+    "tg_linear_forward_scratch_bytes": (sz, [c_int, i64, i64, i64]),
+    "tg_linear_forward": (c_int, [c_int, vp, vp, vp, vp, i64, i64, i64, vp, vp]),
     "tg_linear_backward_scratch_bytes": (sz, [c_int, i64, i64, i64, u32]),
     "tg_linear_backward": (c_int, [c_int, vp, vp, vp, vp, vp, vp, i64, i64, i64, u32, dbl, vp,
                                    vp]),
@@ -108,7 +109,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tg_attention_backward_scratch_bytes": (sz, [c_int, POINTER(AttnShape)]),
     "tg_attention_backward": (c_int, [c_int, POINTER(AttnShape), vp, vp, vp, vp, vp, vp, vp, vp,
                                       vp, vp, vp]),
-    "tg_conv2d_cols_ld": (i64, [POINTER(ConvShape)]),
+    "tg_conv2d_cols_shape": (c_int, [POINTER(ConvShape), pi64, pi64]),
     "tg_conv2d_forward_scratch_bytes": (sz, [c_int, POINTER(ConvShape)]),
     "tg_conv2d_forward": (c_int, [c_int, POINTER(ConvShape), vp, vp, vp, vp, vp, vp, vp]),
     "tg_conv2d_backward_scratch_bytes": (sz, [c_int, POINTER(ConvShape), c_int]),

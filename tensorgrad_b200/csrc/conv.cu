@@ -11,6 +11,10 @@
 //             col2im as a gather over the kernel offsets (no atomics: deterministic).
 // Batch-norm statistics and the reductions of its VJP are per-channel sums accumulated in
 // float64 per thread and block, combined in chunk order (deterministic).
+#include <algorithm>
+#include <initializer_list>
+#include <type_traits>
+
 #include "common.cuh"
 #include "gemm.cuh"
 
@@ -19,7 +23,16 @@ namespace {
 
 constexpr int kThreads = 256;
 
-inline int64_t cols_ld(const tg_conv_shape& s) { return (s.c * s.kh * s.kw + 3) / 4 * 4; }
+// V consecutive elements moved as one access (16 bytes for float x 4).
+template <typename T, int V>
+struct alignas(sizeof(T) * V) Vec {
+  T v[V];
+};
+
+// Patch rows (c*kh*kw rounded up to 4: the filter matrix's rows then suit the TMA) and the
+// patch matrix's row stride (n*oh*ow rounded up to 4).
+inline int64_t patch_rows(const tg_conv_shape& s) { return (s.c * s.kh * s.kw + 3) / 4 * 4; }
+inline int64_t patch_ld(const tg_conv_shape& s) { return (s.n * s.oh * s.ow + 3) / 4 * 4; }
 
 inline size_t align256(size_t b) { return (b + 255) / 256 * 256; }
 
@@ -32,65 +45,166 @@ int check_conv(const tg_conv_shape* s, bool pool) {
   TG_CHECK_ARG(s->oh ==(s->h + 2 * s->ph - s->kh) / s->sh + 1 &&
                    s->ow == (s->w + 2 * s->pw - s->kw) / s->sw + 1 && s->oh > 0 && s->ow > 0,
                "conv2d: output size does not match the input, kernel, stride and padding");
+  TG_CHECK_ARG(s->h * s->w < INT32_MAX && s->oh * s->ow < INT32_MAX && s->kh * s->kw < 65536,
+               "conv2d: planes of at most 2^31 pixels, windows of at most 65535 cells");
   return TG_OK;
 }
 
 // ------------------------------------------------------------------ im2col / col2im
-// cols[m][kk], m = (img, oy, ox), kk = (ch, i, j) < c*kh*kw, zero elsewhere. One thread per
-// element of a row-major patch matrix: the stores are coalesced (the matrix is ~kh*kw times
-// the input, so its writes dominate the traffic).
+// The patch matrix is stored patch-major: cols[kk][m], kk = (ch, i, j) < kp (rows kk >= c*kh*kw
+// zero), m = image * oh*ow + pixel < n*oh*ow, row stride ldm (a multiple of 4).
+//
+// Index arithmetic by runtime sizes (divisions) costs more than the bytes each element moves,
+// so every kernel below fixes a thread's position inside a plane (decoded once) and walks the
+// planes (images, channels) with constant strides: the loop body is a few loads and a store.
+// Grids: x over in-plane positions (one per thread), y and z over plane ranges. In-plane
+// indices are 32-bit (the host checks planes of fewer than 2^31 pixels).
+
+// Image range [i0, i1) of block z out of gridDim.z.
+__device__ __forceinline__ void image_range(int64_t n, int64_t& i0, int64_t& i1) {
+  i0 = (int64_t)blockIdx.z * n / gridDim.z;
+  i1 = ((int64_t)blockIdx.z + 1) * n / gridDim.z;
+}
+
+// Grid (pixel blocks, patch rows, image ranges). Consecutive threads take consecutive output
+// pixels: stores are whole lines and (for stride 1) loads are unit-stride runs of x.
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
-im2col_kernel(const T* __restrict__ x, T* __restrict__ cols, tg_conv_shape s, int64_t ld) {
-  const int64_t total = s.n * s.oh * s.ow * ld;
-  const int64_t K = s.c * s.kh * s.kw;
-  const int64_t khw = s.kh * s.kw, ohw = s.oh * s.ow;
-  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t m = idx / ld, kk = idx - m * ld;
-    T v = T(0);
-    if (kk < K) {
-      const int64_t ch = kk / khw, r = kk - ch * khw;
-      const int64_t i = r / s.kw, j = r - i * s.kw;
-      const int64_t img = m / ohw, p = m - img * ohw;
-      const int64_t oy = p / s.ow, ox = p - oy * s.ow;
-      const int64_t iy = oy * s.sh - s.ph + i, ix = ox * s.sw - s.pw + j;
-      if (iy >= 0 && iy < s.h && ix >= 0 && ix < s.w)
-        v = x[((img * s.c + ch) * s.h + iy) * s.w + ix];
+im2col_kernel(const T* __restrict__ x, T* __restrict__ cols, tg_conv_shape s, int64_t K,
+              int64_t kp, int64_t ldm) {
+  const int ohw = (int)(s.oh * s.ow);
+  const int p = blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= ohw) return;
+  const int ow = (int)s.ow, h = (int)s.h, w = (int)s.w;
+  const int oy = p / ow, ox = p - oy * ow;
+  const int khw = (int)(s.kh * s.kw), kw = (int)s.kw;
+  const int64_t plane = (int64_t)h * w, img_stride = s.c * plane;
+  int64_t i0, i1;
+  image_range(s.n, i0, i1);
+  for (int64_t kk = blockIdx.y; kk < kp; kk += gridDim.y) {
+    T* out = cols + kk * ldm + p;
+    bool live = kk < K;
+    int64_t src = 0;
+    if (live) {
+      const int64_t ch = kk / khw;
+      const int r = (int)(kk - ch * khw), i = r / kw, j = r - i * kw;
+      const int iy = oy * (int)s.sh - (int)s.ph + i, ix = ox * (int)s.sw - (int)s.pw + j;
+      live = iy >= 0 && iy < h && ix >= 0 && ix < w;
+      src = ch * plane + (int64_t)iy * w + ix;
     }
-    cols[idx] = v;
+    if (live) {
+#pragma unroll 4
+      for (int64_t img = i0; img < i1; ++img) out[img * ohw] = x[img * img_stride + src];
+    } else {
+#pragma unroll 4
+      for (int64_t img = i0; img < i1; ++img) out[img * ohw] = T(0);
+    }
   }
 }
 
 // dx[img][ch][y][x] = sum over kernel offsets (i, j) whose window covers (y, x) of
-// dcols[(img, oy, ox)][(ch, i, j)], in ascending (i, j) (the reference's col2im order).
+// dcols[(ch, i, j)][(img, oy, ox)], in ascending (i, j) (the reference's col2im order).
+// Grid (pixel blocks, channels, image ranges). The covering windows of a pixel are the same
+// for every image and channel: found once, as an output row per kernel row and an output
+// column per kernel column (-1: no window), for windows of up to MAXW x MAXW.
+template <typename T, int MAXW>
+__global__ void __launch_bounds__(kThreads)
+col2im_kernel(const T* __restrict__ dcols, T* __restrict__ gx, tg_conv_shape s, int64_t ldm) {
+  const int hw = (int)(s.h * s.w);
+  const int q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= hw) return;
+  const int w = (int)s.w, yh = q / w, xw = q - yh * w;
+  const int kh = (int)s.kh, kw = (int)s.kw, sh = (int)s.sh, sw = (int)s.sw;
+  const int oh = (int)s.oh, ow = (int)s.ow, ohw = oh * ow;
+  int oyv[MAXW], oxv[MAXW];
+#pragma unroll
+  for (int i = 0; i < MAXW; ++i) {
+    const int ty = yh + (int)s.ph - i;
+    oyv[i] = (i < kh && ty >= 0 && ty % sh == 0 && ty / sh < oh) ? ty / sh : -1;
+  }
+#pragma unroll
+  for (int j = 0; j < MAXW; ++j) {
+    const int tx = xw + (int)s.pw - j;
+    oxv[j] = (j < kw && tx >= 0 && tx % sw == 0 && tx / sw < ow) ? tx / sw : -1;
+  }
+  int64_t i0, i1;
+  image_range(s.n, i0, i1);
+  for (int64_t ch = blockIdx.y; ch < s.c; ch += gridDim.y) {
+    const T* base = dcols + ch * kh * kw * ldm;
+    for (int64_t img = i0; img < i1; ++img) {
+      const T* bi = base + img * ohw;
+      T acc = T(0);
+#pragma unroll
+      for (int i = 0; i < MAXW; ++i) {
+        if (oyv[i] < 0) continue;
+#pragma unroll
+        for (int j = 0; j < MAXW; ++j) {
+          if (oxv[j] < 0) continue;
+          acc += bi[(int64_t)(i * kw + j) * ldm + oyv[i] * ow + oxv[j]];
+        }
+      }
+      gx[(img * s.c + ch) * hw + q] = acc;
+    }
+  }
+}
+
+// The same for windows larger than 16 x 16: the covering windows found per image.
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
-col2im_kernel(const T* __restrict__ dcols, T* __restrict__ gx, tg_conv_shape s, int64_t ld) {
-  const int64_t total = s.n * s.c * s.h * s.w;
-  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t xw = idx % s.w;
-    int64_t rest = idx / s.w;
-    const int64_t yh = rest % s.h;
-    rest /= s.h;
-    const int64_t ch = rest % s.c, img = rest / s.c;
-    T acc = T(0);
-    for (int64_t i = 0; i < s.kh; ++i) {
-      const int64_t ty = yh + s.ph - i;
-      if (ty < 0 || ty % s.sh) continue;
-      const int64_t oy = ty / s.sh;
-      if (oy >= s.oh) continue;
-      for (int64_t j = 0; j < s.kw; ++j) {
-        const int64_t tx = xw + s.pw - j;
-        if (tx < 0 || tx % s.sw) continue;
-        const int64_t ox = tx / s.sw;
-        if (ox >= s.ow) continue;
-        acc += dcols[((img * s.oh + oy) * s.ow + ox) * ld + (ch * s.kh + i) * s.kw + j];
+col2im_large_kernel(const T* __restrict__ dcols, T* __restrict__ gx, tg_conv_shape s,
+                    int64_t ldm) {
+  const int hw = (int)(s.h * s.w);
+  const int q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= hw) return;
+  const int w = (int)s.w, yh = q / w, xw = q - yh * w;
+  const int kh = (int)s.kh, kw = (int)s.kw, sh = (int)s.sh, sw = (int)s.sw;
+  const int oh = (int)s.oh, ow = (int)s.ow, ohw = oh * ow;
+  int64_t i0, i1;
+  image_range(s.n, i0, i1);
+  for (int64_t ch = blockIdx.y; ch < s.c; ch += gridDim.y) {
+    const T* base = dcols + ch * kh * kw * ldm;
+    for (int64_t img = i0; img < i1; ++img) {
+      T acc = T(0);
+      for (int i = 0; i < kh; ++i) {
+        const int ty = yh + (int)s.ph - i;
+        if (ty < 0 || ty % sh || ty / sh >= oh) continue;
+        for (int j = 0; j < kw; ++j) {
+          const int tx = xw + (int)s.pw - j;
+          if (tx < 0 || tx % sw || tx / sw >= ow) continue;
+          acc += base[(int64_t)(i * kw + j) * ldm + img * ohw + (ty / sh) * ow + tx / sw];
+        }
       }
+      gx[(img * s.c + ch) * hw + q] = acc;
     }
-    gx[idx] = acc;
   }
+}
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline unsigned clamp_grid(int64_t v, int64_t cap) { return (unsigned)(v < 1 ? 1 : v > cap ? cap : v); }
+
+// About 16 resident-sized blocks per SM in total: enough to cover the memory latency, while
+// each block loops over many planes (a block per plane would be too little work to pay for
+// its own launch).
+constexpr int64_t kGridTarget = 148 * 16;
+
+// x over in-plane positions (one per thread), y (and z) over plane ranges: about
+// kGridTarget blocks in all, each plane range walked by one block.
+inline dim3 position_grid(int64_t positions, int64_t ranges_y, int64_t ranges_z = 1) {
+  const int64_t x = ceil_div(positions, kThreads);
+  const int64_t y = std::min<int64_t>(ranges_y, 65535);
+  const int64_t want_z = ceil_div(kGridTarget, x * y);
+  const int64_t z = std::max<int64_t>(1, std::min<int64_t>({want_z, ranges_z, 65535}));
+  if (ranges_z > 1) return dim3((unsigned)x, (unsigned)y, (unsigned)z);
+  const int64_t yy = std::max<int64_t>(1, std::min<int64_t>({ceil_div(kGridTarget, x), ranges_y,
+                                                            65535}));
+  return dim3((unsigned)x, (unsigned)yy, 1);
+}
+
+// x over groups of a plane (kThreads per block, at most 16 blocks), y over planes.
+inline dim3 plane_grid(int64_t groups, int64_t planes) {
+  const unsigned x = clamp_grid(ceil_div(groups, kThreads), 16);
+  return dim3(x, clamp_grid(planes < ceil_div(kGridTarget, x) ? planes : ceil_div(kGridTarget, x),
+                            65535));
 }
 
 // W (c_out, K) -> Wp (c_out, ld) with zero columns K..ld-1.
@@ -114,7 +228,7 @@ __global__ void pad_rows_kernel(const T* __restrict__ w, T* __restrict__ wp, int
 //   MODE_SUM  : sum g (second slot 0).
 enum { MODE_STATS = 0, MODE_GRAD = 1, MODE_SUM = 2 };
 
-template <typename T, int MODE>
+template <typename T, int MODE, int V>
 __global__ void __launch_bounds__(kThreads)
 channel_sums_kernel(const T* __restrict__ a, const T* __restrict__ x, const T* __restrict__ mean,
                     int64_t n, int64_t C, int64_t hw, int chunks, double* __restrict__ partial) {
@@ -126,19 +240,28 @@ channel_sums_kernel(const T* __restrict__ a, const T* __restrict__ x, const T* _
   if (MODE == MODE_STATS) shift = (double)a[ch * hw];
   if (MODE == MODE_GRAD) shift = (double)mean[ch];
   double s0 = 0.0, s1 = 0.0;
+  const int64_t nv = hw / V;
   for (int64_t img = i0; img < i1; ++img) {
     const int64_t base = (img * C + ch) * hw;
-    for (int64_t j = threadIdx.x; j < hw; j += blockDim.x) {
-      const double v = (double)a[base + j];
-      if (MODE == MODE_STATS) {
-        const double d = v - shift;
-        s0 += d;
-        s1 += d * d;
-      } else if (MODE == MODE_GRAD) {
-        s0 += v;
-        s1 += v * ((double)x[base + j] - shift);
-      } else {
-        s0 += v;
+    const Vec<T, V>* av = reinterpret_cast<const Vec<T, V>*>(a + base);
+    const Vec<T, V>* xv = reinterpret_cast<const Vec<T, V>*>(MODE == MODE_GRAD ? x + base : a + base);
+    for (int64_t j = threadIdx.x; j < nv; j += blockDim.x) {
+      const Vec<T, V> va = av[j];
+      Vec<T, V> vx;
+      if (MODE == MODE_GRAD) vx = xv[j];
+#pragma unroll
+      for (int e = 0; e < V; ++e) {
+        const double v = (double)va.v[e];
+        if (MODE == MODE_STATS) {
+          const double d = v - shift;
+          s0 += d;
+          s1 += d * d;
+        } else if (MODE == MODE_GRAD) {
+          s0 += v;
+          s1 += v * ((double)vx.v[e] - shift);
+        } else {
+          s0 += v;
+        }
       }
     }
   }
@@ -183,18 +306,31 @@ __global__ void bn_stats_final_kernel(const double* __restrict__ partial, int ch
   }
 }
 
-template <typename T>
+// Grid: x over V-element groups of a plane (image, channel), y over planes; the channel's
+// statistics are loaded once per plane.
+template <typename T, int V>
 __global__ void __launch_bounds__(kThreads)
 bn_apply_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ b,
                 const T* __restrict__ mean, const T* __restrict__ rstd, T* __restrict__ y,
-                int64_t total, int64_t C, int64_t hw) {
-  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t ch = (idx / hw) % C;
-    T v = (x[idx] - mean[ch]) * rstd[ch];
-    if (w) v = v * w[ch];
-    if (b) v = v + b[ch];
-    y[idx] = v;
+                int64_t planes, int64_t C, int64_t hw) {
+  const int64_t nv = hw / V;
+  for (int64_t plane = blockIdx.y; plane < planes; plane += gridDim.y) {
+    const int64_t ch = plane % C;
+    const T mu = mean[ch], r = rstd[ch];
+    const Vec<T, V>* xv = reinterpret_cast<const Vec<T, V>*>(x + plane * hw);
+    Vec<T, V>* yv = reinterpret_cast<Vec<T, V>*>(y + plane * hw);
+    for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < nv;
+         j += (int64_t)gridDim.x * blockDim.x) {
+      Vec<T, V> v = xv[j];
+#pragma unroll
+      for (int e = 0; e < V; ++e) {
+        T t = (v.v[e] - mu) * r;
+        if (w) t = t * w[ch];
+        if (b) t = t + b[ch];
+        v.v[e] = t;
+      }
+      yv[j] = v;
+    }
   }
 }
 
@@ -223,17 +359,31 @@ __global__ void bn_grad_final_kernel(const double* __restrict__ partial, int chu
   }
 }
 
-template <typename T>
+template <typename T, int V>
 __global__ void __launch_bounds__(kThreads)
 bn_grad_input_kernel(const T* __restrict__ g, const T* __restrict__ x,
                      const T* __restrict__ mean, const T* __restrict__ rstd,
-                     const T* __restrict__ coef, T* __restrict__ gx, int64_t total, int64_t C,
+                     const T* __restrict__ coef, T* __restrict__ gx, int64_t planes, int64_t C,
                      int64_t hw) {
-  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t ch = (idx / hw) % C;
-    const T xhat = (x[idx] - mean[ch]) * rstd[ch];
-    gx[idx] = coef[3 * ch] * (g[idx] - coef[3 * ch + 1] - xhat * coef[3 * ch + 2]);
+  const int64_t nv = hw / V;
+  for (int64_t plane = blockIdx.y; plane < planes; plane += gridDim.y) {
+    const int64_t ch = plane % C;
+    const T mu = mean[ch], r = rstd[ch];
+    const T k0 = coef[3 * ch], k1 = coef[3 * ch + 1], k2 = coef[3 * ch + 2];
+    const Vec<T, V>* gv = reinterpret_cast<const Vec<T, V>*>(g + plane * hw);
+    const Vec<T, V>* xv = reinterpret_cast<const Vec<T, V>*>(x + plane * hw);
+    Vec<T, V>* ov = reinterpret_cast<Vec<T, V>*>(gx + plane * hw);
+    for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < nv;
+         j += (int64_t)gridDim.x * blockDim.x) {
+      const Vec<T, V> a = gv[j], xx = xv[j];
+      Vec<T, V> o;
+#pragma unroll
+      for (int e = 0; e < V; ++e) {
+        const T xhat = (xx.v[e] - mu) * r;
+        o.v[e] = k0 * (a.v[e] - k1 - xhat * k2);
+      }
+      ov[j] = o;
+    }
   }
 }
 
@@ -251,69 +401,118 @@ __global__ void channel_total_kernel(const double* __restrict__ partial, int chu
 template <typename T>
 __device__ __forceinline__ bool is_nan(T v) { return v != v; }
 
-template <typename T>
-__global__ void __launch_bounds__(kThreads)
-maxpool_fwd_kernel(const T* __restrict__ x, T* __restrict__ y, uint8_t* __restrict__ arg,
-                   tg_conv_shape s) {
-  const int64_t total = s.n * s.c * s.oh * s.ow;
-  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t ox = idx % s.ow;
-    int64_t rest = idx / s.ow;
-    const int64_t oy = rest % s.oh;
-    const int64_t plane = rest / s.oh;
-    const T* xp = x + plane * s.h * s.w;
-    T best = T(0);
-    int bk = -1;
-    for (int64_t i = 0; i < s.kh; ++i) {
-      const int64_t iy = oy * s.sh - s.ph + i;
-      for (int64_t j = 0; j < s.kw; ++j) {
-        const int64_t ix = ox * s.sw - s.pw + j;
-        const bool inside = iy >= 0 && iy < s.h && ix >= 0 && ix < s.w;
-        const T v = inside ? xp[iy * s.w + ix] : T(-INFINITY);
-        // First maximum in row-major order; a NaN wins and stays.
-        if (bk < 0 || v > best || (is_nan(v) && !is_nan(best))) {
-          best = v;
-          bk = (int)(i * s.kw + j);
-        }
-      }
-    }
-    y[idx] = best;
-    arg[idx] = (uint8_t)bk;
-  }
+// Pooling grids: x over in-plane positions (one per thread, decoded once), y over plane
+// (image, channel) ranges.
+__device__ __forceinline__ void plane_range(int64_t planes, int64_t& p0, int64_t& p1) {
+  p0 = (int64_t)blockIdx.y * planes / gridDim.y;
+  p1 = ((int64_t)blockIdx.y + 1) * planes / gridDim.y;
 }
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
-maxpool_bwd_kernel(const T* __restrict__ g, const uint8_t* __restrict__ arg, T* __restrict__ gx,
+maxpool_fwd_kernel(const T* __restrict__ x, T* __restrict__ y, uint8_t* __restrict__ arg,
                    tg_conv_shape s) {
-  const int64_t total = s.n * s.c * s.h * s.w;
-  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t xw = idx % s.w;
-    int64_t rest = idx / s.w;
-    const int64_t yh = rest % s.h;
-    const int64_t plane = rest / s.h;
-    // Windows (oy, ox) whose cell (i, j) = (yh + ph - oy*sh, xw + pw - ox*sw) is in range.
-    int64_t oy0 = yh + s.ph - s.kh + 1;
-    oy0 = oy0 <= 0 ? 0 : (oy0 + s.sh - 1) / s.sh;
-    int64_t oy1 = (yh + s.ph) / s.sh;
-    if (oy1 > s.oh - 1) oy1 = s.oh - 1;
-    int64_t ox0 = xw + s.pw - s.kw + 1;
-    ox0 = ox0 <= 0 ? 0 : (ox0 + s.sw - 1) / s.sw;
-    int64_t ox1 = (xw + s.pw) / s.sw;
-    if (ox1 > s.ow - 1) ox1 = s.ow - 1;
-    T acc = T(0);
-    for (int64_t oy = oy0; oy <= oy1; ++oy) {
-      const int64_t i = yh + s.ph - oy * s.sh;
-      for (int64_t ox = ox0; ox <= ox1; ++ox) {
-        const int64_t j = xw + s.pw - ox * s.sw;
-        const int64_t o = (plane * s.oh + oy) * s.ow + ox;
-        if ((int64_t)arg[o] == i * s.kw + j) acc += g[o];
+  const int ohw = (int)(s.oh * s.ow);
+  const int o = blockIdx.x * blockDim.x + threadIdx.x;
+  if (o >= ohw) return;
+  const int h = (int)s.h, w = (int)s.w, ow = (int)s.ow, hw = h * w;
+  const int kh = (int)s.kh, kw = (int)s.kw;
+  const int oy = o / ow, ox = o - oy * ow;
+  const int iy0 = oy * (int)s.sh - (int)s.ph, ix0 = ox * (int)s.sw - (int)s.pw;
+  int64_t p0, p1;
+  plane_range(s.n * s.c, p0, p1);
+  for (int64_t plane = p0; plane < p1; ++plane) {
+    const T* xp = x + plane * hw;
+    T best = T(0);
+    int bk = -1;
+    for (int i = 0; i < kh; ++i) {
+      const int iy = iy0 + i;
+      for (int j = 0; j < kw; ++j) {
+        const int ix = ix0 + j;
+        const bool inside = iy >= 0 && iy < h && ix >= 0 && ix < w;
+        const T v = inside ? xp[iy * w + ix] : T(-INFINITY);
+        // First maximum in row-major order; a NaN wins and stays.
+        if (bk < 0 || v > best || (is_nan(v) && !is_nan(best))) {
+          best = v;
+          bk = i * kw + j;
+        }
       }
     }
-    gx[idx] = acc;
+    y[plane * ohw + o] = best;
+    arg[plane * ohw + o] = (uint8_t)bk;
   }
+}
+
+// gx[cell] = sum of g over the windows whose winner is that cell. With windows that do not
+// overlap (stride >= kernel) a cell lies in at most one window: one load of its winner byte.
+template <typename T, bool DISJOINT>
+__global__ void __launch_bounds__(kThreads)
+maxpool_bwd_kernel(const T* __restrict__ g, const uint8_t* __restrict__ arg, T* __restrict__ gx,
+                   tg_conv_shape s) {
+  const int h = (int)s.h, w = (int)s.w, hw = h * w;
+  const int q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= hw) return;
+  const int oh = (int)s.oh, ow = (int)s.ow, ohw = oh * ow;
+  const int kh = (int)s.kh, kw = (int)s.kw, sh = (int)s.sh, sw = (int)s.sw;
+  const int ph = (int)s.ph, pw = (int)s.pw;
+  const int yh = q / w, xw = q - yh * w;
+  int64_t p0, p1;
+  plane_range(s.n * s.c, p0, p1);
+  if (DISJOINT) {
+    const int oy = (yh + ph) / sh, ox = (xw + pw) / sw;
+    const int i = yh + ph - oy * sh, j = xw + pw - ox * sw;
+    const bool covered = oy < oh && ox < ow && i < kh && j < kw;
+    const int o = covered ? oy * ow + ox : 0, cell = i * kw + j;
+    for (int64_t plane = p0; plane < p1; ++plane) {
+      T v = T(0);
+      if (covered && (int)arg[plane * ohw + o] == cell) v = g[plane * ohw + o];
+      gx[plane * hw + q] = v;
+    }
+  } else {
+    // Windows (oy, ox) whose cell (i, j) = (yh + ph - oy*sh, xw + pw - ox*sw) is in range.
+    int oy0 = yh + ph - kh + 1;
+    oy0 = oy0 <= 0 ? 0 : (oy0 + sh - 1) / sh;
+    const int oy1 = min((yh + ph) / sh, oh - 1);
+    int ox0 = xw + pw - kw + 1;
+    ox0 = ox0 <= 0 ? 0 : (ox0 + sw - 1) / sw;
+    const int ox1 = min((xw + pw) / sw, ow - 1);
+    for (int64_t plane = p0; plane < p1; ++plane) {
+      const T* gp = g + plane * ohw;
+      const uint8_t* ap = arg + plane * ohw;
+      T acc = T(0);
+      for (int oy = oy0; oy <= oy1; ++oy) {
+        const int i = yh + ph - oy * sh;
+        for (int ox = ox0; ox <= ox1; ++ox) {
+          const int j = xw + pw - ox * sw;
+          const int o = oy * ow + ox;
+          if ((int)ap[o] == i * kw + j) acc += gp[o];
+        }
+      }
+      gx[plane * hw + q] = acc;
+    }
+  }
+}
+
+// Per-plane kernels take 16-byte groups when T is float, planes hold a multiple of 4 elements
+// and every buffer is 16-byte aligned.
+template <typename T>
+bool plane_vec4(int64_t hw, std::initializer_list<const void*> ptrs) {
+  if (!std::is_same<T, float>::value || hw % 4) return false;
+  for (const void* p : ptrs)
+    if (p && (reinterpret_cast<uintptr_t>(p) & 15)) return false;
+  return true;
+}
+
+template <typename T, int MODE>
+void launch_channel_sums(const T* a, const T* x, const T* mean, int64_t n, int64_t C,
+                         int64_t hw, int chunks, double* partial, cudaStream_t st) {
+  const dim3 grid(chunks, (unsigned)C);
+  if (plane_vec4<T>(hw, {a, x}))
+    channel_sums_kernel<T, MODE, 4><<<grid, kThreads, 0, st>>>(a, x, mean, n, C, hw, chunks,
+                                                               partial);
+  else
+    channel_sums_kernel<T, MODE, 1><<<grid, kThreads, 0, st>>>(a, x, mean, n, C, hw, chunks,
+                                                               partial);
 }
 
 // ------------------------------------------------------------------ scratch layout
@@ -323,12 +522,12 @@ struct ConvScratch {
 
 ConvScratch conv_bwd_layout(int dtype, const tg_conv_shape& s, bool need_gx) {
   const size_t es = dtype == TG_F64 ? 8 : 4;
-  const int64_t ld = cols_ld(s), K = s.c * s.kh * s.kw;
+  const int64_t kp = patch_rows(s), K = s.c * s.kh * s.kw;
   ConvScratch L{};
-  L.wpad = (ld != K) ? align256((size_t)(s.c_out * ld) * es) : 0;
+  L.wpad = (kp != K) ? align256((size_t)(s.c_out * kp) * es) : 0;
   // Split-K partials of dW: up to one split per SM.
-  L.ws = dtype == TG_F32 ? align256((size_t)148 * (size_t)(s.c_out * K) * sizeof(float)) : 0;
-  L.dcols = need_gx ? align256((size_t)(s.n * s.oh * s.ow * ld) * es) : 0;
+  L.ws = dtype == TG_F32 ? align256((size_t)148 * (size_t)(s.c_out * kp) * sizeof(float)) : 0;
+  L.dcols = need_gx ? align256((size_t)(kp * patch_ld(s)) * es) : 0;
   L.partial = align256((size_t)s.c_out * chunks_for(s.n, s.c_out) * 2 * sizeof(double));
   L.total = L.wpad + L.ws + L.dcols + L.partial;
   return L;
@@ -341,13 +540,18 @@ using namespace tg;
 
 extern "C" {
 
-int64_t tg_conv2d_cols_ld(const tg_conv_shape* s) { return s ? cols_ld(*s) : 0; }
+int tg_conv2d_cols_shape(const tg_conv_shape* s, int64_t* rows, int64_t* ld) {
+  TG_CHECK_ARG(s && rows && ld, "conv2d: null argument");
+  *rows = patch_rows(*s);
+  *ld = patch_ld(*s);
+  return TG_OK;
+}
 
 size_t tg_conv2d_forward_scratch_bytes(int dtype, const tg_conv_shape* s) {
   if (!s) return 0;
   const size_t es = dtype == TG_F64 ? 8 : 4;
-  const int64_t ld = cols_ld(*s), K = s->c * s->kh * s->kw;
-  return ld != K ? align256((size_t)(s->c_out * ld) * es) : 16;
+  const int64_t kp = patch_rows(*s), K = s->c * s->kh * s->kw;
+  return kp != K ? align256((size_t)(s->c_out * kp) * es) : 16;
 }
 
 int tg_conv2d_forward(int dtype, const tg_conv_shape* s, const void* x, const void* w,
@@ -355,31 +559,33 @@ int tg_conv2d_forward(int dtype, const tg_conv_shape* s, const void* x, const vo
   int rc = check_conv(s, false);
   if (rc) return rc;
   cudaStream_t st = as_stream(stream);
-  const int64_t ld = cols_ld(*s), K = s->c * s->kh * s->kw;
+  const int64_t kp = patch_rows(*s), ldm = patch_ld(*s), K = s->c * s->kh * s->kw;
   const int64_t rows = s->n * s->oh * s->ow, ohw = s->oh * s->ow;
   if (rows == 0) return TG_OK;
-  TG_CHECK_ARG(ld == K || scratch, "conv2d: scratch required");
+  TG_CHECK_ARG(kp == K || scratch, "conv2d: scratch required");
   return TG_DISPATCH_FLOAT(dtype, T, [&] {
-    im2col_kernel<T><<<grid_for(rows * ld, kThreads, 148 * 64), kThreads, 0, st>>>(
-        (const T*)x, (T*)cols, *s, ld);
+    const dim3 grid = position_grid(ohw, kp, s->n);
+    im2col_kernel<T><<<grid, kThreads, 0, st>>>((const T*)x, (T*)cols, *s, K, kp, ldm);
     int launched = 1;
     const T* wk = (const T*)w;
-    if (ld != K) {
-      pad_rows_kernel<T><<<grid_for(s->c_out * ld, kThreads), kThreads, 0, st>>>(
-          (const T*)w, (T*)scratch, s->c_out, K, ld);
+    if (kp != K) {
+      pad_rows_kernel<T><<<grid_for(s->c_out * kp, kThreads), kThreads, 0, st>>>(
+          (const T*)w, (T*)scratch, s->c_out, K, kp);
       wk = (const T*)scratch;
       ++launched;
     }
     int r = check_launch("conv2d(im2col)", launched);
     if (r) return r;
+    // y(image*ohw + pixel, channel) = sum_kk cols[kk][m] W[channel][kk] + b: A is the
+    // patch matrix read MN-major, the epilogue writes NCHW.
     GemmArgs<T> p{};
-    p.m = rows; p.n = s->c_out; p.k = ld;
-    p.a = (const T*)cols; p.lda = ld; p.stride_a = 0;
-    p.b = wk; p.ldb = ld; p.stride_b = 0;
+    p.m = rows; p.n = s->c_out; p.k = kp;
+    p.a = (const T*)cols; p.lda = ldm; p.stride_a = 0;
+    p.b = wk; p.ldb = kp; p.stride_b = 0;
     p.c = (T*)y; p.ldc = ohw; p.stride_c = s->c_out * ohw;
     p.bias = (const T*)b;
     p.alpha = T(1); p.beta = T(0);
-    p.trans_a = 0; p.trans_b = 1;
+    p.trans_a = 1; p.trans_b = 1;
     p.batch = 1;
     p.c_hw = ohw;
     return gemm_run<T>(p, st);
@@ -398,7 +604,7 @@ int tg_conv2d_backward(int dtype, const tg_conv_shape* s, const void* g, const v
   int rc = check_conv(s, false);
   if (rc) return rc;
   cudaStream_t st = as_stream(stream);
-  const int64_t ld = cols_ld(*s), K = s->c * s->kh * s->kw;
+  const int64_t kp = patch_rows(*s), ldm = patch_ld(*s), K = s->c * s->kh * s->kw;
   const int64_t rows = s->n * s->oh * s->ow, ohw = s->oh * s->ow;
   const ConvScratch L = conv_bwd_layout(dtype, *s, gx != nullptr);
   TG_CHECK_ARG(L.total == 0 || scratch, "conv2d backward: scratch required");
@@ -411,13 +617,16 @@ int tg_conv2d_backward(int dtype, const tg_conv_shape* s, const void* g, const v
       return check_launch("conv2d backward(empty)", 0);
     }
     if (gw) {
+      // dW[channel][kk] = sum over (image, pixel) of G[image][channel][pixel] cols[kk][m]:
+      // both operands K-major, A folded over the images of the NCHW gradient. The product
+      // has kp columns; columns K..kp-1 (zero patch rows) are not stored.
       GemmArgs<T> p{};
       p.m = s->c_out; p.n = K; p.k = rows;
       p.a = (const T*)g; p.lda = ohw; p.stride_a = s->c_out * ohw; p.a_fold = ohw;
-      p.b = (const T*)cols; p.ldb = ld; p.stride_b = 0;
+      p.b = (const T*)cols; p.ldb = ldm; p.stride_b = 0;
       p.c = (T*)gw; p.ldc = K; p.stride_c = 0;
       p.alpha = T(1); p.beta = T(0);
-      p.trans_a = 0; p.trans_b = 0;
+      p.trans_a = 0; p.trans_b = 1;
       p.batch = 1;
       if (L.ws) {
         p.workspace = reinterpret_cast<float*>(base + L.wpad);
@@ -429,8 +638,8 @@ int tg_conv2d_backward(int dtype, const tg_conv_shape* s, const void* g, const v
     if (gb) {
       const int chunks = chunks_for(s->n, s->c_out);
       double* partial = reinterpret_cast<double*>(base + L.wpad + L.ws + L.dcols);
-      channel_sums_kernel<T, MODE_SUM><<<dim3(chunks, (unsigned)s->c_out), kThreads, 0, st>>>(
-          (const T*)g, nullptr, nullptr, s->n, s->c_out, ohw, chunks, partial);
+      launch_channel_sums<T, MODE_SUM>((const T*)g, nullptr, nullptr, s->n, s->c_out, ohw,
+                                       chunks, partial, st);
       channel_total_kernel<T><<<(unsigned)((s->c_out + 127) / 128), 128, 0, st>>>(
           partial, chunks, s->c_out, (T*)gb);
       int r = check_launch("conv2d backward(bias)", 2);
@@ -438,26 +647,38 @@ int tg_conv2d_backward(int dtype, const tg_conv_shape* s, const void* g, const v
     }
     if (gx) {
       const T* wk = (const T*)w;
-      if (ld != K) {
-        pad_rows_kernel<T><<<grid_for(s->c_out * ld, kThreads), kThreads, 0, st>>>(
-            (const T*)w, (T*)base, s->c_out, K, ld);
+      if (kp != K) {
+        pad_rows_kernel<T><<<grid_for(s->c_out * kp, kThreads), kThreads, 0, st>>>(
+            (const T*)w, (T*)base, s->c_out, K, kp);
         int r = check_launch("conv2d backward(pad)");
         if (r) return r;
         wk = (const T*)base;
       }
+      // dcols[kk][image*ohw + pixel] = sum_ch G[image][ch][pixel] W[ch][kk], per image: rows
+      // = pixels (A = the image's gradient, MN-major), columns = patch rows (B = W, shared),
+      // written column-major by the NCHW epilogue so the patch-major layout comes out.
       T* dcols = reinterpret_cast<T*>(base + L.wpad + L.ws);
       GemmArgs<T> p{};
-      p.m = ohw; p.n = ld; p.k = s->c_out;
+      p.m = ohw; p.n = kp; p.k = s->c_out;
       p.a = (const T*)g; p.lda = ohw; p.stride_a = s->c_out * ohw;
-      p.b = wk; p.ldb = ld; p.stride_b = 0;
-      p.c = dcols; p.ldc = ld; p.stride_c = ohw * ld;
+      p.b = wk; p.ldb = kp; p.stride_b = 0;
+      p.c = dcols; p.ldc = ldm; p.stride_c = 0; p.stride_ch = ohw;
       p.alpha = T(1); p.beta = T(0);
       p.trans_a = 1; p.trans_b = 0;
       p.batch = s->n;
+      p.c_hw = ohw;
       int r = gemm_run<T>(p, st);
       if (r) return r;
-      col2im_kernel<T><<<grid_for(s->n * s->c * s->h * s->w, kThreads, 148 * 64), kThreads, 0,
-                         st>>>(dcols, (T*)gx, *s, ld);
+      const dim3 grid = position_grid(s->h * s->w, s->c, s->n);
+      const int64_t win = std::max(s->kh, s->kw);
+      if (win <= 3)
+        col2im_kernel<T, 3><<<grid, kThreads, 0, st>>>(dcols, (T*)gx, *s, ldm);
+      else if (win <= 7)
+        col2im_kernel<T, 7><<<grid, kThreads, 0, st>>>(dcols, (T*)gx, *s, ldm);
+      else if (win <= 16)
+        col2im_kernel<T, 16><<<grid, kThreads, 0, st>>>(dcols, (T*)gx, *s, ldm);
+      else
+        col2im_large_kernel<T><<<grid, kThreads, 0, st>>>(dcols, (T*)gx, *s, ldm);
       r = check_launch("conv2d backward(col2im)");
       if (r) return r;
     }
@@ -480,16 +701,20 @@ int tg_batch_norm_forward(int dtype, int64_t n, int64_t c, int64_t hw, const voi
   cudaStream_t st = as_stream(stream);
   const int chunks = chunks_for(n, c);
   double* partial = reinterpret_cast<double*>(scratch);
-  const int64_t total = n * c * hw;
   return TG_DISPATCH_FLOAT(dtype, T, [&] {
-    channel_sums_kernel<T, MODE_STATS><<<dim3(chunks, (unsigned)c), kThreads, 0, st>>>(
-        (const T*)x, nullptr, nullptr, n, c, hw, chunks, partial);
+    launch_channel_sums<T, MODE_STATS>((const T*)x, nullptr, nullptr, n, c, hw, chunks, partial,
+                                       st);
     bn_stats_final_kernel<T><<<(unsigned)((c + 127) / 128), 128, 0, st>>>(
         partial, chunks, (const T*)x, c, hw, (double)(n * hw), (T*)mean, (T*)rstd,
         (T*)running_mean, (T*)running_var, momentum, eps);
-    bn_apply_kernel<T><<<grid_for(total, kThreads, 148 * 64), kThreads, 0, st>>>(
-        (const T*)x, (const T*)w, (const T*)b, (const T*)mean, (const T*)rstd, (T*)y, total, c,
-        hw);
+    if (plane_vec4<T>(hw, {x, y}))
+      bn_apply_kernel<T, 4><<<plane_grid(hw / 4, n * c), kThreads, 0, st>>>(
+          (const T*)x, (const T*)w, (const T*)b, (const T*)mean, (const T*)rstd, (T*)y, n * c,
+          c, hw);
+    else
+      bn_apply_kernel<T, 1><<<plane_grid(hw, n * c), kThreads, 0, st>>>(
+          (const T*)x, (const T*)w, (const T*)b, (const T*)mean, (const T*)rstd, (T*)y, n * c,
+          c, hw);
     return check_launch("batch_norm", 3);
   });
 }
@@ -503,18 +728,21 @@ int tg_batch_norm_backward(int dtype, int64_t n, int64_t c, int64_t hw, const vo
   const int chunks = chunks_for(n, c);
   double* partial = reinterpret_cast<double*>(scratch);
   const size_t coef_off = align256((size_t)c * chunks * 2 * sizeof(double));
-  const int64_t total = n * c * hw;
   return TG_DISPATCH_FLOAT(dtype, T, [&] {
     T* coef = reinterpret_cast<T*>((uint8_t*)scratch + coef_off);
-    channel_sums_kernel<T, MODE_GRAD><<<dim3(chunks, (unsigned)c), kThreads, 0, st>>>(
-        (const T*)g, (const T*)x, (const T*)mean, n, c, hw, chunks, partial);
+    launch_channel_sums<T, MODE_GRAD>((const T*)g, (const T*)x, (const T*)mean, n, c, hw,
+                                      chunks, partial, st);
     bn_grad_final_kernel<T><<<(unsigned)((c + 127) / 128), 128, 0, st>>>(
         partial, chunks, c, (double)(n * hw), (const T*)w, (const T*)rstd, (T*)gw, (T*)gb,
         gx ? coef : nullptr);
     int launched = 2;
     if (gx) {
-      bn_grad_input_kernel<T><<<grid_for(total, kThreads, 148 * 64), kThreads, 0, st>>>(
-          (const T*)g, (const T*)x, (const T*)mean, (const T*)rstd, coef, (T*)gx, total, c, hw);
+      if (plane_vec4<T>(hw, {g, x, gx}))
+        bn_grad_input_kernel<T, 4><<<plane_grid(hw / 4, n * c), kThreads, 0, st>>>(
+            (const T*)g, (const T*)x, (const T*)mean, (const T*)rstd, coef, (T*)gx, n * c, c, hw);
+      else
+        bn_grad_input_kernel<T, 1><<<plane_grid(hw, n * c), kThreads, 0, st>>>(
+            (const T*)g, (const T*)x, (const T*)mean, (const T*)rstd, coef, (T*)gx, n * c, c, hw);
       ++launched;
     }
     return check_launch("batch_norm backward", launched);
@@ -532,8 +760,8 @@ int tg_max_pool2d_forward(int dtype, const tg_conv_shape* s, const void* x, void
   if (total == 0) return TG_OK;
   cudaStream_t st = as_stream(stream);
   return TG_DISPATCH_FLOAT(dtype, T, [&] {
-    maxpool_fwd_kernel<T><<<grid_for(total, kThreads, 148 * 64), kThreads, 0, st>>>(
-        (const T*)x, (T*)y, argmax, *s);
+    const dim3 grid = position_grid(s->oh * s->ow, s->n * s->c);
+    maxpool_fwd_kernel<T><<<grid, kThreads, 0, st>>>((const T*)x, (T*)y, argmax, *s);
     return check_launch("max_pool2d");
   });
 }
@@ -546,8 +774,11 @@ int tg_max_pool2d_backward(int dtype, const tg_conv_shape* s, const void* g,
   if (total == 0) return TG_OK;
   cudaStream_t st = as_stream(stream);
   return TG_DISPATCH_FLOAT(dtype, T, [&] {
-    maxpool_bwd_kernel<T><<<grid_for(total, kThreads, 148 * 64), kThreads, 0, st>>>(
-        (const T*)g, argmax, (T*)gx, *s);
+    const dim3 grid = position_grid(s->h * s->w, s->n * s->c);
+    if (s->sh >= s->kh && s->sw >= s->kw)
+      maxpool_bwd_kernel<T, true><<<grid, kThreads, 0, st>>>((const T*)g, argmax, (T*)gx, *s);
+    else
+      maxpool_bwd_kernel<T, false><<<grid, kThreads, 0, st>>>((const T*)g, argmax, (T*)gx, *s);
     return check_launch("max_pool2d backward");
   });
 }

@@ -70,6 +70,51 @@ cudaEvent_t take_event() {
 // Largest split-K workspace the linear VJP asks its caller for.
 constexpr size_t kLinearWorkspaceCap = size_t(128) << 20;
 
+
+// Scratch of tg_linear_backward: column-sum partials (cs), split-K partials (ws, fp32 only)
+// and, for fp32 with out_features not a multiple of 4, a copy of the gradient with rows padded
+// to a multiple of 4 elements (gpad), which the tensor maps need.
+struct LinearBwdScratch {
+  size_t cs = 0, ws = 0, gpad = 0, total = 0;
+};
+
+LinearBwdScratch linear_bwd_scratch(int dtype, int64_t rows, int64_t in_features,
+                                    int64_t out_features, unsigned need) {
+  const size_t es = dtype == TG_F64 ? 8 : 4;
+  LinearBwdScratch L;
+  if (need & 4) L.cs = (tg_colsum_scratch_bytes(dtype, rows, out_features) + 255) / 256 * 256;
+  if (dtype == TG_F32) {
+    int64_t mn = 0;
+    if (need & 1) mn = rows * in_features;
+    if ((need & 2) && out_features * in_features > mn) mn = out_features * in_features;
+    size_t ws = (size_t)mn * es * 4;  // room for four split-K partials
+    if (ws > kLinearWorkspaceCap) ws = kLinearWorkspaceCap;
+    L.ws = (ws + 255) / 256 * 256;
+    if ((out_features % 4) && (need & 3))
+      L.gpad = ((size_t)rows * (size_t)((out_features + 3) / 4 * 4) * es + 255) / 256 * 256;
+  }
+  L.total = L.cs + L.ws + L.gpad;
+  return L;
+}
+
+// Split-K partials for a linear forward whose output has too few tiles to fill the SMs while
+// its reduction is long (e.g. a classifier head over a wide flattened input): room for up to
+// about two splits per SM. Zero when the product already fills the GPU or is not fp32.
+size_t linear_fwd_workspace(int dtype, int64_t rows, int64_t in_features, int64_t out_features) {
+  if (dtype != TG_F32 || rows <= 0 || out_features <= 0 || in_features < 1024) return 0;
+  const int64_t tiles = ((rows + 127) / 128) * ((out_features + 63) / 64);
+  if (tiles >= 74) return 0;
+  const int64_t splits = (296 + tiles - 1) / tiles;
+  return ((size_t)splits * (size_t)rows * (size_t)out_features * sizeof(float) + 255) / 256 * 256;
+}
+
+// dst (rows x cols, row stride ldd) = src (row stride lds).
+template <typename T>
+__global__ void copy_rows_kernel(const T* __restrict__ src, int64_t lds, T* __restrict__ dst,
+                                 int64_t ldd, int64_t rows, int64_t cols) {
+  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y)
+    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) dst[r * ldd + c] = src[r * lds + c];
+}
 // Process-wide matmul precision of the fp32 tensor-core path (tg_set_matmul_precision).
 int g_precision = 0;
 
@@ -218,26 +263,33 @@ int tg_gemm_profile_read(double* total_ms, int64_t* launches, double* flops) {
   return TG_OK;
 }
 
+size_t tg_linear_forward_scratch_bytes(int dtype, int64_t rows, int64_t in_features,
+                                       int64_t out_features) {
+  const size_t ws = linear_fwd_workspace(dtype, rows, in_features, out_features);
+  return ws ? ws : 16;
+}
+
 int tg_linear_forward(int dtype, const void* x, const void* w, const void* bias, void* y,
-                      int64_t rows, int64_t in_features, int64_t out_features, void* stream) {
-  return tg_gemm(dtype, 0, 1, rows, out_features, in_features, 1.0, x, in_features, w,
-                 in_features, 0.0, y, out_features, bias, stream);
+                      int64_t rows, int64_t in_features, int64_t out_features, void* scratch,
+                      void* stream) {
+  const size_t ws = scratch ? linear_fwd_workspace(dtype, rows, in_features, out_features) : 0;
+  if (ws == 0)
+    return tg_gemm(dtype, 0, 1, rows, out_features, in_features, 1.0, x, in_features, w,
+                   in_features, 0.0, y, out_features, bias, stream);
+  int rc = check_gemm(0, 1, rows, out_features, in_features, in_features, in_features,
+                      out_features);
+  if (rc) return rc;
+  auto p = make_args<float>(0, 1, rows, out_features, in_features, 1.0, x, in_features, 0, w,
+                            in_features, 0, 0.0, y, out_features, 0, bias, 1);
+  p.workspace = reinterpret_cast<float*>(scratch);
+  p.workspace_bytes = ws;
+  return gemm_dispatch<float>(p, true, as_stream(stream));
 }
 
 size_t tg_linear_backward_scratch_bytes(int dtype, int64_t rows, int64_t in_features,
                                         int64_t out_features, unsigned need) {
-  const size_t es = dtype == TG_F64 ? 8 : 4;
-  size_t bytes = (need & 4) ? (tg_colsum_scratch_bytes(dtype, rows, out_features) + 255) / 256 * 256
-                            : 0;
-  if (dtype == TG_F32) {
-    int64_t mn = 0;
-    if (need & 1) mn = rows * in_features;
-    if ((need & 2) && out_features * in_features > mn) mn = out_features * in_features;
-    size_t ws = (size_t)mn * es * 4;  // room for four split-K partials
-    if (ws > kLinearWorkspaceCap) ws = kLinearWorkspaceCap;
-    bytes += ws;
-  }
-  return bytes ? bytes : 16;
+  const LinearBwdScratch L = linear_bwd_scratch(dtype, rows, in_features, out_features, need);
+  return L.total ? L.total : 16;
 }
 
 int tg_linear_backward(int dtype, const void* g, const void* x, const void* w, void* gx, void* gw,
@@ -247,31 +299,41 @@ int tg_linear_backward(int dtype, const void* g, const void* x, const void* w, v
                       in_features);
   if (rc) return rc;
   TG_CHECK_ARG(!((need & 4) && gb) || scratch, "linear_backward: scratch is NULL");
-  // Split-K partials (tensor-core products) live after the column-sum partials.
-  const size_t cs = (need & 4) ? (tg_colsum_scratch_bytes(dtype, rows, out_features) + 255) / 256 * 256
-                               : 0;
-  const size_t total = scratch ? tg_linear_backward_scratch_bytes(dtype, rows, in_features,
-                                                                  out_features, need) : 0;
-  float* ws = (scratch && total > cs + 16) ? reinterpret_cast<float*>((uint8_t*)scratch + cs)
-                                           : nullptr;
-  const size_t ws_bytes = ws ? total - cs : 0;
+  // Scratch: column-sum partials, then split-K partials (tensor-core products), then the
+  // gradient re-laid with 16-byte rows when out_features is not a multiple of 4.
+  const LinearBwdScratch L = scratch ? linear_bwd_scratch(dtype, rows, in_features,
+                                                          out_features, need)
+                                     : LinearBwdScratch{};
+  uint8_t* base = (uint8_t*)scratch;
+  float* ws = L.ws ? reinterpret_cast<float*>(base + L.cs) : nullptr;
   cudaStream_t s = as_stream(stream);
   rc = TG_DISPATCH_FLOAT(dtype, T, [&] {
+    const T* gk = (const T*)g;
+    int64_t ldg = out_features;
+    if (L.gpad && (((need & 1) && gx) || ((need & 2) && gw))) {
+      ldg = (out_features + 3) / 4 * 4;
+      T* gp = reinterpret_cast<T*>(base + L.cs + L.ws);
+      copy_rows_kernel<T><<<dim3(1, (unsigned)(rows < 65535 ? rows : 65535)), 128, 0, s>>>(
+          (const T*)g, out_features, gp, ldg, rows, out_features);
+      const int r = check_launch("linear_backward(relayout)");
+      if (r) return r;
+      gk = gp;
+    }
     if ((need & 1) && gx) {
       // gx[rows, in] = g[rows, out] @ w[out, in]
-      auto p = make_args<T>(0, 0, rows, in_features, out_features, 1.0, g, out_features, 0, w,
+      auto p = make_args<T>(0, 0, rows, in_features, out_features, 1.0, gk, ldg, 0, w,
                             in_features, 0, 0.0, gx, in_features, 0, nullptr, 1);
       p.workspace = ws;
-      p.workspace_bytes = ws_bytes;
+      p.workspace_bytes = L.ws;
       const int r = gemm_dispatch<T>(p, true, s);
       if (r) return r;
     }
     if ((need & 2) && gw) {
       // gw[out, in] = g^T @ x: A = g stored rows x out (k x m), B = x stored rows x in (k x n)
-      auto p = make_args<T>(1, 0, out_features, in_features, rows, 1.0, g, out_features, 0, x,
+      auto p = make_args<T>(1, 0, out_features, in_features, rows, 1.0, gk, ldg, 0, x,
                             in_features, 0, beta_gw, gw, in_features, 0, nullptr, 1);
       p.workspace = ws;
-      p.workspace_bytes = ws_bytes;
+      p.workspace_bytes = L.ws;
       const int r = gemm_dispatch<T>(p, true, s);
       if (r) return r;
     }

@@ -32,8 +32,9 @@ struct GemmArgs {
   //   a_fold > 0: the reduction index of a K-major A (trans_a == 0) folds as
   //               k = q * a_fold + r -> element (m, k) at a + q * stride_a + m * lda + r,
   //               so k may run over images of an NCHW tensor (A itself is then not batched).
-  //   c_hw > 0  : C(m, n) at c + (m / c_hw) * stride_c + n * ldc + (m % c_hw): the GEMM row
-  //               is image * hw + pixel and the column a channel, written as NCHW (batch 1).
+  //   c_hw > 0  : C(m, n) of batch entry bz at c + bz * stride_ch + (m / c_hw) * stride_c +
+  //               n * ldc + (m % c_hw): the GEMM row is image * hw + pixel and the column a
+  //               channel, written as NCHW (column-major tiles; heads must be 1).
   int64_t a_fold = 0;
   int64_t c_hw = 0;
   // Batch entries split as (outer, head) with bz = outer * heads + head; each operand is
@@ -60,7 +61,7 @@ struct GemmArgs {
 template <typename T>
 __host__ __device__ __forceinline__ int64_t gemm_c_offset(const GemmArgs<T>& p, int64_t bz,
                                                           int64_t m, int64_t n) {
-  if (p.c_hw > 0) return (m / p.c_hw) * p.stride_c + n * p.ldc + (m % p.c_hw);
+  if (p.c_hw > 0) return bz * p.stride_ch + (m / p.c_hw) * p.stride_c + n * p.ldc + (m % p.c_hw);
   return (bz / p.heads) * p.stride_c + (bz % p.heads) * p.stride_ch + m * p.ldc + n;
 }
 

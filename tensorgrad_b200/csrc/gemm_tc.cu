@@ -630,7 +630,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       if (part) {
         crow = args.ws + ((int64_t)ti.split * args.m + row) * args.n;
       } else if (args.c_hw > 0) {
-        crow = args.c + (row / args.c_hw) * args.stride_c + row % args.c_hw;
+        crow = args.c + (int64_t)ti.bz * args.stride_ch + (row / args.c_hw) * args.stride_c +
+               row % args.c_hw;
         cstep = args.ldc;
       } else {
         crow = args.c + (int64_t)(ti.bz / args.heads) * args.stride_c +
@@ -1088,8 +1089,8 @@ int gemm_tc_f32(const GemmArgs<float>& p, cudaStream_t stream) {
   if (p.a_fold > 0 && (p.trans_a || p.batch != 1 || p.a_fold % tc::BK || p.k % p.a_fold ||
                        (p.stride_a % 4) || p.k / p.a_fold > INT32_MAX))
     return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: folded A needs K-major, fold %% 16 == 0");
-  if (p.c_hw > 0 && p.batch != 1)
-    return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: NCHW output is not batched");
+  if (p.c_hw > 0 && p.heads != 1)
+    return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: NCHW output takes no heads");
   const bool a_mn = p.trans_a != 0;   // A stored k x m
   const bool b_mn = p.trans_b == 0;   // B stored k x n
   // Tile width by estimated makespan: each persistent CTA runs ceil(tiles / SMs) tiles. A tile

@@ -276,6 +276,7 @@ ln_final_kernel(const T* __restrict__ part_w, const T* __restrict__ part_b, T* _
   const int c = blockIdx.x * 32 + tx;
   T sw = T(0), sb = T(0);
   if (c < cols) {
+#pragma unroll 4
     for (int i = ty; i < nparts; i += 8) {
       sw += part_w[(int64_t)i * cols + c];
       sb += part_b[(int64_t)i * cols + c];

@@ -75,14 +75,31 @@ colsum_partial_kernel(const T* __restrict__ x, T* __restrict__ partial, int64_t 
   }
 }
 
+// out[c] (+)= sum over chunks of partial[chunk][c]. Blocks of 32 columns x 8 chunk lanes:
+// lane y sums chunks y, y+8, ... (loads batched by the unrolled loop), then the 8 lane sums
+// are added in lane order. The order is fixed by the shape: deterministic.
 template <typename T>
-__global__ void colsum_final_kernel(const T* __restrict__ partial, T* __restrict__ out,
-                                    int64_t cols, int64_t chunks, int accumulate) {
-  for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < cols;
-       c += (int64_t)gridDim.x * blockDim.x) {
+__global__ void __launch_bounds__(256)
+colsum_final_kernel(const T* __restrict__ partial, T* __restrict__ out, int64_t cols,
+                    int64_t chunks, int accumulate) {
+  __shared__ T sh[8][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int64_t c0 = (int64_t)blockIdx.x * 32; c0 < cols; c0 += (int64_t)gridDim.x * 32) {
+    const int64_t c = c0 + tx;
     T s = T(0);
-    for (int64_t i = 0; i < chunks; ++i) s += partial[i * cols + c];
-    out[c] = accumulate ? out[c] + s : s;
+    if (c < cols) {
+#pragma unroll 4
+      for (int64_t i = ty; i < chunks; i += 8) s += partial[i * cols + c];
+    }
+    sh[ty][tx] = s;
+    __syncthreads();
+    if (ty == 0 && c < cols) {
+      T t = sh[0][tx];
+#pragma unroll
+      for (int k = 1; k < 8; ++k) t += sh[k][tx];
+      out[c] = accumulate ? out[c] + t : t;
+    }
+    __syncthreads();
   }
 }
 
@@ -165,8 +182,9 @@ int colsum(const T* x, T* out, int64_t rows, int64_t cols, int accumulate, void*
     colsum_partial_kernel<T><<<grid, dim3(kColTile, kRowLanes), 0, stream>>>(x, partial, rows,
                                                                             cols, rpc);
   }
-  colsum_final_kernel<T><<<grid_for(cols, 256), 256, 0, stream>>>(partial, out, cols, chunks,
-                                                                  accumulate);
+  const int64_t col_tiles = (cols + 31) / 32;
+  colsum_final_kernel<T><<<(unsigned)(col_tiles < 4096 ? col_tiles : 4096), 256, 0, stream>>>(
+      partial, out, cols, chunks, accumulate);
   return check_launch("colsum", 2);
 }
 template int colsum<float>(const float*, float*, int64_t, int64_t, int, void*, cudaStream_t);

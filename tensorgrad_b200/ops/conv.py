@@ -79,8 +79,9 @@ def conv2d(x: Any, weight: Any, bias: Any = None, stride: IntPair = 1,
     s = _shape(tx.shape, c_out, (tw.shape[2], tw.shape[3]), st, pad)
     code = dtype_code(xd.dtype)
     ref = ctypes.byref(s)
-    ld = lib.tg_conv2d_cols_ld(ref)
-    cols = device.empty((s.n * s.oh * s.ow, ld), xd.dtype)
+    rows, ld = ctypes.c_int64(), ctypes.c_int64()
+    check(lib.tg_conv2d_cols_shape(ref, ctypes.byref(rows), ctypes.byref(ld)), "conv2d")
+    cols = device.empty((rows.value, ld.value), xd.dtype)
     y = device.empty((s.n, c_out, s.oh, s.ow), xd.dtype)
     scratch = device.scratch(lib.tg_conv2d_forward_scratch_bytes(code, ref))
     check(lib.tg_conv2d_forward(code, ref, xd.ptr, wd.ptr, bd.ptr if bd is not None else None,

@@ -42,8 +42,12 @@ def linear(x: Any, weight: Any, bias: Any = None) -> Tensor:
     rows = xd.size // in_f if in_f else 0
     code = dtype_code(xd.dtype)
     y = device.empty((*tx.shape[:-1], out_f), xd.dtype)
+    fwd_bytes = lib.tg_linear_forward_scratch_bytes(code, rows, in_f, out_f)
+    fwd_scratch = device.scratch(fwd_bytes) if fwd_bytes > 16 else None
     check(lib.tg_linear_forward(code, xd.ptr, wd.ptr, bd.ptr if bd is not None else None, y.ptr,
-                                rows, in_f, out_f, device.stream()), "linear")
+                                rows, in_f, out_f,
+                                fwd_scratch.ptr if fwd_scratch is not None else None,
+                                device.stream()), "linear")
     has_bias = tb is not None
 
     def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray | None, ...]:

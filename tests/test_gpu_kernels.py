@@ -101,11 +101,16 @@ def test_gemm_simt_fp64():
 
 
 # ------------------------------------------------------------------------------- layers
-def test_linear(dtype):
+# (batch dims, in, out): plain; out not a multiple of 4 (the VJP re-lays the gradient with
+# 16-byte rows for the tensor maps); a wide input with few output tiles (split-K forward).
+@pytest.mark.parametrize("lead,fin,fout", [((4, 9), 24, 40), ((33, 7), 48, 65),
+                                           ((256,), 4096, 4)])
+def test_linear(dtype, lead, fin, fout):
     import tensorgrad_b200 as tg
 
-    rng = np.random.default_rng(1)
-    x, w, b, g = (rng.standard_normal(s) for s in ((4, 9, 24), (40, 24), (40,), (4, 9, 40)))
+    rng = np.random.default_rng(fin + fout)
+    x, w, b, g = (rng.standard_normal(s) for s in ((*lead, fin), (fout, fin), (fout,),
+                                                    (*lead, fout)))
     tx, tw, tb = tensor(x, dtype), tensor(w, dtype), tensor(b, dtype)
     y = tg.linear(tx, tw, tb)
     y.backward(g.astype(dtype))
