@@ -137,7 +137,7 @@ def _train_step(tg, model_fn, params, loss_fn, reducer, clip: float | None):
         if reducer is not None:
             reducer.reduce()
         if clip is not None:
-            tg.optim.clip_grad_norm_(params, clip)
+            tg.optim.clip_grad_norm_(params, clip, sync=False)
         opt.step()
         return loss
 

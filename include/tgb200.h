@@ -194,10 +194,12 @@ int tg_layer_norm_backward_noalloc(int dtype, const void* g, const void* x, cons
                                    void* stream);
 
 /* ------------------------------------------------------------------ embedding
- * ops/layers.py:209-232. out[i, :] = w[ids[i], :]. Ids must be in [0, num) (checked on the
- * host by the caller, as the reference does before indexing). */
+ * ops/layers.py:209-232. out[i, :] = w[ids[i], :]. Ids outside [0, num) give a zero row and
+ * set *bad_id_dev (int32, may be NULL) to 1: host ids are checked by the caller before the
+ * call, as the reference checks them; device-resident ids are checked here and the flag is
+ * read back at the caller's next synchronisation. */
 int tg_embedding_forward(int dtype, const int64_t* ids, const void* w, void* out, int64_t n,
-                         int64_t num, int64_t dim, void* stream);
+                         int64_t num, int64_t dim, int* bad_id_dev, void* stream);
 /* Scatter-add of gradient rows into gw[num, dim] in the reference's order
  * (ops/layers.py:192-206: stable sort of ids, then a sum per run of equal ids):
  * `order` is the stable argsort of ids, `seg_start[nseg + 1]` the run boundaries in it and
@@ -205,6 +207,17 @@ int tg_embedding_forward(int dtype, const int64_t* ids, const void* w, void* out
 int tg_embedding_backward(int dtype, const void* g, const int64_t* order,
                           const int64_t* seg_start, const int64_t* seg_id, int64_t nseg,
                           void* gw, int64_t num, int64_t dim, int accumulate, void* stream);
+/* The same order computed on the device, for device-resident ids: tg_embedding_sort writes
+ * sorted_keys[n] = the ascending keys id * n + position (unique keys, so this is the stable
+ * sort by id; an id outside [0, num) is counted as 0 and sets *bad_id_dev). `scratch`:
+ * tg_embedding_sort_scratch_bytes(n, num). tg_embedding_backward_sorted then sums each run of
+ * equal ids in ascending position into its row of gw. */
+size_t tg_embedding_sort_scratch_bytes(int64_t n, int64_t num);
+int tg_embedding_sort(const int64_t* ids, int64_t n, int64_t num, uint64_t* sorted_keys,
+                      int* bad_id_dev, void* scratch, size_t scratch_bytes, void* stream);
+int tg_embedding_backward_sorted(int dtype, const void* g, const uint64_t* sorted_keys,
+                                 int64_t n, void* gw, int64_t num, int64_t dim, int accumulate,
+                                 void* stream);
 
 /* ------------------------------------------------------------------ cross entropy
  * ops/loss.py:23-97 with ops/activation.py:48-52 (class axis last). Per row: lse = log sum

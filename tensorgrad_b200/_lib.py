@@ -98,8 +98,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                        vp]),
     "tg_layer_norm_backward_noalloc": (c_int, [c_int, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64,
                                                u32, vp]),
-    "tg_embedding_forward": (c_int, [c_int, vp, vp, vp, i64, i64, i64, vp]),
+    "tg_embedding_forward": (c_int, [c_int, vp, vp, vp, i64, i64, i64, vp, vp]),
     "tg_embedding_backward": (c_int, [c_int, vp, vp, vp, vp, i64, vp, i64, i64, c_int, vp]),
+    "tg_embedding_sort_scratch_bytes": (sz, [i64, i64]),
+    "tg_embedding_sort": (c_int, [vp, i64, i64, vp, vp, vp, sz, vp]),
+    "tg_embedding_backward_sorted": (c_int, [c_int, vp, vp, i64, vp, i64, i64, c_int, vp]),
     "tg_cross_entropy_forward": (c_int, [c_int, vp, vp, vp, vp, vp, i64, i64, i64, c_int, vp, vp,
                                          vp]),
     "tg_cross_entropy_backward": (c_int, [c_int, vp, vp, vp, vp, vp, vp, i64, i64, i64, c_int,

@@ -1,27 +1,40 @@
 // Embedding gather / scatter-add (ops/layers.py:192-232) and softmax cross-entropy with the
 // class axis last (ops/loss.py:23-97, ops/activation.py:48-52).
+#include <cub/device/device_radix_sort.cuh>
+
 #include "common.cuh"
 
 namespace tg {
 namespace {
 
 // ---------------------------------------------------------------- embedding
+// Ids outside [0, num) give a zero row and set *bad (when given): device-resident ids are
+// validated where they are read, the flag is read back at the next host synchronisation.
 template <typename T>
 __global__ void embed_fwd_kernel(const int64_t* __restrict__ ids, const T* __restrict__ w,
-                                 T* __restrict__ out, int64_t n, int64_t dim) {
+                                 T* __restrict__ out, int64_t n, int64_t num, int64_t dim,
+                                 int* __restrict__ bad) {
   for (int64_t r = blockIdx.x; r < n; r += gridDim.x) {
-    const T* src = w + ids[r] * dim;
+    const int64_t id = ids[r];
+    const bool ok = id >= 0 && id < num;
+    if (!ok && bad && threadIdx.x == 0) atomicOr(bad, 1);
+    const T* src = w + (ok ? id : 0) * dim;
     T* dst = out + r * dim;
-    for (int64_t c = threadIdx.x; c < dim; c += blockDim.x) dst[c] = src[c];
+    for (int64_t c = threadIdx.x; c < dim; c += blockDim.x) dst[c] = ok ? src[c] : T(0);
   }
 }
 
 __global__ void embed_fwd_vec4_kernel(const int64_t* __restrict__ ids, const float4* __restrict__ w,
-                                      float4* __restrict__ out, int64_t n, int64_t dim4) {
+                                      float4* __restrict__ out, int64_t n, int64_t num,
+                                      int64_t dim4, int* __restrict__ bad) {
   for (int64_t r = blockIdx.x; r < n; r += gridDim.x) {
-    const float4* src = w + ids[r] * dim4;
+    const int64_t id = ids[r];
+    const bool ok = id >= 0 && id < num;
+    if (!ok && bad && threadIdx.x == 0) atomicOr(bad, 1);
+    const float4* src = w + (ok ? id : 0) * dim4;
     float4* dst = out + r * dim4;
-    for (int64_t c = threadIdx.x; c < dim4; c += blockDim.x) dst[c] = src[c];
+    for (int64_t c = threadIdx.x; c < dim4; c += blockDim.x)
+      dst[c] = ok ? src[c] : make_float4(0.f, 0.f, 0.f, 0.f);
   }
 }
 
@@ -41,6 +54,66 @@ __global__ void embed_bwd_kernel(const T* __restrict__ g, const int64_t* __restr
       dst[c] = accumulate ? dst[c] + acc : acc;
     }
   }
+}
+
+// Sort keys id * n + position (ids clamped into [0, num), an out-of-range id flagged in *bad).
+// The keys are unique, so their ascending order is the stable sort by id that the reference
+// takes, whatever algorithm sorts them.
+__global__ void embed_keys_kernel(const int64_t* __restrict__ ids, int64_t n, int64_t num,
+                                  uint64_t* __restrict__ keys, int* __restrict__ bad) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t id = ids[i];
+    if (id < 0 || id >= num) {
+      if (bad) atomicOr(bad, 1);
+      id = 0;
+    }
+    keys[i] = (uint64_t)id * (uint64_t)n + (uint64_t)i;
+  }
+}
+
+// The VJP from sorted keys: one warp per sorted position; the warp at the first position of a
+// run of equal ids sums that run's gradient rows in ascending position and writes (or adds)
+// the id's row. Other warps return at once.
+template <typename T>
+__global__ void embed_bwd_sorted_kernel(const T* __restrict__ g, const uint64_t* __restrict__ keys,
+                                        int64_t n, T* __restrict__ gw, int64_t dim,
+                                        int accumulate) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const uint64_t un = (uint64_t)n;
+  for (int64_t k = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); k < n;
+       k += warps) {
+    const uint64_t id = keys[k] / un;
+    if (k > 0 && keys[k - 1] / un == id) continue;
+    // Run end: the first later key of another id, 32 keys at a time.
+    const uint64_t limit = (id + 1) * un;  // keys of this id are below it
+    int64_t e = k + 1;
+    while (true) {
+      const int64_t i = e + lane;
+      const bool same = i < n && keys[i] < limit;
+      const unsigned m = __ballot_sync(0xffffffffu, same);
+      if (m != 0xffffffffu) {
+        e += __ffs(~m) - 1;
+        break;
+      }
+      e += 32;
+    }
+    const uint64_t base = id * un;
+    T* dst = gw + (int64_t)id * dim;
+    for (int64_t c = lane; c < dim; c += 32) {
+      T acc = T(0);
+#pragma unroll 4
+      for (int64_t i = k; i < e; ++i) acc += g[(int64_t)(keys[i] - base) * dim + c];
+      dst[c] = accumulate ? dst[c] + acc : acc;
+    }
+  }
+}
+
+int key_bits(uint64_t max_key) {
+  int b = 1;
+  while (b < 64 && (max_key >> b)) ++b;
+  return b;
 }
 
 // ---------------------------------------------------------------- cross entropy
@@ -179,18 +252,65 @@ using namespace tg;
 extern "C" {
 
 int tg_embedding_forward(int dtype, const int64_t* ids, const void* w, void* out, int64_t n,
-                         int64_t num, int64_t dim, void* stream) {
-  (void)num;
+                         int64_t num, int64_t dim, int* bad_id_dev, void* stream) {
   if (n <= 0 || dim <= 0) return TG_OK;
+  TG_CHECK_ARG(num > 0, "embedding: empty table");
   cudaStream_t s = as_stream(stream);
   const unsigned grid = (unsigned)(n < 148 * 16 ? n : 148 * 16);
   if (dtype == TG_F32 && dim % 4 == 0 && aligned16(w) && aligned16(out)) {
-    embed_fwd_vec4_kernel<<<grid, 128, 0, s>>>(ids, (const float4*)w, (float4*)out, n, dim / 4);
+    embed_fwd_vec4_kernel<<<grid, 128, 0, s>>>(ids, (const float4*)w, (float4*)out, n, num,
+                                               dim / 4, bad_id_dev);
     return check_launch("embedding_forward");
   }
   return TG_DISPATCH_FLOAT(dtype, T, [&] {
-    embed_fwd_kernel<T><<<grid, 128, 0, s>>>(ids, (const T*)w, (T*)out, n, dim);
+    embed_fwd_kernel<T><<<grid, 128, 0, s>>>(ids, (const T*)w, (T*)out, n, num, dim, bad_id_dev);
     return check_launch("embedding_forward");
+  });
+}
+
+size_t tg_embedding_sort_scratch_bytes(int64_t n, int64_t num) {
+  if (n <= 0 || num <= 0 || n > INT32_MAX) return 16;
+  size_t temp = 0;
+  const int bits = key_bits((uint64_t)num * (uint64_t)n - 1);
+  cub::DeviceRadixSort::SortKeys(nullptr, temp, (const uint64_t*)nullptr, (uint64_t*)nullptr,
+                                 (int)n, 0, bits);
+  return ((size_t)n * 8 + 255) / 256 * 256 + temp + 256;
+}
+
+int tg_embedding_sort(const int64_t* ids, int64_t n, int64_t num, uint64_t* sorted_keys,
+                      int* bad_id_dev, void* scratch, size_t scratch_bytes, void* stream) {
+  TG_CHECK_ARG(n >= 0 && num > 0 && n <= INT32_MAX, "embedding_sort: bad sizes");
+  TG_CHECK_ARG((uint64_t)num <= UINT64_MAX / (uint64_t)(n > 0 ? n : 1),
+               "embedding_sort: num * n overflows 64 bits");
+  if (n == 0) return TG_OK;
+  TG_CHECK_ARG(scratch && scratch_bytes >= tg_embedding_sort_scratch_bytes(n, num),
+               "embedding_sort: scratch too small");
+  cudaStream_t s = as_stream(stream);
+  uint64_t* keys = reinterpret_cast<uint64_t*>(scratch);
+  const size_t keys_bytes = ((size_t)n * 8 + 255) / 256 * 256;
+  const unsigned grid = (unsigned)((n + 255) / 256 < 148 * 8 ? (n + 255) / 256 : 148 * 8);
+  embed_keys_kernel<<<grid, 256, 0, s>>>(ids, n, num, keys, bad_id_dev);
+  int r = check_launch("embedding_sort(keys)");
+  if (r) return r;
+  const int bits = key_bits((uint64_t)num * (uint64_t)n - 1);
+  size_t temp = scratch_bytes - keys_bytes;
+  TG_CUDA_TRY(cub::DeviceRadixSort::SortKeys((uint8_t*)scratch + keys_bytes, temp, keys,
+                                             sorted_keys, (int)n, 0, bits, s));
+  return check_launch("embedding_sort(radix)", 0);
+}
+
+int tg_embedding_backward_sorted(int dtype, const void* g, const uint64_t* sorted_keys,
+                                 int64_t n, void* gw, int64_t num, int64_t dim, int accumulate,
+                                 void* stream) {
+  cudaStream_t s = as_stream(stream);
+  const size_t es = dtype == TG_F64 ? 8 : 4;
+  if (!accumulate && num * dim > 0) TG_CUDA_TRY(cudaMemsetAsync(gw, 0, num * dim * es, s));
+  if (n <= 0 || dim <= 0) return TG_OK;
+  return TG_DISPATCH_FLOAT(dtype, T, [&] {
+    const int64_t blocks = (n + 7) / 8;  // 8 warps per block
+    embed_bwd_sorted_kernel<T><<<(unsigned)(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, s>>>(
+        (const T*)g, sorted_keys, n, (T*)gw, dim, accumulate);
+    return check_launch("embedding_backward");
   });
 }
 

@@ -73,7 +73,50 @@ def dtype_code(dtype: np.dtype[Any]) -> int:
 
 
 def synchronize() -> None:
+    """Wait for the stream; then raise any error that device-side validation recorded."""
     check(lib.tg_stream_synchronize(_State.stream), "synchronize")
+    if _Async.pending:
+        _raise_async_errors()
+
+
+# Device-side validation. Ops that take device-resident indices (embedding ids, class
+# targets) cannot check them on the host without a synchronisation per call, so their
+# kernels check them and set a flag word instead; the flags are read back at the next host
+# synchronisation, which raises the error the op raises for host inputs.
+ASYNC_EMBEDDING_ID = 0
+ASYNC_CLASS_TARGET = 1
+_ASYNC_MESSAGES = {
+    ASYNC_EMBEDDING_ID: "embedding ids out of range (device-resident ids, checked on the device)",
+    ASYNC_CLASS_TARGET: "cross_entropy target out of range (device-resident targets, checked on "
+                        "the device)",
+}
+
+
+class _Async:
+    words: DeviceArray | None = None
+    pending = False
+
+
+def async_error_word(kind: int) -> int:
+    """Device address of the int32 flag word of ``kind`` (ASYNC_*); marks a check pending."""
+    if _Async.words is None or _Async.words._t.device != current_device():
+        _Async.words = zeros((len(_ASYNC_MESSAGES),), np.int32)
+    _Async.pending = True
+    return _Async.words.ptr + 4 * kind
+
+
+def _raise_async_errors() -> None:
+    _Async.pending = False
+    words = _Async.words
+    if words is None:
+        return
+    host = np.zeros(words.shape, np.int32)
+    check(lib.tg_memcpy_d2h(host.ctypes.data, words.ptr, host.nbytes, _State.stream), "d2h")
+    check(lib.tg_stream_synchronize(_State.stream), "synchronize")
+    if host.any():
+        check(lib.tg_memset_zero(words.ptr, words.nbytes, _State.stream), "zeros")
+        kind = int(np.flatnonzero(host)[0])
+        raise IndexError(_ASYNC_MESSAGES[kind])
 
 
 class DeviceArray:

@@ -8,6 +8,7 @@ from typing import Any
 
 import numpy as np
 
+from tensorgrad_b200 import device
 from tensorgrad_b200.nn import init
 from tensorgrad_b200.nn.attention import MultiHeadAttention
 from tensorgrad_b200.nn.layers import GELU, Dropout, Embedding, LayerNorm, Linear, Sequential
@@ -87,10 +88,11 @@ class GPT(Module):
                 init.normal_(module.weight, 0.0, 0.02)
 
     def forward(self, idx: Any, cache: object = None) -> Tensor:
-        """Token ids ``(B, T)`` (host array or tensor) to logits ``(B, T, vocab_size)``."""
+        """Token ids ``(B, T)`` to logits ``(B, T, vocab_size)``. Host ids are checked on the
+        host; ids in a device tensor stay on the device (checked there, see ``embedding``)."""
         if cache is not None:
             raise NotImplementedError("KV-cache inference is not on the device training path")
-        tokens = idx.numpy() if isinstance(idx, Tensor) else np.asarray(idx)
+        tokens = idx if isinstance(idx, Tensor) else np.asarray(idx)
         if tokens.ndim != 2:
             raise ValueError(f"expected (B, T) token ids, got shape {tokens.shape}")
         t = tokens.shape[1]
@@ -102,11 +104,13 @@ class GPT(Module):
         return self.head(self.ln_f(x))
 
 
-_POSITIONS: dict[int, np.ndarray] = {}
+_POSITIONS: dict[tuple[int, str], Tensor] = {}
 
 
-def _positions(t: int) -> np.ndarray:
-    p = _POSITIONS.get(t)
+def _positions(t: int) -> Tensor:
+    """Positions 0..t-1 as a device tensor, uploaded once per length and device."""
+    key = (t, str(device.current_device()))
+    p = _POSITIONS.get(key)
     if p is None:
-        p = _POSITIONS[t] = np.arange(t)
+        p = _POSITIONS[key] = Tensor(np.arange(t, dtype=np.int64))
     return p

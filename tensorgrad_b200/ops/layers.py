@@ -243,26 +243,49 @@ def _segments(ids: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
 @profiled("embedding")
 def embedding(indices: Any, weight: Any) -> Tensor:
     """Row lookup; the VJP is a scatter-add in the reference's sorted order
-    (ops/layers.py:209-232). Ids are checked on the host before any device work."""
+    (ops/layers.py:209-232).
+
+    Host ids are checked before any device work, as the reference checks them, and sorted on
+    the host. Device-resident ids (a Tensor or DeviceArray) stay on the device: the gather
+    checks them (an out-of-range id raises IndexError at the next host synchronisation) and
+    the VJP sorts them on the device, so the step needs no host round trip."""
     tw = as_tensor(weight)
-    if isinstance(indices, Tensor):
-        idx = indices.numpy()
-    elif isinstance(indices, DeviceArray):
-        idx = indices.numpy()
-    else:
-        idx = np.asarray(indices)
+    num, dim = tw.shape
+    wd = tw.data
+    code = dtype_code(wd.dtype)
+    dev_ids = indices.data if isinstance(indices, Tensor) else indices
+    if isinstance(dev_ids, DeviceArray):
+        if dev_ids.dtype.kind not in "iu":
+            raise TypeError(f"embedding indices must be integers, got {dev_ids.dtype}")
+        ids_dev = dev_ids if dev_ids.dtype == np.int64 else cast_array(dev_ids, np.dtype(np.int64))
+        shape, n = dev_ids.shape, dev_ids.size
+        out = device.empty((*shape, dim), wd.dtype)
+        check(lib.tg_embedding_forward(code, ids_dev.ptr, wd.ptr, out.ptr, n, num, dim,
+                                       device.async_error_word(device.ASYNC_EMBEDDING_ID),
+                                       device.stream()), "embedding")
+
+        def backward_dev(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+            scr = device.scratch(lib.tg_embedding_sort_scratch_bytes(n, num))
+            keys = device.empty((n,), np.int64)  # uint64 sort keys
+            check(lib.tg_embedding_sort(ids_dev.ptr, n, num, keys.ptr, None, scr.ptr,
+                                        scr.nbytes, device.stream()), "embedding sort")
+            gw = device.empty((num, dim), g.dtype)
+            check(lib.tg_embedding_backward_sorted(dtype_code(g.dtype), g.ptr, keys.ptr, n,
+                                                   gw.ptr, num, dim, 0, device.stream()),
+                  "embedding backward")
+            return (gw,)
+
+        return make_result(out, (tw,), backward_dev, "embedding")
+    idx = np.asarray(indices)
     if not np.issubdtype(idx.dtype, np.integer):
         raise TypeError(f"embedding indices must be integers, got {idx.dtype}")
-    num, dim = tw.shape
     if idx.size and (idx.min() < 0 or idx.max() >= num):
         raise IndexError(f"embedding ids must be in [0, {num}), got {idx.min()}..{idx.max()}")
     flat = np.ascontiguousarray(idx.reshape(-1), dtype=np.int64)
-    ids_dev = device.from_numpy(flat)
-    wd = tw.data
-    code = dtype_code(wd.dtype)
+    ids_host = device.from_numpy(flat)
     out = device.empty((*idx.shape, dim), wd.dtype)
-    check(lib.tg_embedding_forward(code, ids_dev.ptr, wd.ptr, out.ptr, flat.size, num, dim,
-                                   device.stream()), "embedding")
+    check(lib.tg_embedding_forward(code, ids_host.ptr, wd.ptr, out.ptr, flat.size, num, dim,
+                                   None, device.stream()), "embedding")
 
     def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
         order, seg_start, seg_id = _segments(flat)

@@ -28,37 +28,51 @@ def cross_entropy(logits: Any, target: Any, *, ignore_index: int = -100,
 
     One kernel pass per row computes the log-sum-exp (online max and sum) and the row loss;
     the mean over non-ignored rows is a fixed-order float64 sum. The VJP is one pass writing
-    ``(softmax - onehot) * g / n_valid``. Targets are validated on the host, as the reference
-    does, before any device work.
+    ``(softmax - onehot) * g / n_valid``. Host targets are validated on the host, as the
+    reference does, before any device work; device-resident targets are validated by the
+    kernel and an out-of-range one raises at the next host synchronisation.
     """
     tl = as_tensor(logits)
-    if isinstance(target, Tensor | DeviceArray):
-        t = target.numpy()
+    classes = tl.shape[-1]
+    dev_t = target.data if isinstance(target, Tensor) else target
+    bad = None
+    if isinstance(dev_t, DeviceArray):
+        # Device-resident targets stay on the device: the kernel checks them and an
+        # out-of-range target raises IndexError at the next host synchronisation.
+        if dev_t.dtype.kind not in "iu":
+            raise TypeError(f"cross_entropy targets must be integers, got {dev_t.dtype}")
+        if tl.shape[:-1] != dev_t.shape:
+            raise ValueError(f"logits {tl.shape} and targets {dev_t.shape} are incompatible")
+        if reduction not in _RED:
+            raise ValueError(f"unknown reduction {reduction!r}")
+        tgt = dev_t if dev_t.dtype == np.int64 else cast_array(dev_t, np.dtype(np.int64))
+        t_shape = dev_t.shape
+        bad = device.async_error_word(device.ASYNC_CLASS_TARGET)
     else:
         t = np.asarray(target)
-    if not np.issubdtype(t.dtype, np.integer):
-        raise TypeError(f"cross_entropy targets must be integers, got {t.dtype}")
-    if tl.shape[:-1] != t.shape:
-        raise ValueError(f"logits {tl.shape} and targets {t.shape} are incompatible")
-    if reduction not in _RED:
-        raise ValueError(f"unknown reduction {reduction!r}")
-    classes = tl.shape[-1]
-    flat_t = np.ascontiguousarray(t.reshape(-1), dtype=np.int64)
-    valid = flat_t != ignore_index
-    safe = np.where(valid, flat_t, 0)
-    if np.any((safe < 0) | (safe >= classes)):
-        raise IndexError(f"target out of range for {classes} classes")
+        if not np.issubdtype(t.dtype, np.integer):
+            raise TypeError(f"cross_entropy targets must be integers, got {t.dtype}")
+        if tl.shape[:-1] != t.shape:
+            raise ValueError(f"logits {tl.shape} and targets {t.shape} are incompatible")
+        if reduction not in _RED:
+            raise ValueError(f"unknown reduction {reduction!r}")
+        flat_t = np.ascontiguousarray(t.reshape(-1), dtype=np.int64)
+        valid = flat_t != ignore_index
+        safe = np.where(valid, flat_t, 0)
+        if np.any((safe < 0) | (safe >= classes)):
+            raise IndexError(f"target out of range for {classes} classes")
+        tgt = device.from_numpy(flat_t)
+        t_shape = t.shape
     x = tl.data if tl.dtype.kind == "f" else cast_array(tl.data, np.dtype(np.float64))
-    rows = flat_t.size
+    rows = tgt.size
     code = dtype_code(x.dtype)
     red = _RED[reduction]
-    tgt = device.from_numpy(flat_t)
     lse = device.empty((rows,), x.dtype)
     row_loss = device.empty((rows,), x.dtype)
     n_valid = device.empty((1,), np.int64)
-    out = row_loss.reshape(t.shape) if red == 2 else device.empty((), x.dtype)
+    out = row_loss.reshape(t_shape) if red == 2 else device.empty((), x.dtype)
     check(lib.tg_cross_entropy_forward(code, x.ptr, tgt.ptr, lse.ptr, row_loss.ptr, out.ptr,
-                                       rows, classes, ignore_index, red, n_valid.ptr, None,
+                                       rows, classes, ignore_index, red, n_valid.ptr, bad,
                                        device.stream()), "cross_entropy")
 
     def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:

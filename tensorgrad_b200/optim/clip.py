@@ -62,8 +62,12 @@ def grad_norm_device(params: Iterable[Tensor]) -> tuple[DeviceArray, dict[str, l
     return total, segs
 
 
-def clip_grad_norm_(params: Iterable[Tensor], max_norm: float, eps: float = 1e-6) -> float:
+def clip_grad_norm_(params: Iterable[Tensor], max_norm: float, eps: float = 1e-6, *,
+                    sync: bool = True) -> float | Tensor:
     """Rescale gradients in place so their global L2 norm is at most ``max_norm``.
+
+    The norm and the scale stay on the device. ``sync=False`` returns the norm as a 0-d device
+    tensor instead of a float, so a training step does not wait for the device here.
 
     Returns:
         The total norm before clipping.
@@ -74,4 +78,6 @@ def clip_grad_norm_(params: Iterable[Tensor], max_norm: float, eps: float = 1e-6
         check(lib.tg_clip_scale_multi(code, len(bufs), ptr_array(b.ptr for b in bufs),
                                       int64_array(b.size for b in bufs), total.ptr, max_norm,
                                       eps, None, device.stream()), "clip")
+    if not sync:
+        return Tensor._wrap(total.reshape(()))
     return float(total.item())

@@ -35,7 +35,9 @@ def build(cfg: ogpt.Config, params: dict[str, np.ndarray], dtype):
     return model, names
 
 
-def run_steps(cfg, spec_batch, spec_seq, seed, steps, max_norm, dtype):
+def run_steps(cfg, spec_batch, spec_seq, seed, steps, max_norm, dtype, device_ids=False):
+    """``device_ids``: token ids and targets as device tensors (checked and sorted on the
+    device) and the clip norm returned as a device scalar, the no-round-trip step."""
     import tensorgrad_b200 as tg
 
     model, names = build(cfg, ogpt.init_params(cfg, seed), dtype)
@@ -44,10 +46,13 @@ def run_steps(cfg, spec_batch, spec_seq, seed, steps, max_norm, dtype):
     out = []
     for step in range(1, steps + 1):
         ids, targets = ogpt.synthetic_batch(cfg, spec_batch, spec_seq, seed + step)
+        if device_ids:
+            ids, targets = tg.Tensor(ids), tg.Tensor(targets)
         loss = tg.cross_entropy(model(ids), targets)
         opt.zero_grad()
         loss.backward()
-        total = tg.optim.clip_grad_norm_(params, max_norm)
+        total = tg.optim.clip_grad_norm_(params, max_norm, sync=not device_ids)
+        total = float(total.item()) if device_ids else total
         rec = {"loss": float(loss.item()), "total_norm": total,
                "grads": {n: p.grad.numpy() for n, p in zip(names, params, strict=True)},
                "before": {n: p.numpy() for n, p in zip(names, params, strict=True)}}
@@ -98,10 +103,11 @@ def test_gpt_small_two_steps_match_reference_fixture(dtype, rel):
     check_against(recs, golden_steps(gold, s["steps"], list(recs[0]["grads"])), rel)
 
 
-def test_char_gpt_config_matches_oracle():
+@pytest.mark.parametrize("device_ids", [False, True], ids=["host_ids", "device_ids"])
+def test_char_gpt_config_matches_oracle(device_ids):
     cfg = ogpt.Config(vocab_size=65, block_size=128, n_layer=4, n_head=4, n_embd=128)
     seed, batch = 7, 32
-    recs = run_steps(cfg, batch, 128, seed, 1, 1.0, np.float32)
+    recs = run_steps(cfg, batch, 128, seed, 1, 1.0, np.float32, device_ids)
     ref = ogpt.train_step(ogpt.init_params(cfg, seed),
                           *ogpt.synthetic_batch(cfg, batch, 128, seed + 1), cfg, max_norm=1.0)
     check_against(recs, [ref], 1e-4)

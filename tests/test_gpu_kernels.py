@@ -175,6 +175,45 @@ def test_embedding_scatter_add(dtype, vocab):
     assert_parity(tw.grad.numpy(), O.embedding_backward(ids, g, vocab), rel(dtype), "scatter")
 
 
+@pytest.mark.parametrize("vocab,shape", [(5, (7, 11)), (65, (32, 128)), (50304, (3, 1000))])
+def test_embedding_device_ids(dtype, vocab, shape):
+    """Device-resident ids: gather checked on the device, the VJP's stable order sorted on the
+    device; the gradient equals the oracle's (same order of summation per row) and the result
+    of the host-id path bit for bit."""
+    import tensorgrad_b200 as tg
+
+    rng = np.random.default_rng(vocab + shape[1])
+    ids = rng.integers(0, vocab, size=shape)
+    ids[0, :5] = ids[0, 0]  # a run of equal ids
+    dim = 8
+    w = rng.standard_normal((vocab, dim))
+    g = rng.standard_normal((*shape, dim))
+    tw = tensor(w, dtype)
+    out = tg.embedding(tg.Tensor(ids), tw)
+    out.backward(g.astype(dtype))
+    assert np.array_equal(out.numpy(), w.astype(dtype)[ids])
+    assert_parity(tw.grad.numpy(), O.embedding_backward(ids, g, vocab), rel(dtype), "scatter")
+    tw_host = tensor(w, dtype)
+    tg.embedding(ids, tw_host).backward(g.astype(dtype))
+    assert np.array_equal(tw.grad.numpy(), tw_host.grad.numpy())
+
+
+def test_device_ids_and_targets_out_of_range_raise_at_sync():
+    import tensorgrad_b200 as tg
+
+    w = tg.Tensor(np.arange(12.0).reshape(4, 3))
+    out = tg.embedding(tg.Tensor(np.array([1, 4])), w)  # id 4 is out of range: a zero row
+    with pytest.raises(IndexError, match="embedding ids"):
+        out.numpy()
+    assert np.array_equal(tg.embedding(tg.Tensor(np.array([1, 2])), w).numpy(),
+                          np.arange(12.0).reshape(4, 3)[[1, 2]])
+    loss = tg.cross_entropy(tg.Tensor(np.zeros((2, 3))), tg.Tensor(np.array([0, 3])))
+    with pytest.raises(IndexError, match="target out of range"):
+        loss.item()
+    ok = tg.cross_entropy(tg.Tensor(np.zeros((2, 3))), tg.Tensor(np.array([0, 2])))
+    assert ok.item() == pytest.approx(np.log(3.0))
+
+
 def test_embedding_rejects_bad_ids():
     import tensorgrad_b200 as tg
 
@@ -215,6 +254,22 @@ def test_cross_entropy_all_ignored_and_bad_target():
     assert out.item() == 0.0
     with pytest.raises(IndexError, match="target out of range"):
         tg.cross_entropy(tg.Tensor(np.zeros((2, 3))), np.array([0, 3]))
+
+
+def test_cross_entropy_device_targets(dtype):
+    import tensorgrad_b200 as tg
+
+    rng = np.random.default_rng(5)
+    logits = rng.standard_normal((300, 65)) * 2
+    target = rng.integers(0, 65, size=300)
+    target[::7] = -100
+    tl = tensor(logits, dtype)
+    loss = tg.cross_entropy(tl, tg.Tensor(target))
+    loss.backward()
+    ref, logp = O.cross_entropy_forward(logits, target)
+    assert float(loss.item()) == pytest.approx(float(ref), rel=rel(dtype))
+    assert_parity(tl.grad.numpy(), O.cross_entropy_backward(1.0, logp, target, logits.shape),
+                  rel(dtype), "ce grad")
 
 
 # ------------------------------------------------------------------------------- attention
