@@ -228,8 +228,9 @@ class MHAWorkload(Workload):
 
         dev = tuple(tg.Tensor(a, requires_grad=i < 3) for i, a in enumerate(arrays))
         nbytes = arrays[0].nbytes
+        outs = [device.pinned_empty(self.SHAPE, np.float32) for _ in range(3)]
         return Built(step, dev, _pinned(device, arrays), 4 * nbytes, 3 * nbytes,
-                     lambda grads: [g.numpy() for g in grads])
+                     lambda grads: [g.numpy(out=o) for g, o in zip(grads, outs, strict=True)])
 
     def cpu_step(self, threads: int):
         import numpy as np

@@ -245,11 +245,14 @@ int attention_tc_backward(const tg_attn_shape* s, const float* q, const float* k
   row_dot_kernel<<<grid_for(rows * 32, 256), 256, 0, st>>>(dO, O, delta, p.H, p.Tq, p.D, rows);
   if ((rc = check_launch("attention delta"))) return rc;
   const int skip = causal ? GEMM_K_SKIP_UPPER : GEMM_K_FULL;
-  if ((rc = bgemm(bgemm_args(0, 1, p.Tq, p.Tk, p.D, scale, Q, K, Sv, p, skip), st))) return rc;
-  // dP = dO V^T, with P and dS = P (dP - delta) scale produced by the epilogue.
+  // P = exp(scale Q K^T - lse) straight from the product's epilogue (the scores are never
+  // stored), then dP = dO V^T with dS = P (dP - delta) scale produced by its epilogue.
+  GemmArgs<float> gp = bgemm_args(0, 1, p.Tq, p.Tk, p.D, scale, Q, K, Sv, p, skip);
+  gp.epi = GEMM_EPI_SOFTMAX_P;
+  gp.rv0 = lse;
+  if ((rc = bgemm(gp, st))) return rc;
   GemmArgs<float> g = bgemm_args(0, 1, p.Tq, p.Tk, p.D, scale, dO, V, dPv, p, skip);
   g.epi = GEMM_EPI_SOFTMAX_DS;
-  g.rv0 = lse;
   g.rv1 = delta;
   g.aux = S;
   if ((rc = bgemm(g, st))) return rc;

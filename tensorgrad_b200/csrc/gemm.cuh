@@ -11,7 +11,7 @@ namespace tg {
 //   GEMM_K_SKIP_UPPER -- full reduction, but tiles whose first column n0 > m0 + 127 are
 //                        skipped (never written)
 enum GemmKMode { GEMM_K_FULL = 0, GEMM_K_UP_TO_ROW = 1, GEMM_K_FROM_ROW = 2, GEMM_K_SKIP_UPPER = 3 };
-enum GemmEpilogue { GEMM_EPI_STORE = 0, GEMM_EPI_SOFTMAX_DS = 1 };
+enum GemmEpilogue { GEMM_EPI_STORE = 0, GEMM_EPI_SOFTMAX_DS = 1, GEMM_EPI_SOFTMAX_P = 2 };
 
 template <typename T>
 struct GemmArgs {
@@ -42,10 +42,12 @@ struct GemmArgs {
   // arbitrary strides, e.g. the packed QKV projection). heads == 1: plain batch strides.
   int64_t heads = 1;
   int64_t stride_ah = 0, stride_bh = 0, stride_ch = 0;
-  // Epilogue (tensor-core path): GEMM_EPI_STORE, or GEMM_EPI_SOFTMAX_DS for the attention
-  // backward: with the product dP, the scores S in `aux` (same layout as C), rv0 = lse and
-  // rv1 = delta per output row (index bz * m + row), it writes P = exp(S - lse) (zero above
-  // the diagonal when kmode is GEMM_K_SKIP_UPPER) over S and dS = P (dP - delta) alpha to C.
+  // Epilogue (tensor-core path), for the attention backward besides GEMM_EPI_STORE:
+  //   GEMM_EPI_SOFTMAX_P : C = P = exp(alpha * acc - rv0[row]) with rv0 = lse per output row
+  //                        (index bz * m + row), zero above the diagonal when kmode is
+  //                        GEMM_K_SKIP_UPPER (the scores S = alpha Q K^T are never stored);
+  //   GEMM_EPI_SOFTMAX_DS: C = dS = P (acc - rv1[row]) alpha with P read from `aux` (same
+  //                        layout as C) and rv1 = delta per output row.
   int epi = 0;
   const T* rv0 = nullptr;
   const T* rv1 = nullptr;

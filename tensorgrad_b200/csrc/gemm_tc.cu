@@ -176,6 +176,23 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// TMA store of a shared-memory box (bulk-group completion) and its group bookkeeping.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int x,
+                                             int y, int h, int b) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "r"(h), "r"(b)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N committed store groups still read their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                    smem_u32(slot)),
@@ -309,14 +326,20 @@ struct TcArgs {
   int heads;              // batch entry bz = outer * heads + head
   int64_t stride_ch;      // head stride of C
   int epi;                // GemmEpilogue
-  const float* rv0;       // GEMM_EPI_SOFTMAX_DS: lse, delta per row; aux = scores in, P out
+  const float* rv0;       // softmax epilogues: lse (P) or delta (dS) per row
   const float* rv1;
-  float* aux;
+  float* aux;             // GEMM_EPI_SOFTMAX_DS: P in (same layout as C)
+  int tma_c;              // 1: whole tiles go out through shared memory and TMA stores (tmC),
+                          //    the dS epilogue's P through TMA loads (tmX)
 };
 
 constexpr int kThreads = 512;
 constexpr int kSplitWarp0 = 4, kSplitThreads = 256;  // warps 4..11
 constexpr int kEpiWarp0 = 12;                        // warps 12..15
+// Epilogue staging: per epilogue warp two 32 x 32 fp32 boxes (128-byte swizzle), one TMA
+// store (or load) each.
+constexpr uint32_t kEpiBox = 32 * 32 * 4;
+constexpr uint32_t kEpiBytes = 4 * 2 * kEpiBox;
 
 // PAIR: a CTA of a cta_group::2 pair holds its 128 rows of A and half of the BN columns of B.
 template <int BN, bool PAIR = false>
@@ -390,19 +413,22 @@ __device__ __forceinline__ TileInfo tile_info(const TcArgs& a, int t, int bn, in
 template <int BN, int STAGES, bool A_MN, bool B_MN, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX,
                TcArgs args) {
   using L = Layout<BN, PAIR>;
   constexpr int TILE_M = PAIR ? 2 * BM : BM;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * L::STAGE);
+  uint8_t* ebuf_all = smem + STAGES * L::STAGE;  // kEpiBytes of epilogue staging
+  uint64_t* full = reinterpret_cast<uint64_t*>(ebuf_all + kEpiBytes);
   uint64_t* split = full + STAGES;
   uint64_t* empty = split + STAGES;
   uint64_t* acc_full = empty + STAGES;   // [2]
   uint64_t* acc_empty = acc_full + 2;    // [2]
   uint64_t* drain = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* ebar_all = drain + 1;        // [4 warps][2]: epilogue TMA loads
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ebar_all + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -416,8 +442,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      // PAIR: one arrival per local split warp, plus (even CTA) the odd CTA's relay.
-      mbar_init(&split[s], PAIR ? (kSplitThreads / 32) + (rank == 0 ? 1 : 0) : kSplitThreads);
+      // One arrival per split warp, plus (even CTA of a pair) the odd CTA's relay.
+      mbar_init(&split[s], (kSplitThreads / 32) + (PAIR && rank == 0 ? 1 : 0));
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -425,6 +451,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       mbar_init(&acc_empty[b], PAIR ? 8 : 4);  // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
+    for (int b = 0; b < 8; ++b) mbar_init(&ebar_all[b], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -594,15 +621,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
           for (int i = t0; i < (int)(L::B_BYTES / 16); i += kSplitThreads) lo4(b_raw, b_lo, i);
         }
+        // One arrival per warp after all its lanes fenced (256 arrivals on one barrier would
+        // serialise in the shared-memory atomics); in a pair the odd CTA's relay thread
+        // forwards its stage to the even CTA.
         fence_proxy_async_smem();
-        if (PAIR) {
-          // One local arrival per warp after all lanes fenced; the odd CTA's relay thread
-          // forwards its stage to the even CTA.
-          __syncwarp();
-          if ((threadIdx.x & 31) == 0) mbar_arrive(&split[s]);
-        } else {
-          mbar_arrive(&split[s]);
-        }
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive(&split[s]);
       }
     }
   } else if (warp >= kEpiWarp0) {
@@ -612,10 +636,124 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                      (args.stride_ch % 4 == 0) &&
                      ((reinterpret_cast<uintptr_t>(args.c) & 15) == 0) &&
                      (!args.bias || (reinterpret_cast<uintptr_t>(args.bias) & 15) == 0);
+    // Shared-memory staging of this warp: two 32 x 32 boxes with their load barriers.
+    uint8_t* ebuf = ebuf_all + ew * 2 * kEpiBox;
+    uint64_t* ebar = ebar_all + 2 * ew;
+    uint32_t eph = 0;  // phase bits of ebar[0], ebar[1]
+    int q = 0;         // boxes stored so far (alternates the two buffers)
     for (int t = unit; t < total; t += units) {
       const TileInfo ti = tile_info(args, t, BN, TILE_M);
       if (ti.skip) continue;
       const int buf = tc & 1;
+      if (!PAIR && args.tma_c && args.splits == 1) {
+        // Whole 32 x 32 boxes: lane = row in registers, written to shared memory with a
+        // 128-byte swizzle (conflict-free), stored by one TMA store per box (rows and columns
+        // past the product are clipped by the map). dS also reads its P boxes by TMA, two
+        // boxes ahead, the first two issued before the accumulator is ready.
+        const int hh = ti.bz % args.heads, bo = ti.bz / args.heads;
+        const int row0 = (int)ti.m0 + 32 * ew;
+        const bool rows_in = row0 < args.m;
+        const int64_t left = (args.n - ti.n0 + 31) / 32;
+        const int nch = (int)(left < BN / 32 ? left : BN / 32);
+        const bool dsm = args.epi == GEMM_EPI_SOFTMAX_DS;
+        const bool pmm = args.epi == GEMM_EPI_SOFTMAX_P;
+        const bool causal = args.kmode == GEMM_K_SKIP_UPPER;
+        if (dsm && rows_in) {
+          if (lane == 0) {
+            bulk_wait_read<0>();
+            for (int b = 0; b < 2 && b < nch; ++b) {
+              mbar_arrive_expect_tx(&ebar[b], kEpiBox);
+              tma_load_4d(ebuf + b * kEpiBox, &tmX, &ebar[b], (int)ti.n0 + 32 * b, row0, hh, bo);
+            }
+          }
+          __syncwarp();
+        }
+        const bool have =
+            __all_sync(0xffffffffu, wait_bar(&acc_full[buf], (tc >> 1) & 1, abort_flag));
+        if (!have) {
+          if (dsm && rows_in)
+            for (int b = 0; b < 2 && b < nch; ++b) wait_bar(&ebar[b], (eph >> b) & 1, abort_flag, false);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc = tmem + (uint32_t)(buf * BN) + ((uint32_t)(32 * ew) << 16);
+        const int64_t row = (int64_t)row0 + lane;
+        float rv = 0.f;
+        if ((dsm || pmm) && row < args.m)
+          rv = (dsm ? args.rv1 : args.rv0)[(int64_t)ti.bz * args.m + row];
+        bool ok = true;
+#pragma unroll 1
+        for (int cc = 0; cc < nch && rows_in; ++cc) {
+          uint32_t r[32];
+          tmem_ld32(acc + (uint32_t)(cc * 32), r);
+          const int c0 = (int)ti.n0 + cc * 32;
+          float4* box;
+          if (dsm) {
+            const int b = cc & 1;
+            box = reinterpret_cast<float4*>(ebuf + b * kEpiBox);
+            if (!__all_sync(0xffffffffu, wait_bar(&ebar[b], (eph >> b) & 1, abort_flag, false))) {
+              ok = false;
+              break;
+            }
+            eph ^= 1u << b;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const float4 pv = box[lane * 8 + (k ^ (lane & 7))];
+              const float a0 = ti.nk ? __uint_as_float(r[4 * k]) : 0.f;
+              const float a1 = ti.nk ? __uint_as_float(r[4 * k + 1]) : 0.f;
+              const float a2 = ti.nk ? __uint_as_float(r[4 * k + 2]) : 0.f;
+              const float a3 = ti.nk ? __uint_as_float(r[4 * k + 3]) : 0.f;
+              r[4 * k] = __float_as_uint(pv.x * (a0 - rv) * args.alpha);
+              r[4 * k + 1] = __float_as_uint(pv.y * (a1 - rv) * args.alpha);
+              r[4 * k + 2] = __float_as_uint(pv.z * (a2 - rv) * args.alpha);
+              r[4 * k + 3] = __float_as_uint(pv.w * (a3 - rv) * args.alpha);
+            }
+            __syncwarp();  // every lane has read the box before it is overwritten
+          } else {
+            box = reinterpret_cast<float4*>(ebuf + (q & 1) * kEpiBox);
+            ++q;
+            if (lane == 0) bulk_wait_read<1>();  // the store from this buffer two boxes ago
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float a = ti.nk ? __uint_as_float(r[j]) : 0.f;
+              float v;
+              if (pmm) {
+                v = (causal && c0 + j > row) ? 0.f : expf(__fmul_rn(args.alpha, a) - rv);
+              } else {
+                v = args.alpha * a;
+                if (args.bias && c0 + j < args.n) v += args.bias[c0 + j];
+              }
+              r[j] = __float_as_uint(v);
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            box[lane * 8 + (k ^ (lane & 7))] =
+                make_float4(__uint_as_float(r[4 * k]), __uint_as_float(r[4 * k + 1]),
+                            __uint_as_float(r[4 * k + 2]), __uint_as_float(r[4 * k + 3]));
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_4d(&tmC, box, c0, row0, hh, bo);
+            bulk_commit();
+          }
+          if (dsm && cc + 2 < nch) {
+            if (lane == 0) {
+              bulk_wait_read<0>();
+              mbar_arrive_expect_tx(&ebar[cc & 1], kEpiBox);
+              tma_load_4d(box, &tmX, &ebar[cc & 1], c0 + 64, row0, hh, bo);
+            }
+            __syncwarp();
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        ++tc;
+        if (!ok) break;
+        continue;
+      }
       // tcgen05.ld is warp-collective: decide per warp.
       const bool have = __all_sync(0xffffffffu, wait_bar(&acc_full[buf], (tc >> 1) & 1, abort_flag));
       if (!have) break;
@@ -641,60 +779,51 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const float* bias = part ? nullptr : args.bias;
       const bool vrow = part ? (args.n % 4 == 0) : vec;
       const uint32_t acc = tmem + (uint32_t)(buf * BN) + ((uint32_t)(32 * ew) << 16);
-      // Attention backward: P = exp(S - lse) over S (in aux), dS = P (dP - delta) alpha to C.
+      // Attention softmax epilogues: P = exp(alpha acc - lse) (zero above the diagonal of a
+      // causal product), or dS = P (acc - delta) alpha with P read from aux.
       const bool ds = args.epi == GEMM_EPI_SOFTMAX_DS && !part;
+      const bool pm = args.epi == GEMM_EPI_SOFTMAX_P && !part;
       const bool causal = args.kmode == GEMM_K_SKIP_UPPER;
-      float* arow = ds ? args.aux + (crow - args.c) : nullptr;
-      float lse_r = 0.f, delta_r = 0.f;
-      if (ds && row < args.m) {
-        lse_r = args.rv0[(int64_t)ti.bz * args.m + row];
-        delta_r = args.rv1[(int64_t)ti.bz * args.m + row];
-      }
+      const float* arow = ds ? args.aux + (crow - args.c) : nullptr;
+      float rv = 0.f;
+      if ((ds || pm) && row < args.m) rv = (ds ? args.rv1 : args.rv0)[(int64_t)ti.bz * args.m + row];
 #pragma unroll 1
       for (int cc = 0; cc < BN / 32; ++cc) {
         uint32_t r[32];
         tmem_ld32(acc + (uint32_t)(cc * 32), r);
         const int64_t c0 = ti.n0 + cc * 32;
-        if (ds && row < args.m && c0 < args.n) {
-          // Loads of each 16-column half first: the stores below may alias them for the
-          // compiler, which would otherwise serialise every load behind the previous store.
+        if ((ds || pm) && row < args.m && c0 < args.n) {
           const bool full = vrow && c0 + 32 <= args.n;
 #pragma unroll
           for (int h = 0; h < 32; h += 16) {
             float sv[16];
-            if (full) {
+            if (ds && full) {
 #pragma unroll
               for (int j = 0; j < 16; j += 4) {
                 const float4 t = *reinterpret_cast<const float4*>(arow + c0 + h + j);
                 sv[j] = t.x; sv[j + 1] = t.y; sv[j + 2] = t.z; sv[j + 3] = t.w;
               }
-            } else {
+            } else if (ds) {
 #pragma unroll
               for (int j = 0; j < 16; ++j) sv[j] = c0 + h + j < args.n ? arow[c0 + h + j] : 0.f;
             }
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              const float p = (causal && c0 + h + j > row) ? 0.f : expf(sv[j] - lse_r);
-              sv[j] = p;
-              r[h + j] = __float_as_uint(p * (__uint_as_float(r[h + j]) - delta_r) * alpha);
+              const float a = ti.nk ? __uint_as_float(r[h + j]) : 0.f;
+              r[h + j] = __float_as_uint(
+                  ds ? sv[j] * (a - rv) * alpha
+                     : ((causal && c0 + h + j > row) ? 0.f : expf(__fmul_rn(alpha, a) - rv)));
             }
             if (full) {
 #pragma unroll
-              for (int j = 0; j < 16; j += 4) {
-                *reinterpret_cast<float4*>(arow + c0 + h + j) =
-                    make_float4(sv[j], sv[j + 1], sv[j + 2], sv[j + 3]);
+              for (int j = 0; j < 16; j += 4)
                 *reinterpret_cast<float4*>(crow + c0 + h + j) =
                     make_float4(__uint_as_float(r[h + j]), __uint_as_float(r[h + j + 1]),
                                 __uint_as_float(r[h + j + 2]), __uint_as_float(r[h + j + 3]));
-              }
             } else {
 #pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                if (c0 + h + j < args.n) {
-                  arow[c0 + h + j] = sv[j];
-                  crow[c0 + h + j] = __uint_as_float(r[h + j]);
-                }
-              }
+              for (int j = 0; j < 16; ++j)
+                if (c0 + h + j < args.n) crow[c0 + h + j] = __uint_as_float(r[h + j]);
             }
           }
         } else if (row < args.m && c0 < args.n) {
@@ -750,6 +879,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       }
       ++tc;
     }
+    if (lane == 0) bulk_wait_all();  // TMA stores complete before the kernel ends
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
@@ -957,7 +1088,7 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
     rc = make_map(&tb, p.b, p.k, p.n, p.ldb, bh, p.stride_bh, bn, p.stride_b, BK, L::B_ROWS,
                   kSwK);
   if (rc != TG_OK) return rc;
-  const size_t smem = STAGES * L::STAGE + 1024 + 256;
+  const size_t smem = STAGES * L::STAGE + kEpiBytes + 1024 + 512;
   static bool configured = false;
   static int max_pairs = 0;
   if (!configured) {
@@ -1009,6 +1140,25 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
     a.splits = (nk_all + a.kb_per_split - 1) / a.kb_per_split;  // every split non-empty
     a.ws = p.workspace;
   }
+  // Epilogue through shared memory and TMA stores: whole-tile outputs (no split partials,
+  // no NCHW scatter, no accumulation into C) whose rows suit a tensor map.
+  CUtensorMap tcm = ta, txm = ta;
+  a.tma_c = 0;
+  {
+    auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    const bool strides_ok = p.ldc % 4 == 0 && (p.heads == 1 || p.stride_ch % 4 == 0) &&
+                            (nb == 1 || p.stride_c % 4 == 0);
+    const bool want = !PAIR && a.splits == 1 && p.c_hw == 0 && p.beta == 0.f && p.m >= 32 &&
+                      p.n >= 32 && strides_ok && al16(p.c) &&
+                      (p.epi != GEMM_EPI_SOFTMAX_DS || (p.aux && al16(p.aux)));
+    if (want &&
+        make_map(&tcm, p.c, p.n, p.m, p.ldc, p.heads, p.stride_ch, nb, p.stride_c, 32, 32,
+                 CU_TENSOR_MAP_SWIZZLE_128B) == TG_OK &&
+        (p.epi != GEMM_EPI_SOFTMAX_DS ||
+         make_map(&txm, p.aux, p.n, p.m, p.ldc, p.heads, p.stride_ch, nb, p.stride_c, 32, 32,
+                  CU_TENSOR_MAP_SWIZZLE_128B) == TG_OK))
+      a.tma_c = 1;
+  }
   const int64_t tiles = (int64_t)a.m_tiles * a.n_tiles * a.batch * a.splits;
   if (PAIR) {
     const int pairs = (int)(tiles < max_pairs ? tiles : max_pairs);
@@ -1024,10 +1174,10 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    TG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, ta, tb, a));
+    TG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, ta, tb, tcm, txm, a));
   } else {
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
-    kernel<<<grid, kThreads, smem, stream>>>(ta, tb, a);
+    kernel<<<grid, kThreads, smem, stream>>>(ta, tb, tcm, txm, a);
   }
   if (a.splits > 1) {
     const int64_t mn = p.m * p.n;

@@ -159,9 +159,15 @@ class DeviceArray:
         return _shape_ops.permute_array(self, tuple(reversed(range(self.ndim))))
 
     # ------------------------------------------------------------- host transfer
-    def numpy(self) -> np.ndarray:
-        """A host copy (synchronises the stream)."""
-        out = np.empty(self.shape, dtype=self.dtype)
+    def numpy(self, out: np.ndarray | None = None) -> np.ndarray:
+        """A host copy (synchronises the stream), into ``out`` when given (a C-contiguous
+        array of this shape and dtype; page-locked memory is copied at full bus speed)."""
+        if out is None:
+            out = np.empty(self.shape, dtype=self.dtype)
+        elif (out.shape != tuple(self.shape) or out.dtype != self.dtype
+              or not out.flags.c_contiguous):
+            raise ValueError(f"numpy(out=...) needs a C-contiguous {self.dtype} array of shape "
+                             f"{tuple(self.shape)}, got {out.dtype} {out.shape}")
         if out.nbytes:
             check(lib.tg_memcpy_d2h(out.ctypes.data, self.ptr, out.nbytes, _State.stream), "d2h")
             synchronize()

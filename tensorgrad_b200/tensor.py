@@ -216,9 +216,10 @@ class Tensor:
         return self
 
     # ------------------------------------------------------------------ conversion
-    def numpy(self) -> np.ndarray:
-        """A host copy of the data."""
-        return self.data.numpy()
+    def numpy(self, out: np.ndarray | None = None) -> np.ndarray:
+        """A host copy of the data (into ``out`` when given, e.g. a page-locked buffer from
+        ``device.pinned_empty``, which the copy engine fills at full bus speed)."""
+        return self.data.numpy(out)
 
     def __array__(self, dtype: Any = None, copy: bool | None = None) -> np.ndarray:
         arr = self.data.numpy()
