@@ -267,6 +267,28 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64
       : "memory");
 }
 
+// A from tensor memory (128 lanes = rows, 8 columns = the k-step's 8 tf32 values per row).
+__device__ __forceinline__ void mma_tf32_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 8 consecutive 32-bit columns of this warp's 32 lanes.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile(
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -335,6 +357,8 @@ struct TcArgs {
 
 constexpr int kThreads = 512;
 constexpr int kSplitWarp0 = 4, kSplitThreads = 256;  // warps 4..11
+// Split warps per k-block: one group of 8 warps (two per TMEM lane quarter).
+constexpr int kSplitGroups = 1, kGroupThreads = kSplitThreads / kSplitGroups;
 constexpr int kEpiWarp0 = 12;                        // warps 12..15
 // Epilogue staging: per epilogue warp two 32 x 32 fp32 boxes (128-byte swizzle), one TMA
 // store (or load) each.
@@ -342,19 +366,25 @@ constexpr uint32_t kEpiBox = 32 * 32 * 4;
 constexpr uint32_t kEpiBytes = 4 * 2 * kEpiBox;
 
 // PAIR: a CTA of a cta_group::2 pair holds its 128 rows of A and half of the BN columns of B.
-template <int BN, bool PAIR = false>
+template <int BN, bool PAIR = false, bool ATM = false>
 struct Layout {
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
   static constexpr uint32_t A_BYTES = BM * BK * 4;  // 8 KB
   static constexpr uint32_t B_BYTES = B_ROWS * BK * 4;
-  static constexpr uint32_t STAGE = 2 * A_BYTES + 2 * B_BYTES;  // raw + lo of A and B
-  static constexpr uint32_t TMEM_COLS = 2 * BN;                 // two accumulators
+  // ATM (A in tensor memory): a stage holds raw A, raw B and B's lo; A's hi and lo go to
+  // TMEM columns after the two accumulators (2 * BK per stage). Otherwise raw + lo of both.
+  static constexpr uint32_t B_OFF = ATM ? A_BYTES : 2 * A_BYTES;
+  static constexpr uint32_t STAGE = B_OFF + 2 * B_BYTES;
+  static constexpr uint32_t ACC_COLS = 2 * BN;  // two accumulators
+  static constexpr uint32_t TMEM_COLS = ATM ? 512 : ACC_COLS;
 };
 
-template <int BN, bool PAIR = false>
+template <int BN, bool PAIR = false, bool ATM = false>
 constexpr int stages_for() {
-  constexpr uint32_t s = Layout<BN, PAIR>::STAGE;
-  return (200 * 1024) / s > 8 ? 8 : (200 * 1024) / s;
+  constexpr uint32_t s = Layout<BN, PAIR, ATM>::STAGE;
+  constexpr int by_smem = (int)((200 * 1024) / s);
+  constexpr int cap = ATM ? (int)((512 - 2 * BN) / (2 * BK)) : 8;
+  return by_smem > cap ? cap : by_smem;
 }
 
 // Descriptor of k-step kk (8 tf32 along K) of a stage tile.
@@ -410,12 +440,13 @@ __device__ __forceinline__ TileInfo tile_info(const TcArgs& a, int t, int bn, in
 // CTAs on its own 128 rows and half of B, except the MMA issuer (even CTA only). The split
 // warps and the epilogue of the odd CTA arrive on the even CTA's barriers; the MMA commits
 // arrive on both CTAs' barriers.
-template <int BN, int STAGES, bool A_MN, bool B_MN, bool PAIR>
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool PAIR, bool ATM>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX,
                TcArgs args) {
-  using L = Layout<BN, PAIR>;
+  using L = Layout<BN, PAIR, ATM>;
+  static_assert(!ATM || (!PAIR && !A_MN), "A in tensor memory: single CTA, K-major A");
   constexpr int TILE_M = PAIR ? 2 * BM : BM;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -443,7 +474,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       // One arrival per split warp, plus (even CTA of a pair) the odd CTA's relay.
-      mbar_init(&split[s], (kSplitThreads / 32) + (PAIR && rank == 0 ? 1 : 0));
+      mbar_init(&split[s], (kGroupThreads / 32) + (PAIR && rank == 0 ? 1 : 0));
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -476,7 +507,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           if (round > 0 && !wait_bar(&empty[s], (round - 1) & 1, abort_flag)) { stop = true; break; }
           uint8_t* st = smem + s * L::STAGE;
           uint8_t* a_raw = st;
-          uint8_t* b_raw = st + 2 * L::A_BYTES;
+          uint8_t* b_raw = st + L::B_OFF;
           mbar_arrive_expect_tx(&full[s], L::A_BYTES + L::B_BYTES);
           const int k0 = (ti.kb0 + j) * BK;
           const int hh = ti.bz % args.heads, bo = ti.bz / args.heads;
@@ -554,12 +585,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           tc_fence_after();
           const uint32_t st = smem_u32(smem + s * L::STAGE);
           const uint32_t a_raw = st, a_lo = st + L::A_BYTES;
-          const uint32_t b_raw = st + 2 * L::A_BYTES, b_lo = b_raw + L::B_BYTES;
+          const uint32_t b_raw = st + L::B_OFF, b_lo = b_raw + L::B_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 8; ++kk) {
             const uint64_t ah = tile_desc<A_MN>(a_raw, kk), al = tile_desc<A_MN>(a_lo, kk);
             const uint64_t bh = tile_desc<B_MN>(b_raw, kk), bl = tile_desc<B_MN>(b_lo, kk);
-            if (PAIR) {
+            if (ATM) {
+              // A's hi (the raw bits) and lo of this stage in TMEM columns after the
+              // accumulators: [hi k 0..15 | lo k 0..15].
+              const uint32_t th = tmem + L::ACC_COLS + (uint32_t)(s * 2 * BK + kk * 8);
+              if (args.raw) {
+                mma_tf32_ta(acc, th, bh, idesc, (j | kk) != 0);
+              } else {
+                mma_tf32_ta(acc, th + BK, bh, idesc, (j | kk) != 0);
+                mma_tf32_ta(acc, th, bl, idesc, 1);
+                mma_tf32_ta(acc, th, bh, idesc, 1);
+              }
+            } else if (PAIR) {
               if (args.raw) {
                 mma_tf32_pair(acc, ah, bh, idesc, (j | kk) != 0);
               } else {
@@ -591,35 +633,72 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       }
     }
   } else if (warp >= kSplitWarp0 && warp < kEpiWarp0) {
-    const int t0 = threadIdx.x - kSplitWarp0 * 32;
+    constexpr int kGroupWarps = kGroupThreads / 32;
+    const int grp = (warp - kSplitWarp0) / kGroupWarps;
+    const int t0 = threadIdx.x - (kSplitWarp0 + kGroupWarps * grp) * 32;  // 0 .. kGroupThreads-1
     int it = 0;
     bool stop = false;
     for (int t = unit; t < total && !stop; t += units) {
       const TileInfo ti = tile_info(args, t, BN, TILE_M);
       for (int j = 0; j < ti.nk; ++j, ++it) {
+        if (it % kSplitGroups != grp) continue;
         const int s = it % STAGES, round = it / STAGES;
         // Warp-uniform decision: the warp stays converged for the arrival below.
         const bool landed = wait_bar(&full[s], round & 1, abort_flag);
         if (!__all_sync(0xffffffffu, landed)) { stop = true; break; }
+        uint8_t* st = smem + s * L::STAGE;
+        auto lo_of = [](float x) {
+          return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+        };
+        auto lo4 = [&](const float4* x, float4* lo, int i) {
+          const float4 v = x[i];
+          lo[i] = make_float4(lo_of(v.x), lo_of(v.y), lo_of(v.z), lo_of(v.w));
+        };
         if (!args.raw) {
-          uint8_t* st = smem + s * L::STAGE;
-          const float4* a_raw = reinterpret_cast<const float4*>(st);
-          float4* a_lo = reinterpret_cast<float4*>(st + L::A_BYTES);
-          const float4* b_raw = reinterpret_cast<const float4*>(st + 2 * L::A_BYTES);
-          float4* b_lo = reinterpret_cast<float4*>(st + 2 * L::A_BYTES + L::B_BYTES);
-          auto lo4 = [](const float4* x, float4* lo, int i) {
-            const float4 v = x[i];
-            float4 l;
-            l.x = v.x - __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
-            l.y = v.y - __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
-            l.z = v.z - __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
-            l.w = v.w - __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
-            lo[i] = l;
-          };
+          const float4* b_raw = reinterpret_cast<const float4*>(st + L::B_OFF);
+          float4* b_lo = reinterpret_cast<float4*>(st + L::B_OFF + L::B_BYTES);
+          if (!ATM) {
+            const float4* a_raw = reinterpret_cast<const float4*>(st);
+            float4* a_lo = reinterpret_cast<float4*>(st + L::A_BYTES);
 #pragma unroll
-          for (int i = t0; i < (int)(L::A_BYTES / 16); i += kSplitThreads) lo4(a_raw, a_lo, i);
+            for (int i = t0; i < (int)(L::A_BYTES / 16); i += kGroupThreads) lo4(a_raw, a_lo, i);
+          }
 #pragma unroll
-          for (int i = t0; i < (int)(L::B_BYTES / 16); i += kSplitThreads) lo4(b_raw, b_lo, i);
+          for (int i = t0; i < (int)(L::B_BYTES / 16); i += kGroupThreads) lo4(b_raw, b_lo, i);
+        }
+        if (ATM) {
+          // A rows to TMEM: the warp's lane quarter (warp % 4) holds rows 32 q .. 32 q + 31;
+          // the group's warps of one quarter share its 16 k values in halves of 8. The TMA
+          // wrote A K-major in 64-byte rows with the 64-byte swizzle: 16-byte chunk c of row
+          // r sits at chunk c ^ ((r / 2) % 4).
+          constexpr int kHalvesPerWarp = 2 / (kGroupThreads / 128);
+          const int qr = warp & 3, h0 = ((warp - kSplitWarp0) >> 2) % (kGroupThreads / 128);
+          const int r = 32 * qr + lane, sw = (r >> 1) & 3;
+          const uint8_t* arow = st + r * (BK * 4);
+#pragma unroll
+          for (int hh = 0; hh < kHalvesPerWarp; ++hh) {
+            const int hk = h0 * kHalvesPerWarp + hh;
+            const float4 v0 = *reinterpret_cast<const float4*>(arow + (((2 * hk) ^ sw) << 4));
+            const float4 v1 =
+                *reinterpret_cast<const float4*>(arow + (((2 * hk + 1) ^ sw) << 4));
+            const uint32_t taddr = tmem + ((uint32_t)(32 * qr) << 16) + L::ACC_COLS +
+                                   (uint32_t)(s * 2 * BK + hk * 8);
+            const uint32_t hi[8] = {__float_as_uint(v0.x), __float_as_uint(v0.y),
+                                    __float_as_uint(v0.z), __float_as_uint(v0.w),
+                                    __float_as_uint(v1.x), __float_as_uint(v1.y),
+                                    __float_as_uint(v1.z), __float_as_uint(v1.w)};
+            tmem_st8(taddr, hi);
+            if (!args.raw) {
+              const uint32_t lo[8] = {
+                  __float_as_uint(lo_of(v0.x)), __float_as_uint(lo_of(v0.y)),
+                  __float_as_uint(lo_of(v0.z)), __float_as_uint(lo_of(v0.w)),
+                  __float_as_uint(lo_of(v1.x)), __float_as_uint(lo_of(v1.y)),
+                  __float_as_uint(lo_of(v1.z)), __float_as_uint(lo_of(v1.w))};
+              tmem_st8(taddr + BK, lo);
+            }
+          }
+          tmem_wait_st();
+          tc_fence_before();
         }
         // One arrival per warp after all its lanes fenced (256 arrivals on one barrier would
         // serialise in the shared-memory atomics); in a pair the odd CTA's relay thread
@@ -719,7 +798,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               const float a = ti.nk ? __uint_as_float(r[j]) : 0.f;
               float v;
               if (pmm) {
-                v = (causal && c0 + j > row) ? 0.f : expf(__fmul_rn(args.alpha, a) - rv);
+                // The fast exponential intrinsic: the argument is <= 0 up to rounding and
+                // its relative error (a few ulp plus ~|x| 2^-22) stays far below 1e-4.
+                v = (causal && c0 + j > row) ? 0.f : __expf(__fmul_rn(args.alpha, a) - rv);
               } else {
                 v = args.alpha * a;
                 if (args.bias && c0 + j < args.n) v += args.bias[c0 + j];
@@ -812,7 +893,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               const float a = ti.nk ? __uint_as_float(r[h + j]) : 0.f;
               r[h + j] = __float_as_uint(
                   ds ? sv[j] * (a - rv) * alpha
-                     : ((causal && c0 + h + j > row) ? 0.f : expf(__fmul_rn(alpha, a) - rv)));
+                     : ((causal && c0 + h + j > row) ? 0.f : __expf(__fmul_rn(alpha, a) - rv)));
             }
             if (full) {
 #pragma unroll
@@ -1060,10 +1141,13 @@ splitk_reduce_vec4(const float4* __restrict__ ws, int splits, GemmArgs<float> p)
 
 template <int BN, bool A_MN, bool B_MN, bool PAIR>
 static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
-  using L = Layout<BN, PAIR>;
-  constexpr int STAGES = stages_for<BN, PAIR>();
+  // A in tensor memory wherever the accumulators leave room (tiles up to 128 wide) and A is
+  // K-major: the MMAs then read only B from shared memory.
+  constexpr bool ATM = !PAIR && !A_MN && BN <= 128;
+  using L = Layout<BN, PAIR, ATM>;
+  constexpr int STAGES = stages_for<BN, PAIR, ATM>();
   constexpr int TILE_M = PAIR ? 2 * BM : BM;
-  auto kernel = gemm_tc_kernel<BN, STAGES, A_MN, B_MN, PAIR>;
+  auto kernel = gemm_tc_kernel<BN, STAGES, A_MN, B_MN, PAIR, ATM>;
   CUtensorMap ta, tb;
   int rc;
   // A: K-major = m rows of k; MN-major = k rows of m. Likewise B with n. An operand shared
@@ -1243,47 +1327,38 @@ int gemm_tc_f32(const GemmArgs<float>& p, cudaStream_t stream) {
     return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: NCHW output takes no heads");
   const bool a_mn = p.trans_a != 0;   // A stored k x m
   const bool b_mn = p.trans_b == 0;   // B stored k x n
-  // Tile width by estimated makespan: each persistent CTA runs ceil(tiles / SMs) tiles. A tile
-  // of width 128 (64) takes about 0.8 (0.7) of the time of a 256-wide one at the same depth
-  // (measured on B200: narrower tiles re-read A from shared memory for fewer columns).
+  // Tile width BN and split count s chosen together by modelled makespan, in units of a
+  // k-block of a 64-wide tile:
+  //   ceil(tiles(BN) * s / SMs) * (ceil(nk / s) + 2 + part(BN, s)) * kb(BN)
+  // kb = 7 : 8 : 10 for BN = 64 : 128 : 256 is the measured time of one k-block (B200: a
+  // k-block of a narrow tile costs nearly as much as of a wide one, so wide tiles and split
+  // reductions win when the output has few tiles); every tile pays about two k-blocks of
+  // pipeline fill and epilogue; a split tile about 12 * BN / 256 more for writing its fp32
+  // partial and reading it back in the reduction. Splits need a caller workspace (batch 1,
+  // full reductions) and keep at least 8 k-blocks each.
   const int64_t mt = (p.m + tc::BM - 1) / tc::BM, sms = tc::sm_count();
-  int best = 0;
-  int64_t best_cost = INT64_MAX;
+  const int64_t nk = (p.k + tc::BK - 1) / tc::BK;
+  const bool can_split = p.workspace && p.batch == 1 && p.kmode == GEMM_K_FULL;
+  const int64_t fit =
+      can_split ? (int64_t)(p.workspace_bytes / (sizeof(float) * (size_t)(p.m * p.n))) : 1;
+  auto kb_cost = [](int bn) { return bn == 256 ? 10.0 : (bn == 128 ? 8.0 : 7.0); };
+  int best = 0, splits = 1;
+  double best_cost = 0.0;
   for (int bn : {256, 128, 64}) {
     if (bn > 64 && p.n <= bn / 2) continue;
     const int64_t tiles = mt * ((p.n + bn - 1) / bn) * p.batch;
-    const int64_t tile_cost = bn == 256 ? 10 : (bn == 128 ? 8 : 7);
-    const int64_t cost = (tiles + sms - 1) / sms * tile_cost;
-    if (cost < best_cost) {
-      best_cost = cost;
-      best = bn;
-    }
-  }
-  // Split-K (when the caller supplied a workspace): the number of splits s minimising the
-  // modelled makespan ceil(tiles * s / SMs) * (nk / s + 2 + 12 [s > 1]), in k-block units:
-  // every tile also pays about two k-blocks of pipeline fill and epilogue, and a split tile
-  // about twelve more for writing its fp32 partial and reading it back in the reduction
-  // (a 128 x 256 partial is 128 KB each way at an SM's share of HBM bandwidth). It fills the
-  // SMs when the output has few tiles and evens out the last wave of long reductions; every
-  // split keeps at least 8 k-blocks.
-  int splits = 1;
-  if (p.workspace && p.batch == 1 && p.kmode == GEMM_K_FULL) {
-    const int64_t tiles = mt * ((p.n + best - 1) / best);
-    const int64_t nk = (p.k + tc::BK - 1) / tc::BK;
-    const int64_t fit = (int64_t)(p.workspace_bytes / (sizeof(float) * (size_t)(p.m * p.n)));
-    int64_t smax = nk / 8;
+    int64_t smax = can_split ? nk / 8 : 1;
     if (smax > fit) smax = fit;
     if (smax > sms) smax = sms;
-    auto cost = [&](int64_t s) {
-      return (double)((tiles * s + sms - 1) / sms) *
-             ((double)nk / (double)s + 2.0 + (s > 1 ? 12.0 : 0.0));
-    };
-    double best_t = cost(1);
-    for (int64_t s = 2; s <= smax; ++s) {
-      const double t = cost(s);
-      if (t < best_t - 1e-9) {
-        best_t = t;
-        splits = (int)s;
+    if (smax < 1) smax = 1;
+    for (int64_t sp = 1; sp <= smax; ++sp) {
+      const double part = sp > 1 ? 12.0 * bn / 256.0 : 0.0;
+      const double cost = (double)((tiles * sp + sms - 1) / sms) *
+                          ((double)((nk + sp - 1) / sp) + 2.0 + part) * kb_cost(bn);
+      if (best == 0 || cost < best_cost - 1e-9) {
+        best_cost = cost;
+        best = bn;
+        splits = (int)sp;
       }
     }
   }
@@ -1295,8 +1370,8 @@ int gemm_tc_f32(const GemmArgs<float>& p, cudaStream_t stream) {
     const int64_t pairs = sms / 2;
     const int64_t mt2 = (p.m + 2 * tc::BM - 1) / (2 * tc::BM);
     const int64_t tiles2 = mt2 * ((p.n + best - 1) / best);
-    const int64_t single_tile = best == 256 ? 10 : 8;
-    const int64_t pair_cost = (tiles2 + pairs - 1) / pairs * single_tile * 3 / 4;
+    const double pair_cost =
+        (double)((tiles2 + pairs - 1) / pairs) * ((double)nk + 2.0) * kb_cost(best) * 0.75;
     if (pair_cost < best_cost) {
       if (best == 128) return tc::launch_any<128, true>(p, a_mn, b_mn, 1, stream);
       return tc::launch_any<256, true>(p, a_mn, b_mn, 1, stream);

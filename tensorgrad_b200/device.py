@@ -376,7 +376,9 @@ _PINNED: list[tuple[int, int, Any]] = []
 
 
 def pinned_empty(shape: Sequence[int], dtype: Any) -> np.ndarray:
-    """A host array in page-locked memory: uploads from it are asynchronous DMA copies."""
+    """A host array in page-locked memory: uploads from it (``from_numpy``, ``Tensor(...)``)
+    are asynchronous DMA copies that read it after the call returns, so it must not be
+    changed before the next synchronisation."""
     dt = np.dtype(dtype)
     t = torch.empty(max(math.prod(shape), 1), dtype=_TORCH_DTYPES[dt], pin_memory=True)
     arr = t.numpy()[: math.prod(shape)].reshape(shape)
@@ -387,6 +389,11 @@ def pinned_empty(shape: Sequence[int], dtype: Any) -> np.ndarray:
 def _is_pinned(arr: np.ndarray) -> bool:
     p = arr.ctypes.data
     return any(base <= p and p + arr.nbytes <= base + n for base, n, _ in _PINNED)
+
+
+def is_pinned(arr: np.ndarray) -> bool:
+    """Whether ``arr`` lies in page-locked memory from ``pinned_empty``."""
+    return _is_pinned(arr)
 
 
 def from_numpy(arr: np.ndarray, dtype: Any = None) -> DeviceArray:

@@ -54,6 +54,12 @@ def get_default_dtype() -> Any:
 
 def _host_array(data: object, dtype: Any) -> np.ndarray:
     if isinstance(data, np.ndarray | np.generic):
+        if (isinstance(data, np.ndarray) and (dtype is None or np.dtype(dtype) == data.dtype)
+                and data.flags.c_contiguous and _device.is_pinned(data)):
+            # Page-locked memory (device.pinned_empty) is uploaded by an asynchronous DMA
+            # straight from the caller's buffer, which must stay unchanged until the next
+            # synchronisation (the contract of pinned_empty).
+            return data
         return np.array(data, dtype=dtype, copy=True)
     arr = np.asarray(data, dtype=dtype)
     if dtype is None and arr.dtype == np.float64:
