@@ -192,6 +192,11 @@ RnnBwdLayout rnn_bwd_layout(int dtype, int64_t T_, int64_t B, int64_t I, int64_t
   return L;
 }
 
+// Forward scratch: the summed biases (LSTM) or h W_hn + b_hn (GRU), then (fp32) a split-K
+// workspace for the per-step recurrent products, whose outputs (batch x gates) have few tiles.
+size_t fwd_ws_offset(int dtype, size_t head) { return dtype == TG_F32 ? align256(head) : 0; }
+size_t fwd_ws_bytes(int dtype) { return dtype == TG_F32 ? kWorkspaceFloats * sizeof(float) : 0; }
+
 int check_rnn(int64_t T_, int64_t B, int64_t I, int64_t H) {
   TG_CHECK_ARG(T_ > 0 && B > 0 && I > 0 && H > 0, "rnn: empty sequence or sizes");
   return TG_OK;
@@ -262,7 +267,8 @@ extern "C" {
 size_t tg_lstm_forward_scratch_bytes(int dtype, int64_t T_, int64_t B, int64_t I, int64_t H) {
   (void)T_; (void)B; (void)I;
   const size_t es = dtype == TG_F64 ? 8 : 4;
-  return align256((size_t)(4 * H) * es);
+  const size_t head = align256((size_t)(4 * H) * es);
+  return head + fwd_ws_bytes(dtype);
 }
 
 int tg_lstm_forward(int dtype, int64_t T_, int64_t B, int64_t I, int64_t H, const void* x,
@@ -297,6 +303,11 @@ int tg_lstm_forward(int dtype, int64_t T_, int64_t B, int64_t I, int64_t H, cons
       T* zt = z + t * B * G;
       auto rec = gemm_args<T>(0, 1, B, G, H, h_prev, h_ld, (const T*)w_hh, H, zt, G, nullptr,
                               T(1));
+      if (fwd_ws_bytes(dtype)) {
+        rec.workspace = reinterpret_cast<float*>(
+            (uint8_t*)scratch + fwd_ws_offset(dtype, align256((size_t)G * sizeof(T))));
+        rec.workspace_bytes = fwd_ws_bytes(dtype);
+      }
       if ((r = gemm_run<T>(rec, st))) return r;
       lstm_cell_fwd<T><<<grid_for(B * H, kThreads), kThreads, 0, st>>>(
           zt, c_prev, c_ld, o + t * B * 2 * H, (T*)tanh_c + t * B * H, B, H);
@@ -356,7 +367,7 @@ int tg_lstm_backward(int dtype, int64_t T_, int64_t B, int64_t I, int64_t H, con
 size_t tg_gru_forward_scratch_bytes(int dtype, int64_t T_, int64_t B, int64_t I, int64_t H) {
   (void)T_; (void)I;
   const size_t es = dtype == TG_F64 ? 8 : 4;
-  return align256((size_t)(B * 3 * H) * es);
+  return align256((size_t)(B * 3 * H) * es) + fwd_ws_bytes(dtype);
 }
 
 int tg_gru_forward(int dtype, int64_t T_, int64_t B, int64_t I, int64_t H, const void* x,
@@ -381,6 +392,11 @@ int tg_gru_forward(int dtype, int64_t T_, int64_t B, int64_t I, int64_t H, const
       const T* h_prev = t == 0 ? (const T*)h0 : o + (t - 1) * B * H;
       auto rec = gemm_args<T>(0, 1, B, G, H, h_prev, H, (const T*)w_hh, H, hw, G,
                               (const T*)b_hh, T(0));
+      if (fwd_ws_bytes(dtype)) {
+        rec.workspace = reinterpret_cast<float*>(
+            (uint8_t*)scratch + fwd_ws_offset(dtype, align256((size_t)(B * G) * sizeof(T))));
+        rec.workspace_bytes = fwd_ws_bytes(dtype);
+      }
       if ((r = gemm_run<T>(rec, st))) return r;
       gru_cell_fwd<T><<<grid_for(B * H, kThreads), kThreads, 0, st>>>(
           a + t * B * G, hw, h_prev, (T*)hn + t * B * H, o + t * B * H, B, H);
