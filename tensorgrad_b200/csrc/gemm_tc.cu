@@ -368,8 +368,11 @@ constexpr uint32_t kEpiBytes = 4 * 2 * kEpiBox;
 // PAIR: a CTA of a cta_group::2 pair holds its 128 rows of A and half of the BN columns of B.
 template <int BN, bool PAIR = false, bool ATM = false>
 struct Layout {
+  // k-block depth: 32 fp32 (128-byte rows, 128-byte swizzle) for single-CTA tiles up to 128
+  // wide, whose time per k-block is mostly a fixed cost; 16 (64-byte rows) otherwise.
+  static constexpr int BK = (!PAIR && BN <= 128) ? 32 : 16;
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
-  static constexpr uint32_t A_BYTES = BM * BK * 4;  // 8 KB
+  static constexpr uint32_t A_BYTES = BM * BK * 4;
   static constexpr uint32_t B_BYTES = B_ROWS * BK * 4;
   // ATM (A in tensor memory): a stage holds raw A, raw B and B's lo; A's hi and lo go to
   // TMEM columns after the two accumulators (2 * BK per stage). Otherwise raw + lo of both.
@@ -383,19 +386,21 @@ template <int BN, bool PAIR = false, bool ATM = false>
 constexpr int stages_for() {
   constexpr uint32_t s = Layout<BN, PAIR, ATM>::STAGE;
   constexpr int by_smem = (int)((200 * 1024) / s);
-  constexpr int cap = ATM ? (int)((512 - 2 * BN) / (2 * BK)) : 8;
+  constexpr int cap = ATM ? (int)((512 - 2 * BN) / (2 * Layout<BN, PAIR, ATM>::BK)) : 8;
   return by_smem > cap ? cap : by_smem;
 }
 
-// Descriptor of k-step kk (8 tf32 along K) of a stage tile.
-//  K-major : rows of BK = 16 K values (64 B), 64-byte swizzle; the step starts 32 B into each
-//            row; the next 8-row group is 512 B on.
-//  MN-major: 32-wide MN chunks of BK K-rows (128 B each, 2 KB per chunk), 128-byte swizzle
-//            with 32-byte atoms: the step starts 8 rows (1024 B) on, the next 4-row group is
-//            512 B on (SBO), the next MN chunk 2 KB on (LBO).
-template <bool MN>
+// Descriptor of k-step kk (8 tf32 along K) of a stage tile with KB k values per row.
+//  K-major : rows of KB K values; KB = 16: 64-byte rows, 64-byte swizzle, the next 8-row
+//            group 512 B on; KB = 32: 128-byte rows, 128-byte swizzle, the next 8-row group
+//            1024 B on. The step starts 32 B further into each row.
+//  MN-major: 32-wide MN chunks of KB K-rows (128 B each), 128-byte swizzle with 32-byte
+//            atoms: the step starts 8 rows (1024 B) on, the next 4-row group is 512 B on
+//            (SBO), the next MN chunk KB * 128 B on (LBO).
+template <bool MN, int KB>
 __device__ __forceinline__ uint64_t tile_desc(uint32_t tile_base, int kk) {
-  if (MN) return smem_desc(tile_base + kk * 1024, /*lbo*/ 32 * BK * 4, /*sbo*/ 512, 1);
+  if (MN) return smem_desc(tile_base + kk * 1024, /*lbo*/ 32 * KB * 4, /*sbo*/ 512, 1);
+  if (KB == 32) return smem_desc(tile_base + kk * 32, /*lbo (unused)*/ 16, /*sbo*/ 1024, 2);
   return smem_desc(tile_base + kk * 32, /*lbo (unused)*/ 16, /*sbo*/ 512, 4);
 }
 
@@ -406,7 +411,7 @@ struct TileInfo {
   bool skip;
 };
 
-__device__ __forceinline__ TileInfo tile_info(const TcArgs& a, int t, int bn, int bm = BM) {
+__device__ __forceinline__ TileInfo tile_info(const TcArgs& a, int t, int bn, int bm, int bk) {
   TileInfo ti;
   const int mt = t % a.m_tiles;
   int rest = t / a.m_tiles;
@@ -419,16 +424,16 @@ __device__ __forceinline__ TileInfo tile_info(const TcArgs& a, int t, int bn, in
   // Causal attention products: a tile strictly above the diagonal is skipped outright, and
   // reductions over a triangular operand stop at / start from the tile's first output row.
   ti.skip = a.kmode == GEMM_K_SKIP_UPPER && ti.n0 > ti.m0 + BM - 1;
-  const int nk_all = (int)((a.k + BK - 1) / BK);
+  const int nk_all = (int)((a.k + bk - 1) / bk);
   int kb0 = 0, kb1 = nk_all;
   if (a.splits > 1) {
     kb0 = ti.split * a.kb_per_split;
     kb1 = kb0 + a.kb_per_split < nk_all ? kb0 + a.kb_per_split : nk_all;
   } else if (a.kmode == GEMM_K_UP_TO_ROW) {
     const int64_t kend = ti.m0 + BM < a.k ? ti.m0 + BM : a.k;
-    kb1 = (int)((kend + BK - 1) / BK);
+    kb1 = (int)((kend + bk - 1) / bk);
   } else if (a.kmode == GEMM_K_FROM_ROW) {
-    kb0 = (int)(ti.m0 / BK);
+    kb0 = (int)(ti.m0 / bk);
   }
   ti.kb0 = kb0;
   ti.nk = (ti.skip || kb1 <= kb0) ? 0 : kb1 - kb0;
@@ -448,6 +453,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   using L = Layout<BN, PAIR, ATM>;
   static_assert(!ATM || (!PAIR && !A_MN), "A in tensor memory: single CTA, K-major A");
   constexpr int TILE_M = PAIR ? 2 * BM : BM;
+  constexpr int KB = L::BK;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -501,7 +507,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       int it = 0;
       bool stop = false;
       for (int t = unit; t < total && !stop; t += units) {
-        const TileInfo ti = tile_info(args, t, BN, TILE_M);
+        const TileInfo ti = tile_info(args, t, BN, TILE_M, KB);
         for (int j = 0; j < ti.nk; ++j, ++it) {
           const int s = it % STAGES, round = it / STAGES;
           if (round > 0 && !wait_bar(&empty[s], (round - 1) & 1, abort_flag)) { stop = true; break; }
@@ -509,7 +515,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           uint8_t* a_raw = st;
           uint8_t* b_raw = st + L::B_OFF;
           mbar_arrive_expect_tx(&full[s], L::A_BYTES + L::B_BYTES);
-          const int k0 = (ti.kb0 + j) * BK;
+          const int k0 = (ti.kb0 + j) * KB;
           const int hh = ti.bz % args.heads, bo = ti.bz / args.heads;
           const int ha = args.a_bcast ? 0 : hh, ba = args.a_bcast ? 0 : bo;
           const int hb = args.b_bcast ? 0 : hh, bb = args.b_bcast ? 0 : bo;
@@ -518,7 +524,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           if (A_MN) {
 #pragma unroll
             for (int c = 0; c < BM / 32; ++c)
-              tma_load_4d(a_raw + c * 32 * BK * 4, &tmA, &full[s], am0 + 32 * c, k0, ha, ba);
+              tma_load_4d(a_raw + c * 32 * KB * 4, &tmA, &full[s], am0 + 32 * c, k0, ha, ba);
           } else if (args.a_fold > 0) {
             tma_load_4d(a_raw, &tmA, &full[s], k0 % args.a_fold, am0, 0, k0 / args.a_fold);
           } else {
@@ -527,7 +533,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           if (B_MN) {
 #pragma unroll
             for (int c = 0; c < L::B_ROWS / 32; ++c)
-              tma_load_4d(b_raw + c * 32 * BK * 4, &tmB, &full[s], bn0 + 32 * c, k0, hb, bb);
+              tma_load_4d(b_raw + c * 32 * KB * 4, &tmB, &full[s], bn0 + 32 * c, k0, hb, bb);
           } else {
             tma_load_4d(b_raw, &tmB, &full[s], k0, bn0, hb, bb);
           }
@@ -555,7 +561,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       int it = 0;
       bool ok = true;
       for (int t = unit; t < total && ok; t += units) {
-        const TileInfo ti = tile_info(args, t, BN, TILE_M);
+        const TileInfo ti = tile_info(args, t, BN, TILE_M, KB);
         for (int j = 0; j < ti.nk; ++j, ++it) {
           const int s = it % STAGES, round = it / STAGES;
           if (!wait_bar(&split[s], round & 1, abort_flag)) { ok = false; break; }
@@ -569,7 +575,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       int it = 0, tc = 0;
       bool ok = true;
       for (int t = unit; t < total && ok; t += units) {
-        const TileInfo ti = tile_info(args, t, BN, TILE_M);
+        const TileInfo ti = tile_info(args, t, BN, TILE_M, KB);
         if (ti.skip) continue;
         const int buf = tc & 1;
         if (tc >= 2) {
@@ -587,17 +593,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           const uint32_t a_raw = st, a_lo = st + L::A_BYTES;
           const uint32_t b_raw = st + L::B_OFF, b_lo = b_raw + L::B_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < BK / 8; ++kk) {
-            const uint64_t ah = tile_desc<A_MN>(a_raw, kk), al = tile_desc<A_MN>(a_lo, kk);
-            const uint64_t bh = tile_desc<B_MN>(b_raw, kk), bl = tile_desc<B_MN>(b_lo, kk);
+          for (int kk = 0; kk < KB / 8; ++kk) {
+            const uint64_t ah = tile_desc<A_MN, KB>(a_raw, kk), al = tile_desc<A_MN, KB>(a_lo, kk);
+            const uint64_t bh = tile_desc<B_MN, KB>(b_raw, kk), bl = tile_desc<B_MN, KB>(b_lo, kk);
             if (ATM) {
               // A's hi (the raw bits) and lo of this stage in TMEM columns after the
               // accumulators: [hi k 0..15 | lo k 0..15].
-              const uint32_t th = tmem + L::ACC_COLS + (uint32_t)(s * 2 * BK + kk * 8);
+              const uint32_t th = tmem + L::ACC_COLS + (uint32_t)(s * 2 * KB + kk * 8);
               if (args.raw) {
                 mma_tf32_ta(acc, th, bh, idesc, (j | kk) != 0);
               } else {
-                mma_tf32_ta(acc, th + BK, bh, idesc, (j | kk) != 0);
+                mma_tf32_ta(acc, th + KB, bh, idesc, (j | kk) != 0);
                 mma_tf32_ta(acc, th, bl, idesc, 1);
                 mma_tf32_ta(acc, th, bh, idesc, 1);
               }
@@ -639,7 +645,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     int it = 0;
     bool stop = false;
     for (int t = unit; t < total && !stop; t += units) {
-      const TileInfo ti = tile_info(args, t, BN, TILE_M);
+      const TileInfo ti = tile_info(args, t, BN, TILE_M, KB);
       for (int j = 0; j < ti.nk; ++j, ++it) {
         if (it % kSplitGroups != grp) continue;
         const int s = it % STAGES, round = it / STAGES;
@@ -668,21 +674,24 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
         if (ATM) {
           // A rows to TMEM: the warp's lane quarter (warp % 4) holds rows 32 q .. 32 q + 31;
-          // the group's warps of one quarter share its 16 k values in halves of 8. The TMA
-          // wrote A K-major in 64-byte rows with the 64-byte swizzle: 16-byte chunk c of row
-          // r sits at chunk c ^ ((r / 2) % 4).
-          constexpr int kHalvesPerWarp = 2 / (kGroupThreads / 128);
-          const int qr = warp & 3, h0 = ((warp - kSplitWarp0) >> 2) % (kGroupThreads / 128);
-          const int r = 32 * qr + lane, sw = (r >> 1) & 3;
-          const uint8_t* arow = st + r * (BK * 4);
+          // the group's warps of one quarter share its KB k values in units of 8. The TMA
+          // wrote A K-major in rows of KB floats with the KB*4-byte swizzle: 16-byte chunk c
+          // of row r sits at chunk c ^ ((r / 2) % 4) (64-byte rows) or c ^ (r % 8) (128-byte).
+          constexpr int kUnits = KB / 8;
+          constexpr int kWarpsPerQuarter = kGroupThreads / 128;
+          constexpr int kUnitsPerWarp = kUnits / kWarpsPerQuarter;
+          const int qr = warp & 3;
+          const int u0 = (((warp - kSplitWarp0) >> 2) % kWarpsPerQuarter) * kUnitsPerWarp;
+          const int r = 32 * qr + lane, sw = KB == 32 ? (r & 7) : ((r >> 1) & 3);
+          const uint8_t* arow = st + r * (KB * 4);
 #pragma unroll
-          for (int hh = 0; hh < kHalvesPerWarp; ++hh) {
-            const int hk = h0 * kHalvesPerWarp + hh;
-            const float4 v0 = *reinterpret_cast<const float4*>(arow + (((2 * hk) ^ sw) << 4));
+          for (int uu = 0; uu < kUnitsPerWarp; ++uu) {
+            const int u = u0 + uu;
+            const float4 v0 = *reinterpret_cast<const float4*>(arow + (((2 * u) ^ sw) << 4));
             const float4 v1 =
-                *reinterpret_cast<const float4*>(arow + (((2 * hk + 1) ^ sw) << 4));
+                *reinterpret_cast<const float4*>(arow + (((2 * u + 1) ^ sw) << 4));
             const uint32_t taddr = tmem + ((uint32_t)(32 * qr) << 16) + L::ACC_COLS +
-                                   (uint32_t)(s * 2 * BK + hk * 8);
+                                   (uint32_t)(s * 2 * KB + u * 8);
             const uint32_t hi[8] = {__float_as_uint(v0.x), __float_as_uint(v0.y),
                                     __float_as_uint(v0.z), __float_as_uint(v0.w),
                                     __float_as_uint(v1.x), __float_as_uint(v1.y),
@@ -694,7 +703,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                   __float_as_uint(lo_of(v0.z)), __float_as_uint(lo_of(v0.w)),
                   __float_as_uint(lo_of(v1.x)), __float_as_uint(lo_of(v1.y)),
                   __float_as_uint(lo_of(v1.z)), __float_as_uint(lo_of(v1.w))};
-              tmem_st8(taddr + BK, lo);
+              tmem_st8(taddr + KB, lo);
             }
           }
           tmem_wait_st();
@@ -721,7 +730,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint32_t eph = 0;  // phase bits of ebar[0], ebar[1]
     int q = 0;         // boxes stored so far (alternates the two buffers)
     for (int t = unit; t < total; t += units) {
-      const TileInfo ti = tile_info(args, t, BN, TILE_M);
+      const TileInfo ti = tile_info(args, t, BN, TILE_M, KB);
       if (ti.skip) continue;
       const int buf = tc & 1;
       if (!PAIR && args.tma_c && args.splits == 1) {
@@ -1152,7 +1161,9 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
   int rc;
   // A: K-major = m rows of k; MN-major = k rows of m. Likewise B with n. An operand shared
   // by every batch entry (stride 0) gets a map of depth 1; a folded A has depth k / a_fold.
-  constexpr CUtensorMapSwizzle kSwK = CU_TENSOR_MAP_SWIZZLE_64B;
+  constexpr int KB = L::BK;
+  constexpr CUtensorMapSwizzle kSwK =
+      KB == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   constexpr CUtensorMapSwizzle kSwMN = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
   const bool a_bcast = p.batch > 1 && p.stride_a == 0 && p.stride_ah == 0;
   const bool b_bcast = p.batch > 1 && p.stride_b == 0 && p.stride_bh == 0;
@@ -1160,16 +1171,16 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
   const int64_t ah = a_bcast ? 1 : p.heads, an = a_bcast ? 1 : nb;
   const int64_t bh = b_bcast ? 1 : p.heads, bn = b_bcast ? 1 : nb;
   if (A_MN)
-    rc = make_map(&ta, p.a, p.m, p.k, p.lda, ah, p.stride_ah, an, p.stride_a, 32, BK, kSwMN);
+    rc = make_map(&ta, p.a, p.m, p.k, p.lda, ah, p.stride_ah, an, p.stride_a, 32, KB, kSwMN);
   else if (p.a_fold > 0)
-    rc = make_map(&ta, p.a, p.a_fold, p.m, p.lda, 1, 0, p.k / p.a_fold, p.stride_a, BK, BM,
+    rc = make_map(&ta, p.a, p.a_fold, p.m, p.lda, 1, 0, p.k / p.a_fold, p.stride_a, KB, BM,
                   kSwK);
-  else rc = make_map(&ta, p.a, p.k, p.m, p.lda, ah, p.stride_ah, an, p.stride_a, BK, BM, kSwK);
+  else rc = make_map(&ta, p.a, p.k, p.m, p.lda, ah, p.stride_ah, an, p.stride_a, KB, BM, kSwK);
   if (rc != TG_OK) return rc;
   if (B_MN)
-    rc = make_map(&tb, p.b, p.n, p.k, p.ldb, bh, p.stride_bh, bn, p.stride_b, 32, BK, kSwMN);
+    rc = make_map(&tb, p.b, p.n, p.k, p.ldb, bh, p.stride_bh, bn, p.stride_b, 32, KB, kSwMN);
   else
-    rc = make_map(&tb, p.b, p.k, p.n, p.ldb, bh, p.stride_bh, bn, p.stride_b, BK, L::B_ROWS,
+    rc = make_map(&tb, p.b, p.k, p.n, p.ldb, bh, p.stride_bh, bn, p.stride_b, KB, L::B_ROWS,
                   kSwK);
   if (rc != TG_OK) return rc;
   const size_t smem = STAGES * L::STAGE + kEpiBytes + 1024 + 512;
@@ -1216,7 +1227,7 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
   a.rv0 = p.rv0;
   a.rv1 = p.rv1;
   a.aux = p.aux;
-  const int nk_all = (int)((p.k + BK - 1) / BK);
+  const int nk_all = (int)((p.k + KB - 1) / KB);
   a.splits = 1;
   a.kb_per_split = nk_all;
   if (splits > 1) {
@@ -1320,7 +1331,7 @@ int gemm_tc_f32(const GemmArgs<float>& p, cudaStream_t stream) {
                      (long long)p.batch, (long long)p.heads);
   if (p.m > INT32_MAX / 2 || p.n > INT32_MAX / 2 || p.k > INT32_MAX / 2)
     return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: dimension beyond int32");
-  if (p.a_fold > 0 && (p.trans_a || p.batch != 1 || p.a_fold % tc::BK || p.k % p.a_fold ||
+  if (p.a_fold > 0 && (p.trans_a || p.batch != 1 || p.a_fold % 16 || p.k % p.a_fold ||
                        (p.stride_a % 4) || p.k / p.a_fold > INT32_MAX))
     return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: folded A needs K-major, fold %% 16 == 0");
   if (p.c_hw > 0 && p.heads != 1)
@@ -1337,15 +1348,19 @@ int gemm_tc_f32(const GemmArgs<float>& p, cudaStream_t stream) {
   // partial and reading it back in the reduction. Splits need a caller workspace (batch 1,
   // full reductions) and keep at least 8 k-blocks each.
   const int64_t mt = (p.m + tc::BM - 1) / tc::BM, sms = tc::sm_count();
-  const int64_t nk = (p.k + tc::BK - 1) / tc::BK;
   const bool can_split = p.workspace && p.batch == 1 && p.kmode == GEMM_K_FULL;
   const int64_t fit =
       can_split ? (int64_t)(p.workspace_bytes / (sizeof(float) * (size_t)(p.m * p.n))) : 1;
-  auto kb_cost = [](int bn) { return bn == 256 ? 10.0 : (bn == 128 ? 8.0 : 7.0); };
+  // k-block depth per tile width (tc::Layout::BK) and the time of one k-block.
+  auto bk_of = [](int bn) { return bn <= 128 ? 32 : 16; };
+  auto kb_cost = [](int bn) { return bn == 256 ? 10.0 : (bn == 128 ? 12.0 : 10.0); };
   int best = 0, splits = 1;
   double best_cost = 0.0;
   for (int bn : {256, 128, 64}) {
-    if (bn > 64 && p.n <= bn / 2) continue;
+    // A folded k-block stays inside one image; the 16-deep tiles always qualify.
+    if (p.a_fold > 0 && p.a_fold % bk_of(bn)) continue;
+    if (bn > 64 && p.n <= bn / 2 && !(bn == 256 && p.a_fold > 0 && p.a_fold % 32)) continue;
+    const int64_t nk = (p.k + bk_of(bn) - 1) / bk_of(bn);
     const int64_t tiles = mt * ((p.n + bn - 1) / bn) * p.batch;
     int64_t smax = can_split ? nk / 8 : 1;
     if (smax > fit) smax = fit;
@@ -1370,8 +1385,9 @@ int gemm_tc_f32(const GemmArgs<float>& p, cudaStream_t stream) {
     const int64_t pairs = sms / 2;
     const int64_t mt2 = (p.m + 2 * tc::BM - 1) / (2 * tc::BM);
     const int64_t tiles2 = mt2 * ((p.n + best - 1) / best);
+    const int64_t nk16 = (p.k + 15) / 16;  // pair tiles are 16 deep
     const double pair_cost =
-        (double)((tiles2 + pairs - 1) / pairs) * ((double)nk + 2.0) * kb_cost(best) * 0.75;
+        (double)((tiles2 + pairs - 1) / pairs) * ((double)nk16 + 2.0) * 10.0 * 0.75;
     if (pair_cost < best_cost) {
       if (best == 128) return tc::launch_any<128, true>(p, a_mn, b_mn, 1, stream);
       return tc::launch_any<256, true>(p, a_mn, b_mn, 1, stream);
