@@ -11,18 +11,20 @@
 // lo*lo term and the truncation of lo are ~2^-20 relative.
 //
 // Persistent, warp-specialised (one CTA of 512 threads per SM, tiles of 128 x BN,
-// BN = 64/128/256, BK = 16 fp32 = one 64-byte swizzle row):
+// BN = 64/128/256; k-blocks of BK = 32 fp32 (128-byte rows) for tiles up to 128 wide, 16
+// (64-byte rows) for 256-wide and pair tiles):
 //   warp 0 (lane 0)  : TMA producer over every (tile, k-block) of this CTA, STAGES-deep ring.
-//   warps 4..11      : write lo for each stage, fence the generic-proxy writes for the async
-//                      proxy, arrive on split[s].
+//   warps 4..11      : write lo for each stage (A's hi and lo into TMEM when A is K-major and
+//                      the tile at most 128 wide), fence the generic-proxy writes for the
+//                      async proxy, arrive on split[s].
 //   warp 1 (lane 0)  : MMA issuer: 3 x (BK/8) tcgen05.mma per stage into one of two TMEM
 //                      accumulators; tcgen05.commit frees the stage and, after a tile's last
 //                      k-block, hands the accumulator to the epilogue.
 //   warps 12..15     : epilogue: tcgen05.ld of TMEM lanes 32*(warp%4).., alpha/beta/bias,
 //                      16-byte stores; then the accumulator is released to the MMA warp.
 // So a tile's epilogue overlaps the next tile's loads and MMAs. K-major operands use the
-// 64-byte swizzle; MN-major TF32 operands the 128-byte swizzle with 32-byte atoms, the only
-// swizzle UMMA accepts for them. No TMA multicast is used.
+// 64- or 128-byte swizzle (by row length); MN-major TF32 operands the 128-byte swizzle with
+// 32-byte atoms, the only swizzle UMMA accepts for them. No TMA multicast is used.
 //
 // Every mbarrier wait is bounded (clock64 budget). On expiry the kernel records
 // TG_ERR_TIMEOUT in a device status word, stops issuing work, drains what it started
@@ -43,7 +45,6 @@ namespace tg {
 namespace tc {
 
 constexpr int BM = 128;
-constexpr int BK = 16;                       // fp32 elements per 64-byte swizzle row
 constexpr long long kTimeoutCycles = 4000000000LL;  // ~2 s at 2 GHz
 
 __device__ int g_status = 0;
@@ -809,7 +810,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               if (pmm) {
                 // The fast exponential intrinsic: the argument is <= 0 up to rounding and
                 // its relative error (a few ulp plus ~|x| 2^-22) stays far below 1e-4.
-                v = (causal && c0 + j > row) ? 0.f : __expf(__fmul_rn(args.alpha, a) - rv);
+                // Exponential first, then a select: a conditional around it would make the
+                // compiler branch per element.
+                const float e = __expf(__fmul_rn(args.alpha, a) - rv);
+                v = (causal && c0 + j > row) ? 0.f : e;
               } else {
                 v = args.alpha * a;
                 if (args.bias && c0 + j < args.n) v += args.bias[c0 + j];
@@ -900,9 +904,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               const float a = ti.nk ? __uint_as_float(r[h + j]) : 0.f;
-              r[h + j] = __float_as_uint(
-                  ds ? sv[j] * (a - rv) * alpha
-                     : ((causal && c0 + h + j > row) ? 0.f : __expf(__fmul_rn(alpha, a) - rv)));
+              const float e = ds ? 0.f : __expf(__fmul_rn(alpha, a) - rv);
+              r[h + j] = __float_as_uint(ds ? sv[j] * (a - rv) * alpha
+                                            : ((causal && c0 + h + j > row) ? 0.f : e));
             }
             if (full) {
 #pragma unroll
