@@ -195,8 +195,14 @@ static float* carve(char*& cur, size_t floats) {
   return out;
 }
 
+// The fused forward (flash_tc.cu): heads of 32 or 64 features.
+bool flash_fwd_supported(const tg_attn_shape* s);
+int flash_fwd_tc(const tg_attn_shape* s, const float* q, const float* k, const float* v,
+                 float* o, float* lse, cudaStream_t st);
+
 int attention_tc_forward(const tg_attn_shape* s, const float* q, const float* k, const float* v,
                          float* o, float* lse, void* scratch, cudaStream_t st) {
+  if (flash_fwd_supported(s)) return flash_fwd_tc(s, q, k, v, o, lse, st);
   const Plan p = make_plan(s);
   char* cur = reinterpret_cast<char*>(scratch);
   float* S = carve(cur, p.blk_s);
