@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 
 from oracle import ops as O
-from tests.conftest import assert_parity, load_golden
+from tests.conftest import assert_parity, assert_zero_gradient, load_golden
 from tests.golden.specs import ATTN_CASES, attention_inputs
 
 pytestmark = pytest.mark.gpu
@@ -301,6 +301,35 @@ def test_attention_causal_with_longer_keys(dtype):
     for ours, ref, name in zip((o, dq, dk, dv), (ref_o, *O.attention_backward(do, q, k, v, p)),
                                ("out", "dq", "dk", "dv"), strict=True):
         assert_parity(ours.numpy(), ref, rel(dtype), name)
+
+
+# Heads of 32 and 64 features take the fused forward (scores only in tensor memory): ragged
+# lengths, more keys than queries, both masks, against the float64 oracle.
+@pytest.mark.parametrize("qshape,tk,causal", [((2, 3, 150, 64), 150, False),
+                                              ((1, 2, 70, 64), 130, False),
+                                              ((1, 2, 97, 32), 97, False),
+                                              ((2, 2, 1, 64), 1, True),
+                                              ((1, 3, 257, 64), 257, True)])
+def test_fused_attention_forward_shapes(dtype, qshape, tk, causal):
+    import tensorgrad_b200 as tg
+
+    rng = np.random.default_rng(qshape[2] + tk)
+    b, h, tq, d = qshape
+    q, k, v = (rng.standard_normal(s) for s in (qshape, (b, h, tk, d), (b, h, tk, d)))
+    do = rng.standard_normal(qshape)
+    tq_, tk_, tv_ = (tensor(a, dtype) for a in (q, k, v))
+    o = tg.nn.functional.scaled_dot_product_attention(tq_, tk_, tv_, causal=causal)
+    dq, dk, dv = tg.autograd.grad(o, [tq_, tk_, tv_], grad_outputs=do.astype(dtype))
+    ref_o, p = O.attention_forward(q, k, v, causal)
+    refs = (ref_o, *O.attention_backward(do, q, k, v, p))
+    for ours, ref, name in zip((o, dq, dk, dv), refs, ("out", "dq", "dk", "dv"), strict=True):
+        if np.max(np.abs(ref)) == 0.0:
+            # A single visible key: softmax is 1 whatever the scores, dq = dk = 0 exactly;
+            # both sides hold only rounding noise of dP - delta, checked against the scale
+            # of the value gradient.
+            assert_zero_gradient(ours.numpy(), float(np.max(np.abs(refs[3]))), rel(dtype), name)
+        else:
+            assert_parity(ours.numpy(), ref, rel(dtype), name)
 
 
 @pytest.mark.parametrize("b,t,h,hd", [(2, 64, 4, 32), (1, 129, 2, 64), (2, 40, 3, 16),
