@@ -195,10 +195,14 @@ static float* carve(char*& cur, size_t floats) {
   return out;
 }
 
-// The fused forward (flash_tc.cu): heads of 32 or 64 features.
+// The fused kernels (flash_tc.cu), heads of 32 or 64 features: the forward, and P with dS of
+// the backward.
 bool flash_fwd_supported(const tg_attn_shape* s);
 int flash_fwd_tc(const tg_attn_shape* s, const float* q, const float* k, const float* v,
                  float* o, float* lse, cudaStream_t st);
+int attn_pds_tc(const tg_attn_shape* s, const float* q, const float* k, const float* v,
+                const float* dout, const float* lse, const float* delta, float* P, float* dS,
+                int64_t ldS, cudaStream_t st);
 
 int attention_tc_forward(const tg_attn_shape* s, const float* q, const float* k, const float* v,
                          float* o, float* lse, void* scratch, cudaStream_t st) {
@@ -251,17 +255,22 @@ int attention_tc_backward(const tg_attn_shape* s, const float* q, const float* k
   row_dot_kernel<<<grid_for(rows * 32, 256), 256, 0, st>>>(dO, O, delta, p.H, p.Tq, p.D, rows);
   if ((rc = check_launch("attention delta"))) return rc;
   const int skip = causal ? GEMM_K_SKIP_UPPER : GEMM_K_FULL;
-  // P = exp(scale Q K^T - lse) straight from the product's epilogue (the scores are never
-  // stored), then dP = dO V^T with dS = P (dP - delta) scale produced by its epilogue.
-  GemmArgs<float> gp = bgemm_args(0, 1, p.Tq, p.Tk, p.D, scale, Q, K, Sv, p, skip);
-  gp.epi = GEMM_EPI_SOFTMAX_P;
-  gp.rv0 = lse;
-  if ((rc = bgemm(gp, st))) return rc;
-  GemmArgs<float> g = bgemm_args(0, 1, p.Tq, p.Tk, p.D, scale, dO, V, dPv, p, skip);
-  g.epi = GEMM_EPI_SOFTMAX_DS;
-  g.rv1 = delta;
-  g.aux = S;
-  if ((rc = bgemm(g, st))) return rc;
+  if (flash_fwd_supported(s)) {
+    // Both score products on chip, P and dS written once (heads of 32 / 64).
+    if ((rc = attn_pds_tc(s, q, k, v, dout, lse, delta, S, dP, p.ldS, st))) return rc;
+  } else {
+    // P = exp(scale Q K^T - lse) straight from the product's epilogue (the scores are never
+    // stored), then dP = dO V^T with dS = P (dP - delta) scale produced by its epilogue.
+    GemmArgs<float> gp = bgemm_args(0, 1, p.Tq, p.Tk, p.D, scale, Q, K, Sv, p, skip);
+    gp.epi = GEMM_EPI_SOFTMAX_P;
+    gp.rv0 = lse;
+    if ((rc = bgemm(gp, st))) return rc;
+    GemmArgs<float> g = bgemm_args(0, 1, p.Tq, p.Tk, p.D, scale, dO, V, dPv, p, skip);
+    g.epi = GEMM_EPI_SOFTMAX_DS;
+    g.rv1 = delta;
+    g.aux = S;
+    if ((rc = bgemm(g, st))) return rc;
+  }
   const int up = causal ? GEMM_K_UP_TO_ROW : GEMM_K_FULL;
   const int from = causal ? GEMM_K_FROM_ROW : GEMM_K_FULL;
   // dV = P^T dO: P stored Tq x Tk is the "k x m" operand.

@@ -428,6 +428,370 @@ int launch_flash(const tg_attn_shape* s, const float* q, const float* k, const f
   return check_launch("attention forward (fused)");
 }
 
+// ------------------------------------------------------------------ backward: P and dS
+// The two score products of the attention backward in one kernel: per (batch-head, 128-query
+// block) item and 64-key block, S = Q K^T and dP = dO V^T into TMEM, then (lane = query row)
+// P = exp(scale S - lse), dS = P (dP - delta) scale, masked like the forward, written to the
+// row-major P and dS blocks (row stride ldS) that the dV, dK and dQ products read.
+//   warp 0: TMA of Q and dO once per item, K and V blocks through a ring;
+//   warps 4..11: Q's and dO's hi/lo into TMEM, lo of each K and V block;
+//   warp 1: both products of a block into one of two TMEM buffer pairs;
+//   warps 12..15: the element-wise VJP and the stores.
+// TMEM: S [0, 128) and dP [128, 256) (two 64-column buffers each), Q hi/lo [256, 384), dO
+// hi/lo [384, 512).
+struct PdsArgs {
+  int64_t Tq, Tk, H, BH, ldS;
+  int causal;
+  float scale;
+  const float* lse;
+  const float* delta;
+  float* P;
+  float* dS;
+  int q_blocks, items;
+};
+
+template <int D>
+struct PLayout {
+  static constexpr uint32_t Q_BYTES = FQ * D * 4;  // one of Q, dO
+  static constexpr uint32_t KV = FK * D * 4;
+  static constexpr uint32_t STAGE = 4 * KV;
+  static constexpr int STAGES = D == 64 ? 2 : 5;
+  static constexpr uint32_t S_COL = 0, DP_COL = 2 * FK, Q_COL = 4 * FK, DO_COL = 4 * FK + 2 * D;
+  static constexpr uint32_t BOX = 32 * 32 * 4;      // one 32 x 32 output box
+  static constexpr uint32_t STAGING = 4 * 2 * BOX;  // per softmax warp: a P box and a dS box
+  static constexpr uint32_t SMEM = 2 * Q_BYTES + STAGES * STAGE + STAGING + 1024 + 512;
+};
+
+__device__ __forceinline__ void pds_item(const PdsArgs& a, int item, int& bh, int& qb) {
+  qb = a.q_blocks - 1 - item / (int)a.BH;
+  bh = item % (int)a.BH;
+}
+
+__device__ __forceinline__ int pds_blocks(const PdsArgs& a, int qb) {
+  const int64_t end = a.causal ? ((int64_t)(qb + 1) * FQ < a.Tk ? (int64_t)(qb + 1) * FQ : a.Tk)
+                               : a.Tk;
+  return (int)((end + FK - 1) / FK);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kFThreads, 1)
+attn_pds_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmO,
+                const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmS,
+                PdsArgs a) {
+  using L = PLayout<D>;
+  constexpr int ST = L::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* q_smem = smem;
+  uint8_t* do_smem = smem + L::Q_BYTES;
+  uint8_t* kv_smem = smem + 2 * L::Q_BYTES;
+  uint8_t* staging = kv_smem + ST * L::STAGE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(staging + L::STAGING);
+  uint64_t* q_full = bars;
+  uint64_t* q_ready = bars + 1;
+  uint64_t* q_empty = bars + 2;
+  uint64_t* drain = bars + 3;
+  uint64_t* sd_full = bars + 4;   // [2]
+  uint64_t* sd_empty = bars + 6;  // [2]
+  uint64_t* kv_full = bars + 8;   // [ST]
+  uint64_t* kv_split = kv_full + ST;
+  uint64_t* kv_empty = kv_split + ST;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(kv_empty + ST);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  auto k_raw = [&](int s) { return kv_smem + s * L::STAGE; };
+  auto k_lo = [&](int s) { return kv_smem + s * L::STAGE + L::KV; };
+  auto v_raw = [&](int s) { return kv_smem + s * L::STAGE + 2 * L::KV; };
+  auto v_lo = [&](int s) { return kv_smem + s * L::STAGE + 3 * L::KV; };
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_ready, 8);
+    mbar_init(q_empty, 1);
+    mbar_init(drain, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sd_full[b], 1);
+      mbar_init(&sd_empty[b], 4);
+    }
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_split[s], 8);
+      mbar_init(&kv_empty[s], 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0, tq = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x, ++tq) {
+        int bh, qb;
+        pds_item(a, item, bh, qb);
+        const int h = (int)(bh % a.H), b = (int)(bh / a.H);
+        if (tq > 0 && !wait_bar(q_ready, (tq - 1) & 1, abort_flag)) break;
+        mbar_arrive_expect_tx(q_full, 2 * L::Q_BYTES);
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          tma_load_4d(q_smem + c * FQ * 128, &tmQ, q_full, 32 * c, qb * FQ, h, b);
+          tma_load_4d(do_smem + c * FQ * 128, &tmO, q_full, 32 * c, qb * FQ, h, b);
+        }
+        const int nkb = pds_blocks(a, qb);
+        for (int j = 0; j < nkb; ++j, ++it) {
+          const int s = it % ST, round = it / ST;
+          if (round > 0 && !wait_bar(&kv_empty[s], (round - 1) & 1, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&kv_full[s], 2 * L::KV);
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            tma_load_4d(k_raw(s) + c * FK * 128, &tmK, &kv_full[s], 32 * c, j * FK, h, b);
+            tma_load_4d(v_raw(s) + c * FK * 128, &tmV, &kv_full[s], 32 * c, j * FK, h, b);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idS = instr_desc(FQ, FK, false, false);
+      int it = 0, tq = 0, sj = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x, ++tq) {
+        int bh, qb;
+        pds_item(a, item, bh, qb);
+        const int nkb = pds_blocks(a, qb);
+        if (!wait_bar(q_ready, tq & 1, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        for (int j = 0; j < nkb; ++j, ++it) {
+          const int s = it % ST, round = it / ST;
+          if (!wait_bar(&kv_split[s], round & 1, abort_flag)) { ok = false; break; }
+          const int b = sj & 1;
+          if (sj >= 2 && !wait_bar(&sd_empty[b], ((sj >> 1) - 1) & 1, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t kr = smem_u32(k_raw(s)), kl = smem_u32(k_lo(s));
+          const uint32_t vr = smem_u32(v_raw(s)), vl = smem_u32(v_lo(s));
+          const uint32_t sacc = tmem + L::S_COL + b * FK, dacc = tmem + L::DP_COL + b * FK;
+#pragma unroll
+          for (int kk = 0; kk < D / 8; ++kk) {
+            const uint32_t off = (kk >> 2) * FK * 128 + (kk & 3) * 32;
+            const uint64_t kh = smem_desc(kr + off, 16, 1024, 2);
+            const uint64_t klo = smem_desc(kl + off, 16, 1024, 2);
+            const uint64_t vh = smem_desc(vr + off, 16, 1024, 2);
+            const uint64_t vlo = smem_desc(vl + off, 16, 1024, 2);
+            const uint32_t qh = tmem + L::Q_COL + kk * 8, qlo = qh + D;
+            const uint32_t oh = tmem + L::DO_COL + kk * 8, olo = oh + D;
+            mma_tf32_ta(sacc, qlo, kh, idS, kk != 0);
+            mma_tf32_ta(sacc, qh, klo, idS, 1);
+            mma_tf32_ta(sacc, qh, kh, idS, 1);
+            mma_tf32_ta(dacc, olo, vh, idS, kk != 0);
+            mma_tf32_ta(dacc, oh, vlo, idS, 1);
+            mma_tf32_ta(dacc, oh, vh, idS, 1);
+          }
+          mma_commit(&sd_full[b]);
+          mma_commit(&kv_empty[s]);
+          ++sj;
+          if (j == nkb - 1) mma_commit(q_empty);
+        }
+      }
+      if (!ok) {
+        mma_commit(drain);
+        wait_bar(drain, 0, abort_flag, false);
+      }
+    }
+  } else if (warp >= kSplit0 && warp < kSoft0) {
+    const int t0 = threadIdx.x - kSplit0 * 32;
+    const int qr = warp & 3, qc = (warp - kSplit0) >> 2;
+    auto lo_of = [](float x) { return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); };
+    int it = 0, tq = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x, ++tq) {
+      int bh, qb;
+      pds_item(a, item, bh, qb);
+      const int nkb = pds_blocks(a, qb);
+      const bool landed = wait_bar(q_full, tq & 1, abort_flag) &&
+                          (tq == 0 || wait_bar(q_empty, (tq - 1) & 1, abort_flag));
+      if (!__all_sync(0xffffffffu, landed)) break;
+      if (qc < D / 32) {
+        const int r = 32 * qr + lane, sw = r & 7;
+#pragma unroll
+        for (int which = 0; which < 2; ++which) {
+          const uint8_t* row = (which ? do_smem : q_smem) + qc * FQ * 128 + r * 128;
+          const uint32_t col0 = which ? L::DO_COL : L::Q_COL;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float4 v0 = *reinterpret_cast<const float4*>(row + (((2 * u) ^ sw) << 4));
+            const float4 v1 = *reinterpret_cast<const float4*>(row + (((2 * u + 1) ^ sw) << 4));
+            const uint32_t taddr = tmem + ((uint32_t)(32 * qr) << 16) + col0 + 32 * qc + 8 * u;
+            const uint32_t hi[8] = {__float_as_uint(v0.x), __float_as_uint(v0.y),
+                                    __float_as_uint(v0.z), __float_as_uint(v0.w),
+                                    __float_as_uint(v1.x), __float_as_uint(v1.y),
+                                    __float_as_uint(v1.z), __float_as_uint(v1.w)};
+            const uint32_t lo[8] = {__float_as_uint(lo_of(v0.x)), __float_as_uint(lo_of(v0.y)),
+                                    __float_as_uint(lo_of(v0.z)), __float_as_uint(lo_of(v0.w)),
+                                    __float_as_uint(lo_of(v1.x)), __float_as_uint(lo_of(v1.y)),
+                                    __float_as_uint(lo_of(v1.z)), __float_as_uint(lo_of(v1.w))};
+            tmem_st8(taddr, hi);
+            tmem_st8(taddr + D, lo);
+          }
+        }
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_ready);
+      for (int j = 0; j < nkb; ++j, ++it) {
+        const int s = it % ST, round = it / ST;
+        if (!__all_sync(0xffffffffu, wait_bar(&kv_full[s], round & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        const float4* kr = reinterpret_cast<const float4*>(k_raw(s));
+        float4* kl = reinterpret_cast<float4*>(k_lo(s));
+        const float4* vr = reinterpret_cast<const float4*>(v_raw(s));
+        float4* vl = reinterpret_cast<float4*>(v_lo(s));
+#pragma unroll
+        for (int i = t0; i < (int)(L::KV / 16); i += 256) {
+          const float4 x = kr[i], y = vr[i];
+          kl[i] = make_float4(lo_of(x.x), lo_of(x.y), lo_of(x.z), lo_of(x.w));
+          vl[i] = make_float4(lo_of(y.x), lo_of(y.y), lo_of(y.z), lo_of(y.w));
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&kv_split[s]);
+      }
+    }
+  } else if (warp >= kSoft0) {
+    const int ew = warp - kSoft0;
+    const uint32_t lanes = (uint32_t)(32 * ew) << 16;
+    int tq = 0, sj = 0;
+    for (int item = blockIdx.x; item < a.items; item += gridDim.x, ++tq) {
+      int bh, qb;
+      pds_item(a, item, bh, qb);
+      const int nkb = pds_blocks(a, qb);
+      const int row0 = qb * FQ + 32 * ew;
+      const int64_t row = (int64_t)row0 + lane;
+      const bool live = row < a.Tq;
+      const float lse_r = live ? a.lse[bh * a.Tq + row] : 0.f;
+      const float delta_r = live ? a.delta[bh * a.Tq + row] : 0.f;
+      bool ok = true;
+      for (int j = 0; j < nkb; ++j) {
+        const int b = sj & 1;
+        if (!__all_sync(0xffffffffu, wait_bar(&sd_full[b], (sj >> 1) & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int64_t key0 = (int64_t)j * FK;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t sv[32], dv[32];
+          tmem_ld32(tmem + lanes + L::S_COL + b * FK + 32 * h, sv);
+          tmem_ld32(tmem + lanes + L::DP_COL + b * FK + 32 * h, dv);
+          if (h == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sd_empty[b]);
+          }
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const int64_t key = key0 + 32 * h + c;
+            const bool valid = key < a.Tk && (!a.causal || key <= row);
+            const float e = __expf(__fmul_rn(__uint_as_float(sv[c]), a.scale) - lse_r);
+            const float p = valid ? e : 0.f;
+            sv[c] = __float_as_uint(p);
+            dv[c] = __float_as_uint(p * (__uint_as_float(dv[c]) - delta_r) * a.scale);
+          }
+          // 32 x 32 boxes of P and dS through shared memory (128-byte swizzle: lane = row,
+          // 16-byte chunk k at k ^ (lane % 8)) and one TMA store each; rows and keys past the
+          // product are clipped by the maps. The previous pair must have been read first.
+          float4* pbox = reinterpret_cast<float4*>(staging + ew * 2 * L::BOX);
+          float4* dbox = reinterpret_cast<float4*>(staging + ew * 2 * L::BOX + L::BOX);
+          if (lane == 0) bulk_wait_read<0>();
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int slot = lane * 8 + (k ^ (lane & 7));
+            pbox[slot] = make_float4(__uint_as_float(sv[4 * k]), __uint_as_float(sv[4 * k + 1]),
+                                     __uint_as_float(sv[4 * k + 2]), __uint_as_float(sv[4 * k + 3]));
+            dbox[slot] = make_float4(__uint_as_float(dv[4 * k]), __uint_as_float(dv[4 * k + 1]),
+                                     __uint_as_float(dv[4 * k + 2]), __uint_as_float(dv[4 * k + 3]));
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && row0 < a.Tq) {
+            tma_store_4d(&tmP, pbox, (int)key0 + 32 * h, row0, 0, bh);
+            tma_store_4d(&tmS, dbox, (int)key0 + 32 * h, row0, 0, bh);
+            bulk_commit();
+          }
+        }
+        ++sj;
+      }
+      if (!ok) break;
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int D>
+int launch_pds(const tg_attn_shape* s, const float* q, const float* k, const float* v,
+               const float* dout, const float* lse, const float* delta, float* P, float* dS,
+               int64_t ldS, cudaStream_t st) {
+  using L = PLayout<D>;
+  CUtensorMap mq, mo, mk, mv;
+  int rc;
+  if ((rc = make_map(&mq, q, D, s->tq, s->q_st, s->heads, s->q_sh, s->batch, s->q_sb, 32, FQ,
+                     CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if ((rc = make_map(&mo, dout, D, s->tq, s->o_st, s->heads, s->o_sh, s->batch, s->o_sb, 32, FQ,
+                     CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if ((rc = make_map(&mk, k, D, s->tk, s->k_st, s->heads, s->k_sh, s->batch, s->k_sb, 32, FK,
+                     CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if ((rc = make_map(&mv, v, D, s->tk, s->v_st, s->heads, s->v_sh, s->batch, s->v_sb, 32, FK,
+                     CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  // P and dS: (B*H) blocks of Tq rows x Tk keys, row stride ldS.
+  CUtensorMap mp, md;
+  const int64_t bh = s->batch * s->heads;
+  if ((rc = make_map(&mp, P, s->tk, s->tq, ldS, 1, 0, bh, s->tq * ldS, 32, 32,
+                     CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if ((rc = make_map(&md, dS, s->tk, s->tq, ldS, 1, 0, bh, s->tq * ldS, 32, 32,
+                     CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  static bool configured = false;
+  if (!configured) {
+    TG_CUDA_TRY(cudaFuncSetAttribute(attn_pds_kernel<D>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::SMEM));
+    configured = true;
+  }
+  PdsArgs a{};
+  a.Tq = s->tq; a.Tk = s->tk; a.H = s->heads; a.BH = s->batch * s->heads; a.ldS = ldS;
+  a.causal = s->causal;
+  a.scale = (float)(1.0 / sqrt((double)D));
+  a.lse = lse; a.delta = delta; a.P = P; a.dS = dS;
+  a.q_blocks = (int)((s->tq + FQ - 1) / FQ);
+  a.items = (int)(a.BH * a.q_blocks);
+  const int grid = a.items < sm_count() ? a.items : sm_count();
+  attn_pds_kernel<D><<<grid, kFThreads, L::SMEM, st>>>(mq, mo, mk, mv, mp, md, a);
+  return check_launch("attention backward (P, dS)");
+}
+
 }  // namespace
 }  // namespace tc
 
@@ -442,6 +806,14 @@ int flash_fwd_tc(const tg_attn_shape* s, const float* q, const float* k, const f
                  float* o, float* lse, cudaStream_t st) {
   if (s->head_dim == 32) return tc::launch_flash<32>(s, q, k, v, o, lse, st);
   return tc::launch_flash<64>(s, q, k, v, o, lse, st);
+}
+
+// P and dS of the attention backward (row stride ldS), same shapes as the fused forward.
+int attn_pds_tc(const tg_attn_shape* s, const float* q, const float* k, const float* v,
+                const float* dout, const float* lse, const float* delta, float* P, float* dS,
+                int64_t ldS, cudaStream_t st) {
+  if (s->head_dim == 32) return tc::launch_pds<32>(s, q, k, v, dout, lse, delta, P, dS, ldS, st);
+  return tc::launch_pds<64>(s, q, k, v, dout, lse, delta, P, dS, ldS, st);
 }
 
 }  // namespace tg
