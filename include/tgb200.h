@@ -82,6 +82,8 @@ uint64_t tg_launch_count(void);
 /* Reads (and with reset != 0 clears) the tensor-core GEMM's device status word: TG_OK, or
  * TG_ERR_TIMEOUT when a bounded pipeline wait gave up. Synchronous. */
 int tg_gemm_tc_status(int reset);
+/* The same record for the fused attention kernels (forward; P and dS of the backward). */
+int tg_attention_tc_status(int reset);
 /* Strided-batched GEMM: `batch` products at element offsets i*stride_{a,b,c}. */
 int tg_gemm_batched(int dtype, int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
                     double alpha, const void* a, int64_t lda, int64_t stride_a, const void* b,

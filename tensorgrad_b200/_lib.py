@@ -66,6 +66,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tg_gemm_simt": (c_int, [c_int, c_int, c_int, i64, i64, i64, dbl, vp, i64, vp, i64, dbl, vp,
                              i64, vp, vp]),
     "tg_gemm_tc_status": (c_int, [c_int]),
+    "tg_attention_tc_status": (c_int, [c_int]),
     "tg_set_matmul_precision": (c_int, [c_int]),
     "tg_gemm_profile": (c_int, [c_int]),
     "tg_gemm_profile_read": (c_int, [POINTER(c_double), POINTER(c_int64), POINTER(c_double)]),

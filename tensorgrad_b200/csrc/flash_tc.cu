@@ -817,3 +817,14 @@ int attn_pds_tc(const tg_attn_shape* s, const float* q, const float* k, const fl
 }
 
 }  // namespace tg
+
+// The fused attention kernels' timeout record (this unit's status word); reset when asked.
+extern "C" int tg_attention_tc_status(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, tg::tc::g_status, sizeof(int)) != cudaSuccess) return -1;
+  if (reset) {
+    const int z = 0;
+    cudaMemcpyToSymbol(tg::tc::g_status, &z, sizeof(int));
+  }
+  return v;
+}

@@ -312,6 +312,7 @@ def test_attention_causal_with_longer_keys(dtype):
                                               ((1, 3, 257, 64), 257, True)])
 def test_fused_attention_forward_shapes(dtype, qshape, tk, causal):
     import tensorgrad_b200 as tg
+    from tensorgrad_b200._lib import lib
 
     rng = np.random.default_rng(qshape[2] + tk)
     b, h, tq, d = qshape
@@ -322,6 +323,7 @@ def test_fused_attention_forward_shapes(dtype, qshape, tk, causal):
     dq, dk, dv = tg.autograd.grad(o, [tq_, tk_, tv_], grad_outputs=do.astype(dtype))
     ref_o, p = O.attention_forward(q, k, v, causal)
     refs = (ref_o, *O.attention_backward(do, q, k, v, p))
+    assert lib.tg_attention_tc_status(1) == 0  # no bounded wait of the fused kernels expired
     for ours, ref, name in zip((o, dq, dk, dv), refs, ("out", "dq", "dk", "dv"), strict=True):
         if np.max(np.abs(ref)) == 0.0:
             # A single visible key: softmax is 1 whatever the scores, dq = dk = 0 exactly;
