@@ -311,8 +311,11 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
           if (c < 32) r0[c] = __float_as_uint(v); else r1[c - 32] = __float_as_uint(v);
           mloc = fmaxf(mloc, v);
         }
-        const float m_new = fmaxf(m, mloc);
-        const float corr = __expf(m - m_new);  // 0 for the first block (m = -inf)
+        // The running max used for the exponentials moves only when a block's max exceeds it
+        // by more than 8 (a factor e^8 ~ 3e3, harmless in fp32): O and the sum are then
+        // rescaled far less often. lse = max + log(sum) holds for any such max.
+        const float m_new = mloc > m + 8.f ? mloc : m;
+        const float corr = __expf(m - m_new);  // 0 for the first block (m = -inf), else <= 1
         float lsum = 0.f;
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
