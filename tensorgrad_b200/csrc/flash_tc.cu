@@ -28,6 +28,8 @@ constexpr int FQ = 128;  // query rows per item (TMEM lanes)
 constexpr int FK = 64;   // keys per block
 constexpr int kFThreads = 512;
 constexpr int kSplit0 = 4, kSoft0 = 12;
+// The P / dS kernel: split warps 4..7, element-wise warps 8..15.
+constexpr int kPSplit0 = 4, kPElem0 = 8;
 
 struct FlashArgs {
   int64_t Tq, Tk, H, BH;
@@ -437,9 +439,10 @@ int launch_flash(const tg_attn_shape* s, const float* q, const float* k, const f
 // P = exp(scale S - lse), dS = P (dP - delta) scale, masked like the forward, written to the
 // row-major P and dS blocks (row stride ldS) that the dV, dK and dQ products read.
 //   warp 0: TMA of Q and dO once per item, K and V blocks through a ring;
-//   warps 4..11: Q's and dO's hi/lo into TMEM, lo of each K and V block;
+//   warps 4..7: Q's and dO's hi/lo into TMEM, lo of each K and V block;
 //   warp 1: both products of a block into one of two TMEM buffer pairs;
-//   warps 12..15: the element-wise VJP and the stores.
+//   warps 8..15: the element-wise VJP and the stores, two warps per lane quarter (one per
+//   32-key half of a block).
 // TMEM: S [0, 128) and dP [128, 256) (two 64-column buffers each), Q hi/lo [256, 384), dO
 // hi/lo [384, 512).
 struct PdsArgs {
@@ -460,8 +463,8 @@ struct PLayout {
   static constexpr uint32_t STAGE = 4 * KV;
   static constexpr int STAGES = D == 64 ? 2 : 5;
   static constexpr uint32_t S_COL = 0, DP_COL = 2 * FK, Q_COL = 4 * FK, DO_COL = 4 * FK + 2 * D;
-  static constexpr uint32_t BOX = 32 * 32 * 4;      // one 32 x 32 output box
-  static constexpr uint32_t STAGING = 4 * 2 * BOX;  // per softmax warp: a P box and a dS box
+  static constexpr uint32_t BOX = 32 * 32 * 4;  // one 32 x 32 output box
+  static constexpr uint32_t STAGING = 8 * BOX;  // one box per element-wise warp
   static constexpr uint32_t SMEM = 2 * Q_BYTES + STAGES * STAGE + STAGING + 1024 + 512;
 };
 
@@ -512,16 +515,16 @@ attn_pds_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    mbar_init(q_ready, 8);
+    mbar_init(q_ready, 4);
     mbar_init(q_empty, 1);
     mbar_init(drain, 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sd_full[b], 1);
-      mbar_init(&sd_empty[b], 4);
+      mbar_init(&sd_empty[b], 8);
     }
     for (int s = 0; s < ST; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_split[s], 8);
+      mbar_init(&kv_split[s], 4);
       mbar_init(&kv_empty[s], 1);
     }
     *abort_flag = 0;
@@ -608,9 +611,9 @@ attn_pds_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         wait_bar(drain, 0, abort_flag, false);
       }
     }
-  } else if (warp >= kSplit0 && warp < kSoft0) {
-    const int t0 = threadIdx.x - kSplit0 * 32;
-    const int qr = warp & 3, qc = (warp - kSplit0) >> 2;
+  } else if (warp >= kPSplit0 && warp < kPElem0) {
+    const int t0 = threadIdx.x - kPSplit0 * 32;
+    const int qr = warp & 3;
     auto lo_of = [](float x) { return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); };
     int it = 0, tq = 0;
     bool ok = true;
@@ -621,7 +624,8 @@ attn_pds_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       const bool landed = wait_bar(q_full, tq & 1, abort_flag) &&
                           (tq == 0 || wait_bar(q_empty, (tq - 1) & 1, abort_flag));
       if (!__all_sync(0xffffffffu, landed)) break;
-      if (qc < D / 32) {
+#pragma unroll
+      for (int qc = 0; qc < D / 32; ++qc) {
         const int r = 32 * qr + lane, sw = r & 7;
 #pragma unroll
         for (int which = 0; which < 2; ++which) {
@@ -644,8 +648,8 @@ attn_pds_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
             tmem_st8(taddr + D, lo);
           }
         }
-        tmem_wait_st();
       }
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(q_ready);
@@ -660,7 +664,7 @@ attn_pds_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         const float4* vr = reinterpret_cast<const float4*>(v_raw(s));
         float4* vl = reinterpret_cast<float4*>(v_lo(s));
 #pragma unroll
-        for (int i = t0; i < (int)(L::KV / 16); i += 256) {
+        for (int i = t0; i < (int)(L::KV / 16); i += 128) {
           const float4 x = kr[i], y = vr[i];
           kl[i] = make_float4(lo_of(x.x), lo_of(x.y), lo_of(x.z), lo_of(x.w));
           vl[i] = make_float4(lo_of(y.x), lo_of(y.y), lo_of(y.z), lo_of(y.w));
@@ -670,9 +674,11 @@ attn_pds_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         if (lane == 0) mbar_arrive(&kv_split[s]);
       }
     }
-  } else if (warp >= kSoft0) {
-    const int ew = warp - kSoft0;
+  } else if (warp >= kPElem0) {
+    // Eight warps: lane quarter warp % 4 (rows), half hh of the 64 keys of a block.
+    const int ew = warp & 3, hh = (warp - kPElem0) >> 2;
     const uint32_t lanes = (uint32_t)(32 * ew) << 16;
+    float4* box = reinterpret_cast<float4*>(staging + (warp - kPElem0) * L::BOX);
     int tq = 0, sj = 0;
     for (int item = blockIdx.x; item < a.items; item += gridDim.x, ++tq) {
       int bh, qb;
@@ -691,50 +697,43 @@ attn_pds_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           break;
         }
         tc_fence_after();
-        const int64_t key0 = (int64_t)j * FK;
+        const int64_t key0 = (int64_t)j * FK + 32 * hh;
+        uint32_t sv[32], dv[32];
+        tmem_ld32(tmem + lanes + L::S_COL + b * FK + 32 * hh, sv);
+        tmem_ld32(tmem + lanes + L::DP_COL + b * FK + 32 * hh, dv);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sd_empty[b]);
+        ++sj;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint32_t sv[32], dv[32];
-          tmem_ld32(tmem + lanes + L::S_COL + b * FK + 32 * h, sv);
-          tmem_ld32(tmem + lanes + L::DP_COL + b * FK + 32 * h, dv);
-          if (h == 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&sd_empty[b]);
-          }
+        for (int c = 0; c < 32; ++c) {
+          const int64_t key = key0 + c;
+          const bool valid = key < a.Tk && (!a.causal || key <= row);
+          const float e = __expf(__fmul_rn(__uint_as_float(sv[c]), a.scale) - lse_r);
+          const float p = valid ? e : 0.f;
+          sv[c] = __float_as_uint(p);
+          dv[c] = __float_as_uint(p * (__uint_as_float(dv[c]) - delta_r) * a.scale);
+        }
+        // 32 x 32 boxes of P, then dS, through this warp's shared-memory box (128-byte
+        // swizzle: lane = row, 16-byte chunk k at k ^ (lane % 8)) and one TMA store each;
+        // rows and keys past the product are clipped by the maps.
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const int64_t key = key0 + 32 * h + c;
-            const bool valid = key < a.Tk && (!a.causal || key <= row);
-            const float e = __expf(__fmul_rn(__uint_as_float(sv[c]), a.scale) - lse_r);
-            const float p = valid ? e : 0.f;
-            sv[c] = __float_as_uint(p);
-            dv[c] = __float_as_uint(p * (__uint_as_float(dv[c]) - delta_r) * a.scale);
-          }
-          // 32 x 32 boxes of P and dS through shared memory (128-byte swizzle: lane = row,
-          // 16-byte chunk k at k ^ (lane % 8)) and one TMA store each; rows and keys past the
-          // product are clipped by the maps. The previous pair must have been read first.
-          float4* pbox = reinterpret_cast<float4*>(staging + ew * 2 * L::BOX);
-          float4* dbox = reinterpret_cast<float4*>(staging + ew * 2 * L::BOX + L::BOX);
+        for (int which = 0; which < 2; ++which) {
+          const uint32_t* v = which ? dv : sv;
           if (lane == 0) bulk_wait_read<0>();
           __syncwarp();
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const int slot = lane * 8 + (k ^ (lane & 7));
-            pbox[slot] = make_float4(__uint_as_float(sv[4 * k]), __uint_as_float(sv[4 * k + 1]),
-                                     __uint_as_float(sv[4 * k + 2]), __uint_as_float(sv[4 * k + 3]));
-            dbox[slot] = make_float4(__uint_as_float(dv[4 * k]), __uint_as_float(dv[4 * k + 1]),
-                                     __uint_as_float(dv[4 * k + 2]), __uint_as_float(dv[4 * k + 3]));
-          }
+          for (int kq = 0; kq < 8; ++kq)
+            box[lane * 8 + (kq ^ (lane & 7))] =
+                make_float4(__uint_as_float(v[4 * kq]), __uint_as_float(v[4 * kq + 1]),
+                            __uint_as_float(v[4 * kq + 2]), __uint_as_float(v[4 * kq + 3]));
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0 && row0 < a.Tq) {
-            tma_store_4d(&tmP, pbox, (int)key0 + 32 * h, row0, 0, bh);
-            tma_store_4d(&tmS, dbox, (int)key0 + 32 * h, row0, 0, bh);
+            tma_store_4d(which ? &tmS : &tmP, box, (int)key0, row0, 0, bh);
             bulk_commit();
           }
         }
-        ++sj;
       }
       if (!ok) break;
     }
