@@ -6,16 +6,17 @@
 // truncates; lo = x - hi):
 //   warp 0 (lane 0): TMA producer: the item's Q (128 x D) once, then K and V blocks (64 x D)
 //                    through a STAGES-deep ring.
-//   warps 4..11    : Q's hi and lo into tensor memory (the A operand of S = Q K^T); lo of each
+//   warps 4..7     : Q's hi and lo into tensor memory (the A operand of S = Q K^T); lo of each
 //                    K and V block in shared memory.
 //   warp 1 (lane 0): MMA issuer: S_j = Q K_j^T into one of two TMEM score buffers, then
 //                    O += P_{j-1} V_{j-1} (P from TMEM), so S_j overlaps the softmax of j-1.
-//   warps 12..15   : online softmax, lane = query row: S_j from TMEM, scale and causal /
-//                    length mask, running max and sum, O rescaled in TMEM when the max grows,
-//                    P_j's hi and lo into TMEM; at the end O / sum to global memory and
-//                    lse = max + log(sum).
+//   warps 8..15    : online softmax, lane = query row, two warps per lane quarter (one per
+//                    32-key half of a block, agreeing on the row max through two TMEM columns):
+//                    S_j from TMEM, scale and causal / length mask, running max and sum, O
+//                    rescaled in TMEM when the max grows, P_j's hi and lo into TMEM; at the end
+//                    O / sum to global memory and lse = max + log(sum).
 // TMEM columns: O [0, D), S [D, D + 128) (two buffers), P hi/lo [D + 128, D + 256), Q hi/lo
-// [D + 256, 3 D + 256). Every wait is bounded; on expiry the kernel records TG_ERR_TIMEOUT in
+// [D + 256, 3 D + 256), the max exchange [3 D + 256, 3 D + 260). Every wait is bounded; on expiry the kernel records TG_ERR_TIMEOUT in
 // this unit's status word, stops, drains and frees its TMEM.
 #include "common.cuh"
 #include "tc_ptx.cuh"
@@ -49,6 +50,9 @@ struct FLayout {
   static constexpr int STAGES = D == 64 ? 3 : 6;
   static constexpr uint32_t O_COL = 0, S_COL = D, P_COL = D + 2 * FK, Q_COL = D + 4 * FK;
   static constexpr uint32_t SMEM = Q_BYTES + STAGES * STAGE + 1024 + 512;
+  // Columns through which the two softmax warps of a lane quarter exchange one value per row:
+  // [parity][half].
+  static constexpr uint32_t X_COL = 3 * D + 4 * FK;
 };
 
 __device__ __forceinline__ void item_of(const FlashArgs& a, int item, int& bh, int& qb) {
@@ -88,7 +92,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
   uint64_t* kv_full = bars + 12;  // [ST]
   uint64_t* kv_split = kv_full + ST;
   uint64_t* kv_empty = kv_split + ST;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(kv_empty + ST);
+  uint64_t* xbar = kv_empty + ST;  // [4]: the two softmax warps of a lane quarter
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -99,22 +104,23 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    mbar_init(q_ready, 8);
+    mbar_init(q_ready, 4);
     mbar_init(q_empty, 1);
-    mbar_init(p_full, 4);
+    mbar_init(p_full, 8);
     mbar_init(p_empty, 1);
     mbar_init(o_full, 1);
-    mbar_init(o_empty, 4);
+    mbar_init(o_empty, 8);
     mbar_init(drain, 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&s_empty[b], 4);
+      mbar_init(&s_empty[b], 8);
     }
     for (int s = 0; s < ST; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_split[s], 8);
+      mbar_init(&kv_split[s], 4);
       mbar_init(&kv_empty[s], 1);
     }
+    for (int q = 0; q < 4; ++q) mbar_init(&xbar[q], 2);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -217,9 +223,9 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
         wait_bar(drain, 0, abort_flag, false);
       }
     }
-  } else if (warp >= kSplit0 && warp < kSoft0) {
-    const int t0 = threadIdx.x - kSplit0 * 32;
-    const int qr = warp & 3, qc = (warp - kSplit0) >> 2;  // lane quarter, 32-wide d chunk
+  } else if (warp >= kPSplit0 && warp < kPElem0) {
+    const int t0 = threadIdx.x - kPSplit0 * 32;
+    const int qr = warp & 3;  // lane quarter
     auto lo_of = [](float x) { return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); };
     int it = 0, tq = 0;
     bool ok = true;
@@ -230,7 +236,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
       const bool landed = wait_bar(q_full, tq & 1, abort_flag) &&
                           (tq == 0 || wait_bar(q_empty, (tq - 1) & 1, abort_flag));
       if (!__all_sync(0xffffffffu, landed)) break;
-      if (qc < D / 32) {
+#pragma unroll
+      for (int qc = 0; qc < D / 32; ++qc) {
         // Row r = 32 qr + lane of the 128-byte-swizzled box of d chunk qc: 16-byte chunk c
         // sits at c ^ (r % 8).
         const int r = 32 * qr + lane, sw = r & 7;
@@ -251,8 +258,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
           tmem_st8(taddr, hi);
           tmem_st8(taddr + D, lo);
         }
-        tmem_wait_st();
       }
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(q_ready);
@@ -267,7 +274,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
         const float4* vr = reinterpret_cast<const float4*>(v_raw(s));
         float4* vl = reinterpret_cast<float4*>(v_lo(s));
 #pragma unroll
-        for (int i = t0; i < (int)(L::KV / 16); i += 256) {
+        for (int i = t0; i < (int)(L::KV / 16); i += 128) {
           const float4 x = kr[i], y = vr[i];
           kl[i] = make_float4(lo_of(x.x), lo_of(x.y), lo_of(x.z), lo_of(x.w));
           vl[i] = make_float4(lo_of(y.x), lo_of(y.y), lo_of(y.z), lo_of(y.w));
@@ -277,17 +284,40 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
         if (lane == 0) mbar_arrive(&kv_split[s]);
       }
     }
-  } else if (warp >= kSoft0) {
-    const int ew = warp - kSoft0;
+  } else if (warp >= kPElem0) {
+    // Eight warps: lane quarter ew = warp % 4 (query rows), half hh of each 64-key block
+    // (and of O's columns). The two warps of a quarter agree on the running max through
+    // `xch` and a two-arrival barrier per exchange (bounded, like every wait here).
+    const int ew = warp & 3, hh = (warp - kPElem0) >> 2;
     const uint32_t lanes = (uint32_t)(32 * ew) << 16;
-    int tq = 0, sj = 0, pjs = 0;
+    constexpr int OC = D / 2;  // O columns of this warp
+    int tq = 0, sj = 0, pjs = 0, xs = 0;
     bool ok = true;
+    // Exchange one value per row with the partner warp through two TMEM columns (same
+    // lanes, alternating by parity so a slot is rewritten only after the partner read it);
+    // returns the partner's value.
+    auto exchange = [&](float v) -> float {
+      const uint32_t xcol = tmem + lanes + L::X_COL + (uint32_t)((xs & 1) * 2);
+      tmem_st1(xcol + hh, __float_as_uint(v));
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xbar[ew]);
+      const bool got = __all_sync(0xffffffffu, wait_bar(&xbar[ew], xs & 1, abort_flag));
+      ++xs;
+      if (!got) {
+        ok = false;
+        return v;
+      }
+      tc_fence_after();
+      return __uint_as_float(tmem_ld1(xcol + (1 - hh)));
+    };
     for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x, ++tq) {
       int bh, qb;
       item_of(a, item, bh, qb);
       const int nkb = key_blocks(a, qb);
       const int64_t row = (int64_t)qb * FQ + 32 * ew + lane;
-      float m = -INFINITY, l = 0.f;
+      float m = -INFINITY, l = 0.f;  // l: this warp's half of the row sum
       for (int j = 0; j < nkb; ++j) {
         const int b = sj & 1;
         if (!__all_sync(0xffffffffu, wait_bar(&s_full[b], (sj >> 1) & 1, abort_flag))) {
@@ -295,24 +325,25 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
           break;
         }
         tc_fence_after();
-        uint32_t r0[32], r1[32];
-        tmem_ld32(tmem + lanes + L::S_COL + b * FK, r0);
-        tmem_ld32(tmem + lanes + L::S_COL + b * FK + 32, r1);
+        uint32_t r0[32];
+        tmem_ld32(tmem + lanes + L::S_COL + b * FK + 32 * hh, r0);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_empty[b]);
         ++sj;
-        const int64_t key0 = (int64_t)j * FK;
+        const int64_t key0 = (int64_t)j * FK + 32 * hh;
         float mloc = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
+        for (int c = 0; c < 32; ++c) {
           const int64_t key = key0 + c;
           const bool valid = key < a.Tk && (!a.causal || key <= row);
-          const float x = __fmul_rn(__uint_as_float(c < 32 ? r0[c] : r1[c - 32]), a.scale);
+          const float x = __fmul_rn(__uint_as_float(r0[c]), a.scale);
           const float v = valid ? x : -INFINITY;
-          if (c < 32) r0[c] = __float_as_uint(v); else r1[c - 32] = __float_as_uint(v);
+          r0[c] = __float_as_uint(v);
           mloc = fmaxf(mloc, v);
         }
+        mloc = fmaxf(mloc, exchange(mloc));
+        if (!ok) break;
         // The running max used for the exponentials moves only when a block's max exceeds it
         // by more than 8 (a factor e^8 ~ 3e3, harmless in fp32): O and the sum are then
         // rescaled far less often. lse = max + log(sum) holds for any such max.
@@ -320,10 +351,10 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
         const float corr = __expf(m - m_new);  // 0 for the first block (m = -inf), else <= 1
         float lsum = 0.f;
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const float p = __expf(__uint_as_float(c < 32 ? r0[c] : r1[c - 32]) - m_new);
+        for (int c = 0; c < 32; ++c) {
+          const float p = __expf(__uint_as_float(r0[c]) - m_new);
           lsum += p;
-          if (c < 32) r0[c] = __float_as_uint(p); else r1[c - 32] = __float_as_uint(p);
+          r0[c] = __float_as_uint(p);
         }
         l = l * corr + lsum;
         m = m_new;
@@ -335,29 +366,27 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
         tc_fence_after();
         // P first (its registers are then free), then O rescaled when the max grew.
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < 4; ++u) {
           uint32_t hi[8], lo[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            const int c = 8 * u + e;
-            const float p = __uint_as_float(c < 32 ? r0[c] : r1[c - 32]);
+            const float p = __uint_as_float(r0[8 * u + e]);
             hi[e] = __float_as_uint(p);
             lo[e] = __float_as_uint(p - __uint_as_float(__float_as_uint(p) & 0xFFFFE000u));
           }
-          tmem_st8(tmem + lanes + L::P_COL + 8 * u, hi);
-          tmem_st8(tmem + lanes + L::P_COL + FK + 8 * u, lo);
+          tmem_st8(tmem + lanes + L::P_COL + 32 * hh + 8 * u, hi);
+          tmem_st8(tmem + lanes + L::P_COL + FK + 32 * hh + 8 * u, lo);
         }
         if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
-#pragma unroll
-          for (int c0 = 0; c0 < D; c0 += 32) {
-            uint32_t ov[32];
-            tmem_ld32(tmem + lanes + L::O_COL + c0, ov);
+          uint32_t ov[32];
+          tmem_ld32(tmem + lanes + L::O_COL + (D == 64 ? 32 * hh : 0), ov);
+          if (D == 64 || hh == 0) {
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               uint32_t w[8];
 #pragma unroll
               for (int e = 0; e < 8; ++e) w[e] = __float_as_uint(__uint_as_float(ov[8 * u + e]) * corr);
-              tmem_st8(tmem + lanes + L::O_COL + c0 + 8 * u, w);
+              tmem_st8(tmem + lanes + L::O_COL + (D == 64 ? 32 * hh : 0) + 8 * u, w);
             }
           }
         }
@@ -368,16 +397,18 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
         ++pjs;
       }
       if (!ok) break;
+      const float l_all = l + exchange(l);
+      if (!ok) break;
       if (!__all_sync(0xffffffffu, wait_bar(o_full, tq & 1, abort_flag))) break;
       tc_fence_after();
-      const float inv = 1.f / l;
+      const float inv = 1.f / l_all;
       const int h = (int)(bh % a.H), b = (int)(bh / a.H);
       float* orow = a.o + (int64_t)b * a.o_sb + (int64_t)h * a.o_sh + row * a.o_st;
-#pragma unroll
-      for (int c0 = 0; c0 < D; c0 += 32) {
+      {
+        const int c0 = D == 64 ? 32 * hh : 0;
         uint32_t ov[32];
         tmem_ld32(tmem + lanes + L::O_COL + c0, ov);
-        if (row < a.Tq) {
+        if (row < a.Tq && (D == 64 || hh == 0)) {
 #pragma unroll
           for (int e = 0; e < 32; e += 4)
             *reinterpret_cast<float4*>(orow + c0 + e) =
@@ -385,7 +416,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                             __uint_as_float(ov[e + 2]) * inv, __uint_as_float(ov[e + 3]) * inv);
         }
       }
-      if (row < a.Tq) a.lse[(int64_t)bh * a.Tq + row] = m + logf(l);
+      if (row < a.Tq && hh == 0) a.lse[(int64_t)bh * a.Tq + row] = m + logf(l_all);
+      (void)OC;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(o_empty);
