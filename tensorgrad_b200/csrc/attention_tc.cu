@@ -179,7 +179,11 @@ bool attention_tc_supported(int dtype, const tg_attn_shape* s) {
          strides_ok(s->v_sb, s->v_sh, s->v_st) && strides_ok(s->o_sb, s->o_sh, s->o_st);
 }
 
+// Heads of 32 or 64 features take the fused kernels (flash_tc.cu).
+bool flash_fwd_supported(const tg_attn_shape* s);
+
 size_t attention_tc_forward_scratch(const tg_attn_shape* s) {
+  if (flash_fwd_supported(s)) return 256;  // the fused forward keeps its scores on chip
   const Plan p = make_plan(s);
   return p.blk_s * sizeof(float) + 512;
 }
@@ -195,9 +199,8 @@ static float* carve(char*& cur, size_t floats) {
   return out;
 }
 
-// The fused kernels (flash_tc.cu), heads of 32 or 64 features: the forward, and P with dS of
-// the backward.
-bool flash_fwd_supported(const tg_attn_shape* s);
+// The fused kernels (flash_tc.cu), heads of 32 or 64 features (flash_fwd_supported, declared
+// above): the forward, and P with dS of the backward.
 int flash_fwd_tc(const tg_attn_shape* s, const float* q, const float* k, const float* v,
                  float* o, float* lse, cudaStream_t st);
 int attn_pds_tc(const tg_attn_shape* s, const float* q, const float* k, const float* v,
