@@ -84,6 +84,12 @@ uint64_t tg_launch_count(void);
 int tg_gemm_tc_status(int reset);
 /* The same record for the fused attention kernels (forward; P and dS of the backward). */
 int tg_attention_tc_status(int reset);
+/* Test support for those bounded waits (no reference counterpart): budget_cycles sets the
+ * cycle budget of every wait in the fused attention kernels (<= 0 restores the default,
+ * about two seconds); withhold_loads != 0 makes the forward's producer issue no load, so its
+ * first wait on a load runs out, TG_ERR_TIMEOUT is recorded and the kernel drains and
+ * returns with nothing in flight. Synchronous. */
+int tg_attention_set_wait_test(int64_t budget_cycles, int withhold_loads);
 /* Strided-batched GEMM: `batch` products at element offsets i*stride_{a,b,c}. */
 int tg_gemm_batched(int dtype, int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
                     double alpha, const void* a, int64_t lda, int64_t stride_a, const void* b,
@@ -186,10 +192,11 @@ int tg_layer_norm_backward(int dtype, const void* g, const void* x, const void* 
  * counterpart in the reference, which allocates its NumPy temporaries freely. The weight/
  * bias partial sums use a file-scope device array of 4 MiB per device instead of `scratch`;
  * a call whose partials need more (tg_layer_norm_scratch_bytes(dtype, rows, cols) > 4 MiB)
- * returns TG_ERR_ARG. The array's device address is looked up on a device's first call,
- * which should therefore come before any stream capture. All calls on a device share its
- * array, so calls that overlap on that GPU (e.g. on two streams) race; each call overwrites
- * every partial it reads, so no clearing is needed between calls. */
+ * returns TG_ERR_ARG. The array's device address is looked up on every call made outside
+ * stream capture and cached per device; a call on a capturing stream uses the cached
+ * address, so a device's first call should come before any stream capture. All calls on a
+ * device share its array, so calls that overlap on that GPU (e.g. on two streams) race; each
+ * call overwrites every partial it reads, so no clearing is needed between calls. */
 int tg_layer_norm_backward_noalloc(int dtype, const void* g, const void* x, const void* w,
                                    const void* mean, const void* rstd, void* gx, void* gw,
                                    void* gb, int64_t rows, int64_t cols, unsigned need,
@@ -377,6 +384,17 @@ int tg_clip_scale_multi(int dtype, int count, void* const* ptrs, const int64_t* 
 int tg_adam_update(int dtype, int64_t n, void* p, const void* g, void* m, void* v, double lr,
                    double beta1, double beta2, double eps, double weight_decay, int64_t step,
                    int decoupled, void* stream);
+/* clip_grad_norm_ and AdamW fused (optim/clip.py:15-31 then optim/adam.py:59-94): the same
+ * update, with the gradient read as g * (g's dtype)(max_norm / (total + clip_eps)) when that
+ * factor is below 1, total = clip_total_dev[0] (tg_sumsq_multi's result). g itself is left
+ * as it was (the host applies tg_clip_scale_multi later if the clipped gradient is read), so
+ * one pass moves 28 bytes per fp32 parameter instead of the rewrite's 8 plus the update's 28.
+ * clip_total_dev = NULL is tg_adam_update. */
+int tg_adam_update_clipped(int dtype, int64_t n, void* p, const void* g, void* m, void* v,
+                           double lr, double beta1, double beta2, double eps,
+                           double weight_decay, int64_t step, int decoupled,
+                           const double* clip_total_dev, double max_norm, double clip_eps,
+                           void* stream);
 /* Multi-tensor variant: one launch over `count` ranges (HOST pointer/size/step arrays). */
 size_t tg_adam_multi_scratch_bytes(int count);
 int tg_adam_update_multi(int dtype, int count, void* const* p, void* const* g, void* const* m,

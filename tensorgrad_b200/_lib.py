@@ -67,6 +67,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                              i64, vp, vp]),
     "tg_gemm_tc_status": (c_int, [c_int]),
     "tg_attention_tc_status": (c_int, [c_int]),
+    "tg_attention_set_wait_test": (c_int, [i64, c_int]),
     "tg_set_matmul_precision": (c_int, [c_int]),
     "tg_gemm_profile": (c_int, [c_int]),
     "tg_gemm_profile_read": (c_int, [POINTER(c_double), POINTER(c_int64), POINTER(c_double)]),
@@ -138,6 +139,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tg_clip_scale_multi": (c_int, [c_int, c_int, pvp, pi64, vp, dbl, dbl, vp, vp]),
     "tg_adam_update": (c_int, [c_int, i64, vp, vp, vp, vp, dbl, dbl, dbl, dbl, dbl, i64, c_int,
                                vp]),
+    "tg_adam_update_clipped": (c_int, [c_int, i64, vp, vp, vp, vp, dbl, dbl, dbl, dbl, dbl, i64,
+                                       c_int, vp, dbl, dbl, vp]),
     "tg_adam_multi_scratch_bytes": (sz, [c_int]),
     "tg_adam_update_multi": (c_int, [c_int, c_int, pvp, pvp, pvp, pvp, pi64, pi64, dbl, dbl, dbl,
                                      dbl, dbl, c_int, vp, vp]),

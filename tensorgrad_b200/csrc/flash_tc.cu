@@ -32,6 +32,11 @@ constexpr int kSplit0 = 4, kSoft0 = 12;
 // The P / dS kernel: split warps 4..7, element-wise warps 8..15.
 constexpr int kPSplit0 = 4, kPElem0 = 8;
 
+// Set only by tg_attention_set_wait_test: the forward's TMA producer then issues no load at
+// all (not even the first item's Q), so the first wait on a load times out and the kernel's
+// abort-and-drain path runs with nothing in flight.
+__device__ int g_withhold_loads = 0;
+
 struct FlashArgs {
   int64_t Tq, Tk, H, BH;
   int causal;
@@ -133,7 +138,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
   if (warp == 0) {
     if (lane == 0) {
       int it = 0, tq = 0;
-      bool ok = true;
+      bool ok = *(volatile int*)&g_withhold_loads == 0;
       for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x, ++tq) {
         int bh, qb;
         item_of(a, item, bh, qb);
@@ -831,8 +836,12 @@ int launch_pds(const tg_attn_shape* s, const float* q, const float* k, const flo
 
 // The fused forward takes fp32 heads of 32 or 64 features with the tensor-core path's
 // layout rules (16-byte strides and bases), at least one key, and a bounded item count.
+// The causal mask of both fused kernels is `key <= query` (aligned at the top left), which
+// is the reference's `key <= query + tk - tq` only when tq == tk; other causal shapes go to
+// the batched-GEMM path, which applies the shift.
 bool flash_fwd_supported(const tg_attn_shape* s) {
   return (s->head_dim == 32 || s->head_dim == 64) && s->tk >= 1 && s->tq >= 1 &&
+         (!s->causal || s->tq == s->tk) &&
          s->batch * s->heads * ((s->tq + 127) / 128) < (int64_t)1 << 30;
 }
 
@@ -856,9 +865,22 @@ int attn_pds_tc(const tg_attn_shape* s, const float* q, const float* k, const fl
 extern "C" int tg_attention_tc_status(int reset) {
   int v = 0;
   if (cudaMemcpyFromSymbol(&v, tg::tc::g_status, sizeof(int)) != cudaSuccess) return -1;
-  if (reset) {
+  if (reset && v != 0) {
     const int z = 0;
     cudaMemcpyToSymbol(tg::tc::g_status, &z, sizeof(int));
   }
   return v;
+}
+
+// Test support for the bounded waits of the fused attention kernels (no reference
+// counterpart): a wait budget in clock cycles (<= 0 restores the default of about two
+// seconds) and, with withhold_loads != 0, a forward whose producer issues no load, so that
+// the first wait on a load runs out, the kernel records TG_ERR_TIMEOUT and drains.
+// Synchronous; affects later launches of this unit's kernels only.
+extern "C" int tg_attention_set_wait_test(int64_t budget_cycles, int withhold_loads) {
+  const long long b = budget_cycles > 0 ? (long long)budget_cycles : tg::tc::kTimeoutCycles;
+  const int w = withhold_loads ? 1 : 0;
+  TG_CUDA_TRY(cudaMemcpyToSymbol(tg::tc::g_wait_budget, &b, sizeof(b)));
+  TG_CUDA_TRY(cudaMemcpyToSymbol(tg::tc::g_withhold_loads, &w, sizeof(w)));
+  return TG_OK;
 }

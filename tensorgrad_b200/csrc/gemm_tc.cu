@@ -1002,7 +1002,7 @@ int gemm_tc_f32(const GemmArgs<float>& p, cudaStream_t stream) {
 extern "C" int tg_gemm_tc_status(int reset) {
   int v = 0;
   if (cudaMemcpyFromSymbol(&v, tg::tc::g_status, sizeof(int)) != cudaSuccess) return -1;
-  if (reset) {
+  if (reset && v != 0) {
     const int z = 0;
     cudaMemcpyToSymbol(tg::tc::g_status, &z, sizeof(int));
   }

@@ -479,17 +479,26 @@ static __device__ __align__(256) unsigned char g_ln_static_scratch[kLnStaticScra
 void* g_ln_static_ptr[kMaxDevices] = {};
 std::mutex g_ln_static_mutex;
 
-// Device address of the array on the current device (host code only sees a stand-in
-// symbol, so the address is looked up once per device, with that device current).
-int ln_static_scratch(void** out) {
+// Device address of the array on the current device. Host code only sees a stand-in
+// symbol, so the address is looked up with that device current: on every call made outside
+// stream capture (the lookup is cheap, and a context rebuilt after cudaDeviceReset may place
+// the array elsewhere), and from the cache while `stream` is being captured, which therefore
+// needs one earlier uncaptured call on the device.
+int ln_static_scratch(void** out, cudaStream_t stream) {
   int dev = 0;
   TG_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices) return set_error(TG_ERR_UNSUPPORTED, "device %d", dev);
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  TG_CUDA_TRY(cudaStreamIsCapturing(stream, &capture));
   std::lock_guard<std::mutex> lock(g_ln_static_mutex);
-  if (!g_ln_static_ptr[dev]) {
+  if (capture == cudaStreamCaptureStatusNone) {
     void* p = nullptr;
     TG_CUDA_TRY(cudaGetSymbolAddress(&p, g_ln_static_scratch));
     g_ln_static_ptr[dev] = p;
+  } else if (!g_ln_static_ptr[dev]) {
+    return set_error(TG_ERR_ARG,
+                     "layer_norm_backward_noalloc: the first call on device %d is being "
+                     "captured; make one call outside capture first", dev);
   }
   *out = g_ln_static_ptr[dev];
   return TG_OK;
@@ -513,7 +522,7 @@ extern "C" int tg_layer_norm_backward_noalloc(int dtype, const void* g, const vo
                          bytes, tg::kLnStaticScratchBytes, (long long)rows, (long long)cols);
   void* scratch = nullptr;
   if (partials) {
-    const int rc = tg::ln_static_scratch(&scratch);
+    const int rc = tg::ln_static_scratch(&scratch, static_cast<cudaStream_t>(stream));
     if (rc != TG_OK) return rc;
   }
   // Every partial the second pass reads is written by the first pass of the same call, so

@@ -21,6 +21,9 @@ constexpr int BM = 128;
 constexpr long long kTimeoutCycles = 4000000000LL;  // ~2 s at 2 GHz
 
 __device__ int g_status = 0;  // this unit's timeout record
+// Cycle budget of every bounded wait in this unit (kTimeoutCycles unless a test shortened it
+// to make a wait run out on purpose; read only once a wait has to spin).
+__device__ long long g_wait_budget = kTimeoutCycles;
 
 // ------------------------------------------------------------------ PTX wrappers
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -64,11 +67,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                          bool respect_abort = true) {
   if (mbar_try_wait(bar, parity)) return true;
-  const long long t0 = clock64();
+  const long long t0 = clock64(), budget = *(volatile long long*)&g_wait_budget;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (respect_abort && *abort_flag) return false;
-    if (clock64() - t0 > kTimeoutCycles) {
+    if (clock64() - t0 > budget) {
       *abort_flag = 1;
       atomicExch(&g_status, (int)TG_ERR_TIMEOUT);
       return false;
@@ -128,11 +131,11 @@ __device__ __forceinline__ bool wait_bar_cluster(uint64_t* bar, uint32_t parity,
                                                  volatile int* abort_flag,
                                                  bool respect_abort = true) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
-  const long long t0 = clock64();
+  const long long t0 = clock64(), budget = *(volatile long long*)&g_wait_budget;
   while (true) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
     if (respect_abort && *abort_flag) return false;
-    if (clock64() - t0 > kTimeoutCycles) {
+    if (clock64() - t0 > budget) {
       *abort_flag = 1;
       atomicExch(&g_status, (int)TG_ERR_TIMEOUT);
       return false;

@@ -73,10 +73,27 @@ def dtype_code(dtype: np.dtype[Any]) -> int:
 
 
 def synchronize() -> None:
-    """Wait for the stream; then raise any error that device-side validation recorded."""
+    """Wait for the stream; then raise any error that the device recorded: a bounded wait of
+    a tensor-core kernel that ran out (its outputs are then incomplete), or an index that
+    device-side validation rejected."""
     check(lib.tg_stream_synchronize(_State.stream), "synchronize")
+    _raise_kernel_timeouts()
     if _Async.pending:
         _raise_async_errors()
+
+
+def _raise_kernel_timeouts() -> None:
+    """The tensor-core GEMM and the fused attention kernels give up a pipeline wait after a
+    cycle budget (about two seconds) instead of hanging; they then record TG_ERR_TIMEOUT in
+    a device status word, drain and return without finishing their outputs. Both words are
+    read (and cleared) at every host synchronisation, so such a step raises here."""
+    failed = [name for name, fn in (("tensor-core GEMM", lib.tg_gemm_tc_status),
+                                    ("fused attention", lib.tg_attention_tc_status))
+              if fn(1) != 0]
+    if failed:
+        raise RuntimeError(f"{' and '.join(failed)}: a bounded device-side wait ran out "
+                           "(TG_ERR_TIMEOUT); the outputs of the kernels since the last "
+                           "synchronisation are incomplete")
 
 
 # Device-side validation. Ops that take device-resident indices (embedding ids, class
