@@ -96,11 +96,29 @@ __device__ __forceinline__ void adam_elem(T& p, T g, T& m, T& v, T decay, T l2, 
   p = p - step_size * m / denom;
 }
 
+// The factor clip_grad_norm_ applies to every gradient, decided on the device from the total
+// norm: (T)(max_norm / (total + eps)) when that is below 1, else no rescale (clip_kernel's
+// rule, so a gradient scaled here equals the one clip_kernel would have written).
+struct ClipFactor {
+  const double* total;  // nullptr: no clip pending
+  double max_norm, eps;
+};
+
+template <typename T>
+__device__ __forceinline__ bool clip_factor(const ClipFactor& c, T& f) {
+  if (c.total == nullptr) return false;
+  const double scale = c.max_norm / (c.total[0] + c.eps);
+  f = (T)scale;
+  return scale < 1.0;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256)
-adam_multi_kernel(AdamList L, T b1, T b2, T eps, T decay, T l2) {
+adam_multi_kernel(AdamList L, T b1, T b2, T eps, T decay, T l2, ClipFactor clip = {}) {
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const T omb1 = T(1) - b1, omb2 = T(1) - b2;
+  T cf = T(1);
+  const bool scaled = clip_factor<T>(clip, cf);
   for (int t = 0; t < L.count; ++t) {
     T* p = reinterpret_cast<T*>(L.p[t]);
     const T* g = reinterpret_cast<const T*>(L.g[t]);
@@ -109,7 +127,8 @@ adam_multi_kernel(AdamList L, T b1, T b2, T eps, T decay, T l2) {
     const T ss = (T)L.step_size[t], bs = (T)L.bc2_sqrt[t];
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < L.numel[t]; i += stride) {
       T pi = p[i], mi = m[i], vi = v[i];
-      adam_elem<T>(pi, g[i], mi, vi, decay, l2, b1, omb1, b2, omb2, ss, bs, eps);
+      const T gi = scaled ? g[i] * cf : g[i];
+      adam_elem<T>(pi, gi, mi, vi, decay, l2, b1, omb1, b2, omb2, ss, bs, eps);
       p[i] = pi;
       m[i] = mi;
       v[i] = vi;
@@ -117,15 +136,20 @@ adam_multi_kernel(AdamList L, T b1, T b2, T eps, T decay, T l2) {
   }
 }
 
-// Flat fp32 range with 16-byte vectors.
+// Flat fp32 range with 16-byte vectors. With a clip pending (clip.total set), the gradient
+// is read rescaled and the update is the whole of clip_grad_norm_'s rewrite plus AdamW in
+// one pass: 28 bytes per parameter instead of 8 + 28.
 __global__ void __launch_bounds__(256)
 adam_flat_vec4_kernel(int64_t n4, float4* __restrict__ p, const float4* __restrict__ g,
                       float4* __restrict__ m, float4* __restrict__ v, float b1, float b2,
-                      float eps, float decay, float l2, float ss, float bs) {
+                      float eps, float decay, float l2, float ss, float bs, ClipFactor clip) {
   const float omb1 = 1.f - b1, omb2 = 1.f - b2;
+  float cf = 1.f;
+  const bool scaled = clip_factor<float>(clip, cf);
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
        i += (int64_t)gridDim.x * blockDim.x) {
     float4 P = p[i], G = g[i], M = m[i], V = v[i];
+    if (scaled) G = make_float4(G.x * cf, G.y * cf, G.z * cf, G.w * cf);
     adam_elem<float>(P.x, G.x, M.x, V.x, decay, l2, b1, omb1, b2, omb2, ss, bs, eps);
     adam_elem<float>(P.y, G.y, M.y, V.y, decay, l2, b1, omb1, b2, omb2, ss, bs, eps);
     adam_elem<float>(P.z, G.z, M.z, V.z, decay, l2, b1, omb1, b2, omb2, ss, bs, eps);
@@ -193,10 +217,26 @@ int tg_clip_scale_multi(int dtype, int count, void* const* ptrs, const int64_t* 
   });
 }
 
+int tg_adam_update_clipped(int dtype, int64_t n, void* p, const void* g, void* m, void* v,
+                           double lr, double beta1, double beta2, double eps,
+                           double weight_decay, int64_t step, int decoupled,
+                           const double* clip_total_dev, double max_norm, double clip_eps,
+                           void* stream);
+
 int tg_adam_update(int dtype, int64_t n, void* p, const void* g, void* m, void* v, double lr,
                    double beta1, double beta2, double eps, double weight_decay, int64_t step,
                    int decoupled, void* stream) {
+  return tg_adam_update_clipped(dtype, n, p, g, m, v, lr, beta1, beta2, eps, weight_decay, step,
+                                decoupled, nullptr, 0.0, 0.0, stream);
+}
+
+int tg_adam_update_clipped(int dtype, int64_t n, void* p, const void* g, void* m, void* v,
+                           double lr, double beta1, double beta2, double eps,
+                           double weight_decay, int64_t step, int decoupled,
+                           const double* clip_total_dev, double max_norm, double clip_eps,
+                           void* stream) {
   TG_CHECK_ARG(step >= 1, "adam_update: step must be >= 1");
+  const ClipFactor clip{clip_total_dev, max_norm, clip_eps};
   if (n <= 0) return TG_OK;
   cudaStream_t s = as_stream(stream);
   const double ss = lr / (1.0 - pow(beta1, (double)step));
@@ -207,7 +247,7 @@ int tg_adam_update(int dtype, int64_t n, void* p, const void* g, void* m, void* 
       aligned16(v)) {
     adam_flat_vec4_kernel<<<grid_for(n / 4, 256), 256, 0, s>>>(
         n / 4, (float4*)p, (const float4*)g, (float4*)m, (float4*)v, (float)beta1,
-        (float)beta2, (float)eps, (float)decay, (float)l2, (float)ss, (float)bs);
+        (float)beta2, (float)eps, (float)decay, (float)l2, (float)ss, (float)bs, clip);
     return check_launch("adam_update");
   }
   return TG_DISPATCH_FLOAT(dtype, T, [&] {
@@ -216,7 +256,7 @@ int tg_adam_update(int dtype, int64_t n, void* p, const void* g, void* m, void* 
     L.p[0] = p; L.g[0] = g; L.m[0] = m; L.v[0] = v; L.numel[0] = n;
     L.step_size[0] = ss; L.bc2_sqrt[0] = bs;
     adam_multi_kernel<T><<<grid_for(n, 256), 256, 0, s>>>(L, (T)beta1, (T)beta2, (T)eps,
-                                                          (T)decay, (T)l2);
+                                                          (T)decay, (T)l2, clip);
     return check_launch("adam_update");
   });
 }

@@ -161,6 +161,8 @@ class GradientAllReduce:
             self._remove = autograd.add_leaf_hook(lambda t: self.buckets.ready(id(t)))
 
     def reduce(self) -> None:
+        for arena in self.arenas:
+            arena.settle_clip()
         self.buckets.finish()
 
     def close(self) -> None:

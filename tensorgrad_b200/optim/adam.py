@@ -93,11 +93,15 @@ class Adam(Optimizer[_AdamState]):
                 for st in states:
                     st.step += 1
                 m_buf, v_buf = self._moments[id(arena)]
-                check(lib.tg_adam_update(dtype_code(arena.dtype), arena.numel,
-                                         arena.param_buf.ptr, arena.grad_buf.ptr, m_buf.ptr,
-                                         v_buf.ptr, group.lr, b1, b2, self.eps, wd,
-                                         states[0].step, int(self.decoupled_weight_decay),
-                                         device.stream()), "adam step")
+                # A clip rescale left pending by clip_grad_norm_ is applied in the same pass
+                # (and stays pending on the gradients themselves).
+                clip = arena.pending_clip
+                check(lib.tg_adam_update_clipped(
+                    dtype_code(arena.dtype), arena.numel, arena.param_buf.ptr,
+                    arena.grad_buf.ptr, m_buf.ptr, v_buf.ptr, group.lr, b1, b2, self.eps, wd,
+                    states[0].step, int(self.decoupled_weight_decay),
+                    clip[0].ptr if clip else None, clip[1] if clip else 0.0,
+                    clip[2] if clip else 0.0, device.stream()), "adam step")
                 continue
             by_dtype: dict[str, list[tuple[Tensor, DeviceArray, _AdamState]]] = {}
             for p in group.params:
@@ -118,6 +122,77 @@ class Adam(Optimizer[_AdamState]):
                     int64_array(p.size for p, _, _ in items),
                     int64_array(s.step for _, _, s in items), group.lr, b1, b2, self.eps, wd,
                     int(self.decoupled_weight_decay), None, device.stream()), "adam step")
+
+
+    # ------------------------------------------------------------------ checkpoints
+    # No counterpart in the reference, which cannot save optimizer state (README.md:231-232).
+    # Keys: "group.{g}.lr" / "group.{g}.weight_decay", "betas", "eps", and per parameter with
+    # state (index i over all groups in order) "state.{i}.step", "state.{i}.exp_avg",
+    # "state.{i}.exp_avg_sq". Moments held in an arena come to the host in one copy each.
+    def _indexed_params(self) -> list[Tensor]:
+        return [p for group in self.param_groups for p in group.params]
+
+    def state_dict(self) -> dict[str, Any]:
+        import numpy as np
+
+        out: dict[str, Any] = {"betas": np.asarray(self.betas, np.float64),
+                               "eps": np.asarray(self.eps, np.float64)}
+        for g, group in enumerate(self.param_groups):
+            out[f"group.{g}.lr"] = np.asarray(group.lr, np.float64)
+            out[f"group.{g}.weight_decay"] = np.asarray(group.weight_decay, np.float64)
+        host_moments: dict[int, tuple[Any, Any]] = {}
+        for i, p in enumerate(self._indexed_params()):
+            st = self.state.get(id(p))
+            if st is None:
+                continue
+            arena = getattr(p, "_arena", None)
+            key = id(arena)
+            if arena is not None and key in self._moments and arena.intact():
+                if key not in host_moments:
+                    host_moments[key] = tuple(b.numpy() for b in self._moments[key])
+                m_host, v_host = host_moments[key]
+                off = arena.offsets[arena.index[id(p)]]
+                m_buf, _ = self._moments[key]
+                if st.exp_avg.ptr == m_buf.ptr + off * arena.dtype.itemsize:
+                    m = m_host[off:off + p.size].reshape(p.shape).copy()
+                    v = v_host[off:off + p.size].reshape(p.shape).copy()
+                else:
+                    m, v = st.exp_avg.numpy(), st.exp_avg_sq.numpy()
+            else:
+                m, v = st.exp_avg.numpy(), st.exp_avg_sq.numpy()
+            out[f"state.{i}.step"] = np.asarray(st.step, np.int64)
+            out[f"state.{i}.exp_avg"] = m
+            out[f"state.{i}.exp_avg_sq"] = v
+        return out
+
+    def load_state_dict(self, state: Any) -> None:
+        """Restore moments, step counts and hyper-parameters saved by :meth:`state_dict`."""
+        import numpy as np
+
+        params = self._indexed_params()
+        for g, group in enumerate(self.param_groups):
+            if f"group.{g}.lr" in state:
+                group.lr = float(state[f"group.{g}.lr"])
+            if f"group.{g}.weight_decay" in state:
+                group.weight_decay = float(state[f"group.{g}.weight_decay"])
+        if "betas" in state:
+            b = np.asarray(state["betas"], np.float64)
+            self.betas = (float(b[0]), float(b[1]))
+        if "eps" in state:
+            self.eps = float(state["eps"])
+        indices = sorted({int(k.split(".")[1]) for k in state if k.startswith("state.")})
+        for i in indices:
+            if not 0 <= i < len(params):
+                raise KeyError(f"optimizer state for parameter {i}, which does not exist")
+            p = params[i]
+            st = self._state_for(p)
+            for name, buf in (("exp_avg", st.exp_avg), ("exp_avg_sq", st.exp_avg_sq)):
+                value = np.asarray(state[f"state.{i}.{name}"])
+                if value.shape != tuple(p.shape):
+                    raise ValueError(f"shape mismatch for 'state.{i}.{name}': expected "
+                                     f"{tuple(p.shape)}, got {value.shape}")
+                buf[...] = value
+            st.step = int(state[f"state.{i}.step"])
 
 
 class AdamW(Adam):

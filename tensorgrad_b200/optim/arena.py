@@ -51,6 +51,24 @@ class Arena:
                 device.copy_into(p._grad_slot, p._grad.data.astype(self.dtype, copy=False))
                 p._grad = Tensor._wrap(p._grad_slot)
             p._arena = self  # type: ignore[attr-defined]
+        # A clip_grad_norm_ rescale not yet written into grad_buf: (total norm as a float64
+        # device scalar, max_norm, eps). AdamW applies it inside its update pass; anything
+        # else that reads or adds to the gradients first calls settle_clip().
+        self.pending_clip: tuple[DeviceArray, float, float] | None = None
+
+    def settle_clip(self) -> None:
+        """Write a pending clip rescale into the gradient buffer (the reference's in-place
+        ``g *= scale``), so that the gradients read as clipped."""
+        pend = self.pending_clip
+        if pend is None:
+            return
+        self.pending_clip = None
+        from tensorgrad_b200._lib import check, int64_array, lib, ptr_array
+
+        total, max_norm, eps = pend
+        check(lib.tg_clip_scale_multi(device.dtype_code(self.dtype), 1,
+                                      ptr_array([self.grad_buf.ptr]), int64_array([self.numel]),
+                                      total.ptr, max_norm, eps, None, device.stream()), "clip")
 
     def intact(self) -> bool:
         """Every parameter still lives in its slot (nobody re-assigned ``p.data``)."""

@@ -2,9 +2,12 @@
 
 The global L2 norm is accumulated in float64 over all gradients (one launch for a flat
 arena, or a multi-tensor launch), and the rescale ``g *= max_norm / (total + eps)`` (the
-factor rounded to the gradient dtype, as the reference casts it) runs only when that
-factor is below 1, decided on the device. Returning the norm as a Python float reads 8 bytes
-back, which synchronises the stream once per call.
+factor rounded to the gradient dtype, as the reference casts it) applies only when that
+factor is below 1, decided on the device. For a flat arena the rescale is left pending:
+AdamW's update pass reads the gradients rescaled (clip and update in one pass), and any
+other reader of a gradient writes the rescale first, so the gradients always read as the
+reference's clipped ones. Returning the norm as a Python float reads 8 bytes back, which
+synchronises the stream once per call.
 """
 
 from __future__ import annotations
@@ -26,6 +29,7 @@ def _segments(params: list[Tensor]) -> dict[str, list[DeviceArray]]:
     """Gradient buffers to reduce, per dtype: the whole flat arena when it is exact."""
     arena = arena_of(params)
     if arena is not None and arena.grads_in_slots():
+        arena.settle_clip()
         return {str(arena.dtype): [arena.grad_buf]}
     out: dict[str, list[DeviceArray]] = {}
     for p in params:
@@ -72,7 +76,16 @@ def clip_grad_norm_(params: Iterable[Tensor], max_norm: float, eps: float = 1e-6
     Returns:
         The total norm before clipping.
     """
+    params = list(params)
     total, segs = grad_norm_device(params)
+    arena = arena_of(params)
+    if (arena is not None and len(segs) == 1
+            and next(iter(segs.values()))[0] is arena.grad_buf):
+        # One flat arena: the rescale stays pending, and AdamW's update pass applies it while
+        # it reads the gradients (one pass over them instead of two); reading a gradient
+        # first writes it.
+        arena.pending_clip = (total, float(max_norm), float(eps))
+        segs = {}
     for bufs in segs.values():
         code = dtype_code(bufs[0].dtype)
         check(lib.tg_clip_scale_multi(code, len(bufs), ptr_array(b.ptr for b in bufs),

@@ -69,8 +69,15 @@ class Optimizer(ABC, Generic[StateT]):
 
     def zero_grad(self) -> None:
         """Reset the gradient of every managed parameter (``grad = None``)."""
+        cleared = {id(p) for group in self.param_groups for p in group.params}
         for group in self.param_groups:
             for p in group.params:
+                arena = p._arena
+                # A clip rescale still pending on gradients that are all being dropped
+                # needs no writing.
+                if (arena is not None and arena.pending_clip is not None
+                        and all(id(q) in cleared for q in arena.params)):
+                    arena.pending_clip = None
                 p.grad = None
 
     @abstractmethod

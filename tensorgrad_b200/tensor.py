@@ -130,10 +130,14 @@ class Tensor:
 
     @property
     def grad(self) -> Tensor | None:
+        if self._arena is not None and self._arena.pending_clip is not None:
+            self._arena.settle_clip()
         return self._grad
 
     @grad.setter
     def grad(self, value: Any) -> None:
+        if self._arena is not None and self._arena.pending_clip is not None:
+            self._arena.settle_clip()
         if value is not None:
             if isinstance(value, DeviceArray):
                 value = Tensor._wrap(value)
@@ -189,6 +193,8 @@ class Tensor:
         slot = self._grad_slot
         if slot is not None:
             # The gradient lives in a flat arena (optimizer / data-parallel bucket).
+            if self._arena is not None and self._arena.pending_clip is not None:
+                self._arena.settle_clip()
             from tensorgrad_b200.ops.elementwise import binary_array
 
             cur = self._grad

@@ -379,6 +379,50 @@ def test_clip_and_adamw_match_reference(dtype):
             assert_parity(p.numpy(), r, rel(dtype), f"param step {step}")
 
 
+def test_fused_clip_and_adamw_equal_the_separate_passes(dtype):
+    # clip_grad_norm_ on a flat arena leaves its rescale pending and AdamW applies it inside
+    # its update pass; reading the gradients before the step writes the rescale first. Both
+    # orders must give the same parameters, moments and gradients bit for bit, and match the
+    # float64 reference.
+    import tensorgrad_b200 as tg
+
+    rng = np.random.default_rng(31)
+    shapes = [(33, 7), (128,), (5, 4, 3)]
+    ps = [rng.standard_normal(s) for s in shapes]
+    gs = [rng.standard_normal(s) for s in shapes]
+    runs = []
+    for read_grads_first in (True, False):
+        params = [tg.nn.Parameter(p.astype(dtype)) for p in ps]
+        opt = tg.optim.AdamW(params, lr=1e-2, weight_decay=0.1)
+        for step in (1, 2):
+            opt.zero_grad()
+            for p, g in zip(params, gs, strict=True):
+                # Accumulate through the engine, as a backward pass does.
+                p._accumulate_grad(tg.Tensor(g.astype(dtype) * step).data)
+            total = tg.optim.clip_grad_norm_(params, 0.5)
+            grads = [p.grad.numpy() for p in params] if read_grads_first else None
+            opt.step()
+            if not read_grads_first:
+                grads = [p.grad.numpy() for p in params]
+        runs.append((total, grads, [p.numpy() for p in params]))
+    (t1, g1, p1), (t2, g2, p2) = runs
+    assert t1 == t2
+    for a, b in zip(g1 + p1, g2 + p2, strict=True):
+        np.testing.assert_array_equal(a, b)
+    ref_p = list(ps)
+    ref_m, ref_v = [np.zeros_like(p) for p in ps], [np.zeros_like(p) for p in ps]
+    for step in (1, 2):
+        _, clipped = O.clip_grad_norm([g * step for g in gs], 0.5)
+        for i in range(len(ps)):
+            ref_p[i], ref_m[i], ref_v[i] = O.adamw_update(ref_p[i], clipped[i], ref_m[i],
+                                                          ref_v[i], step, 1e-2, (0.9, 0.999),
+                                                          1e-8, 0.1)
+    for got, ref in zip(p2, ref_p, strict=True):
+        assert_parity(got, ref, rel(dtype), "params after fused clip + AdamW")
+    for got, ref in zip(g2, clipped, strict=True):
+        assert_parity(got, ref, rel(dtype), "clipped gradients read after the step")
+
+
 def test_adam_state_is_per_parameter():
     import tensorgrad_b200 as tg
 
