@@ -171,6 +171,17 @@ int tg_relu_backward(int dtype, int64_t n, const void* g, const void* x, void* g
 int tg_unary_backward(int dtype, int op, int64_t n, const void* g, const void* x, const void* y,
                       double alpha, void* gx, void* stream);
 
+/* Inverted dropout (ops/layers.py:235-259; attention weights, ops/attention.py:59-68) with
+ * the reference's keep-mask (_random.py:53-70) generated on the device: y[i] = x[i] * m,
+ * m = scale if 16-bit word (first_element + i) of the PCG64 stream is >= threshold, else 0.
+ * pcg_state = {state_hi, state_lo, inc_hi, inc_lo}: NumPy's PCG64 state before the mask's
+ * first draw; word e is bits [16 (e % 4), 16 (e % 4) + 16) of the stream's 64-bit output
+ * e / 4 (0-based), exactly as keep_mask views random_raw(). The same call with the same
+ * state on the upstream gradient is the VJP. The caller advances its generator past the
+ * ceil(n_total / 4) outputs the whole mask consumes. threshold = round(p * 65536). */
+int tg_dropout_pcg64(int dtype, int64_t n, const void* x, void* y, const uint64_t* pcg_state,
+                     int64_t first_element, uint32_t threshold, double scale, void* stream);
+
 /* ------------------------------------------------------------------ layer norm
  * ops/layers.py:65-141. Per row of `cols`: mean, rstd = 1/sqrt(var + eps) (biased var),
  * y = (x - mean) * rstd * w + b; w/b may be NULL. mean/rstd[rows] are saved for backward. */
@@ -274,6 +285,25 @@ size_t tg_attention_backward_scratch_bytes(int dtype, const tg_attn_shape* s);
 int tg_attention_backward(int dtype, const tg_attn_shape* s, const void* q, const void* k,
                           const void* v, const void* o, const void* lse, const void* dout,
                           void* dq, void* dk, void* dv, void* scratch, void* stream);
+
+/* Attention with dropout on the attention weights (ops/attention.py:59-116 with dropout_p >
+ * 0 in training): the reference's keep-mask over the whole (B, H, tq, tk) probability array
+ * (element ((b H + h) tq + i) tk + j uses 16-bit word of that index of the PCG64 stream whose
+ * state before the draw is pcg_state, as tg_dropout_pcg64), regenerated by the VJP rather
+ * than stored. Weights W = P * (keep ? keep_scale : 0); O = W V; the VJP is the reference's
+ * attention_backward with the mask applied to dW = dO V^T. fp32 and float64; the products
+ * are the library's batched GEMMs, the probabilities live in `scratch`
+ * (tg_attention_dropout_scratch_bytes, the same for both directions) for the call. */
+size_t tg_attention_dropout_scratch_bytes(int dtype, const tg_attn_shape* s);
+int tg_attention_forward_dropout(int dtype, const tg_attn_shape* s, const void* q, const void* k,
+                                 const void* v, void* o, void* lse, const uint64_t* pcg_state,
+                                 uint32_t threshold, double keep_scale, void* scratch,
+                                 void* stream);
+int tg_attention_backward_dropout(int dtype, const tg_attn_shape* s, const void* q,
+                                  const void* k, const void* v, const void* dout, void* dq,
+                                  void* dk, void* dv, const uint64_t* pcg_state,
+                                  uint32_t threshold, double keep_scale, void* scratch,
+                                  void* stream);
 
 /* ------------------------------------------------------------------ convolution / pooling
  * conv2d (ops/conv.py:128-177): cross-correlation of x (n, c, h, w) with w (c_out, c, kh, kw)

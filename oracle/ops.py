@@ -125,10 +125,25 @@ def causal_forbidden(q_len: int, k_len: int) -> np.ndarray:
     return np.triu(np.ones((q_len, k_len), dtype=np.bool_), k=1 + k_len - q_len)
 
 
+def keep_mask(shape: tuple[int, ...], p: float,
+              rng: np.random.Generator) -> tuple[np.ndarray, float]:
+    """The reference's dropout keep-mask (_random.py:53-70): threshold ``t = round(p 2^16)``;
+    16-bit words from ``random_raw(ceil(n / 4))`` viewed as uint16; keep where ``word >= t``;
+    survivors scale by ``2^16 / (2^16 - t)``; all dropped (no draw) when ``t >= 2^16``."""
+    t = round(p * 65536)
+    if t >= 65536:
+        return np.zeros(shape, dtype=np.bool_), 0.0
+    n = int(np.prod(shape))
+    words = rng.bit_generator.random_raw((n + 3) // 4).view(np.uint16)[:n]
+    return (words >= t).reshape(shape), 65536.0 / (65536 - t)
+
+
 def attention_forward(
-    q: np.ndarray, k: np.ndarray, v: np.ndarray, causal: bool
+    q: np.ndarray, k: np.ndarray, v: np.ndarray, causal: bool,
+    keep: np.ndarray | None = None, keep_scale: float = 1.0,
 ) -> tuple[np.ndarray, np.ndarray]:
-    """``(out, probs)`` of ``softmax(q k^T / sqrt(d) + mask) v`` (ops/attention.py:71-88)."""
+    """``(out, probs)`` of ``softmax(q k^T / sqrt(d) + mask) v`` (ops/attention.py:71-88);
+    with a dropout ``keep`` mask the weights are ``probs * keep * keep_scale``."""
     scale = 1.0 / math.sqrt(q.shape[-1])
     s = (q @ np.swapaxes(k, -1, -2)) * scale
     if causal:
@@ -137,17 +152,23 @@ def attention_forward(
     m = np.where(np.isfinite(m), m, 0.0)
     p = np.exp(s - m)
     p /= p.sum(axis=-1, keepdims=True)
-    return p @ v, p
+    w = p if keep is None else p * keep * keep_scale
+    return w @ v, p
 
 
 def attention_backward(
-    g: np.ndarray, q: np.ndarray, k: np.ndarray, v: np.ndarray, p: np.ndarray
+    g: np.ndarray, q: np.ndarray, k: np.ndarray, v: np.ndarray, p: np.ndarray,
+    keep: np.ndarray | None = None, keep_scale: float = 1.0,
 ) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
-    """``(dq, dk, dv)``: ``dV = P^T g``, ``dS = P (g V^T - rowsum(g V^T P)) / sqrt(d)``,
-    ``dQ = dS K``, ``dK = dS^T Q`` (ops/attention.py:91-116)."""
+    """``(dq, dk, dv)``: ``dV = W^T g`` (``W`` the dropped-out weights), ``dP' = g V^T``
+    masked like ``W``, ``dS = P (dP' - rowsum(dP' P)) / sqrt(d)``, ``dQ = dS K``,
+    ``dK = dS^T Q`` (ops/attention.py:91-116)."""
     scale = 1.0 / math.sqrt(q.shape[-1])
-    dv = np.swapaxes(p, -1, -2) @ g
+    w = p if keep is None else p * keep * keep_scale
+    dv = np.swapaxes(w, -1, -2) @ g
     ds = g @ np.swapaxes(v, -1, -2)
+    if keep is not None:
+        ds = ds * keep * keep_scale
     ds = (ds - (ds * p).sum(axis=-1, keepdims=True)) * p * scale
     return ds @ k, np.swapaxes(ds, -1, -2) @ q, dv
 

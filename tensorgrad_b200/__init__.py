@@ -20,7 +20,7 @@ from tensorgrad_b200.tensor import (
     tensor, zeros, zeros_like,
 )
 
-from tensorgrad_b200 import nn, optim  # noqa: E402  (after the ops they use)
+from tensorgrad_b200 import nn, optim, utils  # noqa: E402  (after the ops they use)
 
 __version__ = "0.1.0"
 
@@ -39,5 +39,5 @@ __all__ = [
     "mean", "min", "mse_loss", "mul", "neg", "nn", "no_grad", "ones", "ones_like", "optim",
     "permute", "pow", "profiler", "rand", "randn", "relu", "reshape", "set_default_dtype",
     "set_device", "sigmoid", "sqrt", "squeeze", "stack", "sub", "sum", "synchronize", "tanh", "tensor",
-    "transpose", "unsqueeze", "var", "zeros", "zeros_like",
+    "transpose", "unsqueeze", "utils", "var", "zeros", "zeros_like",
 ]

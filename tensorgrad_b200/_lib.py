@@ -94,6 +94,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tg_gelu_backward": (c_int, [c_int, i64, vp, vp, vp, vp]),
     "tg_relu_backward": (c_int, [c_int, i64, vp, vp, vp, vp]),
     "tg_unary_backward": (c_int, [c_int, c_int, i64, vp, vp, vp, dbl, vp, vp]),
+    "tg_dropout_pcg64": (c_int, [c_int, i64, vp, vp, POINTER(ctypes.c_uint64), i64, ctypes.c_uint32,
+                                 dbl, vp]),
     "tg_layer_norm_forward": (c_int, [c_int, vp, vp, vp, vp, vp, vp, i64, i64, dbl, vp]),
     "tg_layer_norm_scratch_bytes": (sz, [c_int, i64, i64]),
     "tg_layer_norm_backward": (c_int, [c_int, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, u32, vp,
@@ -114,6 +116,13 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tg_attention_backward_scratch_bytes": (sz, [c_int, POINTER(AttnShape)]),
     "tg_attention_backward": (c_int, [c_int, POINTER(AttnShape), vp, vp, vp, vp, vp, vp, vp, vp,
                                       vp, vp, vp]),
+    "tg_attention_dropout_scratch_bytes": (sz, [c_int, POINTER(AttnShape)]),
+    "tg_attention_forward_dropout": (c_int, [c_int, POINTER(AttnShape), vp, vp, vp, vp, vp,
+                                             POINTER(ctypes.c_uint64), ctypes.c_uint32, dbl, vp,
+                                             vp]),
+    "tg_attention_backward_dropout": (c_int, [c_int, POINTER(AttnShape), vp, vp, vp, vp, vp, vp,
+                                              vp, POINTER(ctypes.c_uint64), ctypes.c_uint32, dbl,
+                                              vp, vp]),
     "tg_conv2d_cols_shape": (c_int, [POINTER(ConvShape), pi64, pi64]),
     "tg_conv2d_forward_scratch_bytes": (sz, [c_int, POINTER(ConvShape)]),
     "tg_conv2d_forward": (c_int, [c_int, POINTER(ConvShape), vp, vp, vp, vp, vp, vp, vp]),

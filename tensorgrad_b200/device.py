@@ -427,6 +427,26 @@ def copy_into(dst: DeviceArray, src: DeviceArray) -> None:
         check(lib.tg_memcpy_d2d(dst.ptr, src.ptr, src.nbytes, _State.stream), "d2d")
 
 
+def numpy_many(arrays: Sequence[DeviceArray]) -> list[np.ndarray]:
+    """Host copies of several device arrays with one synchronisation: every copy is queued
+    into one page-locked staging block (16-byte aligned slots), then the stream is waited on
+    once and the slots are unpacked into ordinary arrays."""
+    offsets, total = [], 0
+    for a in arrays:
+        offsets.append(total)
+        total += -(-a.nbytes // 16) * 16
+    if not arrays:
+        return []
+    staging = torch.empty(max(total, 16), dtype=torch.uint8, pin_memory=True).numpy()
+    base = staging.ctypes.data
+    for a, off in zip(arrays, offsets, strict=True):
+        if a.nbytes:
+            check(lib.tg_memcpy_d2h(base + off, a.ptr, a.nbytes, _State.stream), "d2h")
+    synchronize()
+    return [staging[off:off + a.nbytes].view(a.dtype).reshape(a.shape).copy()
+            for a, off in zip(arrays, offsets, strict=True)]
+
+
 def scalar_like(value: Any, dtype: np.dtype[Any]) -> DeviceArray:
     return from_numpy(np.asarray(value, dtype=dtype))
 

@@ -1,7 +1,9 @@
-"""In-place parameter initialisers (the reference's nn/init.py:16-59).
+"""In-place initialisers for device parameters (API of the reference's nn/init.py).
 
-Values are drawn on the host from the global generator in the reference's order and
-uploaded, so a seeded model starts from the same weights as the reference's.
+Random values come from the global host generator with the NumPy call the reference's
+initialiser makes (``uniform(low, high, size)`` / ``normal(mean, std, size)``), so seeded
+initialisation matches the reference draw for draw; they are uploaded into the parameter's
+device storage in one copy. Constant fills run on the device.
 """
 
 from __future__ import annotations
@@ -19,20 +21,24 @@ __all__ = ["calculate_fans", "kaiming_uniform_", "normal_", "ones_", "uniform_",
 
 
 def calculate_fans(t: Tensor) -> tuple[int, int]:
+    """``(fan_in, fan_out)`` of a weight laid out ``(out, in, *kernel)``."""
     if t.ndim < 2:
         raise ValueError("fans are defined for tensors with at least 2 dimensions")
-    receptive = math.prod(t.shape[2:])
-    return t.shape[1] * receptive, t.shape[0] * receptive
+    kernel = math.prod(t.shape[2:])
+    return t.shape[1] * kernel, t.shape[0] * kernel
+
+
+def _fill(t: T, values) -> T:  # noqa: ANN001
+    t.data[...] = values
+    return t
 
 
 def uniform_(t: T, low: float = 0.0, high: float = 1.0) -> T:
-    t.data[...] = get_rng().uniform(low, high, size=t.shape)
-    return t
+    return _fill(t, get_rng().uniform(low, high, size=t.shape))
 
 
 def normal_(t: T, mean: float = 0.0, std: float = 1.0) -> T:
-    t.data[...] = get_rng().normal(mean, std, size=t.shape)
-    return t
+    return _fill(t, get_rng().normal(mean, std, size=t.shape))
 
 
 def zeros_(t: T) -> T:
@@ -46,13 +52,13 @@ def ones_(t: T) -> T:
 
 
 def xavier_uniform_(t: T, gain: float = 1.0) -> T:
+    """``U(-a, a)``, ``a = gain sqrt(6 / (fan_in + fan_out))``."""
     fan_in, fan_out = calculate_fans(t)
-    bound = gain * math.sqrt(6.0 / (fan_in + fan_out))
-    return uniform_(t, -bound, bound)
+    a = gain * math.sqrt(6.0 / (fan_in + fan_out))
+    return uniform_(t, -a, a)
 
 
 def kaiming_uniform_(t: T, nonlinearity_gain: float = math.sqrt(2.0)) -> T:
-    fan_in, _ = calculate_fans(t)
-    bound = nonlinearity_gain * math.sqrt(3.0 / fan_in)
-    return uniform_(t, -bound, bound)
-
+    """``U(-a, a)``, ``a = gain sqrt(3 / fan_in)``."""
+    a = nonlinearity_gain * math.sqrt(3.0 / calculate_fans(t)[0])
+    return uniform_(t, -a, a)

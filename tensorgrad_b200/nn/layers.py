@@ -1,16 +1,21 @@
-"""Standard layers (the reference's nn/layers.py:42-341) on device tensors."""
+"""Standard layers on device tensors (API of the reference's nn/layers.py:42-341).
+
+Trainable tensors are created straight from their initial values: each draw is taken on the
+host from the global generator, in the order and with the NumPy call the reference's
+initialiser makes (so a seeded model starts from the reference's weights), and uploaded once.
+Layers without parameters are thin adaptors over a functional op.
+"""
 
 from __future__ import annotations
 
-import itertools
 import math
-from collections.abc import Iterator, Sequence
+from collections.abc import Callable, Iterator, Sequence
 from typing import Any, Literal
 
 import numpy as np
 
 from tensorgrad_b200 import ops
-from tensorgrad_b200.nn import init
+from tensorgrad_b200._random import get_rng
 from tensorgrad_b200.nn.module import Module, Parameter
 from tensorgrad_b200.tensor import Tensor, get_default_dtype
 
@@ -19,22 +24,28 @@ __all__ = ["GELU", "MLP", "BatchNorm1d", "BatchNorm2d", "Conv2d", "Dropout", "Em
            "Sigmoid", "Tanh"]
 
 
-def _empty(*shape: int) -> Parameter:
-    return Parameter(np.zeros(shape, dtype=get_default_dtype()))
+def _param(values: np.ndarray) -> Parameter:
+    return Parameter(np.asarray(values, dtype=get_default_dtype()))
+
+
+def _uniform(shape: tuple[int, ...], bound: float) -> Parameter:
+    """U(-bound, bound) in the default dtype (init.uniform_'s draw)."""
+    return _param(get_rng().uniform(-bound, bound, size=shape))
+
+
+def _constant(shape: tuple[int, ...], value: float) -> Parameter:
+    return _param(np.full(shape, value))
 
 
 class Linear(Module):
-    """``y = x W^T + b``; init ``U(-1/sqrt(in), 1/sqrt(in))`` (nn/layers.py:42-62)."""
+    """``y = x W^T + b`` with weight and bias from ``U(-1/sqrt(in), 1/sqrt(in))``."""
 
     def __init__(self, in_features: int, out_features: int, bias: bool = True) -> None:
         super().__init__()
-        self.in_features = in_features
-        self.out_features = out_features
+        self.in_features, self.out_features = in_features, out_features
         bound = 1.0 / math.sqrt(in_features)
-        self.weight = init.uniform_(_empty(out_features, in_features), -bound, bound)
-        self.bias: Parameter | None = (
-            init.uniform_(_empty(out_features), -bound, bound) if bias else None
-        )
+        self.weight = _uniform((out_features, in_features), bound)
+        self.bias: Parameter | None = _uniform((out_features,), bound) if bias else None
 
     def forward(self, x: Tensor) -> Tensor:
         return ops.linear(x, self.weight, self.bias)
@@ -44,23 +55,17 @@ class Linear(Module):
 
 
 class Conv2d(Module):
-    """2-D convolution over ``(N, C, H, W)`` (nn/layers.py:65-98)."""
+    """Cross-correlation of ``(N, C, H, W)`` inputs with square kernels; weight and bias from
+    ``U(-1/sqrt(fan_in), 1/sqrt(fan_in))``, ``fan_in = C k k``."""
 
     def __init__(self, in_channels: int, out_channels: int, kernel_size: int, stride: int = 1,
                  padding: int = 0, bias: bool = True) -> None:
         super().__init__()
-        self.in_channels = in_channels
-        self.out_channels = out_channels
-        self.kernel_size = kernel_size
-        self.stride = stride
-        self.padding = padding
+        self.in_channels, self.out_channels = in_channels, out_channels
+        self.kernel_size, self.stride, self.padding = kernel_size, stride, padding
         bound = 1.0 / math.sqrt(in_channels * kernel_size * kernel_size)
-        self.weight = init.uniform_(
-            _empty(out_channels, in_channels, kernel_size, kernel_size), -bound, bound
-        )
-        self.bias: Parameter | None = (
-            init.uniform_(_empty(out_channels), -bound, bound) if bias else None
-        )
+        self.weight = _uniform((out_channels, in_channels, kernel_size, kernel_size), bound)
+        self.bias: Parameter | None = _uniform((out_channels,), bound) if bias else None
 
     def forward(self, x: Tensor) -> Tensor:
         from tensorgrad_b200.ops.conv import conv2d
@@ -73,13 +78,11 @@ class Conv2d(Module):
 
 
 class MaxPool2d(Module):
-    """Max pooling over ``(N, C, H, W)`` (nn/layers.py:101-114)."""
+    """Window maxima over ``(N, C, H, W)``; the stride defaults to the window."""
 
     def __init__(self, kernel_size: int, stride: int | None = None, padding: int = 0) -> None:
         super().__init__()
-        self.kernel_size = kernel_size
-        self.stride = stride
-        self.padding = padding
+        self.kernel_size, self.stride, self.padding = kernel_size, stride, padding
 
     def forward(self, x: Tensor) -> Tensor:
         from tensorgrad_b200.ops.conv import max_pool2d
@@ -91,13 +94,12 @@ class MaxPool2d(Module):
 
 
 class Embedding(Module):
-    """Lookup table, init ``N(0, 1)`` (nn/layers.py:117-130)."""
+    """Rows of a ``(num, dim)`` table from ``N(0, 1)``, gathered by integer ids."""
 
     def __init__(self, num_embeddings: int, embedding_dim: int) -> None:
         super().__init__()
-        self.num_embeddings = num_embeddings
-        self.embedding_dim = embedding_dim
-        self.weight = init.normal_(_empty(num_embeddings, embedding_dim))
+        self.num_embeddings, self.embedding_dim = num_embeddings, embedding_dim
+        self.weight = _param(get_rng().normal(0.0, 1.0, size=(num_embeddings, embedding_dim)))
 
     def forward(self, indices: Any) -> Tensor:
         return ops.embedding(indices, self.weight)
@@ -107,18 +109,16 @@ class Embedding(Module):
 
 
 class LayerNorm(Module):
-    """Layer normalisation over the last axis (nn/layers.py:133-152)."""
+    """Normalisation over the last axis with an optional affine map (scale 1, shift 0)."""
 
     def __init__(self, normalized_shape: int, eps: float = 1e-5,
                  elementwise_affine: bool = True) -> None:
         super().__init__()
-        self.normalized_shape = normalized_shape
-        self.eps = eps
-        self.weight: Parameter | None = None
-        self.bias: Parameter | None = None
-        if elementwise_affine:
-            self.weight = init.ones_(_empty(normalized_shape))
-            self.bias = init.zeros_(_empty(normalized_shape))
+        self.normalized_shape, self.eps = normalized_shape, eps
+        self.weight: Parameter | None = (
+            _constant((normalized_shape,), 1.0) if elementwise_affine else None)
+        self.bias: Parameter | None = (
+            _constant((normalized_shape,), 0.0) if elementwise_affine else None)
 
     def forward(self, x: Tensor) -> Tensor:
         if x.shape[-1] != self.normalized_shape:
@@ -130,31 +130,26 @@ class LayerNorm(Module):
 
 
 class _BatchNorm(Module):
-    """Batch normalisation with running statistics (nn/layers.py:155-214)."""
+    """Batch statistics over every axis but the channel axis 1 in training (running mean and
+    unbiased variance updated with ``momentum``), running statistics in evaluation."""
 
-    _layouts: tuple[int, ...] = ()
-    _layout_names = ""
+    ranks: tuple[int, ...] = ()
+    layout = ""
 
     def __init__(self, num_features: int, eps: float = 1e-5, momentum: float = 0.1,
                  affine: bool = True) -> None:
         super().__init__()
-        self.num_features = num_features
-        self.eps = eps
-        self.momentum = momentum
-        self.weight: Parameter | None = None
-        self.bias: Parameter | None = None
-        if affine:
-            self.weight = init.ones_(_empty(num_features))
-            self.bias = init.zeros_(_empty(num_features))
-        self.register_buffer("running_mean", np.zeros(num_features, dtype=get_default_dtype()))
-        self.register_buffer("running_var", np.ones(num_features, dtype=get_default_dtype()))
+        self.num_features, self.eps, self.momentum = num_features, eps, momentum
+        self.weight: Parameter | None = _constant((num_features,), 1.0) if affine else None
+        self.bias: Parameter | None = _constant((num_features,), 0.0) if affine else None
+        dt = get_default_dtype()
+        self.register_buffer("running_mean", np.zeros(num_features, dtype=dt))
+        self.register_buffer("running_var", np.ones(num_features, dtype=dt))
 
     def forward(self, x: Tensor) -> Tensor:
-        if x.ndim not in self._layouts or x.shape[1] != self.num_features:
-            raise ValueError(
-                f"{type(self).__name__}({self.num_features}) expects "
-                f"{self._layout_names} input, got {x.shape}"
-            )
+        if x.ndim not in self.ranks or x.shape[1] != self.num_features:
+            raise ValueError(f"{type(self).__name__}({self.num_features}) expects {self.layout} "
+                             f"input, got {x.shape}")
         return ops.batch_norm(x, self.running_mean, self.running_var, self.weight, self.bias,
                               training=self.training, momentum=self.momentum, eps=self.eps)
 
@@ -163,17 +158,15 @@ class _BatchNorm(Module):
 
 
 class BatchNorm1d(_BatchNorm):
-    _layouts = (2, 3)
-    _layout_names = "(N, C) or (N, C, L)"
+    ranks, layout = (2, 3), "(N, C) or (N, C, L)"
 
 
 class BatchNorm2d(_BatchNorm):
-    _layouts = (4,)
-    _layout_names = "(N, C, H, W)"
+    ranks, layout = (4,), "(N, C, H, W)"
 
 
 class Dropout(Module):
-    """Inverted dropout; the identity in evaluation mode (nn/layers.py:217-230)."""
+    """Inverted dropout with probability ``p`` in training; the identity in evaluation."""
 
     def __init__(self, p: float = 0.5) -> None:
         super().__init__()
@@ -188,32 +181,38 @@ class Dropout(Module):
         return f"p={self.p}"
 
 
-class ReLU(Module):
+class _Pointwise(Module):
+    """A parameter-free layer applying one functional op."""
+
+    fn: Callable[[Tensor], Tensor]
+
     def forward(self, x: Tensor) -> Tensor:
-        return ops.relu(x)
+        return type(self).fn(x)
 
 
-class GELU(Module):
-    def forward(self, x: Tensor) -> Tensor:
-        return ops.gelu(x)
+class ReLU(_Pointwise):
+    fn = staticmethod(ops.relu)
 
 
-class Tanh(Module):
-    def forward(self, x: Tensor) -> Tensor:
-        return ops.tanh(x)
+class GELU(_Pointwise):
+    fn = staticmethod(ops.gelu)
 
 
-class Sigmoid(Module):
-    def forward(self, x: Tensor) -> Tensor:
-        return ops.sigmoid(x)
+class Tanh(_Pointwise):
+    fn = staticmethod(ops.tanh)
 
 
-class Identity(Module):
-    def forward(self, x: Tensor) -> Tensor:
-        return x
+class Sigmoid(_Pointwise):
+    fn = staticmethod(ops.sigmoid)
+
+
+class Identity(_Pointwise):
+    fn = staticmethod(lambda x: x)
 
 
 class Flatten(Module):
+    """Merge every axis from ``start_axis`` on into one."""
+
     def __init__(self, start_axis: int = 1) -> None:
         super().__init__()
         self.start_axis = start_axis
@@ -223,7 +222,7 @@ class Flatten(Module):
 
 
 class Sequential(Module):
-    """Chain modules (nn/layers.py:279-308)."""
+    """Layers applied in order; registered as children ``"0"``, ``"1"``, ..."""
 
     def __init__(self, *layers: Module) -> None:
         super().__init__()
@@ -236,16 +235,16 @@ class Sequential(Module):
         self._length += 1
         return self
 
-    def __getitem__(self, index: int) -> Module:
-        if not -self._length <= index < self._length:
-            raise IndexError(f"index {index} out of range for Sequential of length {len(self)}")
-        return self.__dict__["_modules"][str(index % self._length)]  # type: ignore[no-any-return]
-
     def __len__(self) -> int:
         return self._length
 
+    def __getitem__(self, index: int) -> Module:
+        if index < -self._length or index >= self._length:
+            raise IndexError(f"index {index} out of range for Sequential of length {len(self)}")
+        return getattr(self, str(index % self._length))  # type: ignore[no-any-return]
+
     def __iter__(self) -> Iterator[Module]:
-        return self.children()
+        return (getattr(self, str(i)) for i in range(self._length))
 
     def forward(self, x: Tensor) -> Tensor:
         for layer in self:
@@ -257,18 +256,20 @@ _ACTIVATIONS: dict[str, type[Module]] = {"relu": ReLU, "gelu": GELU, "tanh": Tan
 
 
 class MLP(Sequential):
-    """``Linear -> activation [-> Dropout]`` blocks (nn/layers.py:314-341)."""
+    """``Linear`` layers of the given sizes with an activation after each hidden one (and
+    after the last with ``final_activation``), dropout after hidden activations."""
 
     def __init__(self, sizes: Sequence[int], activation: Literal["relu", "gelu", "tanh"] = "relu",
                  dropout: float = 0.0, final_activation: bool = False) -> None:
         if len(sizes) < 2:
             raise ValueError("an MLP needs at least an input and an output size")
         layers: list[Module] = []
-        n_linear = len(sizes) - 1
-        for i, (fan_in, fan_out) in enumerate(itertools.pairwise(sizes)):
-            layers.append(Linear(fan_in, fan_out))
-            if i < n_linear - 1 or final_activation:
+        last = len(sizes) - 2
+        for i in range(last + 1):
+            layers.append(Linear(sizes[i], sizes[i + 1]))
+            hidden = i < last
+            if hidden or final_activation:
                 layers.append(_ACTIVATIONS[activation]())
-                if dropout > 0 and i < n_linear - 1:
-                    layers.append(Dropout(dropout))
+            if hidden and dropout > 0:
+                layers.append(Dropout(dropout))
         super().__init__(*layers)

@@ -10,6 +10,7 @@ reference does.
 
 from __future__ import annotations
 
+import ctypes
 import math
 from typing import Any
 
@@ -17,6 +18,7 @@ import numpy as np
 
 from tensorgrad_b200 import device
 from tensorgrad_b200._lib import AttnShape, check, lib
+from tensorgrad_b200._random import dropout_threshold, get_rng, pcg64_take
 from tensorgrad_b200.device import DeviceArray, dtype_code
 from tensorgrad_b200.ops._util import Need, as_tensor, make_result, unbroadcast
 from tensorgrad_b200.ops.elementwise import cast_array
@@ -50,6 +52,44 @@ def _backward(shape: AttnShape, code: int, q: int, k: int, v: int, o: int, lse: 
                                     device.stream()), "attention backward")
 
 
+def _dropout_state(score_shape: tuple[int, ...], p: float, training: bool,
+                   rng: np.random.Generator | None) -> tuple[np.ndarray, int, float] | None:
+    """The attention-dropout draw (ops/attention.py:59-68): ``None`` when inactive, else the
+    PCG64 state before the reference's keep-mask over ``score_shape`` (the host generator
+    moves past the mask), the 16-bit threshold and the survivor scale."""
+    if not training or p == 0.0:
+        return None
+    if not 0.0 <= p < 1.0:
+        raise ValueError(f"attention dropout must be in [0, 1), got {p}")
+    threshold, scale = dropout_threshold(p)
+    if threshold >= 65536:  # every weight dropped: keep_mask draws nothing
+        return np.zeros(4, np.uint64), threshold, scale
+    state = pcg64_take(rng or get_rng(), (math.prod(score_shape) + 3) // 4)
+    if state is None:
+        raise NotImplementedError("attention dropout on the device needs a PCG64 generator "
+                                  "(NumPy's default)")
+    return state, threshold, scale
+
+
+def _forward_dropout(shape: AttnShape, code: int, q: int, k: int, v: int, o: int, lse: int,
+                     drop: tuple[np.ndarray, int, float]) -> None:
+    state, threshold, scale = drop
+    scratch = device.scratch(lib.tg_attention_dropout_scratch_bytes(code, shape))
+    check(lib.tg_attention_forward_dropout(
+        code, shape, q, k, v, o, lse, state.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)),
+        threshold, scale, scratch.ptr, device.stream()), "attention (dropout)")
+
+
+def _backward_dropout(shape: AttnShape, code: int, q: int, k: int, v: int, do: int, dq: int,
+                      dk: int, dv: int, drop: tuple[np.ndarray, int, float]) -> None:
+    state, threshold, scale = drop
+    scratch = device.scratch(lib.tg_attention_dropout_scratch_bytes(code, shape))
+    check(lib.tg_attention_backward_dropout(
+        code, shape, q, k, v, do, dq, dk, dv,
+        state.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), threshold, scale, scratch.ptr,
+        device.stream()), "attention backward (dropout)")
+
+
 def _as_bhtd(shape: tuple[int, ...]) -> tuple[int, int]:
     """(B, H) of a ``(..., T, d)`` array: the batch axes collapse into B (and H = 1) unless
     there are exactly two."""
@@ -68,12 +108,12 @@ def scaled_dot_product_attention(
 
     ``q, k, v`` share their batch axes, or ``k``/``v`` broadcast over them (e.g. shared
     across heads); their gradients are then summed back (ops/attention.py:211-213). An extra
-    boolean ``mask`` and attention dropout are not part of the fused device kernel.
+    boolean ``mask`` is not supported on the device. Dropout on the attention weights
+    (``training`` and ``dropout_p > 0``) uses the reference's keep-mask, generated on the
+    device from the global (or given) PCG64 generator and regenerated by the VJP.
     """
     if mask is not None:
         raise NotImplementedError("scaled_dot_product_attention: only the causal mask is fused")
-    if training and dropout_p > 0.0:
-        raise NotImplementedError("attention dropout is not fused into the device kernel")
     tq, tk, tv = as_tensor(q), as_tensor(k), as_tensor(v)
     dt = np.result_type(tq.dtype, tk.dtype, tv.dtype)
     qd, kd, vd = (t.data if t.dtype == dt else cast_array(t.data, dt) for t in (tq, tk, tv))
@@ -97,9 +137,13 @@ def scaled_dot_product_attention(
     ks = (h * n_k * d, n_k * d, d)
     shp = _shape(b, h, n_q, n_k, d, qs, ks, ks, qs, causal)
     code = dtype_code(dt)
+    drop = _dropout_state((*batch, n_q, n_k), dropout_p, training, rng)
     out = device.empty(full_shapes[0], dt)
     lse = device.empty((b * h * n_q,), dt)
-    _forward(shp, code, qf.ptr, kf.ptr, vf.ptr, out.ptr, lse.ptr)
+    if drop is None:
+        _forward(shp, code, qf.ptr, kf.ptr, vf.ptr, out.ptr, lse.ptr)
+    else:
+        _forward_dropout(shp, code, qf.ptr, kf.ptr, vf.ptr, out.ptr, lse.ptr, drop)
 
     def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray | None, ...]:
         if g.dtype != dt:
@@ -107,8 +151,12 @@ def scaled_dot_product_attention(
         dq = device.empty(full_shapes[0], dt)
         dk = device.empty(full_shapes[1], dt)
         dv = device.empty(full_shapes[2], dt)
-        _backward(shp, code, qf.ptr, kf.ptr, vf.ptr, out.ptr, lse.ptr, g.ptr, dq.ptr, dk.ptr,
-                  dv.ptr)
+        if drop is None:
+            _backward(shp, code, qf.ptr, kf.ptr, vf.ptr, out.ptr, lse.ptr, g.ptr, dq.ptr,
+                      dk.ptr, dv.ptr)
+        else:
+            _backward_dropout(shp, code, qf.ptr, kf.ptr, vf.ptr, g.ptr, dq.ptr, dk.ptr, dv.ptr,
+                              drop)
         grads = []
         for gr, t, wanted in zip((dq, dk, dv), (tq, tk, tv), need, strict=True):
             if not wanted:
@@ -127,14 +175,13 @@ def packed_self_attention(
     training: bool = False, rng: np.random.Generator | None = None,
 ) -> Tensor:
     """Multi-head self-attention on a packed ``(B, T, 3 * D)`` QKV projection; returns merged
-    heads ``(B, T, D)`` (ops/attention.py:223-272)."""
+    heads ``(B, T, D)`` (ops/attention.py:223-272). Attention dropout as in
+    :func:`scaled_dot_product_attention`, with the mask over ``(B, H, T, T)``."""
     tqkv = as_tensor(qkv)
     if tqkv.ndim != 3 or tqkv.shape[-1] % (3 * num_heads):
         raise ValueError(
             f"expected (B, T, 3 * D) with D divisible by {num_heads}, got {tqkv.shape}"
         )
-    if training and dropout_p > 0.0:
-        raise NotImplementedError("attention dropout is not fused into the device kernel")
     b, t, d3 = tqkv.shape
     d = d3 // 3
     hd = d // num_heads
@@ -144,18 +191,27 @@ def packed_self_attention(
     src = (t * d3, hd, d3)           # strides of q, k, v inside the packed buffer
     dst = (t * d, hd, d)             # strides of the merged-head output
     shp = _shape(b, num_heads, t, t, hd, src, src, src, dst, causal)
+    drop = _dropout_state((b, num_heads, t, t), dropout_p, training, rng)
     out = device.empty((b, t, d), x.dtype)
     lse = device.empty((b * num_heads * t,), x.dtype)
     base = x.ptr
-    _forward(shp, code, base, base + d * es, base + 2 * d * es, out.ptr, lse.ptr)
+    if drop is None:
+        _forward(shp, code, base, base + d * es, base + 2 * d * es, out.ptr, lse.ptr)
+    else:
+        _forward_dropout(shp, code, base, base + d * es, base + 2 * d * es, out.ptr, lse.ptr,
+                         drop)
 
     def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
         if g.dtype != x.dtype:
             g = cast_array(g, x.dtype)
         dqkv = device.empty((b, t, d3), x.dtype)
         gb = dqkv.ptr
-        _backward(shp, code, base, base + d * es, base + 2 * d * es, out.ptr, lse.ptr, g.ptr,
-                  gb, gb + d * es, gb + 2 * d * es)
+        if drop is None:
+            _backward(shp, code, base, base + d * es, base + 2 * d * es, out.ptr, lse.ptr,
+                      g.ptr, gb, gb + d * es, gb + 2 * d * es)
+        else:
+            _backward_dropout(shp, code, base, base + d * es, base + 2 * d * es, g.ptr, gb,
+                              gb + d * es, gb + 2 * d * es, drop)
         return (dqkv,)
 
     return make_result(out, (tqkv,), backward, "self_attention")

@@ -3,13 +3,14 @@ linear, layer norm, batch norm, embedding and dropout."""
 
 from __future__ import annotations
 
+import ctypes
 from typing import Any
 
 import numpy as np
 
 from tensorgrad_b200 import device
 from tensorgrad_b200._lib import MUL, check, lib
-from tensorgrad_b200._random import get_rng, keep_mask
+from tensorgrad_b200._random import dropout_threshold, get_rng, keep_mask, pcg64_take
 from tensorgrad_b200.autograd import no_grad
 from tensorgrad_b200.device import DeviceArray, dtype_code
 from tensorgrad_b200.ops import elementwise, reduce
@@ -304,18 +305,40 @@ def embedding(indices: Any, weight: Any) -> Tensor:
 @profiled("dropout")
 def dropout(x: Any, p: float = 0.5, training: bool = True,
             rng: np.random.Generator | None = None) -> Tensor:
-    """Inverted dropout with the reference's quantised keep-mask, drawn on the host from the
-    global generator and uploaded (ops/layers.py:235-259); the identity when ``p == 0`` or not
-    training."""
+    """Inverted dropout with the reference's quantised keep-mask (ops/layers.py:235-259); the
+    identity when ``p == 0`` or not training. With a PCG64 generator (NumPy's default, and
+    the global one) the mask is generated on the device from the generator's state, equal to
+    the reference's bit for bit, and regenerated by the VJP instead of stored; other
+    generators draw it on the host and upload it."""
     tx = as_tensor(x)
     if not 0.0 <= p <= 1.0:
         raise ValueError(f"dropout probability must be in [0, 1], got {p}")
     if not training or p == 0.0:
         return tx
-    keep, scale = keep_mask(tx.shape, p, rng or get_rng())
-    mask = device.from_numpy((keep * np.asarray(scale, dtype=tx.dtype)).astype(tx.dtype))
+    gen = rng or get_rng()
+    threshold, scale = dropout_threshold(p)
+    n = tx.size
+    # keep_mask draws nothing when every element is dropped.
+    state = (np.zeros(4, np.uint64) if threshold >= 65536
+             else pcg64_take(gen, (n + 3) // 4))
+    if state is None:
+        # Not a PCG64 generator: the reference's mask drawn on the host and uploaded.
+        keep, scale = keep_mask(tx.shape, p, gen)
+        mask = device.from_numpy((keep * np.asarray(scale, dtype=tx.dtype)).astype(tx.dtype))
+
+        def backward_host(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+            return (binary_array(g, mask, MUL),)
+
+        return make_result(binary_array(tx.data, mask, MUL), (tx,), backward_host, "dropout")
+    def apply(src: DeviceArray) -> DeviceArray:
+        out = device.empty(src.shape, src.dtype)
+        check(lib.tg_dropout_pcg64(dtype_code(src.dtype), n, src.ptr, out.ptr,
+                                   state.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), 0,
+                                   threshold, scale, device.stream()), "dropout")
+        return out
 
     def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
-        return (binary_array(g, mask, MUL),)
+        # The VJP multiplies by the same mask, regenerated from the same generator state.
+        return (apply(g if g.dtype == tx.dtype else g.astype(tx.dtype)),)
 
-    return make_result(binary_array(tx.data, mask, MUL), (tx,), backward, "dropout")
+    return make_result(apply(tx.data), (tx,), backward, "dropout")

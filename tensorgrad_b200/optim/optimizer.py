@@ -1,11 +1,17 @@
-"""Optimizer base class and parameter groups (the reference's optim/optimizer.py:15-116)."""
+"""Optimizer base and parameter groups (API and checks of the reference's
+optim/optimizer.py:15-116), for device optimizers.
+
+The constructor accepts a list of tensors or a list of group dicts (``params`` plus optional
+``lr`` / ``weight_decay``) and validates them with the reference's exception types and
+messages. Subclasses implement ``step`` as device kernels over the groups; the per-parameter
+state is keyed by the parameter's identity.
+"""
 
 from __future__ import annotations
 
-from abc import ABC, abstractmethod
 from collections.abc import Iterable
 from dataclasses import dataclass, field
-from typing import Any, Generic, NotRequired, TypedDict, TypeVar, cast
+from typing import Any, Generic, NotRequired, TypedDict, TypeVar
 
 from tensorgrad_b200.tensor import Tensor
 
@@ -20,7 +26,8 @@ class ParamGroupSpec(TypedDict):
 
 @dataclass(eq=False)
 class ParamGroup:
-    """Parameters sharing a learning rate and weight decay; schedulers scale ``initial_lr``."""
+    """Parameters that share a learning rate and weight decay; ``initial_lr`` is the learning
+    rate the group started with (what schedules scale)."""
 
     params: list[Tensor]
     lr: float
@@ -34,9 +41,18 @@ class ParamGroup:
 StateT = TypeVar("StateT")
 
 
-class Optimizer(ABC, Generic[StateT]):
-    """Owns parameter groups and per-parameter state; same validation and messages as the
-    reference. Subclasses implement :meth:`step` with device kernels."""
+def _group_specs(items: list[Any]) -> list[dict[str, Any]]:
+    """The constructor's argument as group dicts: one group for a plain list of tensors."""
+    dicts = [isinstance(item, dict) for item in items]
+    if all(dicts):
+        return [dict(item) for item in items]
+    if any(dicts):
+        raise TypeError("mix of tensors and parameter-group dicts")
+    return [{"params": items}]
+
+
+class Optimizer(Generic[StateT]):
+    """Parameter groups and per-parameter state; ``step`` is the subclass's update."""
 
     def __init__(self, params: Iterable[Any], lr: float, weight_decay: float) -> None:
         if lr < 0:
@@ -46,40 +62,32 @@ class Optimizer(ABC, Generic[StateT]):
         items = list(params)
         if not items:
             raise ValueError("optimizer got an empty parameter list")
-        if all(isinstance(item, dict) for item in items):
-            specs = cast(list[ParamGroupSpec], items)
-        elif any(isinstance(item, dict) for item in items):
-            raise TypeError("mix of tensors and parameter-group dicts")
-        else:
-            specs = [{"params": cast(list[Tensor], items)}]
+        claimed: set[int] = set()
         self.param_groups: list[ParamGroup] = []
-        seen: set[int] = set()
-        for spec in specs:
-            group_params = list(spec["params"])
-            for p in group_params:
+        for spec in _group_specs(items):
+            members = list(spec["params"])
+            for p in members:
                 if not isinstance(p, Tensor) or not p.requires_grad:
                     raise TypeError("optimizers can only update tensors with requires_grad=True")
-                if id(p) in seen:
+                if id(p) in claimed:  # listed twice, in one group or in two
                     raise ValueError("a parameter appears in more than one parameter group")
-                seen.add(id(p))
-            self.param_groups.append(ParamGroup(group_params, lr=spec.get("lr", lr),
-                                                weight_decay=spec.get("weight_decay",
-                                                                      weight_decay)))
+                claimed.add(id(p))
+            self.param_groups.append(ParamGroup(members, spec.get("lr", lr),
+                                                spec.get("weight_decay", weight_decay)))
         self.state: dict[int, StateT] = {}
 
     def zero_grad(self) -> None:
-        """Reset the gradient of every managed parameter (``grad = None``)."""
-        cleared = {id(p) for group in self.param_groups for p in group.params}
-        for group in self.param_groups:
-            for p in group.params:
-                arena = p._arena
-                # A clip rescale still pending on gradients that are all being dropped
-                # needs no writing.
-                if (arena is not None and arena.pending_clip is not None
-                        and all(id(q) in cleared for q in arena.params)):
-                    arena.pending_clip = None
-                p.grad = None
+        """Drop every managed parameter's gradient (``grad = None``)."""
+        everything = [p for g in self.param_groups for p in g.params]
+        ids = {id(p) for p in everything}
+        for p in everything:
+            arena = p._arena
+            # A clip rescale still pending on gradients that all go away needs no writing.
+            if (arena is not None and arena.pending_clip is not None
+                    and all(id(q) in ids for q in arena.params)):
+                arena.pending_clip = None
+            p.grad = None
 
-    @abstractmethod
     def step(self) -> None:
         """Apply one update to every parameter that has a gradient."""
+        raise NotImplementedError

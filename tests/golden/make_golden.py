@@ -1,6 +1,8 @@
 """Generate the golden fixtures of ``tests/golden/`` by running the reference tensorgrad itself.
 
-    PYTHONPATH=/root/reference/src python tests/golden/make_golden.py
+    PYTHONPATH=<the reference's src/ directory> python tests/golden/make_golden.py [name ...]
+
+(with names, only those fixtures are rewritten, e.g. ``gpt_dropout dropout_masks``).
 
 Run in the build container, where the reference is importable (it is pure Python + NumPy).
 Everything runs in float64. Inputs are regenerated in the tests from the same seeds
@@ -28,7 +30,8 @@ from oracle import cnn as ocnn  # noqa: E402
 from oracle import rnn as ornn  # noqa: E402
 from oracle import gpt as ogpt  # noqa: E402
 from tests.golden.specs import (  # noqa: E402
-    ATTN_CASES, CNN_SMALL, CONV_CASES, GPT_SMALL, POOL_CASES, RNN_CASES, RNN_SMALL,
+    ATTN_CASES, CNN_SMALL, CONV_CASES, DROPOUT_CASES, GPT_DROPOUT, GPT_SMALL, POOL_CASES,
+    RNN_CASES, RNN_SMALL,
     attention_inputs, conv_inputs, pool_input, rnn_inputs,
 )
 
@@ -38,11 +41,13 @@ def run_gpt(spec: dict) -> dict[str, np.ndarray]:
     tg.manual_seed(0)
     model = nn.GPT(nn.GPTConfig(vocab_size=cfg.vocab_size, block_size=cfg.block_size,
                                 n_layer=cfg.n_layer, n_head=cfg.n_head, n_embd=cfg.n_embd,
-                                dropout=0.0))
+                                dropout=spec.get("dropout", 0.0)))
     init = ogpt.init_params(cfg, spec["seed"])
     state = dict(init)
     state["head.weight"] = init["tok_emb.weight"]
     model.load_state_dict(state)
+    if "reseed" in spec:  # the dropout masks then start from a known generator state
+        tg.manual_seed(spec["reseed"])
     params = list(model.parameters())
     names = [n for n, _ in model.named_parameters()]
     assert names == [n for n, _ in ogpt.param_shapes(cfg)], names
@@ -198,14 +203,73 @@ def run_rnn_models(spec: dict) -> dict[str, np.ndarray]:
     return out
 
 
+def run_dropout_masks() -> dict[str, np.ndarray]:
+    """The reference's keep_mask for seeded generators, and the generator's next raw draws
+    after it (so the stream position after a mask is pinned too)."""
+    from tensorgrad._random import keep_mask
+
+    out: dict[str, np.ndarray] = {}
+    for i, (shape, p, seed) in enumerate(DROPOUT_CASES):
+        rng = np.random.default_rng(seed)
+        rng.integers(0, 2**32, size=3, dtype=np.uint32)  # leaves a buffered 32-bit half
+        keep, scale = keep_mask(shape, p, rng)
+        out[f"case{i}/keep"] = keep
+        out[f"case{i}/scale"] = np.asarray(scale)
+        out[f"case{i}/next_u32"] = rng.integers(0, 2**32, size=3, dtype=np.uint32)
+        out[f"case{i}/next_raw"] = rng.bit_generator.random_raw(2)
+    return out
+
+
+def write_checkpoint(path: str) -> None:
+    """The reference's own checkpoint file: a freshly initialised GPT (manual_seed(7), so the
+    weights also pin the initialisation order) saved with tensorgrad.utils.save."""
+    cfg = GPT_SMALL["cfg"]
+    tg.set_default_dtype(np.float64)
+    tg.manual_seed(7)
+    model = nn.GPT(nn.GPTConfig(vocab_size=cfg.vocab_size, block_size=cfg.block_size,
+                                n_layer=cfg.n_layer, n_head=cfg.n_head, n_embd=cfg.n_embd))
+    tg.utils.save(model, path)
+
+
+def run_generate() -> dict[str, np.ndarray]:
+    """KV-cache generation by the reference: a freshly initialised GPT (manual_seed(7), block
+    16) extends a 5-token prompt by 20 tokens, greedily (top_k = 1) and by sampling at
+    temperature 0.8 from a seeded generator; the window slides past the block after 11 new
+    tokens, so both the cached and the re-encoded paths run. Also the logits of one
+    full-window forward in evaluation mode."""
+    cfg = GPT_SMALL["cfg"]
+    tg.set_default_dtype(np.float64)
+    tg.manual_seed(7)
+    model = nn.GPT(nn.GPTConfig(vocab_size=cfg.vocab_size, block_size=cfg.block_size,
+                                n_layer=cfg.n_layer, n_head=cfg.n_head, n_embd=cfg.n_embd))
+    prompt = np.random.default_rng(17).integers(0, cfg.vocab_size, size=(2, 5))
+    greedy = model.generate(prompt, 20, top_k=1, rng=np.random.default_rng(1))
+    sampled = model.generate(prompt, 20, temperature=0.8, rng=np.random.default_rng(2))
+    model.eval()
+    logits = np.array(model(greedy[:, :cfg.block_size]).data)
+    return {"prompt": prompt, "greedy": greedy, "sampled": sampled, "logits": logits}
+
+
 def main() -> None:
-    np.savez_compressed(os.path.join(HERE, "gpt_small.npz"), **run_gpt(GPT_SMALL))
-    np.savez_compressed(os.path.join(HERE, "attention.npz"), **run_attention())
-    np.savez_compressed(os.path.join(HERE, "cnn_small.npz"), **run_cnn(CNN_SMALL))
-    np.savez_compressed(os.path.join(HERE, "conv_pool.npz"), **run_conv_pool())
-    np.savez_compressed(os.path.join(HERE, "rnn_ops.npz"), **run_rnn_ops())
-    np.savez_compressed(os.path.join(HERE, "rnn_small.npz"), **run_rnn_models(RNN_SMALL))
-    print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
+    jobs = {
+        "gpt_small": lambda: run_gpt(GPT_SMALL),
+        "attention": run_attention,
+        "cnn_small": lambda: run_cnn(CNN_SMALL),
+        "conv_pool": run_conv_pool,
+        "rnn_ops": run_rnn_ops,
+        "rnn_small": lambda: run_rnn_models(RNN_SMALL),
+        "gpt_dropout": lambda: run_gpt(GPT_DROPOUT),
+        "dropout_masks": run_dropout_masks,
+        "gpt_generate": run_generate,
+    }
+    names = sys.argv[1:] or [*jobs, "gpt_checkpoint"]
+    for name in names:
+        path = os.path.join(HERE, f"{name}.npz")
+        if name == "gpt_checkpoint":
+            write_checkpoint(path)
+        else:
+            np.savez_compressed(path, **jobs[name]())
+    print("wrote", names)
 
 
 if __name__ == "__main__":

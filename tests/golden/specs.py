@@ -11,6 +11,13 @@ from oracle import gpt as ogpt
 #: ``max_norm`` sits below the gradient norm so that clipping is exercised.
 GPT_SMALL = dict(cfg=ogpt.Config(vocab_size=65, block_size=16, n_layer=2, n_head=2, n_embd=16),
                  batch=4, seq=16, seed=0, max_norm=0.5, steps=2)
+#: The same GPT trained with dropout 0.1 everywhere the reference applies it (embeddings,
+#: attention weights, the attention projection and the MLP output), the global generator
+#: re-seeded right after the weights are loaded so the masks start from a known state.
+GPT_DROPOUT = dict(GPT_SMALL, dropout=0.1, reseed=4321)
+#: (shape, p, seed) of the keep-mask fixtures: odd sizes (a partial last 64-bit draw), a
+#: common rate, and a rate that rounds to "drop everything" (no draw at all).
+DROPOUT_CASES = [((7, 13), 0.1, 1), ((3, 5, 4), 0.5, 2), ((10,), 0.99999999, 3)]
 #: ((B, H, T, d), causal, seed) of the attention fixtures.
 ATTN_CASES = [((2, 2, 24, 8), True, 1), ((1, 3, 17, 16), False, 2), ((2, 1, 33, 32), True, 3)]
 
