@@ -13,13 +13,14 @@
 // Persistent, warp-specialised (one CTA of 512 threads per SM, tiles of 128 x BN,
 // BN = 64/128/256; k-blocks of BK = 32 fp32 (128-byte rows) for tiles up to 128 wide, 16
 // (64-byte rows) for 256-wide and pair tiles):
-//   warp 0 (lane 0)  : TMA producer over every (tile, k-block) of this CTA, STAGES-deep ring.
-//   warps 4..11      : write lo for each stage (A's hi and lo into TMEM when A is K-major and
-//                      the tile at most 128 wide), fence the generic-proxy writes for the
-//                      async proxy, arrive on split[s].
-//   warp 1 (lane 0)  : MMA issuer: 3 x (BK/8) tcgen05.mma per stage into one of two TMEM
-//                      accumulators; tcgen05.commit frees the stage and, after a tile's last
-//                      k-block, hands the accumulator to the epilogue.
+//   warp 0 (lane 0)  : TMA producer over every (tile, k-block) of this CTA into a raw ring
+//                      of 4 to 8 slots.
+//   warps 4..11      : write lo for each k-block into a 2- or 3-slot lo ring (A's hi and lo
+//                      into TMEM when A is K-major and the tile at most 128 wide), fence the
+//                      generic-proxy writes for the async proxy, arrive on split[l].
+//   warp 1 (lane 0)  : MMA issuer: 3 x (BK/8) tcgen05.mma per k-block into one of two TMEM
+//                      accumulators; tcgen05.commit frees the raw and lo slots and, after a
+//                      tile's last k-block, hands the accumulator to the epilogue.
 //   warps 12..15     : epilogue: tcgen05.ld of TMEM lanes 32*(warp%4).., alpha/beta/bias,
 //                      16-byte stores; then the accumulator is released to the MMA warp.
 // So a tile's epilogue overlaps the next tile's loads and MMAs. K-major operands use the
@@ -65,7 +66,7 @@ struct TcArgs {
 constexpr int kThreads = 512;
 constexpr int kSplitWarp0 = 4, kSplitThreads = 256;  // warps 4..11
 // Split warps per k-block: one group of 8 warps (two per TMEM lane quarter).
-constexpr int kSplitGroups = 1, kGroupThreads = kSplitThreads / kSplitGroups;
+constexpr int kSplitGroups = 2, kGroupThreads = kSplitThreads / kSplitGroups;
 constexpr int kEpiWarp0 = 12;                        // warps 12..15
 // Epilogue staging: per epilogue warp two 32 x 32 fp32 boxes (128-byte swizzle), one TMA
 // store (or load) each.
@@ -73,6 +74,13 @@ constexpr uint32_t kEpiBox = 32 * 32 * 4;
 constexpr uint32_t kEpiBytes = 4 * 2 * kEpiBox;
 
 // PAIR: a CTA of a cta_group::2 pair holds its 128 rows of A and half of the BN columns of B.
+//
+// Two rings. The raw ring holds what the TMA brings (A then B of one k-block per slot) and a
+// slot stays busy until the k-block's MMAs complete; the lo ring holds what the split warps
+// write (A's lo, unless A goes to tensor memory, then B's lo) and is only needed from the
+// split to the MMAs. A k-block's trip through the raw ring is dominated by the TMA latency
+// (about 1.5 us under load), so the raw ring gets the depth and the lo ring two or three
+// slots.
 template <int BN, bool PAIR = false, bool ATM = false>
 struct Layout {
   // k-block depth: 32 fp32 (128-byte rows, 128-byte swizzle) for single-CTA tiles up to 128
@@ -81,21 +89,21 @@ struct Layout {
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
   static constexpr uint32_t A_BYTES = BM * BK * 4;
   static constexpr uint32_t B_BYTES = B_ROWS * BK * 4;
-  // ATM (A in tensor memory): a stage holds raw A, raw B and B's lo; A's hi and lo go to
-  // TMEM columns after the two accumulators (2 * BK per stage). Otherwise raw + lo of both.
-  static constexpr uint32_t B_OFF = ATM ? A_BYTES : 2 * A_BYTES;
-  static constexpr uint32_t STAGE = B_OFF + 2 * B_BYTES;
+  static constexpr uint32_t RAW = A_BYTES + B_BYTES;               // raw slot: A, then B
+  static constexpr uint32_t LO = (ATM ? 0 : A_BYTES) + B_BYTES;    // lo slot: A lo, B lo
   static constexpr uint32_t ACC_COLS = 2 * BN;  // two accumulators
+  // ATM (A in tensor memory): A's hi and lo of each lo slot go to TMEM columns after the
+  // accumulators (2 * BK per slot).
   static constexpr uint32_t TMEM_COLS = ATM ? 512 : ACC_COLS;
+  // Slot counts: the lo ring 2 (3 when its slots are small), bounded by TMEM with ATM; the
+  // raw ring whatever fits in 193 KB beside it (at most 8).
+  static constexpr int LO_TMEM_CAP = ATM ? (int)((512 - 2 * BN) / (2 * BK)) : 8;
+  static constexpr int LST0 = 3;
+  static constexpr int LST = LST0 < LO_TMEM_CAP ? LST0 : LO_TMEM_CAP;
+  static constexpr int RST0 = (int)((193 * 1024 - LST * LO) / RAW);
+  static constexpr int RST = RST0 < 8 ? RST0 : 8;
+  static constexpr uint32_t RINGS = RST * RAW + LST * LO;
 };
-
-template <int BN, bool PAIR = false, bool ATM = false>
-constexpr int stages_for() {
-  constexpr uint32_t s = Layout<BN, PAIR, ATM>::STAGE;
-  constexpr int by_smem = (int)((200 * 1024) / s);
-  constexpr int cap = ATM ? (int)((512 - 2 * BN) / (2 * Layout<BN, PAIR, ATM>::BK)) : 8;
-  return by_smem > cap ? cap : by_smem;
-}
 
 // Descriptor of k-step kk (8 tf32 along K) of a stage tile with KB k values per row.
 //  K-major : rows of KB K values; KB = 16: 64-byte rows, 64-byte swizzle, the next 8-row
@@ -152,7 +160,7 @@ __device__ __forceinline__ TileInfo tile_info(const TcArgs& a, int t, int bn, in
 // CTAs on its own 128 rows and half of B, except the MMA issuer (even CTA only). The split
 // warps and the epilogue of the odd CTA arrive on the even CTA's barriers; the MMA commits
 // arrive on both CTAs' barriers.
-template <int BN, int STAGES, bool A_MN, bool B_MN, bool PAIR, bool ATM>
+template <int BN, bool A_MN, bool B_MN, bool PAIR, bool ATM>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX,
@@ -161,14 +169,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   static_assert(!ATM || (!PAIR && !A_MN), "A in tensor memory: single CTA, K-major A");
   constexpr int TILE_M = PAIR ? 2 * BM : BM;
   constexpr int KB = L::BK;
+  constexpr int RST = L::RST, LST = L::LST;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint8_t* ebuf_all = smem + STAGES * L::STAGE;  // kEpiBytes of epilogue staging
-  uint64_t* full = reinterpret_cast<uint64_t*>(ebuf_all + kEpiBytes);
-  uint64_t* split = full + STAGES;
-  uint64_t* empty = split + STAGES;
-  uint64_t* acc_full = empty + STAGES;   // [2]
+  uint8_t* raw_ring = smem;                       // RST slots of L::RAW bytes
+  uint8_t* lo_ring = smem + RST * L::RAW;         // LST slots of L::LO bytes
+  uint8_t* ebuf_all = smem + L::RINGS;            // kEpiBytes of epilogue staging
+  uint64_t* full = reinterpret_cast<uint64_t*>(ebuf_all + kEpiBytes);  // [RST] raw landed
+  uint64_t* empty = full + RST;                   // [RST] raw slot consumed by the MMAs
+  uint64_t* split = empty + RST;                  // [LST] lo slot written
+  uint64_t* acc_full = split + LST;      // [2]
   uint64_t* acc_empty = acc_full + 2;    // [2]
   uint64_t* drain = acc_empty + 2;
   uint64_t* ebar_all = drain + 1;        // [4 warps][2]: epilogue TMA loads
@@ -184,11 +195,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   const int64_t row_off = (int64_t)rank * BM;  // this CTA's rows within a pair tile
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < RST; ++s) {
       mbar_init(&full[s], 1);
-      // One arrival per split warp, plus (even CTA of a pair) the odd CTA's relay.
-      mbar_init(&split[s], (kGroupThreads / 32) + (PAIR && rank == 0 ? 1 : 0));
       mbar_init(&empty[s], 1);
+    }
+    for (int l = 0; l < LST; ++l) {
+      // One arrival per split warp, plus (even CTA of a pair) the odd CTA's relay.
+      mbar_init(&split[l], (kGroupThreads / 32) + (PAIR && rank == 0 ? 1 : 0));
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -216,11 +229,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       for (int t = unit; t < total && !stop; t += units) {
         const TileInfo ti = tile_info(args, t, BN, TILE_M, KB);
         for (int j = 0; j < ti.nk; ++j, ++it) {
-          const int s = it % STAGES, round = it / STAGES;
+          const int s = it % RST, round = it / RST;
           if (round > 0 && !wait_bar(&empty[s], (round - 1) & 1, abort_flag)) { stop = true; break; }
-          uint8_t* st = smem + s * L::STAGE;
-          uint8_t* a_raw = st;
-          uint8_t* b_raw = st + L::B_OFF;
+          uint8_t* a_raw = raw_ring + s * L::RAW;
+          uint8_t* b_raw = a_raw + L::A_BYTES;
           mbar_arrive_expect_tx(&full[s], L::A_BYTES + L::B_BYTES);
           const int k0 = (ti.kb0 + j) * KB;
           const int hh = ti.bz % args.heads, bo = ti.bz / args.heads;
@@ -248,16 +260,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       }
       if (*abort_flag) {
         // Let the copies already issued land before the CTA's shared memory goes away.
-        for (int j = it - STAGES; j < it; ++j) {
+        for (int j = it - RST; j < it; ++j) {
           if (j < 0) continue;
-          wait_bar(&full[j % STAGES], (j / STAGES) & 1, abort_flag, false);
+          wait_bar(&full[j % RST], (j / RST) & 1, abort_flag, false);
         }
       } else {
-        // Tail: the MMA's last stage releases (tcgen05.commit arrivals on this CTA's empty
+        // Tail: the MMA's last raw-slot releases (tcgen05.commit arrivals on this CTA's empty
         // barriers) land before the CTA may exit.
-        for (int j = it - STAGES; j < it; ++j) {
+        for (int j = it - RST; j < it; ++j) {
           if (j < 0) continue;
-          wait_bar(&empty[j % STAGES], (j / STAGES) & 1, abort_flag);
+          wait_bar(&empty[j % RST], (j / RST) & 1, abort_flag);
         }
       }
     }
@@ -270,9 +282,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       for (int t = unit; t < total && ok; t += units) {
         const TileInfo ti = tile_info(args, t, BN, TILE_M, KB);
         for (int j = 0; j < ti.nk; ++j, ++it) {
-          const int s = it % STAGES, round = it / STAGES;
-          if (!wait_bar(&split[s], round & 1, abort_flag)) { ok = false; break; }
-          mbar_arrive_cluster(map_to_rank(&split[s], 0));
+          const int l = it % LST;
+          if (!wait_bar(&split[l], (it / LST) & 1, abort_flag)) { ok = false; break; }
+          mbar_arrive_cluster(map_to_rank(&split[l], 0));
         }
       }
     }
@@ -292,29 +304,51 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         tc_fence_after();
         const uint32_t acc = tmem + (uint32_t)(buf * BN);
         for (int j = 0; j < ti.nk; ++j, ++it) {
-          const int s = it % STAGES, round = it / STAGES;
-          if (!(PAIR ? wait_bar_cluster(&split[s], round & 1, abort_flag)
-                     : wait_bar(&split[s], round & 1, abort_flag))) { ok = false; break; }
+          const int s = it % RST, l = it % LST;
+          const uint32_t a_raw = smem_u32(raw_ring + s * L::RAW), b_raw = a_raw + L::A_BYTES;
+          const uint32_t a_lo = smem_u32(lo_ring + l * L::LO);
+          const uint32_t b_lo = a_lo + (ATM ? 0u : L::A_BYTES);
+          if (!PAIR) {
+            // hi x hi needs only what the TMA brought: issue it as soon as the raw slot has
+            // landed, so the tensor pipe works while the split warps write lo; then the two
+            // lo products (A's lo and hi from TMEM when ATM).
+            // The TMA's writes are visible to the MMAs once the barrier completes (both in the
+            // async proxy); the split warps fenced their stores for the async proxy before
+            // arriving. Only A's hi/lo in TMEM (ATM) need the tcgen05 thread-sync fence.
+            if (!wait_bar(&full[s], (it / RST) & 1, abort_flag)) { ok = false; break; }
+#pragma unroll
+            for (int kk = 0; kk < KB / 8; ++kk)
+              mma_tf32(acc, tile_desc<A_MN, KB>(a_raw, kk), tile_desc<B_MN, KB>(b_raw, kk),
+                       idesc, (j | kk) != 0);
+            if (!args.raw) {
+              if (!wait_bar(&split[l], (it / LST) & 1, abort_flag)) { ok = false; break; }
+              if (ATM) tc_fence_after();
+#pragma unroll
+              for (int kk = 0; kk < KB / 8; ++kk) {
+                const uint64_t bh = tile_desc<B_MN, KB>(b_raw, kk);
+                const uint64_t bl = tile_desc<B_MN, KB>(b_lo, kk);
+                if (ATM) {
+                  // A's hi (the raw bits) and lo of this lo slot in TMEM columns after the
+                  // accumulators: [hi k 0..KB-1 | lo k 0..KB-1].
+                  const uint32_t th = tmem + L::ACC_COLS + (uint32_t)(l * 2 * KB + kk * 8);
+                  mma_tf32_ta(acc, th + KB, bh, idesc, 1);
+                  mma_tf32_ta(acc, th, bl, idesc, 1);
+                } else {
+                  mma_tf32(acc, tile_desc<A_MN, KB>(a_lo, kk), bh, idesc, 1);
+                  mma_tf32(acc, tile_desc<A_MN, KB>(a_raw, kk), bl, idesc, 1);
+                }
+              }
+            }
+            mma_commit(&empty[s]);  // frees the raw slot, and with it lo slot l (see the split)
+            continue;
+          }
+          if (!wait_bar_cluster(&split[l], (it / LST) & 1, abort_flag)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t st = smem_u32(smem + s * L::STAGE);
-          const uint32_t a_raw = st, a_lo = st + L::A_BYTES;
-          const uint32_t b_raw = st + L::B_OFF, b_lo = b_raw + L::B_BYTES;
 #pragma unroll
           for (int kk = 0; kk < KB / 8; ++kk) {
             const uint64_t ah = tile_desc<A_MN, KB>(a_raw, kk), al = tile_desc<A_MN, KB>(a_lo, kk);
             const uint64_t bh = tile_desc<B_MN, KB>(b_raw, kk), bl = tile_desc<B_MN, KB>(b_lo, kk);
-            if (ATM) {
-              // A's hi (the raw bits) and lo of this stage in TMEM columns after the
-              // accumulators: [hi k 0..15 | lo k 0..15].
-              const uint32_t th = tmem + L::ACC_COLS + (uint32_t)(s * 2 * KB + kk * 8);
-              if (args.raw) {
-                mma_tf32_ta(acc, th, bh, idesc, (j | kk) != 0);
-              } else {
-                mma_tf32_ta(acc, th + KB, bh, idesc, (j | kk) != 0);
-                mma_tf32_ta(acc, th, bl, idesc, 1);
-                mma_tf32_ta(acc, th, bh, idesc, 1);
-              }
-            } else if (PAIR) {
+            if (PAIR) {
               if (args.raw) {
                 mma_tf32_pair(acc, ah, bh, idesc, (j | kk) != 0);
               } else {
@@ -322,16 +356,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 mma_tf32_pair(acc, ah, bl, idesc, 1);
                 mma_tf32_pair(acc, ah, bh, idesc, 1);
               }
-            } else if (args.raw) {
-              mma_tf32(acc, ah, bh, idesc, (j | kk) != 0);
-            } else {
-              mma_tf32(acc, al, bh, idesc, (j | kk) != 0);
-              mma_tf32(acc, ah, bl, idesc, 1);
-              mma_tf32(acc, ah, bh, idesc, 1);
             }
           }
-          if (PAIR) mma_commit_pair_both(&empty[s]);
-          else mma_commit(&empty[s]);
+          mma_commit_pair_both(&empty[s]);
         }
         if (!ok) break;
         // with nk == 0 this fires at once; the epilogue uses 0
@@ -350,16 +377,24 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int grp = (warp - kSplitWarp0) / kGroupWarps;
     const int t0 = threadIdx.x - (kSplitWarp0 + kGroupWarps * grp) * 32;  // 0 .. kGroupThreads-1
     int it = 0;
-    bool stop = false;
+    // Plain TF32 on one CTA: the MMAs read only what the TMA brought, nothing to split.
+    bool stop = !PAIR && args.raw;
     for (int t = unit; t < total && !stop; t += units) {
       const TileInfo ti = tile_info(args, t, BN, TILE_M, KB);
       for (int j = 0; j < ti.nk; ++j, ++it) {
         if (it % kSplitGroups != grp) continue;
-        const int s = it % STAGES, round = it / STAGES;
-        // Warp-uniform decision: the warp stays converged for the arrival below.
-        const bool landed = wait_bar(&full[s], round & 1, abort_flag);
+        const int s = it % RST, l = it % LST;
+        // Warp-uniform decision: the warp stays converged for the arrival below. The raw slot
+        // has landed, and the lo slot (and its TMEM columns) is free again: its last user,
+        // k-block it - LST, released its raw slot with the same commit (one commit per k-block
+        // serves both rings; LST <= RST).
+        const int prev = it - LST;
+        const bool landed =
+            wait_bar(&full[s], (it / RST) & 1, abort_flag) &&
+            (prev < 0 || wait_bar(&empty[prev % RST], (prev / RST) & 1, abort_flag));
         if (!__all_sync(0xffffffffu, landed)) { stop = true; break; }
-        uint8_t* st = smem + s * L::STAGE;
+        uint8_t* st = raw_ring + s * L::RAW;
+        uint8_t* lo = lo_ring + l * L::LO;
         auto lo_of = [](float x) {
           return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
         };
@@ -368,11 +403,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           lo[i] = make_float4(lo_of(v.x), lo_of(v.y), lo_of(v.z), lo_of(v.w));
         };
         if (!args.raw) {
-          const float4* b_raw = reinterpret_cast<const float4*>(st + L::B_OFF);
-          float4* b_lo = reinterpret_cast<float4*>(st + L::B_OFF + L::B_BYTES);
+          const float4* b_raw = reinterpret_cast<const float4*>(st + L::A_BYTES);
+          float4* b_lo = reinterpret_cast<float4*>(lo + (ATM ? 0u : L::A_BYTES));
           if (!ATM) {
             const float4* a_raw = reinterpret_cast<const float4*>(st);
-            float4* a_lo = reinterpret_cast<float4*>(st + L::A_BYTES);
+            float4* a_lo = reinterpret_cast<float4*>(lo);
 #pragma unroll
             for (int i = t0; i < (int)(L::A_BYTES / 16); i += kGroupThreads) lo4(a_raw, a_lo, i);
           }
@@ -398,7 +433,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const float4 v1 =
                 *reinterpret_cast<const float4*>(arow + (((2 * u + 1) ^ sw) << 4));
             const uint32_t taddr = tmem + ((uint32_t)(32 * qr) << 16) + L::ACC_COLS +
-                                   (uint32_t)(s * 2 * KB + u * 8);
+                                   (uint32_t)(l * 2 * KB + u * 8);
             const uint32_t hi[8] = {__float_as_uint(v0.x), __float_as_uint(v0.y),
                                     __float_as_uint(v0.z), __float_as_uint(v0.w),
                                     __float_as_uint(v1.x), __float_as_uint(v1.y),
@@ -421,7 +456,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         // forwards its stage to the even CTA.
         fence_proxy_async_smem();
         __syncwarp();
-        if ((threadIdx.x & 31) == 0) mbar_arrive(&split[s]);
+        if ((threadIdx.x & 31) == 0) mbar_arrive(&split[l]);
       }
     }
   } else if (warp >= kEpiWarp0) {
@@ -753,9 +788,9 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
   // K-major: the MMAs then read only B from shared memory.
   constexpr bool ATM = !PAIR && !A_MN && BN <= 128;
   using L = Layout<BN, PAIR, ATM>;
-  constexpr int STAGES = stages_for<BN, PAIR, ATM>();
+  static_assert(L::RST >= 3 && L::LST >= 2, "GEMM rings too shallow");
   constexpr int TILE_M = PAIR ? 2 * BM : BM;
-  auto kernel = gemm_tc_kernel<BN, STAGES, A_MN, B_MN, PAIR, ATM>;
+  auto kernel = gemm_tc_kernel<BN, A_MN, B_MN, PAIR, ATM>;
   CUtensorMap ta, tb;
   int rc;
   // A: K-major = m rows of k; MN-major = k rows of m. Likewise B with n. An operand shared
@@ -782,7 +817,7 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
     rc = make_map(&tb, p.b, p.k, p.n, p.ldb, bh, p.stride_bh, bn, p.stride_b, KB, L::B_ROWS,
                   kSwK);
   if (rc != TG_OK) return rc;
-  const size_t smem = STAGES * L::STAGE + kEpiBytes + 1024 + 512;
+  const size_t smem = L::RINGS + kEpiBytes + 1024 + 512;
   static bool configured = false;
   static int max_pairs = 0;
   if (!configured) {
@@ -975,6 +1010,17 @@ int gemm_tc_f32(const GemmArgs<float>& p, cudaStream_t stream) {
         splits = (int)sp;
       }
     }
+  }
+  // TG_GEMM_BN=64|128|256 pins the tile width (unsplit) for kernel probes.
+  static int forced_bn = -1;
+  if (forced_bn < 0) {
+    const char* e = getenv("TG_GEMM_BN");
+    const int v = e ? atoi(e) : 0;
+    forced_bn = (v == 64 || v == 128 || v == 256) ? v : 0;
+  }
+  if (forced_bn && !(p.a_fold > 0 && p.a_fold % bk_of(forced_bn))) {
+    best = forced_bn;
+    splits = 1;
   }
   // CTA pairs (256-row tiles, cta_group::2) for plain single products when their makespan
   // wins. A pair tile is two single tiles' work on two SMs; with the B-operand traffic per SM
