@@ -144,6 +144,56 @@ __global__ void row_dot_kernel(View a, View b, float* __restrict__ out, int64_t 
   }
 }
 
+// The same with 16-byte loads: G = D / 4 lanes per row (D a multiple of 4, at most 128; the
+// tensor-core path's strides are 16-byte multiples), 32 / G rows per warp, the row's dot
+// product reduced within its lane group.
+template <int G>
+__global__ void __launch_bounds__(256)
+row_dot_vec4_kernel(View a, View b, float* __restrict__ out, int64_t H, int64_t T, int64_t rows) {
+  constexpr int kRowsPerWarp = 32 / G;
+  const int lane = threadIdx.x & 31, sub = lane / G, c = lane % G;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+       w * kRowsPerWarp < rows; w += warps) {
+    const int64_t r = w * kRowsPerWarp + sub;
+    float acc = 0.f;
+    if (r < rows) {
+      const int64_t t = r % T, bh = r / T, bi = bh / H, hi = bh % H;
+      const float4 x = reinterpret_cast<const float4*>(a.p + bi * a.sb + hi * a.sh + t * a.st)[c];
+      const float4 y = reinterpret_cast<const float4*>(b.p + bi * b.sb + hi * b.sh + t * b.st)[c];
+      acc = (x.x * y.x + x.y * y.y) + (x.z * y.z + x.w * y.w);
+    }
+#pragma unroll
+    for (int o = G / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (r < rows && c == 0) out[r] = acc;
+  }
+}
+
+int row_dot(View dO, View O, float* delta, const Plan& p, cudaStream_t st) {
+  const int64_t rows = p.BH * p.Tq;
+  const bool vec = p.D % 4 == 0 && p.D <= 128 &&
+                   (reinterpret_cast<uintptr_t>(dO.p) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(O.p) & 15) == 0;
+  if (!vec) {
+    row_dot_kernel<<<grid_for(rows * 32, 256), 256, 0, st>>>(dO, O, delta, p.H, p.Tq, p.D, rows);
+    return check_launch("attention delta");
+  }
+  const int g = (int)(p.D / 4);
+  const int64_t per_warp = 32 / (g >= 32 ? 32 : (g >= 16 ? 16 : (g >= 8 ? 8 : (g >= 4 ? 4 : (g >= 2 ? 2 : 1)))));
+  const unsigned grid = (unsigned)grid_for((rows + per_warp - 1) / per_warp * 32, 256);
+  switch (g) {
+    case 32: row_dot_vec4_kernel<32><<<grid, 256, 0, st>>>(dO, O, delta, p.H, p.Tq, rows); break;
+    case 16: row_dot_vec4_kernel<16><<<grid, 256, 0, st>>>(dO, O, delta, p.H, p.Tq, rows); break;
+    case 8: row_dot_vec4_kernel<8><<<grid, 256, 0, st>>>(dO, O, delta, p.H, p.Tq, rows); break;
+    case 4: row_dot_vec4_kernel<4><<<grid, 256, 0, st>>>(dO, O, delta, p.H, p.Tq, rows); break;
+    case 2: row_dot_vec4_kernel<2><<<grid, 256, 0, st>>>(dO, O, delta, p.H, p.Tq, rows); break;
+    case 1: row_dot_vec4_kernel<1><<<grid, 256, 0, st>>>(dO, O, delta, p.H, p.Tq, rows); break;
+    default:
+      row_dot_kernel<<<grid_for(rows * 32, 256), 256, 0, st>>>(dO, O, delta, p.H, p.Tq, p.D, rows);
+  }
+  return check_launch("attention delta");
+}
+
 View score_view(const Plan& p, const float* base) {
   return View{base, p.H * p.Tq * p.ldS, p.Tq * p.ldS, p.ldS};
 }
@@ -255,8 +305,7 @@ int attention_tc_backward(const tg_attn_shape* s, const float* q, const float* k
   const View dV{dv, s->v_sb, s->v_sh, s->v_st};
   const View Sv = score_view(p, S), dPv = score_view(p, dP);
   int rc;
-  row_dot_kernel<<<grid_for(rows * 32, 256), 256, 0, st>>>(dO, O, delta, p.H, p.Tq, p.D, rows);
-  if ((rc = check_launch("attention delta"))) return rc;
+  if ((rc = row_dot(dO, O, delta, p, st))) return rc;
   const int skip = causal ? GEMM_K_SKIP_UPPER : GEMM_K_FULL;
   if (flash_fwd_supported(s)) {
     // Both score products on chip, P and dS written once (heads of 32 / 64).

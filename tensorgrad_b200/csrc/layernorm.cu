@@ -7,6 +7,7 @@
 // each block reduces its warps' per-lane sums in shared memory and writes one partial row to
 // `scratch`; a second kernel sums the partial rows in a fixed order (deterministic), 32
 // columns x 8 row groups per block.
+#include <algorithm>
 #include <initializer_list>
 
 #include "common.cuh"
@@ -196,8 +197,12 @@ ln_fwd_vec4(const float* __restrict__ x, const float* __restrict__ w,
   }
 }
 
+// The fp32 VJP with 16-byte rows. The weight/bias column sums accumulate in shared memory
+// (each warp its own pair of rows there), not in registers: that keeps a thread near 64
+// registers, so three or four blocks share an SM and more rows are in flight (a warp's loads
+// of one row are its only memory-level parallelism). Up to kMaxPartialsVec blocks.
 template <int NV>
-__global__ void __launch_bounds__(kWarps * 32)
+__global__ void __launch_bounds__(kWarps * 32, 3)
 ln_bwd_vec4(const float* __restrict__ g, const float* __restrict__ x,
             const float* __restrict__ w, const float* __restrict__ mean_in,
             const float* __restrict__ rstd_in, float* __restrict__ gx,
@@ -209,36 +214,43 @@ ln_bwd_vec4(const float* __restrict__ g, const float* __restrict__ x,
   const int64_t nwarps = (int64_t)gridDim.x * kWarps;
   const int nv = cols >> 2;
   const float4* w4 = reinterpret_cast<const float4*>(w);
-  float4 aw[NV], ab[NV];
-#pragma unroll
-  for (int j = 0; j < NV; ++j) aw[j] = ab[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4* acc_w = reinterpret_cast<float4*>(sh + (wid * 2 + 0) * cols);
+  float4* acc_b = reinterpret_cast<float4*>(sh + (wid * 2 + 1) * cols);
+  if (part_w) {
+    for (int i = lane; i < nv; i += 32) acc_w[i] = acc_b[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   for (int64_t r = warp0; r < rows; r += nwarps) {
     const float4* xr = reinterpret_cast<const float4*>(x + r * cols);
     const float4* gr = reinterpret_cast<const float4*>(g + r * cols);
     const float mean = mean_in[r], rstd = rstd_in[r];
-    float4 xh[NV], gh[NV];
+    float4 xv[NV], gv[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int i = lane + 32 * j;
+      xv[j] = i < nv ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      gv[j] = i < nv ? gr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       const int i = lane + 32 * j;
-      if (i < nv) {
-        const float4 xv = xr[i], gv = gr[i];
-        xh[j] = make_float4((xv.x - mean) * rstd, (xv.y - mean) * rstd, (xv.z - mean) * rstd,
-                            (xv.w - mean) * rstd);
-        aw[j].x += gv.x * xh[j].x; aw[j].y += gv.y * xh[j].y;
-        aw[j].z += gv.z * xh[j].z; aw[j].w += gv.w * xh[j].w;
-        ab[j].x += gv.x; ab[j].y += gv.y; ab[j].z += gv.z; ab[j].w += gv.w;
-        if (w) {
-          const float4 ww = w4[i];
-          gh[j] = make_float4(gv.x * ww.x, gv.y * ww.y, gv.z * ww.z, gv.w * ww.w);
-        } else {
-          gh[j] = gv;
-        }
-      } else {
-        xh[j] = gh[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      // xv becomes xhat, gv becomes g * w (the column sums take the raw g first).
+      xv[j] = make_float4((xv[j].x - mean) * rstd, (xv[j].y - mean) * rstd,
+                          (xv[j].z - mean) * rstd, (xv[j].w - mean) * rstd);
+      if (part_w && i < nv) {
+        float4 a = acc_w[i], b = acc_b[i];
+        a.x += gv[j].x * xv[j].x; a.y += gv[j].y * xv[j].y;
+        a.z += gv[j].z * xv[j].z; a.w += gv[j].w * xv[j].w;
+        b.x += gv[j].x; b.y += gv[j].y; b.z += gv[j].z; b.w += gv[j].w;
+        acc_w[i] = a;
+        acc_b[i] = b;
       }
-      s1 += sum4(gh[j]);
-      s2 += (gh[j].x * xh[j].x + gh[j].y * xh[j].y) + (gh[j].z * xh[j].z + gh[j].w * xh[j].w);
+      if (w && i < nv) {
+        const float4 ww = w4[i];
+        gv[j] = make_float4(gv[j].x * ww.x, gv[j].y * ww.y, gv[j].z * ww.z, gv[j].w * ww.w);
+      }
+      s1 += sum4(gv[j]);
+      s2 += (gv[j].x * xv[j].x + gv[j].y * xv[j].y) + (gv[j].z * xv[j].z + gv[j].w * xv[j].w);
     }
     if (gx) {
       const float m1 = warp_sum(s1) / (float)cols, m2 = warp_sum(s2) / (float)cols;
@@ -247,22 +259,14 @@ ln_bwd_vec4(const float* __restrict__ g, const float* __restrict__ x,
       for (int j = 0; j < NV; ++j) {
         const int i = lane + 32 * j;
         if (i < nv)
-          gxr[i] = make_float4(rstd * (gh[j].x - m1 - xh[j].x * m2),
-                               rstd * (gh[j].y - m1 - xh[j].y * m2),
-                               rstd * (gh[j].z - m1 - xh[j].z * m2),
-                               rstd * (gh[j].w - m1 - xh[j].w * m2));
+          gxr[i] = make_float4(rstd * (gv[j].x - m1 - xv[j].x * m2),
+                               rstd * (gv[j].y - m1 - xv[j].y * m2),
+                               rstd * (gv[j].z - m1 - xv[j].z * m2),
+                               rstd * (gv[j].w - m1 - xv[j].w * m2));
       }
     }
   }
   if (!part_w) return;
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const int i = lane + 32 * j;
-    if (i < nv) {
-      reinterpret_cast<float4*>(sh + (wid * 2 + 0) * cols)[i] = aw[j];
-      reinterpret_cast<float4*>(sh + (wid * 2 + 1) * cols)[i] = ab[j];
-    }
-  }
   ln_block_partials<float>(sh, part_w, part_b, cols);
 }
 
@@ -297,9 +301,61 @@ ln_final_kernel(const T* __restrict__ part_w, const T* __restrict__ part_b, T* _
   }
 }
 
+// fp32 partial rows of a multiple of 4 columns: a block covers 32 columns as 8 float4 lanes
+// by 32 row groups (each group sums every 32nd partial row, four independent chains), then the
+// 32 group sums are added in order. Four times the row parallelism of the scalar kernel: its
+// threads are latency-bound on the serial partial-row loads.
+__global__ void __launch_bounds__(256)
+ln_final_vec4(const float4* __restrict__ part_w, const float4* __restrict__ part_b,
+              float* __restrict__ gw, float* __restrict__ gb, int nparts, int cols) {
+  __shared__ float4 sw_sh[32][8], sb_sh[32][8];
+  const int q = threadIdx.x & 7, grp = threadIdx.x >> 3;
+  const int nq = cols >> 2, cq = blockIdx.x * 8 + q;
+  float4 w0 = make_float4(0.f, 0.f, 0.f, 0.f), w1 = w0, b0 = w0, b1 = w0;
+  if (cq < nq) {
+    int i = grp;
+    for (; i + 32 < nparts; i += 64) {
+      const float4 a = part_w[(int64_t)i * nq + cq], a2 = part_w[(int64_t)(i + 32) * nq + cq];
+      const float4 b = part_b[(int64_t)i * nq + cq], b2 = part_b[(int64_t)(i + 32) * nq + cq];
+      w0.x += a.x; w0.y += a.y; w0.z += a.z; w0.w += a.w;
+      w1.x += a2.x; w1.y += a2.y; w1.z += a2.z; w1.w += a2.w;
+      b0.x += b.x; b0.y += b.y; b0.z += b.z; b0.w += b.w;
+      b1.x += b2.x; b1.y += b2.y; b1.z += b2.z; b1.w += b2.w;
+    }
+    if (i < nparts) {
+      const float4 a = part_w[(int64_t)i * nq + cq], b = part_b[(int64_t)i * nq + cq];
+      w0.x += a.x; w0.y += a.y; w0.z += a.z; w0.w += a.w;
+      b0.x += b.x; b0.y += b.y; b0.z += b.z; b0.w += b.w;
+    }
+  }
+  sw_sh[grp][q] = make_float4(w0.x + w1.x, w0.y + w1.y, w0.z + w1.z, w0.w + w1.w);
+  sb_sh[grp][q] = make_float4(b0.x + b1.x, b0.y + b1.y, b0.z + b1.z, b0.w + b1.w);
+  __syncthreads();
+  if (grp == 0 && cq < nq) {
+    float4 tw = make_float4(0.f, 0.f, 0.f, 0.f), tb = tw;
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) {
+      const float4 a = sw_sh[k][q], b = sb_sh[k][q];
+      tw.x += a.x; tw.y += a.y; tw.z += a.z; tw.w += a.w;
+      tb.x += b.x; tb.y += b.y; tb.z += b.z; tb.w += b.w;
+    }
+    if (gw) reinterpret_cast<float4*>(gw)[cq] = tw;
+    if (gb) reinterpret_cast<float4*>(gb)[cq] = tb;
+  }
+}
+
 int ln_blocks(int64_t rows) {
   int64_t b = (rows + kWarps - 1) / kWarps;
   if (b > kMaxPartials) b = kMaxPartials;
+  if (b < 1) b = 1;
+  return (int)b;
+}
+
+// The vector VJP's grid: three blocks per SM (its occupancy), each warp a row at a time.
+constexpr int kMaxPartialsVec = 3 * 148;
+int ln_blocks_vec(int64_t rows) {
+  int64_t b = (rows + kWarps - 1) / kWarps;
+  if (b > kMaxPartialsVec) b = kMaxPartialsVec;
   if (b < 1) b = 1;
   return (int)b;
 }
@@ -354,7 +410,7 @@ template <int NV>
 int ln_backward_vec(const float* g, const float* x, const float* w, const float* mean,
                     const float* rstd, float* gx, float* gw, float* gb, int64_t rows, int cols,
                     void* scratch, cudaStream_t s) {
-  const int nb = ln_blocks(rows);
+  const int nb = ln_blocks_vec(rows);
   float* part_w = nullptr;
   float* part_b = nullptr;
   if (gw || gb) {
@@ -366,7 +422,11 @@ int ln_backward_vec(const float* g, const float* x, const float* w, const float*
   if (rc) return rc;
   ln_bwd_vec4<NV><<<nb, kWarps * 32, smem, s>>>(g, x, w, mean, rstd, gx, part_w, part_b, rows,
                                                 cols);
-  if (gw || gb)
+  if ((gw || gb) && aligned16(gw) && aligned16(gb) && aligned16(part_w))
+    ln_final_vec4<<<(cols + 31) / 32, 256, 0, s>>>(reinterpret_cast<const float4*>(part_w),
+                                                   reinterpret_cast<const float4*>(part_b), gw,
+                                                   gb, nb, cols);
+  else if (gw || gb)
     ln_final_kernel<float><<<(cols + 31) / 32, 256, 0, s>>>(part_w, part_b, gw, gb, nb, cols);
   return check_launch("layer_norm_backward", (gw || gb) ? 2 : 1);
 }
@@ -417,7 +477,8 @@ int tg_layer_norm_forward(int dtype, const void* x, const void* w, const void* b
 
 size_t tg_layer_norm_scratch_bytes(int dtype, int64_t rows, int64_t cols) {
   const size_t es = dtype == TG_F64 ? 8 : 4;
-  return (size_t)ln_blocks(rows) * 2 * (size_t)cols * es;
+  const int64_t nb = std::max<int64_t>(ln_blocks(rows), dtype == TG_F32 ? ln_blocks_vec(rows) : 0);
+  return (size_t)nb * 2 * (size_t)cols * es;
 }
 
 int tg_layer_norm_backward(int dtype, const void* g, const void* x, const void* w,
