@@ -20,7 +20,7 @@ from tensorgrad_b200.tensor import (
     tensor, zeros, zeros_like,
 )
 
-from tensorgrad_b200 import nn, optim, utils  # noqa: E402  (after the ops they use)
+from tensorgrad_b200 import func, nn, optim, utils  # noqa: E402  (after the ops they use)
 
 __version__ = "0.1.0"
 
@@ -34,7 +34,7 @@ def _lib_launches() -> int:
 __all__ = [
     "DeviceArray", "Tensor", "add", "arange", "autograd", "broadcast_to", "conv2d",
     "cross_entropy", "div",
-    "dropout", "embedding", "enable_grad", "exp", "flatten", "full", "gelu", "get_default_dtype",
+    "dropout", "embedding", "enable_grad", "exp", "flatten", "full", "func", "gelu", "get_default_dtype",
     "get_rng", "is_grad_enabled", "layer_norm", "linear", "log", "manual_seed", "matmul", "max", "max_pool2d",
     "mean", "min", "mse_loss", "mul", "neg", "nn", "no_grad", "ones", "ones_like", "optim",
     "permute", "pow", "profiler", "rand", "randn", "relu", "reshape", "set_default_dtype",

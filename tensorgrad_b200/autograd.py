@@ -7,9 +7,11 @@ contributions, accumulates leaf gradients, and frees each node's saved state unl
 ``retain_graph``. The walk runs on the host; the gradients it carries are device arrays and
 every sum is a device kernel. Error messages match the reference's, word for word.
 
-Differences, by design: ``create_graph=True`` (gradients that carry their own graph) is not
-available on the device path and raises ``NotImplementedError``; a hook lets data-parallel
-training start a gradient all-reduce the moment a leaf's gradient is final.
+``create_graph=True`` runs a second walk whose gradients are tensors built from differentiable
+device ops (each op's ``graph`` VJP), so they carry their own graph and can be differentiated
+again (double backward, ``func.hessian`` ...). Ops without a graph VJP (the fused attention,
+layer norm, convolution and recurrent kernels) raise ``NotImplementedError`` there. A hook lets
+data-parallel training start a gradient all-reduce the moment a leaf's gradient is final.
 """
 
 from __future__ import annotations
@@ -32,6 +34,9 @@ __all__ = ["BackwardFn", "Node", "backward", "enable_grad", "grad", "is_grad_ena
 #: VJP of one op on device arrays: given d(loss)/d(output) and, per input, whether its
 #: gradient is needed, return d(loss)/d(input_i) (``None`` where not needed).
 BackwardFn = Callable[["DeviceArray", tuple[bool, ...]], tuple["DeviceArray | None", ...]]
+#: The same VJP written with differentiable tensor ops: ``graph(g, out, need)`` with the
+#: output tensor ``out``; used when gradients must carry a graph (``create_graph=True``).
+GraphFn = Callable[["Tensor", "Tensor", tuple[bool, ...]], tuple["Tensor | None", ...]]
 GradOutputs: TypeAlias = "Tensor | np.ndarray | Sequence[Tensor | np.ndarray | None] | None"
 
 _R = TypeVar("_R")
@@ -86,12 +91,14 @@ class enable_grad(_GradModeContext):  # noqa: N801
 class Node:
     """A recorded op: its inputs and the VJP that maps the output gradient to theirs."""
 
-    __slots__ = ("_backward", "op", "parents")
+    __slots__ = ("_backward", "_graph", "op", "parents")
 
-    def __init__(self, op: str, parents: tuple[Tensor, ...], backward: BackwardFn) -> None:
+    def __init__(self, op: str, parents: tuple[Tensor, ...], backward: BackwardFn,
+                 graph: GraphFn | None = None) -> None:
         self.op = op
         self.parents = parents
         self._backward: BackwardFn | None = backward
+        self._graph: GraphFn | None = graph
 
     @property
     def released(self) -> bool:
@@ -115,8 +122,9 @@ class Node:
         return self._backward(grad, need)
 
     def release(self) -> None:
-        """Drop the closure (and the device buffers it saved) and the parent references."""
+        """Drop the closures (and the device buffers they saved) and the parent references."""
         self._backward = None
+        self._graph = None
         self.parents = ()
 
     def __repr__(self) -> str:
@@ -200,7 +208,10 @@ def _run_backward(
     *,
     retain_graph: bool,
     targets: Sequence[Tensor] | None,
-) -> dict[int, DeviceArray]:
+    create_graph: bool = False,
+) -> dict[int, Any]:
+    if create_graph:
+        return _graph_pass(roots, seeds, retain_graph, targets)
     prof = _profiler.active()
     if prof is None:
         return _backward_pass(roots, seeds, retain_graph, targets, None)
@@ -271,6 +282,71 @@ def _backward_pass(
     return captured
 
 
+def _graph_pass(
+    roots: Sequence[Tensor],
+    seeds: Sequence[Any],
+    retain_graph: bool,
+    targets: Sequence[Tensor] | None,
+) -> dict[int, Tensor]:
+    """The walk of ``_backward_pass`` with tensor gradients built from differentiable ops
+    (grad mode on), so every gradient it produces has a graph of its own. A leaf's gradient is
+    then a plain tensor (not a slot of a flat arena): ``leaf.grad = leaf.grad + g``."""
+    from tensorgrad_b200.tensor import Tensor
+
+    order = _topological_order(roots)
+    target_ids = None if targets is None else {id(t) for t in targets}
+    live = None if target_ids is None else _leads_to(order, target_ids)
+    captured: dict[int, Tensor] = {}
+    with enable_grad():
+        pending: dict[int, Tensor] = {}
+        for root, seed in zip(roots, seeds, strict=True):
+            # A tensor seed keeps its own graph (e.g. the dummy cotangent of a forward-mode
+            # product, which is differentiated against afterwards).
+            g0 = seed if isinstance(seed, Tensor) else Tensor._wrap(seed)
+            prev = pending.get(id(root))
+            pending[id(root)] = g0 if prev is None else prev + g0
+        for t in reversed(order):
+            g = pending.pop(id(t), None)
+            if g is None:
+                continue
+            node = t._node
+            if target_ids is not None:
+                if id(t) in target_ids:
+                    captured[id(t)] = g
+            elif node is None or t._retains_grad:
+                t.grad = g if t._grad is None else t._grad + g
+            if node is None:
+                continue
+            if node._backward is None:
+                raise node._freed_error()
+            parents = node.parents
+            need = tuple([p._requires_grad and (live is None or id(p) in live)
+                          for p in parents])
+            if not any(need):
+                continue
+            if node._graph is None:
+                raise NotImplementedError(
+                    f"create_graph=True: op '{node.op}' has no differentiable VJP on the device")
+            grads = node._graph(g, t, need)
+            if len(grads) != len(parents):
+                raise RuntimeError(
+                    f"op '{node.op}' returned {len(grads)} gradients for {len(parents)} inputs"
+                )
+            for p, pg, wanted in zip(parents, grads, need, strict=True):
+                if pg is None or not wanted:
+                    continue
+                if pg.shape != p.shape:
+                    raise RuntimeError(
+                        f"op '{node.op}' produced a gradient of shape {pg.shape} "
+                        f"for an input of shape {p.shape}"
+                    )
+                prev = pending.get(id(p))
+                pending[id(p)] = pg if prev is None else prev + pg
+            if not retain_graph:
+                node.release()
+    return captured
+
+
 # ---------------------------------------------------------------------------- public API
 def _as_tensors(value: Any, what: str) -> tuple[Tensor, ...]:
     from tensorgrad_b200.tensor import Tensor
@@ -282,6 +358,19 @@ def _as_tensors(value: Any, what: str) -> tuple[Tensor, ...]:
         if not isinstance(item, Tensor):
             raise TypeError(f"{what} must be tensors, got {type(item).__name__}")
     return items
+
+
+def _graph_seeds(seeds: list[DeviceArray], grad_outputs: GradOutputs) -> list[Any]:
+    """For ``create_graph``: the checked seeds, with every seed given as a tensor that
+    requires grad passed as that tensor (its graph kept)."""
+    from tensorgrad_b200.tensor import Tensor
+
+    if grad_outputs is None or isinstance(grad_outputs, Tensor | np.ndarray):
+        given: list[Any] = [grad_outputs]
+    else:
+        given = list(grad_outputs)
+    return [g if isinstance(g, Tensor) and g.requires_grad and g.dtype == s.dtype else s
+            for g, s in zip(given, seeds, strict=False)] + seeds[len(given):]
 
 
 def _seeds(outputs: tuple[Tensor, ...], grad_outputs: GradOutputs) -> list[DeviceArray]:
@@ -318,28 +407,24 @@ def _seeds(outputs: tuple[Tensor, ...], grad_outputs: GradOutputs) -> list[Devic
     return seeds
 
 
-def _no_create_graph(create_graph: bool) -> None:
-    if create_graph:
-        raise NotImplementedError(
-            "create_graph=True (differentiable gradients) is not available on the device "
-            "backward path"
-        )
-
-
 def backward(
     tensors: Tensor | Sequence[Tensor],
     grad_tensors: GradOutputs = None,
     retain_graph: bool | None = None,
     create_graph: bool = False,
 ) -> None:
-    """Accumulate d(sum of ``tensors``)/d(leaf) into the ``.grad`` of every leaf."""
-    _no_create_graph(create_graph)
+    """Accumulate d(sum of ``tensors``)/d(leaf) into the ``.grad`` of every leaf; with
+    ``create_graph`` the accumulated gradients carry a graph (``retain_graph`` then defaults
+    to True, as in the reference)."""
     outputs = _as_tensors(tensors, "tensors")
     for out in outputs:
         if not out.requires_grad:
             raise RuntimeError("backward() called on a tensor that does not require grad")
-    seeds = _seeds(outputs, grad_tensors)
-    _run_backward(outputs, seeds, retain_graph=bool(retain_graph), targets=None)
+    seeds: list[Any] = _seeds(outputs, grad_tensors)
+    if create_graph:
+        seeds = _graph_seeds(seeds, grad_tensors)
+    keep = create_graph if retain_graph is None else bool(retain_graph)
+    _run_backward(outputs, seeds, retain_graph=keep, targets=None, create_graph=create_graph)
 
 
 def grad(
@@ -353,7 +438,6 @@ def grad(
     """Gradients of ``outputs`` with respect to ``inputs``, returned instead of accumulated."""
     from tensorgrad_b200.tensor import Tensor
 
-    _no_create_graph(create_graph)
     outs = _as_tensors(outputs, "outputs")
     ins = _as_tensors(inputs, "inputs")
     for i, out in enumerate(outs):
@@ -362,8 +446,12 @@ def grad(
     for i, inp in enumerate(ins):
         if not inp.requires_grad:
             raise RuntimeError(f"input {i} does not require grad")
-    seeds = _seeds(outs, grad_outputs)
-    captured = _run_backward(outs, seeds, retain_graph=bool(retain_graph), targets=ins)
+    seeds: list[Any] = _seeds(outs, grad_outputs)
+    if create_graph:
+        seeds = _graph_seeds(seeds, grad_outputs)
+    keep = create_graph if retain_graph is None else bool(retain_graph)
+    captured = _run_backward(outs, seeds, retain_graph=keep, targets=ins,
+                             create_graph=create_graph)
     result: list[Tensor | None] = []
     for i, inp in enumerate(ins):
         g = captured.get(id(inp))
@@ -374,6 +462,8 @@ def grad(
                     "to get None for it instead"
                 )
             result.append(None)
+        elif create_graph:
+            result.append(g)  # a tensor with its own graph
         else:
             # A fresh array: the engine may hand back aliases of other gradients.
             result.append(Tensor._wrap(g.astype(inp.dtype, copy=True)))

@@ -9,7 +9,7 @@ import numpy as np
 
 from tensorgrad_b200 import device
 from tensorgrad_b200._lib import check, int64_array, int_array, lib
-from tensorgrad_b200.autograd import BackwardFn, Node, is_grad_enabled
+from tensorgrad_b200.autograd import BackwardFn, GraphFn, Node, is_grad_enabled
 from tensorgrad_b200.device import DeviceArray, dtype_code
 from tensorgrad_b200.tensor import Tensor
 
@@ -32,14 +32,20 @@ def coerce_pair(a: Any, b: Any) -> tuple[Tensor, Tensor]:
 
 
 def make_result(data: DeviceArray, parents: tuple[Tensor, ...], backward: BackwardFn,
-                op: str) -> Tensor:
+                op: str, graph: GraphFn | None = None) -> Tensor:
     """Wrap an op's output, recording a graph node if any input requires grad
-    (ops/_util.py:28-46). ``backward`` is the VJP on device arrays."""
+    (ops/_util.py:28-46). ``backward`` is the VJP on device arrays; ``graph`` (optional) the
+    same VJP in differentiable tensor ops, for ``create_graph=True``."""
     out = Tensor._wrap(data)
     if is_grad_enabled() and any(p._requires_grad for p in parents):
         out._requires_grad = True
-        out._node = Node(op, parents, backward)
+        out._node = Node(op, parents, backward, graph)
     return out
+
+
+def constant(data: DeviceArray) -> Tensor:
+    """A tensor outside every graph (masks and saved values inside graph VJPs)."""
+    return Tensor._wrap(data)
 
 
 def unbroadcast(grad: DeviceArray, shape: tuple[int, ...]) -> DeviceArray:

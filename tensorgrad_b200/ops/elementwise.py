@@ -5,17 +5,20 @@ Forward values and VJPs follow ops/elementwise.py:43-343; each runs as one devic
 
 from __future__ import annotations
 
+import math
 from typing import Any
 
 import numpy as np
 
 from tensorgrad_b200 import device
 from tensorgrad_b200._lib import (
-    ADD, DIV, EXP, F32, F64, LOG, MUL, NEG, POW, POWS, SIGMOID, SQRT, SUB, TANH, check, int64_array,
-    lib,
+    ADD, DIV, EXP, F32, F64, FILL, LOG, MUL, NEG, POW, POWS, SIGMOID, SQRT, SUB, TANH, check,
+    int64_array, lib,
 )
 from tensorgrad_b200.device import DeviceArray, dtype_code
-from tensorgrad_b200.ops._util import Need, as_tensor, coerce_pair, make_result, unbroadcast
+from tensorgrad_b200.ops._util import (
+    Need, as_tensor, coerce_pair, constant, make_result, unbroadcast,
+)
 from tensorgrad_b200.profiler import profiled
 from tensorgrad_b200.tensor import Tensor
 
@@ -88,6 +91,15 @@ def _unary_bwd(op: int, g: DeviceArray, x: DeviceArray | None, y: DeviceArray | 
     return out
 
 
+def _sum_to(g: Tensor, shape: tuple[int, ...]) -> Tensor:
+    """Differentiable sum of a gradient tensor down to an input's shape (graph VJPs)."""
+    if g.shape == tuple(shape):
+        return g
+    from tensorgrad_b200.ops.shape import sum_to
+
+    return sum_to(g, shape)
+
+
 def _float_input(t: Tensor) -> DeviceArray:
     return t.data if t.dtype.kind == "f" else cast_array(t.data, np.dtype(np.float64))
 
@@ -101,7 +113,10 @@ def add(a: Any, b: Any) -> Tensor:
     def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray | None, DeviceArray | None]:
         return (unbroadcast(g, sa) if need[0] else None, unbroadcast(g, sb) if need[1] else None)
 
-    return make_result(binary_array(ta.data, tb.data, ADD), (ta, tb), backward, "add")
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor | None, Tensor | None]:
+        return (_sum_to(g, sa) if need[0] else None, _sum_to(g, sb) if need[1] else None)
+
+    return make_result(binary_array(ta.data, tb.data, ADD), (ta, tb), backward, "add", graph)
 
 
 @profiled("sub")
@@ -114,7 +129,10 @@ def sub(a: Any, b: Any) -> Tensor:
         return (unbroadcast(g, sa) if need[0] else None,
                 unbroadcast(scale_array(g, -1.0), sb) if need[1] else None)
 
-    return make_result(binary_array(ta.data, tb.data, SUB), (ta, tb), backward, "sub")
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor | None, Tensor | None]:
+        return (_sum_to(g, sa) if need[0] else None, _sum_to(neg(g), sb) if need[1] else None)
+
+    return make_result(binary_array(ta.data, tb.data, SUB), (ta, tb), backward, "sub", graph)
 
 
 @profiled("mul")
@@ -126,7 +144,11 @@ def mul(a: Any, b: Any) -> Tensor:
         return (unbroadcast(binary_array(g, tb.data, MUL), ta.shape) if need[0] else None,
                 unbroadcast(binary_array(g, ta.data, MUL), tb.shape) if need[1] else None)
 
-    return make_result(binary_array(ta.data, tb.data, MUL), (ta, tb), backward, "mul")
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor | None, Tensor | None]:
+        return (_sum_to(mul(g, tb), ta.shape) if need[0] else None,
+                _sum_to(mul(g, ta), tb.shape) if need[1] else None)
+
+    return make_result(binary_array(ta.data, tb.data, MUL), (ta, tb), backward, "mul", graph)
 
 
 @profiled("div")
@@ -143,7 +165,11 @@ def div(a: Any, b: Any) -> Tensor:
             gb = unbroadcast(scale_array(t, -1.0), tb.shape)
         return ga, gb
 
-    return make_result(out, (ta, tb), backward, "div")
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor | None, Tensor | None]:
+        return (_sum_to(div(g, tb), ta.shape) if need[0] else None,
+                _sum_to(neg(div(mul(g, y), tb)), tb.shape) if need[1] else None)
+
+    return make_result(out, (ta, tb), backward, "div", graph)
 
 
 @profiled("neg")
@@ -154,7 +180,10 @@ def neg(a: Any) -> Tensor:
     def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
         return (scale_array(g, -1.0),)
 
-    return make_result(scale_array(ta.data, -1.0), (ta,), backward, "neg")
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
+        return (neg(g),)
+
+    return make_result(scale_array(ta.data, -1.0), (ta,), backward, "neg", graph)
 
 
 @profiled("pow")
@@ -169,7 +198,10 @@ def pow(base: Any, exponent: Any) -> Tensor:  # noqa: A001
         def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
             return (_unary_bwd(POWS, g, x, None, e),)
 
-        return make_result(_unary(x, POWS, e), (tb,), backward, "pow")
+        def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
+            return (mul(g, mul(pow(tb, e - 1.0), e)),)
+
+        return make_result(_unary(x, POWS, e), (tb,), backward, "pow", graph)
     tb, te = coerce_pair(base, exponent)
     out = binary_array(tb.data, te.data, POW)
 
@@ -180,7 +212,12 @@ def pow(base: Any, exponent: Any) -> Tensor:  # noqa: A001
         d = binary_array(binary_array(g, te.data, MUL), binary_array(tb.data, em1, POW), MUL)
         return unbroadcast(d, tb.shape), None
 
-    return make_result(out, (tb, te), backward2, "pow")
+    def graph2(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor | None, Tensor | None]:
+        if need[1]:
+            raise NotImplementedError("pow: gradient with respect to a tensor exponent")
+        return _sum_to(mul(mul(g, te), pow(tb, sub(te, 1.0))), tb.shape), None
+
+    return make_result(out, (tb, te), backward2, "pow", graph2)
 
 
 def _unary_op(name: str, op: int, use_out: bool) -> Any:
@@ -193,10 +230,28 @@ def _unary_op(name: str, op: int, use_out: bool) -> Any:
         def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
             return (_unary_bwd(op, g, None if use_out else x, out if use_out else None),)
 
-        return make_result(out, (ta,), backward, name)
+        def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
+            return (_unary_graph(op, g, ta, y),)
+
+        return make_result(out, (ta,), backward, name, graph)
 
     fn.__name__ = name
     return fn
+
+
+def _unary_graph(op: int, g: Tensor, x: Tensor, y: Tensor) -> Tensor:
+    """The unary VJPs in differentiable ops, from the input ``x`` or the output ``y``."""
+    if op == EXP:
+        return mul(g, y)
+    if op == LOG:
+        return div(g, x)
+    if op == SQRT:
+        return div(mul(g, 0.5), y)
+    if op == TANH:
+        return mul(g, sub(1.0, mul(y, y)))
+    if op == SIGMOID:
+        return mul(g, mul(y, sub(1.0, y)))
+    raise NotImplementedError(f"no differentiable VJP for unary op {op}")
 
 
 exp = _unary_op("exp", EXP, True)        # ops/elementwise.py:170-181
@@ -218,7 +273,11 @@ def relu(a: Any) -> Tensor:
                                    device.stream()), "relu backward")
         return (out,)
 
-    return make_result(_unary(x, 6), (ta,), backward, "relu")
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
+        # g times the constant mask (x > 0), the mask being the VJP of a ones gradient.
+        return (mul(g, constant(backward(_unary(x, FILL, 1.0), need)[0])),)
+
+    return make_result(_unary(x, 6), (ta,), backward, "relu", graph)
 
 
 @profiled("gelu")
@@ -237,7 +296,15 @@ def gelu(a: Any) -> Tensor:
                                    device.stream()), "gelu backward")
         return (gx,)
 
-    return make_result(out, (ta,), backward, "gelu")
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
+        # d gelu / dx = 0.5 (1 + t) + 0.5 x (1 - t^2) c (1 + 3 k x^2), t = tanh(c (x + k x^3)).
+        c, k = math.sqrt(2.0 / math.pi), 0.044715
+        x2 = mul(ta, ta)
+        t = tanh(mul(add(ta, mul(mul(x2, ta), k)), c))
+        slope = mul(mul(mul(ta, sub(1.0, mul(t, t))), add(mul(x2, 3.0 * k), 1.0)), 0.5 * c)
+        return (mul(g, add(mul(add(t, 1.0), 0.5), slope)),)
+
+    return make_result(out, (ta,), backward, "gelu", graph)
 
 
 @profiled("astype")
@@ -253,7 +320,10 @@ def astype(a: Any, dtype: Any) -> Tensor:
     def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
         return (g if g.dtype == source else cast_array(g, source),)
 
-    return make_result(out, (ta,), backward, "astype")
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
+        return (g if g.dtype == source else astype(g, source),)
+
+    return make_result(out, (ta,), backward, "astype", graph)
 
 
 # NEG kept for symmetry with the C enum (used by callers that negate in place).

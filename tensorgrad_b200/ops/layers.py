@@ -69,8 +69,21 @@ def linear(x: Any, weight: Any, bias: Any = None) -> Tensor:
             gx = cast_array(gx, tx.dtype)
         return (gx, gw) if not has_bias else (gx, gw, gb)
 
+    def graph(g: Tensor, out: Tensor, need: Need) -> tuple[Tensor | None, ...]:
+        # gx = g W, gW = g2^T x2 (leading axes flattened), gb = column sums of g2.
+        from tensorgrad_b200.ops.linalg import matmul
+        from tensorgrad_b200.ops.reduce import sum as tsum
+        from tensorgrad_b200.ops.shape import reshape, transpose
+
+        g2 = reshape(g, (rows, out_f))
+        gx = reshape(matmul(g2, tw), tx.shape) if need[0] else None
+        gw = matmul(transpose(g2, 0, 1), reshape(tx, (rows, in_f))) if need[1] else None
+        if not has_bias:
+            return gx, gw
+        return gx, gw, (tsum(g2, axis=0) if need[2] else None)
+
     parents = (tx, tw) if tb is None else (tx, tw, tb)
-    return make_result(y, parents, backward, "linear")
+    return make_result(y, parents, backward, "linear", graph)
 
 
 @profiled("layer_norm")

@@ -58,4 +58,11 @@ def matmul(a: Any, b: Any) -> Tensor:
             gb = unbroadcast(_bmm(af, g, 1, 0, k, n, m, nb).reshape((*batch, k, n)), tb.shape)
         return ga, gb
 
-    return make_result(out, (ta, tb), backward, "matmul")
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor | None, Tensor | None]:
+        from tensorgrad_b200.ops.shape import sum_to, transpose
+
+        ga = sum_to(matmul(g, transpose(tb, -1, -2)), ta.shape) if need[0] else None
+        gb = sum_to(matmul(transpose(ta, -1, -2), g), tb.shape) if need[1] else None
+        return ga, gb
+
+    return make_result(out, (ta, tb), backward, "matmul", graph)

@@ -84,7 +84,34 @@ def cross_entropy(logits: Any, target: Any, *, ignore_index: int = -100,
                                             device.stream()), "cross_entropy backward")
         return (grad if grad.dtype == tl.dtype else cast_array(grad, tl.dtype),)
 
-    return make_result(out, (tl,), backward, "cross_entropy")
+    host_targets = None if isinstance(dev_t, DeviceArray) else flat_t
+
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
+        # (softmax(x) - onehot) * valid * weight in differentiable ops: softmax as e / sum(e)
+        # with e = exp(x - lse), the saved log-sum-exp a constant shift; the one-hot rows
+        # (host targets) uploaded once.
+        from tensorgrad_b200.ops.elementwise import exp, mul, sub
+        from tensorgrad_b200.ops.shape import reshape
+
+        if host_targets is None:
+            raise NotImplementedError("create_graph=True: cross_entropy with device-resident "
+                                      "targets has no differentiable VJP; pass host targets")
+        keep = host_targets != ignore_index
+        onehot = np.zeros((rows, classes), dtype=x.dtype)
+        onehot[np.flatnonzero(keep), host_targets[keep]] = 1.0
+        x2 = reshape(tl, (rows, classes))
+        e = exp(sub(x2, Tensor._wrap(lse.reshape((rows, 1)))))
+        probs = e / reduce.sum(e, axis=-1, keepdims=True)
+        diff = mul(sub(probs, Tensor(onehot)), Tensor(keep.astype(x.dtype).reshape(rows, 1)))
+        if red == 2:
+            weight = reshape(g, (rows, 1))
+        elif red == 0:
+            weight = g / float(max(int(keep.sum()), 1))
+        else:
+            weight = g
+        return (reshape(mul(diff, weight), tl.shape),)
+
+    return make_result(out, (tl,), backward, "cross_entropy", graph)
 
 
 @profiled("mse_loss")

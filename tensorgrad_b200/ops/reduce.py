@@ -43,6 +43,13 @@ def expand_array(g: DeviceArray, shape: tuple[int, ...], axes: tuple[int, ...]) 
     return broadcast_array(g.reshape(_kept_shape(shape, axes)), shape)
 
 
+def _expand(g: Tensor, shape: tuple[int, ...], axes: tuple[int, ...]) -> Tensor:
+    """``expand_array`` in differentiable ops (the graph VJP of the reductions)."""
+    from tensorgrad_b200.ops.shape import broadcast_to, reshape
+
+    return broadcast_to(reshape(g, _kept_shape(shape, axes)), shape)
+
+
 def _drop(a: DeviceArray, axes: tuple[int, ...], keepdims: bool) -> DeviceArray:
     if keepdims:
         return a
@@ -59,7 +66,10 @@ def sum(a: Any, axis: Any = None, keepdims: bool = False) -> Tensor:  # noqa: A0
     def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
         return (expand_array(g, ta.shape, axes),)
 
-    return make_result(out, (ta,), backward, "sum")
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
+        return (_expand(g, ta.shape, axes),)
+
+    return make_result(out, (ta,), backward, "sum", graph)
 
 
 @profiled("mean")
@@ -74,7 +84,12 @@ def mean(a: Any, axis: Any = None, keepdims: bool = False) -> Tensor:
     def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
         return (expand_array(scale_array(g, 1.0 / n), ta.shape, axes),)
 
-    return make_result(out, (ta,), backward, "mean")
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
+        from tensorgrad_b200.ops.elementwise import mul
+
+        return (_expand(mul(g, 1.0 / n), ta.shape, axes),)
+
+    return make_result(out, (ta,), backward, "mean", graph)
 
 
 @profiled("var")

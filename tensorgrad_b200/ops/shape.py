@@ -58,7 +58,10 @@ def reshape(a: Any, shape: tuple[int, ...]) -> Tensor:
     def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
         return (g.reshape(src_shape),)
 
-    return make_result(out, (ta,), backward, "reshape")
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
+        return (reshape(g, src_shape),)
+
+    return make_result(out, (ta,), backward, "reshape", graph)
 
 
 def flatten(a: Any, start_axis: int = 0, end_axis: int = -1) -> Tensor:
@@ -82,7 +85,10 @@ def permute(a: Any, dims: tuple[int, ...]) -> Tensor:
     def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
         return (permute_array(g, inv),)
 
-    return make_result(permute_array(ta.data, perm), (ta,), backward, "permute")
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
+        return (permute(g, inv),)
+
+    return make_result(permute_array(ta.data, perm), (ta,), backward, "permute", graph)
 
 
 def transpose(a: Any, axis0: int, axis1: int) -> Tensor:
@@ -119,7 +125,10 @@ def broadcast_to(a: Any, shape: tuple[int, ...]) -> Tensor:
     def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
         return (unbroadcast(g, src),)
 
-    return make_result(broadcast_array(ta.data, shape), (ta,), backward, "broadcast_to")
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
+        return (sum_to(g, src),)
+
+    return make_result(broadcast_array(ta.data, shape), (ta,), backward, "broadcast_to", graph)
 
 
 def sum_to(a: Any, shape: tuple[int, ...]) -> Tensor:
@@ -132,7 +141,10 @@ def sum_to(a: Any, shape: tuple[int, ...]) -> Tensor:
     def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
         return (broadcast_array(g, target),)
 
-    return make_result(unbroadcast(ta.data, shape), (ta,), backward, "sum_to")
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
+        return (broadcast_to(g, target),)
+
+    return make_result(unbroadcast(ta.data, shape), (ta,), backward, "sum_to", graph)
 
 
 def _basic_view(shape: tuple[int, ...], itemsize: int, index: Any) -> tuple[int, tuple[int, ...], list[int]]:
@@ -168,7 +180,31 @@ def getitem(a: Any, index: Any) -> Tensor:
                      strides, shape, g.itemsize)
         return (gx,)
 
-    return make_result(out, (ta,), backward, "getitem")
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
+        return (_scatter(g, ta.shape, index),)
+
+    return make_result(out, (ta,), backward, "getitem", graph)
+
+
+def _scatter(g: Tensor, shape: tuple[int, ...], index: Any) -> Tensor:
+    """Zeros of ``shape`` with ``g`` at ``[index]``: getitem's VJP as a differentiable op (its
+    own VJP is getitem again), for gradients that carry a graph."""
+    gd = g.data
+    offset, view_shape, strides = _basic_view(shape, gd.itemsize, index)
+    out = device.zeros(shape, gd.dtype)
+    strided_copy(gd.ptr, device.contiguous_strides(view_shape), out.ptr + offset * gd.itemsize,
+                 strides, view_shape, gd.itemsize)
+
+    def backward(gg: DeviceArray, need: Need) -> tuple[DeviceArray]:
+        piece = device.empty(view_shape, gg.dtype)
+        strided_copy(gg.ptr + offset * gg.itemsize, strides, piece.ptr,
+                     device.contiguous_strides(view_shape), view_shape, gg.itemsize)
+        return (piece,)
+
+    def graph(gg: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
+        return (getitem(gg, index),)
+
+    return make_result(out, (g,), backward, "scatter", graph)
 
 
 @profiled("stack")
@@ -204,4 +240,8 @@ def stack(tensors: Any, axis: int = 0) -> Tensor:
             grads.append(gk)
         return tuple(grads)
 
-    return make_result(out, tuple(ts), backward, "stack")
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor | None, ...]:
+        lead = (slice(None),) * ax
+        return tuple(getitem(g, (*lead, k)) if need[k] else None for k in range(len(ts)))
+
+    return make_result(out, tuple(ts), backward, "stack", graph)

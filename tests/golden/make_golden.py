@@ -250,6 +250,51 @@ def run_generate() -> dict[str, np.ndarray]:
     return {"prompt": prompt, "greedy": greedy, "sampled": sampled, "logits": logits}
 
 
+def run_higher_order() -> dict[str, np.ndarray]:
+    """Differentiable gradients by the reference (float64): func.grad / hessian / hvp / jvp /
+    jacobian of small functions of elementwise, matrix and reduction ops, and a gradient
+    penalty (backward through an input gradient built with create_graph) on a small MLP with
+    cross entropy. Inputs regenerate from specs.higher_order_inputs."""
+    from tensorgrad import func
+    from tests.golden.specs import higher_order_inputs
+
+    tg.set_default_dtype(np.float64)
+    d = higher_order_inputs()
+    x, w, v, vw = (tg.Tensor(d[k]) for k in ("x", "w", "v", "vw"))
+
+    def f(x_, w_):
+        return (tg.tanh(x_ @ w_) ** 2).sum()
+
+    def g(x_):
+        return tg.sigmoid(x_ @ tg.Tensor(d["w"])).reshape(-1)
+
+    def h(x_):
+        return tg.mean(tg.exp(x_) / (x_ * x_ + 1.0)) + tg.log(x_ * x_ + 1.0).sum() \
+            + (tg.gelu(x_) * tg.Tensor(d["c"])).sum() + tg.sqrt(x_ * x_ + 2.0).sum()
+
+    out: dict[str, np.ndarray] = {}
+    gx, gw = func.grad(f, argnums=(0, 1))(x, w)
+    out["grad_x"], out["grad_w"] = np.array(gx.data), np.array(gw.data)
+    out["hess_x"] = np.array(func.hessian(f)(x, w).data)
+    _, (hx, hw) = func.hvp(f, (x, w), (v, vw))
+    out["hvp_x"], out["hvp_w"] = np.array(hx.data), np.array(hw.data)
+    _, jv = func.jvp(g, (x,), (v,))
+    out["jvp"] = np.array(jv.data)
+    out["jac"] = np.array(func.jacobian(g)(x).data)
+    out["hess_h"] = np.array(func.hessian(h)(x).data)
+    # Gradient penalty on an MLP: loss + sum(d loss / d input)^2, backward to the weights.
+    w1, b1, w2, b2 = (tg.Tensor(d[k], requires_grad=True) for k in ("w1", "b1", "w2", "b2"))
+    xin = tg.Tensor(d["xin"], requires_grad=True)
+    loss = tg.cross_entropy(tg.linear(tg.relu(tg.linear(xin, w1, b1)), w2, b2), d["labels"])
+    (gin,) = tg.autograd.grad(loss, [xin], create_graph=True)
+    total = loss + (gin * gin).sum()
+    total.backward()
+    out["penalty_total"] = np.asarray(total.item())
+    for k, t in (("w1", w1), ("b1", b1), ("w2", w2), ("b2", b2), ("xin", xin)):
+        out[f"penalty_grad_{k}"] = np.array(t.grad.data)
+    return out
+
+
 def main() -> None:
     jobs = {
         "gpt_small": lambda: run_gpt(GPT_SMALL),
@@ -261,6 +306,7 @@ def main() -> None:
         "gpt_dropout": lambda: run_gpt(GPT_DROPOUT),
         "dropout_masks": run_dropout_masks,
         "gpt_generate": run_generate,
+        "higher_order": run_higher_order,
     }
     names = sys.argv[1:] or [*jobs, "gpt_checkpoint"]
     for name in names:

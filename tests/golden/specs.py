@@ -85,3 +85,16 @@ def rnn_inputs(cell, steps, batch, inputs, hidden, seed):
     b_ih = 0.5 * rng.standard_normal(gates * hidden)
     b_hh = 0.5 * rng.standard_normal(gates * hidden)
     return x, h0, c0, w_ih, w_hh, b_ih, b_hh, rng
+
+
+def higher_order_inputs() -> dict[str, np.ndarray]:
+    """Seeded float64 inputs of the differentiable-gradient fixture (higher_order.npz)."""
+    rng = np.random.default_rng(61)
+    return {
+        "x": rng.standard_normal((3, 4)), "w": rng.standard_normal((4, 2)),
+        "v": rng.standard_normal((3, 4)), "vw": rng.standard_normal((4, 2)),
+        "c": rng.standard_normal((3, 4)),
+        "xin": rng.standard_normal((5, 6)), "labels": rng.integers(0, 3, size=5),
+        "w1": 0.5 * rng.standard_normal((7, 6)), "b1": 0.1 * rng.standard_normal(7),
+        "w2": 0.5 * rng.standard_normal((3, 7)), "b2": 0.1 * rng.standard_normal(3),
+    }
