@@ -30,7 +30,9 @@ enum tg_status {
   TG_ERR_CUDA = 2,        /* a CUDA runtime/launch error */
   TG_ERR_UNSUPPORTED = 3, /* shape/dtype combination not supported */
   TG_ERR_INDEX = 4,       /* id/target out of range (maps to IndexError) */
-  TG_ERR_TIMEOUT = 5      /* a bounded device-side wait ran out */
+  TG_ERR_TIMEOUT = 5,     /* a bounded device-side wait, or a collective, ran out of time */
+  TG_ERR_OOM = 6,         /* device memory exhausted */
+  TG_ERR_COMM = 7         /* a collective failed (the communicator reported an error) */
 };
 enum tg_dtype { TG_F32 = 0, TG_F64 = 1, TG_I64 = 2 /* casts only */ };
 
@@ -42,6 +44,27 @@ const char* tg_status_string(int status);
 int tg_last_error(char* buf, size_t len);
 /* SM count and compute capability of `device`. */
 int tg_device_info(int device, int* sm_count, int* cc_major, int* cc_minor);
+
+/* ------------------------------------------------------------------ memory and devices
+ * The reference keeps every array in host NumPy memory (no allocator of its own). Device
+ * buffers here come from the stream-ordered allocator: tg_malloc / tg_free order the
+ * allocation and the release on `stream`, and each device's pool keeps freed memory for reuse
+ * (no cudaMalloc once a step's working set has been seen). tg_host_alloc gives page-locked
+ * host memory (uploads from it run as asynchronous DMA). Events are timing-free. */
+int tg_malloc(void** ptr, size_t bytes, void* stream);
+int tg_free(void* ptr, void* stream);
+int tg_pool_stats(int device, uint64_t* reserved_bytes, uint64_t* used_bytes);
+int tg_host_alloc(void** ptr, size_t bytes);
+int tg_host_free(void* ptr);
+int tg_set_device(int device);
+int tg_get_device(int* device);
+/* Visible CUDA devices (0 when there is no driver or device; never an error). */
+int tg_device_count(int* count);
+int tg_event_create(void** event);
+int tg_event_record(void* event, void* stream);
+/* 1 once the work before the event has completed, 0 if not yet, < 0 on error. */
+int tg_event_query(void* event);
+int tg_event_destroy(void* event);
 
 /* ------------------------------------------------------------------ memory movement
  * The reference keeps every array in host memory; these move tensor storage and inputs
@@ -394,6 +417,27 @@ int tg_gru_backward(int dtype, int64_t T, int64_t B, int64_t I, int64_t H, const
                     const void* acts, const void* hn, const void* out, void* dx, void* dh0,
                     void* dw_ih, void* dw_hh, void* db_ih, void* db_hh, void* scratch,
                     void* stream);
+
+/* ------------------------------------------------------------------ data-parallel exchange
+ * The averaged gradient all-reduce of batch-sharded training (no reference counterpart: the
+ * reference is single-process), through NCCL loaded at run time from `library_path` (NULL:
+ * "libnccl.so.2"; an NCCL the process already loaded is reused). Communicators are created
+ * nonblocking; tg_comm_init polls their set-up against `timeout_s` (TG_ERR_TIMEOUT if a rank
+ * never joins). Collectives run on the communicator's own stream after the work queued on
+ * `stream`; tg_comm_join makes `stream` wait for them on the device; tg_comm_wait watches them
+ * from the host and, on an asynchronous NCCL error or when `timeout_s` passes, aborts the
+ * communicator and returns TG_ERR_COMM or TG_ERR_TIMEOUT (an aborted communicator stays
+ * unusable). tg_comm_destroy finalises within `timeout_s`, else aborts. */
+int tg_comm_load(const char* library_path);
+int tg_comm_nccl_version(int* version);
+int tg_comm_unique_id(void* out, size_t len);
+int tg_comm_init(int nranks, int rank, const void* unique_id, double timeout_s, void** comm);
+int tg_comm_all_reduce(void* comm, void* buf, size_t count, int dtype, int average, void* stream,
+                       double timeout_s);
+int tg_comm_join(void* comm, void* stream);
+int tg_comm_wait(void* comm, double timeout_s);
+int tg_comm_abort(void* comm);
+int tg_comm_destroy(void* comm, double timeout_s);
 
 /* ------------------------------------------------------------------ optimiser
  * optim/clip.py:15-31: total = sqrt(sum over tensors of sum(g^2)) accumulated in float64.

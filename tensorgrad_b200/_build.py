@@ -65,7 +65,7 @@ def build(verbose: bool = False) -> str:
         objs = list(pool.map(lambda s: _compile(s, verbose), sources))
     if not os.path.exists(LIB) or any(os.path.getmtime(o) > os.path.getmtime(LIB) for o in objs):
         tmp = LIB + ".tmp"
-        cmd = [_nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs]
+        cmd = [_nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs, "-ldl"]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"link of libtgb200.so failed:\n{res.stderr}")

@@ -22,7 +22,9 @@ _STATUS_ERRORS: dict[int, type[Exception]] = {
     2: RuntimeError,
     3: NotImplementedError,
     4: IndexError,
-    5: RuntimeError,
+    5: TimeoutError,
+    6: MemoryError,
+    7: RuntimeError,
 }
 
 
@@ -61,6 +63,27 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tg_memcpy_d2d": (c_int, [vp, vp, sz, vp]),
     "tg_memset_zero": (c_int, [vp, sz, vp]),
     "tg_stream_synchronize": (c_int, [vp]),
+    "tg_malloc": (c_int, [POINTER(c_void_p), sz, vp]),
+    "tg_free": (c_int, [vp, vp]),
+    "tg_pool_stats": (c_int, [c_int, POINTER(ctypes.c_uint64), POINTER(ctypes.c_uint64)]),
+    "tg_host_alloc": (c_int, [POINTER(c_void_p), sz]),
+    "tg_host_free": (c_int, [vp]),
+    "tg_set_device": (c_int, [c_int]),
+    "tg_get_device": (c_int, [pint]),
+    "tg_device_count": (c_int, [pint]),
+    "tg_event_create": (c_int, [POINTER(c_void_p)]),
+    "tg_event_record": (c_int, [vp, vp]),
+    "tg_event_query": (c_int, [vp]),
+    "tg_event_destroy": (c_int, [vp]),
+    "tg_comm_load": (c_int, [c_char_p]),
+    "tg_comm_nccl_version": (c_int, [pint]),
+    "tg_comm_unique_id": (c_int, [vp, sz]),
+    "tg_comm_init": (c_int, [c_int, c_int, vp, dbl, POINTER(c_void_p)]),
+    "tg_comm_all_reduce": (c_int, [vp, vp, sz, c_int, c_int, vp, dbl]),
+    "tg_comm_join": (c_int, [vp, vp]),
+    "tg_comm_wait": (c_int, [vp, dbl]),
+    "tg_comm_abort": (c_int, [vp]),
+    "tg_comm_destroy": (c_int, [vp, dbl]),
     "tg_gemm": (c_int, [c_int, c_int, c_int, i64, i64, i64, dbl, vp, i64, vp, i64, dbl, vp, i64,
                         vp, vp]),
     "tg_gemm_simt": (c_int, [c_int, c_int, c_int, i64, i64, i64, dbl, vp, i64, vp, i64, dbl, vp,

@@ -40,7 +40,9 @@ const char* tg_status_string(int status) {
     case TG_ERR_CUDA: return "CUDA error";
     case TG_ERR_UNSUPPORTED: return "unsupported";
     case TG_ERR_INDEX: return "index out of range";
-    case TG_ERR_TIMEOUT: return "device wait timed out";
+    case TG_ERR_TIMEOUT: return "timed out";
+    case TG_ERR_OOM: return "out of device memory";
+    case TG_ERR_COMM: return "collective failed";
   }
   return "unknown status";
 }

@@ -1,14 +1,18 @@
 """Device-resident storage: :class:`DeviceArray`, the ``data`` of every tensor.
 
-Memory comes from PyTorch's CUDA caching allocator (allocation only: buffers are reused
-across steps without ``cudaMalloc``); every byte that moves or changes does so through
-``libtgb200.so``. A :class:`DeviceArray` is contiguous, row-major, and duck-types the parts
-of ``numpy.ndarray`` that user code reads from ``tensor.data`` (``shape``, ``dtype``,
-``np.asarray(a)``, ``a.item()``, indexing for inspection, whole-array assignment).
+Memory comes from ``libtgb200.so``'s stream-ordered allocator (``tg_malloc`` / ``tg_free``:
+each device's pool keeps freed blocks, so a step's buffers are reused without ``cudaMalloc``)
+and page-locked host memory from ``tg_host_alloc``; every byte that moves or changes does so
+through the library. No framework is imported. A :class:`DeviceArray` is a contiguous,
+row-major view of a :class:`_Block` (several arrays may share one block, e.g. the slots of a
+flat parameter arena), and duck-types the parts of ``numpy.ndarray`` that user code reads from
+``tensor.data`` (``shape``, ``dtype``, ``np.asarray(a)``, ``a.item()``, indexing for
+inspection, whole-array assignment).
 """
 
 from __future__ import annotations
 
+import ctypes
 import math
 import os
 from collections.abc import Sequence
@@ -18,45 +22,58 @@ import numpy as np
 
 from tensorgrad_b200._lib import ADD, DIV, F32, F64, MUL, SUB, check, int64_array, lib
 
-try:  # torch is the allocator and the NCCL plumbing only
-    import torch
-except ImportError as exc:  # pragma: no cover - torch is part of the image
-    raise RuntimeError("tensorgrad_b200 allocates device memory through torch") from exc
-
-_TORCH_DTYPES = {
-    np.dtype(np.float32): torch.float32,
-    np.dtype(np.float64): torch.float64,
-    np.dtype(np.int64): torch.int64,
-    np.dtype(np.int32): torch.int32,
-    np.dtype(np.bool_): torch.bool,
-    np.dtype(np.uint8): torch.uint8,
-}
-
 
 class _State:
-    device: torch.device | None = None
-    stream: int = 0  # the legacy default stream, which torch also uses by default
+    device: int | None = None
+    stream: int = 0  # the legacy default stream (what other CUDA libraries use by default)
 
 
 def set_device(index: int) -> None:
     """Select the CUDA device for new tensors (one process per GPU)."""
-    torch.cuda.set_device(index)
-    _State.device = torch.device("cuda", index)
+    check(lib.tg_set_device(int(index)), "set_device")
+    _State.device = int(index)
 
 
-def current_device() -> torch.device:
+def device_count() -> int:
+    n = ctypes.c_int(0)
+    lib.tg_device_count(ctypes.byref(n))
+    return n.value
+
+
+def current_device() -> int:
+    """Index of the device new tensors go to (``LOCAL_RANK`` by default, else 0)."""
     dev = _State.device
     if dev is None:
-        if not torch.cuda.is_available():
+        if device_count() == 0:
             raise RuntimeError(
                 "tensorgrad_b200 needs a CUDA device (B200): tensors live in device memory "
                 "and there is no CPU fallback"
             )
-        index = int(os.environ.get("LOCAL_RANK", torch.cuda.current_device()))
-        set_device(index)
+        set_device(int(os.environ.get("LOCAL_RANK", "0")))
         dev = _State.device
     assert dev is not None
     return dev
+
+
+class _Block:
+    """One device allocation; freed (stream-ordered) when the last array viewing it goes."""
+
+    __slots__ = ("__weakref__", "device", "nbytes", "ptr")
+
+    def __init__(self, nbytes: int) -> None:
+        self.device = current_device()
+        self.nbytes = nbytes
+        p = ctypes.c_void_p()
+        check(lib.tg_malloc(ctypes.byref(p), nbytes, _State.stream), "device allocation")
+        self.ptr = int(p.value or 0)
+
+    def __del__(self) -> None:
+        if self.ptr:
+            try:
+                lib.tg_free(self.ptr, _State.stream)
+            except Exception:  # noqa: BLE001 - interpreter shutdown: the process frees all
+                pass
+            self.ptr = 0
 
 
 def stream() -> int:
@@ -116,7 +133,7 @@ class _Async:
 
 def async_error_word(kind: int) -> int:
     """Device address of the int32 flag word of ``kind`` (ASYNC_*); marks a check pending."""
-    if _Async.words is None or _Async.words._t.device != current_device():
+    if _Async.words is None or _Async.words._buf.device != current_device():
         _Async.words = zeros((len(_ASYNC_MESSAGES),), np.int32)
     _Async.pending = True
     return _Async.words.ptr + 4 * kind
@@ -137,21 +154,24 @@ def _raise_async_errors() -> None:
 
 
 class DeviceArray:
-    """A contiguous device buffer with a shape and a NumPy dtype."""
+    """A contiguous device array: ``shape`` elements of ``dtype`` at byte ``_off`` of a
+    device allocation."""
 
-    __slots__ = ("_t", "dtype", "shape")
+    __slots__ = ("_buf", "_off", "dtype", "shape")
 
     __array_ufunc__ = None  # ``ndarray op DeviceArray`` defers to our operators
 
-    def __init__(self, t: torch.Tensor, shape: tuple[int, ...], dtype: np.dtype[Any]) -> None:
-        self._t = t
+    def __init__(self, buf: _Block, off: int, shape: tuple[int, ...],
+                 dtype: np.dtype[Any]) -> None:
+        self._buf = buf
+        self._off = off
         self.shape = shape
         self.dtype = dtype
 
     # ------------------------------------------------------------- properties
     @property
     def ptr(self) -> int:
-        return self._t.data_ptr()
+        return self._buf.ptr + self._off
 
     @property
     def size(self) -> int:
@@ -211,7 +231,7 @@ class DeviceArray:
         return self.shape[0]
 
     def __repr__(self) -> str:
-        return f"DeviceArray({self.numpy()!r}, device={self._t.device})"
+        return f"DeviceArray({self.numpy()!r}, device=cuda:{self._buf.device})"
 
     def __getitem__(self, index: Any) -> Any:
         return self.numpy()[index]
@@ -235,12 +255,14 @@ class DeviceArray:
     def reshape(self, *shape: int | Sequence[int]) -> DeviceArray:
         dims = shape[0] if len(shape) == 1 and isinstance(shape[0], Sequence) else shape
         new = _resolve_shape(tuple(int(d) for d in dims), self.size)  # type: ignore[union-attr]
-        return DeviceArray(self._t, new, self.dtype)
+        return DeviceArray(self._buf, self._off, new, self.dtype)
 
     def flat_view(self, offset: int, count: int, shape: tuple[int, ...] | None = None) -> DeviceArray:
         """A view of ``count`` elements starting at element ``offset`` of this buffer."""
-        t = self._t.view(-1)[offset:offset + count]
-        return DeviceArray(t, shape if shape is not None else (count,), self.dtype)
+        if offset < 0 or count < 0 or offset + count > max(self.size, 1):
+            raise ValueError(f"flat_view [{offset}, {offset + count}) of {self.size} elements")
+        return DeviceArray(self._buf, self._off + offset * self.dtype.itemsize,
+                           shape if shape is not None else (count,), self.dtype)
 
     def copy(self) -> DeviceArray:
         out = empty(self.shape, self.dtype)
@@ -332,8 +354,7 @@ def _resolve_shape(shape: tuple[int, ...], size: int) -> tuple[int, ...]:
 def empty(shape: Sequence[int], dtype: Any) -> DeviceArray:
     dt = np.dtype(dtype)
     shp = tuple(int(s) for s in shape)
-    t = torch.empty(max(math.prod(shp), 1), dtype=_TORCH_DTYPES[dt], device=current_device())
-    return DeviceArray(t, shp, dt)
+    return DeviceArray(_Block(max(math.prod(shp), 1) * dt.itemsize), 0, shp, dt)
 
 
 def zeros(shape: Sequence[int], dtype: Any) -> DeviceArray:
@@ -341,6 +362,44 @@ def zeros(shape: Sequence[int], dtype: Any) -> DeviceArray:
     if out.nbytes:
         check(lib.tg_memset_zero(out.ptr, out.nbytes, _State.stream), "zeros")
     return out
+
+
+def _host_bytes(nbytes: int) -> np.ndarray:
+    """A page-locked host byte array that lives as long as the process (they are few and
+    reused: staging blocks and the pinned input arrays of a training loop)."""
+    p = ctypes.c_void_p()
+    check(lib.tg_host_alloc(ctypes.byref(p), max(nbytes, 1)), "pinned allocation")
+    raw = (ctypes.c_ubyte * max(nbytes, 1)).from_address(int(p.value or 0))
+    arr = np.frombuffer(raw, dtype=np.uint8)[:nbytes]
+    _PINNED.append((arr.ctypes.data, nbytes, raw))
+    return arr
+
+
+class _Event:
+    """A timing-free CUDA event recorded behind a copy (to know when its source is free)."""
+
+    __slots__ = ("handle",)
+
+    def __init__(self) -> None:
+        h = ctypes.c_void_p()
+        check(lib.tg_event_create(ctypes.byref(h)), "event")
+        self.handle = h.value
+
+    def record(self) -> None:
+        check(lib.tg_event_record(self.handle, _State.stream), "event record")
+
+    def query(self) -> bool:
+        r = lib.tg_event_query(self.handle)
+        if r < 0:
+            check(-r, "event query")
+        return r == 1
+
+    def __del__(self) -> None:
+        if self.handle:
+            try:
+                lib.tg_event_destroy(self.handle)
+            except Exception:  # noqa: BLE001 - interpreter shutdown
+                pass
 
 
 class _Staging:
@@ -353,7 +412,7 @@ class _Staging:
     LIMIT = 4 << 20  # larger uploads (model initialisation) copy synchronously
 
     def __init__(self) -> None:
-        self.blocks: list[list[Any]] = []  # [pinned tensor, capacity, event or None]
+        self.blocks: list[list[Any]] = []  # [pinned bytes, capacity, event or None]
 
     def upload(self, dst: DeviceArray, arr: np.ndarray) -> None:
         block = None
@@ -363,13 +422,13 @@ class _Staging:
                 break
         if block is None:
             cap = max(1 << 16, 1 << (arr.nbytes - 1).bit_length())
-            block = [torch.empty(cap, dtype=torch.uint8, pin_memory=True), cap, None]
+            block = [_host_bytes(cap), cap, None]
             self.blocks.append(block)
-        host = block[0].numpy()[: arr.nbytes]
+        host = block[0][: arr.nbytes]
         host[:] = arr.reshape(-1).view(np.uint8)
         check(lib.tg_memcpy_h2d(dst.ptr, host.ctypes.data, arr.nbytes, _State.stream), "h2d")
-        ev = block[2] or torch.cuda.Event()
-        ev.record(torch.cuda.current_stream(dst._t.device))
+        ev = block[2] or _Event()
+        ev.record()
         block[2] = ev
 
 
@@ -397,10 +456,8 @@ def pinned_empty(shape: Sequence[int], dtype: Any) -> np.ndarray:
     are asynchronous DMA copies that read it after the call returns, so it must not be
     changed before the next synchronisation."""
     dt = np.dtype(dtype)
-    t = torch.empty(max(math.prod(shape), 1), dtype=_TORCH_DTYPES[dt], pin_memory=True)
-    arr = t.numpy()[: math.prod(shape)].reshape(shape)
-    _PINNED.append((arr.ctypes.data, arr.nbytes, t))
-    return arr
+    n = math.prod(shape)
+    return _host_bytes(max(n, 1) * dt.itemsize)[: n * dt.itemsize].view(dt).reshape(shape)
 
 
 def _is_pinned(arr: np.ndarray) -> bool:
@@ -427,6 +484,16 @@ def copy_into(dst: DeviceArray, src: DeviceArray) -> None:
         check(lib.tg_memcpy_d2d(dst.ptr, src.ptr, src.nbytes, _State.stream), "d2d")
 
 
+_READBACK: list[np.ndarray] = []
+
+
+def _staging_for_readback(nbytes: int) -> np.ndarray:
+    """One reusable page-locked block for bulk device-to-host copies (grown on demand)."""
+    if not _READBACK or _READBACK[0].nbytes < nbytes:
+        _READBACK[:] = [_host_bytes(max(nbytes, 1 << 20))]
+    return _READBACK[0][:nbytes]
+
+
 def numpy_many(arrays: Sequence[DeviceArray]) -> list[np.ndarray]:
     """Host copies of several device arrays with one synchronisation: every copy is queued
     into one page-locked staging block (16-byte aligned slots), then the stream is waited on
@@ -437,7 +504,7 @@ def numpy_many(arrays: Sequence[DeviceArray]) -> list[np.ndarray]:
         total += -(-a.nbytes // 16) * 16
     if not arrays:
         return []
-    staging = torch.empty(max(total, 16), dtype=torch.uint8, pin_memory=True).numpy()
+    staging = _staging_for_readback(max(total, 16))
     base = staging.ctypes.data
     for a, off in zip(arrays, offsets, strict=True):
         if a.nbytes:

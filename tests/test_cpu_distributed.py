@@ -98,3 +98,100 @@ def test_unready_buckets_are_launched_by_finish_in_order():
     red.finish()          # 0 and 2 never got their gradients: launched in bucket order
     assert red.last_order == [3, 1, 0, 2]
     assert red.pending == red.members and not any(red.launched)
+
+
+# ------------------------------------------------------------------ fault injection (host)
+def _fault_rank(rank: int, world: int, port: int, fault: str, queue) -> None:
+    """One gloo rank of a two-step exchange; rank 1's communicator injects ``fault`` into
+    bucket 1 of step 1. Reports what each step did, then leaves without tearing the group
+    down (after a failed collective the group cannot be trusted to shut down cleanly)."""
+    import torch
+    import torch.distributed as dist
+
+    from tensorgrad_b200 import distributed
+    from tensorgrad_b200.distributed import (
+        BucketedAllReduce, CollectiveError, FaultyCommunicator, ProcessGroupCommunicator,
+    )
+
+    import datetime
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    # A short group timeout bounds every gloo operation, also the ones a fault leaves waiting.
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    comm = ProcessGroupCommunicator()
+    if rank == 1 and fault != "leave":
+        comm = FaultyCommunicator(comm, {(1, 1): fault}, delay_s=0.3)
+    flat = torch.zeros(32)
+    red = BucketedAllReduce([(flat, [1, 2, 3, 4], [0, 8, 16, 24], [8, 8, 8, 8])],
+                            bucket_bytes=32, comm=comm, deadline_s=3.0, verify=True)
+    report = []
+    for step in range(2):
+        flat.copy_(torch.arange(32, dtype=torch.float32) * (rank + 1) + step)
+        if fault == "leave" and step == 1:
+            if rank == 1:  # stops between steps, with nothing in flight
+                distributed.leave_job()
+                report.append(("left", None))
+                break
+            # Sequenced so that the announcement lands before this rank's next launch.
+            dist.distributed_c10d._get_default_store().wait([distributed._LEFT.format(1)])
+        try:
+            red.finish()
+            report.append(("ok", flat.numpy().copy()))
+        except CollectiveError as exc:
+            report.append((type(exc).__name__, None))
+            break
+    queue.put((rank, report))
+    queue.close()
+    queue.join_thread()  # the report is handed over before the hard exit
+    os._exit(0)
+
+
+def _run_fault(fault: str) -> dict:
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fault_rank, args=(r, 2, port, fault, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(queue.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    return results
+
+
+def test_dropped_bucket_times_out_on_every_rank():
+    results = _run_fault("drop")
+    expected_first = (np.arange(32) * 1.5).astype(np.float32)  # mean of ranks 1x and 2x
+    for rank in (0, 1):
+        first, second = results[rank]
+        assert first[0] == "ok"
+        np.testing.assert_allclose(first[1], expected_first)
+        assert second[0] == "CollectiveTimeout"
+
+
+def test_delayed_bucket_still_reduces_correctly():
+    results = _run_fault("delay")
+    for rank in (0, 1):
+        assert [kind for kind, _ in results[rank]] == ["ok", "ok"]
+        np.testing.assert_allclose(results[rank][1][1], np.arange(32) * 1.5 + 1.0)
+
+
+def test_corrupted_bucket_is_caught_by_verification():
+    results = _run_fault("corrupt")
+    for rank in (0, 1):
+        first, second = results[rank]
+        assert first[0] == "ok"
+        assert second[0] == "CollectiveMismatch"
+
+
+def test_departed_rank_is_seen_before_the_next_launch():
+    results = _run_fault("leave")
+    assert [kind for kind, _ in results[1]] == ["ok", "left"]
+    first, second = results[0]
+    assert first[0] == "ok"
+    np.testing.assert_allclose(first[1], (np.arange(32) * 1.5).astype(np.float32))
+    assert second[0] == "CollectiveError"  # raised by the peer check, not a deadline

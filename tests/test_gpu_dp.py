@@ -64,3 +64,55 @@ def test_two_rank_data_parallel_matches_full_batch_oracle(tmp_path):
         order = list(got[f"step{step}/buckets"])
         assert len(order) > 2 and order[0] == max(order)
         params, state = ref["params"], ref["state"]
+
+
+_NO_NVLS = {"NCCL_NVLS_ENABLE": "0"}
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+def test_departed_rank_raises_before_the_next_exchange(tmp_path):
+    cmd = ["timeout", "-k", "30", "180", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+           "--master-port", str(_port()), os.path.join(ROOT, "tests", "dp_fault_worker.py"),
+           str(tmp_path)]
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="0,1", **_NO_NVLS)
+    res = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=240)
+    assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
+    r0 = (tmp_path / "rank0.txt").read_text().split()
+    r1 = (tmp_path / "rank1.txt").read_text().split()
+    assert r0[:2] == r1[:2] and r0[0] == "step1=ok"  # same averaged gradient on both
+    assert r1[2:] == ["left"]
+    assert r0[2:] == ["step2=CollectiveError", "device_after=56.0"]
+
+
+def test_communicator_setup_times_out_without_peers():
+    """A two-rank NCCL set-up with no second rank ends in CollectiveTimeout after its
+    deadline (the library aborts the half-made communicator); the device still works."""
+    code = (
+        "import ctypes, time, numpy as np, tensorgrad_b200 as tg\n"
+        "from tensorgrad_b200._lib import lib\n"
+        "from tensorgrad_b200.distributed import NcclCommunicator, CollectiveTimeout, "
+        "_nccl_library\n"
+        "tg.set_device(0)\n"
+        "assert lib.tg_comm_load((_nccl_library() or '').encode()) == 0\n"
+        "uid = ctypes.create_string_buffer(128)\n"
+        "assert lib.tg_comm_unique_id(uid, 128) == 0\n"
+        "t = time.monotonic()\n"
+        "try:\n"
+        "    NcclCommunicator(2, 0, uid.raw, timeout_s=3.0)\n"
+        "    print('no-timeout')\n"
+        "except CollectiveTimeout as e:\n"
+        "    print('timeout', round(time.monotonic() - t, 1))\n"
+        "x = tg.Tensor(np.arange(8, dtype=np.float32))\n"
+        "print('device', float((x * 2.0).sum().item()))\n")
+    env = dict(os.environ, **_NO_NVLS)
+    res = subprocess.run(["timeout", "-k", "10", "90", sys.executable, "-c", code], cwd=ROOT,
+                         env=env, capture_output=True, text=True, timeout=120)
+    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-2000:]
+    # NCCL writes its own warnings (the aborted set-up) to stdout too.
+    mine = [ln for ln in res.stdout.splitlines() if ln.split()[:1] in (["timeout"], ["device"],
+                                                                          ["no-timeout"])]
+    assert len(mine) == 2, res.stdout[-2000:]
+    kind, secs = mine[0].split()
+    assert kind == "timeout" and 2.5 <= float(secs) < 30.0
+    assert mine[1] == "device 56.0"
