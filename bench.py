@@ -53,6 +53,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="gpt2")
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
+    p.add_argument("--no-hbm", action="store_true",
+                   help="skip the per-kernel HBM roofline leg (HBM-bound kernels timed alone)")
     p.add_argument("--gemm", metavar="M,N,K,TA,TB",
                    help="time one fp32 tg_gemm of this shape instead of a training step "
                         "(a kernel probe: C = op(A) op(B), TA/TB = 1 for transposed storage)")
@@ -557,6 +559,162 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- our arm
+def _hbm_cases(wl: Workload, device, lib) -> list:
+    """The workload's HBM-bound kernels at the step's shapes, each as (name, algorithmic bytes
+    per launch, a list of argument sets (one per rotating buffer set), a launcher). The
+    algorithmic bytes are the minimum a launch must move: every input read once, every output
+    written once."""
+    import ctypes
+
+    import numpy as np
+
+    f4 = 4
+    st = device.stream()
+    rng = np.random.default_rng(7)
+    zeros = lambda shape, dt=np.float32: _zeroed(device, lib, shape, dt)  # noqa: E731
+
+    def rnd(shape):
+        return device.from_numpy(rng.standard_normal(shape).astype(np.float32))
+
+    def sets(per_set_bytes: int, make) -> list:
+        # Enough buffer sets that consecutive launches do not find their inputs in the L2.
+        return [make() for _ in range(max(2, -(-(384 << 20) // max(per_set_bytes, 1))))]
+
+    cases = []
+    if isinstance(wl, GPTWorkload):
+        n, d, v = wl.batch * wl.seq, wl.cfg["n_embd"], wl.cfg["vocab_size"]
+        f = 4 * d
+        w, b = rnd((d,)), rnd((d,))
+        scratch = zeros((lib.tg_layer_norm_scratch_bytes(0, n, d) // 4 + 1,))
+        gw, gb = zeros((d,)), zeros((d,))
+
+        def ln_set():
+            return dict(x=rnd((n, d)), y=zeros((n, d)), g=rnd((n, d)), gx=zeros((n, d)),
+                        mean=zeros((n,)), rstd=zeros((n,)))
+
+        ln = sets(4 * n * d * f4, ln_set)
+        for a in ln:
+            lib.tg_layer_norm_forward(0, a["x"].ptr, w.ptr, b.ptr, a["y"].ptr, a["mean"].ptr,
+                                      a["rstd"].ptr, n, d, 1e-5, st)
+        cases.append(("ln_fwd (layer norm forward)", 2 * n * d * f4, ln, lambda a: lib.tg_layer_norm_forward(
+            0, a["x"].ptr, w.ptr, b.ptr, a["y"].ptr, a["mean"].ptr, a["rstd"].ptr, n, d, 1e-5, st)))
+        cases.append(("ln_bwd (layer norm VJP: gx, gw, gb)", 3 * n * d * f4, ln,
+                      lambda a: lib.tg_layer_norm_backward(
+                          0, a["g"].ptr, a["x"].ptr, w.ptr, a["mean"].ptr, a["rstd"].ptr,
+                          a["gx"].ptr, gw.ptr, gb.ptr, n, d, 7, scratch.ptr, st)))
+        ge = sets(3 * n * f * f4, lambda: dict(x=rnd((n, f)), y=zeros((n, f)), g=rnd((n, f))))
+        cases.append(("gelu_fwd", 2 * n * f * f4, ge,
+                      lambda a: lib.tg_gelu_forward(0, n * f, a["x"].ptr, a["y"].ptr, st)))
+        cases.append(("gelu_bwd", 3 * n * f * f4, ge,
+                      lambda a: lib.tg_gelu_backward(0, n * f, a["g"].ptr, a["x"].ptr,
+                                                     a["y"].ptr, st)))
+        logits, grad = zeros((n, v)), zeros((n, v))
+        tgt = device.from_numpy(rng.integers(0, v, size=n, dtype=np.int64))
+        lse, rows, out = zeros((n,)), zeros((n,)), zeros((1,))
+        nvalid, bad = zeros((1,), np.int64), zeros((1,), np.int32)
+        one = device.from_numpy(np.ones(1, np.float32))
+        ce = [dict()]
+        cases.append(("ce_fwd (cross entropy, online log-sum-exp)", n * v * f4, ce,
+                      lambda a: lib.tg_cross_entropy_forward(
+                          0, logits.ptr, tgt.ptr, lse.ptr, rows.ptr, out.ptr, n, v, -100, 0,
+                          nvalid.ptr, bad.ptr, st)))
+        cases.append(("ce_bwd (softmax - onehot)", 2 * n * v * f4, ce,
+                      lambda a: lib.tg_cross_entropy_backward(
+                          0, logits.ptr, tgt.ptr, lse.ptr, one.ptr, nvalid.ptr, grad.ptr, n, v,
+                          -100, 0, st)))
+    elif isinstance(wl, CNNWorkload):
+        from tensorgrad_b200._lib import ConvShape
+
+        n, c, hw = 256, 32, 64 * 64
+        w, b = rnd((c,)), rnd((c,))
+        mean, rstd, rm, rv = zeros((c,)), zeros((c,)), zeros((c,)), zeros((c,))
+        gw, gb = zeros((c,)), zeros((c,))
+        scratch = zeros((lib.tg_batch_norm_scratch_bytes(0, n, c, hw) // 4 + 1,))
+        bn = sets(4 * n * c * hw * f4, lambda: dict(x=rnd((n, c, hw)), y=zeros((n, c, hw)),
+                                                    g=rnd((n, c, hw)), gx=zeros((n, c, hw))))
+        cases.append(("bn_fwd (batch norm: statistics + apply)", 2 * n * c * hw * f4, bn,
+                      lambda a: lib.tg_batch_norm_forward(
+                          0, n, c, hw, a["x"].ptr, w.ptr, b.ptr, a["y"].ptr, mean.ptr, rstd.ptr,
+                          rm.ptr, rv.ptr, 0.1, 1e-5, scratch.ptr, st)))
+        cases.append(("bn_bwd (batch norm VJP: gx, gw, gb)", 3 * n * c * hw * f4, bn,
+                      lambda a: lib.tg_batch_norm_backward(
+                          0, n, c, hw, a["g"].ptr, a["x"].ptr, w.ptr, mean.ptr, rstd.ptr,
+                          a["gx"].ptr, gw.ptr, gb.ptr, scratch.ptr, st)))
+        shp = ConvShape(n=n, c=c, h=64, w=64, c_out=c, kh=2, kw=2, sh=2, sw=2, ph=0, pw=0,
+                        oh=32, ow=32)
+        q = n * c * 32 * 32
+        mp = sets(5 * q * f4, lambda: dict(x=rnd((n, c, 64, 64)), y=zeros((n, c, 32, 32)),
+                                           arg=zeros((q,), np.uint8), g=rnd((n, c, 32, 32)),
+                                           gx=zeros((n, c, 64, 64))))
+        for a in mp:
+            lib.tg_max_pool2d_forward(0, ctypes.byref(shp), a["x"].ptr, a["y"].ptr, a["arg"].ptr,
+                                      st)
+        cases.append(("maxpool_fwd (2x2: y + winner byte)", 4 * q * f4 + q * f4 + q, mp,
+                      lambda a: lib.tg_max_pool2d_forward(0, ctypes.byref(shp), a["x"].ptr,
+                                                          a["y"].ptr, a["arg"].ptr, st)))
+        cases.append(("maxpool_bwd (2x2 gather)", q * f4 + q + 4 * q * f4, mp,
+                      lambda a: lib.tg_max_pool2d_backward(0, ctypes.byref(shp), a["g"].ptr,
+                                                           a["arg"].ptr, a["gx"].ptr, st)))
+    return cases
+
+
+def _zeroed(device, lib, shape, dt):
+    a = device.empty(shape, dt)
+    lib.tg_memset_zero(a.ptr, a.nbytes, device.stream())
+    return a
+
+
+def hbm_kernels(wl: Workload, built: Built, reps: int = 20) -> list:
+    """Each HBM-bound kernel of the step, launched alone at the step's shapes through the C ABI
+    and timed with CUDA events over ``reps`` launches that rotate over buffer sets larger than
+    the L2 (so the inputs come from HBM): algorithmic bytes per launch / mean duration,
+    against the measured copy bandwidth. AdamW (clip fused) and the clip norm run over a
+    parameter arena the size of the model's."""
+    import torch
+
+    from tensorgrad_b200 import device
+    from tensorgrad_b200._lib import lib
+
+    hbm = float(peaks().get("hbm_gbs", 6650.0))
+    cases = _hbm_cases(wl, device, lib)
+    nparam = sum(int(p.size) for p in built.params)
+    if nparam:
+        import ctypes
+
+        import numpy as np
+
+        z = lambda: _zeroed(device, lib, (nparam,), np.float32)  # noqa: E731
+        p, g, m, v = z(), z(), z(), z()
+        total = _zeroed(device, lib, (1,), np.float64)
+        scr = _zeroed(device, lib, (lib.tg_sumsq_scratch_bytes(1) // 4 + 1,), np.float32)
+        ptrs, nums = (ctypes.c_void_p * 1)(g.ptr), (ctypes.c_int64 * 1)(nparam)
+        st = device.stream()
+        cases.append(("adam_flat_vec4 (AdamW with the clip factor fused)", 28 * nparam, [{}],
+                      lambda a: lib.tg_adam_update_clipped(
+                          0, nparam, p.ptr, g.ptr, m.ptr, v.ptr, 3e-4, 0.9, 0.999, 1e-8, 1e-4, 2,
+                          1, total.ptr, 1.0, 1e-6, st)))
+        cases.append(("sumsq (clip_grad_norm_ total, float64)", 4 * nparam, [{}],
+                      lambda a: lib.tg_sumsq_multi(0, 1, ptrs, nums, total.ptr, scr.ptr, st)))
+    out = []
+    for name, nbytes, arg_sets, launch in cases:
+        for a in arg_sets[:2]:
+            launch(a)
+        device.synchronize()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for i in range(reps):
+            rc = launch(arg_sets[i % len(arg_sets)])
+            if rc:
+                raise RuntimeError(f"{name}: status {rc}")
+        stop.record()
+        stop.synchronize()
+        us = 1e3 * start.elapsed_time(stop) / reps
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out.append({"kernel": name, "bytes_per_launch": int(nbytes), "us_per_launch": us,
+                    "achieved_gbs": gbs, "frac": gbs / hbm})
+    return out
+
+
 def run_ours(args: argparse.Namespace, wl: Workload) -> None:
     import ctypes
 
@@ -667,6 +825,13 @@ def run_ours(args: argparse.Namespace, wl: Workload) -> None:
         "gpu_launches": launches,
         "final_loss": last,
     }
+    if rank == 0 and not args.no_hbm:
+        out["hbm_kernels"] = {
+            "peak_gbs": float(pk.get("hbm_gbs", 6650.0)),
+            "peak_source": f"{pk['source']} hbm_gbs (STREAM-style copy)",
+            "method": "each kernel alone at the step's shapes, 20 launches rotating over "
+                      "buffer sets larger than the L2, CUDA events; algorithmic bytes",
+            "kernels": hbm_kernels(wl, built)}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(wl)
     if rank == 0:

@@ -32,6 +32,9 @@
 // (bounded again), frees its TMEM and returns; tg_gemm_tc_status() reads the word.
 #include <stdlib.h>
 
+#include <map>
+#include <mutex>
+
 #include "common.cuh"
 #include "gemm.cuh"
 #include "tc_ptx.cuh"
@@ -61,6 +64,17 @@ struct TcArgs {
   float* aux;             // GEMM_EPI_SOFTMAX_DS: P in (same layout as C)
   int tma_c;              // 1: whole tiles go out through shared memory and TMA stores (tmC),
                           //    the dS epilogue's P through TMA loads (tmX)
+  // Stream-K tail (sk_tiles > 0). The first sk_first tiles (whole rounds of the units) go
+  // round-robin as whole tiles; the k-blocks of the last sk_tiles tiles (sk_nk each) are cut
+  // into one contiguous range per unit, sk_q long plus one for the first sk_r units. A tile
+  // cut between units is a set of pieces: each writes its fp32 partial to a slot of sk_ws
+  // ([2 * units][BM][BN], slot 2u for the first piece of unit u's range, 2u + 1 for its last)
+  // and counts itself in sk_cnt ([sk_tiles][4], per epilogue warp); the piece that completes
+  // the count sums all partials in piece order and writes the tile. No piece waits for another.
+  int sk_first, sk_tiles, sk_nk;
+  int64_t sk_q, sk_r;
+  float* sk_ws;
+  int* sk_cnt;
 };
 
 constexpr int kThreads = 512;
@@ -91,13 +105,16 @@ struct Layout {
   static constexpr uint32_t B_BYTES = B_ROWS * BK * 4;
   static constexpr uint32_t RAW = A_BYTES + B_BYTES;               // raw slot: A, then B
   static constexpr uint32_t LO = (ATM ? 0 : A_BYTES) + B_BYTES;    // lo slot: A lo, B lo
-  static constexpr uint32_t ACC_COLS = 2 * BN;  // two accumulators
+  // Two accumulators (the epilogue of one tile overlaps the next tile's k-blocks), except
+  // for 256-wide tiles with A in tensor memory, where one accumulator leaves TMEM room for A.
+  static constexpr int NACC = (ATM && BN > 128) ? 1 : 2;
+  static constexpr uint32_t ACC_COLS = NACC * BN;
   // ATM (A in tensor memory): A's hi and lo of each lo slot go to TMEM columns after the
   // accumulators (2 * BK per slot).
   static constexpr uint32_t TMEM_COLS = ATM ? 512 : ACC_COLS;
   // Slot counts: the lo ring 2 (3 when its slots are small), bounded by TMEM with ATM; the
   // raw ring whatever fits in 193 KB beside it (at most 8).
-  static constexpr int LO_TMEM_CAP = ATM ? (int)((512 - 2 * BN) / (2 * BK)) : 8;
+  static constexpr int LO_TMEM_CAP = ATM ? (int)((512 - ACC_COLS) / (2 * BK)) : 8;
   static constexpr int LST0 = 3;
   static constexpr int LST = LST0 < LO_TMEM_CAP ? LST0 : LO_TMEM_CAP;
   static constexpr int RST0 = (int)((193 * 1024 - LST * LO) / RAW);
@@ -124,6 +141,7 @@ struct TileInfo {
   int64_t m0, n0;
   int bz, split, kb0, nk;
   bool skip;
+  int sk_tile, seg, segs;  // stream-K: tail tile, piece index and count (segs 1: whole tile)
 };
 
 __device__ __forceinline__ TileInfo tile_info(const TcArgs& a, int t, int bn, int bm, int bk) {
@@ -152,7 +170,87 @@ __device__ __forceinline__ TileInfo tile_info(const TcArgs& a, int t, int bn, in
   }
   ti.kb0 = kb0;
   ti.nk = (ti.skip || kb1 <= kb0) ? 0 : kb1 - kb0;
+  ti.sk_tile = -1;
+  ti.seg = 0;
+  ti.segs = 1;
   return ti;
+}
+
+// Stream-K: the unit whose tail range holds tail k-block w, and where unit u's range starts.
+__device__ __forceinline__ int sk_unit_of(const TcArgs& a, int64_t w) {
+  const int64_t big = a.sk_r * (a.sk_q + 1);
+  return w < big ? (int)(w / (a.sk_q + 1)) : (int)(a.sk_r + (w - big) / a.sk_q);
+}
+__device__ __forceinline__ int64_t sk_range_start(const TcArgs& a, int u) {
+  return (int64_t)u * a.sk_q + (u < a.sk_r ? u : a.sk_r);
+}
+
+// The w-th work item of a unit (false: none left): whole tiles unit, unit + units, ... below
+// the stream-K tail (all tiles without one), then the pieces of the unit's range of tail
+// k-blocks, each inside one tail tile. Every warp role walks the same items.
+__device__ __forceinline__ bool work_item(const TcArgs& a, int unit, int units, int w, int bn,
+                                          int bm, int bk, TileInfo& ti) {
+  const int total = a.m_tiles * a.n_tiles * a.batch * a.splits;
+  const int whole = a.sk_tiles ? a.sk_first : total;
+  const int nw = unit < whole ? (whole - unit + units - 1) / units : 0;
+  if (w < nw) {
+    ti = tile_info(a, unit + w * units, bn, bm, bk);
+    return true;
+  }
+  if (!a.sk_tiles) return false;
+  const int64_t nk = a.sk_nk;
+  const int64_t b = sk_range_start(a, unit);
+  const int64_t end = b + a.sk_q + (unit < a.sk_r ? 1 : 0);
+  const int64_t e = w - nw;
+  const int64_t start = e == 0 ? b : (b / nk + e) * nk;
+  if (start >= end) return false;
+  const int j = (int)(start / nk);
+  const int64_t stop = ((int64_t)j + 1) * nk < end ? ((int64_t)j + 1) * nk : end;
+  ti = tile_info(a, a.sk_first + j, bn, bm, bk);
+  ti.kb0 = (int)(start - (int64_t)j * nk);
+  ti.nk = (int)(stop - start);
+  ti.sk_tile = j;
+  const int uf = sk_unit_of(a, (int64_t)j * nk);
+  ti.seg = unit - uf;
+  ti.segs = sk_unit_of(a, ((int64_t)j + 1) * nk - 1) - uf + 1;
+  return true;
+}
+
+// Stream-K partial slot of unit u's piece of tail tile j: its range's first piece (the range
+// starts inside tile j) or its last.
+__device__ __forceinline__ int64_t sk_slot(const TcArgs& a, int u, int j) {
+  return 2 * (int64_t)u + (sk_range_start(a, u) >= (int64_t)j * a.sk_nk ? 0 : 1);
+}
+
+// A partial slot holds BM x BN floats in the order the epilogue warps produce them, so that
+// every access is coalesced: [warp 4][chunk BN/32][k 8][lane 32] float4, where lane = row
+// within the warp's 32 rows and (chunk, k) = columns 32 chunk + 4k .. + 3.
+template <int BN>
+__device__ __forceinline__ float4* sk_chunk(const TcArgs& a, int64_t slot, int ew, int cc) {
+  return reinterpret_cast<float4*>(a.sk_ws) + ((slot * 4 + ew) * (BN / 32) + cc) * 8 * 32;
+}
+
+// Sum, in piece order, of the partials of tail tile j (pieces from unit u_first on) at this
+// lane's row and 32 columns: what the accumulator of an uncut tile would hold there.
+template <int BN>
+__device__ __forceinline__ void sk_sum(const TcArgs& a, int u_first, int segs, int j, int ew,
+                                       int lane, int cc, uint32_t (&r)[32]) {
+  float v[32];
+#pragma unroll 1
+  for (int s = 0; s < segs; ++s) {
+    const float4* p = sk_chunk<BN>(a, sk_slot(a, u_first + s, j), ew, cc) + lane;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float4 q = __ldcg(p + 32 * k);
+      if (s == 0) {
+        v[4 * k] = q.x; v[4 * k + 1] = q.y; v[4 * k + 2] = q.z; v[4 * k + 3] = q.w;
+      } else {
+        v[4 * k] += q.x; v[4 * k + 1] += q.y; v[4 * k + 2] += q.z; v[4 * k + 3] += q.w;
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 32; ++k) r[k] = __float_as_uint(v[k]);
 }
 
 // PAIR = true: launched in clusters of two CTAs; each pair computes 256 x BN tiles with
@@ -187,7 +285,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int total = args.m_tiles * args.n_tiles * args.batch * args.splits;
   // Work unit: a CTA, or a CTA pair (tile t goes to unit t % units).
   const uint32_t rank = PAIR ? cluster_rank() : 0;
   const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
@@ -226,8 +323,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (lane == 0) {
       int it = 0;
       bool stop = false;
-      for (int t = unit; t < total && !stop; t += units) {
-        const TileInfo ti = tile_info(args, t, BN, TILE_M, KB);
+      for (int w = 0; !stop; ++w) {
+        TileInfo ti;
+        if (!work_item(args, unit, units, w, BN, TILE_M, KB, ti)) break;
         for (int j = 0; j < ti.nk; ++j, ++it) {
           const int s = it % RST, round = it / RST;
           if (round > 0 && !wait_bar(&empty[s], (round - 1) & 1, abort_flag)) { stop = true; break; }
@@ -279,8 +377,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       // cluster-scope release arrival tells the even CTA's MMA issuer.
       int it = 0;
       bool ok = true;
-      for (int t = unit; t < total && ok; t += units) {
-        const TileInfo ti = tile_info(args, t, BN, TILE_M, KB);
+      for (int w = 0; ok; ++w) {
+        TileInfo ti;
+        if (!work_item(args, unit, units, w, BN, TILE_M, KB, ti)) break;
         for (int j = 0; j < ti.nk; ++j, ++it) {
           const int l = it % LST;
           if (!wait_bar(&split[l], (it / LST) & 1, abort_flag)) { ok = false; break; }
@@ -293,12 +392,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       constexpr uint32_t idesc = instr_desc(TILE_M, BN, A_MN, B_MN);
       int it = 0, tc = 0;
       bool ok = true;
-      for (int t = unit; t < total && ok; t += units) {
-        const TileInfo ti = tile_info(args, t, BN, TILE_M, KB);
+      for (int w = 0; ok; ++w) {
+        TileInfo ti;
+        if (!work_item(args, unit, units, w, BN, TILE_M, KB, ti)) break;
         if (ti.skip) continue;
-        const int buf = tc & 1;
-        if (tc >= 2) {
-          const uint32_t par = ((tc >> 1) - 1) & 1;
+        const int buf = tc % L::NACC;
+        if (tc >= L::NACC) {
+          const uint32_t par = ((tc / L::NACC) - 1) & 1;
           if (!wait_bar(&acc_empty[buf], par, abort_flag)) { ok = false; break; }
         }
         tc_fence_after();
@@ -379,8 +479,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     int it = 0;
     // Plain TF32 on one CTA: the MMAs read only what the TMA brought, nothing to split.
     bool stop = !PAIR && args.raw;
-    for (int t = unit; t < total && !stop; t += units) {
-      const TileInfo ti = tile_info(args, t, BN, TILE_M, KB);
+    for (int w = 0; !stop; ++w) {
+      TileInfo ti;
+      if (!work_item(args, unit, units, w, BN, TILE_M, KB, ti)) break;
       for (int j = 0; j < ti.nk; ++j, ++it) {
         if (it % kSplitGroups != grp) continue;
         const int s = it % RST, l = it % LST;
@@ -471,10 +572,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint64_t* ebar = ebar_all + 2 * ew;
     uint32_t eph = 0;  // phase bits of ebar[0], ebar[1]
     int q = 0;         // boxes stored so far (alternates the two buffers)
-    for (int t = unit; t < total; t += units) {
-      const TileInfo ti = tile_info(args, t, BN, TILE_M, KB);
+    for (int w = 0;; ++w) {
+      TileInfo ti;
+      if (!work_item(args, unit, units, w, BN, TILE_M, KB, ti)) break;
       if (ti.skip) continue;
-      const int buf = tc & 1;
+      const int buf = tc % L::NACC;
       if (!PAIR && args.tma_c && args.splits == 1) {
         // Whole 32 x 32 boxes: lane = row in registers, written to shared memory with a
         // 128-byte swizzle (conflict-free), stored by one TMA store per box (rows and columns
@@ -499,7 +601,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           __syncwarp();
         }
         const bool have =
-            __all_sync(0xffffffffu, wait_bar(&acc_full[buf], (tc >> 1) & 1, abort_flag));
+            __all_sync(0xffffffffu, wait_bar(&acc_full[buf], (tc / L::NACC) & 1, abort_flag));
         if (!have) {
           if (dsm && rows_in)
             for (int b = 0; b < 2 && b < nch; ++b) wait_bar(&ebar[b], (eph >> b) & 1, abort_flag, false);
@@ -512,10 +614,45 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if ((dsm || pmm) && row < args.m)
           rv = (dsm ? args.rv1 : args.rv0)[(int64_t)ti.bz * args.m + row];
         bool ok = true;
+        // Stream-K piece of a tile cut between units: its partial (every column, unscaled)
+        // goes to this unit's slot and the accumulator is released; the piece that completes
+        // the count of this warp's 32 rows sums all pieces' partials below in place of the
+        // accumulator. Nothing waits for another unit.
+        const bool piece = ti.segs > 1;
+        int u_first = 0;
+        if (piece) {
+          const int64_t slot = sk_slot(args, unit, ti.sk_tile);
+#pragma unroll 1
+          for (int cc = 0; cc < BN / 32; ++cc) {
+            uint32_t r[32];
+            tmem_ld32(acc + (uint32_t)(cc * 32), r);
+            float4* dst = sk_chunk<BN>(args, slot, ew, cc) + lane;
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+              dst[32 * k] = make_float4(__uint_as_float(r[4 * k]), __uint_as_float(r[4 * k + 1]),
+                                   __uint_as_float(r[4 * k + 2]), __uint_as_float(r[4 * k + 3]));
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[buf]);
+          __threadfence();
+          __syncwarp();
+          int arrived = 0;
+          if (lane == 0) arrived = atomicAdd(&args.sk_cnt[ti.sk_tile * 4 + ew], 1);
+          arrived = __shfl_sync(0xffffffffu, arrived, 0);
+          if (arrived != ti.segs - 1) {
+            ++tc;
+            continue;
+          }
+          __threadfence();
+          if (lane == 0) args.sk_cnt[ti.sk_tile * 4 + ew] = 0;  // zero for the next launch
+          u_first = unit - ti.seg;
+        }
 #pragma unroll 1
         for (int cc = 0; cc < nch && rows_in; ++cc) {
           uint32_t r[32];
-          tmem_ld32(acc + (uint32_t)(cc * 32), r);
+          if (piece) sk_sum<BN>(args, u_first, ti.segs, ti.sk_tile, ew, lane, cc, r);
+          else tmem_ld32(acc + (uint32_t)(cc * 32), r);
           const int c0 = (int)ti.n0 + cc * 32;
           float4* box;
           if (dsm) {
@@ -582,15 +719,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             __syncwarp();
           }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        if (!piece) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        }
         ++tc;
         if (!ok) break;
         continue;
       }
       // tcgen05.ld is warp-collective: decide per warp.
-      const bool have = __all_sync(0xffffffffu, wait_bar(&acc_full[buf], (tc >> 1) & 1, abort_flag));
+      const bool have = __all_sync(0xffffffffu, wait_bar(&acc_full[buf], (tc / L::NACC) & 1, abort_flag));
       if (!have) break;
       tc_fence_after();
       const int64_t row = ti.m0 + row_off + 32 * ew + lane;
@@ -782,11 +921,60 @@ splitk_reduce_vec4(const float4* __restrict__ ws, int splits, GemmArgs<float> p)
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, bool PAIR>
+// Stream-K tail on (default) or off (TG_GEMM_STREAMK=0, for the probes that compare both).
+static bool streamk_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("TG_GEMM_STREAMK");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+// The stream-K partial slots and arrival counters of one (device, stream): allocated at the
+// stream's first stream-K product (2 slots of 128 x 256 floats per SM, 39 MB on B200, and
+// 8 counters per SM, zeroed on the stream), kept for the process. Products on one stream run
+// one after another, so they share it; a stream being captured gets none (no allocation
+// inside a capture) and its products run without the stream-K tail.
+struct SkWorkspace {
+  float* ws = nullptr;
+  int* cnt = nullptr;
+};
+
+static int sk_workspace(cudaStream_t stream, SkWorkspace* out) {
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, SkWorkspace> cache;
+  int dev = 0;
+  TG_CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find({dev, stream});
+  if (it != cache.end()) {
+    *out = it->second;
+    return TG_OK;
+  }
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  TG_CUDA_TRY(cudaStreamIsCapturing(stream, &cs));
+  if (cs != cudaStreamCaptureStatusNone)
+    return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: no stream-K workspace inside a capture");
+  const size_t units = (size_t)sm_count();
+  SkWorkspace w;
+  if (cudaMalloc(&w.ws, 2 * units * BM * 256 * sizeof(float)) != cudaSuccess ||
+      cudaMalloc(&w.cnt, 2 * units * 4 * sizeof(int)) != cudaSuccess) {
+    cudaGetLastError();
+    if (w.ws) cudaFree(w.ws);
+    return set_error(TG_ERR_OOM, "gemm_tc: stream-K workspace");
+  }
+  TG_CUDA_TRY(cudaMemsetAsync(w.cnt, 0, 2 * units * 4 * sizeof(int), stream));
+  cache[{dev, stream}] = w;
+  *out = w;
+  return TG_OK;
+}
+
+template <int BN, bool A_MN, bool B_MN, bool PAIR, bool ATM>
 static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
-  // A in tensor memory wherever the accumulators leave room (tiles up to 128 wide) and A is
-  // K-major: the MMAs then read only B from shared memory.
-  constexpr bool ATM = !PAIR && !A_MN && BN <= 128;
+  // ATM: A in tensor memory (single CTA, K-major A); the MMAs then read only B from shared
+  // memory, and the split pass writes no A lo there.
+  static_assert(!ATM || (!PAIR && !A_MN), "A in tensor memory: single CTA, K-major A");
   using L = Layout<BN, PAIR, ATM>;
   static_assert(L::RST >= 3 && L::LST >= 2, "GEMM rings too shallow");
   constexpr int TILE_M = PAIR ? 2 * BM : BM;
@@ -889,6 +1077,37 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
       a.tma_c = 1;
   }
   const int64_t tiles = (int64_t)a.m_tiles * a.n_tiles * a.batch * a.splits;
+  // Stream-K tail: when the tiles fill the SMs' last round only partly, the last one or two
+  // rounds' k-blocks are shared out evenly. Modelled makespan in k-blocks: the whole rounds,
+  // then the shared range and about one k-block of fix-up (partials written and summed).
+  // Only for long reductions (64 k-blocks or more per tile): measured on B200, the 8192-row
+  // products with k = 3072 gain 2-8 %, those with k = 768 lose 1-2 % (SMs of a part-empty
+  // last round run faster than the model assumes, which shrinks what there is to win).
+  if (!PAIR && a.splits == 1 && a.tma_c && p.epi == GEMM_EPI_STORE &&
+      p.kmode == GEMM_K_FULL && nk_all >= 64 && streamk_enabled()) {
+    const int64_t units = tiles < sm_count() ? tiles : sm_count();
+    const int64_t rounds = (tiles + units - 1) / units;
+    if (tiles > units && tiles % units) {
+      const int64_t whole = (tiles / units - 1) * units;
+      const int64_t wk = (tiles - whole) * nk_all;
+      const double cost =
+          (double)(whole / units * nk_all) + (double)((wk + units - 1) / units) + 1.0;
+      SkWorkspace w;
+      if (cost < 0.96 * (double)(rounds * nk_all)) {
+        if (sk_workspace(stream, &w) == TG_OK) {
+          a.sk_first = (int)whole;
+          a.sk_tiles = (int)(tiles - whole);
+          a.sk_nk = nk_all;
+          a.sk_q = wk / units;
+          a.sk_r = wk % units;
+          a.sk_ws = w.ws;
+          a.sk_cnt = w.cnt;
+        } else {
+          cudaGetLastError();
+        }
+      }
+    }
+  }
   if (PAIR) {
     const int pairs = (int)(tiles < max_pairs ? tiles : max_pairs);
     cudaLaunchConfig_t cfg = {};
@@ -926,13 +1145,31 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
   return check_launch(PAIR ? "gemm_tc(pair)" : "gemm_tc");
 }
 
+// A 256-wide tile with A in tensor memory keeps one accumulator (no epilogue overlap) to
+// make room for A; TG_GEMM_ATM256=0|1 chooses it for the probes that decide the default.
+static bool atm_wide() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("TG_GEMM_ATM256");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
 template <int BN, bool PAIR>
 static int launch_any(const GemmArgs<float>& p, bool a_mn, bool b_mn, int splits,
                       cudaStream_t stream) {
-  if (!a_mn && !b_mn) return launch<BN, false, false, PAIR>(p, splits, stream);
-  if (!a_mn && b_mn) return launch<BN, false, true, PAIR>(p, splits, stream);
-  if (a_mn && !b_mn) return launch<BN, true, false, PAIR>(p, splits, stream);
-  return launch<BN, true, true, PAIR>(p, splits, stream);
+  // A in tensor memory wherever the accumulators leave room (tiles up to 128 wide, or 256
+  // wide with one accumulator) and A is K-major.
+  constexpr bool kAtm = !PAIR && BN <= 128;
+  if (!PAIR && BN > 128 && !a_mn && atm_wide()) {
+    if (!b_mn) return launch<BN, false, false, PAIR, !PAIR>(p, splits, stream);
+    return launch<BN, false, true, PAIR, !PAIR>(p, splits, stream);
+  }
+  if (!a_mn && !b_mn) return launch<BN, false, false, PAIR, kAtm>(p, splits, stream);
+  if (!a_mn && b_mn) return launch<BN, false, true, PAIR, kAtm>(p, splits, stream);
+  if (a_mn && !b_mn) return launch<BN, true, false, PAIR, false>(p, splits, stream);
+  return launch<BN, true, true, PAIR, false>(p, splits, stream);
 }
 
 // CTA pairs are opt-in (TG_GEMM_PAIR=1). Measured on B200 they run at about 0.9x of the
