@@ -764,8 +764,10 @@ def run_ours(args: argparse.Namespace, wl: Workload) -> None:
     for _ in range(args.warmup):
         built.step(*built.dev_inputs)
     launches0 = int(lib.tg_launch_count())
+    fallbacks0 = int(lib.tg_gemm_fallback_count())
     sec = timed(args.steps, lambda: built.step(*built.dev_inputs), clocks)
     launches = int(lib.tg_launch_count()) - launches0
+    fallbacks = int(lib.tg_gemm_fallback_count()) - fallbacks0
     clock = clocks.stop()
     # The roofline pass: the same steps again with every tensor-core GEMM bracketed by CUDA
     # events (kept out of the value pass, whose launch rate they would slow).
@@ -823,6 +825,7 @@ def run_ours(args: argparse.Namespace, wl: Workload) -> None:
                 "h2d_bytes_per_step": int(built.h2d_bytes),
                 "d2h_bytes_per_step": int(built.d2h_bytes)},
         "gpu_launches": launches,
+        "gemm_fallbacks": fallbacks,  # fp32 products that could not run on the tensor cores
         "final_loss": last,
     }
     if rank == 0 and not args.no_hbm:

@@ -102,6 +102,10 @@ int tg_gemm_profile(int enable);
 int tg_gemm_profile_read(double* total_ms, int64_t* launches, double* flops);
 /* Kernels launched by this library since load (every entry point counts its own). */
 uint64_t tg_launch_count(void);
+/* fp32 products since load that the tensor-core kernel could not take (an operand or a
+ * stride off a 16-byte boundary) and that ran on the CUDA-core kernel instead. Reductions of
+ * at most 8 always run on the CUDA cores (a memory-bound outer product) and are not counted. */
+uint64_t tg_gemm_fallback_count(void);
 /* Reads (and with reset != 0 clears) the tensor-core GEMM's device status word: TG_OK, or
  * TG_ERR_TIMEOUT when a bounded pipeline wait gave up. Synchronous. */
 int tg_gemm_tc_status(int reset);

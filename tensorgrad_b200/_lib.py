@@ -95,6 +95,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tg_gemm_profile": (c_int, [c_int]),
     "tg_gemm_profile_read": (c_int, [POINTER(c_double), POINTER(c_int64), POINTER(c_double)]),
     "tg_launch_count": (ctypes.c_uint64, []),
+    "tg_gemm_fallback_count": (ctypes.c_uint64, []),
     "tg_gemm_batched": (c_int, [c_int, c_int, c_int, i64, i64, i64, dbl, vp, i64, i64, vp, i64,
                                 i64, dbl, vp, i64, i64, i64, vp]),
     "tg_linear_forward_scratch_bytes": (sz, [c_int, i64, i64, i64]),

@@ -55,6 +55,7 @@ struct ProfileRec {
 std::vector<ProfileRec> g_prof;
 std::vector<cudaEvent_t> g_event_pool;
 bool g_prof_on = false;
+unsigned long long g_fallbacks = 0;  // fp32 products the tensor-core kernel could not take
 
 cudaEvent_t take_event() {
   if (!g_event_pool.empty()) {
@@ -165,10 +166,14 @@ int gemm_dispatch(GemmArgs<T> p, bool allow_tc, cudaStream_t s) {
     // C = beta * C (+ bias): run the SIMT kernel, whose k loop is empty.
     return gemm_simt<T>(p, s);
   }
+  if (gemm_smallk_applies(p)) return gemm_smallk<T>(p, s);
   if constexpr (sizeof(T) == 4) {
     if (allow_tc && !force_simt()) {
       const int rc = tc_timed(p, s);
       if (rc != TG_ERR_UNSUPPORTED) return rc;
+      // Not a tensor-core shape (an operand off a 16-byte boundary, a stride not a multiple
+      // of 4 floats): counted, so that tests can require none on the training steps.
+      __atomic_fetch_add(&g_fallbacks, 1ull, __ATOMIC_RELAXED);
     }
   }
   return gemm_simt<T>(p, s);
@@ -192,6 +197,10 @@ template int gemm_run<double>(const GemmArgs<double>&, cudaStream_t);
 using namespace tg;
 
 extern "C" {
+
+uint64_t tg_gemm_fallback_count(void) {
+  return __atomic_load_n(&g_fallbacks, __ATOMIC_RELAXED);
+}
 
 int tg_gemm(int dtype, int trans_a, int trans_b, int64_t m, int64_t n, int64_t k, double alpha,
             const void* a, int64_t lda, const void* b, int64_t ldb, double beta, void* c,

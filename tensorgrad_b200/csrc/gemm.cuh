@@ -69,6 +69,11 @@ __host__ __device__ __forceinline__ int64_t gemm_c_offset(const GemmArgs<T>& p, 
 
 template <typename T>
 int gemm_simt(const GemmArgs<T>& p, cudaStream_t stream);
+// Reductions of at most 8 (memory-bound outer products) on the CUDA cores.
+template <typename T>
+bool gemm_smallk_applies(const GemmArgs<T>& p);
+template <typename T>
+int gemm_smallk(const GemmArgs<T>& p, cudaStream_t stream);
 
 // The library's GEMM: the tensor-core kernel for fp32 where the TMA can address the
 // operands, the SIMT kernel otherwise (and for fp64); live-profiled like tg_gemm.

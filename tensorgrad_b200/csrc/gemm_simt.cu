@@ -87,7 +87,92 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(GemmArgs<T> p) {
   }
 }
 
+// Products whose reduction is at most kSmallK long (an LSTM/GRU input projection from 2
+// inputs: 51200 x 2048 outputs from k = 2): the output dominates the bytes, so each thread
+// writes 4 consecutive columns of one row, from the row's k values (a warp shares its row)
+// and B's k x 4 block (L1 hits: B is k x n), with fp32/fp64 FMAs in k order.
+constexpr int kSmallK = 8;
+
+template <typename T>
+__global__ void __launch_bounds__(256) gemm_smallk_kernel(GemmArgs<T> p, bool vec) {
+  const int64_t nq = (p.n + 3) / 4;
+  const int64_t total = p.m * nq;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / nq;
+    const int64_t c0 = (i - row * nq) * 4;
+    T a[kSmallK];
+#pragma unroll
+    for (int k = 0; k < kSmallK; ++k)
+      a[k] = k < p.k ? (p.trans_a ? p.a[k * p.lda + row] : p.a[row * p.lda + k]) : T(0);
+    T acc[4] = {T(0), T(0), T(0), T(0)};
+#pragma unroll
+    for (int k = 0; k < kSmallK; ++k) {
+      if (k >= p.k) break;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t col = c0 + j < p.n ? c0 + j : p.n - 1;
+        const T bkj = p.trans_b ? p.b[col * p.ldb + k] : p.b[k * p.ldb + col];
+        acc[j] = fma(a[k], bkj, acc[j]);
+      }
+    }
+    T* crow = p.c + row * p.ldc;
+    T v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t col = c0 + j;
+      v[j] = p.alpha * acc[j];
+      if (col < p.n) {
+        if (p.beta != T(0)) v[j] += p.beta * crow[col];
+        if (p.bias) v[j] += p.bias[col];
+      }
+    }
+    if constexpr (sizeof(T) == 4) {
+      if (vec && c0 + 4 <= p.n) {
+        *reinterpret_cast<float4*>(crow + c0) = make_float4(v[0], v[1], v[2], v[3]);
+        continue;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (c0 + j < p.n) crow[c0 + j] = v[j];
+  }
+}
+
 }  // namespace
+
+template <typename T>
+bool gemm_smallk_applies(const GemmArgs<T>& p) {
+  return p.k >= 1 && p.k <= kSmallK && p.batch == 1 && p.heads == 1 && p.c_hw == 0 &&
+         p.a_fold == 0 && p.epi == GEMM_EPI_STORE && p.kmode == GEMM_K_FULL;
+}
+
+template <typename T>
+int gemm_smallk(const GemmArgs<T>& p, cudaStream_t stream) {
+  if (p.m == 0 || p.n == 0) return TG_OK;
+  const bool vec = sizeof(T) == 4 && p.ldc % 4 == 0 &&
+                   (reinterpret_cast<uintptr_t>(p.c) & 15) == 0;
+  const int64_t work = p.m * ((p.n + 3) / 4);
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        sms <= 0) {
+      cudaGetLastError();
+      sms = 148;
+    }
+  }
+  const int64_t cap = (int64_t)sms * 16;
+  const int blocks = (int)((work + 255) / 256 < cap ? (work + 255) / 256 : cap);
+  gemm_smallk_kernel<T><<<blocks, 256, 0, stream>>>(p, vec);
+  return check_launch("gemm_smallk");
+}
+
+template bool gemm_smallk_applies<float>(const GemmArgs<float>&);
+template bool gemm_smallk_applies<double>(const GemmArgs<double>&);
+template int gemm_smallk<float>(const GemmArgs<float>&, cudaStream_t);
+template int gemm_smallk<double>(const GemmArgs<double>&, cudaStream_t);
 
 template <typename T>
 int gemm_simt(const GemmArgs<T>& p, cudaStream_t stream) {

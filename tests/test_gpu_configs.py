@@ -26,9 +26,13 @@ REL = 1e-4
 
 
 def test_gpt2_width_train_step_matches_oracle():
+    from tensorgrad_b200._lib import lib
+
     cfg = ogpt.Config(vocab_size=50304, block_size=1024, n_layer=2, n_head=12, n_embd=768)
     seed, batch = 21, 2
+    before = lib.tg_gemm_fallback_count()
     recs = run_steps(cfg, batch, 1024, seed, 1, 1.0, np.float32, device_ids=True)
+    assert lib.tg_gemm_fallback_count() == before  # every product on the tensor cores
     ref = ogpt.train_step(ogpt.init_params(cfg, seed),
                           *ogpt.synthetic_batch(cfg, batch, 1024, seed + 1), cfg, max_norm=1.0)
     assert ref["total_norm"] > 1.0  # clipping is active

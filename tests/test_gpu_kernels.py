@@ -40,7 +40,8 @@ def tensor(a, dtype, requires_grad=True):
 # The last two are large enough for CTA pairs (256-row tiles, cta_group::2) when those are
 # enabled: 128- and 256-wide tiles with ragged rows (the odd CTA of the last pair has none)
 # and ragged columns (see test_gemm_cta_pairs_match_float64).
-GEMM_SHAPES = [(1, 1, 1), (7, 5, 3), (128, 128, 32), (130, 257, 100), (300, 64, 768),
+# (Reductions of at most 8 take the small-k kernel: test_gemm_small_k.)
+GEMM_SHAPES = [(1, 1, 9), (7, 5, 12), (128, 128, 32), (130, 257, 100), (300, 64, 768),
                (64, 300, 36), (1000, 333, 68), (8192 // 16, 3072 // 4, 768), (2100, 1000, 100),
                (4096, 2000, 300)]
 
@@ -85,6 +86,49 @@ def test_gemm_cta_pairs_match_float64():
                          env=env, cwd=root, capture_output=True, text=True, timeout=600)
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-2000:]
     assert "8 passed" in res.stdout, res.stdout[-2000:]
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 1, 1), (7, 5, 3), (51200 // 16, 2048, 2), (333, 130, 8)])
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("dt", ["f32", "f64"])
+def test_gemm_small_k(m, n, k, ta, tb, dt):
+    """Reductions of at most 8 (the LSTM/GRU input projection from 2 inputs) run on the
+    CUDA-core small-k kernel: plain FMAs, so fp32 and fp64 both land within rounding."""
+    from tensorgrad_b200 import device
+    from tensorgrad_b200._lib import F32, F64, check, lib
+
+    np_dt, code, rel = (np.float32, F32, 1e-6) if dt == "f32" else (np.float64, F64, 1e-14)
+    rng = np.random.default_rng(m + n + k + 10 * ta + tb)
+    a = rng.standard_normal((k, m) if ta else (m, k))
+    b = rng.standard_normal((n, k) if tb else (k, n))
+    c0 = rng.standard_normal((m, n))
+    bias = rng.standard_normal(n)
+    ref = 0.5 * ((a.T if ta else a) @ (b.T if tb else b)) + 0.25 * c0 + bias
+    da, db = device.from_numpy(a.astype(np_dt)), device.from_numpy(b.astype(np_dt))
+    dc, dbias = device.from_numpy(c0.astype(np_dt)), device.from_numpy(bias.astype(np_dt))
+    before = lib.tg_gemm_fallback_count()
+    check(lib.tg_gemm(code, ta, tb, m, n, k, 0.5, da.ptr, a.shape[1], db.ptr, b.shape[1], 0.25,
+                      dc.ptr, n, dbias.ptr, device.stream()))
+    assert_parity(dc.numpy(), ref, rel, f"small-k gemm {m}x{n}x{k} ta={ta} tb={tb}")
+    assert lib.tg_gemm_fallback_count() == before
+
+
+def test_gemm_fallback_is_counted():
+    """An fp32 product the tensor-core kernel cannot take (a leading dimension that is not a
+    multiple of 4 floats) runs on the CUDA-core kernel, correctly, and is counted."""
+    from tensorgrad_b200 import device
+    from tensorgrad_b200._lib import F32, check, lib
+
+    rng = np.random.default_rng(3)
+    a, b = rng.standard_normal((64, 30)), rng.standard_normal((30, 50))
+    da = device.from_numpy(a.astype(np.float32))
+    db = device.from_numpy(b.astype(np.float32))
+    dc = device.empty((64, 50), np.float32)
+    before = lib.tg_gemm_fallback_count()
+    check(lib.tg_gemm(F32, 0, 0, 64, 50, 30, 1.0, da.ptr, 30, db.ptr, 50, 0.0, dc.ptr, 50, None,
+                      device.stream()))
+    assert_parity(dc.numpy(), a @ b, 1e-5, "fallback gemm")
+    assert lib.tg_gemm_fallback_count() == before + 1
 
 
 def test_gemm_simt_fp64():
@@ -453,7 +497,7 @@ def test_tensor_core_tf32_input_conversion_and_plain_tf32_mode():
 
     ulp = 2.0**-10
     xs = np.array([1 + 0.75 * ulp, 1 + 0.5 * ulp, 1 + 1.5 * ulp, -(1 + 0.75 * ulp)] * 32)
-    m, k, n = xs.size, 4, 128
+    m, k, n = xs.size, 16, 128  # k > 8: the tensor-core kernel, not the small-k one
     a = np.zeros((m, k), np.float32)
     a[:, 0] = xs
     b = np.zeros((k, n), np.float32)

@@ -126,9 +126,15 @@ def test_regressor_two_steps_match_reference_fixture(cell, dtype):
 @pytest.mark.parametrize("cell", ["lstm", "gru"])
 def test_recurrent_config_step_matches_oracle(cell):
     # The LSTM / GRU configuration: 100 steps, batch 512, hidden 512, input 2.
+    # Every fp32 product of the step runs on the tensor cores, or (the input projection from
+    # 2 inputs) on the small-k kernel: none falls back to the CUDA-core GEMM.
+    from tensorgrad_b200._lib import lib
+
     cfg = ornn.Config(cell=cell)
     seed, batch = 9, 512
+    before = lib.tg_gemm_fallback_count()
     recs = run_regressor(cfg, batch, seed, 1, np.float32)
+    assert lib.tg_gemm_fallback_count() == before
     x, y = ornn.synthetic_batch(cfg, batch, seed + 1)
     ref = ornn.train_step(ornn.init_params(cfg, seed), cfg, x, y)
     check_steps(recs, [ref], 1e-4)
