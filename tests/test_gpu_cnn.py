@@ -80,12 +80,15 @@ def test_conv2d_matches_naive_loops(rng, stride, pad):
     assert_parity(y.numpy(), naive_conv2d(x, w, b, stride, pad), 1e-4, "conv vs loops")
 
 
-@pytest.mark.parametrize(("k", "stride", "pad"), [(2, 2, 0), (3, 1, 1), (3, 2, 1), (2, 1, 0)])
-def test_max_pool2d_ties_and_nans_follow_argmax(k, stride, pad):
+# (8, 12) and (16, 8) with 2 x 2 windows at stride 2 take the vectorised 2 x 2 kernels.
+@pytest.mark.parametrize(("k", "stride", "pad", "hw"),
+                         [(2, 2, 0, (7, 6)), (3, 1, 1, (7, 6)), (3, 2, 1, (7, 6)),
+                          (2, 1, 0, (7, 6)), (2, 2, 0, (8, 12)), (2, 2, 0, (16, 8))])
+def test_max_pool2d_ties_and_nans_follow_argmax(k, stride, pad, hw):
     import tensorgrad_b200 as tg
 
-    rng = np.random.default_rng(k * 10 + stride)
-    x = np.round(rng.standard_normal((2, 3, 7, 6)))
+    rng = np.random.default_rng(k * 10 + stride + hw[1])
+    x = np.round(rng.standard_normal((2, 3, *hw)))
     x.reshape(-1)[::13] = np.nan
     (t,) = tensors(np.float32, x)
     out = tg.max_pool2d(t, k, stride, pad)
