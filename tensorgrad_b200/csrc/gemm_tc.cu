@@ -977,6 +977,9 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
   static_assert(!ATM || (!PAIR && !A_MN), "A in tensor memory: single CTA, K-major A");
   using L = Layout<BN, PAIR, ATM>;
   static_assert(L::RST >= 3 && L::LST >= 2, "GEMM rings too shallow");
+  // A lo slot is known free from the raw ring's barrier of the k-block that last used it
+  // (one commit serves both rings): that barrier must not have been re-armed since.
+  static_assert(L::LST <= L::RST, "the lo ring may not be deeper than the raw ring");
   constexpr int TILE_M = PAIR ? 2 * BM : BM;
   auto kernel = gemm_tc_kernel<BN, A_MN, B_MN, PAIR, ATM>;
   CUtensorMap ta, tb;
