@@ -107,11 +107,15 @@ struct Layout {
   static constexpr uint32_t LO = (ATM ? 0 : A_BYTES) + B_BYTES;    // lo slot: A lo, B lo
   // Two accumulators (the epilogue of one tile overlaps the next tile's k-blocks), except
   // for 256-wide tiles with A in tensor memory, where one accumulator leaves TMEM room for A.
-  static constexpr int NACC = (ATM && BN > 128) ? 1 : 2;
+  static constexpr int NACC = (ATM && BN > 192) ? 1 : 2;
   static constexpr uint32_t ACC_COLS = NACC * BN;
   // ATM (A in tensor memory): A's hi and lo of each lo slot go to TMEM columns after the
   // accumulators (2 * BK per slot).
-  static constexpr uint32_t TMEM_COLS = ATM ? 512 : ACC_COLS;
+  // tcgen05.alloc takes a power of two from 32 to 512 columns.
+  static constexpr uint32_t TMEM_COLS =
+      ATM ? 512 : (ACC_COLS <= 32 ? 32 : ACC_COLS <= 64 ? 64 : ACC_COLS <= 128 ? 128
+                                       : ACC_COLS <= 256 ? 256 : 512);
+  static_assert(ACC_COLS <= 512, "accumulators exceed tensor memory");
   // Slot counts: the lo ring 2 (3 when its slots are small), bounded by TMEM with ATM; the
   // raw ring whatever fits in 193 KB beside it (at most 8).
   static constexpr int LO_TMEM_CAP = ATM ? (int)((512 - ACC_COLS) / (2 * BK)) : 8;
@@ -1162,10 +1166,10 @@ static bool atm_wide() {
 template <int BN, bool PAIR>
 static int launch_any(const GemmArgs<float>& p, bool a_mn, bool b_mn, int splits,
                       cudaStream_t stream) {
-  // A in tensor memory wherever the accumulators leave room (tiles up to 128 wide, or 256
-  // wide with one accumulator) and A is K-major.
-  constexpr bool kAtm = !PAIR && BN <= 128;
-  if (!PAIR && BN > 128 && !a_mn && atm_wide()) {
+  // A in tensor memory wherever the accumulators leave room (tiles up to 192 wide; 256 wide
+  // only with one accumulator) and A is K-major.
+  constexpr bool kAtm = !PAIR && BN <= 192;
+  if (!PAIR && BN > 192 && !a_mn && atm_wide()) {
     if (!b_mn) return launch<BN, false, false, PAIR, !PAIR>(p, splits, stream);
     return launch<BN, false, true, PAIR, !PAIR>(p, splits, stream);
   }
@@ -1256,7 +1260,7 @@ int gemm_tc_f32(const GemmArgs<float>& p, cudaStream_t stream) {
   if (forced_bn < 0) {
     const char* e = getenv("TG_GEMM_BN");
     const int v = e ? atoi(e) : 0;
-    forced_bn = (v == 64 || v == 128 || v == 256) ? v : 0;
+    forced_bn = (v == 64 || v == 128 || v == 192 || v == 256) ? v : 0;
   }
   if (forced_bn && !(p.a_fold > 0 && p.a_fold % bk_of(forced_bn))) {
     best = forced_bn;
@@ -1280,6 +1284,7 @@ int gemm_tc_f32(const GemmArgs<float>& p, cudaStream_t stream) {
   }
   if (best == 64) return tc::launch_any<64, false>(p, a_mn, b_mn, splits, stream);
   if (best == 128) return tc::launch_any<128, false>(p, a_mn, b_mn, splits, stream);
+  if (best == 192) return tc::launch_any<192, false>(p, a_mn, b_mn, splits, stream);
   return tc::launch_any<256, false>(p, a_mn, b_mn, splits, stream);
 }
 
