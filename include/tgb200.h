@@ -117,6 +117,10 @@ int tg_attention_tc_status(int reset);
  * first wait on a load runs out, TG_ERR_TIMEOUT is recorded and the kernel drains and
  * returns with nothing in flight. Synchronous. */
 int tg_attention_set_wait_test(int64_t budget_cycles, int withhold_loads);
+/* Test support (no reference counterpart): y[i] = the fp32 exponential the fused attention
+ * kernels compute on the FMA pipe for part of their softmax numerators (range reduction plus
+ * a fitted polynomial; see csrc/expfma.cuh), so a test can bound its error. */
+int tg_test_exp_fma(int64_t n, const float* x, float* y, void* stream);
 /* Strided-batched GEMM: `batch` products at element offsets i*stride_{a,b,c}. */
 int tg_gemm_batched(int dtype, int trans_a, int trans_b, int64_t m, int64_t n, int64_t k,
                     double alpha, const void* a, int64_t lda, int64_t stride_a, const void* b,

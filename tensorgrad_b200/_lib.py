@@ -91,6 +91,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tg_gemm_tc_status": (c_int, [c_int]),
     "tg_attention_tc_status": (c_int, [c_int]),
     "tg_attention_set_wait_test": (c_int, [i64, c_int]),
+    "tg_test_exp_fma": (c_int, [i64, vp, vp, vp]),
     "tg_set_matmul_precision": (c_int, [c_int]),
     "tg_gemm_profile": (c_int, [c_int]),
     "tg_gemm_profile_read": (c_int, [POINTER(c_double), POINTER(c_int64), POINTER(c_double)]),

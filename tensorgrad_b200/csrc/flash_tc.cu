@@ -19,6 +19,7 @@
 // [D + 256, 3 D + 256), the max exchange [3 D + 256, 3 D + 260). Every wait is bounded; on expiry the kernel records TG_ERR_TIMEOUT in
 // this unit's status word, stops, drains and frees its TMEM.
 #include "common.cuh"
+#include "expfma.cuh"
 #include "tc_ptx.cuh"
 
 namespace tg {
@@ -31,6 +32,22 @@ constexpr int kFThreads = 512;
 constexpr int kSplit0 = 4, kSoft0 = 12;
 // The P / dS kernel: split warps 4..7, element-wise warps 8..15.
 constexpr int kPSplit0 = 4, kPElem0 = 8;
+
+// Every kExpFmaEvery-th exponential of the softmax warps (by column, fixed at compile time)
+// can run on the FMA pipe (exp_fma) instead of the XU pipe's approximate exponential; 0 =
+// none. Measured on B200 (causal MHA 16 x 8 x 512 x 64, forward + backward): every 3rd
+// 2648 and every 2nd 2608 calls/s against 2706 with none, so the XU pipe, although the
+// busiest unit in the counters, is not what bounds these kernels, and the default is none.
+#ifndef TG_EXP_FMA_EVERY
+#define TG_EXP_FMA_EVERY 0
+#endif
+constexpr int kExpFmaEvery = TG_EXP_FMA_EVERY;
+
+__device__ __forceinline__ float softmax_exp(float x, int c) {
+  if (kExpFmaEvery > 0 && c % (kExpFmaEvery > 0 ? kExpFmaEvery : 1) == kExpFmaEvery - 1)
+    return exp_fma(x);
+  return __expf(x);
+}
 
 // Set only by tg_attention_set_wait_test: the forward's TMA producer then issues no load at
 // all (not even the first item's Q), so the first wait on a load times out and the kernel's
@@ -357,7 +374,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
         float lsum = 0.f;
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          const float p = __expf(__uint_as_float(r0[c]) - m_new);
+          const float p = softmax_exp(__uint_as_float(r0[c]) - m_new, c);
           lsum += p;
           r0[c] = __float_as_uint(p);
         }
@@ -746,7 +763,7 @@ attn_pds_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         for (int c = 0; c < 32; ++c) {
           const int64_t key = key0 + c;
           const bool valid = key < a.Tk && (!a.causal || key <= row);
-          const float e = __expf(__fmul_rn(__uint_as_float(sv[c]), a.scale) - lse_r);
+          const float e = softmax_exp(__fmul_rn(__uint_as_float(sv[c]), a.scale) - lse_r, c);
           const float p = valid ? e : 0.f;
           sv[c] = __float_as_uint(p);
           dv[c] = __float_as_uint(p * (__uint_as_float(dv[c]) - delta_r) * a.scale);
@@ -877,6 +894,28 @@ extern "C" int tg_attention_tc_status(int reset) {
 // seconds) and, with withhold_loads != 0, a forward whose producer issues no load, so that
 // the first wait on a load runs out, the kernel records TG_ERR_TIMEOUT and drains.
 // Synchronous; affects later launches of this unit's kernels only.
+namespace tg {
+namespace tc {
+namespace {
+__global__ void exp_fma_test_kernel(const float* __restrict__ x, float* __restrict__ y,
+                                    int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = exp_fma(x[i]);
+}
+}  // namespace
+}  // namespace tc
+}  // namespace tg
+
+// Test-only: y = exp_fma(x) elementwise (the FMA-pipe exponential of the fused kernels).
+extern "C" int tg_test_exp_fma(int64_t n, const float* x, float* y, void* stream) {
+  TG_CHECK_ARG(n >= 0 && (n == 0 || (x && y)), "tg_test_exp_fma: bad arguments");
+  if (n == 0) return TG_OK;
+  const int64_t blocks = (n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184;
+  tg::tc::exp_fma_test_kernel<<<(int)blocks, 256, 0, tg::as_stream(stream)>>>(x, y, n);
+  return tg::check_launch("exp_fma test");
+}
+
 extern "C" int tg_attention_set_wait_test(int64_t budget_cycles, int withhold_loads) {
   const long long b = budget_cycles > 0 ? (long long)budget_cycles : tg::tc::kTimeoutCycles;
   const int w = withhold_loads ? 1 : 0;

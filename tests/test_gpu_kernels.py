@@ -522,3 +522,25 @@ def test_tensor_core_tf32_input_conversion_and_plain_tf32_mode():
     matched = [name for name, v in modes.items() if np.array_equal(got, v)]
     print("tensor-core fp32->tf32 conversion:", matched)
     assert matched, f"TF32 conversion matches no known rounding: {got[:4]}"
+
+
+def test_fma_pipe_exponential_error_bound():
+    """The exponential the fused attention kernels compute on the FMA pipe for part of their
+    softmax numerators: within 3e-7 relative of exp in float64 over [-87, 8] (the reduction
+    x - n ln2 is exact, the fitted polynomial ~8e-8), NaN stays NaN, and exactly 0 below
+    -87.3 (e^x < 2^-126) and for -inf."""
+    from tensorgrad_b200 import device
+    from tensorgrad_b200._lib import check, lib
+
+    x = np.concatenate([np.linspace(-87.0, 8.0, 400001), [0.0, -0.0, 1e-30, -1e-30]])
+    x32 = x.astype(np.float32)
+    dx, dy = device.from_numpy(x32), device.empty(x32.shape, np.float32)
+    check(lib.tg_test_exp_fma(x32.size, dx.ptr, dy.ptr, device.stream()))
+    got = dy.numpy().astype(np.float64)
+    rel = np.abs(got / np.exp(x32.astype(np.float64)) - 1.0)
+    assert rel.max() <= 3e-7, f"max relative error {rel.max()} at {x32[np.argmax(rel)]}"
+    tail = np.array([-np.inf, -87.31, -88.5, -100.0, -1e30, np.nan], dtype=np.float32)
+    dt, dz = device.from_numpy(tail), device.empty(tail.shape, np.float32)
+    check(lib.tg_test_exp_fma(tail.size, dt.ptr, dz.ptr, device.stream()))
+    z = dz.numpy()
+    assert np.all(z[:5] == 0.0) and np.isnan(z[5])
