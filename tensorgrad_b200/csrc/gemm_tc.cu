@@ -71,6 +71,9 @@ struct TcArgs {
   // ([2 * units][BM][BN], slot 2u for the first piece of unit u's range, 2u + 1 for its last)
   // and counts itself in sk_cnt ([sk_tiles][4], per epilogue warp); the piece that completes
   // the count sums all partials in piece order and writes the tile. No piece waits for another.
+  // 1: the MN-major operand has the chunked 5-D map (one copy per k-block instead of one per
+  // 32-wide chunk).
+  int a_chunked, b_chunked;
   int sk_first, sk_tiles, sk_nk;
   int64_t sk_q, sk_r;
   float* sk_ws;
@@ -342,7 +345,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           const int hb = args.b_bcast ? 0 : hh, bb = args.b_bcast ? 0 : bo;
           const int am0 = (int)(ti.m0 + row_off);
           const int bn0 = (int)ti.n0 + (int)rank * L::B_ROWS;
-          if (A_MN) {
+          if (A_MN && args.a_chunked) {
+            tma_load_5d(a_raw, &tmA, &full[s], 0, k0, am0 / 32, ha, ba);
+          } else if (A_MN) {
 #pragma unroll
             for (int c = 0; c < BM / 32; ++c)
               tma_load_4d(a_raw + c * 32 * KB * 4, &tmA, &full[s], am0 + 32 * c, k0, ha, ba);
@@ -351,7 +356,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           } else {
             tma_load_4d(a_raw, &tmA, &full[s], k0, am0, ha, ba);
           }
-          if (B_MN) {
+          if (B_MN && args.b_chunked) {
+            tma_load_5d(b_raw, &tmB, &full[s], 0, k0, bn0 / 32, hb, bb);
+          } else if (B_MN) {
 #pragma unroll
             for (int c = 0; c < L::B_ROWS / 32; ++c)
               tma_load_4d(b_raw + c * 32 * KB * 4, &tmB, &full[s], bn0 + 32 * c, k0, hb, bb);
@@ -925,6 +932,17 @@ splitk_reduce_vec4(const float4* __restrict__ ws, int splits, GemmArgs<float> p)
   }
 }
 
+// Chunked 5-D maps for MN-major operands on (default) or off (TG_GEMM_CHUNKED=0, for the
+// probes that compare both).
+static bool chunked_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("TG_GEMM_CHUNKED");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 // Stream-K tail on (default) or off (TG_GEMM_STREAMK=0, for the probes that compare both).
 static bool streamk_enabled() {
   static int v = -1;
@@ -999,14 +1017,30 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
   const int64_t nb = p.batch / p.heads;
   const int64_t ah = a_bcast ? 1 : p.heads, an = a_bcast ? 1 : nb;
   const int64_t bh = b_bcast ? 1 : p.heads, bn = b_bcast ? 1 : nb;
-  if (A_MN)
+  // MN-major operands whose MN extent is a multiple of 32 (no box reaches past a row) take
+  // the chunked map: one copy per k-block.
+  bool a_chunked = false, b_chunked = false;
+  if (A_MN && p.m % 32 == 0 && chunked_enabled() &&
+      make_map(&ta, p.a, p.m, p.k, p.lda, ah, p.stride_ah, an, p.stride_a, 32, KB, kSwMN,
+               BM / 32) == TG_OK)
+    a_chunked = true;
+  if (A_MN && !a_chunked) {
+    cudaGetLastError();
     rc = make_map(&ta, p.a, p.m, p.k, p.lda, ah, p.stride_ah, an, p.stride_a, 32, KB, kSwMN);
-  else if (p.a_fold > 0)
+  } else if (A_MN) {
+    rc = TG_OK;
+  } else if (p.a_fold > 0)
     rc = make_map(&ta, p.a, p.a_fold, p.m, p.lda, 1, 0, p.k / p.a_fold, p.stride_a, KB, BM,
                   kSwK);
   else rc = make_map(&ta, p.a, p.k, p.m, p.lda, ah, p.stride_ah, an, p.stride_a, KB, BM, kSwK);
   if (rc != TG_OK) return rc;
-  if (B_MN)
+  if (B_MN && p.n % 32 == 0 && chunked_enabled() &&
+      make_map(&tb, p.b, p.n, p.k, p.ldb, bh, p.stride_bh, bn, p.stride_b, 32, KB, kSwMN,
+               L::B_ROWS / 32) == TG_OK)
+    b_chunked = true;
+  if (B_MN && b_chunked)
+    rc = TG_OK;
+  else if (B_MN)
     rc = make_map(&tb, p.b, p.n, p.k, p.ldb, bh, p.stride_bh, bn, p.stride_b, 32, KB, kSwMN);
   else
     rc = make_map(&tb, p.b, p.k, p.n, p.ldb, bh, p.stride_bh, bn, p.stride_b, KB, L::B_ROWS,
@@ -1068,6 +1102,8 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
   // no NCHW scatter, no accumulation into C) whose rows suit a tensor map.
   CUtensorMap tcm = ta, txm = ta;
   a.tma_c = 0;
+  a.a_chunked = a_chunked;
+  a.b_chunked = b_chunked;
   {
     auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
     const bool strides_ok = p.ldc % 4 == 0 && (p.heads == 1 || p.stride_ch % 4 == 0) &&

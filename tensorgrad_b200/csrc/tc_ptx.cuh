@@ -153,6 +153,18 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// 5-D form: an MN-major operand whose MN dimension is split as (32, chunk), so one copy brings
+// several 32-wide chunks ([chunk][k][32] in shared memory, the layout of one copy per chunk).
+__device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int x, int y, int c, int h, int b) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(c), "r"(h),
+      "r"(b)
+      : "memory");
+}
+
 // TMA store of a shared-memory box (bulk-group completion) and its group bookkeeping.
 __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int x,
                                              int y, int h, int b) {
@@ -372,13 +384,22 @@ static int make_map_uncached(CUtensorMap* map, const float* ptr, int64_t inner, 
                              int64_t bstride, uint32_t box_inner, uint32_t box_rows,
                              CUtensorMapSwizzle swizzle);
 
+static int make_map_chunked_uncached(CUtensorMap* map, const float* ptr, int64_t inner,
+                                     int64_t rows, int64_t ld, int64_t heads, int64_t hstride,
+                                     int64_t nb, int64_t bstride, uint32_t box_rows,
+                                     uint32_t box_chunks);
+
+// chunks > 0: the MN-major 5-D map (inner split as 32 x inner / 32; inner % 32 == 0), boxes of
+// 32 x box_rows x chunks; otherwise the 4-D map with boxes of box_inner x box_rows.
 static int make_map(CUtensorMap* map, const float* ptr, int64_t inner, int64_t rows, int64_t ld,
                     int64_t heads, int64_t hstride, int64_t nb, int64_t bstride,
-                    uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
+                    uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swizzle,
+                    uint32_t chunks = 0) {
   int dev = 0;
   cudaGetDevice(&dev);
   MapKey key{ptr, {inner, rows, ld, heads, hstride, nb, bstride,
-                   ((int64_t)box_inner << 32) | ((int64_t)box_rows << 8) | (int64_t)swizzle},
+                   ((int64_t)box_inner << 32) | ((int64_t)chunks << 20) |
+                       ((int64_t)box_rows << 8) | (int64_t)swizzle},
              dev};
   {
     std::lock_guard<std::mutex> lock(g_map_mutex);
@@ -388,8 +409,10 @@ static int make_map(CUtensorMap* map, const float* ptr, int64_t inner, int64_t r
       return TG_OK;
     }
   }
-  const int rc = make_map_uncached(map, ptr, inner, rows, ld, heads, hstride, nb, bstride,
-                                   box_inner, box_rows, swizzle);
+  const int rc = chunks ? make_map_chunked_uncached(map, ptr, inner, rows, ld, heads, hstride,
+                                                     nb, bstride, box_rows, chunks)
+                      : make_map_uncached(map, ptr, inner, rows, ld, heads, hstride, nb,
+                                          bstride, box_inner, box_rows, swizzle);
   if (rc == TG_OK) {
     std::lock_guard<std::mutex> lock(g_map_mutex);
     if (g_map_cache.size() >= kMapCacheCap) g_map_cache.clear();
@@ -417,6 +440,34 @@ static int make_map_uncached(CUtensorMap* map, const float* ptr, int64_t inner, 
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: tensor map encode failed (%d)", (int)r);
+  return TG_OK;
+}
+
+static int make_map_chunked_uncached(CUtensorMap* map, const float* ptr, int64_t inner,
+                                     int64_t rows, int64_t ld, int64_t heads, int64_t hstride,
+                                     int64_t nb, int64_t bstride, uint32_t box_rows,
+                                     uint32_t box_chunks) {
+  EncodeFn enc = get_encode();
+  if (!enc) return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: cuTensorMapEncodeTiled unavailable");
+  if (inner % 32) return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: chunked map needs inner % 32");
+  const int64_t hs = heads > 1 ? hstride : rows * ld;
+  const int64_t bs = nb > 1 ? bstride : (heads > 1 ? heads * hstride : rows * ld);
+  if (hs <= 0 || bs <= 0 || (hs % 4) || (bs % 4))
+    return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: head/batch strides not 16-byte multiples");
+  // (32 along MN, rows along K, chunks of 32 along MN, head, batch): a box of box_chunks
+  // chunks lands as [chunk][row][32], the same bytes as one 32-wide box per chunk.
+  cuuint64_t dims[5] = {32, (cuuint64_t)rows, (cuuint64_t)(inner / 32), (cuuint64_t)heads,
+                        (cuuint64_t)nb};
+  cuuint64_t strides[4] = {(cuuint64_t)ld * 4, 32 * 4, (cuuint64_t)hs * 4, (cuuint64_t)bs * 4};
+  cuuint32_t box[5] = {32, box_rows, box_chunks, 1, 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<float*>(ptr), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: chunked tensor map encode failed (%d)",
+                     (int)r);
   return TG_OK;
 }
 
