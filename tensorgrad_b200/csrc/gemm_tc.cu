@@ -153,12 +153,25 @@ struct TileInfo {
 
 __device__ __forceinline__ TileInfo tile_info(const TcArgs& a, int t, int bn, int bm, int bk) {
   TileInfo ti;
-  const int mt = t % a.m_tiles;
-  int rest = t / a.m_tiles;
-  const int nt = rest % a.n_tiles;
-  rest /= a.n_tiles;
-  ti.bz = rest % a.batch;
-  ti.split = rest / a.batch;
+  int mt, nt;
+  if (a.kmode == GEMM_K_FROM_ROW || a.kmode == GEMM_K_UP_TO_ROW) {
+    // Triangular reductions (no splits): the row tile is the slowest index, heaviest first
+    // (the first row tile reduces over all of k from the row on, the last up to the row), so
+    // the round-robin's first rounds take the longest tiles and the last the shortest.
+    const int per_m = a.n_tiles * a.batch;
+    const int q = t / per_m, r = t - q * per_m;
+    mt = a.kmode == GEMM_K_FROM_ROW ? q : a.m_tiles - 1 - q;
+    nt = r % a.n_tiles;
+    ti.bz = r / a.n_tiles;
+    ti.split = 0;
+  } else {
+    mt = t % a.m_tiles;
+    int rest = t / a.m_tiles;
+    nt = rest % a.n_tiles;
+    rest /= a.n_tiles;
+    ti.bz = rest % a.batch;
+    ti.split = rest / a.batch;
+  }
   ti.m0 = (int64_t)mt * bm;
   ti.n0 = (int64_t)nt * bn;
   // Causal attention products: a tile strictly above the diagonal is skipped outright, and
