@@ -387,7 +387,7 @@ static int make_map_uncached(CUtensorMap* map, const float* ptr, int64_t inner, 
 static int make_map_chunked_uncached(CUtensorMap* map, const float* ptr, int64_t inner,
                                      int64_t rows, int64_t ld, int64_t heads, int64_t hstride,
                                      int64_t nb, int64_t bstride, uint32_t box_rows,
-                                     uint32_t box_chunks);
+                                     uint32_t box_chunks, CUtensorMapSwizzle swizzle);
 
 // chunks > 0: the MN-major 5-D map (inner split as 32 x inner / 32; inner % 32 == 0), boxes of
 // 32 x box_rows x chunks; otherwise the 4-D map with boxes of box_inner x box_rows.
@@ -410,7 +410,7 @@ static int make_map(CUtensorMap* map, const float* ptr, int64_t inner, int64_t r
     }
   }
   const int rc = chunks ? make_map_chunked_uncached(map, ptr, inner, rows, ld, heads, hstride,
-                                                     nb, bstride, box_rows, chunks)
+                                                     nb, bstride, box_rows, chunks, swizzle)
                       : make_map_uncached(map, ptr, inner, rows, ld, heads, hstride, nb,
                                           bstride, box_inner, box_rows, swizzle);
   if (rc == TG_OK) {
@@ -446,7 +446,7 @@ static int make_map_uncached(CUtensorMap* map, const float* ptr, int64_t inner, 
 static int make_map_chunked_uncached(CUtensorMap* map, const float* ptr, int64_t inner,
                                      int64_t rows, int64_t ld, int64_t heads, int64_t hstride,
                                      int64_t nb, int64_t bstride, uint32_t box_rows,
-                                     uint32_t box_chunks) {
+                                     uint32_t box_chunks, CUtensorMapSwizzle swizzle) {
   EncodeFn enc = get_encode();
   if (!enc) return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: cuTensorMapEncodeTiled unavailable");
   if (inner % 32) return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: chunked map needs inner % 32");
@@ -462,8 +462,8 @@ static int make_map_chunked_uncached(CUtensorMap* map, const float* ptr, int64_t
   cuuint32_t box[5] = {32, box_rows, box_chunks, 1, 1};
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<float*>(ptr), dims,
-                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(TG_ERR_UNSUPPORTED, "gemm_tc: chunked tensor map encode failed (%d)",
