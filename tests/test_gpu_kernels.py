@@ -43,7 +43,9 @@ def tensor(a, dtype, requires_grad=True):
 # (Reductions of at most 8 take the small-k kernel: test_gemm_small_k.)
 GEMM_SHAPES = [(1, 1, 9), (7, 5, 12), (128, 128, 32), (130, 257, 100), (300, 64, 768),
                (64, 300, 36), (1000, 333, 68), (8192 // 16, 3072 // 4, 768), (2100, 1000, 100),
-               (4096, 2000, 300)]
+               (4096, 2000, 300), (160, 96, 200)]
+# (160, 96, 200): MN extents that are multiples of 32 but not of the tile, so the chunked
+# 5-D maps of MN-major operands load boxes that reach past the last chunk (zero fill).
 
 
 @pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
@@ -69,6 +71,34 @@ def test_gemm_tensor_core_matches_float64(m, n, k, ta, tb):
     assert lib.tg_gemm_tc_status(1) == 0
     # 3xTF32 reaches near-fp32 accuracy (~1e-5 of max|C|): far inside the 1e-4 tolerance.
     assert_parity(out, ref, 2e-5, f"gemm {m}x{n}x{k} ta={ta} tb={tb}")
+
+
+@pytest.mark.parametrize("m,n,k,tb", [(4096, 1280, 2048, 1), (8192, 768, 3072, 1),
+                                      (8192, 768, 3072, 0)])
+def test_gemm_stream_k_tail_matches_float64(m, n, k, tb):
+    """Products whose tiles fill the SMs' last round only partly and whose reduction is long
+    (64 k-blocks or more per tile) run with the stream-K tail: tiles cut between CTAs sum
+    their partials in piece order. Bias included; run twice to check the arrival counters
+    are left at zero for the next launch."""
+    from tensorgrad_b200 import device
+    from tensorgrad_b200._lib import F32, check, lib
+
+    rng = np.random.default_rng(m + n + k)
+    a = rng.standard_normal((m, k))
+    b = rng.standard_normal((n, k) if tb else (k, n))
+    bias = rng.standard_normal(n)
+    ref = (a @ (b.T if tb else b)) + bias
+    da, db = device.from_numpy(a.astype(np.float32)), device.from_numpy(b.astype(np.float32))
+    dbias = device.from_numpy(bias.astype(np.float32))
+    for _ in range(2):
+        dc = device.empty((m, n), np.float32)
+        check(lib.tg_gemm(F32, 0, tb, m, n, k, 1.0, da.ptr, k, db.ptr, b.shape[1], 0.0, dc.ptr,
+                          n, dbias.ptr, device.stream()))
+        # 1e-4, the fp32 parity bar: with k = 2048-3072 the fp32 accumulator in tensor memory
+        # takes ~1000 additions of partial sums of a few hundred (2e-5 of max|C| measured
+        # 2.3e-5 at k = 3072, with or without the stream-K tail's two-piece sum).
+        assert_parity(dc.numpy(), ref, 1e-4, f"stream-K gemm {m}x{n}x{k} tb={tb}")
+    assert lib.tg_gemm_tc_status(1) == 0
 
 
 def test_gemm_cta_pairs_match_float64():
