@@ -74,6 +74,9 @@ struct TcArgs {
   // 1: the MN-major operand has the chunked 5-D map (one copy per k-block instead of one per
   // 32-wide chunk).
   int a_chunked, b_chunked;
+  // 1: column tiles vary fastest (few column tiles, many row tiles): the column tiles of a
+  // row band run side by side and share its A rows through the L2.
+  int n_fast;
   int sk_first, sk_tiles, sk_nk;
   int64_t sk_q, sk_r;
   float* sk_ws;
@@ -164,6 +167,13 @@ __device__ __forceinline__ TileInfo tile_info(const TcArgs& a, int t, int bn, in
     nt = r % a.n_tiles;
     ti.bz = r / a.n_tiles;
     ti.split = 0;
+  } else if (a.n_fast) {
+    nt = t % a.n_tiles;
+    int rest = t / a.n_tiles;
+    mt = rest % a.m_tiles;
+    rest /= a.m_tiles;
+    ti.bz = rest % a.batch;
+    ti.split = rest / a.batch;
   } else {
     mt = t % a.m_tiles;
     int rest = t / a.m_tiles;
@@ -956,6 +966,16 @@ static bool chunked_enabled() {
   return v == 1;
 }
 
+// Column-fastest tile order where it applies (default) or never (TG_GEMM_NFAST=0, probes).
+static bool nfast_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("TG_GEMM_NFAST");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 // Stream-K tail on (default) or off (TG_GEMM_STREAMK=0, for the probes that compare both).
 static bool streamk_enabled() {
   static int v = -1;
@@ -1117,6 +1137,11 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
   a.tma_c = 0;
   a.a_chunked = a_chunked;
   a.b_chunked = b_chunked;
+  // Row-fastest order makes the SMs' concurrent tiles share a column tile, so with few column
+  // tiles and many row tiles A (the larger operand) is read once per column tile: e.g. the
+  // GPT-2 head's weight gradient read its 1.65 GB operand three times from DRAM (5.2 GB).
+  a.n_fast = p.kmode == GEMM_K_FULL && a.n_tiles > 1 && a.n_tiles <= 4 &&
+             a.m_tiles >= 4 * a.n_tiles && nfast_enabled();
   {
     auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
     const bool strides_ok = p.ldc % 4 == 0 && (p.heads == 1 || p.stride_ch % 4 == 0) &&
