@@ -103,6 +103,11 @@ def run_gemm(args: argparse.Namespace) -> None:
                       "steps": args.steps, "warmup": args.warmup}), flush=True)
 
 
+# roofline.traffic: bytes read + written in DRAM per tensor-core GEMM launch, averaged over
+# the launches of one training step in an ncu capture (a capture cannot run inside the bench).
+GEMM_TRAFFIC_PER_LAUNCH = {"gpt2": 163.8e6}
+
+
 def peaks() -> dict:
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -813,7 +818,14 @@ def run_ours(args: argparse.Namespace, wl: Workload) -> None:
         "roofline": {
             "kernel": "tensor-core GEMM (gemm_tc_kernel, 3xTF32)",
             "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-            "frac": achieved / peak if peak else None, "traffic": None,
+            "frac": achieved / peak if peak else None,
+            # DRAM bytes per GEMM launch over one step, from an ncu capture of that step's
+            # GEMM launches (the 12-layer GPT-2 workload only).
+            "traffic": GEMM_TRAFFIC_PER_LAUNCH.get(wl.name) if not (args.layers or args.batch)
+            else None,
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum over the GEMM "
+                              "launches of one step, per launch" if wl.name in
+                              GEMM_TRAFFIC_PER_LAUNCH else None,
             "peak_source": f"{pk['source']} bf16_tflops_sustained (dense bf16 cuBLAS)",
             "launches": gl.value, "device_ms_per_step": gms.value / args.steps,
             "tf32_ceiling_frac": achieved / (peak / 2) if peak else None,
