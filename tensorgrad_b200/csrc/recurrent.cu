@@ -52,15 +52,17 @@ __global__ void pad_cols_kernel(const T* __restrict__ x, T* __restrict__ xp, int
 // out_t is (B, 2, H): hidden, then cell state.
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
-lstm_cell_fwd(T* __restrict__ z, const T* __restrict__ c_prev, int64_t c_ld,
-              T* __restrict__ out_t, T* __restrict__ tanh_c, int64_t B, int64_t H) {
+lstm_cell_fwd(T* __restrict__ z, const T* __restrict__ rec, const T* __restrict__ c_prev,
+              int64_t c_ld, T* __restrict__ out_t, T* __restrict__ tanh_c, int64_t B, int64_t H) {
   const int64_t total = B * H;
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
     const int64_t b = idx / H, j = idx - b * H;
     T* zr = z + b * 4 * H;
-    const T i = sigm(zr[j]), f = sigm(zr[H + j]);
-    const T g = dev_tanh<T>(zr[2 * H + j]), o = sigm(zr[3 * H + j]);
+    const T* rr = rec + b * 4 * H;
+    const T i = sigm(zr[j] + rr[j]), f = sigm(zr[H + j] + rr[H + j]);
+    const T g = dev_tanh<T>(zr[2 * H + j] + rr[2 * H + j]);
+    const T o = sigm(zr[3 * H + j] + rr[3 * H + j]);
     zr[j] = i;
     zr[H + j] = f;
     zr[2 * H + j] = g;
@@ -264,11 +266,18 @@ using namespace tg;
 
 extern "C" {
 
+// Scratch of the LSTM forward: the summed biases (4H), the step's recurrent product
+// h W_hh^T (B x 4H, written with beta = 0 so the GEMM stores whole tiles through TMA; the
+// cell kernel adds the input projection), then the GEMM's split workspace.
+static size_t lstm_fwd_head(size_t es, int64_t B, int64_t H) {
+  return align256((size_t)(4 * H) * es) + align256((size_t)(B * 4 * H) * es);
+}
+
 size_t tg_lstm_forward_scratch_bytes(int dtype, int64_t T_, int64_t B, int64_t I, int64_t H) {
-  (void)T_; (void)B; (void)I;
+  (void)T_; (void)I;
   const size_t es = dtype == TG_F64 ? 8 : 4;
-  const size_t head = align256((size_t)(4 * H) * es);
-  return head + fwd_ws_bytes(dtype);
+  const size_t head = lstm_fwd_head(es, B, H);
+  return head + fwd_ws_bytes(dtype);  // head is a multiple of 256 bytes
 }
 
 int tg_lstm_forward(int dtype, int64_t T_, int64_t B, int64_t I, int64_t H, const void* x,
@@ -301,16 +310,17 @@ int tg_lstm_forward(int dtype, int64_t T_, int64_t B, int64_t I, int64_t H, cons
       const T* c_prev = t == 0 ? (const T*)c0 : o + (t - 1) * B * 2 * H + H;
       const int64_t c_ld = t == 0 ? H : 2 * H;
       T* zt = z + t * B * G;
-      auto rec = gemm_args<T>(0, 1, B, G, H, h_prev, h_ld, (const T*)w_hh, H, zt, G, nullptr,
-                              T(1));
+      T* rb = reinterpret_cast<T*>((uint8_t*)scratch + align256((size_t)G * sizeof(T)));
+      auto rec = gemm_args<T>(0, 1, B, G, H, h_prev, h_ld, (const T*)w_hh, H, rb, G, nullptr,
+                              T(0));
       if (fwd_ws_bytes(dtype)) {
         rec.workspace = reinterpret_cast<float*>(
-            (uint8_t*)scratch + fwd_ws_offset(dtype, align256((size_t)G * sizeof(T))));
+            (uint8_t*)scratch + fwd_ws_offset(dtype, lstm_fwd_head(sizeof(T), B, H)));
         rec.workspace_bytes = fwd_ws_bytes(dtype);
       }
       if ((r = gemm_run<T>(rec, st))) return r;
       lstm_cell_fwd<T><<<grid_for(B * H, kThreads), kThreads, 0, st>>>(
-          zt, c_prev, c_ld, o + t * B * 2 * H, (T*)tanh_c + t * B * H, B, H);
+          zt, rb, c_prev, c_ld, o + t * B * 2 * H, (T*)tanh_c + t * B * H, B, H);
       if ((r = check_launch("lstm(cell)"))) return r;
     }
     return (int)TG_OK;
