@@ -1140,7 +1140,9 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
   // Row-fastest order makes the SMs' concurrent tiles share a column tile, so with few column
   // tiles and many row tiles A (the larger operand) is read once per column tile: e.g. the
   // GPT-2 head's weight gradient read its 1.65 GB operand three times from DRAM (5.2 GB).
-  a.n_fast = p.kmode == GEMM_K_FULL && a.n_tiles > 1 && a.n_tiles <= 4 &&
+  // Unbatched products only: batched ones (the convolution's per-image input gradients)
+  // measured 8 % slower over the CNN step in column-fastest order.
+  a.n_fast = p.kmode == GEMM_K_FULL && a.batch == 1 && a.n_tiles > 1 && a.n_tiles <= 4 &&
              a.m_tiles >= 4 * a.n_tiles && nfast_enabled();
   {
     auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
