@@ -7,6 +7,7 @@
 #include <stdio.h>
 
 #include <cmath>
+#include <utility>
 
 #include "../../include/tgb200.h"
 
@@ -16,6 +17,35 @@ namespace tg {
 int set_error(int status, const char* fmt, ...);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Programmatic dependent launch, for chains of short kernels (the recurrent steps): a kernel
+// launched with launch_pdl may be scheduled before the kernel ahead of it on the stream has
+// finished. Such a kernel calls pdl_trigger() (lets its own successor be scheduled) and then
+// pdl_wait() before it touches any global memory: the wait returns once the kernel ahead has
+// completed and its writes are visible. A kernel without the attribute waits as usual.
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// TG_PDL=0 launches such kernels plainly (for comparison probes); read once per process.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Returns TG_OK, or TG_ERR_CUDA with the launch error recorded under `what`. `kernels` is
 // how many kernels the calling entry point just launched (added to tg_launch_count()).

@@ -348,6 +348,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   if (PAIR) cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrive
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Single-CTA launches use programmatic dependent launch: the prologue above (barriers,
+  // tensor memory) may overlap the kernel ahead on the stream; nothing in global memory is
+  // touched before this wait.
+  pdl_trigger();
+  pdl_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1208,7 +1213,7 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
     TG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, ta, tb, tcm, txm, a));
   } else {
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
-    kernel<<<grid, kThreads, smem, stream>>>(ta, tb, tcm, txm, a);
+    launch_pdl(kernel, dim3(grid), dim3(kThreads), smem, stream, ta, tb, tcm, txm, a);
   }
   if (a.splits > 1) {
     const int64_t mn = p.m * p.n;

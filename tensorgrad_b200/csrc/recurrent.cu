@@ -55,6 +55,8 @@ __global__ void __launch_bounds__(kThreads)
 lstm_cell_fwd(T* __restrict__ z, const T* __restrict__ rec, const T* __restrict__ c_prev,
               int64_t c_ld, T* __restrict__ out_t, T* __restrict__ tanh_c, int64_t B, int64_t H) {
   const int64_t total = B * H;
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
     const int64_t b = idx / H, j = idx - b * H;
@@ -85,6 +87,8 @@ lstm_cell_bwd(const T* __restrict__ gates, const T* __restrict__ tanh_c,
               const T* __restrict__ dh_carry, T* __restrict__ dc_carry, T* __restrict__ dz,
               int64_t B, int64_t H, int first) {
   const int64_t total = B * H;
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
     const int64_t b = idx / H, j = idx - b * H;
@@ -114,6 +118,8 @@ __global__ void __launch_bounds__(kThreads)
 gru_cell_fwd(T* __restrict__ a, const T* __restrict__ hw, const T* __restrict__ h_prev,
              T* __restrict__ hn_t, T* __restrict__ out_t, int64_t B, int64_t H) {
   const int64_t total = B * H;
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
     const int64_t b = idx / H, j = idx - b * H;
@@ -139,6 +145,8 @@ gru_cell_bwd(const T* __restrict__ gates, const T* __restrict__ hn_t,
              const T* __restrict__ h_prev, const T* __restrict__ g_t, T* __restrict__ dh_buf,
              T* __restrict__ dz_ih, T* __restrict__ dz_hh, int64_t B, int64_t H, int first) {
   const int64_t total = B * H;
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
     const int64_t b = idx / H, j = idx - b * H;
@@ -319,8 +327,8 @@ int tg_lstm_forward(int dtype, int64_t T_, int64_t B, int64_t I, int64_t H, cons
         rec.workspace_bytes = fwd_ws_bytes(dtype);
       }
       if ((r = gemm_run<T>(rec, st))) return r;
-      lstm_cell_fwd<T><<<grid_for(B * H, kThreads), kThreads, 0, st>>>(
-          zt, rb, c_prev, c_ld, o + t * B * 2 * H, (T*)tanh_c + t * B * H, B, H);
+      launch_pdl(lstm_cell_fwd<T>, dim3(grid_for(B * H, kThreads)), dim3(kThreads), 0, st, zt,
+                 rb, c_prev, c_ld, o + t * B * 2 * H, (T*)tanh_c + t * B * H, B, H);
       if ((r = check_launch("lstm(cell)"))) return r;
     }
     return (int)TG_OK;
@@ -354,7 +362,7 @@ int tg_lstm_backward(int dtype, int64_t T_, int64_t B, int64_t I, int64_t H, con
       const T* c_prev = t == 0 ? (const T*)c0 : o + (t - 1) * B * 2 * H + H;
       const int64_t c_ld = t == 0 ? H : 2 * H;
       T* dzt = dz + t * B * G;
-      lstm_cell_bwd<T><<<grid_for(B * H, kThreads), kThreads, 0, st>>>(
+      launch_pdl(lstm_cell_bwd<T>, dim3(grid_for(B * H, kThreads)), dim3(kThreads), 0, st,
           (const T*)acts + t * B * G, (const T*)tanh_c + t * B * H, c_prev, c_ld,
           (const T*)g + t * B * 2 * H, dh, dc, dzt, B, H, t == T_ - 1);
       if ((r = check_launch("lstm backward(cell)"))) return r;
@@ -408,7 +416,7 @@ int tg_gru_forward(int dtype, int64_t T_, int64_t B, int64_t I, int64_t H, const
         rec.workspace_bytes = fwd_ws_bytes(dtype);
       }
       if ((r = gemm_run<T>(rec, st))) return r;
-      gru_cell_fwd<T><<<grid_for(B * H, kThreads), kThreads, 0, st>>>(
+      launch_pdl(gru_cell_fwd<T>, dim3(grid_for(B * H, kThreads)), dim3(kThreads), 0, st,
           a + t * B * G, hw, h_prev, (T*)hn + t * B * H, o + t * B * H, B, H);
       if ((r = check_launch("gru(cell)"))) return r;
     }
@@ -441,7 +449,7 @@ int tg_gru_backward(int dtype, int64_t T_, int64_t B, int64_t I, int64_t H, cons
     int r;
     for (int64_t t = T_ - 1; t >= 0; --t) {
       const T* h_prev = t == 0 ? (const T*)h0 : o + (t - 1) * B * H;
-      gru_cell_bwd<T><<<grid_for(B * H, kThreads), kThreads, 0, st>>>(
+      launch_pdl(gru_cell_bwd<T>, dim3(grid_for(B * H, kThreads)), dim3(kThreads), 0, st,
           (const T*)acts + t * B * G, (const T*)hn + t * B * H, h_prev, (const T*)g + t * B * H,
           dh, dz_ih + t * B * G, dz_hh + t * B * G, B, H, t == T_ - 1);
       if ((r = check_launch("gru backward(cell)"))) return r;
