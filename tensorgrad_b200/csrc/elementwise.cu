@@ -40,6 +40,8 @@ __global__ void binary_contig_kernel(const T* __restrict__ a, const T* __restric
 template <typename T>
 __global__ void binary_add_vec4_kernel(const float4* __restrict__ a, const float4* __restrict__ b,
                                        float4* __restrict__ out, int64_t n4) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
        i += (int64_t)gridDim.x * blockDim.x) {
     float4 x = a[i], y = b[i];
@@ -150,6 +152,8 @@ __global__ void gelu_fwd_kernel(int64_t n, const T* __restrict__ x, T* __restric
 
 __global__ void gelu_fwd_vec4_kernel(int64_t n4, const float4* __restrict__ x,
                                      float4* __restrict__ y) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
        i += (int64_t)gridDim.x * blockDim.x) {
     float4 v = x[i];
@@ -180,6 +184,8 @@ __global__ void gelu_bwd_kernel(int64_t n, const T* __restrict__ g, const T* __r
 
 __global__ void gelu_bwd_vec4_kernel(int64_t n4, const float4* __restrict__ g,
                                      const float4* __restrict__ x, float4* __restrict__ gx) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
        i += (int64_t)gridDim.x * blockDim.x) {
     const float4 v = x[i], w = g[i];
@@ -236,7 +242,7 @@ int tg_binary(int dtype, int op, int ndim, const int64_t* shape, const void* a,
     const unsigned grid = grid_for(n, 256);
     if (simple && am == n && bm == n && op == TG_ADD && sizeof(T) == 4 && n % 4 == 0 &&
         aligned16(a) && aligned16(b) && aligned16(out)) {
-      binary_add_vec4_kernel<T><<<grid_for(n / 4, 256), 256, 0, s>>>(
+      launch_pdl(binary_add_vec4_kernel<T>, dim3(grid_for(n / 4, 256)), dim3(256), 0, s,
           (const float4*)a, (const float4*)b, (float4*)out, n / 4);
     } else if (simple) {
       switch (op) {
@@ -304,7 +310,8 @@ int tg_gelu_forward(int dtype, int64_t n, const void* x, void* y, void* stream) 
   if (n <= 0) return TG_OK;
   cudaStream_t s = as_stream(stream);
   if (dtype == TG_F32 && n % 4 == 0 && aligned16(x) && aligned16(y)) {
-    gelu_fwd_vec4_kernel<<<grid_for(n / 4, 256), 256, 0, s>>>(n / 4, (const float4*)x,
+    launch_pdl(gelu_fwd_vec4_kernel, dim3(grid_for(n / 4, 256)), dim3(256), 0, s,
+               n / 4, (const float4*)x,
                                                                (float4*)y);
     return check_launch("gelu_forward");
   }
@@ -318,7 +325,8 @@ int tg_gelu_backward(int dtype, int64_t n, const void* g, const void* x, void* g
   if (n <= 0) return TG_OK;
   cudaStream_t s = as_stream(stream);
   if (dtype == TG_F32 && n % 4 == 0 && aligned16(x) && aligned16(g) && aligned16(gx)) {
-    gelu_bwd_vec4_kernel<<<grid_for(n / 4, 256), 256, 0, s>>>(n / 4, (const float4*)g,
+    launch_pdl(gelu_bwd_vec4_kernel, dim3(grid_for(n / 4, 256)), dim3(256), 0, s,
+               n / 4, (const float4*)g,
                                                                (const float4*)x, (float4*)gx);
     return check_launch("gelu_backward");
   }

@@ -928,6 +928,8 @@ splitk_reduce_kernel(const float* __restrict__ ws, int splits, GemmArgs<float> p
 // splits' loads of one vector issued together.
 __global__ void __launch_bounds__(256)
 splitk_reduce_vec4(const float4* __restrict__ ws, int splits, GemmArgs<float> p) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   const int64_t mn4 = p.m * p.n / 4, n4 = p.n / 4;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < mn4;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -1224,7 +1226,8 @@ static int launch(const GemmArgs<float>& p, int splits, cudaStream_t stream) {
     const int blocks = (int)((work + 255) / 256 < 8 * sm_count() ? (work + 255) / 256
                                                                     : 8 * sm_count());
     if (v4)
-      splitk_reduce_vec4<<<blocks, 256, 0, stream>>>(reinterpret_cast<const float4*>(p.workspace),
+      launch_pdl(splitk_reduce_vec4, dim3(blocks), dim3(256), 0, stream,
+                 reinterpret_cast<const float4*>(p.workspace),
                                                      a.splits, p);
     else
       splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(p.workspace, a.splits, p);

@@ -148,6 +148,8 @@ __global__ void __launch_bounds__(kWarps * 32)
 ln_fwd_vec4(const float* __restrict__ x, const float* __restrict__ w,
             const float* __restrict__ b, float* __restrict__ y, float* __restrict__ mean_out,
             float* __restrict__ rstd_out, int64_t rows, int cols, float eps) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t r = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
   if (r >= rows) return;
@@ -207,6 +209,8 @@ ln_bwd_vec4(const float* __restrict__ g, const float* __restrict__ x,
             const float* __restrict__ w, const float* __restrict__ mean_in,
             const float* __restrict__ rstd_in, float* __restrict__ gx,
             float* __restrict__ part_w, float* __restrict__ part_b, int64_t rows, int cols) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   extern __shared__ unsigned char smem_raw[];
   float* sh = reinterpret_cast<float*>(smem_raw);  // [kWarps][2][cols]
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -308,6 +312,8 @@ ln_final_kernel(const T* __restrict__ part_w, const T* __restrict__ part_b, T* _
 __global__ void __launch_bounds__(256)
 ln_final_vec4(const float4* __restrict__ part_w, const float4* __restrict__ part_b,
               float* __restrict__ gw, float* __restrict__ gb, int nparts, int cols) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   __shared__ float4 sw_sh[32][8], sb_sh[32][8];
   const int q = threadIdx.x & 7, grp = threadIdx.x >> 3;
   const int nq = cols >> 2, cq = blockIdx.x * 8 + q;
@@ -374,7 +380,8 @@ template <int NV>
 int ln_forward_vec(const float* x, const float* w, const float* b, float* y, float* mean,
                    float* rstd, int64_t rows, int cols, float eps, cudaStream_t s) {
   const unsigned grid = (unsigned)((rows + kWarps - 1) / kWarps);
-  ln_fwd_vec4<NV><<<grid, kWarps * 32, 0, s>>>(x, w, b, y, mean, rstd, rows, cols, eps);
+  launch_pdl(ln_fwd_vec4<NV>, dim3(grid), dim3(kWarps * 32), 0, s,
+             x, w, b, y, mean, rstd, rows, cols, eps);
   return check_launch("layer_norm_forward");
 }
 
@@ -420,10 +427,12 @@ int ln_backward_vec(const float* g, const float* x, const float* w, const float*
   const size_t smem = (gw || gb) ? (size_t)kWarps * 2 * cols * sizeof(float) : 0;
   int rc = set_smem(ln_bwd_vec4<NV>, smem);
   if (rc) return rc;
-  ln_bwd_vec4<NV><<<nb, kWarps * 32, smem, s>>>(g, x, w, mean, rstd, gx, part_w, part_b, rows,
+  launch_pdl(ln_bwd_vec4<NV>, dim3(nb), dim3(kWarps * 32), smem, s,
+             g, x, w, mean, rstd, gx, part_w, part_b, rows,
                                                 cols);
   if ((gw || gb) && aligned16(gw) && aligned16(gb) && aligned16(part_w))
-    ln_final_vec4<<<(cols + 31) / 32, 256, 0, s>>>(reinterpret_cast<const float4*>(part_w),
+    launch_pdl(ln_final_vec4, dim3((cols + 31) / 32), dim3(256), 0, s,
+               reinterpret_cast<const float4*>(part_w),
                                                    reinterpret_cast<const float4*>(part_b), gw,
                                                    gb, nb, cols);
   else if (gw || gb)

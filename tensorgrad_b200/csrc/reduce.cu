@@ -16,6 +16,8 @@ constexpr int kVecCols = 4 * kColTile;
 __global__ void __launch_bounds__(kColTile * kRowLanes)
 colsum_partial_vec4(const float* __restrict__ x, float* __restrict__ partial, int64_t rows,
                     int64_t cols, int64_t rows_per_chunk) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   __shared__ float4 sh[kRowLanes][kColTile];
   const int64_t c4 = (int64_t)blockIdx.x * kColTile + threadIdx.x;  // float4 column index
   const int64_t n4 = cols >> 2;
@@ -82,6 +84,8 @@ template <typename T>
 __global__ void __launch_bounds__(256)
 colsum_final_kernel(const T* __restrict__ partial, T* __restrict__ out, int64_t cols,
                     int64_t chunks, int accumulate) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   __shared__ T sh[8][33];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   for (int64_t c0 = (int64_t)blockIdx.x * 32; c0 < cols; c0 += (int64_t)gridDim.x * 32) {
@@ -175,7 +179,7 @@ int colsum(const T* x, T* out, int64_t rows, int64_t cols, int accumulate, void*
   if (sizeof(T) == 4 && cols % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
       (reinterpret_cast<uintptr_t>(scratch) & 15) == 0) {
     dim3 grid((unsigned)((cols + kVecCols - 1) / kVecCols), (unsigned)chunks);
-    colsum_partial_vec4<<<grid, dim3(kColTile, kRowLanes), 0, stream>>>(
+    launch_pdl(colsum_partial_vec4, dim3(grid), dim3(kColTile, kRowLanes), 0, stream,
         reinterpret_cast<const float*>(x), reinterpret_cast<float*>(partial), rows, cols, rpc);
   } else {
     dim3 grid((unsigned)((cols + kColTile - 1) / kColTile), (unsigned)chunks);
@@ -183,8 +187,8 @@ int colsum(const T* x, T* out, int64_t rows, int64_t cols, int accumulate, void*
                                                                             cols, rpc);
   }
   const int64_t col_tiles = (cols + 31) / 32;
-  colsum_final_kernel<T><<<(unsigned)(col_tiles < 4096 ? col_tiles : 4096), 256, 0, stream>>>(
-      partial, out, cols, chunks, accumulate);
+  launch_pdl(colsum_final_kernel<T>, dim3((unsigned)(col_tiles < 4096 ? col_tiles : 4096)),
+             dim3(256), 0, stream, partial, out, cols, chunks, accumulate);
   return check_launch("colsum", 2);
 }
 template int colsum<float>(const float*, float*, int64_t, int64_t, int, void*, cudaStream_t);
