@@ -150,6 +150,8 @@ __global__ void row_dot_kernel(View a, View b, float* __restrict__ out, int64_t 
 template <int G>
 __global__ void __launch_bounds__(256)
 row_dot_vec4_kernel(View a, View b, float* __restrict__ out, int64_t H, int64_t T, int64_t rows) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   constexpr int kRowsPerWarp = 32 / G;
   const int lane = threadIdx.x & 31, sub = lane / G, c = lane % G;
   const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -182,10 +184,14 @@ int row_dot(View dO, View O, float* delta, const Plan& p, cudaStream_t st) {
   const int64_t per_warp = 32 / (g >= 32 ? 32 : (g >= 16 ? 16 : (g >= 8 ? 8 : (g >= 4 ? 4 : (g >= 2 ? 2 : 1)))));
   const unsigned grid = (unsigned)grid_for((rows + per_warp - 1) / per_warp * 32, 256);
   switch (g) {
-    case 32: row_dot_vec4_kernel<32><<<grid, 256, 0, st>>>(dO, O, delta, p.H, p.Tq, rows); break;
-    case 16: row_dot_vec4_kernel<16><<<grid, 256, 0, st>>>(dO, O, delta, p.H, p.Tq, rows); break;
-    case 8: row_dot_vec4_kernel<8><<<grid, 256, 0, st>>>(dO, O, delta, p.H, p.Tq, rows); break;
-    case 4: row_dot_vec4_kernel<4><<<grid, 256, 0, st>>>(dO, O, delta, p.H, p.Tq, rows); break;
+    case 32: launch_pdl(row_dot_vec4_kernel<32>, dim3(grid), dim3(256), 0, st, dO, O, delta, p.H,
+                         p.Tq, rows); break;
+    case 16: launch_pdl(row_dot_vec4_kernel<16>, dim3(grid), dim3(256), 0, st, dO, O, delta, p.H,
+                         p.Tq, rows); break;
+    case 8: launch_pdl(row_dot_vec4_kernel<8>, dim3(grid), dim3(256), 0, st, dO, O, delta, p.H,
+                         p.Tq, rows); break;
+    case 4: launch_pdl(row_dot_vec4_kernel<4>, dim3(grid), dim3(256), 0, st, dO, O, delta, p.H,
+                         p.Tq, rows); break;
     case 2: row_dot_vec4_kernel<2><<<grid, 256, 0, st>>>(dO, O, delta, p.H, p.Tq, rows); break;
     case 1: row_dot_vec4_kernel<1><<<grid, 256, 0, st>>>(dO, O, delta, p.H, p.Tq, rows); break;
     default:

@@ -151,6 +151,8 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_trigger();  // launched with launch_pdl: the prologue above touches no global memory
+  pdl_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -483,7 +485,7 @@ int launch_flash(const tg_attn_shape* s, const float* q, const float* k, const f
   a.q_blocks = (int)((s->tq + FQ - 1) / FQ);
   a.items = (int)(a.BH * a.q_blocks);
   const int grid = a.items < sm_count() ? a.items : sm_count();
-  flash_fwd_kernel<D><<<grid, kFThreads, L::SMEM, st>>>(mq, mk, mv, a);
+  launch_pdl(flash_fwd_kernel<D>, dim3(grid), dim3(kFThreads), L::SMEM, st, mq, mk, mv, a);
   return check_launch("attention forward (fused)");
 }
 
@@ -589,6 +591,8 @@ attn_pds_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_trigger();  // launched with launch_pdl: the prologue above touches no global memory
+  pdl_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -844,7 +848,8 @@ int launch_pds(const tg_attn_shape* s, const float* q, const float* k, const flo
   a.q_blocks = (int)((s->tq + FQ - 1) / FQ);
   a.items = (int)(a.BH * a.q_blocks);
   const int grid = a.items < sm_count() ? a.items : sm_count();
-  attn_pds_kernel<D><<<grid, kFThreads, L::SMEM, st>>>(mq, mo, mk, mv, mp, md, a);
+  launch_pdl(attn_pds_kernel<D>, dim3(grid), dim3(kFThreads), L::SMEM, st, mq, mo, mk, mv, mp,
+             md, a);
   return check_launch("attention backward (P, dS)");
 }
 
