@@ -110,6 +110,8 @@ im2col_kernel(const T* __restrict__ x, T* __restrict__ cols, tg_conv_shape s, in
 template <typename T, int MAXW>
 __global__ void __launch_bounds__(kThreads)
 col2im_kernel(const T* __restrict__ dcols, T* __restrict__ gx, tg_conv_shape s, int64_t ldm) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   const int hw = (int)(s.h * s.w);
   const int q = blockIdx.x * blockDim.x + threadIdx.x;
   if (q >= hw) return;
@@ -155,6 +157,8 @@ col2im_kernel(const T* __restrict__ dcols, T* __restrict__ gx, tg_conv_shape s, 
 __global__ void __launch_bounds__(kThreads)
 im2col4_kernel(const float* __restrict__ x, float* __restrict__ cols, tg_conv_shape s,
                int64_t K, int64_t kp, int64_t ldm) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   const int ohw = (int)(s.oh * s.ow);
   const int p = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
   if (p >= ohw) return;
@@ -293,6 +297,8 @@ template <typename T, int MODE, int V>
 __global__ void __launch_bounds__(kThreads)
 channel_sums_kernel(const T* __restrict__ a, const T* __restrict__ x, const T* __restrict__ mean,
                     int64_t n, int64_t C, int64_t hw, int chunks, double* __restrict__ partial) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   __shared__ double sh[32];
   const int64_t ch = blockIdx.y;
   const int chunk = blockIdx.x;
@@ -347,6 +353,8 @@ __global__ void bn_stats_final_kernel(const double* __restrict__ partial, int ch
                                       T* __restrict__ mean, T* __restrict__ rstd,
                                       T* __restrict__ running_mean, T* __restrict__ running_var,
                                       double momentum, double eps) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   const int64_t ch = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (ch >= C) return;
   double s0 = 0.0, s1 = 0.0;
@@ -374,6 +382,8 @@ __global__ void __launch_bounds__(kThreads)
 bn_apply_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ b,
                 const T* __restrict__ mean, const T* __restrict__ rstd, T* __restrict__ y,
                 int64_t planes, int64_t C, int64_t hw) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   const int64_t nv = hw / V;
   for (int64_t plane = blockIdx.y; plane < planes; plane += gridDim.y) {
     const int64_t ch = plane % C;
@@ -402,6 +412,8 @@ __global__ void bn_grad_final_kernel(const double* __restrict__ partial, int chu
                                      double m, const T* __restrict__ w,
                                      const T* __restrict__ rstd, T* __restrict__ gw,
                                      T* __restrict__ gb, T* __restrict__ coef) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   const int64_t ch = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (ch >= C) return;
   double sg = 0.0, sgx = 0.0;
@@ -426,6 +438,8 @@ bn_grad_input_kernel(const T* __restrict__ g, const T* __restrict__ x,
                      const T* __restrict__ mean, const T* __restrict__ rstd,
                      const T* __restrict__ coef, T* __restrict__ gx, int64_t planes, int64_t C,
                      int64_t hw) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   const int64_t nv = hw / V;
   for (int64_t plane = blockIdx.y; plane < planes; plane += gridDim.y) {
     const int64_t ch = plane % C;
@@ -575,6 +589,8 @@ __device__ __forceinline__ void pool4_first_max(float v0, float v1, float v2, fl
 __global__ void __launch_bounds__(kThreads)
 maxpool2x2_fwd_kernel(const float* __restrict__ x, float* __restrict__ y,
                       uint8_t* __restrict__ arg, int64_t planes, int h, int w) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   const int oh = h / 2, ow = w / 2, quads = w / 4;
   const int64_t per_plane = (int64_t)oh * quads, total = planes * per_plane;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
@@ -600,6 +616,8 @@ maxpool2x2_fwd_kernel(const float* __restrict__ x, float* __restrict__ y,
 __global__ void __launch_bounds__(kThreads)
 maxpool2x2_bwd_kernel(const float* __restrict__ g, const uint8_t* __restrict__ arg,
                       float* __restrict__ gx, int64_t planes, int h, int w) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   const int oh = h / 2, ow = w / 2, quads = w / 4;
   const int64_t per_plane = (int64_t)oh * quads, total = planes * per_plane;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
@@ -653,11 +671,11 @@ void launch_channel_sums(const T* a, const T* x, const T* mean, int64_t n, int64
                          int64_t hw, int chunks, double* partial, cudaStream_t st) {
   const dim3 grid(chunks, (unsigned)C);
   if (plane_vec4<T>(hw, {a, x}))
-    channel_sums_kernel<T, MODE, 4><<<grid, kThreads, 0, st>>>(a, x, mean, n, C, hw, chunks,
-                                                               partial);
+    launch_pdl(channel_sums_kernel<T, MODE, 4>, dim3(grid), dim3(kThreads), 0, st,
+               a, x, mean, n, C, hw, chunks, partial);
   else
-    channel_sums_kernel<T, MODE, 1><<<grid, kThreads, 0, st>>>(a, x, mean, n, C, hw, chunks,
-                                                               partial);
+    launch_pdl(channel_sums_kernel<T, MODE, 1>, dim3(grid), dim3(kThreads), 0, st,
+               a, x, mean, n, C, hw, chunks, partial);
 }
 
 // ------------------------------------------------------------------ scratch layout
@@ -711,7 +729,8 @@ int tg_conv2d_forward(int dtype, const tg_conv_shape* s, const void* x, const vo
   return TG_DISPATCH_FLOAT(dtype, T, [&] {
     if (conv_vec4<T>(*s, {cols}) && ldm % 4 == 0) {
       const dim3 grid = position_grid(ohw / 4, kp, s->n);
-      im2col4_kernel<<<grid, kThreads, 0, st>>>((const float*)x, (float*)cols, *s, K, kp, ldm);
+      launch_pdl(im2col4_kernel, dim3(grid), dim3(kThreads), 0, st,
+                 (const float*)x, (float*)cols, *s, K, kp, ldm);
     } else {
       const dim3 grid = position_grid(ohw, kp, s->n);
       im2col_kernel<T><<<grid, kThreads, 0, st>>>((const T*)x, (T*)cols, *s, K, kp, ldm);
@@ -822,11 +841,14 @@ int tg_conv2d_backward(int dtype, const tg_conv_shape* s, const void* g, const v
       const dim3 grid = position_grid(s->h * s->w, s->c, s->n);
       const int64_t win = std::max(s->kh, s->kw);
       if (win <= 3)
-        col2im_kernel<T, 3><<<grid, kThreads, 0, st>>>(dcols, (T*)gx, *s, ldm);
+        launch_pdl(col2im_kernel<T, 3>, dim3(grid), dim3(kThreads), 0, st,
+                   dcols, (T*)gx, *s, ldm);
       else if (win <= 7)
-        col2im_kernel<T, 7><<<grid, kThreads, 0, st>>>(dcols, (T*)gx, *s, ldm);
+        launch_pdl(col2im_kernel<T, 7>, dim3(grid), dim3(kThreads), 0, st,
+                   dcols, (T*)gx, *s, ldm);
       else if (win <= 16)
-        col2im_kernel<T, 16><<<grid, kThreads, 0, st>>>(dcols, (T*)gx, *s, ldm);
+        launch_pdl(col2im_kernel<T, 16>, dim3(grid), dim3(kThreads), 0, st,
+                   dcols, (T*)gx, *s, ldm);
       else
         col2im_large_kernel<T><<<grid, kThreads, 0, st>>>(dcols, (T*)gx, *s, ldm);
       r = check_launch("conv2d backward(col2im)");
@@ -854,17 +876,17 @@ int tg_batch_norm_forward(int dtype, int64_t n, int64_t c, int64_t hw, const voi
   return TG_DISPATCH_FLOAT(dtype, T, [&] {
     launch_channel_sums<T, MODE_STATS>((const T*)x, nullptr, nullptr, n, c, hw, chunks, partial,
                                        st);
-    bn_stats_final_kernel<T><<<(unsigned)((c + 127) / 128), 128, 0, st>>>(
-        partial, chunks, (const T*)x, c, hw, (double)(n * hw), (T*)mean, (T*)rstd,
-        (T*)running_mean, (T*)running_var, momentum, eps);
+    launch_pdl(bn_stats_final_kernel<T>, dim3((unsigned)((c + 127) / 128)), dim3(128), 0, st,
+               partial, chunks, (const T*)x, c, hw, (double)(n * hw), (T*)mean, (T*)rstd,
+               (T*)running_mean, (T*)running_var, momentum, eps);
     if (plane_vec4<T>(hw, {x, y}))
-      bn_apply_kernel<T, 4><<<plane_grid(hw / 4, n * c), kThreads, 0, st>>>(
-          (const T*)x, (const T*)w, (const T*)b, (const T*)mean, (const T*)rstd, (T*)y, n * c,
-          c, hw);
+      launch_pdl(bn_apply_kernel<T, 4>, dim3(plane_grid(hw / 4, n * c)), dim3(kThreads), 0, st,
+                 (const T*)x, (const T*)w, (const T*)b, (const T*)mean, (const T*)rstd, (T*)y,
+                 n * c, c, hw);
     else
-      bn_apply_kernel<T, 1><<<plane_grid(hw, n * c), kThreads, 0, st>>>(
-          (const T*)x, (const T*)w, (const T*)b, (const T*)mean, (const T*)rstd, (T*)y, n * c,
-          c, hw);
+      launch_pdl(bn_apply_kernel<T, 1>, dim3(plane_grid(hw, n * c)), dim3(kThreads), 0, st,
+                 (const T*)x, (const T*)w, (const T*)b, (const T*)mean, (const T*)rstd, (T*)y,
+                 n * c, c, hw);
     return check_launch("batch_norm", 3);
   });
 }
@@ -882,17 +904,20 @@ int tg_batch_norm_backward(int dtype, int64_t n, int64_t c, int64_t hw, const vo
     T* coef = reinterpret_cast<T*>((uint8_t*)scratch + coef_off);
     launch_channel_sums<T, MODE_GRAD>((const T*)g, (const T*)x, (const T*)mean, n, c, hw,
                                       chunks, partial, st);
-    bn_grad_final_kernel<T><<<(unsigned)((c + 127) / 128), 128, 0, st>>>(
-        partial, chunks, c, (double)(n * hw), (const T*)w, (const T*)rstd, (T*)gw, (T*)gb,
-        gx ? coef : nullptr);
+    launch_pdl(bn_grad_final_kernel<T>, dim3((unsigned)((c + 127) / 128)), dim3(128), 0, st,
+               partial, chunks, c, (double)(n * hw), (const T*)w, (const T*)rstd, (T*)gw, (T*)gb,
+               gx ? coef : nullptr);
     int launched = 2;
     if (gx) {
       if (plane_vec4<T>(hw, {g, x, gx}))
-        bn_grad_input_kernel<T, 4><<<plane_grid(hw / 4, n * c), kThreads, 0, st>>>(
-            (const T*)g, (const T*)x, (const T*)mean, (const T*)rstd, coef, (T*)gx, n * c, c, hw);
+        launch_pdl(bn_grad_input_kernel<T, 4>, dim3(plane_grid(hw / 4, n * c)), dim3(kThreads), 0,
+                   st,
+                   (const T*)g, (const T*)x, (const T*)mean, (const T*)rstd, coef, (T*)gx, n * c,
+                   c, hw);
       else
-        bn_grad_input_kernel<T, 1><<<plane_grid(hw, n * c), kThreads, 0, st>>>(
-            (const T*)g, (const T*)x, (const T*)mean, (const T*)rstd, coef, (T*)gx, n * c, c, hw);
+        launch_pdl(bn_grad_input_kernel<T, 1>, dim3(plane_grid(hw, n * c)), dim3(kThreads), 0, st,
+                   (const T*)g, (const T*)x, (const T*)mean, (const T*)rstd, coef, (T*)gx, n * c,
+                   c, hw);
       ++launched;
     }
     return check_launch("batch_norm backward", launched);
@@ -912,8 +937,9 @@ int tg_max_pool2d_forward(int dtype, const tg_conv_shape* s, const void* x, void
   return TG_DISPATCH_FLOAT(dtype, T, [&] {
     if (pool2x2<T>(*s, {x, y, argmax})) {
       const int64_t planes = s->n * s->c;
-      maxpool2x2_fwd_kernel<<<pool_blocks(planes * (s->h / 2) * (s->w / 4)), kThreads, 0, st>>>(
-          (const float*)x, (float*)y, argmax, planes, (int)s->h, (int)s->w);
+      launch_pdl(maxpool2x2_fwd_kernel, dim3(pool_blocks(planes * (s->h / 2) * (s->w / 4))),
+                 dim3(kThreads), 0, st,
+                 (const float*)x, (float*)y, argmax, planes, (int)s->h, (int)s->w);
       return check_launch("max_pool2d");
     }
     const dim3 grid = position_grid(s->oh * s->ow, s->n * s->c);
@@ -932,8 +958,9 @@ int tg_max_pool2d_backward(int dtype, const tg_conv_shape* s, const void* g,
   return TG_DISPATCH_FLOAT(dtype, T, [&] {
     if (pool2x2<T>(*s, {g, argmax, gx})) {
       const int64_t planes = s->n * s->c;
-      maxpool2x2_bwd_kernel<<<pool_blocks(planes * (s->h / 2) * (s->w / 4)), kThreads, 0, st>>>(
-          (const float*)g, argmax, (float*)gx, planes, (int)s->h, (int)s->w);
+      launch_pdl(maxpool2x2_bwd_kernel, dim3(pool_blocks(planes * (s->h / 2) * (s->w / 4))),
+                 dim3(kThreads), 0, st,
+                 (const float*)g, argmax, (float*)gx, planes, (int)s->h, (int)s->w);
       return check_launch("max_pool2d backward");
     }
     const dim3 grid = position_grid(s->h * s->w, s->n * s->c);

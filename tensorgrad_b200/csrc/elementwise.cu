@@ -108,6 +108,8 @@ __device__ __forceinline__ T apply_unary(int op, T x, T a) {
 template <typename T>
 __global__ void unary_kernel(int op, int64_t n, const T* __restrict__ x, T alpha,
                              T* __restrict__ out) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
     out[i] = apply_unary<T>(op, op == TG_FILL ? T(0) : x[i], alpha);
@@ -197,6 +199,8 @@ __global__ void gelu_bwd_vec4_kernel(int64_t n4, const float4* __restrict__ g,
 template <typename T>
 __global__ void relu_bwd_kernel(int64_t n, const T* __restrict__ g, const T* __restrict__ x,
                                 T* __restrict__ gx) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
     gx[i] = x[i] > T(0) ? g[i] : T(0);
@@ -290,8 +294,8 @@ int tg_unary(int dtype, int op, int64_t n, const void* x, double alpha, void* ou
   TG_CHECK_ARG(op >= TG_NEG && op <= TG_POWS, "unary: bad op %d", op);
   if (n <= 0) return TG_OK;
   return TG_DISPATCH_FLOAT(dtype, T, [&] {
-    unary_kernel<T><<<grid_for(n, 256), 256, 0, as_stream(stream)>>>(op, n, (const T*)x,
-                                                                      (T)alpha, (T*)out);
+    launch_pdl(unary_kernel<T>, dim3(grid_for(n, 256)), dim3(256), 0, as_stream(stream),
+               op, n, (const T*)x, (T)alpha, (T*)out);
     return check_launch("unary");
   });
 }
@@ -339,8 +343,8 @@ int tg_gelu_backward(int dtype, int64_t n, const void* g, const void* x, void* g
 int tg_relu_backward(int dtype, int64_t n, const void* g, const void* x, void* gx, void* stream) {
   if (n <= 0) return TG_OK;
   return TG_DISPATCH_FLOAT(dtype, T, [&] {
-    relu_bwd_kernel<T><<<grid_for(n, 256), 256, 0, as_stream(stream)>>>(n, (const T*)g,
-                                                                         (const T*)x, (T*)gx);
+    launch_pdl(relu_bwd_kernel<T>, dim3(grid_for(n, 256)), dim3(256), 0, as_stream(stream),
+               n, (const T*)g, (const T*)x, (T*)gx);
     return check_launch("relu_backward");
   });
 }
