@@ -54,6 +54,10 @@ int tg_device_info(int device, int* sm_count, int* cc_major, int* cc_minor);
 int tg_malloc(void** ptr, size_t bytes, void* stream);
 int tg_free(void* ptr, void* stream);
 int tg_pool_stats(int device, uint64_t* reserved_bytes, uint64_t* used_bytes);
+/* High-water mark of the pool's bytes in use since the last reset (then reset when `reset`
+ * is nonzero): the device counterpart of the host peak the reference's gradient-checkpointing
+ * tests take with tracemalloc (tests/test_checkpoint.py:116-131). */
+int tg_pool_peak(int device, int reset, uint64_t* used_high_bytes);
 int tg_host_alloc(void** ptr, size_t bytes);
 int tg_host_free(void* ptr);
 int tg_set_device(int device);

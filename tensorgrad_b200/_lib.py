@@ -66,6 +66,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tg_malloc": (c_int, [POINTER(c_void_p), sz, vp]),
     "tg_free": (c_int, [vp, vp]),
     "tg_pool_stats": (c_int, [c_int, POINTER(ctypes.c_uint64), POINTER(ctypes.c_uint64)]),
+    "tg_pool_peak": (c_int, [c_int, c_int, POINTER(ctypes.c_uint64)]),
     "tg_host_alloc": (c_int, [POINTER(c_void_p), sz]),
     "tg_host_free": (c_int, [vp]),
     "tg_set_device": (c_int, [c_int]),

@@ -12,6 +12,9 @@ host sees the same stream as in the reference.
 
 from __future__ import annotations
 
+import contextlib
+from collections.abc import Iterator
+
 import numpy as np
 
 
@@ -27,6 +30,21 @@ def manual_seed(seed: int) -> None:
 def get_rng() -> np.random.Generator:
     """Return the global generator."""
     return _RngState.generator
+
+
+@contextlib.contextmanager
+def replaying(generator: np.random.Generator) -> Iterator[None]:
+    """Install ``generator`` as the global generator for the block and put the previous one
+    back afterwards (the reference's _random.py:35-46). Gradient checkpointing recomputes a
+    function inside this with a copy of the generator taken before its forward pass, so the
+    device dropout kernels, which take their PCG64 state from the global generator, draw the
+    same keep-masks again."""
+    previous = _RngState.generator
+    _RngState.generator = generator
+    try:
+        yield
+    finally:
+        _RngState.generator = previous
 
 
 #: Bit generators whose raw words carry 64 uniform bits (four 16-bit uniforms each).

@@ -72,6 +72,19 @@ int tg_pool_stats(int device, uint64_t* reserved_bytes, uint64_t* used_bytes) {
   return TG_OK;
 }
 
+int tg_pool_peak(int device, int reset, uint64_t* used_high_bytes) {
+  cudaMemPool_t pool;
+  TG_CUDA_TRY(cudaDeviceGetDefaultMemPool(&pool, device));
+  uint64_t high = 0;
+  TG_CUDA_TRY(cudaMemPoolGetAttribute(pool, cudaMemPoolAttrUsedMemHigh, &high));
+  if (used_high_bytes) *used_high_bytes = high;
+  if (reset) {
+    uint64_t zero = 0;  // the watermark can only be reset to zero (then tracks from now)
+    TG_CUDA_TRY(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrUsedMemHigh, &zero));
+  }
+  return TG_OK;
+}
+
 int tg_host_alloc(void** ptr, size_t bytes) {
   TG_CHECK_ARG(ptr != nullptr, "tg_host_alloc: NULL result pointer");
   *ptr = nullptr;

@@ -81,6 +81,18 @@ def stream() -> int:
     return _State.stream
 
 
+def memory_stats(reset_peak: bool = False) -> dict[str, int]:
+    """Bytes of the current device's memory pool: ``reserved`` (held by the pool), ``used``
+    (in live buffers) and ``peak`` (the most in use at once since the last reset; with
+    ``reset_peak`` the mark starts again from now). Frees are stream-ordered, so synchronize
+    first for figures that include everything already released."""
+    dev = current_device()
+    reserved, used, peak = ctypes.c_uint64(0), ctypes.c_uint64(0), ctypes.c_uint64(0)
+    check(lib.tg_pool_stats(dev, ctypes.byref(reserved), ctypes.byref(used)), "memory_stats")
+    check(lib.tg_pool_peak(dev, int(reset_peak), ctypes.byref(peak)), "memory_stats")
+    return {"reserved": reserved.value, "used": used.value, "peak": peak.value}
+
+
 def dtype_code(dtype: np.dtype[Any]) -> int:
     if dtype == np.float32:
         return F32

@@ -25,6 +25,7 @@ from tensorgrad_b200.nn.attention import LayerCache, MultiHeadAttention
 from tensorgrad_b200.nn.layers import GELU, Dropout, Embedding, LayerNorm, Linear, Sequential
 from tensorgrad_b200.nn.module import Module
 from tensorgrad_b200.tensor import Tensor
+from tensorgrad_b200.utils.grad_checkpoint import checkpoint
 
 __all__ = ["GPT", "GPTConfig", "KVCache", "TransformerBlock"]
 
@@ -77,7 +78,11 @@ _RESIDUAL_OUTPUTS = ("attn.proj", "mlp.2")
 
 
 class GPT(Module):
-    """Decoder-only transformer language model: ids ``(B, T)`` to logits ``(B, T, V)``."""
+    """Decoder-only transformer language model: ids ``(B, T)`` to logits ``(B, T, V)``.
+
+    With :attr:`gradient_checkpointing` set, a training forward pass keeps only the residual
+    stream between blocks and recomputes each block in the backward pass
+    (``tensorgrad_b200.utils.checkpoint``; the reference's nn/transformer.py:155-159)."""
 
     gradient_checkpointing: bool
 
@@ -126,12 +131,10 @@ class GPT(Module):
             raise ValueError(f"sequence length {start + t} exceeds block_size "
                              f"{self.config.block_size}")
         if cache is None:
-            if self.gradient_checkpointing and is_grad_enabled():
-                raise NotImplementedError("gradient checkpointing (block recomputation) is not "
-                                          "available on the device path")
             x = self.drop(self.tok_emb(tokens) + self.pos_emb(_positions(0, t)))
+            recompute = self.gradient_checkpointing and is_grad_enabled()
             for block in self.blocks:
-                x = block(x)
+                x = checkpoint(block, x) if recompute else block(x)
             return self.head(self.ln_f(x))
         if self.training:
             raise ValueError("a KV cache is for inference: call eval() first")

@@ -83,3 +83,29 @@ def test_pcg64_take_is_random_raw():
     np.testing.assert_array_equal(_outputs_from(state, 1000), b.bit_generator.random_raw(1000))
     assert a.bit_generator.state == b.bit_generator.state
     assert pcg64_take(np.random.Generator(np.random.MT19937(0)), 4) is None
+
+
+def test_replaying_repeats_the_draws_and_restores_the_generator():
+    """Gradient checkpointing's recomputation: a copy of the generator taken before a forward
+    pass, installed with ``replaying``, hands the dropout kernels the same PCG64 states; the
+    outer generator comes back afterwards, also when the block raises."""
+    import copy
+
+    from tensorgrad_b200 import _random as R
+
+    R.manual_seed(5)
+    R.get_rng().standard_normal(3)
+    snapshot = copy.deepcopy(R.get_rng())
+    first = [R.pcg64_take(R.get_rng(), n) for n in (10, 3)]
+    outer = R.get_rng()
+    after = copy.deepcopy(outer.bit_generator.state)
+    with R.replaying(copy.deepcopy(snapshot)):
+        assert R.get_rng() is not outer
+        again = [R.pcg64_take(R.get_rng(), n) for n in (10, 3)]
+    assert R.get_rng() is outer
+    assert outer.bit_generator.state == after
+    for a, b in zip(first, again, strict=True):
+        np.testing.assert_array_equal(a, b)
+    with pytest.raises(KeyError), R.replaying(copy.deepcopy(snapshot)):
+        raise KeyError("inside")
+    assert R.get_rng() is outer

@@ -4,7 +4,8 @@
   where the generator continues);
 * attention dropout (scaled_dot_product_attention and the packed self-attention) against the
   float64 oracle driven with the same mask;
-* two GPT training steps with dropout 0.1 everywhere against the reference's own run.
+* two GPT training steps with dropout 0.1 everywhere against the reference's own run, with
+  and without gradient checkpointing of every block.
 """
 
 from __future__ import annotations
@@ -88,9 +89,13 @@ def test_packed_attention_dropout_matches_oracle():
     assert_parity(x.grad.numpy(), ref, 1e-4, "dqkv")
 
 
+@pytest.mark.parametrize("recompute", [False, True], ids=["plain", "checkpointed"])
 @pytest.mark.parametrize("dtype,rel", [(np.float32, 1e-4), (np.float64, 1e-10)],
                          ids=["fp32", "fp64"])
-def test_gpt_with_dropout_matches_reference_fixture(dtype, rel):
+def test_gpt_with_dropout_matches_reference_fixture(dtype, rel, recompute):
+    """With ``recompute`` every block is checkpointed (``GPT.gradient_checkpointing``): the
+    backward pass recomputes each block under the generator state of its forward pass, so
+    losses, gradients and updates still match the reference's run without checkpointing."""
     import tensorgrad_b200 as tg
 
     gold = load_golden("gpt_dropout.npz")
@@ -101,6 +106,7 @@ def test_gpt_with_dropout_matches_reference_fixture(dtype, rel):
         model = tg.nn.GPT(tg.nn.GPTConfig(vocab_size=cfg.vocab_size, block_size=cfg.block_size,
                                           n_layer=cfg.n_layer, n_head=cfg.n_head,
                                           n_embd=cfg.n_embd, dropout=s["dropout"]))
+        model.gradient_checkpointing = recompute
         init = ogpt.init_params(cfg, s["seed"])
         model.load_state_dict({**init, "head.weight": init["tok_emb.weight"]})
         tg.manual_seed(s["reseed"])
