@@ -361,6 +361,10 @@ int tg_conv2d_cols_shape(const tg_conv_shape* s, int64_t* rows, int64_t* ld);
 size_t tg_conv2d_forward_scratch_bytes(int dtype, const tg_conv_shape* s);
 int tg_conv2d_forward(int dtype, const tg_conv_shape* s, const void* x, const void* w,
                       const void* b, void* y, void* cols, void* scratch, void* stream);
+/* The patch matrix alone (what tg_conv2d_forward writes to `cols`): the weight-gradient
+ * product as an op of its own, for the differentiable VJPs of conv2d (ops/conv.py:215-250). */
+int tg_conv2d_im2col(int dtype, const tg_conv_shape* s, const void* x, void* cols,
+                     void* stream);
 /* g: (n, c_out, oh, ow). gx / gw / gb may be NULL (not needed). */
 size_t tg_conv2d_backward_scratch_bytes(int dtype, const tg_conv_shape* s, int need_gx);
 int tg_conv2d_backward(int dtype, const tg_conv_shape* s, const void* g, const void* cols,
@@ -392,6 +396,10 @@ int tg_max_pool2d_forward(int dtype, const tg_conv_shape* s, const void* x, void
                           uint8_t* argmax, void* stream);
 int tg_max_pool2d_backward(int dtype, const tg_conv_shape* s, const void* g,
                            const uint8_t* argmax, void* gx, void* stream);
+/* The adjoint of the backward: out (n, c, oh, ow) = u (n, c, h, w) at each window's recorded
+ * winner (0 for a winner in the padding); the VJP of the VJP (ops/conv.py:340-356). */
+int tg_max_pool2d_gather(int dtype, const tg_conv_shape* s, const void* u,
+                         const uint8_t* argmax, void* out, void* stream);
 
 /* ------------------------------------------------------------------ recurrent layers
  * ops/recurrent.py:223-437: a whole time-major sequence x (T, B, I) per call; gate order and

@@ -152,6 +152,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tg_conv2d_cols_shape": (c_int, [POINTER(ConvShape), pi64, pi64]),
     "tg_conv2d_forward_scratch_bytes": (sz, [c_int, POINTER(ConvShape)]),
     "tg_conv2d_forward": (c_int, [c_int, POINTER(ConvShape), vp, vp, vp, vp, vp, vp, vp]),
+    "tg_conv2d_im2col": (c_int, [c_int, POINTER(ConvShape), vp, vp, vp]),
     "tg_conv2d_backward_scratch_bytes": (sz, [c_int, POINTER(ConvShape), c_int]),
     "tg_conv2d_backward": (c_int, [c_int, POINTER(ConvShape), vp, vp, vp, vp, vp, vp, vp, vp]),
     "tg_batch_norm_scratch_bytes": (sz, [c_int, i64, i64, i64]),
@@ -161,6 +162,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                        vp]),
     "tg_max_pool2d_forward": (c_int, [c_int, POINTER(ConvShape), vp, vp, vp, vp]),
     "tg_max_pool2d_backward": (c_int, [c_int, POINTER(ConvShape), vp, vp, vp, vp]),
+    "tg_max_pool2d_gather": (c_int, [c_int, POINTER(ConvShape), vp, vp, vp, vp]),
     "tg_lstm_forward_scratch_bytes": (sz, [c_int, i64, i64, i64, i64]),
     "tg_lstm_forward": (c_int, [c_int, i64, i64, i64, i64] + [vp] * 12),
     "tg_lstm_backward_scratch_bytes": (sz, [c_int, i64, i64, i64, i64]),

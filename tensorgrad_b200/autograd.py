@@ -9,9 +9,11 @@ every sum is a device kernel. Error messages match the reference's, word for wor
 
 ``create_graph=True`` runs a second walk whose gradients are tensors built from differentiable
 device ops (each op's ``graph`` VJP), so they carry their own graph and can be differentiated
-again (double backward, ``func.hessian`` ...). Ops without a graph VJP (the fused attention,
-layer norm, convolution and recurrent kernels) raise ``NotImplementedError`` there. A hook lets
-data-parallel training start a gradient all-reduce the moment a leaf's gradient is final.
+again (double backward, ``func.hessian`` ...). Every op has one: the fused kernels (attention,
+layer and batch norm, convolution, pooling, recurrent layers, dropout, embedding) give theirs
+as differentiable ops of their own or as the same function composed of differentiable ops. A
+hook lets data-parallel training start a gradient all-reduce the moment a leaf's gradient is
+final.
 """
 
 from __future__ import annotations

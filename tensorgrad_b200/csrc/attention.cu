@@ -345,6 +345,131 @@ int attn_backward_any(const AttnDims& p, const T* q, const T* k, const T* v, con
                    (long long)p.D);
 }
 
+// Head sizes without kernels of their own (up to 128) run on the next wider kernel over
+// zero-padded contiguous copies: zero features add nothing to q.k, the padded value columns
+// give output features that are dropped, and the scale stays 1/sqrt(head_dim).
+int64_t padded_head(int64_t d) {
+  for (int64_t w : {8, 16, 32, 64, 128})
+    if (d <= w) return w;
+  return 0;
+}
+
+bool native_head(int64_t d) { return d == 8 || d == 16 || d == 32 || d == 64 || d == 128; }
+
+constexpr int kPadThreads = 256;
+
+// dst (B, H, n, dp), contiguous = src (strides sb, sh, st; d features), zero beyond d.
+template <typename T>
+__global__ void __launch_bounds__(kPadThreads)
+head_pad_kernel(const T* __restrict__ src, int64_t sb, int64_t sh, int64_t st,
+                T* __restrict__ dst, int64_t H, int64_t n, int64_t d, int64_t dp,
+                int64_t total) {
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = e % dp, r = e / dp, t = r % n, bh = r / n;
+    const int64_t b = bh / H, h = bh % H;
+    dst[e] = c < d ? src[b * sb + h * sh + t * st + c] : T(0);
+  }
+}
+
+// The first d features of src (B, H, n, dp), contiguous, into dst (strides sb, sh, st).
+template <typename T>
+__global__ void __launch_bounds__(kPadThreads)
+head_unpad_kernel(const T* __restrict__ src, T* __restrict__ dst, int64_t sb, int64_t sh,
+                  int64_t st, int64_t H, int64_t n, int64_t d, int64_t dp, int64_t total) {
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = e % d, r = e / d, t = r % n, bh = r / n;
+    const int64_t b = bh / H, h = bh % H;
+    dst[b * sb + h * sh + t * st + c] = src[r * dp + c];
+  }
+}
+
+template <typename T>
+void head_pad(const T* src, int64_t sb, int64_t sh, int64_t st, T* dst, const AttnDims& p,
+              int64_t n, int64_t dp, cudaStream_t s) {
+  const int64_t total = p.B * p.H * n * dp;
+  head_pad_kernel<T><<<grid_for(total, kPadThreads), kPadThreads, 0, s>>>(
+      src, sb, sh, st, dst, p.H, n, p.D, dp, total);
+}
+
+template <typename T>
+void head_unpad(const T* src, T* dst, int64_t sb, int64_t sh, int64_t st, const AttnDims& p,
+                int64_t n, int64_t dp, cudaStream_t s) {
+  const int64_t total = p.B * p.H * n * p.D;
+  head_unpad_kernel<T><<<grid_for(total, kPadThreads), kPadThreads, 0, s>>>(
+      src, dst, sb, sh, st, p.H, n, p.D, dp, total);
+}
+
+// `p` with head size dp and contiguous (B, H, T, dp) strides for every operand.
+AttnDims padded_dims(const AttnDims& p, int64_t dp) {
+  AttnDims c = p;
+  c.D = dp;
+  c.q_sb = c.o_sb = p.H * p.Tq * dp;
+  c.q_sh = c.o_sh = p.Tq * dp;
+  c.k_sb = c.v_sb = p.H * p.Tk * dp;
+  c.k_sh = c.v_sh = p.Tk * dp;
+  c.q_st = c.k_st = c.v_st = c.o_st = dp;
+  return c;  // the scale stays 1/sqrt(p.D)
+}
+
+// Scratch of the padded path, in elements: forward q, o (Tq rows) and k, v (Tk rows);
+// backward q, o, dout, dq and k, v, dk, dv.
+int64_t padded_elems(const tg_attn_shape* s, int per_side) {
+  const int64_t dp = padded_head(s->head_dim);
+  return (int64_t)per_side * s->batch * s->heads * (s->tq + s->tk) * dp;
+}
+
+template <typename T>
+int attn_forward_padded(const AttnDims& p, const T* q, const T* k, const T* v, T* o, T* lse,
+                        void* scratch, cudaStream_t s) {
+  const int64_t dp = padded_head(p.D);
+  const int64_t nq = p.B * p.H * p.Tq * dp, nk = p.B * p.H * p.Tk * dp;
+  T* qp = reinterpret_cast<T*>(scratch);
+  T* op = qp + nq;
+  T* kp = op + nq;
+  T* vp = kp + nk;
+  head_pad<T>(q, p.q_sb, p.q_sh, p.q_st, qp, p, p.Tq, dp, s);
+  head_pad<T>(k, p.k_sb, p.k_sh, p.k_st, kp, p, p.Tk, dp, s);
+  head_pad<T>(v, p.v_sb, p.v_sh, p.v_st, vp, p, p.Tk, dp, s);
+  int r = check_launch("attention(pad)", 3);
+  if (r) return r;
+  r = attn_forward_any<T>(padded_dims(p, dp), qp, kp, vp, op, lse, s);
+  if (r) return r;
+  head_unpad<T>(op, o, p.o_sb, p.o_sh, p.o_st, p, p.Tq, dp, s);
+  return check_launch("attention(unpad)");
+}
+
+template <typename T>
+int attn_backward_padded(const AttnDims& p, const T* q, const T* k, const T* v, const T* o,
+                         const T* lse, const T* dout, T* dq, T* dk, T* dv, T* delta,
+                         T* pad, cudaStream_t s) {
+  const int64_t dp = padded_head(p.D);
+  const int64_t nq = p.B * p.H * p.Tq * dp, nk = p.B * p.H * p.Tk * dp;
+  T* qp = pad;
+  T* op = qp + nq;
+  T* gop = op + nq;
+  T* dqp = gop + nq;
+  T* kp = dqp + nq;
+  T* vp = kp + nk;
+  T* dkp = vp + nk;
+  T* dvp = dkp + nk;
+  head_pad<T>(q, p.q_sb, p.q_sh, p.q_st, qp, p, p.Tq, dp, s);
+  head_pad<T>(o, p.o_sb, p.o_sh, p.o_st, op, p, p.Tq, dp, s);
+  head_pad<T>(dout, p.o_sb, p.o_sh, p.o_st, gop, p, p.Tq, dp, s);
+  head_pad<T>(k, p.k_sb, p.k_sh, p.k_st, kp, p, p.Tk, dp, s);
+  head_pad<T>(v, p.v_sb, p.v_sh, p.v_st, vp, p, p.Tk, dp, s);
+  int r = check_launch("attention backward(pad)", 5);
+  if (r) return r;
+  r = attn_backward_any<T>(padded_dims(p, dp), qp, kp, vp, op, lse, gop, dqp, dkp, dvp, delta,
+                           s);
+  if (r) return r;
+  head_unpad<T>(dqp, dq, p.q_sb, p.q_sh, p.q_st, p, p.Tq, dp, s);
+  head_unpad<T>(dkp, dk, p.k_sb, p.k_sh, p.k_st, p, p.Tk, dp, s);
+  head_unpad<T>(dvp, dv, p.v_sb, p.v_sh, p.v_st, p, p.Tk, dp, s);
+  return check_launch("attention backward(unpad)", 3);
+}
+
 }  // namespace
 }  // namespace tg
 
@@ -384,7 +509,9 @@ bool aligned(std::initializer_list<const void*> ptrs) {
 extern "C" {
 
 size_t tg_attention_forward_scratch_bytes(int dtype, const tg_attn_shape* s) {
-  return use_tc(dtype, s) ? attention_tc_forward_scratch(s) : 16;
+  if (use_tc(dtype, s)) return attention_tc_forward_scratch(s);
+  if (native_head(s->head_dim) || padded_head(s->head_dim) == 0) return 16;
+  return (size_t)padded_elems(s, 2) * (dtype == TG_F64 ? 8 : 4) + 16;
 }
 
 int tg_attention_forward(int dtype, const tg_attn_shape* s, const void* q, const void* k,
@@ -399,6 +526,16 @@ int tg_attention_forward(int dtype, const tg_attn_shape* s, const void* q, const
                                 (float*)lse, scratch, st);
   }
   const AttnDims p = make_dims(s);
+  if (!native_head(s->head_dim)) {
+    if (padded_head(s->head_dim) == 0)
+      return set_error(TG_ERR_UNSUPPORTED, "attention: head_dim %lld (at most 128 here)",
+                       (long long)s->head_dim);
+    TG_CHECK_ARG(scratch, "attention_forward: NULL scratch");
+    return TG_DISPATCH_FLOAT(dtype, T, [&] {
+      return attn_forward_padded<T>(p, (const T*)q, (const T*)k, (const T*)v, (T*)o, (T*)lse,
+                                    scratch, st);
+    });
+  }
   return TG_DISPATCH_FLOAT(dtype, T, [&] {
     return attn_forward_any<T>(p, (const T*)q, (const T*)k, (const T*)v, (T*)o, (T*)lse, st);
   });
@@ -407,7 +544,10 @@ int tg_attention_forward(int dtype, const tg_attn_shape* s, const void* q, const
 size_t tg_attention_backward_scratch_bytes(int dtype, const tg_attn_shape* s) {
   if (use_tc(dtype, s)) return attention_tc_backward_scratch(s);
   const size_t es = dtype == TG_F64 ? 8 : 4;
-  return (size_t)(s->batch * s->heads * s->tq) * es + 16;
+  size_t bytes = (size_t)(s->batch * s->heads * s->tq) * es + 16;
+  if (!native_head(s->head_dim) && padded_head(s->head_dim) != 0)
+    bytes += 256 + (size_t)padded_elems(s, 4) * es;
+  return bytes;
 }
 
 int tg_attention_backward(int dtype, const tg_attn_shape* s, const void* q, const void* k,
@@ -421,6 +561,19 @@ int tg_attention_backward(int dtype, const tg_attn_shape* s, const void* q, cons
                                  (const float*)o, (const float*)lse, (const float*)dout,
                                  (float*)dq, (float*)dk, (float*)dv, scratch, st);
   const AttnDims p = make_dims(s);
+  if (!native_head(s->head_dim)) {
+    if (padded_head(s->head_dim) == 0)
+      return set_error(TG_ERR_UNSUPPORTED, "attention: head_dim %lld (at most 128 here)",
+                       (long long)s->head_dim);
+    return TG_DISPATCH_FLOAT(dtype, T, [&] {
+      // delta (B H Tq) first, the padded copies from the next 256-byte boundary.
+      const size_t off = ((size_t)(p.B * p.H * p.Tq) * sizeof(T) + 255) & ~(size_t)255;
+      T* pad = reinterpret_cast<T*>(reinterpret_cast<uint8_t*>(scratch) + off);
+      return attn_backward_padded<T>(p, (const T*)q, (const T*)k, (const T*)v, (const T*)o,
+                                     (const T*)lse, (const T*)dout, (T*)dq, (T*)dk, (T*)dv,
+                                     (T*)scratch, pad, st);
+    });
+  }
   return TG_DISPATCH_FLOAT(dtype, T, [&] {
     return attn_backward_any<T>(p, (const T*)q, (const T*)k, (const T*)v, (const T*)o,
                                 (const T*)lse, (const T*)dout, (T*)dq, (T*)dk, (T*)dv,

@@ -568,6 +568,28 @@ maxpool_bwd_kernel(const T* __restrict__ g, const uint8_t* __restrict__ arg, T* 
   }
 }
 
+// The adjoint of maxpool_bwd_kernel (used by differentiable pooling VJPs): each output takes
+// the value of u at its window's recorded winner; a winner in the padding reads 0.
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+maxpool_gather_kernel(const T* __restrict__ u, const uint8_t* __restrict__ arg,
+                      T* __restrict__ out, tg_conv_shape s) {
+  const int ohw = (int)(s.oh * s.ow);
+  const int o = blockIdx.x * blockDim.x + threadIdx.x;
+  if (o >= ohw) return;
+  const int h = (int)s.h, w = (int)s.w, ow = (int)s.ow, hw = h * w, kw = (int)s.kw;
+  const int oy = o / ow, ox = o - oy * ow;
+  const int iy0 = oy * (int)s.sh - (int)s.ph, ix0 = ox * (int)s.sw - (int)s.pw;
+  int64_t p0, p1;
+  plane_range(s.n * s.c, p0, p1);
+  for (int64_t plane = p0; plane < p1; ++plane) {
+    const int cell = (int)arg[plane * ohw + o];
+    const int iy = iy0 + cell / kw, ix = ix0 + cell % kw;
+    const bool inside = iy >= 0 && iy < h && ix >= 0 && ix < w;
+    out[plane * ohw + o] = inside ? u[plane * hw + iy * w + ix] : T(0);
+  }
+}
+
 // 2 x 2 windows, stride 2, no padding, rows of a multiple of 4 floats (the CNN's pooling):
 // each thread takes two neighbouring outputs of one output row, from one 16-byte load per
 // input row, and writes both maxima (8 bytes) and both winner bytes (2 bytes). Same rule as
@@ -701,6 +723,28 @@ ConvScratch conv_bwd_layout(int dtype, const tg_conv_shape& s, bool need_gx) {
 
 using namespace tg;
 
+namespace tg {
+namespace {
+
+// The patch matrix of x (layout of tg_conv2d_cols_shape): rows of whole 16-byte groups of
+// pixels when the shape allows, else one pixel per thread.
+template <typename T>
+void launch_im2col(const tg_conv_shape& s, const void* x, void* cols, cudaStream_t st) {
+  const int64_t kp = patch_rows(s), ldm = patch_ld(s), K = s.c * s.kh * s.kw;
+  const int64_t ohw = s.oh * s.ow;
+  if (conv_vec4<T>(s, {cols}) && ldm % 4 == 0) {
+    const dim3 grid = position_grid(ohw / 4, kp, s.n);
+    launch_pdl(im2col4_kernel, dim3(grid), dim3(kThreads), 0, st,
+               (const float*)x, (float*)cols, s, K, kp, ldm);
+  } else {
+    const dim3 grid = position_grid(ohw, kp, s.n);
+    im2col_kernel<T><<<grid, kThreads, 0, st>>>((const T*)x, (T*)cols, s, K, kp, ldm);
+  }
+}
+
+}  // namespace
+}  // namespace tg
+
 extern "C" {
 
 int tg_conv2d_cols_shape(const tg_conv_shape* s, int64_t* rows, int64_t* ld) {
@@ -717,6 +761,18 @@ size_t tg_conv2d_forward_scratch_bytes(int dtype, const tg_conv_shape* s) {
   return kp != K ? align256((size_t)(s->c_out * kp) * es) : 16;
 }
 
+int tg_conv2d_im2col(int dtype, const tg_conv_shape* s, const void* x, void* cols,
+                     void* stream) {
+  int rc = check_conv(s, false);
+  if (rc) return rc;
+  if (s->n * s->oh * s->ow == 0) return TG_OK;
+  cudaStream_t st = as_stream(stream);
+  return TG_DISPATCH_FLOAT(dtype, T, [&] {
+    launch_im2col<T>(*s, x, cols, st);
+    return check_launch("conv2d(im2col)");
+  });
+}
+
 int tg_conv2d_forward(int dtype, const tg_conv_shape* s, const void* x, const void* w,
                       const void* b, void* y, void* cols, void* scratch, void* stream) {
   int rc = check_conv(s, false);
@@ -727,14 +783,7 @@ int tg_conv2d_forward(int dtype, const tg_conv_shape* s, const void* x, const vo
   if (rows == 0) return TG_OK;
   TG_CHECK_ARG(kp == K || scratch, "conv2d: scratch required");
   return TG_DISPATCH_FLOAT(dtype, T, [&] {
-    if (conv_vec4<T>(*s, {cols}) && ldm % 4 == 0) {
-      const dim3 grid = position_grid(ohw / 4, kp, s->n);
-      launch_pdl(im2col4_kernel, dim3(grid), dim3(kThreads), 0, st,
-                 (const float*)x, (float*)cols, *s, K, kp, ldm);
-    } else {
-      const dim3 grid = position_grid(ohw, kp, s->n);
-      im2col_kernel<T><<<grid, kThreads, 0, st>>>((const T*)x, (T*)cols, *s, K, kp, ldm);
-    }
+    launch_im2col<T>(*s, x, cols, st);
     int launched = 1;
     const T* wk = (const T*)w;
     if (kp != K) {
@@ -969,6 +1018,20 @@ int tg_max_pool2d_backward(int dtype, const tg_conv_shape* s, const void* g,
     else
       maxpool_bwd_kernel<T, false><<<grid, kThreads, 0, st>>>((const T*)g, argmax, (T*)gx, *s);
     return check_launch("max_pool2d backward");
+  });
+}
+
+int tg_max_pool2d_gather(int dtype, const tg_conv_shape* s, const void* u,
+                         const uint8_t* argmax, void* out, void* stream) {
+  int rc = check_conv(s, true);
+  if (rc) return rc;
+  TG_CHECK_ARG(s->kh * s->kw <= 256, "max_pool2d: at most 256 cells per window");
+  if (s->n * s->c * s->oh * s->ow == 0) return TG_OK;
+  cudaStream_t st = as_stream(stream);
+  return TG_DISPATCH_FLOAT(dtype, T, [&] {
+    const dim3 grid = position_grid(s->oh * s->ow, s->n * s->c);
+    maxpool_gather_kernel<T><<<grid, kThreads, 0, st>>>((const T*)u, argmax, (T*)out, *s);
+    return check_launch("max_pool2d gather");
   });
 }
 

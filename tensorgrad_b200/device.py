@@ -483,7 +483,8 @@ def is_pinned(arr: np.ndarray) -> bool:
 
 
 def from_numpy(arr: np.ndarray, dtype: Any = None) -> DeviceArray:
-    a = np.ascontiguousarray(arr, dtype=dtype)
+    # ascontiguousarray gives 0-d input a shape of (1,): keep the caller's shape.
+    a = np.ascontiguousarray(arr, dtype=dtype).reshape(np.shape(arr))
     out = empty(a.shape, a.dtype)
     upload_into(out, a)
     return out

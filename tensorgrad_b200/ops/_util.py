@@ -48,6 +48,31 @@ def constant(data: DeviceArray) -> Tensor:
     return Tensor._wrap(data)
 
 
+def identity(x: Tensor) -> Tensor:
+    """A node that passes gradients straight through to ``x``: differentiating against it
+    reaches ``x``'s own graph."""
+    return make_result(x.data, (x,), lambda g, need: (g,), "identity",
+                       lambda g, y, need: (g,))
+
+
+def graph_by_composite(parents: tuple[Tensor, ...], composite: Any, g: Tensor,
+                       need: Need) -> tuple[Tensor | None, ...]:
+    """The differentiable VJP of a fused op, taken through ``composite``: the same function
+    of ``parents`` written with differentiable ops. It runs on identity nodes over the
+    parents that need a gradient, and its own graph VJPs (kept, ``create_graph``) give
+    gradients that are differentiable again, in ``g`` and in the parents."""
+    from tensorgrad_b200 import autograd
+
+    with autograd.enable_grad():
+        leaves = [identity(p) if n else p for p, n in zip(parents, need, strict=True)]
+        y = composite(*leaves)
+    wanted = [t for t, n in zip(leaves, need, strict=True) if n]
+    if not wanted or not y.requires_grad:
+        return (None,) * len(parents)
+    found = iter(autograd.grad(y, wanted, grad_outputs=g, create_graph=True, allow_unused=True))
+    return tuple(next(found) if n else None for n in need)
+
+
 def unbroadcast(grad: DeviceArray, shape: tuple[int, ...]) -> DeviceArray:
     """Sum ``grad`` down to ``shape``: the adjoint of broadcasting (ops/_util.py:49-63).
 

@@ -6,6 +6,13 @@ instead of the ``(T_q, T_k)`` probabilities, and the VJP recomputes them.
 :func:`packed_self_attention` reads Q, K and V as strided views of the packed ``(B, T, 3D)``
 QKV projection and writes their gradients straight into one ``(B, T, 3D)`` buffer, as the
 reference does.
+
+Both are differentiable to any order (``create_graph=True``): their graph VJPs differentiate
+the same function written with differentiable ops (``q k^T`` and ``P v`` products, the
+softmax normalised against the forward's saved log-sum-exp, the causal mask as a ``-inf``
+bias, the dropout keep-mask regenerated from the call's generator state as a constant), as
+the reference's graph VJPs do (ops/attention.py:118-160). That path materialises the
+``(T_q, T_k)`` probabilities; first-order training never takes it.
 """
 
 from __future__ import annotations
@@ -20,7 +27,9 @@ from tensorgrad_b200 import device
 from tensorgrad_b200._lib import AttnShape, check, lib
 from tensorgrad_b200._random import dropout_threshold, get_rng, pcg64_take
 from tensorgrad_b200.device import DeviceArray, dtype_code
-from tensorgrad_b200.ops._util import Need, as_tensor, make_result, unbroadcast
+from tensorgrad_b200.ops._util import (
+    Need, as_tensor, constant, graph_by_composite, make_result, unbroadcast,
+)
 from tensorgrad_b200.ops.elementwise import cast_array
 from tensorgrad_b200.profiler import profiled
 from tensorgrad_b200.tensor import Tensor
@@ -88,6 +97,47 @@ def _backward_dropout(shape: AttnShape, code: int, q: int, k: int, v: int, do: i
         code, shape, q, k, v, do, dq, dk, dv,
         state.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), threshold, scale, scratch.ptr,
         device.stream()), "attention backward (dropout)")
+
+
+def _causal_bias(n_q: int, n_k: int, dtype: np.dtype[Any]) -> Tensor:
+    """0 where attention is allowed, ``-inf`` where the causal mask forbids it."""
+    bias = np.where(causal_mask(n_q, n_k), -np.inf, 0.0).astype(dtype)
+    return constant(device.from_numpy(bias))
+
+
+def _keep_scaled(score_shape: tuple[int, ...], dtype: np.dtype[Any],
+                 drop: tuple[np.ndarray, int, float]) -> Tensor:
+    """The call's attention-dropout keep-mask times the survivor scale over ``score_shape``,
+    regenerated from its PCG64 state (the same element order as the fused kernels)."""
+    from tensorgrad_b200.ops.shape import broadcast_array
+
+    state, threshold, scale = drop
+    ones = broadcast_array(device.scalar_like(1.0, dtype), score_shape)
+    out = device.empty(score_shape, dtype)
+    check(lib.tg_dropout_pcg64(dtype_code(dtype), ones.size, ones.ptr, out.ptr,
+                               state.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), 0,
+                               threshold, scale, device.stream()), "attention dropout mask")
+    return constant(out)
+
+
+def _composite(q: Tensor, k: Tensor, v: Tensor, bias: Tensor | None, lse: Tensor,
+               keep: Tensor | None) -> Tensor:
+    """Attention in differentiable ops: ``softmax(q k^T / sqrt(d) + bias) [* keep] v`` with
+    the softmax shifted by the forward's row log-sum-exp (a constant: any shift gives the same
+    function, this one keeps every exponent <= 0)."""
+    from tensorgrad_b200.ops import elementwise as E
+    from tensorgrad_b200.ops import reduce as R
+    from tensorgrad_b200.ops.linalg import matmul
+    from tensorgrad_b200.ops.shape import transpose
+
+    scores = E.mul(matmul(q, transpose(k, -1, -2)), 1.0 / math.sqrt(q.shape[-1]))
+    if bias is not None:
+        scores = E.add(scores, bias)
+    e = E.exp(E.sub(scores, lse))
+    p = E.div(e, R.sum(e, -1, keepdims=True))
+    if keep is not None:
+        p = E.mul(p, keep)
+    return matmul(p, v)
 
 
 def _as_bhtd(shape: tuple[int, ...]) -> tuple[int, int]:
@@ -166,7 +216,15 @@ def scaled_dot_product_attention(
             grads.append(gr if gr.dtype == t.dtype else cast_array(gr, t.dtype))
         return tuple(grads)
 
-    return make_result(out, (tq, tk, tv), backward, "attention")
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor | None, ...]:
+        bias = _causal_bias(n_q, n_k, dt) if causal else None
+        keep = None if drop is None else _keep_scaled((*batch, n_q, n_k), dt, drop)
+        lse_t = constant(lse.reshape((*batch, n_q, 1)))
+        return graph_by_composite((tq, tk, tv),
+                                  lambda a, b_, c: _composite(a, b_, c, bias, lse_t, keep),
+                                  g, need)
+
+    return make_result(out, (tq, tk, tv), backward, "attention", graph)
 
 
 @profiled("self_attention")
@@ -214,4 +272,18 @@ def packed_self_attention(
                               gb + d * es, gb + 2 * d * es, drop)
         return (dqkv,)
 
-    return make_result(out, (tqkv,), backward, "self_attention")
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor | None, ...]:
+        from tensorgrad_b200.ops.shape import permute, reshape
+
+        bias = _causal_bias(t, t, x.dtype) if causal else None
+        keep = None if drop is None else _keep_scaled((b, num_heads, t, t), x.dtype, drop)
+        lse_t = constant(lse.reshape((b, num_heads, t, 1)))
+
+        def composite(packed: Tensor) -> Tensor:
+            parts = permute(reshape(packed, (b, t, 3, num_heads, hd)), (2, 0, 3, 1, 4))
+            o = _composite(parts[0], parts[1], parts[2], bias, lse_t, keep)
+            return reshape(permute(o, (0, 2, 1, 3)), (b, t, d))
+
+        return graph_by_composite((tqkv,), composite, g, need)
+
+    return make_result(out, (tqkv,), backward, "self_attention", graph)

@@ -14,7 +14,7 @@ from tensorgrad_b200._random import dropout_threshold, get_rng, keep_mask, pcg64
 from tensorgrad_b200.autograd import no_grad
 from tensorgrad_b200.device import DeviceArray, dtype_code
 from tensorgrad_b200.ops import elementwise, reduce
-from tensorgrad_b200.ops._util import Need, as_tensor, make_result
+from tensorgrad_b200.ops._util import Need, as_tensor, constant, make_result
 from tensorgrad_b200.ops.elementwise import binary_array, cast_array
 from tensorgrad_b200.profiler import profiled
 from tensorgrad_b200.tensor import Tensor
@@ -135,8 +135,43 @@ def layer_norm(x: Any, weight: Any = None, bias: Any = None, eps: float = 1e-5) 
             grads.append(gb)
         return tuple(grads)
 
+    def graph(g: Tensor, y_: Tensor, need: Need) -> tuple[Tensor | None, ...]:
+        # The same closed form with the row statistics recomputed as differentiable ops
+        # (ops/layers.py:120-138), so derivatives of any order flow through x as well.
+        return _normalized_vjp(g, tx, tw, tb, (tx.ndim - 1,), eps, need, None)
+
     parents = tuple(t for t in (tx, tw, tb) if t is not None)
-    return make_result(y, parents, backward, "layer_norm")
+    return make_result(y, parents, backward, "layer_norm", graph)
+
+
+def _normalized_vjp(g: Tensor, x: Tensor, w: Tensor | None, b: Tensor | None,
+                    axes: tuple[int, ...], eps: float, need: Need,
+                    view: tuple[int, ...] | None) -> tuple[Tensor | None, ...]:
+    """Graph VJP of ``xhat * w + b`` with ``xhat`` normalised over ``axes`` (biased
+    variance): ``gx = rstd (gh - mean(gh) - xhat mean(gh xhat))``, ``gh = g w``,
+    ``gw = sum(g xhat)``, ``gb = sum(g)``, the sums over the other axes. ``view`` reshapes
+    ``w`` to broadcast against ``x`` (batch norm's per-channel parameters)."""
+    from tensorgrad_b200.ops.shape import reshape
+
+    mul, sub, add = elementwise.mul, elementwise.sub, elementwise.add
+    centred = sub(x, reduce.mean(x, axes, keepdims=True))
+    rstd = elementwise.pow(add(reduce.mean(mul(centred, centred), axes, keepdims=True), eps),
+                           -0.5)
+    xhat = mul(centred, rstd)
+    other = tuple(i for i in range(x.ndim) if i not in axes)
+    grads: list[Tensor | None] = [None]
+    if need[0]:
+        gh = g if w is None else mul(g, w if view is None else reshape(w, view))
+        inner = sub(sub(gh, reduce.mean(gh, axes, keepdims=True)),
+                    mul(xhat, reduce.mean(mul(gh, xhat), axes, keepdims=True)))
+        grads[0] = mul(rstd, inner)
+    k = 1
+    for param, term in ((w, lambda: mul(g, xhat)), (b, lambda: g)):
+        if param is None:
+            continue
+        grads.append(reshape(reduce.sum(term(), other), param.shape) if need[k] else None)
+        k += 1
+    return tuple(grads)
 
 
 @profiled("batch_norm")
@@ -241,8 +276,14 @@ def _batch_norm_train(x: Tensor, running_mean: DeviceArray | None,
             grads.append(None if gb is None else gb.reshape(bias.shape))
         return tuple(grads)
 
+    def graph(g: Tensor, y_: Tensor, need: Need) -> tuple[Tensor | None, ...]:
+        # The composite the reference records, differentiated as differentiable ops: per
+        # channel statistics over the batch and spatial axes.
+        view = (1, c, *([1] * (x.ndim - 2)))
+        return _normalized_vjp(g, x, weight, bias, (0, *range(2, x.ndim)), eps, need, view)
+
     parents = tuple(t for t in (x, weight, bias) if t is not None)
-    return make_result(y, parents, backward, "batch_norm")
+    return make_result(y, parents, backward, "batch_norm", graph)
 
 
 def _segments(ids: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
@@ -278,7 +319,7 @@ def embedding(indices: Any, weight: Any) -> Tensor:
                                        device.async_error_word(device.ASYNC_EMBEDDING_ID),
                                        device.stream()), "embedding")
 
-        def backward_dev(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+        def scatter_dev(g: DeviceArray) -> DeviceArray:
             scr = device.scratch(lib.tg_embedding_sort_scratch_bytes(n, num))
             keys = device.empty((n,), np.int64)  # uint64 sort keys
             check(lib.tg_embedding_sort(ids_dev.ptr, n, num, keys.ptr, None, scr.ptr,
@@ -287,9 +328,11 @@ def embedding(indices: Any, weight: Any) -> Tensor:
             check(lib.tg_embedding_backward_sorted(dtype_code(g.dtype), g.ptr, keys.ptr, n,
                                                    gw.ptr, num, dim, 0, device.stream()),
                   "embedding backward")
-            return (gw,)
+            return gw
 
-        return make_result(out, (tw,), backward_dev, "embedding")
+        rows = _Rows(ids_dev, shape, num, dim,
+                     device.async_error_word(device.ASYNC_EMBEDDING_ID), scatter_dev)
+        return make_result(out, (tw,), rows.backward, "embedding", rows.graph)
     idx = np.asarray(indices)
     if not np.issubdtype(idx.dtype, np.integer):
         raise TypeError(f"embedding indices must be integers, got {idx.dtype}")
@@ -301,7 +344,7 @@ def embedding(indices: Any, weight: Any) -> Tensor:
     check(lib.tg_embedding_forward(code, ids_host.ptr, wd.ptr, out.ptr, flat.size, num, dim,
                                    None, device.stream()), "embedding")
 
-    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+    def scatter_host(g: DeviceArray) -> DeviceArray:
         order, seg_start, seg_id = _segments(flat)
         packed = device.from_numpy(np.concatenate([order, seg_start, seg_id]))
         n, ns = order.size, seg_id.size
@@ -310,9 +353,43 @@ def embedding(indices: Any, weight: Any) -> Tensor:
         check(lib.tg_embedding_backward(dtype_code(g.dtype), g.ptr, base, base + 8 * n,
                                         base + 8 * (n + ns + 1), ns, gw.ptr, num, dim, 0,
                                         device.stream()), "embedding backward")
-        return (gw,)
+        return gw
 
-    return make_result(out, (tw,), backward, "embedding")
+    rows = _Rows(ids_host, idx.shape, num, dim, None, scatter_host)
+    return make_result(out, (tw,), rows.backward, "embedding", rows.graph)
+
+
+class _Rows:
+    """An embedding call's ids: the row lookup (a gather) and its adjoint, the scatter-add of
+    gradient rows, as array functions and as differentiable ops whose VJPs are each other
+    (the reference's graph VJP is its ``scatter_add`` op, ops/layers.py:229-232)."""
+
+    def __init__(self, ids: DeviceArray, shape: tuple[int, ...], num: int, dim: int,
+                 err_word: Any, scatter_array: Any) -> None:
+        self.ids, self.shape, self.num, self.dim = ids, tuple(shape), num, dim
+        self.err_word, self.scatter_array = err_word, scatter_array
+
+    def gather_array(self, u: DeviceArray) -> DeviceArray:
+        out = device.empty((*self.shape, self.dim), u.dtype)
+        check(lib.tg_embedding_forward(dtype_code(u.dtype), self.ids.ptr, u.ptr, out.ptr,
+                                       self.ids.size, self.num, self.dim, self.err_word,
+                                       device.stream()), "embedding")
+        return out
+
+    def backward(self, g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+        return (self.scatter_array(g),)
+
+    def graph(self, g: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
+        return (self.scatter(g),)
+
+    def scatter(self, g: Tensor) -> Tensor:
+        return make_result(self.scatter_array(g.data), (g,),
+                           lambda u, need: (self.gather_array(u),), "embedding_backward",
+                           lambda u, y, need: (self.gather(u),))
+
+    def gather(self, u: Tensor) -> Tensor:
+        return make_result(self.gather_array(u.data), (u,),
+                           lambda v, need: (self.scatter_array(v),), "embedding", self.graph)
 
 
 @profiled("dropout")
@@ -342,7 +419,12 @@ def dropout(x: Any, p: float = 0.5, training: bool = True,
         def backward_host(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
             return (binary_array(g, mask, MUL),)
 
-        return make_result(binary_array(tx.data, mask, MUL), (tx,), backward_host, "dropout")
+        def graph_host(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
+            return (elementwise.mul(g, constant(mask)),)
+
+        return make_result(binary_array(tx.data, mask, MUL), (tx,), backward_host, "dropout",
+                           graph_host)
+
     def apply(src: DeviceArray) -> DeviceArray:
         out = device.empty(src.shape, src.dtype)
         check(lib.tg_dropout_pcg64(dtype_code(src.dtype), n, src.ptr, out.ptr,
@@ -354,4 +436,12 @@ def dropout(x: Any, p: float = 0.5, training: bool = True,
         # The VJP multiplies by the same mask, regenerated from the same generator state.
         return (apply(g if g.dtype == tx.dtype else g.astype(tx.dtype)),)
 
-    return make_result(apply(tx.data), (tx,), backward, "dropout")
+    def masked(t: Tensor) -> Tensor:
+        """The same mask applied to ``t`` as a differentiable op (self-adjoint)."""
+        return make_result(apply(t.data if t.dtype == tx.dtype else t.data.astype(tx.dtype)),
+                           (t,), backward, "dropout", graph)
+
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
+        return (masked(g),)
+
+    return make_result(apply(tx.data), (tx,), backward, "dropout", graph)

@@ -5,6 +5,11 @@ Each op runs a whole time-major sequence as one graph node and one C-ABI call pe
 the host loop over time steps is C++ inside the library, which launches the per-step
 recurrent GEMM (tensor cores for fp32) and the gate kernel. Weight layouts and gate order are
 the reference's (PyTorch's): LSTM rows (i, f, g, o), GRU rows (r, u, n).
+
+Under ``create_graph=True`` the VJP differentiates the same recurrence unrolled in
+differentiable ops (one input projection, then per step the recurrent product, the gates and
+the state update), so BPTT gradients are differentiable again, as the reference's graph VJPs
+are (ops/recurrent.py:294-332, 405-437).
 """
 
 from __future__ import annotations
@@ -17,7 +22,7 @@ import numpy as np
 from tensorgrad_b200 import device
 from tensorgrad_b200._lib import check, lib
 from tensorgrad_b200.device import DeviceArray, dtype_code
-from tensorgrad_b200.ops._util import Need, as_tensor, make_result
+from tensorgrad_b200.ops._util import Need, as_tensor, graph_by_composite, make_result
 from tensorgrad_b200.ops.elementwise import cast_array
 from tensorgrad_b200.profiler import profiled
 from tensorgrad_b200.tensor import Tensor
@@ -62,6 +67,54 @@ def _ptr(a: DeviceArray | None) -> int | None:
     return None if a is None else a.ptr
 
 
+def _cols(z: Tensor, start: int, stop: int) -> Tensor:
+    from tensorgrad_b200.ops.shape import getitem
+
+    return getitem(z, (slice(None), slice(start, stop)))
+
+
+def _lstm_composite(x: Tensor, h0: Tensor, c0: Tensor, w_ih: Tensor, w_hh: Tensor,
+                    b_ih: Tensor | None = None, b_hh: Tensor | None = None) -> Tensor:
+    """The LSTM recurrence in differentiable ops, ``(T, B, 2, H)`` like :func:`lstm`."""
+    from tensorgrad_b200.ops import elementwise as E
+    from tensorgrad_b200.ops.layers import linear
+    from tensorgrad_b200.ops.shape import getitem, stack
+
+    hid = h0.shape[1]
+    xw = linear(x, w_ih, b_ih)
+    h, c = h0, c0
+    steps = []
+    for t in range(x.shape[0]):
+        z = E.add(getitem(xw, t), linear(h, w_hh, b_hh))
+        i, f = E.sigmoid(_cols(z, 0, hid)), E.sigmoid(_cols(z, hid, 2 * hid))
+        g, o = E.tanh(_cols(z, 2 * hid, 3 * hid)), E.sigmoid(_cols(z, 3 * hid, 4 * hid))
+        c = E.add(E.mul(f, c), E.mul(i, g))
+        h = E.mul(o, E.tanh(c))
+        steps.append(stack([h, c], 1))
+    return stack(steps, 0)
+
+
+def _gru_composite(x: Tensor, h0: Tensor, w_ih: Tensor, w_hh: Tensor,
+                   b_ih: Tensor | None = None, b_hh: Tensor | None = None) -> Tensor:
+    """The GRU recurrence in differentiable ops, ``(T, B, H)`` like :func:`gru`."""
+    from tensorgrad_b200.ops import elementwise as E
+    from tensorgrad_b200.ops.layers import linear
+    from tensorgrad_b200.ops.shape import getitem, stack
+
+    hid = h0.shape[1]
+    xw = linear(x, w_ih, b_ih)
+    h = h0
+    steps = []
+    for t in range(x.shape[0]):
+        a, b = getitem(xw, t), linear(h, w_hh, b_hh)
+        r = E.sigmoid(E.add(_cols(a, 0, hid), _cols(b, 0, hid)))
+        u = E.sigmoid(E.add(_cols(a, hid, 2 * hid), _cols(b, hid, 2 * hid)))
+        n = E.tanh(E.add(_cols(a, 2 * hid, 3 * hid), E.mul(r, _cols(b, 2 * hid, 3 * hid))))
+        h = E.add(E.mul(E.sub(1.0, u), n), E.mul(u, h))
+        steps.append(h)
+    return stack(steps, 0)
+
+
 @profiled("lstm")
 def lstm(x: Any, h0: Any, c0: Any, w_ih: Any, w_hh: Any, b_ih: Any = None,
          b_hh: Any = None) -> Tensor:
@@ -104,7 +157,10 @@ def lstm(x: Any, h0: Any, c0: Any, w_ih: Any, w_hh: Any, b_ih: Any = None,
         grads = [dx, dh0, dc0, dw_ih, dw_hh]
         return tuple(grads + [db_ih, db_hh] if has_bias else grads)
 
-    return make_result(out, parents, backward, "lstm")
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor | None, ...]:
+        return graph_by_composite(parents, _lstm_composite, g, need)
+
+    return make_result(out, parents, backward, "lstm", graph)
 
 
 @profiled("gru")
@@ -146,4 +202,7 @@ def gru(x: Any, h0: Any, w_ih: Any, w_hh: Any, b_ih: Any = None, b_hh: Any = Non
         grads = [dx, dh0, dw_ih, dw_hh]
         return tuple(grads + [db_ih, db_hh] if has_bias else grads)
 
-    return make_result(out, parents, backward, "gru")
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor | None, ...]:
+        return graph_by_composite(parents, _gru_composite, g, need)
+
+    return make_result(out, parents, backward, "gru", graph)

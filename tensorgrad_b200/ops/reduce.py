@@ -110,7 +110,13 @@ def var(a: Any, axis: Any = None, keepdims: bool = False, correction: int = 1) -
     def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
         return (binary_array(expand_array(scale_array(g, scale), ta.shape, axes), centered, MUL),)
 
-    return make_result(out, (ta,), backward, "var")
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
+        from tensorgrad_b200.ops.elementwise import mul, sub
+
+        return (mul(_expand(mul(g, scale), ta.shape, axes),
+                    sub(ta, mean(ta, axes, keepdims=True))),)
+
+    return make_result(out, (ta,), backward, "var", graph)
 
 
 def max(a: Any, axis: Any = None, keepdims: bool = False) -> Tensor:  # noqa: A001

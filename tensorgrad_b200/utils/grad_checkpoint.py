@@ -28,19 +28,12 @@ from tensorgrad_b200 import autograd
 from tensorgrad_b200._random import get_rng, replaying
 from tensorgrad_b200.autograd import enable_grad, no_grad
 from tensorgrad_b200.device import DeviceArray
-from tensorgrad_b200.ops._util import as_tensor, make_result
+from tensorgrad_b200.ops._util import as_tensor, identity, make_result
 from tensorgrad_b200.tensor import Tensor
 
 __all__ = ["checkpoint"]
 
 Need = tuple[bool, ...]
-
-
-def _identity(x: Tensor) -> Tensor:
-    """A node that passes gradients straight through to ``x`` (keeps ``x``'s graph
-    reachable from a recomputation made under ``create_graph``)."""
-    return make_result(x.data, (x,), lambda g, need: (g,), "checkpoint_input",
-                       graph=lambda g, y, need: (g,))
 
 
 def _unique(tensors: Iterable[Tensor]) -> list[Tensor]:
@@ -94,7 +87,7 @@ def checkpoint(fn: Callable[..., Tensor], *args: Any, params: Iterable[Tensor] |
         and the recomputed output."""
         with enable_grad():
             if connect:
-                leaves = [_identity(x) if x._requires_grad else x for x in inputs]
+                leaves = [identity(x) if x._requires_grad else x for x in inputs]
             else:
                 leaves = [Tensor._wrap(x.data).requires_grad_() if x._requires_grad else x
                           for x in inputs]

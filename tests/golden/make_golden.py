@@ -295,6 +295,40 @@ def run_higher_order() -> dict[str, np.ndarray]:
     return out
 
 
+def run_higher_order_layers() -> dict[str, np.ndarray]:
+    """Second derivatives through the fused layers by the reference (float64): Hessian-vector
+    products of small functions of layer norm, variance, attention (with and without the
+    causal mask and dropout, and the packed form), embedding + layer norm + cross entropy,
+    LSTM, GRU and dropout; gradient penalties through conv2d, batch norm, ReLU and max
+    pooling (overlapping 3 x 3 windows, and 2 x 2); and one GPT step on a gradient penalty
+    with dropout 0.1. The programs are shared with the tests (specs.py)."""
+    import types
+
+    from tensorgrad import func
+    from tensorgrad.ops import attention as ref_attention
+    from tensorgrad.ops import layers as ref_layers
+    from tensorgrad.ops import recurrent as ref_recurrent
+    from tests.golden.specs import (
+        GPT_PENALTY, gpt_penalty_program, higher_order_layer_inputs, higher_order_layer_program,
+    )
+
+    tg.set_default_dtype(np.float64)
+    O = types.SimpleNamespace(
+        tanh=tg.tanh, relu=tg.relu, layer_norm=tg.layer_norm, var=tg.var,
+        sdpa=ref_attention.scaled_dot_product_attention,
+        packed=ref_attention.packed_self_attention, conv2d=tg.conv2d,
+        batch_norm=ref_layers.batch_norm, max_pool2d=tg.max_pool2d, embedding=tg.embedding,
+        linear=tg.linear, cross_entropy=tg.cross_entropy, lstm=ref_recurrent.lstm,
+        gru=ref_recurrent.gru, dropout=tg.dropout)
+
+    def host(t):
+        return np.array(t.data)
+
+    out = higher_order_layer_program(tg, O, func, host, higher_order_layer_inputs())
+    out.update(gpt_penalty_program(tg, nn, host, GPT_PENALTY))
+    return out
+
+
 def main() -> None:
     jobs = {
         "gpt_small": lambda: run_gpt(GPT_SMALL),
@@ -307,6 +341,7 @@ def main() -> None:
         "dropout_masks": run_dropout_masks,
         "gpt_generate": run_generate,
         "higher_order": run_higher_order,
+        "higher_order_layers": run_higher_order_layers,
     }
     names = sys.argv[1:] or [*jobs, "gpt_checkpoint"]
     for name in names:

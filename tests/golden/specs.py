@@ -98,3 +98,142 @@ def higher_order_inputs() -> dict[str, np.ndarray]:
         "w1": 0.5 * rng.standard_normal((7, 6)), "b1": 0.1 * rng.standard_normal(7),
         "w2": 0.5 * rng.standard_normal((3, 7)), "b2": 0.1 * rng.standard_normal(3),
     }
+
+
+#: The GPT of GPT_DROPOUT trained one step on ``loss + penalty * sum(grad^2)``: a gradient
+#: penalty that differentiates every op of the model twice (embedding, dropout, layer norm,
+#: packed attention with dropout, GELU, the head and cross entropy).
+GPT_PENALTY = dict(GPT_DROPOUT, penalty=0.01)
+
+
+def higher_order_layer_inputs() -> dict[str, np.ndarray]:
+    """Seeded float64 inputs of the second-order fixture of the fused layers
+    (higher_order_layers.npz)."""
+    rng = np.random.default_rng(83)
+    n = rng.standard_normal
+    return {
+        "ln_x": n((4, 6)), "ln_w": 1.0 + 0.1 * n(6), "ln_b": 0.1 * n(6), "ln_c": n((4, 6)),
+        "ln_vx": n((4, 6)), "ln_vw": n(6), "var_x": n((3, 5)),
+        "q": n((2, 2, 5, 4)), "k": n((2, 2, 5, 4)), "v": n((2, 2, 5, 4)),
+        "attn_c": n((2, 2, 5, 4)), "vq": n((2, 2, 5, 4)), "vk": n((2, 2, 5, 4)),
+        "vv": n((2, 2, 5, 4)),
+        "qkv": n((2, 5, 24)), "qkv_c": n((2, 5, 8)), "qkv_v": n((2, 5, 24)),
+        "cx": n((2, 3, 7, 7)), "cw": 0.3 * n((4, 3, 3, 3)), "cb": 0.1 * n(4),
+        "bn_w": 1.0 + 0.1 * n(4), "bn_b": 0.1 * n(4), "cc": n((2, 4, 4, 4)),
+        "cx2": n((2, 3, 8, 8)), "cc2": n((2, 4, 2, 2)),
+        "ids": rng.integers(0, 10, size=(3, 5)), "targets": rng.integers(0, 4, size=(3, 5)),
+        "emb": n((10, 6)), "head": 0.5 * n((4, 6)), "v_emb": n((10, 6)), "v_head": n((4, 6)),
+        "rx": n((4, 2, 3)), "rh0": 0.5 * n((2, 5)), "rc0": 0.5 * n((2, 5)),
+        "r_vx": n((4, 2, 3)),
+        "l_wih": 0.4 * n((20, 3)), "l_whh": 0.4 * n((20, 5)), "l_bih": 0.1 * n(20),
+        "l_bhh": 0.1 * n(20), "l_c": n((4, 2, 2, 5)), "l_vw": n((20, 5)),
+        "g_wih": 0.4 * n((15, 3)), "g_whh": 0.4 * n((15, 5)), "g_bih": 0.1 * n(15),
+        "g_bhh": 0.1 * n(15), "g_c": n((4, 2, 5)), "g_vw": n((15, 5)),
+        "d_x": n((6, 7)), "d_c": n((6, 7)), "d_v": n((6, 7)),
+    }
+
+
+def higher_order_layer_program(tg, O, func, host, d: dict[str, np.ndarray]) -> dict[str, np.ndarray]:
+    """Second derivatives through each fused layer, written once for both implementations:
+    ``tg`` is the package, ``O`` a namespace of its ops (tanh, relu, layer_norm, var, sdpa,
+    packed, conv2d, batch_norm, max_pool2d, embedding, linear, cross_entropy, lstm, gru,
+    dropout), ``func`` its function transforms and ``host(t)`` a tensor's values as an array.
+    Hessian-vector products of scalar functions of each layer, and gradient penalties
+    (``loss + sum(d loss / dx ** 2)`` differentiated to the parameters) through the CNN layers."""
+    T = tg.Tensor
+    out: dict[str, np.ndarray] = {}
+
+    def hvp(name: str, f, primals, tangents, keys) -> None:
+        _, hs = func.hvp(f, [T(d[p]) for p in primals], [T(d[t]) for t in tangents])
+        for k, h in zip(keys, hs, strict=True):
+            out[f"{name}_hvp_{k}"] = host(h)
+
+    hvp("ln", lambda x, w: (O.tanh(O.layer_norm(x, w, T(d["ln_b"]))) * T(d["ln_c"])).sum(),
+        ("ln_x", "ln_w"), ("ln_vx", "ln_vw"), ("x", "w"))
+    out["var_hess"] = host(func.hessian(lambda x: (O.var(x, axis=1) ** 2).sum())(T(d["var_x"])))
+
+    def attention(p: float, causal: bool):
+        def f(q, k, v):
+            rng = np.random.default_rng(71) if p else None
+            y = O.sdpa(q, k, v, causal=causal, dropout_p=p, training=p > 0, rng=rng)
+            return (O.tanh(y) * T(d["attn_c"])).sum()
+        return f
+
+    for name, p, causal in (("attn", 0.0, True), ("attn_full", 0.0, False),
+                            ("attn_drop", 0.25, True)):
+        hvp(name, attention(p, causal), ("q", "k", "v"), ("vq", "vk", "vv"), ("q", "k", "v"))
+
+    def packed(qkv):
+        y = O.packed(qkv, 2, causal=True, dropout_p=0.25, training=True,
+                     rng=np.random.default_rng(72))
+        return (O.tanh(y) * T(d["qkv_c"])).sum()
+
+    hvp("packed", packed, ("qkv",), ("qkv_v",), ("qkv",))
+
+    def cnn_penalty(name: str, x: str, c: str, conv: tuple[int, int], pool: tuple[int, ...]):
+        ts = [T(d[k], requires_grad=True) for k in (x, "cw", "cb", "bn_w", "bn_b")]
+        xs, w, b, bw, bb = ts
+        h = O.conv2d(xs, w, b, stride=conv[0], padding=conv[1])
+        h = O.batch_norm(h, None, None, bw, bb, training=True)
+        h = O.max_pool2d(O.relu(h), pool[0], pool[1], pool[2])
+        loss = (O.tanh(h) * T(d[c])).sum()
+        (gx,) = tg.autograd.grad(loss, [xs], create_graph=True)
+        total = loss + (gx * gx).sum()
+        total.backward()
+        out[f"{name}_total"] = np.asarray(host(total))
+        for k, t in zip(("x", "w", "b", "bn_w", "bn_b"), ts, strict=True):
+            out[f"{name}_grad_{k}"] = host(t.grad)
+
+    cnn_penalty("cnn", "cx", "cc", (1, 1), (3, 2, 1))
+    cnn_penalty("cnn2", "cx2", "cc2", (2, 1), (2, 2, 0))
+
+    def lm(e, w):
+        logits = O.linear(O.layer_norm(O.embedding(d["ids"], e)), w)
+        return O.cross_entropy(logits, d["targets"])
+
+    hvp("emb", lm, ("emb", "head"), ("v_emb", "v_head"), ("emb", "head"))
+
+    def lstm(x, w_hh):
+        y = O.lstm(x, T(d["rh0"]), T(d["rc0"]), T(d["l_wih"]), w_hh, T(d["l_bih"]),
+                   T(d["l_bhh"]))
+        return (O.tanh(y) * T(d["l_c"])).sum()
+
+    def gru(x, w_hh):
+        y = O.gru(x, T(d["rh0"]), T(d["g_wih"]), w_hh, T(d["g_bih"]), T(d["g_bhh"]))
+        return (O.tanh(y) * T(d["g_c"])).sum()
+
+    hvp("lstm", lstm, ("rx", "l_whh"), ("r_vx", "l_vw"), ("x", "w_hh"))
+    hvp("gru", gru, ("rx", "g_whh"), ("r_vx", "g_vw"), ("x", "w_hh"))
+
+    def dropped(x):
+        y = O.dropout(x, 0.3, True, np.random.default_rng(9))
+        return (O.tanh(y) * T(d["d_c"])).sum()
+
+    hvp("dropout", dropped, ("d_x",), ("d_v",), ("x",))
+    return out
+
+
+def gpt_penalty_program(tg, nn, host, spec: dict) -> dict[str, np.ndarray]:
+    """One GPT_PENALTY step: ``loss + penalty * sum over parameters of sum(grad ** 2)``,
+    differentiated to every parameter (the gradients built with ``create_graph``)."""
+    cfg = spec["cfg"]
+    model = nn.GPT(nn.GPTConfig(vocab_size=cfg.vocab_size, block_size=cfg.block_size,
+                                n_layer=cfg.n_layer, n_head=cfg.n_head, n_embd=cfg.n_embd,
+                                dropout=spec["dropout"]))
+    init = ogpt.init_params(cfg, spec["seed"])
+    model.load_state_dict({**init, "head.weight": init["tok_emb.weight"]})
+    tg.manual_seed(spec["reseed"])
+    names = [n for n, _ in model.named_parameters()]
+    params = list(model.parameters())
+    ids, targets = ogpt.synthetic_batch(cfg, spec["batch"], spec["seq"], spec["seed"] + 1)
+    loss = tg.cross_entropy(model(ids), targets)
+    grads = tg.autograd.grad(loss, params, create_graph=True)
+    penalty = (grads[0] * grads[0]).sum()
+    for g in grads[1:]:
+        penalty = penalty + (g * g).sum()
+    total = loss + penalty * spec["penalty"]
+    total.backward()
+    out = {"gpt_loss": np.asarray(host(loss)), "gpt_total": np.asarray(host(total))}
+    for n, p in zip(names, params, strict=True):
+        out[f"gpt_grad/{n}"] = host(p.grad)
+    return out

@@ -69,11 +69,16 @@ def test_gradient_penalty_backward_matches_reference(dtype, rel):
         assert_parity(t.grad.numpy(), gold[f"penalty_grad_{k}"], rel, f"penalty grad {k}")
 
 
-def test_ops_without_a_differentiable_vjp_raise():
+def test_a_node_without_a_differentiable_vjp_raises():
+    """Every op of the package has a graph VJP; a node made without one (a user's own op)
+    is refused by ``create_graph`` with its name, and still works to first order."""
     import tensorgrad_b200 as tg
+    from tensorgrad_b200.ops._util import make_result
 
     x = tg.Tensor(np.random.default_rng(0).standard_normal((2, 8)).astype(np.float32),
                   requires_grad=True)
-    y = tg.layer_norm(x).sum()
-    with pytest.raises(NotImplementedError, match="layer_norm"):
-        tg.autograd.grad(y, [x], create_graph=True)
+    y = make_result(x.data, (x,), lambda g, need: (g,), "user_identity").sum()
+    with pytest.raises(NotImplementedError, match="user_identity"):
+        tg.autograd.grad(y, [x], create_graph=True, retain_graph=True)
+    (g,) = tg.autograd.grad(y, [x])
+    np.testing.assert_array_equal(g.numpy(), np.ones((2, 8), np.float32))

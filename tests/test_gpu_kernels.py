@@ -408,8 +408,32 @@ def test_fused_attention_forward_shapes(dtype, qshape, tk, causal):
             assert_parity(ours.numpy(), ref, rel(dtype), name)
 
 
+# Head sizes without kernels of their own take the next wider CUDA-core kernel over
+# zero-padded copies (fp32 heads of a multiple of 4 features with tq == tk stay on the
+# tensor-core path).
+@pytest.mark.parametrize("qshape,tk,causal", [((1, 2, 7, 6), 7, True),
+                                              ((2, 1, 9, 12), 11, False),
+                                              ((1, 2, 5, 4), 8, True),
+                                              ((1, 1, 13, 100), 13, True),
+                                              ((2, 2, 6, 3), 6, False)])
+def test_attention_other_head_sizes(dtype, qshape, tk, causal):
+    import tensorgrad_b200 as tg
+
+    rng = np.random.default_rng(qshape[3] + tk)
+    b, h, tq, d = qshape
+    q, k, v = (rng.standard_normal(s) for s in (qshape, (b, h, tk, d), (b, h, tk, d)))
+    do = rng.standard_normal(qshape)
+    tq_, tk_, tv_ = (tensor(a, dtype) for a in (q, k, v))
+    o = tg.nn.functional.scaled_dot_product_attention(tq_, tk_, tv_, causal=causal)
+    dq, dk, dv = tg.autograd.grad(o, [tq_, tk_, tv_], grad_outputs=do.astype(dtype))
+    ref_o, p = O.attention_forward(q, k, v, causal)
+    for ours, ref, name in zip((o, dq, dk, dv), (ref_o, *O.attention_backward(do, q, k, v, p)),
+                               ("out", "dq", "dk", "dv"), strict=True):
+        assert_parity(ours.numpy(), ref, rel(dtype), name)
+
+
 @pytest.mark.parametrize("b,t,h,hd", [(2, 64, 4, 32), (1, 129, 2, 64), (2, 40, 3, 16),
-                                      (1, 70, 1, 128), (2, 300, 2, 64)])
+                                      (1, 70, 1, 128), (2, 300, 2, 64), (2, 9, 3, 6)])
 def test_packed_self_attention(dtype, b, t, h, hd):
     import tensorgrad_b200 as tg
 
