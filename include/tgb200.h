@@ -172,7 +172,8 @@ int tg_sum_all(int dtype, const void* x, void* out, int64_t n, void* scratch, vo
 /* ------------------------------------------------------------------ elementwise
  * Broadcast binary op: out (contiguous, shape[ndim]) = a op b, with a/b read through element
  * strides (0 on broadcast axes). ops/elementwise.py:43-121. op: */
-enum tg_binary_op { TG_ADD = 0, TG_SUB = 1, TG_MUL = 2, TG_DIV = 3, TG_POW = 4 };
+enum tg_binary_op { TG_ADD = 0, TG_SUB = 1, TG_MUL = 2, TG_DIV = 3, TG_POW = 4,
+                    TG_EQ = 5 /* 1 where a == b, else 0 (the extrema's tie masks) */ };
 int tg_binary(int dtype, int op, int ndim, const int64_t* shape, const void* a,
               const int64_t* a_strides, const void* b, const int64_t* b_strides, void* out,
               void* stream);
@@ -185,9 +186,36 @@ int tg_scale_by_device_scalar(int dtype, int64_t n, const void* x, const void* s
 /* Unary ops: out = f(x). ops/elementwise.py:133-268. */
 enum tg_unary_op {
   TG_NEG = 0, TG_EXP = 1, TG_LOG = 2, TG_SQRT = 3, TG_TANH = 4, TG_SIGMOID = 5, TG_RELU = 6,
-  TG_SQUARE = 7, TG_FILL = 8 /* out = alpha */, TG_POWS = 9 /* out = x ** alpha */
+  TG_SQUARE = 7, TG_FILL = 8 /* out = alpha */, TG_POWS = 9 /* out = x ** alpha */,
+  TG_ABS = 10, TG_FINITE_OR_ZERO = 11 /* x where finite, else 0 (softmax's row shift) */,
+  TG_LOG1P = 12 /* log(1 + x), accurate for small x (binary cross entropy's softplus) */
 };
 int tg_unary(int dtype, int op, int64_t n, const void* x, double alpha, void* out, void* stream);
+/* out = cond ? a : b with broadcasting (ops/shape.py:290-328, where / masked_fill): `cond`
+ * read as != 0, of cond_dtype -1 (one byte per element, NumPy bool), TG_F32, TG_F64 or
+ * TG_I64; every operand addressed by its own element strides over the output shape (0 on
+ * broadcast axes). */
+int tg_where(int dtype, int cond_dtype, int ndim, const int64_t* shape, const void* cond,
+             const int64_t* cond_strides, const void* a, const int64_t* a_strides,
+             const void* b, const int64_t* b_strides, void* out, void* stream);
+/* out (bytes) = a op b with broadcasting, op 0..5 = ==, !=, <, <=, >, >= (Tensor's
+ * comparison operators, tensor.py); strides as tg_where's. */
+int tg_compare(int dtype, int op, int ndim, const int64_t* shape, const void* a,
+               const int64_t* a_strides, const void* b, const int64_t* b_strides, uint8_t* out,
+               void* stream);
+/* Keep-axis maximum (is_min = 0) or minimum of x over the axes with keep[i] == 0
+ * (ops/reduce.py:70-105); a NaN anywhere in a reduced set gives NaN, as np.max does. */
+int tg_reduce_extremum(int dtype, int is_min, int ndim, const int64_t* in_shape,
+                       const int* keep, const void* x, void* out, void* stream);
+/* Tensor.all / any (tensor.py:418-429): one byte per kept element, whether every (any)
+ * element of its reduced set is nonzero; x of in_dtype -1 (bytes), TG_F32, TG_F64 or
+ * TG_I64. An empty set gives 1 for all and 0 for any. */
+int tg_reduce_truth(int in_dtype, int is_all, int ndim, const int64_t* in_shape,
+                    const int* keep, const void* x, uint8_t* out, void* stream);
+/* Tensor.argmax (tensor.py:431-435): int64 index within the reduced set (row-major over the
+ * reduced axes) of its first maximum, a NaN counting as the maximum. */
+int tg_argmax(int dtype, int ndim, const int64_t* in_shape, const int* keep, const void* x,
+              int64_t* out, void* stream);
 /* dtype conversion of n elements (ops/elementwise.py:323-343 astype). */
 int tg_cast(int src_dtype, int dst_dtype, int64_t n, const void* src, void* dst, void* stream);
 /* dst[idx . dst_strides] = src[idx . src_strides] for every index of shape[ndim] (element
@@ -437,6 +465,19 @@ int tg_gru_backward(int dtype, int64_t T, int64_t B, int64_t I, int64_t H, const
                     const void* acts, const void* hn, const void* out, void* dx, void* dh0,
                     void* dw_ih, void* dw_hh, void* db_ih, void* db_hh, void* scratch,
                     void* stream);
+
+/* Elman RNN (ops/recurrent.py:140-219; G = 1): h_t = act(x_t W_ih^T + b_ih + h_{t-1} W_hh^T
+ * + b_hh), act = tanh (relu = 0) or max(., 0) (relu = 1); out (T, B, H) holds h_1 .. h_T,
+ * which is all the VJP needs. g is the gradient of out. */
+size_t tg_rnn_forward_scratch_bytes(int dtype, int64_t T, int64_t B, int64_t I, int64_t H);
+int tg_rnn_forward(int dtype, int relu, int64_t T, int64_t B, int64_t I, int64_t H,
+                   const void* x, const void* h0, const void* w_ih, const void* w_hh,
+                   const void* b_ih, const void* b_hh, void* out, void* scratch, void* stream);
+size_t tg_rnn_backward_scratch_bytes(int dtype, int64_t T, int64_t B, int64_t I, int64_t H);
+int tg_rnn_backward(int dtype, int relu, int64_t T, int64_t B, int64_t I, int64_t H,
+                    const void* g, const void* x, const void* h0, const void* w_ih,
+                    const void* w_hh, const void* out, void* dx, void* dh0, void* dw_ih,
+                    void* dw_hh, void* db_ih, void* db_hh, void* scratch, void* stream);
 
 /* ------------------------------------------------------------------ data-parallel exchange
  * The averaged gradient all-reduce of batch-sharded training (no reference counterpart: the

@@ -14,8 +14,9 @@ from ctypes import POINTER, c_char_p, c_double, c_int, c_int64, c_size_t, c_uint
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libtgb200.so")
 
 F32, F64 = 0, 1
-ADD, SUB, MUL, DIV, POW = 0, 1, 2, 3, 4
-NEG, EXP, LOG, SQRT, TANH, SIGMOID, RELU, SQUARE, FILL, POWS = range(10)
+ADD, SUB, MUL, DIV, POW, EQ = 0, 1, 2, 3, 4, 5
+(NEG, EXP, LOG, SQRT, TANH, SIGMOID, RELU, SQUARE, FILL, POWS, ABS, FINITE_OR_ZERO,
+ LOG1P) = range(13)
 
 _STATUS_ERRORS: dict[int, type[Exception]] = {
     1: ValueError,
@@ -108,6 +109,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tg_colsum_scratch_bytes": (sz, [c_int, i64, i64]),
     "tg_colsum": (c_int, [c_int, vp, vp, i64, i64, c_int, vp, vp]),
     "tg_reduce_sum": (c_int, [c_int, c_int, pi64, pint, vp, vp, vp]),
+    "tg_reduce_extremum": (c_int, [c_int, c_int, c_int, pi64, pint, vp, vp, vp]),
+    "tg_reduce_truth": (c_int, [c_int, c_int, c_int, pi64, pint, vp, vp, vp]),
+    "tg_argmax": (c_int, [c_int, c_int, pi64, pint, vp, vp, vp]),
+    "tg_compare": (c_int, [c_int, c_int, c_int, pi64, vp, pi64, vp, pi64, vp, vp]),
+    "tg_where": (c_int, [c_int, c_int, c_int, pi64, vp, pi64, vp, pi64, vp, pi64, vp, vp]),
     "tg_sum_all_scratch_bytes": (sz, []),
     "tg_sum_all": (c_int, [c_int, vp, vp, i64, vp, vp]),
     "tg_binary": (c_int, [c_int, c_int, c_int, pi64, vp, pi64, vp, pi64, vp, vp]),
@@ -171,6 +177,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tg_gru_forward": (c_int, [c_int, i64, i64, i64, i64] + [vp] * 11),
     "tg_gru_backward_scratch_bytes": (sz, [c_int, i64, i64, i64, i64]),
     "tg_gru_backward": (c_int, [c_int, i64, i64, i64, i64] + [vp] * 16),
+    "tg_rnn_forward_scratch_bytes": (sz, [c_int, i64, i64, i64, i64]),
+    "tg_rnn_forward": (c_int, [c_int, c_int, i64, i64, i64, i64] + [vp] * 9),
+    "tg_rnn_backward_scratch_bytes": (sz, [c_int, i64, i64, i64, i64]),
+    "tg_rnn_backward": (c_int, [c_int, c_int, i64, i64, i64, i64] + [vp] * 14),
     "tg_sumsq_scratch_bytes": (sz, [c_int]),
     "tg_sumsq_multi": (c_int, [c_int, c_int, pvp, pi64, vp, vp, vp]),
     "tg_clip_scale_multi": (c_int, [c_int, c_int, pvp, pi64, vp, dbl, dbl, vp, vp]),

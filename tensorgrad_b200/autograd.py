@@ -31,7 +31,8 @@ if TYPE_CHECKING:
     from tensorgrad_b200.device import DeviceArray
     from tensorgrad_b200.tensor import Tensor
 
-__all__ = ["BackwardFn", "Node", "backward", "enable_grad", "grad", "is_grad_enabled", "no_grad"]
+__all__ = ["BackwardFn", "GradOutputs", "Node", "backward", "enable_grad", "grad", "is_grad_enabled",
+           "no_grad"]
 
 #: VJP of one op on device arrays: given d(loss)/d(output) and, per input, whether its
 #: gradient is needed, return d(loss)/d(input_i) (``None`` where not needed).
@@ -217,7 +218,8 @@ def _run_backward(
     prof = _profiler.active()
     if prof is None:
         return _backward_pass(roots, seeds, retain_graph, targets, None)
-    return prof.timed(_profiler.ENGINE, _backward_pass, roots, seeds, retain_graph, targets, prof)
+    return prof.timed(_profiler.ENGINE, True, _backward_pass, roots, seeds, retain_graph, targets,
+                      prof)
 
 
 def _backward_pass(
@@ -264,7 +266,7 @@ def _backward_pass(
         if prof is None:
             grads = fn(g, need)
         else:
-            grads = prof.timed(node.op, fn, g, need)
+            grads = prof.timed(node.op, True, fn, g, need)
         if len(grads) != len(parents):
             raise RuntimeError(
                 f"op '{node.op}' returned {len(grads)} gradients for {len(parents)} inputs"

@@ -20,6 +20,7 @@ __device__ __forceinline__ T apply_binary(int op, T x, T y) {
     case TG_SUB: return x - y;
     case TG_MUL: return x * y;
     case TG_DIV: return x / y;
+    case TG_EQ: return x == y ? T(1) : T(0);
     default: return pow(x, y);
   }
 }
@@ -101,6 +102,10 @@ __device__ __forceinline__ T apply_unary(int op, T x, T a) {
     case TG_RELU: return x > T(0) ? x : T(0);
     case TG_SQUARE: return x * x;
     case TG_FILL: return a;
+    case TG_ABS: return fabs(x);
+    case TG_FINITE_OR_ZERO: return isfinite(x) ? x : T(0);
+    case TG_LOG1P: return log1p(x);
+    case TG_POWS: return pow(x, a);
     default: return pow(x, a);
   }
 }
@@ -219,7 +224,7 @@ int tg_binary(int dtype, int op, int ndim, const int64_t* shape, const void* a,
               const int64_t* a_strides, const void* b, const int64_t* b_strides, void* out,
               void* stream) {
   TG_CHECK_ARG(ndim >= 0 && ndim <= kMaxDims, "binary: ndim %d out of range", ndim);
-  TG_CHECK_ARG(op >= TG_ADD && op <= TG_POW, "binary: bad op %d", op);
+  TG_CHECK_ARG(op >= TG_ADD && op <= TG_EQ, "binary: bad op %d", op);
   int64_t n = 1;
   for (int i = 0; i < ndim; ++i) n *= shape[i];
   if (n == 0) return TG_OK;
@@ -254,6 +259,7 @@ int tg_binary(int dtype, int op, int ndim, const int64_t* shape, const void* a,
         case TG_SUB: binary_contig_kernel<T, TG_SUB><<<grid, 256, 0, s>>>((const T*)a, (const T*)b, (T*)out, n, am, bm); break;
         case TG_MUL: binary_contig_kernel<T, TG_MUL><<<grid, 256, 0, s>>>((const T*)a, (const T*)b, (T*)out, n, am, bm); break;
         case TG_DIV: binary_contig_kernel<T, TG_DIV><<<grid, 256, 0, s>>>((const T*)a, (const T*)b, (T*)out, n, am, bm); break;
+        case TG_EQ: binary_contig_kernel<T, TG_EQ><<<grid, 256, 0, s>>>((const T*)a, (const T*)b, (T*)out, n, am, bm); break;
         default: binary_contig_kernel<T, TG_POW><<<grid, 256, 0, s>>>((const T*)a, (const T*)b, (T*)out, n, am, bm); break;
       }
     } else {
@@ -291,7 +297,7 @@ int tg_scale_by_device_scalar(int dtype, int64_t n, const void* x, const void* s
 }
 
 int tg_unary(int dtype, int op, int64_t n, const void* x, double alpha, void* out, void* stream) {
-  TG_CHECK_ARG(op >= TG_NEG && op <= TG_POWS, "unary: bad op %d", op);
+  TG_CHECK_ARG(op >= TG_NEG && op <= TG_LOG1P, "unary: bad op %d", op);
   if (n <= 0) return TG_OK;
   return TG_DISPATCH_FLOAT(dtype, T, [&] {
     launch_pdl(unary_kernel<T>, dim3(grid_for(n, 256)), dim3(256), 0, as_stream(stream),

@@ -1,4 +1,5 @@
-// LSTM and GRU over a whole sequence with backpropagation through time (ops/recurrent.py).
+// Elman RNN, LSTM and GRU over a whole sequence with backpropagation through time
+// (ops/recurrent.py).
 //
 // One C-ABI call runs a whole sequence, so the host loop over time steps is C++, not Python:
 //   forward : the input projection of every step as one GEMM (bias in its epilogue), then per
@@ -165,6 +166,36 @@ gru_cell_bwd(const T* __restrict__ gates, const T* __restrict__ hn_t,
     dr_[H + j] = du;
     dr_[2 * H + j] = dn * r;
     dh_buf[idx] = dh * u;
+  }
+}
+
+// ------------------------------------------------------------------ Elman cells
+// z (B, H) holds x W_ih^T + b_ih and becomes the state act(z + h W_hh^T + b_hh).
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+rnn_cell_fwd(T* __restrict__ z, const T* __restrict__ rec, int64_t n, int relu) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const T v = z[idx] + rec[idx];
+    z[idx] = relu ? (v > T(0) ? v : T(0)) : dev_tanh<T>(v);
+  }
+}
+
+// One reverse step: dh = g_t (+ the carry dz_{t+1} W_hh), dz_t = dh act'(h_t) with
+// act' = 1 - h^2 (tanh) or [h > 0] (relu).
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+rnn_cell_bwd(const T* __restrict__ h_t, const T* __restrict__ g_t, const T* __restrict__ carry,
+             T* __restrict__ dz_t, int64_t n, int relu, int first) {
+  pdl_trigger();  // launched with launch_pdl: no global access before the wait
+  pdl_wait();
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const T dh = first ? g_t[idx] : carry[idx] + g_t[idx];
+    const T h = h_t[idx];
+    dz_t[idx] = relu ? (h > T(0) ? dh : T(0)) : dh * (T(1) - h * h);
   }
 }
 
@@ -464,6 +495,87 @@ int tg_gru_backward(int dtype, int64_t T_, int64_t B, int64_t I, int64_t H, cons
       TG_CUDA_TRY(cudaMemcpyAsync(dh0, dh, (size_t)(B * H) * sizeof(T), cudaMemcpyDeviceToDevice, st));
     }
     return rnn_weight_grads<T>(T_, B, I, H, 3, dz_ih, dz_hh, (const T*)x, (const T*)h0, o, H,
+                               (const T*)w_ih, (T*)dx, (T*)dw_ih, (T*)dw_hh, (T*)db_ih,
+                               (T*)db_hh, L, base, st);
+  });
+}
+
+size_t tg_rnn_forward_scratch_bytes(int dtype, int64_t T_, int64_t B, int64_t I, int64_t H) {
+  (void)T_; (void)I;
+  const size_t es = dtype == TG_F64 ? 8 : 4;
+  return align256((size_t)(B * H) * es) + fwd_ws_bytes(dtype);
+}
+
+int tg_rnn_forward(int dtype, int relu, int64_t T_, int64_t B, int64_t I, int64_t H,
+                   const void* x, const void* h0, const void* w_ih, const void* w_hh,
+                   const void* b_ih, const void* b_hh, void* out, void* scratch, void* stream) {
+  int rc = check_rnn(T_, B, I, H);
+  if (rc) return rc;
+  TG_CHECK_ARG((b_ih == nullptr) == (b_hh == nullptr), "rnn: pass both biases or neither");
+  TG_CHECK_ARG(scratch, "rnn: scratch required");
+  cudaStream_t st = as_stream(stream);
+  return TG_DISPATCH_FLOAT(dtype, T, [&] {
+    T* hw = reinterpret_cast<T*>(scratch);
+    T* o = (T*)out;
+    int r;
+    auto proj = gemm_args<T>(0, 1, T_ * B, H, I, (const T*)x, I, (const T*)w_ih, I, o, H,
+                             (const T*)b_ih, T(0));
+    if ((r = gemm_run<T>(proj, st))) return r;
+    for (int64_t t = 0; t < T_; ++t) {
+      const T* h_prev = t == 0 ? (const T*)h0 : o + (t - 1) * B * H;
+      auto rec = gemm_args<T>(0, 1, B, H, H, h_prev, H, (const T*)w_hh, H, hw, H,
+                              (const T*)b_hh, T(0));
+      if (fwd_ws_bytes(dtype)) {
+        rec.workspace = reinterpret_cast<float*>(
+            (uint8_t*)scratch + fwd_ws_offset(dtype, align256((size_t)(B * H) * sizeof(T))));
+        rec.workspace_bytes = fwd_ws_bytes(dtype);
+      }
+      if ((r = gemm_run<T>(rec, st))) return r;
+      launch_pdl(rnn_cell_fwd<T>, dim3(grid_for(B * H, kThreads)), dim3(kThreads), 0, st,
+                 o + t * B * H, (const T*)hw, B * H, relu);
+      if ((r = check_launch("rnn(cell)"))) return r;
+    }
+    return (int)TG_OK;
+  });
+}
+
+size_t tg_rnn_backward_scratch_bytes(int dtype, int64_t T_, int64_t B, int64_t I, int64_t H) {
+  return rnn_bwd_layout(dtype, T_, B, I, H, 1, false).total;
+}
+
+int tg_rnn_backward(int dtype, int relu, int64_t T_, int64_t B, int64_t I, int64_t H,
+                    const void* g, const void* x, const void* h0, const void* w_ih,
+                    const void* w_hh, const void* out, void* dx, void* dh0, void* dw_ih,
+                    void* dw_hh, void* db_ih, void* db_hh, void* scratch, void* stream) {
+  int rc = check_rnn(T_, B, I, H);
+  if (rc) return rc;
+  TG_CHECK_ARG(scratch && g, "rnn backward: scratch and g required");
+  cudaStream_t st = as_stream(stream);
+  const RnnBwdLayout L = rnn_bwd_layout(dtype, T_, B, I, H, 1, false);
+  uint8_t* base = (uint8_t*)scratch;
+  return TG_DISPATCH_FLOAT(dtype, T, [&] {
+    T* dz = reinterpret_cast<T*>(base);
+    T* carry = reinterpret_cast<T*>(base + L.dz + L.dz2);
+    float* ws = reinterpret_cast<float*>(base + L.total - L.ws);
+    const T* o = (const T*)out;
+    int r;
+    for (int64_t t = T_ - 1; t >= 0; --t) {
+      launch_pdl(rnn_cell_bwd<T>, dim3(grid_for(B * H, kThreads)), dim3(kThreads), 0, st,
+                 o + t * B * H, (const T*)g + t * B * H, (const T*)carry, dz + t * B * H,
+                 B * H, relu, t == T_ - 1);
+      if ((r = check_launch("rnn backward(cell)"))) return r;
+      if (t > 0 || dh0) {
+        auto q = gemm_args<T>(0, 0, B, H, H, dz + t * B * H, H, (const T*)w_hh, H, carry, H,
+                              nullptr, T(0));
+        if (L.ws) { q.workspace = ws; q.workspace_bytes = L.ws; }
+        if ((r = gemm_run<T>(q, st))) return r;
+      }
+    }
+    if (dh0) {
+      TG_CUDA_TRY(cudaMemcpyAsync(dh0, carry, (size_t)(B * H) * sizeof(T),
+                                  cudaMemcpyDeviceToDevice, st));
+    }
+    return rnn_weight_grads<T>(T_, B, I, H, 1, dz, dz, (const T*)x, (const T*)h0, o, H,
                                (const T*)w_ih, (T*)dx, (T*)dw_ih, (T*)dw_hh, (T*)db_ih,
                                (T*)db_hh, L, base, st);
   });

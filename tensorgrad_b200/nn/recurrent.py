@@ -1,7 +1,7 @@
-"""Stacked LSTM and GRU layers on the device (API of the reference's nn/recurrent.py:24-205,
-PyTorch's parameter names and call signatures).
+"""Stacked Elman RNN, LSTM and GRU layers on the device (API of the reference's
+nn/recurrent.py:24-205, PyTorch's parameter names and call signatures).
 
-Each layer of the stack is one fused sequence op (``ops.recurrent.lstm`` / ``gru``: the input
+Each layer of the stack is one fused sequence op (``ops.recurrent.rnn`` / ``lstm`` / ``gru``: the input
 projection for all steps, then the recurrence, and backpropagation through time, inside one
 C call). Layers take the previous layer's hidden sequence (with dropout between layers in
 training); the final states are the last step of each layer.
@@ -16,11 +16,11 @@ import numpy as np
 from tensorgrad_b200 import ops
 from tensorgrad_b200._random import get_rng
 from tensorgrad_b200.nn.module import Module, Parameter
-from tensorgrad_b200.ops.recurrent import gru, lstm
+from tensorgrad_b200.ops.recurrent import gru, lstm, rnn
 from tensorgrad_b200.ops.shape import stack
 from tensorgrad_b200.tensor import Tensor, get_default_dtype
 
-__all__ = ["GRU", "LSTM"]
+__all__ = ["GRU", "LSTM", "RNN"]
 
 
 class _RecurrentStack(Module):
@@ -131,3 +131,35 @@ class GRU(_RecurrentStack):
 
     def __call__(self, x: Tensor, h0: Tensor | None = None) -> tuple[Tensor, Tensor]:  # type: ignore[override]
         return self.forward(x, h0)
+
+
+class RNN(_RecurrentStack):
+    """Multi-layer Elman RNN, ``h_t = act(x_t W_ih^T + b_ih + h_{t-1} W_hh^T + b_hh)`` with
+    ``act`` tanh or relu: ``output, h_n = rnn(x, h_0)``."""
+
+    gates = 1
+
+    def __init__(self, input_size: int, hidden_size: int, num_layers: int = 1,
+                 nonlinearity: str = "tanh", bias: bool = True, batch_first: bool = False,
+                 dropout: float = 0.0) -> None:
+        if nonlinearity not in ("tanh", "relu"):
+            raise ValueError(f"nonlinearity must be 'tanh' or 'relu', got {nonlinearity!r}")
+        super().__init__(input_size, hidden_size, num_layers, bias, batch_first, dropout)
+        self.nonlinearity = nonlinearity
+
+    def forward(self, x: Tensor, h0: Tensor | None = None) -> tuple[Tensor, Tensor]:  # type: ignore[override]
+        seq = self._sequence(x)
+        state = self._state(h0, seq.shape[1], seq.dtype)
+        last = []
+        hs = seq
+        for k in range(self.num_layers):
+            hs = rnn(seq, state[k], *self.layer_weights(k), nonlinearity=self.nonlinearity)
+            last.append(hs[-1])
+            seq = self._between_layers(hs, k)
+        return self._result(hs), stack(last, 0)
+
+    def __call__(self, x: Tensor, h0: Tensor | None = None) -> tuple[Tensor, Tensor]:  # type: ignore[override]
+        return self.forward(x, h0)
+
+    def extra_repr(self) -> str:
+        return super().extra_repr() + f", nonlinearity={self.nonlinearity!r}"

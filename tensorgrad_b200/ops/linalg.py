@@ -33,36 +33,51 @@ def _bmm(a: DeviceArray, b: DeviceArray, ta: int, tb: int, m: int, n: int, k: in
 
 @profiled("matmul")
 def matmul(a: Any, b: Any) -> Tensor:
-    """``a @ b`` for operands with at least two axes; leading axes broadcast."""
+    """``a @ b`` with NumPy's rules (ops/linalg.py:16-63): leading axes broadcast; a 1-D
+    ``a`` is a row and a 1-D ``b`` a column, whose axis is dropped from the result (two
+    vectors give their dot product)."""
     ta, tb = coerce_pair(a, b)
-    if ta.ndim < 2 or tb.ndim < 2:
-        raise NotImplementedError("matmul on device tensors needs operands with >= 2 axes")
+    if ta.ndim == 0 or tb.ndim == 0:
+        raise ValueError("matmul: both operands need at least one axis")
     dt = np.result_type(ta.dtype, tb.dtype)
     ad = ta.data if ta.dtype == dt else cast_array(ta.data, dt)
     bd = tb.data if tb.dtype == dt else cast_array(tb.data, dt)
-    m, k = ta.shape[-2:]
-    k2, n = tb.shape[-2:]
+    a_vec, b_vec = ta.ndim == 1, tb.ndim == 1
+    a2 = ad.reshape((1, ad.shape[0])) if a_vec else ad
+    b2 = bd.reshape((bd.shape[0], 1)) if b_vec else bd
+    m, k = a2.shape[-2:]
+    k2, n = b2.shape[-2:]
     if k != k2:
         raise ValueError(f"matmul: shapes {ta.shape} and {tb.shape} are not aligned")
-    batch = tuple(np.broadcast_shapes(ta.shape[:-2], tb.shape[:-2]))
+    batch = tuple(np.broadcast_shapes(a2.shape[:-2], b2.shape[:-2]))
     nb = math.prod(batch)
-    af = broadcast_array(ad, (*batch, m, k))
-    bf = broadcast_array(bd, (*batch, k, n))
-    out = _bmm(af, bf, 0, 0, m, n, k, nb).reshape((*batch, m, n))
+    af = broadcast_array(a2, (*batch, m, k))
+    bf = broadcast_array(b2, (*batch, k, n))
+    full = (*batch, m, n)
+    shape = (*batch, *(() if a_vec else (m,)), *(() if b_vec else (n,)))
+    out = _bmm(af, bf, 0, 0, m, n, k, nb).reshape(shape)
 
     def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray | None, DeviceArray | None]:
+        g = g.reshape(full)
         ga = gb = None
         if need[0]:  # g @ b^T
-            ga = unbroadcast(_bmm(g, bf, 0, 1, m, k, n, nb).reshape((*batch, m, k)), ta.shape)
+            ga = unbroadcast(_bmm(g, bf, 0, 1, m, k, n, nb).reshape((*batch, m, k)), a2.shape)
+            ga = ga.reshape(ta.shape)
         if need[1]:  # a^T @ g
-            gb = unbroadcast(_bmm(af, g, 1, 0, k, n, m, nb).reshape((*batch, k, n)), tb.shape)
+            gb = unbroadcast(_bmm(af, g, 1, 0, k, n, m, nb).reshape((*batch, k, n)), b2.shape)
+            gb = gb.reshape(tb.shape)
         return ga, gb
 
     def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor | None, Tensor | None]:
-        from tensorgrad_b200.ops.shape import sum_to, transpose
+        from tensorgrad_b200.ops.shape import reshape, sum_to, transpose
 
-        ga = sum_to(matmul(g, transpose(tb, -1, -2)), ta.shape) if need[0] else None
-        gb = sum_to(matmul(transpose(ta, -1, -2), g), tb.shape) if need[1] else None
+        g2 = reshape(g, full)
+        ra = reshape(ta, a2.shape) if a_vec else ta
+        rb = reshape(tb, b2.shape) if b_vec else tb
+        ga = reshape(sum_to(matmul(g2, transpose(rb, -1, -2)), a2.shape), ta.shape) \
+            if need[0] else None
+        gb = reshape(sum_to(matmul(transpose(ra, -1, -2), g2), b2.shape), tb.shape) \
+            if need[1] else None
         return ga, gb
 
     return make_result(out, (ta, tb), backward, "matmul", graph)

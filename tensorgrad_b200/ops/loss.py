@@ -15,7 +15,7 @@ from tensorgrad_b200.ops.elementwise import cast_array
 from tensorgrad_b200.profiler import profiled
 from tensorgrad_b200.tensor import Tensor
 
-__all__ = ["Reduction", "cross_entropy", "mse_loss"]
+__all__ = ["Reduction", "binary_cross_entropy_with_logits", "cross_entropy", "mse_loss"]
 
 Reduction = Literal["mean", "sum", "none"]
 _RED = {"mean": 0, "sum": 1, "none": 2}
@@ -127,3 +127,57 @@ def mse_loss(prediction: Any, target: Any, *, reduction: Reduction = "mean") -> 
     if reduction == "none":
         return sq
     raise ValueError(f"unknown reduction {reduction!r}")
+
+
+@profiled("binary_cross_entropy")
+def binary_cross_entropy_with_logits(logits: Any, target: Any, *,
+                                     reduction: Reduction = "mean") -> Tensor:
+    """Binary cross entropy of ``sigmoid(logits)`` against ``target`` in [0, 1]
+    (ops/loss.py:100-145): ``max(z, 0) - z y + log1p(exp(-|z|))`` on the device, so nothing
+    overflows; the gradient is ``sigmoid(z) - y`` for the logits and ``-z`` for the targets."""
+    from tensorgrad_b200._lib import ABS, ADD, EXP, LOG1P, MUL, NEG, RELU, SIGMOID, SUB
+    from tensorgrad_b200.ops.elementwise import _unary, binary_array, scale_array
+
+    tz, ty = coerce_pair(logits, target)
+    if tz.shape != ty.shape:
+        raise ValueError(f"logits {tz.shape} and target {ty.shape} must have the same shape")
+    if reduction not in ("mean", "sum", "none"):
+        raise ValueError(f"unknown reduction {reduction!r}")
+    dt = np.result_type(tz.dtype, ty.dtype)
+    if dt.kind != "f":
+        dt = np.dtype(np.float64)
+    z = tz.data if tz.dtype == dt else cast_array(tz.data, dt)
+    y = ty.data if ty.dtype == dt else cast_array(ty.data, dt)
+    softplus_tail = _unary(_unary(_unary(_unary(z, ABS), NEG), EXP), LOG1P)
+    losses = binary_array(binary_array(_unary(z, RELU), binary_array(z, y, MUL), SUB),
+                          softplus_tail, ADD)
+    n = max(losses.size, 1)
+    if reduction == "none":
+        out = losses
+    else:
+        total = reduce.sum_array(losses, tuple(range(losses.ndim))).reshape(())
+        out = scale_array(total, 1.0 / n) if reduction == "mean" else total
+    scale = 1.0 / n if reduction == "mean" else 1.0
+
+    def upstream_array(g: DeviceArray) -> DeviceArray:
+        if reduction == "none":
+            return g
+        from tensorgrad_b200.ops.shape import broadcast_array
+
+        return broadcast_array(scale_array(g, scale), z.shape)
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray | None, DeviceArray | None]:
+        up = upstream_array(g)
+        return (binary_array(binary_array(_unary(z, SIGMOID), y, SUB), up, MUL)
+                if need[0] else None,
+                binary_array(_unary(z, NEG), up, MUL) if need[1] else None)
+
+    def graph(g: Tensor, y_: Tensor, need: Need) -> tuple[Tensor | None, Tensor | None]:
+        from tensorgrad_b200.ops.elementwise import sigmoid
+        from tensorgrad_b200.ops.shape import broadcast_to
+
+        up = g if reduction == "none" else broadcast_to(g * scale, tz.shape)
+        return ((sigmoid(tz) - ty) * up if need[0] else None,
+                -tz * up if need[1] else None)
+
+    return make_result(out, (tz, ty), backward, "binary_cross_entropy", graph)

@@ -27,9 +27,9 @@ from tensorgrad_b200.ops.elementwise import cast_array
 from tensorgrad_b200.profiler import profiled
 from tensorgrad_b200.tensor import Tensor
 
-__all__ = ["gru", "lstm"]
+__all__ = ["gru", "lstm", "rnn"]
 
-_GATES = {"lstm": 4, "gru": 3}
+_GATES = {"rnn": 1, "lstm": 4, "gru": 3}
 
 
 def _prepare(kind: str, x: Any, states: Sequence[Any], w_ih: Any, w_hh: Any, b_ih: Any,
@@ -206,3 +206,70 @@ def gru(x: Any, h0: Any, w_ih: Any, w_hh: Any, b_ih: Any = None, b_hh: Any = Non
         return graph_by_composite(parents, _gru_composite, g, need)
 
     return make_result(out, parents, backward, "gru", graph)
+
+
+def _rnn_composite(x: Tensor, h0: Tensor, w_ih: Tensor, w_hh: Tensor,
+                   b_ih: Tensor | None = None, b_hh: Tensor | None = None, *,
+                   relu: bool = False) -> Tensor:
+    """The Elman recurrence in differentiable ops, ``(T, B, H)`` like :func:`rnn`."""
+    from tensorgrad_b200.ops import elementwise as E
+    from tensorgrad_b200.ops.layers import linear
+    from tensorgrad_b200.ops.shape import getitem, stack
+
+    xw = linear(x, w_ih, b_ih)
+    h = h0
+    steps = []
+    for t in range(x.shape[0]):
+        pre = E.add(getitem(xw, t), linear(h, w_hh, b_hh))
+        h = E.relu(pre) if relu else E.tanh(pre)
+        steps.append(h)
+    return stack(steps, 0)
+
+
+@profiled("rnn")
+def rnn(x: Any, h0: Any, w_ih: Any, w_hh: Any, b_ih: Any = None, b_hh: Any = None, *,
+        nonlinearity: str = "tanh") -> Tensor:
+    """Elman RNN ``h_t = act(x_t W_ih^T + b_ih + h_{t-1} W_hh^T + b_hh)`` over a
+    ``(T, B, input_size)`` sequence, ``act`` tanh or relu (ops/recurrent.py:140-219); returns
+    ``h_1 .. h_T``, ``(T, B, H)``."""
+    if nonlinearity not in ("tanh", "relu"):
+        raise ValueError(f"nonlinearity must be 'tanh' or 'relu', got {nonlinearity!r}")
+    relu = int(nonlinearity == "relu")
+    parents, arrays = _prepare("rnn", x, (h0,), w_ih, w_hh, b_ih, b_hh)
+    xd, h0d, w_ihd, w_hhd = arrays[:4]
+    bias = arrays[4:] if len(arrays) > 4 else [None, None]
+    steps, batch, width = xd.shape
+    hid = h0d.shape[1]
+    dt = xd.dtype
+    code = dtype_code(dt)
+    out = device.empty((steps, batch, hid), dt)
+    scratch = device.scratch(lib.tg_rnn_forward_scratch_bytes(code, steps, batch, width, hid))
+    check(lib.tg_rnn_forward(code, relu, steps, batch, width, hid, xd.ptr, h0d.ptr, w_ihd.ptr,
+                             w_hhd.ptr, _ptr(bias[0]), _ptr(bias[1]), out.ptr, scratch.ptr,
+                             device.stream()), "rnn")
+    has_bias = len(arrays) > 4
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray | None, ...]:
+        if g.dtype != dt:
+            g = cast_array(g, dt)
+
+        def want(k: int, shape: tuple[int, ...]) -> DeviceArray | None:
+            return device.empty(shape, dt) if need[k] else None
+
+        dx, dh0 = want(0, xd.shape), want(1, h0d.shape)
+        dw_ih, dw_hh = want(2, w_ihd.shape), want(3, w_hhd.shape)
+        db_ih = want(4, (hid,)) if has_bias else None
+        db_hh = want(5, (hid,)) if has_bias else None
+        scr = device.scratch(lib.tg_rnn_backward_scratch_bytes(code, steps, batch, width, hid))
+        check(lib.tg_rnn_backward(
+            code, relu, steps, batch, width, hid, g.ptr, xd.ptr, h0d.ptr, w_ihd.ptr,
+            w_hhd.ptr, out.ptr, _ptr(dx), _ptr(dh0), _ptr(dw_ih), _ptr(dw_hh), _ptr(db_ih),
+            _ptr(db_hh), scr.ptr, device.stream()), "rnn backward")
+        grads = [dx, dh0, dw_ih, dw_hh]
+        return tuple(grads + [db_ih, db_hh] if has_bias else grads)
+
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor | None, ...]:
+        return graph_by_composite(
+            parents, lambda *ps: _rnn_composite(*ps, relu=bool(relu)), g, need)
+
+    return make_result(out, parents, backward, "rnn", graph)

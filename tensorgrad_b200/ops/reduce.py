@@ -6,6 +6,8 @@ import builtins
 import math
 from typing import Any
 
+import numpy as np
+
 from tensorgrad_b200 import device
 from tensorgrad_b200._lib import MUL, SUB, check, int64_array, int_array, lib
 from tensorgrad_b200.device import DeviceArray, dtype_code
@@ -119,9 +121,53 @@ def var(a: Any, axis: Any = None, keepdims: bool = False, correction: int = 1) -
     return make_result(out, (ta,), backward, "var", graph)
 
 
+def extremum_array(x: DeviceArray, axes: tuple[int, ...], is_min: bool) -> DeviceArray:
+    """Max (or min) over ``axes``, NaN-propagating; the result keeps the reduced axes."""
+    out = device.empty(_kept_shape(x.shape, axes), x.dtype)
+    keep = [0 if i in axes else 1 for i in range(x.ndim)]
+    check(lib.tg_reduce_extremum(dtype_code(x.dtype), int(is_min), x.ndim,
+                                 int64_array(x.shape), int_array(keep), x.ptr, out.ptr,
+                                 device.stream()), "min" if is_min else "max")
+    return out
+
+
+def _extremum(a: Any, axis: Any, keepdims: bool, is_min: bool, op: str) -> Tensor:
+    """Max / min over ``axis`` (ops/reduce.py:70-105): tied extrema share the gradient
+    equally, a valid subgradient; the share is a constant mask under ``create_graph``."""
+    from tensorgrad_b200._lib import DIV, EQ
+    from tensorgrad_b200.ops.elementwise import cast_array
+
+    ta = as_tensor(a)
+    axes = normalize_axes(axis, ta.ndim)
+    xd = ta.data if ta.dtype.kind == "f" else cast_array(ta.data, np.dtype(np.float64))
+    kept = extremum_array(xd, axes, is_min)
+    out = _drop(kept, axes, keepdims)
+    if ta.dtype.kind != "f":
+        out = cast_array(out, ta.dtype)
+
+    def share() -> DeviceArray:
+        winners = binary_array(xd, kept, EQ)
+        return binary_array(winners, sum_array(winners, axes), DIV)
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+        return (binary_array(expand_array(g, ta.shape, axes), share(), MUL),)
+
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
+        from tensorgrad_b200.ops._util import constant
+        from tensorgrad_b200.ops.elementwise import mul
+
+        return (mul(_expand(g, ta.shape, axes), constant(share())),)
+
+    return make_result(out, (ta,), backward, op, graph)
+
+
+@profiled("max")
 def max(a: Any, axis: Any = None, keepdims: bool = False) -> Tensor:  # noqa: A001
-    raise NotImplementedError("max is not on the device training path")
+    """Maximum over ``axis``; tied maxima share the gradient equally."""
+    return _extremum(a, axis, keepdims, False, "max")
 
 
+@profiled("min")
 def min(a: Any, axis: Any = None, keepdims: bool = False) -> Tensor:  # noqa: A001
-    raise NotImplementedError("min is not on the device training path")
+    """Minimum over ``axis``; tied minima share the gradient equally."""
+    return _extremum(a, axis, keepdims, True, "min")

@@ -15,8 +15,8 @@ from tensorgrad_b200.ops._util import Need, as_tensor, make_result, normalize_ax
 from tensorgrad_b200.profiler import profiled
 from tensorgrad_b200.tensor import Tensor
 
-__all__ = ["broadcast_to", "flatten", "getitem", "permute", "reshape", "squeeze", "stack", "sum_to",
-           "transpose", "unsqueeze"]
+__all__ = ["broadcast_to", "concat", "flatten", "getitem", "masked_fill", "permute", "reshape",
+           "squeeze", "stack", "sum_to", "transpose", "unsqueeze", "where"]
 
 
 def strided_copy(src_ptr: int, src_strides: list[int], dst_ptr: int, dst_strides: list[int],
@@ -245,3 +245,132 @@ def stack(tensors: Any, axis: int = 0) -> Tensor:
         return tuple(getitem(g, (*lead, k)) if need[k] else None for k in range(len(ts)))
 
     return make_result(out, tuple(ts), backward, "stack", graph)
+
+
+@profiled("concat")
+def concat(tensors: Any, axis: int = 0) -> Tensor:
+    """Join tensors along an existing axis (ops/shape.py:243-262): one strided copy per input
+    into its slab of the output; the VJP hands each input its slab of the gradient."""
+    ts = [as_tensor(t) for t in tensors]
+    if not ts:
+        raise ValueError("concat needs at least one tensor")
+    ax = normalize_axis(axis, ts[0].ndim)
+    rest = ts[0].shape[:ax] + ts[0].shape[ax + 1:]
+    for t in ts:
+        if t.ndim != ts[0].ndim or t.shape[:ax] + t.shape[ax + 1:] != rest:
+            raise ValueError(f"concat: shapes {[t.shape for t in ts]} differ off axis {ax}")
+    dt = np.result_type(*[t.dtype for t in ts])
+    sizes = [t.shape[ax] for t in ts]
+    starts = [0, *np.cumsum(sizes)[:-1].tolist()]
+    out_shape = (*ts[0].shape[:ax], int(sum(sizes)), *ts[0].shape[ax + 1:])
+    out = device.empty(out_shape, dt)
+    ostr = device.contiguous_strides(out_shape)
+    for t, start in zip(ts, starts, strict=True):
+        src = t.data if t.dtype == dt else t.data.astype(dt)
+        strided_copy(src.ptr, device.contiguous_strides(t.shape),
+                     out.ptr + start * ostr[ax] * out.itemsize, ostr, t.shape, out.itemsize)
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray | None, ...]:
+        grads: list[DeviceArray | None] = []
+        for t, start, wanted in zip(ts, starts, need, strict=True):
+            if not wanted:
+                grads.append(None)
+                continue
+            piece = device.empty(t.shape, g.dtype)
+            strided_copy(g.ptr + start * ostr[ax] * g.itemsize, ostr, piece.ptr,
+                         device.contiguous_strides(t.shape), t.shape, g.itemsize)
+            grads.append(piece)
+        return tuple(grads)
+
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor | None, ...]:
+        lead = (slice(None),) * ax
+        return tuple(getitem(g, (*lead, slice(start, start + t.shape[ax]))) if wanted else None
+                     for t, start, wanted in zip(ts, starts, need, strict=True))
+
+    return make_result(out, tuple(ts), backward, "concat", graph)
+
+
+_COND_CODES = {np.dtype(np.bool_): -1, np.dtype(np.float32): 0, np.dtype(np.float64): 1,
+               np.dtype(np.int64): 2}
+
+
+def _condition(mask: Any) -> DeviceArray:
+    """A condition on the device, read as ``!= 0``: a boolean, float or int64 device array
+    as it is, anything else (host arrays, bools) uploaded as one byte per element."""
+    data = mask.data if isinstance(mask, Tensor) else mask
+    if isinstance(data, DeviceArray) and data.dtype in _COND_CODES:
+        return data
+    if isinstance(data, DeviceArray):
+        data = data.numpy()
+    return device.from_numpy(np.asarray(data).astype(np.bool_, copy=False))
+
+
+def _bcast(shape: tuple[int, ...], out: tuple[int, ...]) -> list[int]:
+    strides = device.contiguous_strides(shape)
+    pad = len(out) - len(shape)
+    return [0] * pad + [0 if (n == 1 and out[pad + i] != 1) else strides[i]
+                        for i, n in enumerate(shape)]
+
+
+def where_array(cond: DeviceArray, a: DeviceArray, b: DeviceArray) -> DeviceArray:
+    """``cond ? a : b`` broadcast together; ``a`` and ``b`` share one floating dtype."""
+    from tensorgrad_b200.device import dtype_code
+
+    shape = tuple(np.broadcast_shapes(cond.shape, a.shape, b.shape))
+    out = device.empty(shape, a.dtype)
+    check(lib.tg_where(dtype_code(a.dtype), _COND_CODES[cond.dtype], len(shape),
+                       int64_array(shape), cond.ptr, int64_array(_bcast(cond.shape, shape)),
+                       a.ptr, int64_array(_bcast(a.shape, shape)), b.ptr,
+                       int64_array(_bcast(b.shape, shape)), out.ptr, device.stream()), "where")
+    return out
+
+
+@profiled("where")
+def where(condition: Any, a: Any, b: Any) -> Tensor:
+    """Elements of ``a`` where ``condition`` holds, of ``b`` elsewhere, all three broadcast
+    (ops/shape.py:290-309); the gradient goes to the branch that was picked."""
+    from tensorgrad_b200.ops._util import coerce_pair
+    from tensorgrad_b200.ops.elementwise import cast_array
+
+    cond = _condition(condition)
+    ta, tb = coerce_pair(a, b)
+    dt = np.result_type(ta.dtype, tb.dtype)
+    if dt.kind != "f":
+        dt = np.dtype(np.float64)
+    ad = ta.data if ta.dtype == dt else cast_array(ta.data, dt)
+    bd = tb.data if tb.dtype == dt else cast_array(tb.data, dt)
+    out = where_array(cond, ad, bd)
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray | None, DeviceArray | None]:
+        zero = device.scalar_like(0.0, g.dtype)
+        return (unbroadcast(where_array(cond, g, zero), ta.shape) if need[0] else None,
+                unbroadcast(where_array(cond, zero, g), tb.shape) if need[1] else None)
+
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor | None, Tensor | None]:
+        c = Tensor._wrap(cond)
+        return (sum_to(where(c, g, 0.0), ta.shape) if need[0] else None,
+                sum_to(where(c, 0.0, g), tb.shape) if need[1] else None)
+
+    return make_result(out, (ta, tb), backward, "where", graph)
+
+
+@profiled("masked_fill")
+def masked_fill(a: Any, mask: Any, value: float) -> Tensor:
+    """``a`` with ``value`` wherever ``mask`` (broadcastable to ``a``) holds
+    (ops/shape.py:312-328); filled positions get no gradient."""
+    from tensorgrad_b200.ops.elementwise import cast_array
+
+    ta = as_tensor(a)
+    cond = _condition(mask)
+    xd = ta.data if ta.dtype.kind == "f" else cast_array(ta.data, np.dtype(np.float64))
+    out = where_array(cond, device.scalar_like(value, xd.dtype), xd)
+    if out.shape != ta.shape:
+        raise ValueError(f"masked_fill: mask {cond.shape} does not broadcast to {ta.shape}")
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+        return (where_array(cond, device.scalar_like(0.0, g.dtype), g),)
+
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
+        return (masked_fill(g, Tensor._wrap(cond), 0.0),)
+
+    return make_result(out, (ta,), backward, "masked_fill", graph)

@@ -1,9 +1,16 @@
-"""Per-op timing (the reference's ``tensorgrad.profiler`` API, profiler.py:49-152).
+"""Per-op timing (the reference's ``tensorgrad.profiler`` API, profiler.py:25-152).
 
-Inside ``with profile() as prof:`` every public op and every VJP is timed; the device is
-synchronised around each timed call so a row's time is the device work it launched plus its
-host overhead. Self time excludes nested timed calls. ``prof.table()`` prints the summary.
-Timing synchronises the stream, so never profile a run whose throughput you report.
+    with tensorgrad_b200.profiler.profile() as prof:
+        loss = tg.cross_entropy(model(x), y)
+        loss.backward()
+    print(prof.table())
+
+Inside the block every public op and every VJP the backward pass runs is timed, and the
+device is synchronised around each timed call, so a row's time is the device work it
+launched plus its host overhead. Time of ops called by an op (a composite op, a graph VJP) is
+charged to those ops: every row is self time and the rows add up. The "autograd engine" row
+is the backward pass's own time outside VJPs. Timing synchronises the stream, so never
+profile a run whose throughput you report.
 """
 
 from __future__ import annotations
@@ -11,80 +18,125 @@ from __future__ import annotations
 import contextlib
 import functools
 import time
-from collections import defaultdict
 from collections.abc import Callable, Iterator
+from dataclasses import dataclass
 from typing import Any, TypeVar
 
+__all__ = ["ENGINE", "OpStats", "Profile", "profile", "profiled"]
+
+#: Name of the row that holds the backward engine's own time.
 ENGINE = "autograd engine"
 _R = TypeVar("_R")
 
 
-class Profile:
-    def __init__(self) -> None:
-        self.total: dict[tuple[str, bool], float] = defaultdict(float)
-        self.self_time: dict[tuple[str, bool], float] = defaultdict(float)
-        self.calls: dict[tuple[str, bool], int] = defaultdict(int)
-        self._child: list[float] = []
+@dataclass
+class OpStats:
+    """Call counts and self time (seconds) of one op."""
 
-    def timed(self, name: str, fn: Callable[..., _R], *args: Any, backward: bool = True) -> _R:
+    forward_calls: int = 0
+    forward_seconds: float = 0.0
+    backward_calls: int = 0
+    backward_seconds: float = 0.0
+
+    @property
+    def total_seconds(self) -> float:
+        """Forward plus backward self time."""
+        return self.forward_seconds + self.backward_seconds
+
+
+class Profile:
+    """Per-op timings collected by :func:`profile`, keyed by op name."""
+
+    def __init__(self) -> None:
+        self.ops: dict[str, OpStats] = {}
+        #: Wall-clock duration of the ``with`` block.
+        self.wall_seconds = 0.0
+        self._nested: list[float] = []  # time of timed calls inside each call in progress
+
+    def timed(self, name: str, backward: bool, fn: Callable[..., _R], *args: Any,
+              **kwargs: Any) -> _R:
+        """Run ``fn(*args, **kwargs)`` between two device synchronisations and charge its
+        self time to ``name``."""
         from tensorgrad_b200.device import synchronize
 
         synchronize()
-        self._child.append(0.0)
-        t0 = time.perf_counter()
+        self._nested.append(0.0)
+        start = time.perf_counter()
         try:
-            return fn(*args)
+            return fn(*args, **kwargs)
         finally:
             synchronize()
-            dt = time.perf_counter() - t0
-            child = self._child.pop()
-            key = (name, backward)
-            self.total[key] += dt
-            self.self_time[key] += dt - child
-            self.calls[key] += 1
-            if self._child:
-                self._child[-1] += dt
+            elapsed = time.perf_counter() - start
+            own = elapsed - self._nested.pop()
+            if self._nested:
+                self._nested[-1] += elapsed
+            stats = self.ops.setdefault(name, OpStats())
+            if backward:
+                stats.backward_calls += 1
+                stats.backward_seconds += own
+            else:
+                stats.forward_calls += 1
+                stats.forward_seconds += own
 
-    def table(self, limit: int = 20) -> str:
-        rows = sorted(self.self_time.items(), key=lambda kv: -kv[1])[:limit]
-        grand = sum(self.self_time.values()) or 1.0
-        lines = [f"{'op':<28}{'pass':<10}{'calls':>8}{'self ms':>12}{'share':>9}"]
-        for (name, bwd), t in rows:
-            lines.append(
-                f"{name:<28}{'backward' if bwd else 'forward':<10}"
-                f"{self.calls[(name, bwd)]:>8}{1e3 * t:>12.3f}{100 * t / grand:>8.1f}%"
-            )
+    @property
+    def profiled_seconds(self) -> float:
+        """Time inside ops and the engine (the sum of all rows)."""
+        return sum(s.total_seconds for s in self.ops.values())
+
+    def table(self, limit: int | None = None) -> str:
+        """Rows by total self time, as an aligned text table (milliseconds)."""
+        rows = sorted(self.ops.items(), key=lambda kv: kv[1].total_seconds, reverse=True)
+        total = self.profiled_seconds or 1.0
+        width = max([2, *(len(name) for name in self.ops)])
+        head = (f"{'op':<{width}}  {'fwd calls':>9}  {'fwd ms':>9}  {'bwd calls':>9}  "
+                f"{'bwd ms':>9}  {'total ms':>9}  {'share':>6}")
+        lines = [head, "-" * len(head)]
+        for name, s in rows[:limit]:
+            lines.append(f"{name:<{width}}  {s.forward_calls:>9}  {1e3 * s.forward_seconds:>9.2f}  "
+                         f"{s.backward_calls:>9}  {1e3 * s.backward_seconds:>9.2f}  "
+                         f"{1e3 * s.total_seconds:>9.2f}  {s.total_seconds / total:>6.1%}")
+        rest = self.wall_seconds - self.profiled_seconds
+        lines.append(f"ops and engine: {1e3 * self.profiled_seconds:.2f} ms of "
+                     f"{1e3 * self.wall_seconds:.2f} ms wall time ({1e3 * rest:.2f} ms elsewhere: "
+                     "Python code between ops, optimiser, data)")
         return "\n".join(lines)
 
 
-_active: list[Profile] = []
+class _Active:
+    profile: Profile | None = None
 
 
 def active() -> Profile | None:
-    return _active[-1] if _active else None
+    """The profile being collected, if a :func:`profile` block is open."""
+    return _Active.profile
 
 
 @contextlib.contextmanager
 def profile() -> Iterator[Profile]:
-    prof = Profile()
-    _active.append(prof)
+    """Collect per-op timings for the code inside the ``with`` block (blocks do not nest)."""
+    if _Active.profile is not None:
+        raise RuntimeError("profile() blocks cannot be nested")
+    result = Profile()
+    _Active.profile = result
+    start = time.perf_counter()
     try:
-        yield prof
+        yield result
     finally:
-        _active.pop()
+        result.wall_seconds = time.perf_counter() - start
+        _Active.profile = None
 
 
 def profiled(name: str) -> Callable[[Callable[..., _R]], Callable[..., _R]]:
-    """Decorator: time the forward call of a public op when a profile is active."""
+    """Decorator for op functions: time each call under ``name`` while profiling."""
 
-    def deco(fn: Callable[..., _R]) -> Callable[..., _R]:
+    def decorate(fn: Callable[..., _R]) -> Callable[..., _R]:
         @functools.wraps(fn)
         def wrapper(*args: Any, **kwargs: Any) -> _R:
-            prof = active()
+            prof = _Active.profile
             if prof is None:
                 return fn(*args, **kwargs)
-            return prof.timed(name, lambda: fn(*args, **kwargs), backward=False)
+            return prof.timed(name, False, fn, *args, **kwargs)
 
         return wrapper
 
-    return deco
+    return decorate

@@ -299,6 +299,9 @@ class Tensor:
     def __pow__(self, exponent: Any) -> Tensor:
         return _elementwise.pow(self, exponent)
 
+    def __rpow__(self, base: Any) -> Tensor:
+        return _elementwise.pow(base, self)
+
     def __neg__(self) -> Tensor:
         return _elementwise.neg(self)
 
@@ -313,27 +316,29 @@ class Tensor:
 
     __hash__ = object.__hash__
 
-    def _cmp(self, other: object, fn: Any) -> Tensor:
-        o = other.numpy() if isinstance(other, Tensor) else np.asarray(other)
-        return Tensor._wrap(_device.from_numpy(np.asarray(fn(self.numpy(), o))))
+    def _cmp(self, other: object, op: str) -> Tensor:
+        """An elementwise comparison on the device, as a boolean tensor (no graph)."""
+        from tensorgrad_b200.ops import compare as _compare
+
+        return _compare.compare(self, other, op)
 
     def __eq__(self, other: object) -> Tensor:  # type: ignore[override]
-        return self._cmp(other, operator.eq)
+        return self._cmp(other, "eq")
 
     def __ne__(self, other: object) -> Tensor:  # type: ignore[override]
-        return self._cmp(other, operator.ne)
+        return self._cmp(other, "ne")
 
     def __lt__(self, other: object) -> Tensor:
-        return self._cmp(other, operator.lt)
+        return self._cmp(other, "lt")
 
     def __le__(self, other: object) -> Tensor:
-        return self._cmp(other, operator.le)
+        return self._cmp(other, "le")
 
     def __gt__(self, other: object) -> Tensor:
-        return self._cmp(other, operator.gt)
+        return self._cmp(other, "gt")
 
     def __ge__(self, other: object) -> Tensor:
-        return self._cmp(other, operator.ge)
+        return self._cmp(other, "ge")
 
     # ------------------------------------------------------------------ op methods
     def matmul(self, other: Any) -> Tensor:
@@ -368,6 +373,48 @@ class Tensor:
 
     def var(self, axis: Any = None, keepdims: bool = False, correction: int = 1) -> Tensor:
         return _reduce.var(self, axis, keepdims, correction)
+
+    def max(self, axis: Any = None, keepdims: bool = False) -> Tensor:
+        """Maximum over ``axis``; tied maxima share the gradient equally."""
+        return _reduce.max(self, axis, keepdims)
+
+    def min(self, axis: Any = None, keepdims: bool = False) -> Tensor:
+        """Minimum over ``axis``; tied minima share the gradient equally."""
+        return _reduce.min(self, axis, keepdims)
+
+    def all(self, axis: Any = None, keepdims: bool = False) -> Tensor:
+        """Whether every element along ``axis`` is nonzero (a boolean tensor, no graph)."""
+        from tensorgrad_b200.ops import compare as _compare
+
+        return _compare.truth(self, axis, keepdims, True)
+
+    def any(self, axis: Any = None, keepdims: bool = False) -> Tensor:
+        """Whether some element along ``axis`` is nonzero (a boolean tensor, no graph)."""
+        from tensorgrad_b200.ops import compare as _compare
+
+        return _compare.truth(self, axis, keepdims, False)
+
+    def argmax(self, axis: int | None = None, keepdims: bool = False) -> Tensor:
+        """Indices of the first maxima along ``axis`` (int64, no graph)."""
+        from tensorgrad_b200.ops import compare as _compare
+
+        return _compare.argmax(self, axis, keepdims)
+
+    def softmax(self, axis: int = -1) -> Tensor:
+        """Numerically stable softmax along ``axis``."""
+        from tensorgrad_b200.ops import activation as _activation
+
+        return _activation.softmax(self, axis)
+
+    def log_softmax(self, axis: int = -1) -> Tensor:
+        """Numerically stable log-softmax along ``axis``."""
+        from tensorgrad_b200.ops import activation as _activation
+
+        return _activation.log_softmax(self, axis)
+
+    def masked_fill(self, mask: Any, value: float) -> Tensor:
+        """Replace entries where ``mask`` holds by ``value`` (no gradient flows there)."""
+        return _shape.masked_fill(self, mask, value)
 
     def reshape(self, *shape: int | Sequence[int]) -> Tensor:
         dims: Sequence[object] = (

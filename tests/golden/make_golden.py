@@ -329,6 +329,29 @@ def run_higher_order_layers() -> dict[str, np.ndarray]:
     return out
 
 
+def run_ops_extra() -> dict[str, np.ndarray]:
+    """The remaining ops by the reference (float64): softmax family, max / min with ties,
+    where / masked_fill, concat, binary cross entropy, Elman RNN, vector matmuls,
+    comparisons, all / any / argmax (the program is shared with the tests, specs.py); and the
+    batch order of a shuffled DataLoader."""
+    import types
+
+    from tensorgrad import ops as ref_ops
+    from tensorgrad.utils import DataLoader
+    from tests.golden.specs import ops_extra_inputs, ops_extra_program
+
+    tg.set_default_dtype(np.float64)
+
+    def host(t):
+        return np.array(t.data)
+
+    out = ops_extra_program(tg, types.SimpleNamespace(rnn=ref_ops.rnn), host, ops_extra_inputs())
+    loader = DataLoader(np.arange(10), batch_size=4, shuffle=True, seed=5)
+    for epoch in range(2):
+        out[f"loader_epoch{epoch}"] = np.concatenate([np.array(b.data) for (b,) in loader])
+    return out
+
+
 def main() -> None:
     jobs = {
         "gpt_small": lambda: run_gpt(GPT_SMALL),
@@ -342,6 +365,7 @@ def main() -> None:
         "gpt_generate": run_generate,
         "higher_order": run_higher_order,
         "higher_order_layers": run_higher_order_layers,
+        "ops_extra": run_ops_extra,
     }
     names = sys.argv[1:] or [*jobs, "gpt_checkpoint"]
     for name in names:

@@ -237,3 +237,89 @@ def gpt_penalty_program(tg, nn, host, spec: dict) -> dict[str, np.ndarray]:
     for n, p in zip(names, params, strict=True):
         out[f"gpt_grad/{n}"] = host(p.grad)
     return out
+
+
+def ops_extra_inputs() -> dict[str, np.ndarray]:
+    """Seeded float64 inputs of the fixture of the remaining ops (ops_extra.npz): the softmax
+    family, max / min with ties, where / masked_fill, concat, binary cross entropy, the
+    Elman RNN, matmul with vectors, comparisons and all / any / argmax."""
+    rng = np.random.default_rng(97)
+    n = rng.standard_normal
+    masked = n((2, 6))
+    masked[0, [1, 4]] = -np.inf
+    masked[1, 5] = -np.inf
+    z = 3.0 * n(9)
+    z[:3] = (0.0, 40.0, -40.0)
+    return {
+        "s_x": n((3, 5, 4)), "s_g": n((3, 5, 4)), "s_g1": n((3, 4)), "masked": masked,
+        "masked_g": n((2, 6)),
+        "m_x": rng.integers(0, 3, size=(4, 6)).astype(np.float64), "m_g1": n(4),
+        "w_c": rng.random((4, 6)) > 0.5, "w_a": n((4, 6)), "w_b": n(6), "w_g": n((4, 6)),
+        "c_a": n((2, 3)), "c_b": n((2, 5)), "c_c": n((2, 1)), "c_g": n((2, 9)),
+        "b_z": z, "b_y": rng.random(9), "b_g": n(9),
+        "rx": n((5, 2, 3)), "rh0": 0.5 * n((2, 4)), "r_wih": 0.5 * n((4, 3)),
+        "r_whh": 0.5 * n((4, 4)), "r_bih": 0.1 * n(4), "r_bhh": 0.1 * n(4), "r_g": n((5, 2, 4)),
+        "v1": n(4), "v2": n(4), "mm": n((3, 4)), "bm": n((2, 4, 5)), "mm_g": n(3),
+        "bm_g": n((2, 5)),
+    }
+
+
+def ops_extra_program(tg, O, host, d: dict[str, np.ndarray]) -> dict[str, np.ndarray]:
+    """Values and VJPs of the remaining ops, written once for both implementations: ``O``
+    holds ``rnn`` (the ops module's), everything else is the package's top level and Tensor
+    methods; ``host(t)`` a tensor's values as an array."""
+    T = tg.Tensor
+    out: dict[str, np.ndarray] = {}
+
+    def vjp(name: str, y, xs, g) -> None:
+        out[f"{name}/y"] = host(y)
+        grads = tg.autograd.grad(y, xs, grad_outputs=T(g) if g is not None else None,
+                                 allow_unused=True)
+        for i, gr in enumerate(grads):
+            out[f"{name}/g{i}"] = np.zeros(xs[i].shape) if gr is None else host(gr)
+
+    x = T(d["s_x"], requires_grad=True)
+    vjp("softmax", tg.softmax(x, -1), [x], d["s_g"])
+    vjp("softmax_ax1", x.softmax(1), [x], d["s_g"])
+    vjp("log_softmax", tg.log_softmax(x, -1), [x], d["s_g"])
+    vjp("logsumexp", tg.logsumexp(x, 1), [x], d["s_g1"])
+    vjp("logsumexp_keep", tg.logsumexp(x, -1, keepdims=True), [x], d["s_g"][..., :1])
+    xm = T(d["masked"], requires_grad=True)
+    vjp("softmax_masked", tg.softmax(xm), [xm], d["masked_g"])
+    vjp("logsumexp_masked", tg.logsumexp(xm), [xm], d["masked_g"][:, 0])
+    m = T(d["m_x"], requires_grad=True)
+    vjp("max_ax1", tg.max(m, axis=1), [m], d["m_g1"])
+    vjp("min_ax1", m.min(axis=1), [m], d["m_g1"])
+    vjp("max_all", m.max(), [m], None)
+    vjp("min_all_keep", tg.min(m, keepdims=True), [m], np.ones((1, 1)))
+    a, b = T(d["w_a"], requires_grad=True), T(d["w_b"], requires_grad=True)
+    vjp("where", tg.where(d["w_c"], a, b), [a, b], d["w_g"])
+    vjp("masked_fill", tg.masked_fill(a, d["w_c"], -1.5), [a], d["w_g"])
+    vjp("masked_fill_method", a.masked_fill(T(d["w_c"]), 2.0), [a], d["w_g"])
+    ca, cb, cc = (T(d[k], requires_grad=True) for k in ("c_a", "c_b", "c_c"))
+    vjp("concat", tg.concat([ca, cb, cc], axis=1), [ca, cb, cc], d["c_g"])
+    z, y = T(d["b_z"], requires_grad=True), T(d["b_y"], requires_grad=True)
+    for red in ("mean", "sum", "none"):
+        loss = tg.binary_cross_entropy_with_logits(z, y, reduction=red)
+        vjp(f"bce_{red}", loss, [z, y], d["b_g"] if red == "none" else None)
+    rnn_in = [T(d[k], requires_grad=True)
+              for k in ("rx", "rh0", "r_wih", "r_whh", "r_bih", "r_bhh")]
+    for act in ("tanh", "relu"):
+        vjp(f"rnn_{act}", O.rnn(*rnn_in, nonlinearity=act), rnn_in, d["r_g"])
+    v1, v2 = T(d["v1"], requires_grad=True), T(d["v2"], requires_grad=True)
+    mm, bm = T(d["mm"], requires_grad=True), T(d["bm"], requires_grad=True)
+    vjp("dot", v1 @ v2, [v1, v2], None)
+    vjp("matvec", mm @ v1, [mm, v1], d["mm_g"])
+    vjp("vecmat_batched", v1 @ bm, [v1, bm], d["bm_g"])
+    pa, pb = T(d["w_a"]), T(d["w_b"])
+    for op, fn in (("gt", lambda p, q: p > q), ("le", lambda p, q: p <= q),
+                   ("eq", lambda p, q: p == q), ("ne_scalar", lambda p, q: p != 0.5)):
+        out[f"cmp_{op}"] = host(fn(pa, pb)).astype(np.uint8)
+    c = T(d["w_c"])
+    out["all_ax0"] = host(c.all(axis=0)).astype(np.uint8)
+    out["any_ax1"] = host(c.any(axis=1)).astype(np.uint8)
+    out["all"] = np.asarray(host(c.all())).astype(np.uint8)
+    out["argmax_ax1"] = host(T(d["m_x"]).argmax(axis=1))
+    out["argmax_all"] = np.asarray(host(T(d["m_x"]).argmax()))
+    out["argmax_keep"] = host(T(d["w_a"]).argmax(axis=0, keepdims=True))
+    return out

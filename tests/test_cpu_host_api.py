@@ -1,0 +1,116 @@
+"""Host-side parts of the API that need no GPU: the DataLoader's batch order (against the
+reference's own, ``tests/golden/ops_extra.npz``), its argument checks, the graph drawings of
+``viz`` (the reference's output format, on graph nodes made without device data) and the
+host allocator switch."""
+
+from __future__ import annotations
+
+import re
+
+import numpy as np
+import pytest
+
+from tests.conftest import load_golden
+
+
+def test_data_loader_order_matches_reference():
+    from tensorgrad_b200.utils import DataLoader
+
+    gold = load_golden("ops_extra.npz")
+    loader = DataLoader(np.arange(10), batch_size=4, shuffle=True, seed=5)
+    assert len(loader) == 3
+    for epoch in range(2):
+        order = np.concatenate(list(loader.batches()))
+        np.testing.assert_array_equal(order, gold[f"loader_epoch{epoch}"])
+    assert len(DataLoader(np.zeros((10, 3)), batch_size=4, drop_last=True)) == 2
+    assert [b.tolist() for b in DataLoader(np.zeros(5), batch_size=2).batches()] == [
+        [0, 1], [2, 3], [4]]
+    with pytest.raises(ValueError, match="different lengths"):
+        DataLoader(np.zeros(3), np.zeros(4))
+    with pytest.raises(ValueError, match="positive"):
+        DataLoader(np.zeros(3), batch_size=0)
+    with pytest.raises(ValueError, match="at least one"):
+        DataLoader()
+
+
+class _Meta:
+    """Stands in for device data: the drawings read shapes only."""
+
+    def __init__(self, shape):
+        self.shape = tuple(shape)
+        self.ndim = len(self.shape)
+        self.dtype = np.dtype(np.float64)
+        self.size = int(np.prod(self.shape))
+
+
+def _leaf(shape, requires_grad):
+    from tensorgrad_b200.tensor import Tensor
+
+    t = Tensor._wrap(_Meta(shape))
+    t._requires_grad = requires_grad
+    return t
+
+
+def _op(name, shape, *parents):
+    from tensorgrad_b200.autograd import Node
+
+    t = _leaf(shape, True)
+    t._node = Node(name, parents, lambda g, need: (None,) * len(parents))
+    return t
+
+
+def _small_graph():
+    w, x = _leaf((2, 3), True), _leaf((3,), False)
+    y = _op("tanh", (2,), _op("matmul", (2,), w, x))
+    return _op("sum", (), _op("mul", (2,), y, y)), {"w": w, "x": x}
+
+
+def test_mermaid_source_matches_the_reference_format():
+    from tensorgrad_b200 import viz
+
+    loss, names = _small_graph()
+    assert viz.to_mermaid(loss, names=names, direction="LR") == "\n".join([
+        "flowchart LR",
+        '    n0["w<br/>(2, 3)"]:::param',
+        '    n1["x<br/>(3,)"]:::constant',
+        '    n2("matmul<br/>(2,)"):::op',
+        '    n3("tanh<br/>(2,)"):::op',
+        '    n4("mul<br/>(2,)"):::op',
+        '    n5(["sum<br/>scalar"]):::op',
+        "    n0 --> n2",
+        "    n1 --> n2",
+        "    n2 --> n3",
+        "    n3 --> n4",
+        "    n4 --> n5",
+        "    classDef param fill:#dfeafa,stroke:#898781,color:#0b0b0b",
+        "    classDef constant fill:none,stroke:#898781,stroke-dasharray:4 3,color:#898781",
+        "    classDef op fill:#f3f2ee,stroke:#898781,color:#0b0b0b",
+        "",
+    ])
+
+
+def test_dot_source_and_labels():
+    from tensorgrad_b200 import viz
+
+    loss, names = _small_graph()
+    dot = viz.to_dot(loss, names=names)
+    assert dot.startswith("digraph tensorgrad {\n  rankdir=TB;")
+    declared = set(re.findall(r"^  (n\d+) \[label=", dot, re.M))
+    edges = re.findall(r"^  (n\d+) -> (n\d+);", dot, re.M)
+    assert declared == {f"n{i}" for i in range(6)} and len(edges) == 5
+    assert 'label="sum\\nscalar"' in dot and "penwidth=2" in dot
+    assert 'label="x\\n(3,)", shape=box, style="dashed"' in dot
+    a = _leaf((2,), True)
+    hidden = _op("relu", (2,), a)
+    out = _op("sum", (), hidden)
+    named = {'say "a"': a, "hidden": hidden}
+    assert "say #quot;a#quot;<br/>(2,)" in viz.to_mermaid(out, names=named)
+    assert "hidden = relu\\n(2,)" in viz.to_dot(out, names=named)
+    with pytest.raises(ValueError, match="at least one"):
+        viz.to_dot()
+
+
+def test_retain_freed_memory_reports_glibc():
+    from tensorgrad_b200.utils import retain_freed_memory
+
+    assert retain_freed_memory() in (True, False)
