@@ -338,11 +338,15 @@ def embedding(indices: Any, weight: Any) -> Tensor:
         raise TypeError(f"embedding indices must be integers, got {idx.dtype}")
     if idx.size and (idx.min() < 0 or idx.max() >= num):
         raise IndexError(f"embedding ids must be in [0, {num}), got {idx.min()}..{idx.max()}")
+    rows = host_rows(idx, num, dim)
+    return make_result(rows.gather_array(wd), (tw,), rows.backward, "embedding", rows.graph)
+
+
+def host_rows(idx: np.ndarray, num: int, dim: int) -> _Rows:
+    """``_Rows`` for checked host ids: uploaded once; the scatter-add sorts them on the host
+    (the reference's stable order) and sums each run of equal ids on the device."""
     flat = np.ascontiguousarray(idx.reshape(-1), dtype=np.int64)
     ids_host = device.from_numpy(flat)
-    out = device.empty((*idx.shape, dim), wd.dtype)
-    check(lib.tg_embedding_forward(code, ids_host.ptr, wd.ptr, out.ptr, flat.size, num, dim,
-                                   None, device.stream()), "embedding")
 
     def scatter_host(g: DeviceArray) -> DeviceArray:
         order, seg_start, seg_id = _segments(flat)
@@ -355,8 +359,7 @@ def embedding(indices: Any, weight: Any) -> Tensor:
                                         device.stream()), "embedding backward")
         return gw
 
-    rows = _Rows(ids_host, idx.shape, num, dim, None, scatter_host)
-    return make_result(out, (tw,), rows.backward, "embedding", rows.graph)
+    return _Rows(ids_host, idx.shape, num, dim, None, scatter_host)
 
 
 class _Rows:

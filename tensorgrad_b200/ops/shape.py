@@ -161,13 +161,67 @@ def _basic_view(shape: tuple[int, ...], itemsize: int, index: Any) -> tuple[int,
     return offset // itemsize, view.shape, [s // itemsize for s in view.strides]
 
 
+def _normalize_index(index: Any) -> tuple[Any, bool]:
+    """Tensors and lists in an index as host arrays, boolean masks as their nonzero
+    positions; whether the index is advanced (ops/shape.py:162-179)."""
+    items = index if isinstance(index, tuple) else (index,)
+    out: list[Any] = []
+    advanced = False
+    for item in items:
+        value = item.data if isinstance(item, Tensor) else item
+        if isinstance(value, DeviceArray):
+            value = value.numpy()
+        if isinstance(value, list):
+            value = np.asarray(value)
+        if isinstance(value, np.ndarray):
+            advanced = True
+            if value.dtype == np.bool_:
+                out.extend(np.nonzero(value))
+                continue
+            if not np.issubdtype(value.dtype, np.integer):
+                raise IndexError(f"index arrays must be integer or boolean, got {value.dtype}")
+        out.append(value)
+    return (tuple(out) if isinstance(index, tuple) or len(out) != 1 else out[0]), advanced
+
+
+def _gather_elements(ta: Tensor, index: Any) -> Tensor:
+    """``a[index]`` with integer or boolean arrays (NumPy's advanced indexing): the selected
+    flat positions are worked out on the host from the index alone, the elements are gathered
+    on the device, and the VJP scatter-adds the gradient (an element selected twice gets both
+    contributions), as the embedding's row lookup and its adjoint with rows of one element."""
+    from tensorgrad_b200.ops.layers import host_rows
+
+    positions = np.arange(ta.size, dtype=np.int64).reshape(ta.shape)[index]
+    rows = host_rows(positions, max(ta.size, 1), 1)
+    x = ta.data
+    if x.dtype.kind != "f":
+        # Integer data moves bit for bit through the float gather of the same width.
+        width = {8: np.float64, 4: np.float32}.get(x.itemsize)
+        if width is None:
+            return Tensor._wrap(device.from_numpy(x.numpy()[index]))
+        raw = DeviceArray(x._buf, x._off, (x.size, 1), np.dtype(width))
+        got = rows.gather_array(raw)
+        return Tensor._wrap(DeviceArray(got._buf, got._off, positions.shape, x.dtype))
+    out = rows.gather_array(x.reshape((x.size, 1))).reshape(positions.shape)
+
+    def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray]:
+        return (rows.scatter_array(g.reshape((g.size, 1))).reshape(ta.shape),)
+
+    def graph(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
+        return (reshape(rows.scatter(reshape(g, (*positions.shape, 1))), ta.shape),)
+
+    return make_result(out, (ta,), backward, "getitem", graph)
+
+
 @profiled("getitem")
 def getitem(a: Any, index: Any) -> Tensor:
-    """``a[index]`` for ints, slices, ``...`` and ``None``; the VJP scatters the gradient into
-    zeros at the selected positions (ops/shape.py:182-235)."""
+    """``a[index]``: NumPy's basic indexing (ints, slices, ``...``, ``None``) as one strided
+    copy whose VJP writes the gradient into zeros at the selected positions; integer / boolean
+    arrays (and tensors) as a gather whose VJP is a scatter-add (ops/shape.py:182-235)."""
     ta = as_tensor(a)
-    if isinstance(index, Tensor):
-        raise NotImplementedError("getitem on device tensors supports basic indexing only")
+    index, advanced = _normalize_index(index)
+    if advanced:
+        return _gather_elements(ta, index)
     x = ta.data
     offset, shape, strides = _basic_view(ta.shape, x.itemsize, index)
     out = device.empty(shape, x.dtype)

@@ -261,6 +261,8 @@ def ops_extra_inputs() -> dict[str, np.ndarray]:
         "r_whh": 0.5 * n((4, 4)), "r_bih": 0.1 * n(4), "r_bhh": 0.1 * n(4), "r_g": n((5, 2, 4)),
         "v1": n(4), "v2": n(4), "mm": n((3, 4)), "bm": n((2, 4, 5)), "mm_g": n(3),
         "bm_g": n((2, 5)),
+        "ix": n((5, 4, 3)), "ix_rows": np.array([3, 0, 3, 1]), "ix_mask": rng.random((5, 4)) > 0.4,
+        "ix_cols": np.array([2, 0, 2]), "ix_t": rng.integers(0, 4, size=5),
     }
 
 
@@ -311,6 +313,15 @@ def ops_extra_program(tg, O, host, d: dict[str, np.ndarray]) -> dict[str, np.nda
     vjp("dot", v1 @ v2, [v1, v2], None)
     vjp("matvec", mm @ v1, [mm, v1], d["mm_g"])
     vjp("vecmat_batched", v1 @ bm, [v1, bm], d["bm_g"])
+    ix = T(d["ix"], requires_grad=True)
+    rng_g = np.random.default_rng(5)
+    for name, index in (("rows", d["ix_rows"]), ("mask", d["ix_mask"]),
+                        ("cols_repeat", (slice(None), d["ix_cols"])),
+                        ("pairs", (np.arange(5), d["ix_t"])),
+                        ("mixed", (d["ix_rows"], slice(1, 3), 0)),
+                        ("tensor_rows", T(d["ix_rows"]))):
+        y_ix = ix[index]
+        vjp(f"index_{name}", y_ix, [ix], rng_g.standard_normal(y_ix.shape))
     pa, pb = T(d["w_a"]), T(d["w_b"])
     for op, fn in (("gt", lambda p, q: p > q), ("le", lambda p, q: p <= q),
                    ("eq", lambda p, q: p == q), ("ne_scalar", lambda p, q: p != 0.5)):
