@@ -97,11 +97,11 @@ class Node:
     __slots__ = ("_backward", "_graph", "op", "parents")
 
     def __init__(self, op: str, parents: tuple[Tensor, ...], backward: BackwardFn,
-                 graph: GraphFn | None = None) -> None:
+                 graph_backward: GraphFn | None = None) -> None:
         self.op = op
         self.parents = parents
         self._backward: BackwardFn | None = backward
-        self._graph: GraphFn | None = graph
+        self._graph: GraphFn | None = graph_backward
 
     @property
     def released(self) -> bool:
@@ -123,6 +123,15 @@ class Node:
         self.check_alive()
         assert self._backward is not None
         return self._backward(grad, need)
+
+    def apply_graph(self, grad: Tensor, output: Tensor,
+                    need: tuple[bool, ...]) -> tuple[Tensor | None, ...]:
+        """The VJP in differentiable ops (``create_graph``): the gradients carry a graph."""
+        self.check_alive()
+        if self._graph is None:
+            raise NotImplementedError(
+                f"create_graph=True: op '{self.op}' has no differentiable VJP on the device")
+        return self._graph(grad, output, need)
 
     def release(self) -> None:
         """Drop the closures (and the device buffers they saved) and the parent references."""
