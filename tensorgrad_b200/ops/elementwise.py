@@ -189,7 +189,8 @@ def neg(a: Any) -> Tensor:
 @profiled("pow")
 def pow(base: Any, exponent: Any) -> Tensor:  # noqa: A001
     """``base ** exponent`` (ops/elementwise.py:138-167). A Python-number exponent runs as one
-    kernel; the gradient with respect to a tensor exponent is not on the device path."""
+    kernel. The gradient with respect to a tensor exponent, ``out * log(base)``, exists for
+    positive bases only and is zero elsewhere, as in the reference."""
     if isinstance(exponent, int | float) and isinstance(base, Tensor):
         tb = base
         e = float(exponent)
@@ -205,17 +206,38 @@ def pow(base: Any, exponent: Any) -> Tensor:  # noqa: A001
     tb, te = coerce_pair(base, exponent)
     out = binary_array(tb.data, te.data, POW)
 
+    def positive() -> Tensor:
+        from tensorgrad_b200.ops.compare import compare
+
+        return compare(tb, 0.0, "gt")  # a constant mask: log(base) exists where base > 0
+
     def backward2(g: DeviceArray, need: Need) -> tuple[DeviceArray | None, DeviceArray | None]:
+        from tensorgrad_b200.ops.shape import where_array
+
+        g_base = g_exp = None
+        if need[0]:
+            em1 = binary_array(te.data, device.scalar_like(1.0, te.dtype), SUB)
+            d = binary_array(binary_array(g, te.data, MUL), binary_array(tb.data, em1, POW), MUL)
+            g_base = unbroadcast(d, tb.shape)
         if need[1]:
-            raise NotImplementedError("pow: gradient with respect to a tensor exponent")
-        em1 = binary_array(te.data, device.scalar_like(1.0, te.dtype), SUB)
-        d = binary_array(binary_array(g, te.data, MUL), binary_array(tb.data, em1, POW), MUL)
-        return unbroadcast(d, tb.shape), None
+            mask = positive().data
+            one, zero = (device.scalar_like(v, out.dtype) for v in (1.0, 0.0))
+            log_base = _unary(where_array(mask, tb.data if tb.dtype == out.dtype
+                                          else cast_array(tb.data, out.dtype), one), LOG)
+            d = binary_array(binary_array(g, out, MUL), log_base, MUL)
+            g_exp = unbroadcast(where_array(mask, d, zero), te.shape)
+        return g_base, g_exp
 
     def graph2(g: Tensor, y: Tensor, need: Need) -> tuple[Tensor | None, Tensor | None]:
+        from tensorgrad_b200.ops.shape import where
+
+        g_base = _sum_to(mul(mul(g, te), pow(tb, sub(te, 1.0))), tb.shape) if need[0] else None
+        g_exp = None
         if need[1]:
-            raise NotImplementedError("pow: gradient with respect to a tensor exponent")
-        return _sum_to(mul(mul(g, te), pow(tb, sub(te, 1.0))), tb.shape), None
+            mask = positive()
+            log_base = log(where(mask, tb, 1.0))
+            g_exp = _sum_to(where(mask, mul(mul(g, y), log_base), 0.0), te.shape)
+        return g_base, g_exp
 
     return make_result(out, (tb, te), backward2, "pow", graph2)
 

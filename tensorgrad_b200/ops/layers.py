@@ -149,8 +149,9 @@ def _normalized_vjp(g: Tensor, x: Tensor, w: Tensor | None, b: Tensor | None,
                     view: tuple[int, ...] | None) -> tuple[Tensor | None, ...]:
     """Graph VJP of ``xhat * w + b`` with ``xhat`` normalised over ``axes`` (biased
     variance): ``gx = rstd (gh - mean(gh) - xhat mean(gh xhat))``, ``gh = g w``,
-    ``gw = sum(g xhat)``, ``gb = sum(g)``, the sums over the other axes. ``view`` reshapes
-    ``w`` to broadcast against ``x`` (batch norm's per-channel parameters)."""
+    ``gw = sum(g xhat)``, ``gb = sum(g)``. Without ``view`` (layer norm: parameters along the
+    normalised axes) the parameter sums run over the other axes; with ``view`` (batch norm:
+    one parameter per channel, ``w`` reshaped to ``view`` to broadcast) over ``axes``."""
     from tensorgrad_b200.ops.shape import reshape
 
     mul, sub, add = elementwise.mul, elementwise.sub, elementwise.add
@@ -158,7 +159,7 @@ def _normalized_vjp(g: Tensor, x: Tensor, w: Tensor | None, b: Tensor | None,
     rstd = elementwise.pow(add(reduce.mean(mul(centred, centred), axes, keepdims=True), eps),
                            -0.5)
     xhat = mul(centred, rstd)
-    other = tuple(i for i in range(x.ndim) if i not in axes)
+    other = axes if view is not None else tuple(i for i in range(x.ndim) if i not in axes)
     grads: list[Tensor | None] = [None]
     if need[0]:
         gh = g if w is None else mul(g, w if view is None else reshape(w, view))
