@@ -1,13 +1,14 @@
-"""Learning-rate schedules, kept minimal (API of the reference's optim/lr_scheduler.py).
+"""Learning-rate schedules (API of the reference's optim/lr_scheduler.py).
 
-A schedule is a multiplier of each group's initial learning rate as a function of the
-schedule's step count; stepping it writes ``initial_lr * multiplier`` into every group, which
-the next optimizer kernel launch reads as a scalar argument. Nothing here touches the device.
+A schedule maps its step count to a multiplier of every parameter group's ``initial_lr``.
+Building one applies step 0; each ``step()`` advances the count and rewrites the groups'
+``lr``, which the next optimizer launch passes to its kernel as a scalar. Host-only.
 """
 
 from __future__ import annotations
 
 import math
+from abc import ABC, abstractmethod
 from typing import Any
 
 from tensorgrad_b200.optim.optimizer import Optimizer
@@ -15,60 +16,70 @@ from tensorgrad_b200.optim.optimizer import Optimizer
 __all__ = ["CosineWarmupLR", "LRScheduler", "StepLR"]
 
 
-class LRScheduler:
-    """Base schedule: subclasses define ``factor(step)``."""
+class LRScheduler(ABC):
+    """Subclasses give ``factor(step)``, the multiplier of the initial learning rate (an
+    abstract method: the base class cannot be built on its own)."""
 
     def __init__(self, optimizer: Optimizer[Any]) -> None:
         self.optimizer = optimizer
         self.last_step = 0
-        self._write()
+        self._set_rates()
 
+    @abstractmethod
     def factor(self, step: int) -> float:
-        raise NotImplementedError
+        """The multiplier at ``step``."""
 
     def step(self) -> None:
+        """One optimizer update later."""
         self.last_step += 1
-        self._write()
+        self._set_rates()
 
     def get_last_lr(self) -> list[float]:
-        return [g.lr for g in self.optimizer.param_groups]
+        """The learning rate each group has now."""
+        return [group.lr for group in self.optimizer.param_groups]
 
-    def _write(self) -> None:
-        mult = self.factor(self.last_step)
-        for g in self.optimizer.param_groups:
-            g.lr = g.initial_lr * mult
+    def _set_rates(self) -> None:
+        scale = self.factor(self.last_step)
+        for group in self.optimizer.param_groups:
+            group.lr = scale * group.initial_lr
 
 
 class StepLR(LRScheduler):
-    """``gamma ** (step // step_size)``."""
+    """Decay by ``gamma`` once every ``step_size`` steps."""
 
     def __init__(self, optimizer: Optimizer[Any], step_size: int, gamma: float = 0.1) -> None:
         if step_size <= 0:
             raise ValueError("step_size must be positive")
-        self.step_size, self.gamma = step_size, gamma
+        self.step_size = step_size
+        self.gamma = gamma
         super().__init__(optimizer)
 
     def factor(self, step: int) -> float:
-        return float(self.gamma ** (step // self.step_size))
+        decays = step // self.step_size
+        return float(self.gamma ** decays)
 
 
 class CosineWarmupLR(LRScheduler):
-    """Linear warm-up over ``warmup_steps`` (``(step + 1) / warmup``), then a half cosine from
-    1 down to ``min_lr_ratio`` at ``total_steps`` (held there afterwards)."""
+    """Warm up linearly, ``(step + 1) / warmup_steps``, then fall along half a cosine from 1
+    to ``min_lr_ratio``, reached at ``total_steps`` and kept from then on."""
 
     def __init__(self, optimizer: Optimizer[Any], warmup_steps: int, total_steps: int,
                  min_lr_ratio: float = 0.0) -> None:
-        if warmup_steps < 0 or total_steps <= 0 or warmup_steps > total_steps:
+        if total_steps <= 0 or not 0 <= warmup_steps <= total_steps:
             raise ValueError("need 0 <= warmup_steps <= total_steps and total_steps > 0")
         if not 0.0 <= min_lr_ratio <= 1.0:
             raise ValueError("min_lr_ratio must be in [0, 1]")
-        self.warmup_steps, self.total_steps, self.min_lr_ratio = (warmup_steps, total_steps,
-                                                                  min_lr_ratio)
+        self.warmup_steps = warmup_steps
+        self.total_steps = total_steps
+        self.min_lr_ratio = min_lr_ratio
         super().__init__(optimizer)
 
     def factor(self, step: int) -> float:
-        if step < self.warmup_steps:
-            return (step + 1) / self.warmup_steps
-        done = min((step - self.warmup_steps) / max(self.total_steps - self.warmup_steps, 1), 1.0)
-        cosine = 0.5 * (1.0 + math.cos(math.pi * done))
-        return self.min_lr_ratio + (1.0 - self.min_lr_ratio) * cosine
+        w, floor = self.warmup_steps, self.min_lr_ratio
+        if step < w:
+            return (step + 1) / w
+        decay_steps = self.total_steps - w if self.total_steps > w else 1
+        t = (step - w) / decay_steps
+        if t > 1.0:
+            t = 1.0
+        return floor + (1.0 - floor) * (0.5 * (1.0 + math.cos(math.pi * t)))

@@ -1,16 +1,16 @@
-"""Per-op timing (the reference's ``tensorgrad.profiler`` API, profiler.py:25-152).
+"""Per-op timing (the reference's ``tensorgrad.profiler`` API).
 
     with tensorgrad_b200.profiler.profile() as prof:
         loss = tg.cross_entropy(model(x), y)
         loss.backward()
     print(prof.table())
 
-Inside the block every public op and every VJP the backward pass runs is timed, and the
-device is synchronised around each timed call, so a row's time is the device work it
-launched plus its host overhead. Time of ops called by an op (a composite op, a graph VJP) is
-charged to those ops: every row is self time and the rows add up. The "autograd engine" row
-is the backward pass's own time outside VJPs. Timing synchronises the stream, so never
-profile a run whose throughput you report.
+While a profile is open, each public op call and each VJP the engine runs is timed between
+two device synchronisations, so a row holds the device work the call launched plus its host
+overhead. Nested timed calls (the ops inside a composite op or a graph VJP) are subtracted
+from their caller: rows are self times and sum to the profiled total. The backward engine's
+own work outside the VJPs has a row of its own (``ENGINE``). The synchronisations change the
+timing of the code they wrap: never profile a run whose throughput you report.
 """
 
 from __future__ import annotations
@@ -24,14 +24,13 @@ from typing import Any, TypeVar
 
 __all__ = ["ENGINE", "OpStats", "Profile", "profile", "profiled"]
 
-#: Name of the row that holds the backward engine's own time.
-ENGINE = "autograd engine"
-_R = TypeVar("_R")
+ENGINE = "autograd engine"  # the row of the backward engine's own time
+_T = TypeVar("_T")
 
 
 @dataclass
 class OpStats:
-    """Call counts and self time (seconds) of one op."""
+    """One op's calls and self seconds, forward and backward apart."""
 
     forward_calls: int = 0
     forward_seconds: float = 0.0
@@ -40,103 +39,113 @@ class OpStats:
 
     @property
     def total_seconds(self) -> float:
-        """Forward plus backward self time."""
         return self.forward_seconds + self.backward_seconds
+
+    def add(self, backward: bool, seconds: float) -> None:
+        if backward:
+            self.backward_calls += 1
+            self.backward_seconds += seconds
+        else:
+            self.forward_calls += 1
+            self.forward_seconds += seconds
+
+
+# Columns of ``Profile.table``: header, and the cell of a row (9 characters wide).
+_COLUMNS: list[tuple[str, Callable[[OpStats], str]]] = [
+    ("fwd calls", lambda s: f"{s.forward_calls:>9}"),
+    ("fwd ms", lambda s: f"{1e3 * s.forward_seconds:>9.2f}"),
+    ("bwd calls", lambda s: f"{s.backward_calls:>9}"),
+    ("bwd ms", lambda s: f"{1e3 * s.backward_seconds:>9.2f}"),
+    ("total ms", lambda s: f"{1e3 * s.total_seconds:>9.2f}"),
+]
 
 
 class Profile:
-    """Per-op timings collected by :func:`profile`, keyed by op name."""
+    """What one ``profile()`` block collected: ``ops`` maps an op name to its
+    :class:`OpStats`; ``wall_seconds`` is the block's duration."""
 
     def __init__(self) -> None:
         self.ops: dict[str, OpStats] = {}
-        #: Wall-clock duration of the ``with`` block.
         self.wall_seconds = 0.0
-        self._nested: list[float] = []  # time of timed calls inside each call in progress
+        self._inner: list[float] = []  # seconds of timed calls nested in each open call
 
-    def timed(self, name: str, backward: bool, fn: Callable[..., _R], *args: Any,
-              **kwargs: Any) -> _R:
-        """Run ``fn(*args, **kwargs)`` between two device synchronisations and charge its
-        self time to ``name``."""
+    def timed(self, name: str, backward: bool, fn: Callable[..., _T], *args: Any,
+              **kwargs: Any) -> _T:
+        """``fn(*args, **kwargs)``, its self time charged to ``name``."""
         from tensorgrad_b200.device import synchronize
 
         synchronize()
-        self._nested.append(0.0)
-        start = time.perf_counter()
+        self._inner.append(0.0)
+        t0 = time.perf_counter()
         try:
             return fn(*args, **kwargs)
         finally:
             synchronize()
-            elapsed = time.perf_counter() - start
-            own = elapsed - self._nested.pop()
-            if self._nested:
-                self._nested[-1] += elapsed
-            stats = self.ops.setdefault(name, OpStats())
-            if backward:
-                stats.backward_calls += 1
-                stats.backward_seconds += own
-            else:
-                stats.forward_calls += 1
-                stats.forward_seconds += own
+            spent = time.perf_counter() - t0
+            nested = self._inner.pop()
+            if self._inner:
+                self._inner[-1] += spent
+            self.ops.setdefault(name, OpStats()).add(backward, spent - nested)
 
     @property
     def profiled_seconds(self) -> float:
-        """Time inside ops and the engine (the sum of all rows)."""
-        return sum(s.total_seconds for s in self.ops.values())
+        """All rows together: the time inside ops and the engine."""
+        return sum(stats.total_seconds for stats in self.ops.values())
 
     def table(self, limit: int | None = None) -> str:
-        """Rows by total self time, as an aligned text table (milliseconds)."""
-        rows = sorted(self.ops.items(), key=lambda kv: kv[1].total_seconds, reverse=True)
+        """One aligned row per op (largest total first; the first ``limit`` rows) in
+        milliseconds with each op's share, then the profiled and wall totals."""
         total = self.profiled_seconds or 1.0
-        width = max([2, *(len(name) for name in self.ops)])
-        head = (f"{'op':<{width}}  {'fwd calls':>9}  {'fwd ms':>9}  {'bwd calls':>9}  "
-                f"{'bwd ms':>9}  {'total ms':>9}  {'share':>6}")
-        lines = [head, "-" * len(head)]
-        for name, s in rows[:limit]:
-            lines.append(f"{name:<{width}}  {s.forward_calls:>9}  {1e3 * s.forward_seconds:>9.2f}  "
-                         f"{s.backward_calls:>9}  {1e3 * s.backward_seconds:>9.2f}  "
-                         f"{1e3 * s.total_seconds:>9.2f}  {s.total_seconds / total:>6.1%}")
-        rest = self.wall_seconds - self.profiled_seconds
-        lines.append(f"ops and engine: {1e3 * self.profiled_seconds:.2f} ms of "
-                     f"{1e3 * self.wall_seconds:.2f} ms wall time ({1e3 * rest:.2f} ms elsewhere: "
-                     "Python code between ops, optimiser, data)")
-        return "\n".join(lines)
+        width = max(len(name) for name in ["op", *self.ops])
+        header = "  ".join([f"{'op':<{width}}", *(f"{h:>9}" for h, _ in _COLUMNS),
+                            f"{'share':>6}"])
+        out = [header, "-" * len(header)]
+        ranked = sorted(self.ops.items(), key=lambda item: -item[1].total_seconds)
+        for name, stats in ranked[:limit]:
+            cells = [f"{name:<{width}}", *(cell(stats) for _, cell in _COLUMNS),
+                     f"{stats.total_seconds / total:>6.1%}"]
+            out.append("  ".join(cells))
+        inside, wall = 1e3 * self.profiled_seconds, 1e3 * self.wall_seconds
+        out.append(f"ops and engine: {inside:.2f} ms of {wall:.2f} ms wall time "
+                   f"({wall - inside:.2f} ms elsewhere: Python code between ops, optimiser, "
+                   "data)")
+        return "\n".join(out)
 
 
-class _Active:
+class _Current:
     profile: Profile | None = None
 
 
 def active() -> Profile | None:
-    """The profile being collected, if a :func:`profile` block is open."""
-    return _Active.profile
+    """The open profile, or ``None``."""
+    return _Current.profile
 
 
 @contextlib.contextmanager
 def profile() -> Iterator[Profile]:
-    """Collect per-op timings for the code inside the ``with`` block (blocks do not nest)."""
-    if _Active.profile is not None:
+    """Time the ops run inside the ``with`` block (one block at a time, one thread)."""
+    if _Current.profile is not None:
         raise RuntimeError("profile() blocks cannot be nested")
-    result = Profile()
-    _Active.profile = result
-    start = time.perf_counter()
+    prof = _Current.profile = Profile()
+    t0 = time.perf_counter()
     try:
-        yield result
+        yield prof
     finally:
-        result.wall_seconds = time.perf_counter() - start
-        _Active.profile = None
+        prof.wall_seconds = time.perf_counter() - t0
+        _Current.profile = None
 
 
-def profiled(name: str) -> Callable[[Callable[..., _R]], Callable[..., _R]]:
-    """Decorator for op functions: time each call under ``name`` while profiling."""
+def profiled(name: str) -> Callable[[Callable[..., _T]], Callable[..., _T]]:
+    """Mark an op function: while a profile is open its calls are timed as ``name``."""
 
-    def decorate(fn: Callable[..., _R]) -> Callable[..., _R]:
+    def wrap(fn: Callable[..., _T]) -> Callable[..., _T]:
         @functools.wraps(fn)
-        def wrapper(*args: Any, **kwargs: Any) -> _R:
-            prof = _Active.profile
-            if prof is None:
-                return fn(*args, **kwargs)
-            return prof.timed(name, False, fn, *args, **kwargs)
+        def call(*args: Any, **kwargs: Any) -> _T:
+            prof = _Current.profile
+            if prof is not None:
+                return prof.timed(name, False, fn, *args, **kwargs)
+            return fn(*args, **kwargs)
 
-        return wrapper
+        return call
 
-    return decorate
+    return wrap

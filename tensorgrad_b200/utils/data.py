@@ -1,10 +1,11 @@
-"""Mini-batches of in-memory host arrays, uploaded to the device (the reference's
-utils/data.py:15-68: same arguments, same order of examples, same batch boundaries).
+"""Mini-batches of in-memory host arrays, uploaded to the device (API of the reference's
+utils/data.py: the same arguments, example order and batch boundaries).
 
-Each batch is gathered on the host in one indexing pass per array and uploaded with one
-asynchronous copy (through the library's reused page-locked staging blocks); labels stay
-integer tensors (device-resident targets and ids are accepted by the loss and embedding ops
-without a host round trip).
+An epoch is one permutation (or the identity) of the example indices cut into consecutive
+slices of ``batch_size``; each batch is gathered on the host, one ``np.take`` per array, and
+uploaded with one asynchronous copy through the library's reused page-locked staging
+blocks. Integer labels stay int64 tensors, which the loss and embedding ops take on the
+device without a host round trip.
 """
 
 from __future__ import annotations
@@ -21,46 +22,52 @@ __all__ = ["DataLoader"]
 
 
 class DataLoader:
-    """Iterate over aligned arrays (same first dimension) in mini-batches of tensors.
+    """Aligned arrays (one example per row of each) in mini-batches of device tensors.
 
     Args:
-        *arrays: e.g. inputs and labels.
+        *arrays: e.g. inputs and labels, all of one length.
         batch_size: Examples per batch.
-        shuffle: A fresh permutation every epoch, from a generator of its own (``seed``),
-            independent of the global one.
-        drop_last: Skip a final batch smaller than ``batch_size``.
-        seed: Seed of the shuffling generator.
+        shuffle: A new permutation each epoch, drawn from the loader's own generator
+            (seeded by ``seed``, independent of the global generator).
+        drop_last: Leave out a last batch shorter than ``batch_size``.
+        seed: Seed of that generator.
     """
 
     def __init__(self, *arrays: Any, batch_size: int = 32, shuffle: bool = False,
                  drop_last: bool = False, seed: int | None = None) -> None:
-        if not arrays:
+        if len(arrays) == 0:
             raise ValueError("DataLoader needs at least one array")
-        lengths = {len(a) for a in arrays}
-        if len(lengths) != 1:
-            raise ValueError(f"arrays have different lengths: {sorted(lengths)}")
-        if batch_size <= 0:
+        sizes = sorted({len(a) for a in arrays})
+        if len(sizes) > 1:
+            raise ValueError(f"arrays have different lengths: {sizes}")
+        if batch_size < 1:
             raise ValueError("batch_size must be positive")
         self.arrays = tuple(np.asarray(a) for a in arrays)
-        self.batch_size, self.shuffle, self.drop_last = batch_size, shuffle, drop_last
+        self.batch_size = batch_size
+        self.shuffle = shuffle
+        self.drop_last = drop_last
         self._rng = np.random.default_rng(seed)
 
     @property
     def num_examples(self) -> int:
-        """Examples per epoch, before batching."""
-        return len(self.arrays[0])
+        """Examples in one epoch."""
+        return self.arrays[0].shape[0]
+
+    def _used(self) -> int:
+        """Examples that go into batches (all, or whole batches only with ``drop_last``)."""
+        n = self.num_examples
+        return n - n % self.batch_size if self.drop_last else n
 
     def __len__(self) -> int:
-        full, rest = divmod(self.num_examples, self.batch_size)
-        return full if self.drop_last or rest == 0 else full + 1
+        return -(-self._used() // self.batch_size)
 
     def batches(self) -> Iterator[np.ndarray]:
-        """The example indices of each batch of one epoch (host arrays)."""
+        """The example indices of each batch of one epoch."""
         n = self.num_examples
         order = self._rng.permutation(n) if self.shuffle else np.arange(n)
-        stop = n - n % self.batch_size if self.drop_last else n
-        for start in range(0, stop, self.batch_size):
-            yield order[start:start + self.batch_size]
+        used, size = self._used(), self.batch_size
+        for k in range(-(-used // size)):
+            yield order[k * size:min((k + 1) * size, used)]
 
     def __iter__(self) -> Iterator[tuple[Tensor, ...]]:
         for idx in self.batches():

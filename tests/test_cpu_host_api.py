@@ -114,3 +114,72 @@ def test_retain_freed_memory_reports_glibc():
     from tensorgrad_b200.utils import retain_freed_memory
 
     assert retain_freed_memory() in (True, False)
+
+
+class _Group:
+    def __init__(self, lr):
+        self.lr = self.initial_lr = lr
+
+
+class _Opt:
+    def __init__(self, *lrs):
+        self.param_groups = [_Group(lr) for lr in lrs]
+
+
+def test_lr_schedules():
+    import math
+
+    from tensorgrad_b200.optim.lr_scheduler import CosineWarmupLR, LRScheduler, StepLR
+
+    opt = _Opt(0.1, 1.0)
+    sched = StepLR(opt, step_size=2, gamma=0.5)
+    seen = [sched.get_last_lr()]
+    for _ in range(4):
+        sched.step()
+        seen.append(sched.get_last_lr())
+    assert seen == [[0.1, 1.0], [0.1, 1.0], [0.05, 0.5], [0.05, 0.5], [0.025, 0.25]]
+    opt = _Opt(1.0)
+    cos = CosineWarmupLR(opt, warmup_steps=2, total_steps=6, min_lr_ratio=0.1)
+    got = [cos.factor(s) for s in range(8)]
+    want = [0.5, 1.0] + [0.1 + 0.9 * 0.5 * (1 + math.cos(math.pi * min(t / 4, 1.0)))
+                         for t in range(6)]
+    assert got == want and opt.param_groups[0].lr == 0.5
+    for bad in (dict(warmup_steps=3, total_steps=2), dict(warmup_steps=-1, total_steps=2),
+                dict(warmup_steps=0, total_steps=0)):
+        with pytest.raises(ValueError, match="warmup_steps"):
+            CosineWarmupLR(_Opt(1.0), **bad)
+    with pytest.raises(ValueError, match="min_lr_ratio"):
+        CosineWarmupLR(_Opt(1.0), 0, 5, min_lr_ratio=2.0)
+    with pytest.raises(ValueError, match="step_size"):
+        StepLR(_Opt(1.0), 0)
+    with pytest.raises(TypeError):
+        LRScheduler(_Opt(1.0))  # abstract
+
+
+def test_profile_self_times_and_table(monkeypatch):
+    from tensorgrad_b200 import device, profiler
+
+    monkeypatch.setattr(device, "synchronize", lambda: None)  # no device: host timing only
+
+    @profiler.profiled("outer")
+    def outer():
+        return inner() + 1
+
+    @profiler.profiled("inner")
+    def inner():
+        return 1
+
+    with profiler.profile() as prof:
+        assert outer() == 2
+        prof.timed("vjp", True, lambda: None)
+    assert prof.ops["outer"].forward_calls == prof.ops["inner"].forward_calls == 1
+    assert prof.ops["vjp"].backward_calls == 1 and prof.ops["vjp"].forward_calls == 0
+    assert prof.profiled_seconds <= prof.wall_seconds
+    lines = prof.table().splitlines()
+    assert lines[0].split() == ["op", "fwd", "calls", "fwd", "ms", "bwd", "calls", "bwd", "ms",
+                                "total", "ms", "share"]
+    assert set(lines[1]) == {"-"} and len(lines) == 6 and "wall time" in lines[-1]
+    assert len(prof.table(limit=1).splitlines()) == 4
+    assert profiler.active() is None
+    with pytest.raises(RuntimeError, match="nested"), profiler.profile(), profiler.profile():
+        pass
