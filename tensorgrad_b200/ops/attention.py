@@ -140,6 +140,38 @@ def _composite(q: Tensor, k: Tensor, v: Tensor, bias: Tensor | None, lse: Tensor
     return matmul(p, v)
 
 
+def _unfused_attention(tq: Tensor, tk: Tensor, tv: Tensor, causal: bool, mask: Any,
+                       dropout_p: float, training: bool,
+                       rng: np.random.Generator | None) -> Tensor:
+    """``softmax(q k^T / sqrt(d)`` with forbidden scores at ``-inf``) ``[* keep] v`` in
+    differentiable ops (matmul, masked_fill, softmax), for masks and value widths the fused
+    kernels do not take (ops/attention.py:52-90, 163-208)."""
+    from tensorgrad_b200.ops import elementwise as E
+    from tensorgrad_b200.ops.activation import softmax
+    from tensorgrad_b200.ops.linalg import matmul
+    from tensorgrad_b200.ops.shape import masked_fill, transpose
+
+    n_q, n_k, d = tq.shape[-2], tk.shape[-2], tq.shape[-1]
+    if tk.shape[-1] != d or tv.shape[-2] != n_k:
+        raise ValueError(f"attention: incompatible q {tq.shape}, k {tk.shape}, v {tv.shape}")
+    forbidden = None
+    if mask is not None:
+        m = mask.numpy() if isinstance(mask, Tensor) else mask
+        forbidden = np.asarray(m, dtype=np.bool_)
+    if causal:
+        cm = causal_mask(n_q, n_k)
+        forbidden = cm if forbidden is None else forbidden | cm
+    batch = tuple(np.broadcast_shapes(tq.shape[:-2], tk.shape[:-2]))
+    drop = _dropout_state((*batch, n_q, n_k), dropout_p, training, rng)
+    scores = E.mul(matmul(tq, transpose(tk, -1, -2)), 1.0 / math.sqrt(d))
+    if forbidden is not None:
+        scores = masked_fill(scores, forbidden, -np.inf)
+    weights = softmax(scores, -1)
+    if drop is not None:
+        weights = E.mul(weights, _keep_scaled((*batch, n_q, n_k), weights.dtype, drop))
+    return matmul(weights, tv)
+
+
 def _as_bhtd(shape: tuple[int, ...]) -> tuple[int, int]:
     """(B, H) of a ``(..., T, d)`` array: the batch axes collapse into B (and H = 1) unless
     there are exactly two."""
@@ -157,14 +189,17 @@ def scaled_dot_product_attention(
     """``softmax(q k^T / sqrt(d)) v`` over the last two axes, fused (ops/attention.py:163-208).
 
     ``q, k, v`` share their batch axes, or ``k``/``v`` broadcast over them (e.g. shared
-    across heads); their gradients are then summed back (ops/attention.py:211-213). An extra
-    boolean ``mask`` is not supported on the device. Dropout on the attention weights
-    (``training`` and ``dropout_p > 0``) uses the reference's keep-mask, generated on the
-    device from the global (or given) PCG64 generator and regenerated by the VJP.
+    across heads); their gradients are then summed back (ops/attention.py:211-213). Dropout
+    on the attention weights (``training`` and ``dropout_p > 0``) uses the reference's
+    keep-mask, generated on the device from the global (or given) PCG64 generator and
+    regenerated by the VJP. An extra boolean ``mask`` (broadcastable to the scores, ``True``
+    = forbidden, combined with ``causal``) or values of another width than the queries take
+    the unfused path: the same function in differentiable device ops, the scores
+    materialised.
     """
-    if mask is not None:
-        raise NotImplementedError("scaled_dot_product_attention: only the causal mask is fused")
     tq, tk, tv = as_tensor(q), as_tensor(k), as_tensor(v)
+    if mask is not None or tv.shape[-1] != tq.shape[-1]:
+        return _unfused_attention(tq, tk, tv, causal, mask, dropout_p, training, rng)
     dt = np.result_type(tq.dtype, tk.dtype, tv.dtype)
     qd, kd, vd = (t.data if t.dtype == dt else cast_array(t.data, dt) for t in (tq, tk, tv))
     batch = tuple(np.broadcast_shapes(tq.shape[:-2], tk.shape[:-2], tv.shape[:-2]))

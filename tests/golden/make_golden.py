@@ -345,7 +345,10 @@ def run_ops_extra() -> dict[str, np.ndarray]:
     def host(t):
         return np.array(t.data)
 
-    out = ops_extra_program(tg, types.SimpleNamespace(rnn=ref_ops.rnn), host, ops_extra_inputs())
+    from tensorgrad.ops.attention import scaled_dot_product_attention
+
+    O = types.SimpleNamespace(rnn=ref_ops.rnn, sdpa=scaled_dot_product_attention)
+    out = ops_extra_program(tg, O, host, ops_extra_inputs())
     loader = DataLoader(np.arange(10), batch_size=4, shuffle=True, seed=5)
     for epoch in range(2):
         out[f"loader_epoch{epoch}"] = np.concatenate([np.array(b.data) for (b,) in loader])

@@ -263,13 +263,16 @@ def ops_extra_inputs() -> dict[str, np.ndarray]:
         "bm_g": n((2, 5)),
         "ix": n((5, 4, 3)), "ix_rows": np.array([3, 0, 3, 1]), "ix_mask": rng.random((5, 4)) > 0.4,
         "ix_cols": np.array([2, 0, 2]), "ix_t": rng.integers(0, 4, size=5),
+        "aq": n((2, 2, 4, 3)), "ak": n((2, 2, 5, 3)), "av6": n((2, 2, 5, 6)),
+        "av3": n((2, 2, 5, 3)), "ag6": n((2, 2, 4, 6)), "ag3": n((2, 2, 4, 3)),
+        "amask": np.concatenate([np.zeros((4, 1), bool), rng.random((4, 4)) > 0.7], axis=1),
     }
 
 
 def ops_extra_program(tg, O, host, d: dict[str, np.ndarray]) -> dict[str, np.ndarray]:
     """Values and VJPs of the remaining ops, written once for both implementations: ``O``
-    holds ``rnn`` (the ops module's), everything else is the package's top level and Tensor
-    methods; ``host(t)`` a tensor's values as an array."""
+    holds ``rnn`` and ``sdpa`` (scaled_dot_product_attention), everything else is the
+    package's top level and Tensor methods; ``host(t)`` a tensor's values as an array."""
     T = tg.Tensor
     out: dict[str, np.ndarray] = {}
 
@@ -322,6 +325,15 @@ def ops_extra_program(tg, O, host, d: dict[str, np.ndarray]) -> dict[str, np.nda
                         ("tensor_rows", T(d["ix_rows"]))):
         y_ix = ix[index]
         vjp(f"index_{name}", y_ix, [ix], rng_g.standard_normal(y_ix.shape))
+    aq, ak = T(d["aq"], requires_grad=True), T(d["ak"], requires_grad=True)
+    av6, av3 = T(d["av6"], requires_grad=True), T(d["av3"], requires_grad=True)
+    vjp("attn_wide_values", O.sdpa(aq, ak, av6), [aq, ak, av6], d["ag6"])
+    vjp("attn_mask", O.sdpa(aq, ak, av3, mask=d["amask"]), [aq, ak, av3], d["ag3"])
+    vjp("attn_mask_causal", O.sdpa(aq, ak, av3, causal=True, mask=d["amask"]), [aq, ak, av3],
+        d["ag3"])
+    vjp("attn_mask_dropout", O.sdpa(aq, ak, av3, mask=d["amask"], dropout_p=0.25,
+                                    training=True, rng=np.random.default_rng(11)),
+        [aq, ak, av3], d["ag3"])
     pa, pb = T(d["w_a"]), T(d["w_b"])
     for op, fn in (("gt", lambda p, q: p > q), ("le", lambda p, q: p <= q),
                    ("eq", lambda p, q: p == q), ("ne_scalar", lambda p, q: p != 0.5)):

@@ -3,8 +3,9 @@
 ``specs.ops_extra_program``): softmax / log_softmax / logsumexp (also with ``-inf`` entries),
 max / min with tied extrema, where and masked_fill, concat, binary cross entropy with logits
 (every reduction, logits 0 and +-40), the Elman RNN (tanh and relu), matmul with vectors,
-comparisons and all / any / argmax. float64 at 1e-10, fp32 at 1e-4; boolean and index
-results exactly.
+comparisons and all / any / argmax, attention with a boolean mask (also with the causal mask
+and dropout) and with values wider than the keys. float64 at 1e-10, fp32 at 1e-4; boolean
+and index results exactly.
 """
 
 from __future__ import annotations
@@ -30,7 +31,8 @@ def test_extra_ops_match_reference(dtype, rel):
     d = {k: (v.astype(dtype) if v.dtype.kind == "f" else v) for k, v in ops_extra_inputs().items()}
     tg.set_default_dtype(dtype)
     try:
-        ours = ops_extra_program(tg, types.SimpleNamespace(rnn=ops.rnn), lambda t: t.numpy(), d)
+        O = types.SimpleNamespace(rnn=ops.rnn, sdpa=ops.scaled_dot_product_attention)
+        ours = ops_extra_program(tg, O, lambda t: t.numpy(), d)
     finally:
         tg.set_default_dtype(np.float32)
     assert set(ours) == {k for k in gold if not k.startswith("loader_")}
