@@ -22,9 +22,9 @@ namespace {
 
 constexpr int kThreads = 128;
 // Keys (forward, dQ) or queries (dK/dV) per shared-memory tile: two tiles of D-wide rows
-// stay within the 48 KB of static shared memory.
+// stay within the 48 KB of static shared memory (32 KB at most).
 template <typename T, int D>
-constexpr int kTileV = sizeof(T) * D >= 1024 ? 16 : 32;
+constexpr int kTileV = sizeof(T) * D >= 2048 ? 8 : (sizeof(T) * D >= 1024 ? 16 : 32);
 
 template <int TPR, typename T>
 __device__ __forceinline__ T group_sum(T v) {
@@ -325,8 +325,9 @@ int attn_forward_any(const AttnDims& p, const T* q, const T* k, const T* v, T* o
     case 32: return attn_forward_d<T, 32>(p, q, k, v, o, lse, s);
     case 64: return attn_forward_d<T, 64>(p, q, k, v, o, lse, s);
     case 128: return attn_forward_d<T, 128>(p, q, k, v, o, lse, s);
+    case 256: return attn_forward_d<T, 256>(p, q, k, v, o, lse, s);
   }
-  return set_error(TG_ERR_UNSUPPORTED, "attention: head_dim %lld (supported 8/16/32/64/128)",
+  return set_error(TG_ERR_UNSUPPORTED, "attention: head_dim %lld (supported 8/16/32/64/128/256)",
                    (long long)p.D);
 }
 
@@ -340,21 +341,24 @@ int attn_backward_any(const AttnDims& p, const T* q, const T* k, const T* v, con
     case 32: return attn_backward_d<T, 32>(p, q, k, v, o, lse, dout, dq, dk, dv, delta, s);
     case 64: return attn_backward_d<T, 64>(p, q, k, v, o, lse, dout, dq, dk, dv, delta, s);
     case 128: return attn_backward_d<T, 128>(p, q, k, v, o, lse, dout, dq, dk, dv, delta, s);
+    case 256: return attn_backward_d<T, 256>(p, q, k, v, o, lse, dout, dq, dk, dv, delta, s);
   }
-  return set_error(TG_ERR_UNSUPPORTED, "attention: head_dim %lld (supported 8/16/32/64/128)",
+  return set_error(TG_ERR_UNSUPPORTED, "attention: head_dim %lld (supported 8/16/32/64/128/256)",
                    (long long)p.D);
 }
 
-// Head sizes without kernels of their own (up to 128) run on the next wider kernel over
+// Head sizes without kernels of their own (up to 256) run on the next wider kernel over
 // zero-padded contiguous copies: zero features add nothing to q.k, the padded value columns
 // give output features that are dropped, and the scale stays 1/sqrt(head_dim).
 int64_t padded_head(int64_t d) {
-  for (int64_t w : {8, 16, 32, 64, 128})
+  for (int64_t w : {8, 16, 32, 64, 128, 256})
     if (d <= w) return w;
   return 0;
 }
 
-bool native_head(int64_t d) { return d == 8 || d == 16 || d == 32 || d == 64 || d == 128; }
+bool native_head(int64_t d) {
+  return d == 8 || d == 16 || d == 32 || d == 64 || d == 128 || d == 256;
+}
 
 constexpr int kPadThreads = 256;
 
@@ -528,7 +532,7 @@ int tg_attention_forward(int dtype, const tg_attn_shape* s, const void* q, const
   const AttnDims p = make_dims(s);
   if (!native_head(s->head_dim)) {
     if (padded_head(s->head_dim) == 0)
-      return set_error(TG_ERR_UNSUPPORTED, "attention: head_dim %lld (at most 128 here)",
+      return set_error(TG_ERR_UNSUPPORTED, "attention: head_dim %lld (at most 256 here)",
                        (long long)s->head_dim);
     TG_CHECK_ARG(scratch, "attention_forward: NULL scratch");
     return TG_DISPATCH_FLOAT(dtype, T, [&] {
@@ -563,7 +567,7 @@ int tg_attention_backward(int dtype, const tg_attn_shape* s, const void* q, cons
   const AttnDims p = make_dims(s);
   if (!native_head(s->head_dim)) {
     if (padded_head(s->head_dim) == 0)
-      return set_error(TG_ERR_UNSUPPORTED, "attention: head_dim %lld (at most 128 here)",
+      return set_error(TG_ERR_UNSUPPORTED, "attention: head_dim %lld (at most 256 here)",
                        (long long)s->head_dim);
     return TG_DISPATCH_FLOAT(dtype, T, [&] {
       // delta (B H Tq) first, the padded copies from the next 256-byte boundary.

@@ -415,7 +415,9 @@ def test_fused_attention_forward_shapes(dtype, qshape, tk, causal):
                                               ((2, 1, 9, 12), 11, False),
                                               ((1, 2, 5, 4), 8, True),
                                               ((1, 1, 13, 100), 13, True),
-                                              ((2, 2, 6, 3), 6, False)])
+                                              ((2, 2, 6, 3), 6, False),
+                                              ((1, 1, 5, 200), 7, True),
+                                              ((1, 2, 9, 256), 9, False)])
 def test_attention_other_head_sizes(dtype, qshape, tk, causal):
     import tensorgrad_b200 as tg
 
