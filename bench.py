@@ -126,8 +126,7 @@ class Built:
     dev_inputs: tuple             # inputs already in device memory
     pinned_inputs: tuple          # the same inputs in page-locked host memory
     h2d_bytes: int
-    d2h_bytes: int
-    readback: Any                 # readback(result) -> host value (the e2e read of the result)
+    d2h_bytes: int                # bytes of the result read back per step (e2e)
     params: list = field(default_factory=list)
 
 
@@ -159,6 +158,53 @@ def _train_step(tg, model_fn, params, loss_fn, reducer, clip: float | None):
         return loss
 
     return step
+
+
+class _AsyncReadback:
+    """The end-to-end read of each step's result without a blocking wait: right after the
+    step, one asynchronous device-to-host copy per result tensor into page-locked buffers
+    (two sets, used in turn) with an event behind them. A set is reused only after its event
+    (two steps back) has completed, and the values are taken once the timed region has been
+    synchronised. With a blocking read the host could queue the next step only after the
+    device had finished this one; here it queues it while the device works."""
+
+    def __init__(self, lib, device) -> None:
+        self.lib, self.device = lib, device
+        self.buffers: list = [None, None]
+        self.events: list = [None, None]
+        self.turn = 0
+        self.last = None
+
+    def issue(self, result) -> None:
+        import time
+
+        tensors = list(result) if isinstance(result, (list, tuple)) else [result]
+        i = self.turn % 2
+        self.turn += 1
+        if self.events[i] is not None:
+            while not self.events[i].query():
+                time.sleep(0)
+        if self.buffers[i] is None:
+            self.buffers[i] = [self.device.pinned_empty(t.shape, t.dtype) for t in tensors]
+        for t, buf in zip(tensors, self.buffers[i], strict=True):
+            data = t.data
+            if data.nbytes:
+                rc = self.lib.tg_memcpy_d2h(buf.ctypes.data, data.ptr, data.nbytes,
+                                            self.device.stream())
+                if rc:
+                    raise RuntimeError(f"device-to-host copy failed ({rc})")
+        if self.events[i] is None:
+            self.events[i] = self.device._Event()
+        self.events[i].record()
+        self.last = i
+
+    def value(self):
+        """The last result's host values (a float for a one-element result); call after the
+        stream has been synchronised."""
+        if self.last is None:
+            return None
+        bufs = self.buffers[self.last]
+        return float(bufs[0].reshape(-1)[0]) if len(bufs) == 1 and bufs[0].size == 1 else None
 
 
 def _pinned(device, arrays):
@@ -196,7 +242,7 @@ class GPTWorkload(Workload):
         ids = rng.integers(0, v, size=(self.batch, self.seq), dtype=np.int64)
         tgt = rng.integers(0, v, size=(self.batch, self.seq), dtype=np.int64)
         return Built(step, (tg.Tensor(ids), tg.Tensor(tgt)), _pinned(device, (ids, tgt)),
-                     ids.nbytes + tgt.nbytes, 4, lambda loss: loss.item(), params)
+                     ids.nbytes + tgt.nbytes, 4, params)
 
     def cpu_step(self, threads: int):
         import numpy as np
@@ -245,9 +291,7 @@ class MHAWorkload(Workload):
 
         dev = tuple(tg.Tensor(a, requires_grad=i < 3) for i, a in enumerate(arrays))
         nbytes = arrays[0].nbytes
-        outs = [device.pinned_empty(self.SHAPE, np.float32) for _ in range(3)]
-        return Built(step, dev, _pinned(device, arrays), 4 * nbytes, 3 * nbytes,
-                     lambda grads: [g.numpy(out=o) for g, o in zip(grads, outs, strict=True)])
+        return Built(step, dev, _pinned(device, arrays), 4 * nbytes, 3 * nbytes)
 
     def cpu_step(self, threads: int):
         import numpy as np
@@ -298,7 +342,7 @@ class CNNWorkload(Workload):
         x, labels = ocnn.synthetic_batch(cfg, 256, 100 + rank)
         x = x.astype(np.float32)
         return Built(step, (tg.Tensor(x), tg.Tensor(labels)), _pinned(device, (x, labels)),
-                     x.nbytes + labels.nbytes, 4, lambda loss: loss.item(), params)
+                     x.nbytes + labels.nbytes, 4, params)
 
     def cpu_step(self, threads: int):
         import numpy as np
@@ -361,7 +405,7 @@ class RNNWorkload(Workload):
         x, y = ornn.synthetic_batch(cfg, 512, 200 + rank)
         x, y = x.astype(np.float32), y.astype(np.float32)
         return Built(step, (tg.Tensor(x), tg.Tensor(y)), _pinned(device, (x, y)),
-                     x.nbytes + y.nbytes, 4, lambda loss: loss.item(), params)
+                     x.nbytes + y.nbytes, 4, params)
 
     def cpu_step(self, threads: int):
         import numpy as np
@@ -782,13 +826,17 @@ def run_ours(args: argparse.Namespace, wl: Workload) -> None:
     gms, gl, gfl = ctypes.c_double(), ctypes.c_int64(), ctypes.c_double()
     lib.tg_gemm_profile_read(ctypes.byref(gms), ctypes.byref(gl), ctypes.byref(gfl))
 
-    # End to end: pinned host inputs uploaded inside the step, the result read back.
+    # End to end: pinned host inputs uploaded inside the step, every step's result copied
+    # back to page-locked host memory inside the timed region (without blocking the host).
+    reader = _AsyncReadback(lib, device)
+
     def e2e_step():
-        results.append(built.readback(built.step(*built.pinned_inputs)))
+        reader.issue(built.step(*built.pinned_inputs))
 
     for _ in range(args.warmup):
         e2e_step()
     sec_e2e = timed(args.steps, e2e_step)
+    results.append(reader.value())
 
     units = wl.units_per_step * world
     pk = peaks()

@@ -287,24 +287,16 @@ def _batch_norm_train(x: Tensor, running_mean: DeviceArray | None,
     return make_result(y, parents, backward, "batch_norm", graph)
 
 
-def _segments(ids: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
-    """Stable argsort of the ids and the runs of equal ids in it (ops/layers.py:192-206)."""
-    order = np.argsort(ids, kind="stable")
-    sorted_ids = ids[order]
-    starts = np.flatnonzero(np.concatenate(([True], sorted_ids[1:] != sorted_ids[:-1])))
-    seg_start = np.append(starts, ids.size).astype(np.int64)
-    return order.astype(np.int64), seg_start, sorted_ids[starts].astype(np.int64)
-
-
 @profiled("embedding")
 def embedding(indices: Any, weight: Any) -> Tensor:
     """Row lookup; the VJP is a scatter-add in the reference's sorted order
     (ops/layers.py:209-232).
 
-    Host ids are checked before any device work, as the reference checks them, and sorted on
-    the host. Device-resident ids (a Tensor or DeviceArray) stay on the device: the gather
-    checks them (an out-of-range id raises IndexError at the next host synchronisation) and
-    the VJP sorts them on the device, so the step needs no host round trip."""
+    Host ids are checked before any device work, as the reference checks them, then uploaded.
+    Device-resident ids (a Tensor or DeviceArray) stay on the device: the gather checks them
+    (an out-of-range id raises IndexError at the next host synchronisation). Either way the
+    VJP sorts the ids on the device (keys ``id * n + position``: the reference's stable
+    order) and sums each run of equal ids, so the step needs no host work per call."""
     tw = as_tensor(weight)
     num, dim = tw.shape
     wd = tw.data
@@ -320,19 +312,7 @@ def embedding(indices: Any, weight: Any) -> Tensor:
                                        device.async_error_word(device.ASYNC_EMBEDDING_ID),
                                        device.stream()), "embedding")
 
-        def scatter_dev(g: DeviceArray) -> DeviceArray:
-            scr = device.scratch(lib.tg_embedding_sort_scratch_bytes(n, num))
-            keys = device.empty((n,), np.int64)  # uint64 sort keys
-            check(lib.tg_embedding_sort(ids_dev.ptr, n, num, keys.ptr, None, scr.ptr,
-                                        scr.nbytes, device.stream()), "embedding sort")
-            gw = device.empty((num, dim), g.dtype)
-            check(lib.tg_embedding_backward_sorted(dtype_code(g.dtype), g.ptr, keys.ptr, n,
-                                                   gw.ptr, num, dim, 0, device.stream()),
-                  "embedding backward")
-            return gw
-
-        rows = _Rows(ids_dev, shape, num, dim,
-                     device.async_error_word(device.ASYNC_EMBEDDING_ID), scatter_dev)
+        rows = _Rows(ids_dev, shape, num, dim, device.async_error_word(device.ASYNC_EMBEDDING_ID))
         return make_result(out, (tw,), rows.backward, "embedding", rows.graph)
     idx = np.asarray(indices)
     if not np.issubdtype(idx.dtype, np.integer):
@@ -344,23 +324,9 @@ def embedding(indices: Any, weight: Any) -> Tensor:
 
 
 def host_rows(idx: np.ndarray, num: int, dim: int) -> _Rows:
-    """``_Rows`` for checked host ids: uploaded once; the scatter-add sorts them on the host
-    (the reference's stable order) and sums each run of equal ids on the device."""
+    """``_Rows`` for host ids already checked against ``num``: uploaded once."""
     flat = np.ascontiguousarray(idx.reshape(-1), dtype=np.int64)
-    ids_host = device.from_numpy(flat)
-
-    def scatter_host(g: DeviceArray) -> DeviceArray:
-        order, seg_start, seg_id = _segments(flat)
-        packed = device.from_numpy(np.concatenate([order, seg_start, seg_id]))
-        n, ns = order.size, seg_id.size
-        base = packed.ptr
-        gw = device.empty((num, dim), g.dtype)
-        check(lib.tg_embedding_backward(dtype_code(g.dtype), g.ptr, base, base + 8 * n,
-                                        base + 8 * (n + ns + 1), ns, gw.ptr, num, dim, 0,
-                                        device.stream()), "embedding backward")
-        return gw
-
-    return _Rows(ids_host, idx.shape, num, dim, None, scatter_host)
+    return _Rows(device.from_numpy(flat), idx.shape, num, dim, None)
 
 
 class _Rows:
@@ -369,9 +335,23 @@ class _Rows:
     (the reference's graph VJP is its ``scatter_add`` op, ops/layers.py:229-232)."""
 
     def __init__(self, ids: DeviceArray, shape: tuple[int, ...], num: int, dim: int,
-                 err_word: Any, scatter_array: Any) -> None:
+                 err_word: Any) -> None:
         self.ids, self.shape, self.num, self.dim = ids, tuple(shape), num, dim
-        self.err_word, self.scatter_array = err_word, scatter_array
+        self.err_word = err_word
+
+    def scatter_array(self, g: DeviceArray) -> DeviceArray:
+        """``gw[num, dim]`` with row ``i`` of ``g`` added into row ``ids[i]``, in the stable
+        id order (a device sort of the keys ``id * n + position``)."""
+        n, num, dim = self.ids.size, self.num, self.dim
+        scr = device.scratch(lib.tg_embedding_sort_scratch_bytes(n, num))
+        keys = device.empty((n,), np.int64)  # uint64 sort keys
+        check(lib.tg_embedding_sort(self.ids.ptr, n, num, keys.ptr, None, scr.ptr, scr.nbytes,
+                                    device.stream()), "embedding sort")
+        gw = device.empty((num, dim), g.dtype)
+        check(lib.tg_embedding_backward_sorted(dtype_code(g.dtype), g.ptr, keys.ptr, n, gw.ptr,
+                                               num, dim, 0, device.stream()),
+              "embedding backward")
+        return gw
 
     def gather_array(self, u: DeviceArray) -> DeviceArray:
         out = device.empty((*self.shape, self.dim), u.dtype)

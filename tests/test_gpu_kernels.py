@@ -346,6 +346,32 @@ def test_cross_entropy_device_targets(dtype):
                   rel(dtype), "ce grad")
 
 
+def test_embedding_backward_from_host_segments():
+    """``tg_embedding_backward`` (the scatter-add in the order of a host-side stable argsort,
+    for FFI hosts that sort themselves) against NumPy's ``add.at``; the package's own VJP sorts
+    on the device and is covered by the GPT parity tests."""
+    from tensorgrad_b200 import device
+    from tensorgrad_b200._lib import F32, F64, check, lib
+
+    rng = np.random.default_rng(21)
+    ids = rng.integers(0, 7, size=40)
+    for np_dt, code, tol in ((np.float32, F32, 1e-6), (np.float64, F64, 1e-14)):
+        g = rng.standard_normal((40, 5)).astype(np_dt)
+        order = np.argsort(ids, kind="stable")
+        sorted_ids = ids[order]
+        starts = np.flatnonzero(np.concatenate(([True], sorted_ids[1:] != sorted_ids[:-1])))
+        seg_start = np.append(starts, ids.size).astype(np.int64)
+        seg_id = sorted_ids[starts].astype(np.int64)
+        dg, d_order = device.from_numpy(g), device.from_numpy(order.astype(np.int64))
+        d_start, d_id = device.from_numpy(seg_start), device.from_numpy(seg_id)
+        gw = device.empty((7, 5), np_dt)
+        check(lib.tg_embedding_backward(code, dg.ptr, d_order.ptr, d_start.ptr, d_id.ptr,
+                                        seg_id.size, gw.ptr, 7, 5, 0, device.stream()))
+        ref = np.zeros((7, 5))
+        np.add.at(ref, ids, g.astype(np.float64))
+        assert_parity(gw.numpy(), ref, tol, f"segment scatter-add {np.dtype(np_dt).name}")
+
+
 # ------------------------------------------------------------------------------- attention
 @pytest.mark.parametrize("shape,causal,seed", ATTN_CASES)
 def test_attention_matches_reference_fixture(dtype, shape, causal, seed):
