@@ -43,6 +43,18 @@ def make_result(data: DeviceArray, parents: tuple[Tensor, ...], backward: Backwa
     return out
 
 
+def grad_buffer(t: Tensor | None, shape: tuple[int, ...], dtype: Any) -> DeviceArray:
+    """Where a VJP writes the gradient of parent ``t``: the leaf's arena slot when it can take
+    the gradient directly (``Tensor._grad_target``; saves a buffer and a copy per parameter
+    and step), else a new buffer. The caller must write every element."""
+    if (t is not None and t._node is None and t._grad_slot is not None
+            and tuple(shape) == t.shape and np.dtype(dtype) == t.dtype):
+        slot = t._grad_target()
+        if slot is not None:
+            return slot
+    return device.empty(shape, dtype)
+
+
 def constant(data: DeviceArray) -> Tensor:
     """A tensor outside every graph (masks and saved values inside graph VJPs)."""
     return Tensor._wrap(data)

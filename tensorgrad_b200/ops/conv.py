@@ -24,7 +24,7 @@ import numpy as np
 from tensorgrad_b200 import device
 from tensorgrad_b200._lib import ConvShape, check, lib
 from tensorgrad_b200.device import DeviceArray, dtype_code
-from tensorgrad_b200.ops._util import Need, as_tensor, make_result
+from tensorgrad_b200.ops._util import Need, as_tensor, grad_buffer, make_result
 from tensorgrad_b200.ops import reduce
 from tensorgrad_b200.ops.elementwise import cast_array
 from tensorgrad_b200.profiler import profiled
@@ -144,8 +144,8 @@ def conv2d(x: Any, weight: Any, bias: Any = None, stride: IntPair = 1,
     def backward(g: DeviceArray, need: Need) -> tuple[DeviceArray | None, ...]:
         g = _cast(g, xd.dtype)
         gx = device.empty(tx.shape, xd.dtype) if need[0] else None
-        gw = device.empty(tw.shape, xd.dtype) if need[1] else None
-        gb = device.empty((c_out,), xd.dtype) if tb is not None and need[2] else None
+        gw = grad_buffer(tw, tw.shape, xd.dtype) if need[1] else None
+        gb = grad_buffer(tb, (c_out,), xd.dtype) if tb is not None and need[2] else None
         scr = device.scratch(lib.tg_conv2d_backward_scratch_bytes(code, ref, int(gx is not None)))
         check(lib.tg_conv2d_backward(
             code, ref, g.ptr, cols.ptr, wd.ptr, gx.ptr if gx is not None else None,

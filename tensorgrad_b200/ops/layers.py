@@ -14,7 +14,7 @@ from tensorgrad_b200._random import dropout_threshold, get_rng, keep_mask, pcg64
 from tensorgrad_b200.autograd import no_grad
 from tensorgrad_b200.device import DeviceArray, dtype_code
 from tensorgrad_b200.ops import elementwise, reduce
-from tensorgrad_b200.ops._util import Need, as_tensor, constant, make_result
+from tensorgrad_b200.ops._util import Need, as_tensor, constant, grad_buffer, make_result
 from tensorgrad_b200.ops.elementwise import binary_array, cast_array
 from tensorgrad_b200.profiler import profiled
 from tensorgrad_b200.tensor import Tensor
@@ -55,8 +55,8 @@ def linear(x: Any, weight: Any, bias: Any = None) -> Tensor:
         if g.dtype != xd.dtype:
             g = cast_array(g, xd.dtype)
         gx = device.empty(tx.shape, xd.dtype) if need[0] else None
-        gw = device.empty(tw.shape, xd.dtype) if need[1] else None
-        gb = device.empty((out_f,), xd.dtype) if has_bias and need[2] else None
+        gw = grad_buffer(tw, tw.shape, xd.dtype) if need[1] else None
+        gb = grad_buffer(tb, (out_f,), xd.dtype) if has_bias and need[2] else None
         mask = (1 if gx is not None else 0) | (2 if gw is not None else 0) | (4 if gb is not None else 0)
         scratch = device.scratch(lib.tg_linear_backward_scratch_bytes(code, rows, in_f, out_f,
                                                                       mask))
@@ -118,8 +118,8 @@ def layer_norm(x: Any, weight: Any = None, bias: Any = None, eps: float = 1e-5) 
         if tb is not None:
             need_b = need[k]
         gx = device.empty(tx.shape, xd.dtype) if need[0] else None
-        gw = device.empty((cols,), xd.dtype) if need_w else None
-        gb = device.empty((cols,), xd.dtype) if need_b else None
+        gw = grad_buffer(tw, (cols,), xd.dtype) if need_w else None
+        gb = grad_buffer(tb, (cols,), xd.dtype) if need_b else None
         mask = (1 if gx is not None else 0) | (2 if gw is not None else 0) | (4 if gb is not None else 0)
         scratch = (device.scratch(lib.tg_layer_norm_scratch_bytes(code, rows, cols))
                    if (gw is not None or gb is not None) else None)
@@ -263,8 +263,10 @@ def _batch_norm_train(x: Tensor, running_mean: DeviceArray | None,
         if bias is not None:
             need_b = need[k]
         gx = device.empty(x.shape, xd.dtype) if need[0] else None
-        gw = device.empty((c,), xd.dtype) if need_w else None
-        gb = device.empty((c,), xd.dtype) if need_b else None
+        gw = grad_buffer(weight, (c,), xd.dtype) if need_w and weight.shape == (c,) else (
+            device.empty((c,), xd.dtype) if need_w else None)
+        gb = grad_buffer(bias, (c,), xd.dtype) if need_b and bias.shape == (c,) else (
+            device.empty((c,), xd.dtype) if need_b else None)
         scr = device.scratch(lib.tg_batch_norm_scratch_bytes(code, n, c, hw))
         check(lib.tg_batch_norm_backward(
             code, n, c, hw, g.ptr, xd.ptr, wd.ptr if wd is not None else None, mean.ptr,
@@ -312,7 +314,8 @@ def embedding(indices: Any, weight: Any) -> Tensor:
                                        device.async_error_word(device.ASYNC_EMBEDDING_ID),
                                        device.stream()), "embedding")
 
-        rows = _Rows(ids_dev, shape, num, dim, device.async_error_word(device.ASYNC_EMBEDDING_ID))
+        rows = _Rows(ids_dev, shape, num, dim, device.async_error_word(device.ASYNC_EMBEDDING_ID),
+                     target=tw)
         return make_result(out, (tw,), rows.backward, "embedding", rows.graph)
     idx = np.asarray(indices)
     if not np.issubdtype(idx.dtype, np.integer):
@@ -320,6 +323,7 @@ def embedding(indices: Any, weight: Any) -> Tensor:
     if idx.size and (idx.min() < 0 or idx.max() >= num):
         raise IndexError(f"embedding ids must be in [0, {num}), got {idx.min()}..{idx.max()}")
     rows = host_rows(idx, num, dim)
+    rows.target = tw
     return make_result(rows.gather_array(wd), (tw,), rows.backward, "embedding", rows.graph)
 
 
@@ -335,19 +339,21 @@ class _Rows:
     (the reference's graph VJP is its ``scatter_add`` op, ops/layers.py:229-232)."""
 
     def __init__(self, ids: DeviceArray, shape: tuple[int, ...], num: int, dim: int,
-                 err_word: Any) -> None:
+                 err_word: Any, target: Tensor | None = None) -> None:
         self.ids, self.shape, self.num, self.dim = ids, tuple(shape), num, dim
         self.err_word = err_word
+        self.target = target  # the table whose VJP this is (its gradient may go to its slot)
 
-    def scatter_array(self, g: DeviceArray) -> DeviceArray:
-        """``gw[num, dim]`` with row ``i`` of ``g`` added into row ``ids[i]``, in the stable
-        id order (a device sort of the keys ``id * n + position``)."""
+    def scatter_array(self, g: DeviceArray, out: DeviceArray | None = None) -> DeviceArray:
+        """``gw[num, dim]`` (into ``out`` when given) with row ``i`` of ``g`` added into row
+        ``ids[i]``, in the stable id order (a device sort of the keys ``id * n + position``);
+        every row is written (zeros where no id points)."""
         n, num, dim = self.ids.size, self.num, self.dim
         scr = device.scratch(lib.tg_embedding_sort_scratch_bytes(n, num))
         keys = device.empty((n,), np.int64)  # uint64 sort keys
         check(lib.tg_embedding_sort(self.ids.ptr, n, num, keys.ptr, None, scr.ptr, scr.nbytes,
                                     device.stream()), "embedding sort")
-        gw = device.empty((num, dim), g.dtype)
+        gw = device.empty((num, dim), g.dtype) if out is None else out
         check(lib.tg_embedding_backward_sorted(dtype_code(g.dtype), g.ptr, keys.ptr, n, gw.ptr,
                                                num, dim, 0, device.stream()),
               "embedding backward")
@@ -361,7 +367,9 @@ class _Rows:
         return out
 
     def backward(self, g: DeviceArray, need: Need) -> tuple[DeviceArray]:
-        return (self.scatter_array(g),)
+        out = None if self.target is None else grad_buffer(self.target, (self.num, self.dim),
+                                                           g.dtype)
+        return (self.scatter_array(g, out),)
 
     def graph(self, g: Tensor, y: Tensor, need: Need) -> tuple[Tensor]:
         return (self.scatter(g),)

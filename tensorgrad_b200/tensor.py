@@ -84,7 +84,7 @@ class Tensor:
 
     __slots__ = (
         "__weakref__", "_arena", "_grad", "_grad_slot", "_node", "_requires_grad", "_retains_grad",
-        "data",
+        "_slot_taken", "data",
     )
 
     __array_ufunc__ = None
@@ -99,6 +99,7 @@ class Tensor:
         self._node: Node | None = None
         self._retains_grad = False
         self._requires_grad = False
+        self._slot_taken = False
         self.requires_grad = requires_grad
 
     @classmethod
@@ -111,6 +112,7 @@ class Tensor:
         out._node = None
         out._retains_grad = False
         out._requires_grad = False
+        out._slot_taken = False
         return out
 
     # ------------------------------------------------------------------ properties
@@ -187,7 +189,21 @@ class Tensor:
             return
         _autograd.backward(self, grad, retain_graph=retain_graph, create_graph=create_graph)
 
+    def _grad_target(self) -> DeviceArray | None:
+        """This leaf's arena slot, for a VJP to write the leaf's gradient into directly: only
+        while the slot holds no gradient of this pass (``.grad`` is None), no other VJP has
+        taken it, and no clip factor is pending on the arena. The VJP writes the whole slot;
+        ``_accumulate_grad`` then finds the gradient in place and copies nothing."""
+        slot = self._grad_slot
+        if slot is None or self._grad is not None or self._slot_taken:
+            return None
+        if self._arena is not None and self._arena.pending_clip is not None:
+            return None
+        self._slot_taken = True
+        return slot
+
     def _accumulate_grad(self, g: DeviceArray) -> None:
+        self._slot_taken = False
         if g.dtype != self.dtype:
             g = g.astype(self.dtype)
         slot = self._grad_slot
@@ -199,7 +215,8 @@ class Tensor:
 
             cur = self._grad
             if cur is None:
-                _device.copy_into(slot, g)
+                if not (g._buf is slot._buf and g._off == slot._off):
+                    _device.copy_into(slot, g)
             elif cur.data is slot:
                 binary_array(slot, g, 0, out=slot)
             else:
@@ -219,6 +236,7 @@ class Tensor:
 
     def zero_grad(self) -> None:
         self._grad = None
+        self._slot_taken = False
 
     def detach(self) -> Tensor:
         return Tensor._wrap(self.data)
