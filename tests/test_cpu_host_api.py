@@ -183,3 +183,31 @@ def test_profile_self_times_and_table(monkeypatch):
     assert profiler.active() is None
     with pytest.raises(RuntimeError, match="nested"), profiler.profile(), profiler.profile():
         pass
+
+
+def test_gradient_slot_is_handed_out_once_per_pass():
+    """A VJP may write a parameter's gradient straight into its arena slot only while the slot
+    holds no gradient of this pass, nobody else took it, and no clip factor is pending; the
+    claim ends when the engine accumulates the gradient or on zero_grad (host logic only)."""
+    from tensorgrad_b200.ops._util import grad_buffer
+
+    class _Arena:
+        pending_clip = None
+
+    slot = _Meta((2, 3))
+    p = _leaf((2, 3), True)
+    p._grad_slot, p._arena = slot, _Arena()
+    assert p._grad_target() is slot
+    assert p._grad_target() is None  # taken: a second contribution gets a buffer of its own
+    p.zero_grad()
+    assert p._grad_target() is slot
+    p.zero_grad()
+    p._arena.pending_clip = 0.5
+    assert p._grad_target() is None
+    p._arena.pending_clip = None
+    p._grad = _leaf((2, 3), False)  # a gradient from an earlier pass: accumulate, not overwrite
+    assert p._grad_target() is None
+    p._grad = None
+    assert grad_buffer(p, (2, 3), np.float64) is slot
+    q = _leaf((2, 3), True)
+    assert q._grad_target() is None  # no arena slot
