@@ -313,3 +313,47 @@ def adamw_update(
     denom = np.sqrt(v) / math.sqrt(bc2) + eps
     p -= (lr / bc1) * m / denom
     return p, m, v
+
+
+# ---------------------------------------------------------------------------- softmax family
+def _row_shift(x: np.ndarray, axis: int) -> np.ndarray:
+    m = x.max(axis=axis, keepdims=True)
+    return np.where(np.isfinite(m), m, 0.0)
+
+
+def softmax_forward(x: np.ndarray, axis: int = -1) -> np.ndarray:
+    """``exp(x - m) / sum(exp(x - m))`` (ops/activation.py:27-45)."""
+    e = np.exp(x - _row_shift(x, axis))
+    return e / e.sum(axis=axis, keepdims=True)
+
+
+def softmax_backward(g: np.ndarray, s: np.ndarray, axis: int = -1) -> np.ndarray:
+    """``s (g - sum(g s))`` (ops/activation.py:36-37)."""
+    return s * (g - (g * s).sum(axis=axis, keepdims=True))
+
+
+def logsumexp_forward(x: np.ndarray, axis: int = -1) -> np.ndarray:
+    """``log(sum(exp(x - m))) + m`` with the reduced axis kept (ops/activation.py:75-86)."""
+    m = _row_shift(x, axis)
+    return np.log(np.exp(x - m).sum(axis=axis, keepdims=True)) + m
+
+
+def extremum_backward(g_kept: np.ndarray, x: np.ndarray, kept: np.ndarray,
+                      axes: tuple[int, ...]) -> np.ndarray:
+    """Tied extrema share the gradient equally (ops/reduce.py:78-85); ``g_kept`` and ``kept``
+    have the reduced axes kept."""
+    winners = (x == kept).astype(np.float64)
+    return g_kept * winners / winners.sum(axis=axes, keepdims=True)
+
+
+def bce_with_logits_forward(z: np.ndarray, y: np.ndarray) -> np.ndarray:
+    """Per-element ``max(z, 0) - z y + log1p(exp(-|z|))`` (ops/loss.py:115-118)."""
+    return np.maximum(z, 0.0) - z * y + np.log1p(np.exp(-np.abs(z)))
+
+
+def bce_with_logits_backward(up: np.ndarray, z: np.ndarray,
+                             y: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """``(sigmoid(z) - y) up`` and ``-z up`` (ops/loss.py:128-135)."""
+    e = np.exp(-np.abs(z))
+    sig = np.where(z >= 0, 1.0 / (1.0 + e), e / (1.0 + e))
+    return (sig - y) * up, -z * up

@@ -136,6 +136,35 @@ def gru_backward(g, x, h0, w_ih, w_hh, has_bias, out, cache):
     return dx, dh, dw_ih, dw_hh, db_ih, db_hh
 
 
+# ---------------------------------------------------------------------------- Elman RNN
+def rnn_forward(x, h0, w_ih, w_hh, b_ih=None, b_hh=None, relu=False):
+    """``h_t = act(x_t W_ih^T + b_ih + h_{t-1} W_hh^T + b_hh)``, ``(T, B, H)``
+    (ops/recurrent.py:140-181)."""
+    steps, batch = x.shape[0], x.shape[1]
+    out = (x.reshape(-1, x.shape[2]) @ w_ih.T).reshape(steps, batch, -1)
+    if b_ih is not None:
+        out = out + b_ih + b_hh
+    h = h0
+    for t in range(steps):
+        a = out[t] + h @ w_hh.T
+        out[t] = np.maximum(a, 0.0) if relu else np.tanh(a)
+        h = out[t]
+    return out
+
+
+def rnn_backward(g, x, h0, w_ih, w_hh, has_bias, out, relu=False):
+    """BPTT of :func:`rnn_forward`: ``(dx, dh0, dw_ih, dw_hh, db_ih, db_hh)``
+    (ops/recurrent.py:183-193)."""
+    dz = np.empty_like(out)
+    dh = np.zeros_like(h0)
+    for t in range(out.shape[0] - 1, -1, -1):
+        dh = dh + g[t]
+        dz[t] = dh * (out[t] > 0) if relu else dh * (1.0 - out[t] * out[t])
+        dh = dz[t] @ w_hh
+    dx, dw_ih, dw_hh, db_ih, db_hh = _param_grads(dz, dz, x, _previous(h0, out), w_ih, has_bias)
+    return dx, dh, dw_ih, dw_hh, db_ih, db_hh
+
+
 # ---------------------------------------------------------------------------- model
 @dataclass(frozen=True)
 class Config:

@@ -252,3 +252,50 @@ def test_recurrent_regressor_two_steps_match_reference_fixture(cell) -> None:
         for name, p in out["params"].items():
             assert_parity(p, gold[f"{cell}/step{step}/param/{name}"], REL64, f"step{step} {name}")
         params, state = out["params"], out["state"]
+
+
+def test_extra_ops_oracle_matches_reference_fixture() -> None:
+    """The oracle's softmax family, tie-sharing max / min, binary cross entropy and Elman RNN
+    against the reference's own outputs (ops_extra.npz), float64 at 1e-10."""
+    from tests.golden.specs import ops_extra_inputs
+
+    gold = load_golden("ops_extra.npz")
+    d = ops_extra_inputs()
+    x, g = d["s_x"], d["s_g"]
+    s = ops.softmax_forward(x, -1)
+    assert_parity(s, gold["softmax/y"], 1e-10, "softmax")
+    assert_parity(ops.softmax_backward(g, s, -1), gold["softmax/g0"], 1e-10, "softmax vjp")
+    s1 = ops.softmax_forward(x, 1)
+    assert_parity(ops.softmax_backward(g, s1, 1), gold["softmax_ax1/g0"], 1e-10, "softmax ax1")
+    ls = ops.log_softmax(x, -1)
+    assert_parity(ls, gold["log_softmax/y"], 1e-10, "log_softmax")
+    assert_parity(g - np.exp(ls) * g.sum(-1, keepdims=True), gold["log_softmax/g0"], 1e-10,
+                  "log_softmax vjp")
+    lse = ops.logsumexp_forward(x, 1)
+    assert_parity(lse[:, 0], gold["logsumexp/y"], 1e-10, "logsumexp")
+    assert_parity(d["s_g1"][:, None] * np.exp(x - lse), gold["logsumexp/g0"], 1e-10,
+                  "logsumexp vjp")
+    sm = ops.softmax_forward(d["masked"])
+    assert_parity(sm, gold["softmax_masked/y"], 1e-10, "masked softmax")
+    m = d["m_x"]
+    for name, fn in (("max_ax1", np.max), ("min_ax1", np.min)):
+        kept = fn(m, axis=1, keepdims=True)
+        np.testing.assert_array_equal(kept[:, 0], gold[f"{name}/y"])
+        gx = ops.extremum_backward(d["m_g1"][:, None], m, kept, (1,))
+        assert_parity(gx, gold[f"{name}/g0"], 1e-10, name)
+    z, y = d["b_z"], d["b_y"]
+    losses = ops.bce_with_logits_forward(z, y)
+    assert_parity(losses, gold["bce_none/y"], 1e-10, "bce")
+    assert float(losses.mean()) == pytest.approx(float(gold["bce_mean/y"]), rel=1e-12)
+    gz, gy = ops.bce_with_logits_backward(d["b_g"], z, y)
+    assert_parity(gz, gold["bce_none/g0"], 1e-10, "bce dz")
+    assert_parity(gy, gold["bce_none/g1"], 1e-10, "bce dy")
+    args = [d[k] for k in ("rx", "rh0", "r_wih", "r_whh", "r_bih", "r_bhh")]
+    for act in ("tanh", "relu"):
+        relu = act == "relu"
+        out = ornn.rnn_forward(*args, relu=relu)
+        assert_parity(out, gold[f"rnn_{act}/y"], 1e-10, f"rnn {act}")
+        grads = ornn.rnn_backward(d["r_g"], args[0], args[1], args[2], args[3], True, out,
+                               relu=relu)
+        for i, gr in enumerate(grads):
+            assert_parity(gr, gold[f"rnn_{act}/g{i}"], 1e-10, f"rnn {act} grad {i}")
