@@ -7,7 +7,7 @@ through the library. No framework is imported. A :class:`DeviceArray` is a conti
 row-major view of a :class:`_Block` (several arrays may share one block, e.g. the slots of a
 flat parameter arena), and duck-types the parts of ``numpy.ndarray`` that user code reads from
 ``tensor.data`` (``shape``, ``dtype``, ``np.asarray(a)``, ``a.item()``, indexing for
-inspection, whole-array assignment).
+inspection, assignment to the whole array or to an indexed part).
 """
 
 from __future__ import annotations
@@ -249,8 +249,10 @@ class DeviceArray:
         return self.numpy()[index]
 
     def __setitem__(self, index: Any, value: Any) -> None:
-        if index is not Ellipsis and index != slice(None):
-            raise NotImplementedError("only whole-array assignment (a[...] = v) is supported")
+        whole = index is Ellipsis or (isinstance(index, slice) and index == slice(None))
+        if not whole:
+            self._assign_part(index, value)
+            return
         if isinstance(value, DeviceArray):
             if value.shape != self.shape and value.size != 1:
                 value_np = np.broadcast_to(value.numpy(), self.shape)
@@ -262,6 +264,34 @@ class DeviceArray:
             value = value.numpy()
         arr = np.broadcast_to(np.asarray(value, dtype=self.dtype), self.shape)
         upload_into(self, np.ascontiguousarray(arr))
+
+    def _assign_part(self, index: Any, value: Any) -> None:
+        """``a[index] = value``. Basic indexing (ints, slices, ``...``, ``None``) writes the
+        selected strided view on the device with one strided copy of ``value`` broadcast to
+        it; integer or boolean array indices go through a host copy of the array (an
+        interactive edit, not a training-step path)."""
+        from tensorgrad_b200.ops.shape import _basic_view, broadcast_array, strided_copy
+
+        try:
+            offset, shape, strides = _basic_view(self.shape, self.itemsize, index)
+        except NotImplementedError:
+            host = self.numpy()
+            host[index] = value.numpy() if isinstance(value, DeviceArray) else value
+            upload_into(self, host)
+            return
+        if isinstance(value, DeviceArray):
+            src = value if value.dtype == self.dtype else value.astype(self.dtype)
+            if src.shape != shape:
+                if np.broadcast_shapes(src.shape, shape) != tuple(shape):
+                    raise ValueError(f"could not broadcast input array from shape {src.shape} "
+                                     f"into shape {tuple(shape)}")
+                src = broadcast_array(src, tuple(shape))
+        else:
+            src = from_numpy(np.ascontiguousarray(
+                np.broadcast_to(np.asarray(value, dtype=self.dtype), shape)))
+        if math.prod(shape):
+            strided_copy(src.ptr, contiguous_strides(shape), self.ptr + offset * self.itemsize,
+                         strides, shape, self.itemsize)
 
     # ------------------------------------------------------------- views and copies
     def reshape(self, *shape: int | Sequence[int]) -> DeviceArray:

@@ -100,3 +100,29 @@ def test_data_loader_batches_upload_in_order():
             np.testing.assert_array_equal(xb.numpy(), xs[yb.numpy()])
             order.extend(yb.numpy().tolist())
         np.testing.assert_array_equal(order, load_golden("ops_extra.npz")[f"loader_epoch{epoch}"])
+
+
+def test_device_array_assignment():
+    """``tensor.data[index] = value`` as NumPy assigns: whole array, basic-index views (with
+    broadcasting, from host values and from device arrays) and integer / boolean arrays."""
+    import tensorgrad_b200 as tg
+    from tensorgrad_b200 import device
+
+    ref = np.arange(24, dtype=np.float32).reshape(2, 3, 4)
+    t = tg.Tensor(ref.copy())
+    cases = [
+        (Ellipsis, 7.0), ((0, 1), np.array([1, 2, 3, 4], np.float32)), ((slice(None), 2), -1.0),
+        ((1, slice(0, 3, 2), slice(1, None)), np.ones((2, 3), np.float32) * 5),
+        ((Ellipsis, 0), np.arange(3, dtype=np.float32)), (np.array([1, 0]), 9.0),
+        (ref > 20, 0.5),
+    ]
+    for index, value in cases:
+        ref[index] = value
+        t.data[index] = value
+        np.testing.assert_array_equal(t.numpy(), ref, err_msg=str(index))
+    src = device.from_numpy(np.full((4,), 3.0, np.float32))
+    ref[1, :, :] = 3.0
+    t.data[1] = src  # a device row broadcast over the view
+    np.testing.assert_array_equal(t.numpy(), ref)
+    with pytest.raises(ValueError, match="broadcast"):
+        t.data[0] = device.from_numpy(np.ones(5, np.float32))
