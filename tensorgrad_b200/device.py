@@ -234,6 +234,15 @@ class DeviceArray:
     def tolist(self) -> Any:
         return self.numpy().tolist()
 
+    def __getattr__(self, name: str) -> Any:
+        """NumPy's other array methods and attributes (``mean``, ``argmax``, ``std``,
+        ``astype(...).sum()`` ...) for code that inspects ``tensor.data`` as the reference's
+        NumPy arrays allow: taken from a host copy, so they read the values and never change
+        the device array (and cost a device-to-host copy per use)."""
+        if name.startswith("_") or not hasattr(np.ndarray, name):
+            raise AttributeError(f"'DeviceArray' object has no attribute '{name}'")
+        return getattr(self.numpy(), name)
+
     def __float__(self) -> float:
         return float(self.item())
 

@@ -211,3 +211,23 @@ def test_gradient_slot_is_handed_out_once_per_pass():
     assert grad_buffer(p, (2, 3), np.float64) is slot
     q = _leaf((2, 3), True)
     assert q._grad_target() is None  # no arena slot
+
+
+def test_device_array_reads_numpy_methods_from_a_host_copy():
+    """``tensor.data.argmax(1)``, ``.mean()`` and the like work as on the reference's NumPy
+    arrays (read-only, from a host copy); private names are not forwarded."""
+    from tensorgrad_b200.device import DeviceArray
+
+    host = np.array([[0.5, 2.0, -1.0], [3.0, 1.0, 1.5]])
+
+    class _Copyable(DeviceArray):
+        def numpy(self, out=None):
+            return host.copy()
+
+    a = _Copyable(None, 0, host.shape, host.dtype)
+    np.testing.assert_array_equal(a.argmax(1), [1, 0])
+    assert a.mean() == pytest.approx(host.mean())
+    assert a.max(axis=0).tolist() == [3.0, 2.0, 1.5]
+    with pytest.raises(AttributeError):
+        a._not_there
+    assert not hasattr(a, "mul_")  # not a NumPy attribute: no host copy, no forwarding
