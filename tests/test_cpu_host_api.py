@@ -231,3 +231,54 @@ def test_device_array_reads_numpy_methods_from_a_host_copy():
     with pytest.raises(AttributeError):
         a._not_there
     assert not hasattr(a, "mul_")  # not a NumPy attribute: no host copy, no forwarding
+
+
+def test_bench_readback_copies_every_result_without_blocking():
+    """The end-to-end loop's read-back: one asynchronous copy per result tensor into
+    alternating page-locked buffers, a wait only on the copy of two steps back, and the last
+    result's value after the closing synchronisation (fakes stand in for the device)."""
+    import ctypes
+    import types
+
+    import bench
+
+    queried: list[int] = []
+
+    class _Event:
+        count = 0
+
+        def __init__(self):
+            _Event.count += 1
+            self.id = _Event.count
+
+        def record(self):
+            pass
+
+        def query(self):
+            queried.append(self.id)
+            return True
+
+    copies: list[tuple[int, int]] = []
+
+    def memcpy_d2h(dst, src, nbytes, stream):
+        ctypes.memmove(dst, src, nbytes)
+        copies.append((dst, nbytes))
+        return 0
+
+    fake_device = types.SimpleNamespace(pinned_empty=lambda shape, dt: np.empty(shape, dt),
+                                        stream=lambda: 0, _Event=_Event)
+    fake_lib = types.SimpleNamespace(tg_memcpy_d2h=memcpy_d2h)
+
+    def result(value):
+        host = np.array(value, dtype=np.float32)
+        data = types.SimpleNamespace(ptr=host.ctypes.data, nbytes=host.nbytes)
+        return types.SimpleNamespace(shape=host.shape, dtype=host.dtype, data=data, keep=host)
+
+    reader = bench._AsyncReadback(fake_lib, fake_device)
+    assert reader.value() is None
+    losses = [result(v) for v in (4.0, 3.5, 3.25)]
+    for r in losses:
+        reader.issue(r)
+    assert len(copies) == 3 and copies[0][0] != copies[1][0] and copies[0][0] == copies[2][0]
+    assert queried == [1]  # the third step waited for the first step's copy only
+    assert reader.value() == 3.25
