@@ -355,6 +355,18 @@ def run_ops_extra() -> dict[str, np.ndarray]:
     return out
 
 
+def run_profiler_table() -> dict[str, np.ndarray]:
+    """The reference profiler's table for fixed statistics (the text format users parse)."""
+    from tensorgrad import profiler
+    from tests.golden.specs import PROFILE_ROWS
+
+    prof = profiler.Profile()
+    for name, fc, fs, bc, bs in PROFILE_ROWS:
+        prof.ops[name] = profiler.OpStats(fc, fs, bc, bs)
+    prof.wall_seconds = 0.125
+    return {"table": np.array(prof.table()), "table_limit2": np.array(prof.table(limit=2))}
+
+
 def main() -> None:
     jobs = {
         "gpt_small": lambda: run_gpt(GPT_SMALL),
@@ -369,6 +381,7 @@ def main() -> None:
         "higher_order": run_higher_order,
         "higher_order_layers": run_higher_order_layers,
         "ops_extra": run_ops_extra,
+        "profiler_table": run_profiler_table,
     }
     names = sys.argv[1:] or [*jobs, "gpt_checkpoint"]
     for name in names:

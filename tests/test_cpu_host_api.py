@@ -282,3 +282,18 @@ def test_bench_readback_copies_every_result_without_blocking():
     assert len(copies) == 3 and copies[0][0] != copies[1][0] and copies[0][0] == copies[2][0]
     assert queried == [1]  # the third step waited for the first step's copy only
     assert reader.value() == 3.25
+
+
+def test_profile_table_text_matches_reference():
+    """The profiler's table, character for character, against the reference's table for the
+    same statistics (tests/golden/profiler_table.npz)."""
+    from tensorgrad_b200 import profiler
+    from tests.golden.specs import PROFILE_ROWS
+
+    gold = load_golden("profiler_table.npz")
+    prof = profiler.Profile()
+    for name, fc, fs, bc, bs in PROFILE_ROWS:
+        prof.ops[name] = profiler.OpStats(fc, fs, bc, bs)
+    prof.wall_seconds = 0.125
+    assert prof.table() == str(gold["table"])
+    assert prof.table(limit=2) == str(gold["table_limit2"])
