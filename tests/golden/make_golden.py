@@ -367,6 +367,27 @@ def run_profiler_table() -> dict[str, np.ndarray]:
     return {"table": np.array(prof.table()), "table_limit2": np.array(prof.table(limit=2))}
 
 
+def run_viz() -> dict[str, np.ndarray]:
+    """The reference's graph drawings of two small graphs (the text format users render):
+    ``sum((tanh(w @ x))**2)`` with named leaves, and a named intermediate under a quoted
+    name."""
+    from tensorgrad import viz
+
+    tg.set_default_dtype(np.float64)
+    w = tg.Tensor(np.ones((2, 3)), requires_grad=True)
+    x = tg.Tensor(np.ones(3))
+    y = tg.tanh(w @ x)
+    loss = (y * y).sum()
+    a = tg.Tensor([1.0, 2.0], requires_grad=True)
+    hidden = tg.relu(a)
+    out = hidden.sum()
+    named = {'say "a"': a, "hidden": hidden}
+    return {"mermaid_lr": np.array(viz.to_mermaid(loss, names={"w": w, "x": x}, direction="LR")),
+            "dot_tb": np.array(viz.to_dot(loss, names={"w": w, "x": x})),
+            "mermaid_named": np.array(viz.to_mermaid(out, names=named)),
+            "dot_named": np.array(viz.to_dot(out, names=named))}
+
+
 def main() -> None:
     jobs = {
         "gpt_small": lambda: run_gpt(GPT_SMALL),
@@ -382,6 +403,7 @@ def main() -> None:
         "higher_order_layers": run_higher_order_layers,
         "ops_extra": run_ops_extra,
         "profiler_table": run_profiler_table,
+        "viz": run_viz,
     }
     names = sys.argv[1:] or [*jobs, "gpt_checkpoint"]
     for name in names:

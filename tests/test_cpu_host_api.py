@@ -65,47 +65,26 @@ def _small_graph():
     return _op("sum", (), _op("mul", (2,), y, y)), {"w": w, "x": x}
 
 
-def test_mermaid_source_matches_the_reference_format():
+def test_drawings_match_the_reference_text():
+    """``viz.to_mermaid`` / ``to_dot`` of graphs of the same shape as two the reference drew,
+    character for character (tests/golden/viz.npz), from graph nodes made without device
+    data."""
     from tensorgrad_b200 import viz
 
+    gold = load_golden("viz.npz")
     loss, names = _small_graph()
-    assert viz.to_mermaid(loss, names=names, direction="LR") == "\n".join([
-        "flowchart LR",
-        '    n0["w<br/>(2, 3)"]:::param',
-        '    n1["x<br/>(3,)"]:::constant',
-        '    n2("matmul<br/>(2,)"):::op',
-        '    n3("tanh<br/>(2,)"):::op',
-        '    n4("mul<br/>(2,)"):::op',
-        '    n5(["sum<br/>scalar"]):::op',
-        "    n0 --> n2",
-        "    n1 --> n2",
-        "    n2 --> n3",
-        "    n3 --> n4",
-        "    n4 --> n5",
-        "    classDef param fill:#dfeafa,stroke:#898781,color:#0b0b0b",
-        "    classDef constant fill:none,stroke:#898781,stroke-dasharray:4 3,color:#898781",
-        "    classDef op fill:#f3f2ee,stroke:#898781,color:#0b0b0b",
-        "",
-    ])
-
-
-def test_dot_source_and_labels():
-    from tensorgrad_b200 import viz
-
-    loss, names = _small_graph()
-    dot = viz.to_dot(loss, names=names)
-    assert dot.startswith("digraph tensorgrad {\n  rankdir=TB;")
-    declared = set(re.findall(r"^  (n\d+) \[label=", dot, re.M))
-    edges = re.findall(r"^  (n\d+) -> (n\d+);", dot, re.M)
-    assert declared == {f"n{i}" for i in range(6)} and len(edges) == 5
-    assert 'label="sum\\nscalar"' in dot and "penwidth=2" in dot
-    assert 'label="x\\n(3,)", shape=box, style="dashed"' in dot
+    assert viz.to_mermaid(loss, names=names, direction="LR") == str(gold["mermaid_lr"])
+    assert viz.to_dot(loss, names=names) == str(gold["dot_tb"])
     a = _leaf((2,), True)
     hidden = _op("relu", (2,), a)
     out = _op("sum", (), hidden)
     named = {'say "a"': a, "hidden": hidden}
-    assert "say #quot;a#quot;<br/>(2,)" in viz.to_mermaid(out, names=named)
-    assert "hidden = relu\\n(2,)" in viz.to_dot(out, names=named)
+    assert viz.to_mermaid(out, names=named) == str(gold["mermaid_named"])
+    assert viz.to_dot(out, names=named) == str(gold["dot_named"])
+    dot = viz.to_dot(loss, names=names)
+    declared = set(re.findall(r"^  (n\d+) \[label=", dot, re.M))
+    edges = re.findall(r"^  (n\d+) -> (n\d+);", dot, re.M)
+    assert declared == {f"n{i}" for i in range(6)} and len(edges) == 5  # y * y: one edge
     with pytest.raises(ValueError, match="at least one"):
         viz.to_dot()
 
