@@ -38,7 +38,7 @@ def matmul(a: Any, b: Any) -> Tensor:
     vectors give their dot product)."""
     ta, tb = coerce_pair(a, b)
     if ta.ndim == 0 or tb.ndim == 0:
-        raise ValueError("matmul: both operands need at least one axis")
+        raise ValueError("matmul does not accept 0-d tensors; use mul instead")
     dt = np.result_type(ta.dtype, tb.dtype)
     ad = ta.data if ta.dtype == dt else cast_array(ta.data, dt)
     bd = tb.data if tb.dtype == dt else cast_array(tb.data, dt)

@@ -70,6 +70,8 @@ def flatten(a: Any, start_axis: int = 0, end_axis: int = -1) -> Tensor:
         return reshape(ta, (1,))
     s = normalize_axis(start_axis, ta.ndim)
     e = normalize_axis(end_axis, ta.ndim)
+    if s > e:
+        raise ValueError("flatten: start_axis must not come after end_axis")
     shape = ta.shape[:s] + (math.prod(ta.shape[s:e + 1]),) + ta.shape[e + 1:]
     return reshape(ta, shape)
 

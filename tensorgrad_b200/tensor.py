@@ -252,6 +252,10 @@ class Tensor:
         return self.data.numpy(out)
 
     def __array__(self, dtype: Any = None, copy: bool | None = None) -> np.ndarray:
+        # Always a host copy of device data; a dtype change refused with copy=False, as the
+        # reference refuses it.
+        if copy is False and dtype is not None and np.dtype(dtype) != self.dtype:
+            raise ValueError(f"cannot convert {self.dtype} to {np.dtype(dtype)} without a copy")
         arr = self.data.numpy()
         return arr if dtype is None else arr.astype(dtype)
 

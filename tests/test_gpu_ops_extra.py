@@ -126,3 +126,17 @@ def test_device_array_assignment():
     np.testing.assert_array_equal(t.numpy(), ref)
     with pytest.raises(ValueError, match="broadcast"):
         t.data[0] = device.from_numpy(np.ones(5, np.float32))
+
+
+def test_argument_errors_match_reference_messages():
+    import tensorgrad_b200 as tg
+
+    x = tg.Tensor(np.ones((2, 3, 4), np.float32))
+    with pytest.raises(ValueError, match="start_axis must not come after end_axis"):
+        tg.flatten(x, 2, 1)
+    assert tg.flatten(x, 1, 2).shape == (2, 12)
+    with pytest.raises(ValueError, match="0-d tensors; use mul instead"):
+        tg.matmul(tg.Tensor(np.float32(2.0)), x)
+    with pytest.raises(ValueError, match="without a copy"):
+        x.__array__(np.float64, copy=False)
+    assert np.asarray(x, dtype=np.float64).dtype == np.float64
